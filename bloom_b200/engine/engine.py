@@ -1,0 +1,211 @@
+"""LLMEngine: the public generation API.
+
+    eng = LLMEngine.from_preset("llama3-8b")            # or LLMEngine(model_path)
+    outs = eng.generate([[1, 2, 3], [4, 5]], SamplingParams(max_tokens=16))
+
+An engine step = C++ scheduler decision (decode rows + chunked prefill with
+the leftover token budget, prefix reuse, preemption) -> one batched forward
+on the GPU -> GPU sampling -> scheduler update (stop conditions, KV frees).
+Every running request advances by one token per step (in-flight batching).
+
+Reference surface: InferencePipeline::{run, run_stream, run_embedding_batch}
+(crates/engine/src/core/pipeline.rs:375-405), InferenceScheduler::{submit,
+step, cancel_request} (scheduler/mod.rs:1479-1845), GenerationParams
+defaults (max_tokens 128, temperature 0.7, top_p 0.9; crates/core/src/types.rs:242-260).
+"""
+from __future__ import annotations
+
+import os
+import time
+from dataclasses import dataclass, field
+from typing import Callable, Dict, Iterator, List, Optional
+
+import torch
+
+from .._ext import runtime as _rt
+from ..models.config import ModelConfig, preset
+from ..models.llama import DecoderLM, TPInfo
+from .runner import ModelRunner, kv_block_bytes
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 128
+    temperature: float = 0.7
+    top_p: float = 0.9
+    top_k: int = 0
+    seed: Optional[int] = None
+    min_tokens: int = 0
+    ignore_eos: bool = False
+    stop_token_ids: List[int] = field(default_factory=list)
+
+    def to_native(self, default_seed: int):
+        sp = _rt().SamplingParams()
+        sp.max_tokens = int(self.max_tokens)
+        sp.temperature = float(self.temperature)
+        sp.top_p = float(self.top_p)
+        sp.top_k = int(self.top_k)
+        sp.seed = int(self.seed if self.seed is not None else default_seed)
+        sp.min_tokens = int(self.min_tokens)
+        sp.ignore_eos = bool(self.ignore_eos)
+        sp.stop_token_ids = [int(t) for t in self.stop_token_ids]
+        return sp
+
+
+GREEDY = SamplingParams(temperature=0.0, top_p=1.0)
+
+FINISH_REASONS = {0: None, 1: "stop", 2: "length", 3: "abort"}
+
+
+@dataclass
+class RequestOutput:
+    request_id: int
+    prompt_token_ids: List[int]
+    token_ids: List[int] = field(default_factory=list)
+    finished: bool = False
+    finish_reason: Optional[str] = None
+    arrival_time: float = 0.0
+    first_token_time: Optional[float] = None
+    finish_time: Optional[float] = None
+    num_cached_tokens: int = 0
+
+
+@dataclass
+class EngineConfig:
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 8192
+    max_model_len: int = 4096
+    gpu_memory_utilization: float = 0.85
+    num_blocks: Optional[int] = None
+    enable_prefix_caching: bool = True
+    chunked_prefill: bool = True
+    use_cuda_graphs: bool = True
+    seed: int = 0
+
+
+class LLMEngine:
+    def __init__(self, model: DecoderLM, config: Optional[EngineConfig] = None):
+        self.model = model
+        self.cfg = model.cfg
+        self.econf = config or EngineConfig()
+        ec = self.econf
+        rt = _rt()
+        dev = model.device
+        if ec.num_blocks is None:
+            torch.cuda.synchronize(dev)
+            free, total = torch.cuda.mem_get_info(dev)
+            reserve = int(total * (1.0 - ec.gpu_memory_utilization)) + (4 << 30)  # activations, graphs
+            budget = max(free - reserve, 64 * kv_block_bytes(model))
+            need = ec.max_num_seqs * ((ec.max_model_len + 15) // 16) + 64
+            ec.num_blocks = int(min(budget // kv_block_bytes(model), max(need, 1024)))
+        sc = rt.SchedulerConfig()
+        sc.max_num_seqs = ec.max_num_seqs
+        sc.max_num_batched_tokens = ec.max_num_batched_tokens
+        sc.max_model_len = ec.max_model_len
+        sc.chunked_prefill = ec.chunked_prefill
+        sc.eos_token_ids = list(self.cfg.eos_token_ids)
+        self.scheduler = rt.Scheduler(sc, ec.num_blocks, 16, ec.enable_prefix_caching)
+        self.runner = ModelRunner(model, ec.num_blocks, ec.max_num_seqs, ec.max_num_batched_tokens,
+                                  ec.max_model_len, ec.use_cuda_graphs)
+        self.scheduler.set_arena(self.runner.arena_host, self.runner.max_tokens, ec.max_num_seqs,
+                                 self.runner.max_blocks)
+        if ec.use_cuda_graphs:
+            self.scheduler.set_decode_buckets(sorted(self.runner.buckets))
+            self.runner.capture_graphs()
+        self.requests: Dict[int, RequestOutput] = {}
+        self._seed_counter = ec.seed
+        self.step_times: List[float] = []
+
+    # ------------------------------------------------------------ construction helpers
+    @staticmethod
+    def from_preset(name: str, tp: Optional[TPInfo] = None, config: Optional[EngineConfig] = None, seed: int = 0,
+                    device=None) -> "LLMEngine":
+        cfg = preset(name)
+        model = DecoderLM(cfg, tp, device)
+        model.random_init(seed)
+        return LLMEngine(model, config)
+
+    @staticmethod
+    def from_pretrained(path: str, tp: Optional[TPInfo] = None, config: Optional[EngineConfig] = None,
+                        device=None) -> "LLMEngine":
+        from ..formats.loader import load_decoder
+
+        model = load_decoder(path, tp, device)
+        return LLMEngine(model, config)
+
+    # ------------------------------------------------------------ requests
+    def add_request(self, prompt_token_ids: List[int], params: Optional[SamplingParams] = None,
+                    priority: int = 0) -> int:
+        params = params or SamplingParams()
+        self._seed_counter += 1
+        rid = self.scheduler.add_request([int(t) for t in prompt_token_ids], params.to_native(self._seed_counter),
+                                         priority)
+        self.requests[rid] = RequestOutput(rid, list(prompt_token_ids), arrival_time=time.perf_counter())
+        return rid
+
+    def abort(self, request_id: int) -> bool:
+        ok = self.scheduler.abort(request_id)
+        r = self.requests.get(request_id)
+        if ok and r is not None:
+            r.finished = True
+            r.finish_reason = "abort"
+            r.finish_time = time.perf_counter()
+        return ok
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    def step(self) -> List[RequestOutput]:
+        """One engine step; returns the requests that received a token."""
+        t0 = time.perf_counter()
+        meta = self.scheduler.schedule()
+        if meta.num_tokens == 0:
+            return []
+        sampled = self.runner.execute(meta)
+        events = self.scheduler.update(sampled, meta.num_real_logits)
+        now = time.perf_counter()
+        out = []
+        for rid, tok, finished, reason in events:
+            r = self.requests.get(rid)
+            if r is None:
+                continue
+            if r.first_token_time is None:
+                r.first_token_time = now
+                r.num_cached_tokens = 0
+            r.token_ids.append(tok)
+            if finished:
+                r.finished = True
+                r.finish_reason = FINISH_REASONS.get(reason, "stop")
+                r.finish_time = now
+            out.append(r)
+        self.step_times.append(now - t0)
+        return out
+
+    def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None,
+                 on_token: Optional[Callable[[RequestOutput], None]] = None) -> List[RequestOutput]:
+        ids = [self.add_request(p, params) for p in prompts]
+        while self.has_unfinished():
+            for r in self.step():
+                if on_token is not None:
+                    on_token(r)
+        res = [self.requests.pop(i) for i in ids]
+        return res
+
+    def stream(self, prompt: List[int], params: Optional[SamplingParams] = None) -> Iterator[int]:
+        rid = self.add_request(prompt, params)
+        seen = 0
+        while True:
+            self.step()
+            r = self.requests[rid]
+            while seen < len(r.token_ids):
+                yield r.token_ids[seen]
+                seen += 1
+            if r.finished:
+                self.requests.pop(rid, None)
+                return
+
+    def kv_metrics(self) -> dict:
+        return dict(self.scheduler.kv_metrics())
+
+    def shutdown(self) -> None:
+        self.runner.release_graphs()

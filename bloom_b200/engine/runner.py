@@ -1,0 +1,185 @@
+"""Model runner: one GPU's share of an engine step.
+
+The C++ scheduler writes the step's metadata into a pinned arena; the runner
+copies the used part to the device in one transfer, runs the forward (a CUDA
+graph replay for decode-only steps padded to a batch bucket, eager kernels
+otherwise), samples on the GPU and reads back one int32 per sampling row.
+
+Tensor parallel ranks run identical schedulers on identical inputs; sampled
+tokens are made identical across ranks (greedy: distributed argmax over the
+vocabulary shards; stochastic: all-gathered logits with the same Philox
+stream), so no per-step metadata broadcast is needed.
+"""
+from __future__ import annotations
+
+import math
+import time
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import ops
+from .._ext import runtime as _rt
+from ..models.llama import DecoderLM, StepInputs
+
+DEFAULT_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512]
+
+
+def kv_block_bytes(model: DecoderLM, block_size: int = 16) -> int:
+    cfg = model.cfg
+    return cfg.num_layers * 2 * model.nkv * block_size * cfg.head_dim * 2
+
+
+class ModelRunner:
+    def __init__(
+        self,
+        model: DecoderLM,
+        num_blocks: int,
+        max_num_seqs: int = 256,
+        max_num_batched_tokens: int = 8192,
+        max_model_len: int = 4096,
+        use_cuda_graphs: bool = True,
+        graph_buckets: Optional[List[int]] = None,
+    ):
+        self.model = model
+        self.cfg = model.cfg
+        self.device = model.device
+        self.block_size = 16
+        self.max_num_seqs = max_num_seqs
+        self.max_tokens = max(max_num_batched_tokens, max_num_seqs)
+        self.max_blocks = (max_model_len + self.block_size - 1) // self.block_size
+        self.num_blocks = num_blocks
+        cfg = self.cfg
+        self.kv_cache = torch.empty(cfg.num_layers, num_blocks, 2, model.nkv, self.block_size, cfg.head_dim,
+                                    dtype=torch.bfloat16, device=self.device)
+        rt = _rt()
+        worst = rt.arena_layout(self.max_tokens, max_num_seqs, max_num_seqs,
+                                self.max_tokens // 64 + max_num_seqs, max_num_seqs, self.max_blocks)
+        self.arena_words = worst.used_words
+        self.arena_host = torch.zeros(self.arena_words, dtype=torch.int32).pin_memory()
+        self.arena_dev = torch.zeros(self.arena_words, dtype=torch.int32, device=self.device)
+        self.sampled_host = torch.zeros(max(max_num_seqs, 1), dtype=torch.int32).pin_memory()
+        self.buckets = [b for b in (graph_buckets or DEFAULT_BUCKETS) if b <= max_num_seqs]
+        if max_num_seqs not in self.buckets:
+            self.buckets.append(max_num_seqs)
+        self.use_cuda_graphs = use_cuda_graphs
+        # decode attention split-K workspace, sized for the largest need over buckets
+        ws = 1
+        self.decode_splits: Dict[int, int] = {}
+        for b in self.buckets + [max_num_seqs]:
+            s = ops.decode_attention_splits(b, model.nkv, self.max_blocks, self.device.index)
+            self.decode_splits[b] = s
+            ws = max(ws, ops.decode_workspace_numel(b, model.nkv, s))
+        self.decode_ws = torch.empty(ws, dtype=torch.float32, device=self.device)
+        self.graphs: Dict[int, tuple] = {}
+        self.graph_pool = None
+        self.stats = {"steps": 0, "graph_steps": 0, "eager_steps": 0, "tokens": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+
+    # ------------------------------------------------------------ views
+    def _v(self, off: int, n: int, dtype=torch.int32) -> torch.Tensor:
+        if dtype == torch.int32 or dtype == torch.float32:
+            t = self.arena_dev[off:off + n]
+            return t if dtype == torch.int32 else t.view(torch.float32)
+        return self.arena_dev[off:off + 2 * n].view(torch.int64)
+
+    def views(self, m) -> StepInputs:
+        T, Bd, Sp, NT, NL = m.num_tokens, m.num_decode, m.num_prefill, m.num_tiles, m.num_logits
+        MB = self.max_blocks
+        splits = self.decode_splits.get(Bd) or ops.decode_attention_splits(Bd, self.model.nkv, MB, self.device.index)
+        return StepInputs(
+            input_ids=self._v(m.off_input_ids, T),
+            positions=self._v(m.off_positions, T, torch.int64),
+            slot_mapping=self._v(m.off_slot_mapping, T),
+            num_decode=Bd,
+            decode_block_table=self._v(m.off_decode_block_table, Bd * MB).view(Bd, MB) if Bd else None,
+            decode_seq_lens=self._v(m.off_decode_seq_lens, Bd) if Bd else None,
+            decode_splits=splits,
+            decode_workspace=self.decode_ws,
+            num_prefill=Sp,
+            prefill_block_table=self._v(m.off_prefill_block_table, Sp * MB).view(Sp, MB) if Sp else None,
+            prefill_ctx_lens=self._v(m.off_prefill_ctx_lens, Sp) if Sp else None,
+            prefill_cu_q=self._v(m.off_prefill_cu_q, Sp + 1) if Sp else None,
+            tile_seq=self._v(m.off_tile_seq, NT) if Sp else None,
+            tile_start=self._v(m.off_tile_start, NT) if Sp else None,
+            logits_rows=self._v(m.off_logits_rows, NL),
+        )
+
+    def sampling_views(self, m):
+        NL = m.num_logits
+        return (self._v(m.off_temperature, NL, torch.float32), self._v(m.off_top_p, NL, torch.float32),
+                self._v(m.off_top_k, NL), self._v(m.off_seeds, NL, torch.int64), self._v(m.off_offsets, NL, torch.int64))
+
+    # ------------------------------------------------------------ sampling
+    def _sample(self, logits: torch.Tensor, m, greedy: bool) -> torch.Tensor:
+        tp = self.model.tp
+        if tp.size == 1:
+            if greedy:
+                return ops.argmax(logits)
+            return ops.sample(logits, *self.sampling_views(m))
+        return tp.comm.sample_vocab_parallel(logits, greedy, self.sampling_views(m) if not greedy else None,
+                                             self.model.vocab_local)
+
+    def _forward_logits(self, s: StepInputs) -> torch.Tensor:
+        h = self.model.forward(s, self.kv_cache)
+        return self.model.logits(h)
+
+    # ------------------------------------------------------------ graphs
+    def capture_graphs(self, buckets: Optional[List[int]] = None) -> None:
+        if not self.use_cuda_graphs:
+            return
+        rt = _rt()
+        buckets = sorted(buckets or self.buckets, reverse=True)
+        # a valid dummy step: every row reads one page of block 0, writes no KV
+        self.arena_host.zero_()
+        for B in buckets:
+            m = rt.arena_layout(B, B, 0, 0, B, self.max_blocks)
+            h = self.arena_host
+            h[m.off_slot_mapping:m.off_slot_mapping + B] = -1
+            h[m.off_decode_seq_lens:m.off_decode_seq_lens + B] = 1
+            h[m.off_logits_rows:m.off_logits_rows + B] = torch.arange(B, dtype=torch.int32)
+            self.arena_dev[:m.used_words].copy_(self.arena_host[:m.used_words])
+            s = self.views(m)
+            torch.cuda.synchronize(self.device)
+            # warm-up on a side stream (lazy kernel attribute setup, allocator)
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                self._forward_logits(s)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            n0 = ops.LAUNCHES[0]
+            with torch.cuda.graph(g, pool=self.graph_pool):
+                logits = self._forward_logits(s)
+            if self.graph_pool is None:
+                self.graph_pool = g.pool()
+            self.graphs[B] = (g, logits, m, ops.LAUNCHES[0] - n0)
+        torch.cuda.synchronize(self.device)
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+        self.graph_pool = None
+
+    # ------------------------------------------------------------ step
+    def execute(self, m) -> torch.Tensor:
+        """Run one scheduled step; returns host int32 sampled tokens [num_logits]."""
+        used = m.used_words
+        self.arena_dev[:used].copy_(self.arena_host[:used], non_blocking=True)
+        graph = self.graphs.get(m.num_decode) if (m.num_prefill == 0 and m.num_decode > 0) else None
+        if graph is not None and graph[2].used_words == used:
+            g, logits, _, nlaunch = graph
+            g.replay()
+            ops.LAUNCHES[0] += nlaunch
+            self.stats["graph_steps"] += 1
+        else:
+            logits = self._forward_logits(self.views(m))
+            self.stats["eager_steps"] += 1
+        toks = self._sample(logits, m, m.all_greedy)
+        NL = m.num_logits
+        self.sampled_host[:NL].copy_(toks[:NL], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.stats["steps"] += 1
+        self.stats["tokens"] += m.num_tokens
+        self.stats["h2d_bytes"] += 4 * used
+        self.stats["d2h_bytes"] += 4 * NL
+        return self.sampled_host

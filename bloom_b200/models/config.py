@@ -1,0 +1,198 @@
+"""Model architecture descriptions.
+
+`ModelConfig` covers the decoder families the reference serves (Llama incl.
+Mistral/DeepSeek-style GGUF, Qwen2 with QKV bias, Qwen3 with per-head q/k
+RMSNorm; crates/engine/src/executor/candle.rs:28-70) plus Qwen3-MoE, and the
+BERT encoder for embeddings.  `from_hf_config` reads a Hugging Face
+config.json; `PRESETS` names the benchmark shapes.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+
+@dataclass
+class ModelConfig:
+    arch: str = "llama"  # llama | qwen2 | qwen3 | qwen3_moe | mistral | bert
+    vocab_size: int = 32000
+    hidden_size: int = 4096
+    num_layers: int = 32
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 14336
+    rms_norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    rope_scaling: Optional[dict] = None
+    max_position_embeddings: int = 8192
+    tie_word_embeddings: bool = False
+    qkv_bias: bool = False
+    qk_norm: bool = False
+    # MoE
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    norm_topk_prob: bool = True
+    # BERT
+    type_vocab_size: int = 2
+    layer_norm_eps: float = 1e-12
+    bos_token_id: Optional[int] = None
+    eos_token_ids: List[int] = field(default_factory=list)
+    name: str = ""
+
+    @property
+    def q_size(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    def num_params(self) -> int:
+        H, L, V = self.hidden_size, self.num_layers, self.vocab_size
+        attn = H * (self.q_size + 2 * self.kv_size) + self.q_size * H
+        if self.is_moe:
+            mlp = self.num_experts * 3 * H * self.moe_intermediate_size + H * self.num_experts
+        else:
+            mlp = 3 * H * self.intermediate_size
+        emb = V * H * (1 if self.tie_word_embeddings else 2)
+        return L * (attn + mlp + 2 * H) + emb + H
+
+    def kv_bytes_per_token(self, dtype_bytes: int = 2) -> int:
+        # KV/token = 2 * L * kv_heads * head_dim * bytes (reference core/manifest.rs:252)
+        return 2 * self.num_layers * self.num_kv_heads * self.head_dim * dtype_bytes
+
+    def to_json(self) -> str:
+        return json.dumps(dataclasses.asdict(self))
+
+    @staticmethod
+    def from_dict(d: dict) -> "ModelConfig":
+        names = {f.name for f in dataclasses.fields(ModelConfig)}
+        return ModelConfig(**{k: v for k, v in d.items() if k in names})
+
+
+def from_hf_config(cfg: dict) -> ModelConfig:
+    """Map a Hugging Face config.json onto ModelConfig."""
+    mt = (cfg.get("model_type") or "llama").lower()
+    arch = {"llama": "llama", "mistral": "llama", "qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe",
+            "bert": "bert"}.get(mt, "llama")
+    H = cfg.get("hidden_size", 4096)
+    nh = cfg.get("num_attention_heads", 32)
+    eos = cfg.get("eos_token_id")
+    eos_ids = eos if isinstance(eos, list) else ([eos] if eos is not None else [])
+    if arch == "bert":
+        return ModelConfig(
+            arch="bert", vocab_size=cfg.get("vocab_size", 30522), hidden_size=H,
+            num_layers=cfg.get("num_hidden_layers", 12), num_heads=nh, num_kv_heads=nh, head_dim=H // nh,
+            intermediate_size=cfg.get("intermediate_size", 4 * H),
+            max_position_embeddings=cfg.get("max_position_embeddings", 512),
+            type_vocab_size=cfg.get("type_vocab_size", 2), layer_norm_eps=cfg.get("layer_norm_eps", 1e-12),
+            name=cfg.get("_name_or_path", ""))
+    return ModelConfig(
+        arch=arch,
+        vocab_size=cfg.get("vocab_size", 32000),
+        hidden_size=H,
+        num_layers=cfg.get("num_hidden_layers", 32),
+        num_heads=nh,
+        num_kv_heads=cfg.get("num_key_value_heads", nh),
+        head_dim=cfg.get("head_dim") or H // nh,
+        intermediate_size=cfg.get("intermediate_size", 4 * H),
+        rms_norm_eps=cfg.get("rms_norm_eps", 1e-6),
+        rope_theta=cfg.get("rope_theta", 10000.0),
+        rope_scaling=cfg.get("rope_scaling"),
+        max_position_embeddings=cfg.get("max_position_embeddings", 4096),
+        tie_word_embeddings=bool(cfg.get("tie_word_embeddings", False)),
+        qkv_bias=(arch == "qwen2") or bool(cfg.get("attention_bias", False)),
+        qk_norm=arch in ("qwen3", "qwen3_moe"),
+        num_experts=cfg.get("num_experts", 0) if arch == "qwen3_moe" else 0,
+        num_experts_per_tok=cfg.get("num_experts_per_tok", 0),
+        moe_intermediate_size=cfg.get("moe_intermediate_size", 0),
+        norm_topk_prob=bool(cfg.get("norm_topk_prob", True)),
+        bos_token_id=cfg.get("bos_token_id"),
+        eos_token_ids=eos_ids,
+        name=cfg.get("_name_or_path", ""),
+    )
+
+
+def to_hf_config(c: ModelConfig) -> dict:
+    if c.arch == "bert":
+        return {"model_type": "bert", "architectures": ["BertModel"], "vocab_size": c.vocab_size,
+                "hidden_size": c.hidden_size, "num_hidden_layers": c.num_layers, "num_attention_heads": c.num_heads,
+                "intermediate_size": c.intermediate_size, "max_position_embeddings": c.max_position_embeddings,
+                "type_vocab_size": c.type_vocab_size, "layer_norm_eps": c.layer_norm_eps, "hidden_act": "gelu"}
+    mt = {"llama": "llama", "qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe"}.get(c.arch, "llama")
+    d = {"model_type": mt, "vocab_size": c.vocab_size, "hidden_size": c.hidden_size,
+         "num_hidden_layers": c.num_layers, "num_attention_heads": c.num_heads,
+         "num_key_value_heads": c.num_kv_heads, "head_dim": c.head_dim, "intermediate_size": c.intermediate_size,
+         "rms_norm_eps": c.rms_norm_eps, "rope_theta": c.rope_theta, "rope_scaling": c.rope_scaling,
+         "max_position_embeddings": c.max_position_embeddings, "tie_word_embeddings": c.tie_word_embeddings,
+         "torch_dtype": "bfloat16", "hidden_act": "silu"}
+    if c.eos_token_ids:
+        d["eos_token_id"] = c.eos_token_ids if len(c.eos_token_ids) > 1 else c.eos_token_ids[0]
+    if c.bos_token_id is not None:
+        d["bos_token_id"] = c.bos_token_id
+    if c.is_moe:
+        d.update(num_experts=c.num_experts, num_experts_per_tok=c.num_experts_per_tok,
+                 moe_intermediate_size=c.moe_intermediate_size, norm_topk_prob=c.norm_topk_prob)
+    return d
+
+
+PRESETS = {
+    # Llama-3-8B shape (headline serving benchmark)
+    "llama3-8b": ModelConfig(arch="llama", vocab_size=128256, hidden_size=4096, num_layers=32, num_heads=32,
+                             num_kv_heads=8, head_dim=128, intermediate_size=14336, rms_norm_eps=1e-5,
+                             rope_theta=500000.0, max_position_embeddings=8192, eos_token_ids=[128001, 128009],
+                             bos_token_id=128000, name="llama3-8b"),
+    "llama3-70b": ModelConfig(arch="llama", vocab_size=128256, hidden_size=8192, num_layers=80, num_heads=64,
+                              num_kv_heads=8, head_dim=128, intermediate_size=28672, rms_norm_eps=1e-5,
+                              rope_theta=500000.0, max_position_embeddings=8192, eos_token_ids=[128001, 128009],
+                              bos_token_id=128000, name="llama3-70b"),
+    # 1B-shape draft for speculative decoding
+    "llama3-1b-draft": ModelConfig(arch="llama", vocab_size=128256, hidden_size=2048, num_layers=16, num_heads=32,
+                                   num_kv_heads=8, head_dim=64, intermediate_size=8192, rms_norm_eps=1e-5,
+                                   rope_theta=500000.0, max_position_embeddings=8192, tie_word_embeddings=True,
+                                   eos_token_ids=[128001, 128009], bos_token_id=128000, name="llama3-1b-draft"),
+    "qwen3-moe-30b-a3b": ModelConfig(arch="qwen3_moe", vocab_size=151936, hidden_size=2048, num_layers=48,
+                                     num_heads=32, num_kv_heads=4, head_dim=128, intermediate_size=6144,
+                                     rms_norm_eps=1e-6, rope_theta=1000000.0, max_position_embeddings=32768,
+                                     qk_norm=True, num_experts=128, num_experts_per_tok=8, moe_intermediate_size=768,
+                                     eos_token_ids=[151645, 151643], name="qwen3-moe-30b-a3b"),
+    # SmolLM2-135M shape (CPU GGUF Q8_0 config)
+    "smollm2-135m": ModelConfig(arch="llama", vocab_size=49152, hidden_size=576, num_layers=30, num_heads=9,
+                                num_kv_heads=3, head_dim=64, intermediate_size=1536, rms_norm_eps=1e-5,
+                                rope_theta=10000.0, max_position_embeddings=2048, tie_word_embeddings=True,
+                                eos_token_ids=[2], bos_token_id=1, name="smollm2-135m"),
+    "minilm-l6": ModelConfig(arch="bert", vocab_size=30522, hidden_size=384, num_layers=6, num_heads=12,
+                             num_kv_heads=12, head_dim=32, intermediate_size=1536, max_position_embeddings=512,
+                             type_vocab_size=2, layer_norm_eps=1e-12, name="minilm-l6"),
+    # tiny shapes for tests
+    "tiny-llama": ModelConfig(arch="llama", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
+                              num_kv_heads=2, head_dim=128, intermediate_size=512, rms_norm_eps=1e-5,
+                              rope_theta=10000.0, max_position_embeddings=1024, eos_token_ids=[2], bos_token_id=1,
+                              name="tiny-llama"),
+    "tiny-qwen3": ModelConfig(arch="qwen3", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
+                              num_kv_heads=2, head_dim=128, intermediate_size=512, rms_norm_eps=1e-6,
+                              rope_theta=1000000.0, max_position_embeddings=1024, qk_norm=True, eos_token_ids=[2],
+                              name="tiny-qwen3"),
+    "tiny-qwen2": ModelConfig(arch="qwen2", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
+                              num_kv_heads=2, head_dim=128, intermediate_size=512, rms_norm_eps=1e-6,
+                              rope_theta=1000000.0, max_position_embeddings=1024, qkv_bias=True, eos_token_ids=[2],
+                              name="tiny-qwen2"),
+    "tiny-moe": ModelConfig(arch="qwen3_moe", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
+                            num_kv_heads=2, head_dim=128, intermediate_size=512, rms_norm_eps=1e-6,
+                            rope_theta=1000000.0, max_position_embeddings=1024, qk_norm=True, num_experts=8,
+                            num_experts_per_tok=2, moe_intermediate_size=128, eos_token_ids=[2], name="tiny-moe"),
+}
+
+
+def preset(name: str) -> ModelConfig:
+    if name not in PRESETS:
+        raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}")
+    return dataclasses.replace(PRESETS[name])

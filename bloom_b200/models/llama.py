@@ -1,0 +1,326 @@
+"""Decoder-only transformer (Llama / Mistral / Qwen2 / Qwen3 and the MoE
+variant) running on this repository's sm_100a kernels.
+
+Per layer and step (T tokens: decode rows first, then chunked-prefill rows):
+
+    qkv   = gemm(x, W_qkv) (+bias)                      tcgen05 GEMM
+    q     = rope_kv_write(qkv) -> paged KV pages         RoPE (+q/k RMSNorm) fused with the KV write
+    attn  = paged_decode_attention(q[:Bd]) | paged_prefill_attention(q[Bd:])
+    o     = gemm(attn, W_o)                              (split-K fp32 partials on small batches)
+    x     = add_rmsnorm(o -> residual)                   [tensor parallel: reduce across ranks]
+    act   = gemm(x, W_gate_up, epilogue=SwiGLU)          gate/up rows interleaved, SwiGLU in the epilogue
+    d     = gemm(act, W_down)
+    x     = add_rmsnorm(d -> residual)
+
+Weights live in the kernels' layout: fused QKV rows, interleaved gate/up
+rows, nn.Linear [out, in] K-major matrices.  Tensor parallelism shards heads,
+FFN columns and the vocabulary (Megatron column/row split); KV heads are
+replicated when there are fewer KV heads than ranks.
+
+Reference model semantics: candle-transformers llama/qwen2/qwen3 used by
+crates/engine/src/executor/candle.rs:1461-1796 and the streaming Qwen model
+(qwen_streaming.rs:300-801: RMSNorm, rotary, GQA attention, SwiGLU MLP,
+last-position lm_head).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import ops
+from .config import ModelConfig
+
+
+@dataclass
+class StepInputs:
+    """Device views of one engine step (see the scheduler's arena layout)."""
+
+    input_ids: torch.Tensor  # [T] int32
+    positions: torch.Tensor  # [T] int64
+    slot_mapping: torch.Tensor  # [T] int32
+    num_decode: int
+    decode_block_table: Optional[torch.Tensor]  # [Bd, MB]
+    decode_seq_lens: Optional[torch.Tensor]  # [Bd]
+    decode_splits: int
+    decode_workspace: Optional[torch.Tensor]
+    num_prefill: int
+    prefill_block_table: Optional[torch.Tensor]
+    prefill_ctx_lens: Optional[torch.Tensor]
+    prefill_cu_q: Optional[torch.Tensor]
+    tile_seq: Optional[torch.Tensor]
+    tile_start: Optional[torch.Tensor]
+    logits_rows: torch.Tensor  # [NL] int32
+    decode_q_len: int = 1
+
+
+@dataclass
+class TPInfo:
+    rank: int = 0
+    size: int = 1
+    group: object = None
+    comm: object = None  # bloom_b200.parallel.comm.Communicator
+
+
+def _local_heads(cfg: ModelConfig, tp: int, rank: int):
+    assert cfg.num_heads % tp == 0, "num_heads must divide by the TP size"
+    nq = cfg.num_heads // tp
+    if cfg.num_kv_heads >= tp:
+        assert cfg.num_kv_heads % tp == 0
+        nkv = cfg.num_kv_heads // tp
+        kv0 = rank * nkv
+    else:  # replicate KV heads: ranks sharing one KV head hold a copy
+        assert tp % cfg.num_kv_heads == 0
+        nkv = 1
+        kv0 = rank // (tp // cfg.num_kv_heads)
+    return nq, nkv, rank * nq, kv0
+
+
+class DecoderLM:
+    """Weights + forward of a decoder LM shard on one GPU."""
+
+    def __init__(self, cfg: ModelConfig, tp: Optional[TPInfo] = None, device=None):
+        self.cfg = cfg
+        self.tp = tp or TPInfo()
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.nq, self.nkv, self.q0, self.kv0 = _local_heads(cfg, self.tp.size, self.tp.rank)
+        assert cfg.intermediate_size % (16 * self.tp.size) == 0 or cfg.is_moe
+        self.inter = cfg.intermediate_size // self.tp.size
+        self.vocab_local = cfg.vocab_size // self.tp.size
+        assert cfg.vocab_size % self.tp.size == 0, "vocab must divide by the TP size"
+        self.layers: List[Dict[str, torch.Tensor]] = []
+        self.embed: Optional[torch.Tensor] = None
+        self.final_norm: Optional[torch.Tensor] = None
+        self.lm_head: Optional[torch.Tensor] = None
+        self.cos_sin: Optional[torch.Tensor] = None
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.moe = None  # set by qwen3_moe
+
+    # ------------------------------------------------------------ weights
+    def shard_full(self, full: Dict[str, torch.Tensor]) -> None:
+        """Install weights from full (unsharded) HF-named tensors of one layer set.
+
+        Expected names (HF Llama convention, layer index i):
+          model.embed_tokens.weight, model.norm.weight, lm_head.weight,
+          model.layers.{i}.input_layernorm.weight, .post_attention_layernorm.weight,
+          .self_attn.{q,k,v,o}_proj.weight (+ q/k/v bias), .self_attn.{q,k}_norm.weight,
+          .mlp.{gate,up,down}_proj.weight
+        """
+        cfg, dev, bf = self.cfg, self.device, torch.bfloat16
+        r, t = self.tp.rank, self.tp.size
+        hd = cfg.head_dim
+
+        def get(name):
+            return full[name]
+
+        self.embed = get("model.embed_tokens.weight").to(dev, bf).contiguous()
+        self.final_norm = get("model.norm.weight").to(dev, bf).contiguous()
+        lm = full.get("lm_head.weight", full["model.embed_tokens.weight"])
+        V = cfg.vocab_size
+        self.lm_head = lm[r * V // t:(r + 1) * V // t].to(dev, bf).contiguous()
+        self.layers = []
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            q = get(p + "self_attn.q_proj.weight")[self.q0 * hd:(self.q0 + self.nq) * hd]
+            k = get(p + "self_attn.k_proj.weight")[self.kv0 * hd:(self.kv0 + self.nkv) * hd]
+            v = get(p + "self_attn.v_proj.weight")[self.kv0 * hd:(self.kv0 + self.nkv) * hd]
+            layer = {
+                "ln1": get(p + "input_layernorm.weight").to(dev, bf).contiguous(),
+                "ln2": get(p + "post_attention_layernorm.weight").to(dev, bf).contiguous(),
+                "qkv": torch.cat([q, k, v], 0).to(dev, bf).contiguous(),
+                "o": get(p + "self_attn.o_proj.weight")[:, self.q0 * hd:(self.q0 + self.nq) * hd].to(dev, bf)
+                .contiguous(),
+            }
+            if cfg.qkv_bias:
+                qb = get(p + "self_attn.q_proj.bias")[self.q0 * hd:(self.q0 + self.nq) * hd]
+                kb = get(p + "self_attn.k_proj.bias")[self.kv0 * hd:(self.kv0 + self.nkv) * hd]
+                vb = get(p + "self_attn.v_proj.bias")[self.kv0 * hd:(self.kv0 + self.nkv) * hd]
+                layer["qkv_b"] = torch.cat([qb, kb, vb]).to(dev, bf).contiguous()
+            if cfg.qk_norm:
+                layer["q_norm"] = get(p + "self_attn.q_norm.weight").to(dev, bf).contiguous()
+                layer["k_norm"] = get(p + "self_attn.k_norm.weight").to(dev, bf).contiguous()
+            if not cfg.is_moe:
+                I = self.inter
+                g = get(p + "mlp.gate_proj.weight")[r * I:(r + 1) * I]
+                u = get(p + "mlp.up_proj.weight")[r * I:(r + 1) * I]
+                layer["gate_up"] = ops.interleave_gate_up(g.to(dev, bf), u.to(dev, bf))
+                layer["down"] = get(p + "mlp.down_proj.weight")[:, r * I:(r + 1) * I].to(dev, bf).contiguous()
+            self.layers.append(layer)
+        if cfg.is_moe:
+            from .qwen3_moe import MoEBlock
+
+            self.moe = MoEBlock(self, full)
+        self._finish()
+
+    def random_init(self, seed: int = 0, std: float = 0.02) -> None:
+        """N(0, std) weights (norms = 1) generated as full tensors from one seeded
+        stream and then sharded, so every TP size holds the same model."""
+        cfg = self.cfg
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        bf = torch.bfloat16
+
+        def randn(*shape):
+            return (torch.randn(*shape, generator=g, device=self.device, dtype=torch.float32) * std).to(bf)
+
+        H, hd = cfg.hidden_size, cfg.head_dim
+        full: Dict[str, torch.Tensor] = {}
+        full["model.embed_tokens.weight"] = randn(cfg.vocab_size, H)
+        full["model.norm.weight"] = torch.ones(H, dtype=bf, device=self.device)
+        if not cfg.tie_word_embeddings:
+            full["lm_head.weight"] = randn(cfg.vocab_size, H)
+        self.layers = []
+        # generate and install layer by layer to bound peak memory
+        r, t = self.tp.rank, self.tp.size
+        V = cfg.vocab_size
+        self.embed = full["model.embed_tokens.weight"]
+        self.final_norm = full["model.norm.weight"]
+        lm = full.get("lm_head.weight", self.embed)
+        self.lm_head = lm[r * V // t:(r + 1) * V // t].contiguous()
+        if "lm_head.weight" in full:
+            del full["lm_head.weight"]
+        moe_full = {}
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            lay = {
+                p + "input_layernorm.weight": torch.ones(H, dtype=bf, device=self.device),
+                p + "post_attention_layernorm.weight": torch.ones(H, dtype=bf, device=self.device),
+                p + "self_attn.q_proj.weight": randn(cfg.q_size, H),
+                p + "self_attn.k_proj.weight": randn(cfg.kv_size, H),
+                p + "self_attn.v_proj.weight": randn(cfg.kv_size, H),
+                p + "self_attn.o_proj.weight": randn(H, cfg.q_size),
+            }
+            if cfg.qkv_bias:
+                lay[p + "self_attn.q_proj.bias"] = randn(cfg.q_size)
+                lay[p + "self_attn.k_proj.bias"] = randn(cfg.kv_size)
+                lay[p + "self_attn.v_proj.bias"] = randn(cfg.kv_size)
+            if cfg.qk_norm:
+                lay[p + "self_attn.q_norm.weight"] = torch.ones(hd, dtype=bf, device=self.device)
+                lay[p + "self_attn.k_norm.weight"] = torch.ones(hd, dtype=bf, device=self.device)
+            if cfg.is_moe:
+                E, Im = cfg.num_experts, cfg.moe_intermediate_size
+                lay[p + "mlp.gate.weight"] = randn(E, H)
+                lay[p + "mlp.experts.gate_proj"] = randn(E, Im, H)
+                lay[p + "mlp.experts.up_proj"] = randn(E, Im, H)
+                lay[p + "mlp.experts.down_proj"] = randn(E, H, Im)
+            else:
+                lay[p + "mlp.gate_proj.weight"] = randn(cfg.intermediate_size, H)
+                lay[p + "mlp.up_proj.weight"] = randn(cfg.intermediate_size, H)
+                lay[p + "mlp.down_proj.weight"] = randn(H, cfg.intermediate_size)
+            self._install_layer(i, lay)
+            if cfg.is_moe:
+                moe_full.update({k: v for k, v in lay.items() if ".mlp." in k})
+            del lay
+        if cfg.is_moe:
+            from .qwen3_moe import MoEBlock
+
+            self.moe = MoEBlock(self, moe_full)
+        self._finish()
+
+    def _install_layer(self, i: int, lay: Dict[str, torch.Tensor]) -> None:
+        cfg, hd, bf = self.cfg, self.cfg.head_dim, torch.bfloat16
+        r = self.tp.rank
+        p = f"model.layers.{i}."
+        q = lay[p + "self_attn.q_proj.weight"][self.q0 * hd:(self.q0 + self.nq) * hd]
+        k = lay[p + "self_attn.k_proj.weight"][self.kv0 * hd:(self.kv0 + self.nkv) * hd]
+        v = lay[p + "self_attn.v_proj.weight"][self.kv0 * hd:(self.kv0 + self.nkv) * hd]
+        layer = {
+            "ln1": lay[p + "input_layernorm.weight"].to(self.device, bf).contiguous(),
+            "ln2": lay[p + "post_attention_layernorm.weight"].to(self.device, bf).contiguous(),
+            "qkv": torch.cat([q, k, v], 0).to(self.device, bf).contiguous(),
+            "o": lay[p + "self_attn.o_proj.weight"][:, self.q0 * hd:(self.q0 + self.nq) * hd]
+            .to(self.device, bf).contiguous(),
+        }
+        if cfg.qkv_bias:
+            layer["qkv_b"] = torch.cat([
+                lay[p + "self_attn.q_proj.bias"][self.q0 * hd:(self.q0 + self.nq) * hd],
+                lay[p + "self_attn.k_proj.bias"][self.kv0 * hd:(self.kv0 + self.nkv) * hd],
+                lay[p + "self_attn.v_proj.bias"][self.kv0 * hd:(self.kv0 + self.nkv) * hd]]).to(self.device, bf)
+        if cfg.qk_norm:
+            layer["q_norm"] = lay[p + "self_attn.q_norm.weight"].to(self.device, bf).contiguous()
+            layer["k_norm"] = lay[p + "self_attn.k_norm.weight"].to(self.device, bf).contiguous()
+        if not cfg.is_moe:
+            I = self.inter
+            g = lay[p + "mlp.gate_proj.weight"][r * I:(r + 1) * I].to(self.device, bf)
+            u = lay[p + "mlp.up_proj.weight"][r * I:(r + 1) * I].to(self.device, bf)
+            layer["gate_up"] = ops.interleave_gate_up(g, u)
+            layer["down"] = lay[p + "mlp.down_proj.weight"][:, r * I:(r + 1) * I].to(self.device, bf).contiguous()
+        if len(self.layers) <= i:
+            self.layers.append(layer)
+        else:
+            self.layers[i] = layer
+
+    def _finish(self) -> None:
+        cfg = self.cfg
+        self.cos_sin = ops.rope_cos_sin(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, self.device,
+                                        cfg.rope_scaling)
+
+    def weight_bytes(self) -> int:
+        n = 0
+        for lay in self.layers:
+            n += sum(t.numel() * t.element_size() for t in lay.values())
+        for t in (self.embed, self.final_norm, self.lm_head):
+            if t is not None:
+                n += t.numel() * t.element_size()
+        if self.moe is not None:
+            n += self.moe.weight_bytes()
+        return n
+
+    # ------------------------------------------------------------ forward
+    def _reduce(self, t: torch.Tensor) -> torch.Tensor:
+        """Sum a row-parallel output across TP ranks (bf16 [T, H] or f32 partials)."""
+        if self.tp.size == 1:
+            return t
+        return self.tp.comm.all_reduce(t)
+
+    def forward(self, s: StepInputs, kv_cache: torch.Tensor) -> torch.Tensor:
+        """Returns the final-normed hidden states of the logits rows [NL, H] (bf16)."""
+        cfg = self.cfg
+        T = s.input_ids.shape[0]
+        Bd = s.num_decode
+        H = cfg.hidden_size
+        eps = cfg.rms_norm_eps
+        dev = self.device
+        residual = ops.embedding(s.input_ids, self.embed)
+        x = ops.rmsnorm(residual, self.layers[0]["ln1"], eps)
+        qkv_dim = (self.nq + 2 * self.nkv) * cfg.head_dim
+        # split-K for the row-parallel GEMMs when the grid would be small (decode)
+        small = T <= 512
+        o_splits = ops.gemm_default_splits(T, H, self.nq * cfg.head_dim, dev.index) if small else 1
+        d_splits = ops.gemm_default_splits(T, H, self.inter, dev.index) if small and not cfg.is_moe else 1
+        for li, lay in enumerate(self.layers):
+            qkv = ops.gemm(x, lay["qkv"], bias=lay.get("qkv_b"))
+            q = torch.empty(T, self.nq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+            ops.rope_kv_write(qkv, s.positions, s.slot_mapping, self.cos_sin, q, kv_cache, li, self.nq, self.nkv,
+                              lay.get("q_norm"), lay.get("k_norm"), eps)
+            attn = torch.empty_like(q)
+            if Bd > 0:
+                ops.paged_decode_attention(q[:Bd], kv_cache, li, s.decode_block_table, s.decode_seq_lens, attn[:Bd],
+                                           q_len=s.decode_q_len, splits=s.decode_splits,
+                                           workspace=s.decode_workspace, scale=self.scale)
+            if s.num_prefill > 0:
+                ops.paged_prefill_attention(q[Bd:], kv_cache, li, s.prefill_block_table, s.prefill_ctx_lens,
+                                            s.prefill_cu_q, s.tile_seq, s.tile_start, attn[Bd:], scale=self.scale)
+            a2 = attn.view(T, self.nq * cfg.head_dim)
+            if o_splits > 1 and self.tp.size == 1:
+                o = ops.gemm(a2, lay["o"], epi=ops.EPI_PARTIAL_F32, splits=o_splits)
+            else:
+                o = self._reduce(ops.gemm(a2, lay["o"]))
+            x = ops.add_rmsnorm(o, residual, lay["ln2"], eps)
+            if self.moe is not None:
+                d = self._reduce(self.moe.forward(li, x))
+            else:
+                act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU)
+                if d_splits > 1 and self.tp.size == 1:
+                    d = ops.gemm(act, lay["down"], epi=ops.EPI_PARTIAL_F32, splits=d_splits)
+                else:
+                    d = self._reduce(ops.gemm(act, lay["down"]))
+            nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
+            x = ops.add_rmsnorm(d, residual, nxt, eps)
+        return x.index_select(0, s.logits_rows)
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        """Local vocab shard of the logits [NL, V/tp] (bf16)."""
+        return ops.gemm(h, self.lm_head)

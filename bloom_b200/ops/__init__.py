@@ -1,0 +1,233 @@
+"""Python surface of the sm_100a kernels in bloom_b200._C.
+
+Every function here launches one of this repository's own CUDA kernels on the
+current stream.  There is no fallback: on a CUDA tensor the kernel runs, or
+the call raises.  The fp32 oracles for tests live in `bloom_b200.ops.reference`.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .._ext import cuda as _C
+
+# Number of this repository's kernels launched through these wrappers (graph
+# replays add the count recorded while the graph was captured).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
+EPI_BF16 = 0
+EPI_F32 = 1
+EPI_SWIGLU = 2
+EPI_PARTIAL_F32 = 3
+EPI_RESIDUAL = 4
+
+
+def status(device: Optional[int] = None) -> torch.Tensor:
+    """Per-device int32[16] status word that kernels OR error bits into
+    (1: GEMM pipeline wait timed out, 2: attention wait timed out,
+    4: cross-GPU wait timed out, 8: bad argument, 16: MoE buffer overflow)."""
+    if device is None:
+        device = torch.cuda.current_device()
+    return _C().status_tensor(int(device))
+
+
+def check_status(device: Optional[int] = None) -> int:
+    """Read (and clear) the status word; raises if a kernel reported an error."""
+    st = status(device)
+    v = int(st[0].item())
+    if v:
+        st.zero_()
+        raise RuntimeError(f"bloom_b200 kernel status error bits 0x{v:x}")
+    return v
+
+
+# ---------------------------------------------------------------- GEMM
+def gemm(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    out: Optional[torch.Tensor] = None,
+    *,
+    epi: int = EPI_BF16,
+    bias: Optional[torch.Tensor] = None,
+    resid: Optional[torch.Tensor] = None,
+    splits: int = 1,
+) -> torch.Tensor:
+    """y = x @ w.T on tcgen05 (x [M,K] bf16, w [N,K] bf16) with a fused epilogue.
+
+    epi=EPI_SWIGLU expects w's rows interleaved as (16 gate rows, 16 up rows)
+    per 32 rows (see `interleave_gate_up`) and returns silu(gate) * up [M, N/2].
+    epi=EPI_PARTIAL_F32 returns split-K partial sums f32 [splits, M, N] that
+    `add_rmsnorm` reduces.
+    """
+    M, N = x.shape[0], w.shape[0]
+    if out is None:
+        if epi == EPI_SWIGLU:
+            out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
+        elif epi == EPI_F32:
+            out = torch.empty(M, N, dtype=torch.float32, device=x.device)
+        elif epi == EPI_PARTIAL_F32:
+            out = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
+        else:
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index))
+    _count()
+    return out
+
+
+def gemm_default_splits(M: int, N: int, K: int, device: int = 0) -> int:
+    return _C().gemm_default_splits(M, N, K, device)
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[I, H] gate and up -> [2I, H] rows ordered (16 gate, 16 up) per 32 rows."""
+    I, H = gate.shape
+    assert up.shape == gate.shape and I % 16 == 0
+    g = gate.reshape(I // 16, 16, H)
+    u = up.reshape(I // 16, 16, H)
+    return torch.stack([g, u], dim=1).reshape(2 * I, H).contiguous()
+
+
+def deinterleave_gate_up(w: torch.Tensor):
+    n2, H = w.shape
+    v = w.reshape(n2 // 32, 2, 16, H)
+    return v[:, 0].reshape(n2 // 2, H), v[:, 1].reshape(n2 // 2, H)
+
+
+# ---------------------------------------------------------------- norms / embedding / rope
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    _C().rmsnorm(x, w, out, eps)
+    _count()
+    return out
+
+
+def add_rmsnorm(delta: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """residual += delta (bf16 [M,H] or f32 partials [S,M,H]); returns rmsnorm(residual) * w."""
+    if out is None:
+        out = torch.empty_like(residual)
+    _C().add_rmsnorm(delta, residual, w, out, eps)
+    _count()
+    return out
+
+
+def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float,
+              resid: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    _C().layernorm(x, resid, w, b, out, eps)
+    _count()
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    _C().embedding(ids, table, out)
+    _count()
+    return out
+
+
+def rope_kv_write(qkv, positions, slot_mapping, cos_sin, q_out, kv_cache, layer, num_q_heads, num_kv_heads,
+                  q_norm=None, k_norm=None, eps: float = 1e-6):
+    _C().rope_kv_write(qkv, positions, slot_mapping, cos_sin, q_out, kv_cache, layer, num_q_heads, num_kv_heads,
+                       q_norm, k_norm, eps)
+    _count()
+    return q_out
+
+
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device=None, scaling: Optional[dict] = None):
+    """[max_pos, head_dim] f32 table = [cos | sin] of the HF rotate_half convention.
+
+    `scaling` supports the Llama-3.1 "llama3" rope_type (factor, low/high
+    frequency factors, original context) and "linear"."""
+    half = head_dim // 2
+    inv = 1.0 / (theta ** (torch.arange(0, half, dtype=torch.float64) * 2 / head_dim))
+    if scaling:
+        kind = scaling.get("rope_type", scaling.get("type", ""))
+        if kind == "llama3":
+            import math
+
+            factor = scaling["factor"]
+            lo, hi = scaling.get("low_freq_factor", 1.0), scaling.get("high_freq_factor", 4.0)
+            old = scaling.get("original_max_position_embeddings", 8192)
+            lo_wl, hi_wl = old / lo, old / hi
+            wl = 2 * math.pi / inv
+            smooth = (old / wl - lo) / (hi - lo)
+            scaled = torch.where(wl > lo_wl, inv / factor, inv)
+            mid = (wl <= lo_wl) & (wl >= hi_wl)
+            inv = torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
+        elif kind == "linear":
+            inv = inv / scaling["factor"]
+    t = torch.arange(max_pos, dtype=torch.float64)
+    ang = torch.outer(t, inv)
+    tab = torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32)
+    return tab.to(device) if device is not None else tab
+
+
+# ---------------------------------------------------------------- attention
+def decode_attention_splits(batch: int, num_kv_heads: int, max_pages: int, device: int = 0) -> int:
+    return _C().decode_attention_splits(batch, num_kv_heads, max_pages, device)
+
+
+def decode_workspace_numel(batch: int, num_kv_heads: int, splits: int) -> int:
+    return batch * num_kv_heads * splits * 32 * 130 if splits > 1 else 1
+
+
+def paged_decode_attention(q, kv_cache, layer, block_table, seq_lens, out, *, q_len: int = 1, splits: int = 1,
+                           workspace: Optional[torch.Tensor] = None, scale: float):
+    if workspace is None:
+        workspace = torch.empty(
+            decode_workspace_numel(seq_lens.shape[0], kv_cache.shape[3], splits), dtype=torch.float32,
+            device=q.device)
+    _C().paged_decode_attention(q, kv_cache, layer, block_table, seq_lens, out, q_len, splits, workspace, scale,
+                                status(q.device.index))
+    _count(2 if splits > 1 else 1)
+    return out
+
+
+def paged_prefill_attention(q, kv_cache, layer, block_table, ctx_lens, cu_seqlens_q, tile_seq, tile_start, out, *,
+                            scale: float, causal: bool = True):
+    _C().paged_prefill_attention(q, kv_cache, layer, block_table, ctx_lens, cu_seqlens_q, tile_seq, tile_start, out,
+                                 scale, causal, status(q.device.index))
+    _count()
+    return out
+
+
+def prefill_tiles(cu_seqlens_q, ctx_lens, tile_rows: int = 64):
+    """Host helper: (tile_seq, tile_start) int32 lists for paged_prefill_attention."""
+    seqs, starts, ext = [], [], []
+    cu = [int(v) for v in cu_seqlens_q]
+    for s in range(len(cu) - 1):
+        qlen = cu[s + 1] - cu[s]
+        for r in range(0, qlen, tile_rows):
+            seqs.append(s)
+            starts.append(r)
+            ext.append(int(ctx_lens[s]) - qlen + min(r + tile_rows, qlen))
+    order = sorted(range(len(seqs)), key=lambda i: -ext[i])
+    return (torch.tensor([seqs[i] for i in order], dtype=torch.int32),
+            torch.tensor([starts[i] for i in order], dtype=torch.int32))
+
+
+# ---------------------------------------------------------------- sampling
+def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _C().argmax_rows(logits, out)
+    _count()
+    return out
+
+
+def sample(logits, temperature, top_p, top_k, seeds, offsets, out: Optional[torch.Tensor] = None):
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _C().sample_rows(logits, temperature, top_p, top_k, seeds, offsets, out)
+    _count()
+    return out

@@ -1,0 +1,27 @@
+// pybind11 surface of bloom_b200._C (CUDA kernels for sm_100a).
+#include <torch/extension.h>
+
+#include "bloom/ops.h"
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "bloom_b200 sm_100a kernels";
+  m.attr("EPI_BF16") = int(bloom::kEpiBF16);
+  m.attr("EPI_F32") = int(bloom::kEpiF32);
+  m.attr("EPI_SWIGLU") = int(bloom::kEpiSwiGLU);
+  m.attr("EPI_PARTIAL_F32") = int(bloom::kEpiPartialF32);
+  m.attr("EPI_RESIDUAL") = int(bloom::kEpiResidual);
+  m.def("gemm_out", &bloom::gemm_out, "y = x @ w^T on tcgen05 with fused epilogue");
+  m.def("gemm_pick_bn", &bloom::gemm_pick_bn);
+  m.def("gemm_default_splits", &bloom::gemm_default_splits);
+  m.def("rmsnorm", &bloom::rmsnorm);
+  m.def("add_rmsnorm", &bloom::add_rmsnorm);
+  m.def("layernorm", &bloom::layernorm);
+  m.def("embedding", &bloom::embedding);
+  m.def("rope_kv_write", &bloom::rope_kv_write);
+  m.def("paged_decode_attention", &bloom::paged_decode_attention);
+  m.def("paged_prefill_attention", &bloom::paged_prefill_attention);
+  m.def("decode_attention_splits", &bloom::decode_attention_splits);
+  m.def("argmax_rows", &bloom::argmax_rows);
+  m.def("sample_rows", &bloom::sample_rows);
+  m.def("status_tensor", &bloom::status_tensor);
+}

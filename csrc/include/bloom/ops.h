@@ -1,0 +1,62 @@
+// Host entry points of the bloom_b200._C extension (implemented in csrc/kernels/*.cu).
+#pragma once
+
+#include <torch/extension.h>
+
+namespace bloom {
+
+// GEMM epilogues (y = x @ w^T, w in nn.Linear layout [N, K]).
+enum GemmEpilogue : int {
+  kEpiBF16 = 0,        // out bf16 [M, N] (+bias)
+  kEpiF32 = 1,         // out f32 [M, N] (+bias)
+  kEpiSwiGLU = 2,      // w rows interleaved (16 gate | 16 up) per 32 rows; out bf16 [M, N/2] = silu(g) * u
+  kEpiPartialF32 = 3,  // split-K: out f32 [splits, M, N] partial sums
+  kEpiResidual = 4,    // out bf16 [M, N] = acc + resid
+};
+
+void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
+              const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
+              const torch::Tensor& status);
+int gemm_pick_bn(int M);
+int gemm_default_splits(int M, int N, int K, int device);
+
+// Normalisation.
+void rmsnorm(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, double eps);
+// residual += sum_s delta[s] (delta is bf16 [M,H] or f32 [S,M,H]); out = rmsnorm(residual) * w
+void add_rmsnorm(const torch::Tensor& delta, torch::Tensor& residual, const torch::Tensor& w, torch::Tensor& out,
+                 double eps);
+void layernorm(const torch::Tensor& x, const c10::optional<torch::Tensor>& resid, const torch::Tensor& w,
+               const torch::Tensor& b, torch::Tensor& out, double eps);
+
+// Embedding gather: out[t] = table[ids[t]] (rows outside [0, V) give zeros).
+void embedding(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out);
+
+// RoPE on q/k (+ optional per-head RMSNorm of q and k), q to q_out, k/v to the
+// paged cache at slot_mapping (slot = block * 16 + offset; -1 skips).
+void rope_kv_write(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& slot_mapping,
+                   const torch::Tensor& cos_sin, torch::Tensor& q_out, torch::Tensor& kv_cache, int64_t layer,
+                   int64_t num_q_heads, int64_t num_kv_heads, const c10::optional<torch::Tensor>& q_norm,
+                   const c10::optional<torch::Tensor>& k_norm, double eps);
+
+// Paged attention.
+void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                            const torch::Tensor& block_table, const torch::Tensor& seq_lens, torch::Tensor& out,
+                            int64_t q_len, int64_t splits, torch::Tensor& workspace, double scale,
+                            const torch::Tensor& status);
+void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                             const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
+                             const torch::Tensor& cu_seqlens_q, const torch::Tensor& tile_seq,
+                             const torch::Tensor& tile_start, torch::Tensor& out, double scale, bool causal,
+                             const torch::Tensor& status);
+int64_t decode_attention_splits(int64_t batch, int64_t num_kv_heads, int64_t max_pages, int64_t device);
+
+// Sampling.
+void argmax_rows(const torch::Tensor& logits, torch::Tensor& out);
+void sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
+                 const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
+                 torch::Tensor& out);
+
+// Status word.
+torch::Tensor status_tensor(int64_t device);
+
+}  // namespace bloom

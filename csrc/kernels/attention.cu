@@ -1,0 +1,671 @@
+// Paged attention over the HBM-resident KV cache.
+//
+// Cache layout (one tensor per model): [L, NB, 2, KVH, 16, 128] bf16, i.e. a
+// 16-token page of one KV head is a contiguous 4 KiB block.  Pages are moved
+// with 2D TMA tiles (box 64 dims x 16 tokens, 128-byte swizzle) so the
+// ldmatrix reads that feed the tensor cores are bank-conflict free.
+//
+// Decode / speculative verify (q_len 1..8): one CTA per (sequence, KV head,
+// split); the q heads of a GQA group and the q positions of the request are
+// packed into the 16-row M dimension of m16n8k16 MMAs, so every KV page is
+// read from HBM exactly once per step.  Each warp streams its own pages
+// through a private TMA ring; warps and splits are merged flash-decoding style.
+// This op is HBM-bound (arithmetic intensity ~4 FLOP/B at GQA 4), so its
+// roofline is the page bytes at HBM bandwidth, not tensor throughput.
+//
+// Prefill (chunked, with cached prefix pages): FlashAttention-2 style, 64 query
+// rows per CTA, 64-token KV tiles (4 pages) double buffered through TMA.
+//
+// Reference behaviour: scheduler/paged_cache.rs:565-748 (host f32 SDPA with
+// repeat_kv), qwen_streaming.rs:413-424 (naive SDPA), causal + GQA semantics.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "bloom/common.cuh"
+#include "bloom/ops.h"
+#include "bloom/tma_host.h"
+
+namespace bloom {
+namespace attn {
+
+constexpr int D = 128;
+constexpr int PAGE = 16;
+constexpr float kNegBig = -1e30f;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Byte address of element (tok, d) (d multiple of 8) inside a page tile that
+// TMA wrote as two 2 KiB boxes (dims 0-63, 64-127) with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t page_addr(uint32_t base, int tok, int d) {
+  return base + ((d >> 6) << 11) + (tok << 7) + (((((d & 63) >> 3) ^ (tok & 7))) << 4);
+}
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;  // [B*ql, nq, 128]
+  __nv_bfloat16* out;      // [B*ql, nq, 128]
+  const int* block_table;
+  int bt_stride;
+  const int* seq_lens;  // kv length per sequence, including the ql new tokens
+  float* part;          // [B, nkv, splits, 32, 130] (o[128], m, l)
+  int nq, nkv, ql, splits;
+  float scale_log2;
+  int* status;
+};
+
+// Row r of the packed M dimension -> (q position qi, head-in-group hh).
+template <int MT, int NWARPS, int NST>
+__global__ void __launch_bounds__(NWARPS * 32)
+    decode_kernel(const __grid_constant__ CUtensorMap tmKV, const DecodeArgs a) {
+  constexpr int kStageBytes = 2 * PAGE * D * 2;  // K + V page = 8 KiB
+  const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
+  const int warp = warp_id(), lane = lane_id();
+  const int g = lane >> 2, t4 = lane & 3;
+  const int G = a.nq / a.nkv;
+  const int R = a.ql * G;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* wsm = smem + warp * NST * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NWARPS * NST * kStageBytes) + warp * NST;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
+
+  const int kv_len = a.seq_lens[b];
+  const int n_pages = (kv_len + PAGE - 1) / PAGE;
+  const int pps = (n_pages + a.splits - 1) / a.splits;
+  const int p0 = split * pps;
+  const int p1 = min(p0 + pps, n_pages);
+  const int first = p0 + warp;
+  const int my_n = (p1 > first) ? (p1 - first + NWARPS - 1) / NWARPS : 0;
+  const int* bt = a.block_table + (long)b * a.bt_stride;
+
+  if (lane == 0) {
+    for (int s = 0; s < NST; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int i) {
+    const int s = i % NST;
+    const int page = first + i * NWARPS;
+    const int blk = bt[page];
+    const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
+    const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
+    uint8_t* st = wsm + s * kStageBytes;
+    mbar_arrive_expect_tx(&bars[s], kStageBytes);
+    tma_load_2d(st, &tmKV, &bars[s], 0, rowK);
+    tma_load_2d(st + 2048, &tmKV, &bars[s], 64, rowK);
+    tma_load_2d(st + 4096, &tmKV, &bars[s], 0, rowV);
+    tma_load_2d(st + 6144, &tmKV, &bars[s], 64, rowV);
+  };
+  if (lane == 0) {
+    for (int i = 0; i < NST && i < my_n; ++i) issue(i);
+  }
+
+  // Q fragments (A operand), rows beyond R are zero.
+  uint32_t qf[MT][8][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = mt * 16 + g + 8 * hr;
+      const __nv_bfloat16* qrow = nullptr;
+      if (r < R) {
+        const int qi = r / G, hh = r - qi * G;
+        qrow = a.q + ((long)(b * a.ql + qi) * a.nq + kh * G + hh) * D;
+      }
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int d = ks * 16 + 2 * t4;
+        qf[mt][ks][hr] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
+        qf[mt][ks][hr + 2] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
+      }
+    }
+  }
+
+  float m_run[MT][2], l_run[MT][2];
+  float o[MT][16][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    m_run[mt][0] = m_run[mt][1] = kNegBig;
+    l_run[mt][0] = l_run[mt][1] = 0.f;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[mt][n][0] = o[mt][n][1] = o[mt][n][2] = o[mt][n][3] = 0.f;
+  }
+  // causal limit per packed row: kv index must be <= kv_len - ql + qi
+  int limit[MT][2];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = mt * 16 + g + 8 * hr;
+      limit[mt][hr] = (r < R) ? kv_len - a.ql + r / G : -1;
+    }
+
+  int i = 0;
+  for (; i < my_n; ++i) {
+    const int s = i % NST;
+    if (!mbar_wait(&bars[s], (i / NST) & 1, &abort_flag, a.status, kStatusAttnTimeout)) break;
+    const uint32_t sK = smem_u32(wsm + s * kStageBytes);
+    const uint32_t sV = sK + 4096;
+    const int tok_base = (first + i * NWARPS) * PAGE;
+
+    float sc[MT][2][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(page_addr(sK, 8 * nt + (lane & 7), 32 * j + 8 * (lane >> 3)), b0, b1, b2, b3);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          mma_bf16_16816(sc[mt][nt], qf[mt][2 * j], b0, b1);
+          mma_bf16_16816(sc[mt][nt], qf[mt][2 * j + 1], b2, b3);
+        }
+      }
+    }
+
+    uint32_t pa[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        float x[4];
+        float mx = kNegBig;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int idx = tok_base + 8 * nt + 2 * t4 + e;
+            float v = sc[mt][nt][2 * hr + e] * a.scale_log2;
+            if (idx > limit[mt][hr]) v = -INFINITY;
+            x[nt * 2 + e] = v;
+            mx = fmaxf(mx, v);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run[mt][hr], mx);
+        const float alpha = exp2f(m_run[mt][hr] - m_new);
+        m_run[mt][hr] = m_new;
+        float ps = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          x[k] = exp2f(x[k] - m_new);
+          ps += x[k];
+        }
+        l_run[mt][hr] = l_run[mt][hr] * alpha + ps;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          o[mt][n][2 * hr] *= alpha;
+          o[mt][n][2 * hr + 1] *= alpha;
+        }
+        // A fragment of P: [row g | row g+8] x [tokens 0-7 | 8-15]
+        pa[mt][hr] = pack_bf16(x[0], x[1]);      // tokens 2t4, 2t4+1 (n-tile 0)
+        pa[mt][hr + 2] = pack_bf16(x[2], x[3]);  // tokens 8+2t4.. (n-tile 1)
+      }
+    }
+
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(page_addr(sV, (lane & 7) + 8 * ((lane >> 3) & 1), 16 * j + 8 * (lane >> 4)), b0, b1, b2, b3);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        mma_bf16_16816(o[mt][2 * j], pa[mt], b0, b1);
+        mma_bf16_16816(o[mt][2 * j + 1], pa[mt], b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && i + NST < my_n) {
+      fence_proxy_async();
+      issue(i + NST);
+    }
+  }
+  if (i < my_n) {  // aborted: drain the loads this warp still has in flight
+    if (lane == 0)
+      for (int k = i; k < my_n && k < i + NST; ++k) mbar_drain(&bars[k % NST], (k / NST) & 1);
+  }
+
+  // finish row sums across the quad
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float l = l_run[mt][hr];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      l_run[mt][hr] = l;
+    }
+
+  __syncthreads();
+  // cross-warp merge through shared memory: per warp [MT*16 rows][128 o + m + l]
+  constexpr int RS = D + 2;
+  float* cm = reinterpret_cast<float*>(smem);
+  float* wbuf = cm + warp * (MT * 16 * RS);
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = mt * 16 + g + 8 * hr;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        wbuf[r * RS + 8 * n + 2 * t4] = o[mt][n][2 * hr];
+        wbuf[r * RS + 8 * n + 2 * t4 + 1] = o[mt][n][2 * hr + 1];
+      }
+      if (t4 == 0) {
+        wbuf[r * RS + D] = m_run[mt][hr];
+        wbuf[r * RS + D + 1] = l_run[mt][hr];
+      }
+    }
+  __syncthreads();
+  const int rows = min(R, MT * 16);
+  for (int idx = threadIdx.x; idx < rows * D; idx += NWARPS * 32) {
+    const int r = idx / D, d = idx - r * D;
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < NWARPS; ++w) M = fmaxf(M, cm[w * MT * 16 * RS + r * RS + D]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARPS; ++w) {
+      const float* wb = cm + w * MT * 16 * RS + r * RS;
+      const float sc = exp2f(wb[D] - M);
+      L += wb[D + 1] * sc;
+      O += wb[d] * sc;
+    }
+    if (a.splits == 1) {
+      const int qi = r / G, hh = r - qi * G;
+      a.out[((long)(b * a.ql + qi) * a.nq + kh * G + hh) * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+    } else {
+      float* pr = a.part + ((((long)b * a.nkv + kh) * a.splits + split) * 32 + r) * RS;
+      pr[d] = O;
+      if (d == 0) {
+        pr[D] = M;
+        pr[D + 1] = L;
+      }
+    }
+  }
+}
+
+__global__ void decode_combine_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ out, int nq,
+                                      int nkv, int ql, int splits) {
+  constexpr int RS = D + 2;
+  const int b = blockIdx.x, kh = blockIdx.y;
+  const int G = nq / nkv, R = ql * G;
+  const float* base = part + (((long)b * nkv + kh) * splits) * 32 * RS;
+  for (int idx = threadIdx.x; idx < R * D; idx += blockDim.x) {
+    const int r = idx / D, d = idx - r * D;
+    float M = kNegBig;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, base[((long)s * 32 + r) * RS + D]);
+    float L = 0.f, O = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float* pr = base + ((long)s * 32 + r) * RS;
+      const float sc = exp2f(pr[D] - M);
+      L += pr[D + 1] * sc;
+      O += pr[d] * sc;
+    }
+    const int qi = r / G, hh = r - qi * G;
+    out[((long)(b * ql + qi) * nq + kh * G + hh) * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------- prefill
+struct PrefillArgs {
+  const __nv_bfloat16* q;  // [T, nq, 128]
+  __nv_bfloat16* out;      // [T, nq, 128]
+  const int* block_table;
+  int bt_stride;
+  const int* ctx_lens;     // total kv length per sequence after this chunk
+  const int* cu_q;         // [S+1] query token offsets
+  const int* tile_seq;     // per work tile: sequence index
+  const int* tile_start;   // per work tile: first query row (local to the sequence)
+  int nq, nkv;
+  float scale_log2;
+  int causal;
+  int* status;
+};
+
+constexpr int kPfWarps = 4;
+constexpr int kPfRows = 16 * kPfWarps;  // 64 query rows per CTA
+constexpr int kPfKv = 64;               // kv tokens per tile (4 pages)
+constexpr int kPfStageBytes = 2 * kPfKv * D * 2;  // K + V = 32 KiB
+constexpr int kPfStages = 2;
+
+__global__ void __launch_bounds__(kPfWarps * 32)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmKV, const PrefillArgs a) {
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int warp = warp_id(), lane = lane_id();
+  const int g = lane >> 2, t4 = lane & 3;
+  const int G = a.nq / a.nkv;
+  const int kh = h / G;
+  const int s_idx = a.tile_seq[tile];
+  const int row0 = a.tile_start[tile];
+  const int q_begin = a.cu_q[s_idx];
+  const int q_len = a.cu_q[s_idx + 1] - q_begin;
+  const int ctx = a.ctx_lens[s_idx];
+  const int* bt = a.block_table + (long)s_idx * a.bt_stride;
+  const int n_pages = (ctx + PAGE - 1) / PAGE;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPfStages * kPfStageBytes);
+  __shared__ int abort_flag;
+
+  // kv range this tile needs
+  const int last_row = min(row0 + kPfRows, q_len) - 1;
+  const int kv_end = a.causal ? min(ctx, ctx - q_len + last_row + 1) : ctx;
+  const int n_kt = (kv_end + kPfKv - 1) / kPfKv;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kPfStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int kt) {
+    const int s = kt % kPfStages;
+    uint8_t* st = smem + s * kPfStageBytes;
+    mbar_arrive_expect_tx(&bars[s], kPfStageBytes);
+#pragma unroll
+    for (int pg = 0; pg < 4; ++pg) {
+      const int page = kt * 4 + pg;
+      const int blk = bt[page < n_pages ? page : 0];
+      const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
+      const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
+      tma_load_2d(st + pg * 4096, &tmKV, &bars[s], 0, rowK);
+      tma_load_2d(st + pg * 4096 + 2048, &tmKV, &bars[s], 64, rowK);
+      tma_load_2d(st + 16384 + pg * 4096, &tmKV, &bars[s], 0, rowV);
+      tma_load_2d(st + 16384 + pg * 4096 + 2048, &tmKV, &bars[s], 64, rowV);
+    }
+  };
+  if (threadIdx.x == 0)
+    for (int kt = 0; kt < kPfStages && kt < n_kt; ++kt) issue(kt);
+
+  // Q fragments for rows row0 + 16*warp + {g, g+8}
+  uint32_t qf[8][4];
+  int qpos[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int lr = row0 + 16 * warp + g + 8 * hr;
+    const bool valid = lr < q_len;
+    qpos[hr] = valid ? (a.causal ? ctx - q_len + lr : ctx - 1) : -1;
+    const __nv_bfloat16* qrow = valid ? a.q + ((long)(q_begin + lr) * a.nq + h) * D : nullptr;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int d = ks * 16 + 2 * t4;
+      qf[ks][hr] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
+      qf[ks][hr + 2] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
+    }
+  }
+
+  float m_run[2] = {kNegBig, kNegBig}, l_run[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+  int kt = 0;
+  bool ok = true;
+  for (; kt < n_kt; ++kt) {
+    const int s = kt % kPfStages;
+    if (!mbar_wait(&bars[s], (kt / kPfStages) & 1, &abort_flag, a.status, kStatusAttnTimeout)) {
+      ok = false;
+    }
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+    const uint32_t sK = smem_u32(smem + s * kPfStageBytes);
+    const uint32_t sV = sK + 16384;
+    const int kv0 = kt * kPfKv;
+    // skip whole tiles above the diagonal for this warp
+    const bool warp_active = (qpos[0] >= kv0) || (qpos[1] >= kv0);
+    if (__any_sync(0xffffffffu, warp_active)) {
+      float sc[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int tok = 8 * nt + (lane & 7);
+        const uint32_t pbase = sK + (tok >> 4) * 4096;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(page_addr(pbase, tok & 15, 32 * j + 8 * (lane >> 3)), b0, b1, b2, b3);
+          mma_bf16_16816(sc[nt], qf[2 * j], b0, b1);
+          mma_bf16_16816(sc[nt], qf[2 * j + 1], b2, b3);
+        }
+      }
+      uint32_t pa[4][4];
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        float mx = kNegBig;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int idx = kv0 + 8 * nt + 2 * t4 + e;
+            float v = sc[nt][2 * hr + e] * a.scale_log2;
+            if (idx > qpos[hr] || idx >= ctx) v = -INFINITY;
+            sc[nt][2 * hr + e] = v;
+            mx = fmaxf(mx, v);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run[hr], mx);
+        const float alpha = exp2f(m_run[hr] - m_new);
+        m_run[hr] = m_new;
+        float ps = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float p = exp2f(sc[nt][2 * hr + e] - m_new);
+            sc[nt][2 * hr + e] = p;
+            ps += p;
+          }
+        l_run[hr] = l_run[hr] * alpha + ps;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          o[n][2 * hr] *= alpha;
+          o[n][2 * hr + 1] *= alpha;
+        }
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        pa[kk][0] = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]);
+        pa[kk][1] = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
+        pa[kk][2] = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+        pa[kk][3] = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t pbase = sV + kk * 4096;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(page_addr(pbase, (lane & 7) + 8 * ((lane >> 3) & 1), 16 * j + 8 * (lane >> 4)), b0, b1, b2, b3);
+          mma_bf16_16816(o[2 * j], pa[kk], b0, b1);
+          mma_bf16_16816(o[2 * j + 1], pa[kk], b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && kt + kPfStages < n_kt) {
+      fence_proxy_async();
+      issue(kt + kPfStages);
+    }
+  }
+  if (!ok && threadIdx.x == 0) {
+    for (int k = kt; k < n_kt && k < kt + kPfStages; ++k) mbar_drain(&bars[k % kPfStages], (k / kPfStages) & 1);
+  }
+
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float l = l_run[hr];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const int lr = row0 + 16 * warp + g + 8 * hr;
+    if (lr < q_len && ok) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = a.out + ((long)(q_begin + lr) * a.nq + h) * D;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        *reinterpret_cast<uint32_t*>(orow + 8 * n + 2 * t4) = pack_bf16(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
+      }
+    }
+  }
+}
+
+CUtensorMap kv_tmap(const torch::Tensor& kv_cache, int64_t layer) {
+  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(2) == 2 && kv_cache.size(4) == PAGE && kv_cache.size(5) == D,
+              "kv_cache must be [L, NB, 2, KVH, 16, 128]");
+  TORCH_CHECK(kv_cache.is_contiguous() && kv_cache.scalar_type() == at::kBFloat16, "kv_cache contiguous bf16");
+  const uint64_t rows = (uint64_t)kv_cache.size(1) * 2 * kv_cache.size(3) * PAGE;
+  TORCH_CHECK(rows < (1ull << 31), "kv_cache too many rows per layer for int32 TMA coordinates");
+  const auto* base = reinterpret_cast<const __nv_bfloat16*>(kv_cache.data_ptr()) + layer * kv_cache.stride(0);
+  return make_tmap_bf16_2d(base, D, rows, D * 2, 64, PAGE);
+}
+
+template <int MT, int NWARPS, int NST>
+void launch_decode(const CUtensorMap& tm, const DecodeArgs& a, int B, cudaStream_t stream) {
+  constexpr int smem = NWARPS * NST * 8192 + NWARPS * NST * 8 + 1024;
+  static_assert(NWARPS * NST * 8192 >= NWARPS * MT * 16 * (D + 2) * 4, "merge buffer must fit in the stage ring");
+  auto kern = decode_kernel<MT, NWARPS, NST>;
+  static uint64_t configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((configured >> dev) & 1u)) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured |= uint64_t(1) << dev;
+  }
+  dim3 grid(B, a.nkv, a.splits);
+  kern<<<grid, NWARPS * 32, smem, stream>>>(tm, a);
+}
+
+}  // namespace attn
+
+int64_t decode_attention_splits(int64_t batch, int64_t num_kv_heads, int64_t max_pages, int64_t device) {
+  const int64_t ctas = batch * num_kv_heads;
+  const int64_t target = 2 * num_sms(int(device));
+  if (ctas >= target) return 1;
+  int64_t s = (target + ctas - 1) / ctas;
+  // at least 4 pages per warp-quad per split on long contexts
+  const int64_t max_s = std::max<int64_t>(1, max_pages / 8);
+  return std::max<int64_t>(1, std::min<int64_t>(s, std::min<int64_t>(max_s, 64)));
+}
+
+void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                            const torch::Tensor& block_table, const torch::Tensor& seq_lens, torch::Tensor& out,
+                            int64_t q_len, int64_t splits, torch::Tensor& workspace, double scale,
+                            const torch::Tensor& status) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(-1) == attn::D, "decode: q [T,nq,128]");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.stride(1) == 1, "decode: block_table int32");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt, "decode: seq_lens int32");
+  const int B = seq_lens.size(0);
+  if (B == 0) return;
+  const int nq = q.size(-2);
+  const int nkv = kv_cache.size(3);
+  TORCH_CHECK(nq % nkv == 0, "decode: nq must be a multiple of nkv");
+  const int G = nq / nkv;
+  TORCH_CHECK(q_len >= 1 && G * q_len <= 32, "decode: (q heads per kv head) * q_len must be <= 32");
+  TORCH_CHECK(q.numel() / (nq * attn::D) == B * q_len, "decode: q rows must equal batch * q_len");
+  const at::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+
+  attn::DecodeArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_stride = block_table.stride(0);
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.nq = nq;
+  a.nkv = nkv;
+  a.ql = int(q_len);
+  a.splits = std::max<int>(1, int(splits));
+  a.scale_log2 = float(scale * 1.4426950408889634);
+  a.status = status.data_ptr<int>();
+  a.part = nullptr;
+  if (a.splits > 1) {
+    TORCH_CHECK(workspace.scalar_type() == at::kFloat &&
+                    workspace.numel() >= (int64_t)B * nkv * a.splits * 32 * (attn::D + 2),
+                "decode: workspace too small");
+    a.part = workspace.data_ptr<float>();
+  }
+  const CUtensorMap tm = attn::kv_tmap(kv_cache, layer);
+  if (G * q_len <= 16)
+    attn::launch_decode<1, 4, 3>(tm, a, B, stream);
+  else
+    attn::launch_decode<2, 4, 3>(tm, a, B, stream);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (a.splits > 1) {
+    attn::decode_combine_kernel<<<dim3(B, nkv), 256, 0, stream>>>(a.part, a.out, nq, nkv, a.ql, a.splits);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                             const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
+                             const torch::Tensor& cu_seqlens_q, const torch::Tensor& tile_seq,
+                             const torch::Tensor& tile_start, torch::Tensor& out, double scale, bool causal,
+                             const torch::Tensor& status) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(-1) == attn::D, "prefill: q [T,nq,128]");
+  const int n_tiles = tile_seq.size(0);
+  if (n_tiles == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  attn::PrefillArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_stride = block_table.stride(0);
+  a.ctx_lens = ctx_lens.data_ptr<int>();
+  a.cu_q = cu_seqlens_q.data_ptr<int>();
+  a.tile_seq = tile_seq.data_ptr<int>();
+  a.tile_start = tile_start.data_ptr<int>();
+  a.nq = q.size(-2);
+  a.nkv = kv_cache.size(3);
+  a.scale_log2 = float(scale * 1.4426950408889634);
+  a.causal = causal ? 1 : 0;
+  a.status = status.data_ptr<int>();
+  const CUtensorMap tm = attn::kv_tmap(kv_cache, layer);
+  constexpr int smem = attn::kPfStages * attn::kPfStageBytes + 64 + 1024;
+  static uint64_t configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((configured >> dev) & 1u)) {
+    cudaFuncSetAttribute(attn::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured |= uint64_t(1) << dev;
+  }
+  attn::prefill_kernel<<<dim3(n_tiles, a.nq), attn::kPfWarps * 32, smem, stream>>>(tm, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bloom

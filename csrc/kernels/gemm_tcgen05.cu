@@ -1,0 +1,411 @@
+// Dense bf16 GEMM on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+//   y[M, N] = x[M, K] @ w[N, K]^T        (nn.Linear layout, both K-major)
+//
+// The UMMA "A" operand is the weight tile (128 output features = UMMA M) and
+// the "B" operand is the token tile (BN tokens = UMMA N, 16..256).  Putting the
+// features on the 128-lane M side keeps tiny decode batches (M = 1..256
+// tokens) on the tensor cores with no padding of the token dimension beyond a
+// multiple of 16, and the same kernel covers large prefill batches with
+// 128 x 256 tiles.  The accumulator lives in TMEM (lane = feature, column =
+// token) and is double-buffered so the epilogue of tile i overlaps the MMAs of
+// tile i+1.
+//
+// Warp roles (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocator + UMMA issuer (one elected lane)
+//   warps 2..5  epilogue: tcgen05.ld of their TMEM lane quarter, fused
+//               epilogue (bias / SwiGLU / residual / fp32 split-K partials)
+//
+// Replaces the reference's library GEMMs behind candle Linear layers
+// (crates/engine/src/executor/qwen_streaming.rs:216-298, candle-transformers
+// llama/qwen2/qwen3), which never had an sm_100 code path.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "bloom/common.cuh"
+#include "bloom/ops.h"
+#include "bloom/tma_host.h"
+
+namespace bloom {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+struct Args {
+  int M, N, K;
+  int num_feat_tiles, num_tok_tiles, splits, kb_per_split, num_kb;
+  void* out;
+  long ldo;
+  const __nv_bfloat16* resid;
+  long ldr;
+  const __nv_bfloat16* bias;
+  int* status;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+};
+
+__device__ __forceinline__ void decode_tile(const Args& a, int t, int& feat_tile, int& tok_tile, int& split) {
+  split = t % a.splits;
+  const int rest = t / a.splits;
+  tok_tile = rest % a.num_tok_tiles;
+  feat_tile = rest / a.num_tok_tiles;
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const Args& a, uint32_t taddr, int feat_tile, int tok_tile, int split,
+                                              int row, int lane) {
+  const int tok0 = tok_tile * BN;
+  if constexpr (EPI == kEpiSwiGLU) {
+    // Weight rows are interleaved per 32-row group: 16 gate rows then the 16
+    // matching up rows, so gate and up of one feature sit in lanes l and l+16.
+    const int nout = a.N / 2;
+    const int f = feat_tile * (BM / 2) + (row >> 5) * 16 + (row & 15);
+    const bool writer = (lane < 16) && (f < nout);
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    for (int c = 0; c < BN; c += 16) {
+      if (tok0 + c >= a.M) break;
+      float v[16];
+      tmem_ld_32x32b_x16(taddr + c, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float up = __shfl_down_sync(0xffffffffu, v[j], 16);
+        const int tok = tok0 + c + j;
+        if (writer && tok < a.M) out[(long)tok * a.ldo + f] = __float2bfloat16(silu(v[j]) * up);
+      }
+    }
+  } else {
+    const int f = feat_tile * BM + row;
+    const bool fvalid = f < a.N;
+    float bias = 0.f;
+    if constexpr (EPI == kEpiBF16 || EPI == kEpiF32) {
+      if (a.bias != nullptr && fvalid) bias = __bfloat162float(a.bias[f]);
+    }
+    for (int c = 0; c < BN; c += 16) {
+      if (tok0 + c >= a.M) break;
+      float v[16];
+      tmem_ld_32x32b_x16(taddr + c, v);
+      tmem_wait_ld();
+      if (!fvalid) continue;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int tok = tok0 + c + j;
+        if (tok >= a.M) break;
+        if constexpr (EPI == kEpiBF16) {
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] = __float2bfloat16(v[j] + bias);
+        } else if constexpr (EPI == kEpiF32) {
+          reinterpret_cast<float*>(a.out)[(long)tok * a.ldo + f] = v[j] + bias;
+        } else if constexpr (EPI == kEpiPartialF32) {
+          reinterpret_cast<float*>(a.out)[((long)split * a.M + tok) * a.N + f] = v[j];
+        } else if constexpr (EPI == kEpiResidual) {
+          const float r = __bfloat162float(a.resid[(long)tok * a.ldr + f]);
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] = __float2bfloat16(v[j] + r);
+        }
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args a) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::kStages * C::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C::kStages * C::kBBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::kStages;
+  uint64_t* tfull = bars + 2 * C::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = a.num_feat_tiles * a.num_tok_tiles * a.splits;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int ft, tt, sp;
+        decode_tile(a, t, ft, tt, sp);
+        const int kb0 = sp * a.kb_per_split;
+        const int kb1 = min(kb0 + a.kb_per_split, a.num_kb);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.status, kStatusGemmTimeout)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          tma_load_2d_hint(sA + stage * C::kABytes, &tmA, &full[stage], kb * BK, ft * BM, pol_w);
+          tma_load_2d_hint(sB + stage * C::kBBytes, &tmB, &full[stage], kb * BK, tt * BN, pol_x);
+          issued_mask |= 1u << stage;
+          issued_par = phase ? (issued_par | (1u << stage)) : (issued_par & ~(1u << stage));
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < C::kStages; ++s)
+          if ((issued_mask >> s) & 1u) mbar_drain(&full[s], (issued_par >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued_any = false;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int ft, tt, sp;
+        decode_tile(a, t, ft, tt, sp);
+        const int kb0 = sp * a.kb_per_split;
+        const int kb1 = min(kb0 + a.kb_per_split, a.num_kb);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, a.status, kStatusGemmTimeout)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, a.status, kStatusGemmTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * C::kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * C::kBBytes));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // advance 16 bf16 = 32 bytes along K inside the 128-byte swizzle atom
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok && issued_any) {
+        umma_commit(drain);
+        mbar_drain(drain, 0);
+      }
+    }
+  } else {
+    const int q = warp & 3;  // a warp may only touch TMEM lanes [32*(warp%4), +32)
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      int ft, tt, sp;
+      decode_tile(a, t, ft, tt, sp);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status, kStatusGemmTimeout)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      epilogue_tile<BN, EPI>(a, taddr, ft, tt, sp, row, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+template <int BN, int EPI>
+void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, int grid, cudaStream_t stream) {
+  auto kern = gemm_tn_kernel<BN, EPI>;
+  static uint64_t configured = 0;  // one bit per device, per template instantiation
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((configured >> dev) & 1u)) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
+    configured |= uint64_t(1) << dev;
+  }
+  kern<<<grid, 192, Cfg<BN>::kSmem, stream>>>(tmA, tmB, a);
+}
+
+template <int EPI>
+void dispatch_bn(int bn, const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, int grid, cudaStream_t s) {
+  switch (bn) {
+    case 16: launch<16, EPI>(tmA, tmB, a, grid, s); break;
+    case 32: launch<32, EPI>(tmA, tmB, a, grid, s); break;
+    case 64: launch<64, EPI>(tmA, tmB, a, grid, s); break;
+    case 128: launch<128, EPI>(tmA, tmB, a, grid, s); break;
+    default: launch<256, EPI>(tmA, tmB, a, grid, s); break;
+  }
+}
+
+}  // namespace gemm
+
+int gemm_pick_bn(int M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+int gemm_tiles(int M, int N, int epi) {
+  const int bn = gemm_pick_bn(M);
+  const int ntok = (M + bn - 1) / bn;
+  const int nrows = N;  // SwiGLU: N counts interleaved gate+up rows
+  (void)epi;
+  return ntok * ((nrows + gemm::BM - 1) / gemm::BM);
+}
+
+int gemm_default_splits(int M, int N, int K, int device) {
+  const int tiles = gemm_tiles(M, N, kEpiPartialF32);
+  const int num_kb = (K + gemm::BK - 1) / gemm::BK;
+  const int sms = num_sms(device);
+  if (tiles >= sms) return 1;
+  int splits = (sms + tiles - 1) / tiles;
+  splits = std::min(splits, std::max(1, num_kb / 4));
+  return std::max(1, std::min(splits, 16));
+}
+
+void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
+              const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
+              const torch::Tensor& status) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "gemm: tensors must be on CUDA");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: x and w must be bf16");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm: x [M,K], w [N,K]");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm: inner dim must be contiguous");
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "gemm: K mismatch");
+  TORCH_CHECK(K % 8 == 0, "gemm: K must be a multiple of 8");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+
+  const int bn = gemm_pick_bn(M);
+  gemm::Args a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.num_kb = (K + gemm::BK - 1) / gemm::BK;
+  a.num_feat_tiles = (N + gemm::BM - 1) / gemm::BM;
+  a.num_tok_tiles = (M + bn - 1) / bn;
+  a.splits = 1;
+  a.kb_per_split = a.num_kb;
+  a.out = out.data_ptr();
+  a.ldo = out.dim() >= 2 ? out.stride(out.dim() - 2) : N;
+  a.resid = nullptr;
+  a.ldr = 0;
+  a.bias = nullptr;
+  a.status = status.data_ptr<int>();
+
+  switch (epi) {
+    case kEpiBF16:
+      TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(-1) == N, "gemm: out must be bf16 [M,N]");
+      break;
+    case kEpiF32:
+      TORCH_CHECK(out.scalar_type() == at::kFloat && out.size(-1) == N, "gemm: out must be f32 [M,N]");
+      break;
+    case kEpiSwiGLU:
+      TORCH_CHECK(N % 32 == 0, "gemm swiglu: interleaved N must be a multiple of 32");
+      TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(-1) == N / 2, "gemm swiglu: out [M, N/2] bf16");
+      break;
+    case kEpiPartialF32: {
+      TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous(), "gemm partial: out must be contiguous f32");
+      int s = splits > 0 ? int(splits) : 1;
+      s = std::min(s, a.num_kb);
+      a.kb_per_split = (a.num_kb + s - 1) / s;
+      a.splits = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;
+      TORCH_CHECK(out.numel() >= (int64_t)a.splits * M * N, "gemm partial: workspace too small");
+      TORCH_CHECK(a.splits == s, "gemm partial: split count ", s, " not realisable for K=", K);
+      break;
+    }
+    case kEpiResidual:
+      TORCH_CHECK(resid.has_value(), "gemm residual epilogue needs resid");
+      TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(-1) == N, "gemm: out must be bf16 [M,N]");
+      a.resid = reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr());
+      a.ldr = resid->stride(0);
+      break;
+    default:
+      TORCH_CHECK(false, "gemm: unknown epilogue ", epi);
+  }
+  if (bias.has_value() && bias->defined()) {
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N, "gemm: bias must be bf16 [N]");
+    a.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+
+  const CUtensorMap tmA = make_tmap_bf16_2d(w.data_ptr(), K, N, w.stride(0) * 2, gemm::BK, gemm::BM);
+  const CUtensorMap tmB = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, bn);
+  const int total = a.num_feat_tiles * a.num_tok_tiles * a.splits;
+  const int grid = std::min(total, num_sms(x.get_device()));
+  switch (epi) {
+    case kEpiBF16: gemm::dispatch_bn<kEpiBF16>(bn, tmA, tmB, a, grid, stream); break;
+    case kEpiF32: gemm::dispatch_bn<kEpiF32>(bn, tmA, tmB, a, grid, stream); break;
+    case kEpiSwiGLU: gemm::dispatch_bn<kEpiSwiGLU>(bn, tmA, tmB, a, grid, stream); break;
+    case kEpiPartialF32: gemm::dispatch_bn<kEpiPartialF32>(bn, tmA, tmB, a, grid, stream); break;
+    case kEpiResidual: gemm::dispatch_bn<kEpiResidual>(bn, tmA, tmB, a, grid, stream); break;
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bloom

@@ -1,0 +1,287 @@
+// Memory-bound per-token kernels: RMSNorm (with fused residual add and fused
+// split-K reduction), LayerNorm (BERT), embedding gather, and RoPE fused with
+// the paged KV-cache write.
+//
+// Reference behaviour: RMSNorm qwen_streaming.rs:300-324, rotary
+// qwen_streaming.rs:74-116,387 (HF rotate_half convention), KV append
+// qwen_streaming.rs:394-409 / paged write scheduler/paged_cache.rs:208-308
+// (host f32 blocks there; HBM-resident bf16 pages here).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "bloom/common.cuh"
+#include "bloom/ops.h"
+
+namespace bloom {
+
+namespace {
+
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float t = (threadIdx.x < nw) ? red[threadIdx.x] : 0.f;
+  if (w == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[32] = t;
+  __syncthreads();
+  const float r = red[32];
+  __syncthreads();
+  return r;
+}
+
+// x: [M, H] bf16 (row stride ldx), out [M, H] (row stride ldo)
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long ldx, const __nv_bfloat16* __restrict__ w,
+                               __nv_bfloat16* __restrict__ out, long ldo, int H, float eps) {
+  extern __shared__ float buf[];  // H floats
+  __shared__ float red[33];
+  const long row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = __bfloat162float(xr[i]);
+    buf[i] = v;
+    ss += v * v;
+  }
+  const float tot = block_sum(ss, red);
+  const float inv = rsqrtf(tot / H + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    out[row * ldo + i] = __float2bfloat16(buf[i] * inv * __bfloat162float(w[i]));
+}
+
+// residual[M,H] += delta (bf16 [M,H] or f32 partials [S,M,H]); out = rmsnorm(residual) * w
+template <bool kF32Partials>
+__global__ void add_rmsnorm_kernel(const void* __restrict__ delta, int S, long ldd, __nv_bfloat16* __restrict__ resid,
+                                   long ldr, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                   long ldo, int M, int H, float eps) {
+  extern __shared__ float buf[];
+  __shared__ float red[33];
+  const long row = blockIdx.x;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float d;
+    if constexpr (kF32Partials) {
+      const float* dp = reinterpret_cast<const float*>(delta);
+      d = 0.f;
+      for (int s = 0; s < S; ++s) d += dp[((long)s * M + row) * H + i];
+    } else {
+      d = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(delta)[row * ldd + i]);
+    }
+    // the residual stream is stored in bf16 (as the checkpoint's dtype)
+    const __nv_bfloat16 nb = __float2bfloat16(__bfloat162float(resid[row * ldr + i]) + d);
+    resid[row * ldr + i] = nb;
+    const float v = __bfloat162float(nb);
+    buf[i] = v;
+    ss += v * v;
+  }
+  const float tot = block_sum(ss, red);
+  const float inv = rsqrtf(tot / H + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    out[row * ldo + i] = __float2bfloat16(buf[i] * inv * __bfloat162float(w[i]));
+}
+
+// LayerNorm with optional residual input (x + resid), affine.
+__global__ void layernorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
+                                 const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b,
+                                 __nv_bfloat16* __restrict__ out, int H, float eps) {
+  extern __shared__ float buf[];
+  __shared__ float red[33];
+  const long row = blockIdx.x;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float v = __bfloat162float(x[row * H + i]);
+    if (r != nullptr) v += __bfloat162float(r[row * H + i]);
+    buf[i] = v;
+    s += v;
+  }
+  const float mean = block_sum(s, red) / H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float d = buf[i] - mean;
+    ss += d * d;
+  }
+  const float inv = rsqrtf(block_sum(ss, red) / H + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    out[row * H + i] =
+        __float2bfloat16((buf[i] - mean) * inv * __bfloat162float(w[i]) + __bfloat162float(b[i]));
+}
+
+__global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, long V,
+                                 int H, __nv_bfloat16* __restrict__ out) {
+  const long t = blockIdx.x;
+  const long id = ids[t];
+  const bool ok = id >= 0 && id < V;
+  // 16-byte vectors when H is a multiple of 8
+  if ((H & 7) == 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(table + (ok ? id : 0) * H);
+    uint4* dst = reinterpret_cast<uint4*>(out + t * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = ok ? src[i] : make_uint4(0, 0, 0, 0);
+  } else {
+    for (int i = threadIdx.x; i < H; i += blockDim.x)
+      out[t * H + i] = ok ? table[id * H + i] : __float2bfloat16(0.f);
+  }
+}
+
+// One warp per head.  Lane l owns dims {l, l+32, l+64, l+96} of a 128-dim
+// head, so the rotate_half pairs (d, d+64) stay inside the lane.
+// qkv row layout: [q heads | k heads | v heads] x 128.
+// cos_sin: [max_pos, 128] f32 = [cos(0..63) | sin(0..63)].
+// kv cache: [L, NB, 2, KVH, 16, 128].
+__global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, long ldq, const int64_t* __restrict__ pos,
+                                     const int* __restrict__ slots, const float* __restrict__ cos_sin,
+                                     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
+                                     long layer_stride, int nq, int nkv, const __nv_bfloat16* __restrict__ qn,
+                                     const __nv_bfloat16* __restrict__ kn, float eps) {
+  constexpr int D = 128;
+  const long t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const long p = pos[t];
+  const int slot = slots != nullptr ? slots[t] : -1;
+  const float* cs = cos_sin + p * D;
+  const __nv_bfloat16* row = qkv + t * ldq;
+  for (int h = warp; h < nq + 2 * nkv; h += nwarps) {
+    const __nv_bfloat16* src = row + (long)h * D;
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(src[lane + 32 * i]);
+    const bool is_q = h < nq;
+    const bool is_k = !is_q && h < nq + nkv;
+    if (is_q || is_k) {
+      const __nv_bfloat16* nw = is_q ? qn : kn;
+      if (nw != nullptr) {
+        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / D + eps);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = v[i] * inv * __bfloat162float(nw[lane + 32 * i]);
+      }
+      // pairs (lane, lane+64) and (lane+32, lane+96)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int d = lane + 32 * i;
+        const float c = cs[d], s = cs[64 + d];
+        const float x1 = v[i], x2 = v[i + 2];
+        v[i] = x1 * c - x2 * s;
+        v[i + 2] = x2 * c + x1 * s;
+      }
+    }
+    if (is_q) {
+      __nv_bfloat16* dst = q_out + (t * nq + h) * D;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
+    } else if (slot >= 0) {
+      const int kvsel = is_k ? 0 : 1;
+      const int kh = is_k ? h - nq : h - nq - nkv;
+      const long blk = slot >> 4, off = slot & 15;
+      __nv_bfloat16* dst = cache + layer_stride + (((blk * 2 + kvsel) * nkv + kh) * 16 + off) * D;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
+    }
+  }
+}
+
+}  // namespace
+
+void rmsnorm(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, double eps) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "rmsnorm: x bf16 [M,H]");
+  const int M = x.size(0), H = x.size(1);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  rmsnorm_kernel<<<M, kNormThreads, H * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+      out.stride(0), H, float(eps));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void add_rmsnorm(const torch::Tensor& delta, torch::Tensor& residual, const torch::Tensor& w, torch::Tensor& out,
+                 double eps) {
+  TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.dim() == 2, "add_rmsnorm: residual bf16 [M,H]");
+  const int M = residual.size(0), H = residual.size(1);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard g(residual.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const size_t sm = H * sizeof(float);
+  if (delta.scalar_type() == at::kFloat) {
+    TORCH_CHECK(delta.is_contiguous() && delta.numel() % ((int64_t)M * H) == 0, "add_rmsnorm: f32 partials [S,M,H]");
+    const int S = delta.numel() / ((int64_t)M * H);
+    add_rmsnorm_kernel<true><<<M, kNormThreads, sm, stream>>>(
+        delta.data_ptr(), S, H, reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), residual.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+        out.stride(0), M, H, float(eps));
+  } else {
+    TORCH_CHECK(delta.scalar_type() == at::kBFloat16 && delta.stride(1) == 1, "add_rmsnorm: delta bf16 [M,H]");
+    add_rmsnorm_kernel<false><<<M, kNormThreads, sm, stream>>>(
+        delta.data_ptr(), 1, delta.stride(0), reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
+        residual.stride(0), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), M, H, float(eps));
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void layernorm(const torch::Tensor& x, const c10::optional<torch::Tensor>& resid, const torch::Tensor& w,
+               const torch::Tensor& b, torch::Tensor& out, double eps) {
+  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16, "layernorm: x contiguous bf16");
+  const int H = x.size(-1);
+  const int M = x.numel() / H;
+  if (M == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  const __nv_bfloat16* r = nullptr;
+  if (resid.has_value() && resid->defined()) {
+    TORCH_CHECK(resid->is_contiguous() && resid->numel() == x.numel(), "layernorm: resid shape");
+    r = reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr());
+  }
+  layernorm_kernel<<<M, kNormThreads, H * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), r, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H,
+      float(eps));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embedding(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out) {
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "embedding: ids int32");
+  TORCH_CHECK(table.scalar_type() == at::kBFloat16 && table.is_contiguous(), "embedding: table bf16");
+  const int T = ids.numel();
+  if (T == 0) return;
+  const at::cuda::CUDAGuard g(ids.device());
+  embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), table.size(0), table.size(1),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_kv_write(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& slot_mapping,
+                   const torch::Tensor& cos_sin, torch::Tensor& q_out, torch::Tensor& kv_cache, int64_t layer,
+                   int64_t num_q_heads, int64_t num_kv_heads, const c10::optional<torch::Tensor>& q_norm,
+                   const c10::optional<torch::Tensor>& k_norm, double eps) {
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "rope: qkv bf16 [T, *]");
+  TORCH_CHECK(qkv.size(1) >= (num_q_heads + 2 * num_kv_heads) * 128, "rope: head_dim must be 128");
+  TORCH_CHECK(positions.scalar_type() == at::kLong, "rope: positions int64");
+  TORCH_CHECK(slot_mapping.scalar_type() == at::kInt, "rope: slot_mapping int32");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == 128, "rope: cos_sin f32 [P,128]");
+  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(5) == 128 && kv_cache.size(3) == num_kv_heads,
+              "rope: kv_cache [L,NB,2,KVH,16,128]");
+  const int T = qkv.size(0);
+  if (T == 0) return;
+  const at::cuda::CUDAGuard g(qkv.device());
+  const long layer_stride = layer * kv_cache.stride(0);
+  const __nv_bfloat16* qn = (q_norm.has_value() && q_norm->defined())
+                                ? reinterpret_cast<const __nv_bfloat16*>(q_norm->data_ptr())
+                                : nullptr;
+  const __nv_bfloat16* kn = (k_norm.has_value() && k_norm->defined())
+                                ? reinterpret_cast<const __nv_bfloat16*>(k_norm->data_ptr())
+                                : nullptr;
+  rope_kv_write_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),
+      slot_mapping.data_ptr<int>(), cos_sin.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(kv_cache.data_ptr()), layer_stride, int(num_q_heads), int(num_kv_heads), qn,
+      kn, float(eps));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bloom

@@ -1,0 +1,367 @@
+#include "scheduler.h"
+
+#include <algorithm>
+#include <stdexcept>
+
+namespace bloom {
+namespace rt {
+
+Scheduler::Scheduler(const SchedulerConfig& cfg, int num_blocks, int block_size, bool prefix_caching)
+    : cfg_(cfg), bm_(num_blocks, block_size, prefix_caching) {}
+
+int64_t Scheduler::add_request(const std::vector<int32_t>& prompt, const SamplingParams& sp, int priority) {
+  if (prompt.empty()) throw std::invalid_argument("add_request: empty prompt");
+  if (static_cast<int>(prompt.size()) >= cfg_.max_model_len)
+    throw std::invalid_argument("add_request: prompt longer than max_model_len");
+  auto s = std::make_unique<Sequence>();
+  s->id = next_id_++;
+  s->tokens = prompt;
+  s->num_prompt = static_cast<int>(prompt.size());
+  s->sp = sp;
+  s->priority = priority;
+  s->order = next_order_++;
+  Sequence* p = s.get();
+  seqs_[p->id] = std::move(s);
+  // higher priority first, FCFS inside a priority class
+  auto it = waiting_.end();
+  while (it != waiting_.begin() && (*(it - 1))->priority < priority) --it;
+  waiting_.insert(it, p);
+  return p->id;
+}
+
+const Sequence* Scheduler::find(int64_t id) const {
+  auto it = seqs_.find(id);
+  return it == seqs_.end() ? nullptr : it->second.get();
+}
+
+void Scheduler::finish(Sequence* s, FinishReason r) {
+  s->status = SeqStatus::Finished;
+  s->finish = r;
+  bm_.release(s->table, s->hashes);
+}
+
+bool Scheduler::abort(int64_t id) {
+  auto it = seqs_.find(id);
+  if (it == seqs_.end()) return false;
+  Sequence* s = it->second.get();
+  if (s->status == SeqStatus::Finished) return false;
+  waiting_.erase(std::remove(waiting_.begin(), waiting_.end(), s), waiting_.end());
+  running_.erase(std::remove(running_.begin(), running_.end(), s), running_.end());
+  finish(s, FinishReason::Aborted);
+  seqs_.erase(it);
+  return true;
+}
+
+void Scheduler::preempt(Sequence* s) {
+  running_.erase(std::remove(running_.begin(), running_.end(), s), running_.end());
+  bm_.release(s->table, s->hashes);
+  s->num_computed = 0;
+  s->status = SeqStatus::Waiting;
+  ++s->num_preemptions;
+  ++total_preemptions_;
+  waiting_.push_front(s);
+}
+
+bool Scheduler::is_stop(const Sequence& s, int32_t tok) const {
+  if (s.num_generated() >= s.sp.max_tokens) return true;
+  if (static_cast<int>(s.tokens.size()) >= cfg_.max_model_len) return true;
+  if (s.num_generated() < s.sp.min_tokens) return false;
+  if (!s.sp.ignore_eos)
+    for (int32_t e : cfg_.eos_token_ids)
+      if (tok == e) return true;
+  for (int32_t e : s.sp.stop_token_ids)
+    if (tok == e) return true;
+  return false;
+}
+
+StepMeta Scheduler::schedule() {
+  if (arena_.base == nullptr) throw std::runtime_error("Scheduler: arena not set");
+  StepMeta m;
+  const int bs = bm_.block_size();
+  int budget = std::min(cfg_.max_num_batched_tokens, arena_.max_tokens);
+  last_sampling_.clear();
+  last_scheduled_.clear();
+
+  struct Prefill {
+    Sequence* s;
+    int start;
+    int len;
+  };
+  std::vector<Sequence*> decodes;
+  std::vector<Prefill> prefills;
+
+  // 1) decode rows: running sequences that need exactly their last token computed.
+  const std::vector<Sequence*> snapshot = running_;
+  for (Sequence* s : snapshot) {
+    if (s->status != SeqStatus::Running) continue;  // preempted earlier in this loop
+    const int need = static_cast<int>(s->tokens.size()) - s->num_computed;
+    if (need != 1) continue;
+    if (budget <= 0 || static_cast<int>(decodes.size()) >= arena_.max_seqs) break;
+    bool ok = bm_.ensure_capacity(s->table, s->num_computed + 1);
+    while (!ok) {
+      // preempt the most recently admitted running sequence not yet scheduled
+      Sequence* victim = nullptr;
+      for (auto it = running_.rbegin(); it != running_.rend(); ++it)
+        if (*it != s && std::find(decodes.begin(), decodes.end(), *it) == decodes.end()) {
+          victim = *it;
+          break;
+        }
+      if (victim == nullptr) break;
+      preempt(victim);
+      ++m.num_preempted;
+      ok = bm_.ensure_capacity(s->table, s->num_computed + 1);
+    }
+    if (!ok) {
+      preempt(s);
+      ++m.num_preempted;
+      continue;
+    }
+    decodes.push_back(s);
+    budget -= 1;
+  }
+
+  // 2) partially prefilled running sequences (chunked prefill continues)
+  for (Sequence* s : running_) {
+    const int need = static_cast<int>(s->tokens.size()) - s->num_computed;
+    if (need <= 1) continue;
+    if (budget <= 0 || static_cast<int>(prefills.size()) + static_cast<int>(decodes.size()) >= arena_.max_seqs) break;
+    const int len = cfg_.chunked_prefill ? std::min(need, budget) : need;
+    if (len > budget) break;
+    if (!bm_.ensure_capacity(s->table, s->num_computed + len)) break;
+    prefills.push_back({s, s->num_computed, len});
+    budget -= len;
+  }
+
+  // 3) admit waiting sequences
+  while (!waiting_.empty() && budget > 0 && static_cast<int>(running_.size()) < cfg_.max_num_seqs &&
+         static_cast<int>(prefills.size()) + static_cast<int>(decodes.size()) < arena_.max_seqs) {
+    Sequence* s = waiting_.front();
+    if (s->table.empty()) {
+      // prefix reuse: whole cached blocks, always leaving the last token to compute
+      const int max_cached = ((static_cast<int>(s->tokens.size()) - 1) / bs) * bs;
+      s->num_computed = bm_.match_prefix(s->tokens, max_cached, s->table, s->hashes);
+      if (!s->admitted_once) s->num_cached_prefix = s->num_computed;
+    }
+    const int need = static_cast<int>(s->tokens.size()) - s->num_computed;
+    int len = cfg_.chunked_prefill ? std::min(need, budget) : need;
+    if (len > budget) break;
+    if (!bm_.ensure_capacity(s->table, s->num_computed + len)) {
+      if (running_.empty() && decodes.empty() && prefills.empty()) {
+        // nothing else holds blocks: this request can never fit
+        waiting_.pop_front();
+        finish(s, FinishReason::Length);
+        continue;
+      }
+      break;
+    }
+    waiting_.pop_front();
+    s->status = SeqStatus::Running;
+    s->admitted_once = true;
+    running_.push_back(s);
+    if (len == 1 && need == 1) {
+      decodes.push_back(s);
+    } else {
+      prefills.push_back({s, s->num_computed, len});
+    }
+    budget -= len;
+  }
+
+  // ---- layout (decode-only steps padded to a bucket)
+  int Bd = static_cast<int>(decodes.size());
+  const int real_decode = Bd;
+  int T_pref = 0;
+  for (auto& p : prefills) T_pref += p.len;
+  int ntiles = 0;
+  for (auto& p : prefills) ntiles += (p.len + 63) / 64;
+  int nl_real = Bd;
+  for (auto& p : prefills)
+    if (p.start + p.len == static_cast<int>(p.s->tokens.size())) ++nl_real;
+  if (prefills.empty() && Bd > 0) {
+    for (int b : buckets_)
+      if (b >= Bd) {
+        Bd = std::min(b, arena_.max_seqs);
+        break;
+      }
+  }
+  const int T = Bd + T_pref;
+  const int NL = nl_real + (Bd - real_decode);
+  const int mb = arena_.max_blocks;
+  m = [&] {
+    StepMeta lay = arena_layout(T, Bd, static_cast<int>(prefills.size()), ntiles, NL, mb);
+    lay.num_preempted = m.num_preempted;
+    return lay;
+  }();
+  if (m.used_words > arena_.capacity) throw std::runtime_error("Scheduler: step does not fit in the arena");
+  int32_t* A = arena_.base;
+  int32_t* input_ids = A + m.off_input_ids;
+  int32_t* slots = A + m.off_slot_mapping;
+  int64_t* positions = reinterpret_cast<int64_t*>(A + m.off_positions);
+  int32_t* dsl = A + m.off_decode_seq_lens;
+  int32_t* dbt = A + m.off_decode_block_table;
+  int32_t* pctx = A + m.off_prefill_ctx_lens;
+  int32_t* pcu = A + m.off_prefill_cu_q;
+  int32_t* pbt = A + m.off_prefill_block_table;
+  int32_t* tseq = A + m.off_tile_seq;
+  int32_t* tstart = A + m.off_tile_start;
+  int32_t* lrows = A + m.off_logits_rows;
+  int32_t* topk = A + m.off_top_k;
+  float* temp = reinterpret_cast<float*>(A + m.off_temperature);
+  float* topp = reinterpret_cast<float*>(A + m.off_top_p);
+  int64_t* seeds = reinterpret_cast<int64_t*>(A + m.off_seeds);
+  int64_t* offs = reinterpret_cast<int64_t*>(A + m.off_offsets);
+
+  int t = 0;
+  int nsample = 0;
+  m.all_greedy = true;
+  auto add_sample = [&](Sequence* s, int row) {
+    lrows[nsample] = row;
+    temp[nsample] = s ? s->sp.temperature : 0.f;
+    topp[nsample] = s ? s->sp.top_p : 1.f;
+    topk[nsample] = s ? s->sp.top_k : 0;
+    seeds[nsample] = s ? s->sp.seed : 0;
+    offs[nsample] = s ? s->num_generated() : 0;
+    if (s && s->sp.temperature > 0.f) m.all_greedy = false;
+    if (s) last_sampling_.push_back(s);
+    ++nsample;
+  };
+  for (int i = 0; i < Bd; ++i) {
+    int32_t* row_bt = dbt + static_cast<int64_t>(i) * mb;
+    if (i < real_decode) {
+      Sequence* s = decodes[i];
+      const int pos = s->num_computed;
+      input_ids[t] = s->tokens[pos];
+      positions[t] = pos;
+      slots[t] = s->table[pos / bs] * bs + pos % bs;
+      const int nb = static_cast<int>(s->table.size());
+      if (nb > mb) throw std::runtime_error("Scheduler: block table wider than the arena");
+      std::copy(s->table.begin(), s->table.end(), row_bt);
+      dsl[i] = pos + 1;
+      m.max_decode_blocks = std::max(m.max_decode_blocks, (pos + bs) / bs);
+      add_sample(s, t);
+    } else {  // padding row: reads one page of block 0, writes no KV, result ignored
+      input_ids[t] = 0;
+      positions[t] = 0;
+      slots[t] = -1;
+      row_bt[0] = 0;
+      dsl[i] = 1;
+      add_sample(nullptr, t);
+    }
+    ++t;
+  }
+  pcu[0] = 0;
+  struct TileOrder {
+    int seq, start, extent;
+  };
+  std::vector<TileOrder> tiles;
+  tiles.reserve(ntiles);
+  for (size_t j = 0; j < prefills.size(); ++j) {
+    const Prefill& p = prefills[j];
+    Sequence* s = p.s;
+    for (int k = 0; k < p.len; ++k) {
+      const int pos = p.start + k;
+      input_ids[t] = s->tokens[pos];
+      positions[t] = pos;
+      slots[t] = s->table[pos / bs] * bs + pos % bs;
+      ++t;
+    }
+    const int nb = static_cast<int>(s->table.size());
+    if (nb > mb) throw std::runtime_error("Scheduler: block table wider than the arena");
+    std::copy(s->table.begin(), s->table.end(), pbt + static_cast<int64_t>(j) * mb);
+    pctx[j] = p.start + p.len;
+    pcu[j + 1] = pcu[j] + p.len;
+    for (int r = 0; r < p.len; r += 64) tiles.push_back({static_cast<int>(j), r, p.start + std::min(r + 64, p.len)});
+    s->num_computed = p.start + p.len;
+    if (s->num_computed == static_cast<int>(s->tokens.size())) add_sample(s, t - 1);
+  }
+  // heavy tiles (long kv extent) first for load balance
+  std::stable_sort(tiles.begin(), tiles.end(), [](const TileOrder& a, const TileOrder& b) { return a.extent > b.extent; });
+  for (int i = 0; i < static_cast<int>(tiles.size()); ++i) {
+    tseq[i] = tiles[i].seq;
+    tstart[i] = tiles[i].start;
+  }
+  for (Sequence* s : decodes) s->num_computed += 1;
+  for (Sequence* s : decodes) last_scheduled_.push_back(s);
+  for (auto& p : prefills) last_scheduled_.push_back(p.s);
+  m.num_real_decode = real_decode;
+  m.num_real_logits = static_cast<int>(last_sampling_.size());
+  return m;
+}
+
+StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB) {
+  StepMeta m;
+  int64_t off = 0;
+  auto take = [&](int64_t words) {
+    const int64_t o = off;
+    off += words;
+    return o;
+  };
+  auto align2 = [&] { off = (off + 1) & ~int64_t(1); };
+  m.off_input_ids = take(T);
+  m.off_slot_mapping = take(T);
+  align2();
+  m.off_positions = take(2 * int64_t(T));
+  m.off_decode_seq_lens = take(Bd);
+  m.off_decode_block_table = take(int64_t(Bd) * MB);
+  m.off_prefill_ctx_lens = take(Sp);
+  m.off_prefill_cu_q = take(Sp + 1);
+  m.off_prefill_block_table = take(int64_t(Sp) * MB);
+  m.off_tile_seq = take(NT);
+  m.off_tile_start = take(NT);
+  m.off_logits_rows = take(NL);
+  m.off_top_k = take(NL);
+  m.off_temperature = take(NL);
+  m.off_top_p = take(NL);
+  align2();
+  m.off_seeds = take(2 * int64_t(NL));
+  m.off_offsets = take(2 * int64_t(NL));
+  align2();
+  m.used_words = off;
+  m.num_tokens = T;
+  m.num_decode = Bd;
+  m.num_prefill = Sp;
+  m.num_tiles = NT;
+  m.num_logits = NL;
+  return m;
+}
+
+std::vector<Event> Scheduler::update(const int32_t* sampled, int n) {
+  std::vector<Event> ev;
+  if (n < static_cast<int>(last_sampling_.size()))
+    throw std::invalid_argument("Scheduler::update: fewer sampled tokens than sampling rows");
+  n = static_cast<int>(last_sampling_.size());
+  for (Sequence* s : last_scheduled_) bm_.commit_full_blocks(s->tokens, s->num_computed, s->table, s->hashes);
+  for (int i = 0; i < n; ++i) {
+    Sequence* s = last_sampling_[i];
+    if (s->status != SeqStatus::Running) continue;  // aborted meanwhile
+    const int32_t tok = sampled[i];
+    s->tokens.push_back(tok);
+    const bool stop = is_stop(*s, tok);
+    FinishReason r = FinishReason::None;
+    if (stop) {
+      const bool length = s->num_generated() >= s->sp.max_tokens ||
+                          static_cast<int>(s->tokens.size()) >= cfg_.max_model_len;
+      bool eos = false;
+      if (!s->sp.ignore_eos)
+        for (int32_t e : cfg_.eos_token_ids) eos |= (tok == e);
+      for (int32_t e : s->sp.stop_token_ids) eos |= (tok == e);
+      r = (eos && s->num_generated() >= s->sp.min_tokens) ? FinishReason::Stop
+                                                          : (length ? FinishReason::Length : FinishReason::Stop);
+      running_.erase(std::remove(running_.begin(), running_.end(), s), running_.end());
+      finish(s, r);
+    }
+    ev.push_back({s->id, tok, stop, static_cast<int>(r)});
+  }
+  last_sampling_.clear();
+  last_scheduled_.clear();
+  // drop finished sequences
+  for (auto it = seqs_.begin(); it != seqs_.end();) {
+    if (it->second->status == SeqStatus::Finished)
+      it = seqs_.erase(it);
+    else
+      ++it;
+  }
+  return ev;
+}
+
+}  // namespace rt
+}  // namespace bloom

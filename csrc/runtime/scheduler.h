@@ -1,0 +1,162 @@
+// In-flight batching scheduler (host side, C++).
+//
+// One step = decode rows for every running sequence that only needs its last
+// sampled token computed, then prefill rows (chunked) for partially computed
+// and newly admitted sequences with the token budget that is left.  This is
+// the step order of the reference scheduler (crates/engine/src/scheduler/
+// mod.rs:1795-1845: preempt -> decode micro-batches -> prefill with leftover
+// budget; chunked prefill :2042-2217), but here every scheduled row of every
+// sequence goes into ONE batched forward: the step's metadata (token ids,
+// positions, KV slots, block tables, attention tiles, sampling rows and
+// sampling parameters) is written straight into pinned host buffers that the
+// model runner copies to the device in one transfer.
+//
+// Preemption is by recompute (reference mod.rs:2001-2027): when the KV pool
+// cannot grow a running sequence, the most recently admitted running
+// sequence releases its blocks and goes back to the head of the wait queue.
+// Stop conditions come from the model (EOS ids), never a hard-coded token id.
+#pragma once
+
+#include <cstdint>
+#include <deque>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "block_manager.h"
+
+namespace bloom {
+namespace rt {
+
+struct SamplingParams {
+  float temperature = 0.f;  // <= 0: greedy
+  float top_p = 1.f;
+  int top_k = 0;
+  int64_t seed = 0;
+  int max_tokens = 128;
+  int min_tokens = 0;
+  bool ignore_eos = false;
+  std::vector<int32_t> stop_token_ids;
+};
+
+enum class SeqStatus : int { Waiting = 0, Running = 1, Finished = 2 };
+enum class FinishReason : int { None = 0, Stop = 1, Length = 2, Aborted = 3 };
+
+struct Sequence {
+  int64_t id = 0;
+  std::vector<int32_t> tokens;
+  int num_prompt = 0;
+  int num_computed = 0;
+  int num_cached_prefix = 0;
+  std::vector<int32_t> table;
+  std::vector<uint64_t> hashes;
+  SamplingParams sp;
+  SeqStatus status = SeqStatus::Waiting;
+  FinishReason finish = FinishReason::None;
+  int priority = 0;
+  int64_t order = 0;
+  int num_preemptions = 0;
+  bool admitted_once = false;
+  int num_generated() const { return static_cast<int>(tokens.size()) - num_prompt; }
+};
+
+struct SchedulerConfig {
+  int max_num_seqs = 256;
+  int max_num_batched_tokens = 8192;
+  int max_model_len = 4096;
+  bool chunked_prefill = true;
+  std::vector<int32_t> eos_token_ids;
+};
+
+// The scheduler writes each step's metadata into ONE pinned int32 arena in a
+// packed layout, so the runner moves it to the device with a single copy.
+// Offsets (in 32-bit words) depend only on the row counts, so a decode-only
+// step padded to a batch bucket has the same layout every time and can be
+// replayed from a CUDA graph.  Region order:
+//   input_ids[T] slot_mapping[T] positions[T] (int64, 8-byte aligned)
+//   decode_seq_lens[Bd] decode_block_table[Bd * MB]
+//   prefill_ctx_lens[Sp] prefill_cu_q[Sp + 1] prefill_block_table[Sp * MB]
+//   tile_seq[NT] tile_start[NT]
+//   logits_rows[NL] top_k[NL] temperature[NL] (f32) top_p[NL] (f32)
+//   seeds[NL] (int64, aligned) offsets[NL] (int64)
+struct Arena {
+  int32_t* base = nullptr;
+  int64_t capacity = 0;    // words
+  int max_tokens = 0;      // T capacity
+  int max_seqs = 0;        // rows of a block table / sampling rows
+  int max_blocks = 0;      // MB: block-table width
+};
+
+struct StepMeta {
+  int num_tokens = 0;   // T (including decode padding)
+  int num_decode = 0;   // Bd (including padding)
+  int num_real_decode = 0;
+  int num_prefill = 0;  // Sp
+  int num_tiles = 0;    // NT
+  int num_logits = 0;   // NL (including padding)
+  int num_real_logits = 0;
+  int max_decode_blocks = 0;
+  int num_preempted = 0;
+  bool all_greedy = true;
+  // word offsets into the arena
+  int64_t off_input_ids = 0, off_slot_mapping = 0, off_positions = 0;
+  int64_t off_decode_seq_lens = 0, off_decode_block_table = 0;
+  int64_t off_prefill_ctx_lens = 0, off_prefill_cu_q = 0, off_prefill_block_table = 0;
+  int64_t off_tile_seq = 0, off_tile_start = 0;
+  int64_t off_logits_rows = 0, off_top_k = 0, off_temperature = 0, off_top_p = 0, off_seeds = 0, off_offsets = 0;
+  int64_t used_words = 0;
+};
+
+// Packed layout for the given row counts (shared by the scheduler and the runner).
+StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB);
+
+struct Event {
+  int64_t seq_id;
+  int32_t token;
+  bool finished;
+  int finish_reason;
+};
+
+class Scheduler {
+ public:
+  Scheduler(const SchedulerConfig& cfg, int num_blocks, int block_size, bool prefix_caching);
+
+  void set_arena(const Arena& a) { arena_ = a; }
+  // Decode-only steps are padded up to the smallest bucket >= their batch.
+  void set_decode_buckets(const std::vector<int>& b) { buckets_ = b; }
+  int64_t add_request(const std::vector<int32_t>& prompt, const SamplingParams& sp, int priority);
+  bool abort(int64_t id);
+  bool has_unfinished() const { return !waiting_.empty() || !running_.empty(); }
+  int num_waiting() const { return static_cast<int>(waiting_.size()); }
+  int num_running() const { return static_cast<int>(running_.size()); }
+
+  StepMeta schedule();
+  std::vector<Event> update(const int32_t* sampled, int n);
+
+  BlockManager& blocks() { return bm_; }
+  const Sequence* find(int64_t id) const;
+  const SchedulerConfig& config() const { return cfg_; }
+  int64_t total_preemptions() const { return total_preemptions_; }
+
+ private:
+  void preempt(Sequence* s);
+  bool is_stop(const Sequence& s, int32_t tok) const;
+  void finish(Sequence* s, FinishReason r);
+
+  SchedulerConfig cfg_;
+  BlockManager bm_;
+  Arena arena_;
+  std::vector<int> buckets_;
+  std::unordered_map<int64_t, std::unique_ptr<Sequence>> seqs_;
+  std::deque<Sequence*> waiting_;
+  std::vector<Sequence*> running_;
+  std::vector<Sequence*> last_sampling_;
+  std::vector<Sequence*> last_scheduled_;
+  int64_t next_id_ = 1;
+  int64_t next_order_ = 0;
+  int64_t total_preemptions_ = 0;
+};
+
+}  // namespace rt
+}  // namespace bloom

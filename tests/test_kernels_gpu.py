@@ -1,0 +1,248 @@
+"""Numerics of every sm_100a kernel against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from bloom_b200 import ops
+
+    return ops
+
+
+def _ref():
+    from bloom_b200.ops import reference
+
+    return reference
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-6)).item()
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    ops = _ops()
+    ops.status().zero_()
+    yield
+    torch.cuda.synchronize()
+    assert int(ops.status()[0].item()) == 0, "kernel reported a timed-out wait"
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 33, 100, 128, 200, 256, 300, 1000])
+@pytest.mark.parametrize("N,K", [(128, 64), (384, 256), (1000, 512), (256, 4160)])
+def test_gemm_bf16(M, N, K):
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(M * 7 + N)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    y = ops.gemm(x, w)
+    assert rel_err(y, ref.gemm(x, w)) < 1e-2
+
+
+@pytest.mark.parametrize("M", [5, 64, 257])
+def test_gemm_bias_f32_residual(M):
+    ops, ref = _ops(), _ref()
+    N, K = 512, 384
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    b = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    assert rel_err(ops.gemm(x, w, bias=b), ref.gemm(x, w, b)) < 1e-2
+    y32 = ops.gemm(x, w, epi=ops.EPI_F32)
+    assert y32.dtype == torch.float32 and rel_err(y32, ref.gemm(x, w)) < 1e-3
+    r = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    yr = ops.gemm(x, w, epi=ops.EPI_RESIDUAL, resid=r)
+    assert rel_err(yr, ref.gemm(x, w) + r.float()) < 1e-2
+
+
+@pytest.mark.parametrize("M,splits", [(3, 2), (64, 4), (256, 3)])
+def test_gemm_splitk_partials(M, splits):
+    ops, ref = _ops(), _ref()
+    N, K = 384, 1024
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    p = ops.gemm(x, w, epi=ops.EPI_PARTIAL_F32, splits=splits)
+    assert p.shape == (splits, M, N)
+    assert rel_err(p.sum(0), ref.gemm(x, w)) < 1e-3
+
+
+@pytest.mark.parametrize("M", [1, 40, 256, 700])
+def test_gemm_swiglu(M):
+    ops, ref = _ops(), _ref()
+    I, H = 256, 512
+    x = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+    g = torch.randn(I, H, device="cuda", dtype=torch.bfloat16) * 0.05
+    u = torch.randn(I, H, device="cuda", dtype=torch.bfloat16) * 0.05
+    w = ops.interleave_gate_up(g, u)
+    y = ops.gemm(x, w, epi=ops.EPI_SWIGLU)
+    assert y.shape == (M, I)
+    assert rel_err(y, ref.swiglu(ref.gemm(x, g), ref.gemm(x, u))) < 1.5e-2
+
+
+def test_rmsnorm_and_add():
+    ops, ref = _ops(), _ref()
+    M, H = 37, 4096
+    x = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(H, device="cuda", dtype=torch.bfloat16)
+    assert rel_err(ops.rmsnorm(x, w, 1e-5), ref.rmsnorm(x, w, 1e-5)) < 1e-2
+    res = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+    d = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+    exp_res = (res.float() + d.float())
+    r2 = res.clone()
+    out = ops.add_rmsnorm(d, r2, w, 1e-5)
+    assert rel_err(r2, exp_res) < 1e-2
+    assert rel_err(out, ref.rmsnorm(exp_res, w, 1e-5)) < 1.5e-2
+    parts = torch.randn(3, M, H, device="cuda", dtype=torch.float32)
+    r3 = res.clone()
+    out3 = ops.add_rmsnorm(parts, r3, w, 1e-5)
+    e3 = res.float() + parts.sum(0)
+    assert rel_err(r3, e3) < 1e-2 and rel_err(out3, ref.rmsnorm(e3, w, 1e-5)) < 1.5e-2
+
+
+def test_layernorm_embedding():
+    ops, ref = _ops(), _ref()
+    x = torch.randn(10, 384, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(384, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(384, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn(10, 384, device="cuda", dtype=torch.bfloat16)
+    assert rel_err(ops.layernorm(x, w, b, 1e-12, resid=r), ref.layernorm(x.float() + r.float(), w, b, 1e-12)) < 1e-2
+    table = torch.randn(1000, 256, device="cuda", dtype=torch.bfloat16)
+    ids = torch.tensor([0, 5, 999, 17], device="cuda", dtype=torch.int32)
+    assert torch.equal(ops.embedding(ids, table), table[ids.long()])
+
+
+def _make_cache(L, NB, KVH, D=128):
+    return torch.randn(L, NB, 2, KVH, 16, D, device="cuda", dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_rope_kv_write(qk_norm):
+    ops, ref = _ops(), _ref()
+    T, nq, nkv, D = 19, 4, 2, 128
+    cache = torch.zeros(2, 8, 2, nkv, 16, D, device="cuda", dtype=torch.bfloat16)
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda", dtype=torch.bfloat16)
+    pos = torch.randint(0, 500, (T,), device="cuda", dtype=torch.int64)
+    slots = torch.randperm(8 * 16, device="cuda")[:T].to(torch.int32)
+    slots[3] = -1
+    cs = ops.rope_cos_sin(1024, D, 10000.0, "cuda")
+    qn = torch.randn(D, device="cuda", dtype=torch.bfloat16) if qk_norm else None
+    kn = torch.randn(D, device="cuda", dtype=torch.bfloat16) if qk_norm else None
+    q = torch.empty(T, nq, D, device="cuda", dtype=torch.bfloat16)
+    ops.rope_kv_write(qkv, pos, slots, cs, q, cache, 1, nq, nkv, qn, kn, 1e-6)
+    v3 = qkv.view(T, nq + 2 * nkv, D).float()
+    qr, kr, vr = v3[:, :nq], v3[:, nq:nq + nkv], v3[:, nq + nkv:]
+    if qk_norm:
+        qr = ref.rmsnorm(qr, qn, 1e-6)
+        kr = ref.rmsnorm(kr, kn, 1e-6)
+    assert rel_err(q, ref.rope(qr, pos, cs)) < 1e-2
+    kexp = ref.rope(kr, pos, cs)
+    for t in range(T):
+        s = int(slots[t])
+        if s < 0:
+            continue
+        assert rel_err(cache[1, s // 16, 0, :, s % 16], kexp[t]) < 1e-2
+        assert rel_err(cache[1, s // 16, 1, :, s % 16], vr[t]) < 1e-2
+    assert cache[0].abs().sum().item() == 0  # other layer untouched
+
+
+@pytest.mark.parametrize("nq,nkv,q_len", [(32, 8, 1), (8, 8, 1), (16, 2, 1), (32, 8, 4), (8, 1, 4)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_paged_decode_attention(nq, nkv, q_len, splits):
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(1)
+    L, NB, D, MB = 2, 300, 128, 64
+    cache = _make_cache(L, NB, nkv)
+    lens = [1, 17, 200, 513, 35, 1000][: 4 if q_len > 1 else 6]
+    lens = [max(l, q_len) for l in lens]
+    B = len(lens)
+    bt = torch.zeros(B, MB, dtype=torch.int32)
+    perm = torch.randperm(NB)
+    k = 0
+    for b, l in enumerate(lens):
+        nb = (l + 15) // 16
+        bt[b, :nb] = perm[k:k + nb]
+        k += nb
+    bt = bt.cuda()
+    sl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    q = torch.randn(B * q_len, nq, D, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    scale = 1 / math.sqrt(D)
+    ops.paged_decode_attention(q, cache, 1, bt, sl, out, q_len=q_len, splits=splits, scale=scale)
+    for b, l in enumerate(lens):
+        kk, vv = ref.gather_paged(cache, 1, bt[b], l)
+        exp = ref.attention(q[b * q_len:(b + 1) * q_len], kk, vv, causal=True, q_offset=l - q_len, scale=scale)
+        assert rel_err(out[b * q_len:(b + 1) * q_len], exp) < 2e-2, (b, l)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_paged_prefill_attention(causal):
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(2)
+    L, NB, D, MB = 1, 200, 128, 64
+    nq, nkv = 8, 2
+    cache = _make_cache(L, NB, nkv)
+    # (prefix already cached, new query tokens)
+    seqs = [(0, 5), (0, 64), (32, 100), (16, 1), (100, 250)]
+    Sp = len(seqs)
+    bt = torch.zeros(Sp, MB, dtype=torch.int32)
+    perm = torch.randperm(NB)
+    k = 0
+    ctx = []
+    cu = [0]
+    for j, (pre, ql) in enumerate(seqs):
+        c = pre + ql
+        nb = (c + 15) // 16
+        bt[j, :nb] = perm[k:k + nb]
+        k += nb
+        ctx.append(c)
+        cu.append(cu[-1] + ql)
+    T = cu[-1]
+    q = torch.randn(T, nq, D, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros_like(q)
+    tseq, tstart = ops.prefill_tiles(cu, ctx)
+    ops.paged_prefill_attention(q, cache, 0, bt.cuda(), torch.tensor(ctx, dtype=torch.int32, device="cuda"),
+                                torch.tensor(cu, dtype=torch.int32, device="cuda"), tseq.cuda(), tstart.cuda(), out,
+                                scale=1 / math.sqrt(D), causal=causal)
+    for j, (pre, ql) in enumerate(seqs):
+        kk, vv = ref.gather_paged(cache, 0, bt[j].cuda(), ctx[j])
+        exp = ref.attention(q[cu[j]:cu[j + 1]], kk, vv, causal=causal, q_offset=pre, scale=1 / math.sqrt(D))
+        assert rel_err(out[cu[j]:cu[j + 1]], exp) < 2e-2, j
+
+
+def test_argmax_and_sampling():
+    ops = _ops()
+    B, V = 5, 128256
+    logits = torch.randn(B, V, device="cuda", dtype=torch.bfloat16)
+    logits[2, 77777] = 50.0
+    idx = ops.argmax(logits)
+    assert torch.equal(idx.long(), logits.float().argmax(-1))
+    temp = torch.tensor([0.0, 1.0, 1.0, 0.7, 1.0], device="cuda")
+    top_p = torch.tensor([1.0, 1.0, 0.9, 0.5, 1.0], device="cuda")
+    top_k = torch.tensor([0, 1, 0, 0, 3], device="cuda", dtype=torch.int32)
+    seeds = torch.arange(B, device="cuda", dtype=torch.int64)
+    offs = torch.zeros(B, device="cuda", dtype=torch.int64)
+    s = ops.sample(logits, temp, top_p, top_k, seeds, offs)
+    assert int(s[0]) == int(idx[0])  # greedy
+    assert int(s[1]) == int(idx[1])  # top_k = 1
+    assert int(s[2]) == 77777  # overwhelming mass
+    top3 = logits[4].float().topk(3).indices.tolist()
+    assert int(s[4]) in top3
+    s2 = ops.sample(logits, temp, top_p, top_k, seeds, offs)
+    assert torch.equal(s, s2)  # reproducible stream
+
+
+def test_sampling_distribution():
+    ops = _ops()
+    V = 64
+    probs = torch.softmax(torch.randn(V, device="cuda") * 2, 0)
+    logits = probs.log().unsqueeze(0).repeat(4096, 1).contiguous()
+    n = logits.shape[0]
+    s = ops.sample(logits, torch.ones(n, device="cuda"), torch.ones(n, device="cuda"),
+                   torch.zeros(n, device="cuda", dtype=torch.int32), torch.arange(n, device="cuda"),
+                   torch.zeros(n, device="cuda", dtype=torch.int64))
+    freq = torch.bincount(s.long(), minlength=V).float() / n
+    assert (freq - probs).abs().max().item() < 0.03

@@ -1,0 +1,257 @@
+"""Contract tests of the C++ KV block manager and in-flight batching scheduler.
+
+Intent follows the reference's scheduler tests (crates/engine/src/scheduler/
+scheduler_test.rs: budgets, decode-before-prefill, chunked prefill splits,
+preemption, cancellation, prefix caching and pinning, LRU) with a mock
+executor that returns a fixed token, like the reference's MockExecutor.
+"""
+import pytest
+import torch
+
+from bloom_b200._ext import runtime
+
+
+@pytest.fixture(scope="module")
+def rt():
+    return runtime()
+
+
+def make(rt, num_blocks=64, max_seqs=8, budget=64, max_len=512, prefix=True, chunked=True, eos=(2,), buckets=None):
+    cfg = rt.SchedulerConfig()
+    cfg.max_num_seqs = max_seqs
+    cfg.max_num_batched_tokens = budget
+    cfg.max_model_len = max_len
+    cfg.chunked_prefill = chunked
+    cfg.eos_token_ids = list(eos)
+    s = rt.Scheduler(cfg, num_blocks, 16, prefix)
+    mb = (max_len + 15) // 16
+    worst = rt.arena_layout(max(budget, max_seqs), max_seqs, max_seqs, max(budget, max_seqs) // 64 + max_seqs,
+                            max_seqs, mb)
+    arena = torch.zeros(worst.used_words, dtype=torch.int32)
+    s.set_arena(arena, max(budget, max_seqs), max_seqs, mb)
+    if buckets:
+        s.set_decode_buckets(buckets)
+    return s, arena, mb
+
+
+def params(rt, max_tokens=4, **kw):
+    p = rt.SamplingParams()
+    p.max_tokens = max_tokens
+    p.temperature = 0.0
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+def run_step(s, arena, token=42):
+    m = s.schedule()
+    sampled = torch.full((max(m.num_logits, 1),), token, dtype=torch.int32)
+    ev = s.update(sampled, m.num_real_logits)
+    return m, ev
+
+
+def region(arena, off, n, dtype=torch.int32):
+    if dtype == torch.int64:
+        return arena[off:off + 2 * n].view(torch.int64)
+    if dtype == torch.float32:
+        return arena[off:off + n].view(torch.float32)
+    return arena[off:off + n]
+
+
+def test_block_manager_prefix_and_lru(rt):
+    bm = rt.BlockManager(8, 16, True)
+    toks = list(range(40))
+    ok, table = bm.allocate([], 40)
+    assert ok and len(table) == 3
+    hashes = bm.commit(toks, 40, table, [])
+    assert len(hashes) == 2  # only full blocks are hashed
+    bm.release(table, hashes)
+    m = bm.metrics()
+    assert m["cached_blocks"] == 2 and m["free_blocks"] == 6
+    n, t2, h2 = bm.match_prefix(toks, 39)
+    assert n == 32 and t2 == table[:2]
+    assert bm.refcount(t2[0]) == 1
+    # filling the pool evicts cached blocks only when free ones run out
+    ok, t3 = bm.allocate([], 16 * 6)
+    assert ok and bm.metrics()["evictions"] == 0
+    ok, t4 = bm.allocate([], 16)
+    assert not ok  # the two cached blocks are pinned by t2
+
+
+def test_block_manager_eviction_order(rt):
+    bm = rt.BlockManager(4, 16, True)
+    a = list(range(32))
+    ok, ta = bm.allocate([], 32)
+    ha = bm.commit(a, 32, ta, [])
+    bm.release(ta, ha)
+    ok, tb = bm.allocate([], 48)  # needs one cached block: the tail of prefix a goes first
+    assert ok and bm.metrics()["evictions"] == 1
+    n, _, _ = bm.match_prefix(a, 31)
+    assert n == 16
+
+
+def test_decode_before_prefill_and_budget(rt):
+    s, arena, mb = make(rt, budget=40)
+    s.add_request(list(range(10, 40)), params(rt, max_tokens=3))
+    m, ev = run_step(s, arena)
+    assert m.num_prefill == 1 and m.num_decode == 0 and m.num_tokens == 30 and len(ev) == 1
+    s.add_request(list(range(100, 150)), params(rt, max_tokens=3))
+    m, ev = run_step(s, arena)
+    # decode row of request 1 first, then 39 prefill tokens of request 2 (chunked by the budget)
+    assert m.num_decode == 1 and m.num_prefill == 1 and m.num_tokens == 40
+    ids = region(arena, m.off_input_ids, m.num_tokens)
+    assert int(ids[0]) == 42 and int(ids[1]) == 100
+    assert m.num_real_logits == 1  # request 2 not finished prefilling: no sample
+    m, ev = run_step(s, arena)
+    assert m.num_decode == 1 and m.num_tokens == 1 + 11
+    assert m.num_real_logits == 2
+
+
+def test_positions_slots_and_block_tables(rt):
+    s, arena, mb = make(rt, budget=64, prefix=False)
+    s.add_request(list(range(3, 23)), params(rt, max_tokens=5))
+    m, _ = run_step(s, arena)
+    pos = region(arena, m.off_positions, m.num_tokens, torch.int64)
+    assert pos.tolist() == list(range(20))
+    slots = region(arena, m.off_slot_mapping, m.num_tokens)
+    bt = region(arena, m.off_prefill_block_table, mb)
+    assert slots.tolist() == [int(bt[p // 16]) * 16 + p % 16 for p in range(20)]
+    assert region(arena, m.off_prefill_ctx_lens, 1).tolist() == [20]
+    assert region(arena, m.off_prefill_cu_q, 2).tolist() == [0, 20]
+    m, _ = run_step(s, arena)
+    assert m.num_decode == 1
+    assert region(arena, m.off_positions, 1, torch.int64).tolist() == [20]
+    assert region(arena, m.off_decode_seq_lens, 1).tolist() == [21]
+
+
+def test_stop_on_eos_and_max_tokens(rt):
+    s, arena, _ = make(rt, eos=(7,))
+    r1 = s.add_request([5, 6], params(rt, max_tokens=10))
+    r2 = s.add_request([5, 6, 8], params(rt, max_tokens=2, ignore_eos=True))
+    m, ev = run_step(s, arena, token=7)
+    fin = {e[0]: (e[2], e[3]) for e in ev}
+    assert fin[r1] == (True, 1)  # stop (eos)
+    assert fin[r2] == (False, 0)
+    m, ev = run_step(s, arena, token=9)
+    assert ev == [(r2, 9, True, 2)]  # length
+    assert not s.has_unfinished()
+
+
+def test_ignore_eos_and_min_tokens(rt):
+    s, arena, _ = make(rt, eos=(7,))
+    r = s.add_request([5, 6], params(rt, max_tokens=3, ignore_eos=True))
+    for _ in range(2):
+        _, ev = run_step(s, arena, token=7)
+        assert not ev[0][2]
+    _, ev = run_step(s, arena, token=7)
+    assert ev[0][2] and ev[0][3] == 2
+
+
+def test_chunked_prefill_splits(rt):
+    s, arena, _ = make(rt, budget=16)
+    s.add_request(list(range(50)), params(rt, max_tokens=2))
+    lens = []
+    for _ in range(4):
+        m, ev = run_step(s, arena)
+        lens.append(m.num_tokens)
+    assert lens == [16, 16, 16, 2 + 1] or lens[:3] == [16, 16, 16]
+    assert not s.has_unfinished() or s.num_running == 1
+
+
+def test_no_chunking_waits_for_budget(rt):
+    s, arena, _ = make(rt, budget=32, chunked=False)
+    s.add_request(list(range(20)), params(rt))
+    s.add_request(list(range(20)), params(rt))
+    m, _ = run_step(s, arena)
+    assert m.num_prefill == 1 and m.num_tokens == 20
+
+
+def test_preemption_recompute(rt):
+    s, arena, _ = make(rt, num_blocks=4, budget=64, prefix=False, max_seqs=4)
+    a = s.add_request(list(range(31)), params(rt, max_tokens=20))
+    b = s.add_request(list(range(31)), params(rt, max_tokens=20))
+    preempted = 0
+    steps = 0
+    while s.has_unfinished() and steps < 200:
+        m, ev = run_step(s, arena)
+        preempted += m.num_preempted
+        steps += 1
+    assert not s.has_unfinished()
+    assert preempted > 0 and s.total_preemptions == preempted
+
+
+def test_abort(rt):
+    s, arena, _ = make(rt)
+    a = s.add_request(list(range(20)), params(rt, max_tokens=50))
+    run_step(s, arena)
+    assert s.abort(a)
+    assert not s.abort(a)
+    assert not s.has_unfinished()
+    assert s.kv_metrics()["active_blocks"] == 0
+
+
+def test_prefix_reuse_counts(rt):
+    s, arena, _ = make(rt, budget=256)
+    p = list(range(1000, 1040))
+    s.add_request(p, params(rt, max_tokens=1))
+    while s.has_unfinished():
+        run_step(s, arena)
+    r = s.add_request(p + [5, 6], params(rt, max_tokens=1))
+    m = s.schedule()
+    assert m.num_tokens == 42 - 32  # two cached blocks reused
+    assert s.num_cached_prefix(r) == 32
+    s.update(torch.zeros(4, dtype=torch.int32), m.num_real_logits)
+
+
+def test_decode_padding_to_bucket(rt):
+    s, arena, mb = make(rt, buckets=[1, 2, 4, 8])
+    for i in range(3):
+        s.add_request([10 + i, 11, 12], params(rt, max_tokens=4))
+    run_step(s, arena)
+    m = s.schedule()
+    assert m.num_prefill == 0 and m.num_decode == 4 and m.num_real_decode == 3 and m.num_logits == 4
+    lay = rt.arena_layout(4, 4, 0, 0, 4, mb)
+    assert lay.used_words == m.used_words and lay.off_logits_rows == m.off_logits_rows
+    slots = region(arena, m.off_slot_mapping, 4)
+    assert int(slots[3]) == -1
+    ev = s.update(torch.full((4,), 3, dtype=torch.int32), m.num_real_logits)
+    assert len(ev) == 3
+
+
+def test_priority_order(rt):
+    s, arena, _ = make(rt, budget=8, chunked=False)
+    lo = s.add_request(list(range(8)), params(rt), priority=0)
+    hi = s.add_request(list(range(8)), params(rt), priority=5)
+    m, ev = run_step(s, arena)
+    assert [e[0] for e in ev] == [hi]
+
+
+def test_sampling_params_in_arena(rt):
+    s, arena, _ = make(rt)
+    s.add_request([1, 2, 3], params(rt, temperature=0.5, top_p=0.8, top_k=7, seed=99))
+    m = s.schedule()
+    assert not m.all_greedy
+    assert region(arena, m.off_temperature, 1, torch.float32).tolist() == [0.5]
+    assert abs(region(arena, m.off_top_p, 1, torch.float32).item() - 0.8) < 1e-6
+    assert region(arena, m.off_top_k, 1).tolist() == [7]
+    assert region(arena, m.off_seeds, 1, torch.int64).tolist() == [99]
+    s.update(torch.zeros(1, dtype=torch.int32), 1)
+
+
+def test_many_requests_complete(rt):
+    s, arena, _ = make(rt, num_blocks=200, max_seqs=16, budget=128)
+    import random
+
+    rng = random.Random(0)
+    ids = [s.add_request([rng.randrange(100) for _ in range(rng.randint(1, 90))], params(rt, max_tokens=rng.randint(1, 9)))
+           for _ in range(40)]
+    done = set()
+    for _ in range(2000):
+        if not s.has_unfinished():
+            break
+        m, ev = run_step(s, arena, token=rng.randrange(3, 100))
+        for e in ev:
+            if e[2]:
+                done.add(e[0])
+    assert done == set(ids)
+    assert s.kv_metrics()["active_blocks"] == 0
