@@ -66,12 +66,15 @@ class ModelRunner:
         # decode attention split-K workspace, sized for the largest need over buckets
         ws = 1
         self.decode_splits: Dict[int, int] = {}
-        for b in self.buckets + [max_num_seqs]:
+        for b in range(1, max_num_seqs + 1):  # eager steps may have any decode count
             s = ops.decode_attention_splits(b, model.nkv, self.max_blocks, self.device.index)
             self.decode_splits[b] = s
             ws = max(ws, ops.decode_workspace_numel(b, model.nkv, s))
         self.decode_ws = torch.empty(ws, dtype=torch.float32, device=self.device)
         self.graphs: Dict[int, tuple] = {}
+        import os as _os
+
+        self.check_finite = _os.environ.get("BLOOM_CHECK_FINITE", "0") == "1"
         self.graph_pool = None
         self.stats = {"steps": 0, "graph_steps": 0, "eager_steps": 0, "tokens": 0, "h2d_bytes": 0, "d2h_bytes": 0}
 
@@ -85,7 +88,10 @@ class ModelRunner:
     def views(self, m) -> StepInputs:
         T, Bd, Sp, NT, NL = m.num_tokens, m.num_decode, m.num_prefill, m.num_tiles, m.num_logits
         MB = self.max_blocks
-        splits = self.decode_splits.get(Bd) or ops.decode_attention_splits(Bd, self.model.nkv, MB, self.device.index)
+        splits = 1
+        if Bd:
+            splits = self.decode_splits.get(Bd) or ops.decode_attention_splits(Bd, self.model.nkv, MB,
+                                                                              self.device.index)
         return StepInputs(
             input_ids=self._v(m.off_input_ids, T),
             positions=self._v(m.off_positions, T, torch.int64),
@@ -174,6 +180,12 @@ class ModelRunner:
         else:
             logits = self._forward_logits(self.views(m))
             self.stats["eager_steps"] += 1
+        if self.check_finite and m.num_logits:
+            bad = (~torch.isfinite(logits[:m.num_real_logits].float())).any(dim=1)
+            if bool(bad.any()):
+                rows = bad.nonzero().flatten().tolist()
+                raise FloatingPointError(f"non-finite logits in rows {rows} (T={m.num_tokens}, decode={m.num_decode}, "
+                                         f"prefill={m.num_prefill})")
         toks = self._sample(logits, m, m.all_greedy)
         NL = m.num_logits
         self.sampled_host[:NL].copy_(toks[:NL], non_blocking=True)

@@ -84,7 +84,10 @@ class DecoderLM:
     def __init__(self, cfg: ModelConfig, tp: Optional[TPInfo] = None, device=None):
         self.cfg = cfg
         self.tp = tp or TPInfo()
-        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
         self.nq, self.nkv, self.q0, self.kv0 = _local_heads(cfg, self.tp.size, self.tp.rank)
         assert cfg.intermediate_size % (16 * self.tp.size) == 0 or cfg.is_moe
         self.inter = cfg.intermediate_size // self.tp.size

@@ -575,7 +575,7 @@ void launch_decode(const CUtensorMap& tm, const DecodeArgs& a, int B, cudaStream
 int64_t decode_attention_splits(int64_t batch, int64_t num_kv_heads, int64_t max_pages, int64_t device) {
   const int64_t ctas = batch * num_kv_heads;
   const int64_t target = 2 * num_sms(int(device));
-  if (ctas >= target) return 1;
+  if (ctas <= 0 || ctas >= target) return 1;
   int64_t s = (target + ctas - 1) / ctas;
   // at least 4 pages per warp-quad per split on long contexts
   const int64_t max_s = std::max<int64_t>(1, max_pages / 8);

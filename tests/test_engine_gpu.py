@@ -1,8 +1,11 @@
 """End-to-end engine on a tiny random model vs the fp32 PyTorch oracle."""
+import os
+
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+os.environ.setdefault("BLOOM_CHECK_FINITE", "1")
 
 
 def _build(name, std=0.08, graphs=True, **kw):
@@ -23,6 +26,8 @@ def _build(name, std=0.08, graphs=True, **kw):
 
 def _check_greedy(cfg, w, prompt, generated):
     from bloom_b200.models.reference import forward_logits
+
+    assert all(0 <= t < cfg.vocab_size for t in generated), generated
 
     full = list(prompt) + list(generated)
     logits = forward_logits(cfg, w, full)

@@ -229,8 +229,8 @@ def test_argmax_and_sampling():
     assert int(s[0]) == int(idx[0])  # greedy
     assert int(s[1]) == int(idx[1])  # top_k = 1
     assert int(s[2]) == 77777  # overwhelming mass
-    top3 = logits[4].float().topk(3).indices.tolist()
-    assert int(s[4]) in top3
+    third = logits[4].float().topk(3).values[-1].item()
+    assert logits[4, int(s[4])].float().item() >= third  # ties with the 3rd value are kept too
     s2 = ops.sample(logits, temp, top_p, top_k, seeds, offs)
     assert torch.equal(s, s2)  # reproducible stream
 
