@@ -1,0 +1,206 @@
+"""Per-kernel microbenchmark at the Llama-3-8B serving shapes.
+
+    python -m bloom_b200.cli.kernel_bench [--tp 1] [--json out.json]
+
+Each kernel is timed with CUDA events on the launching stream after warm-up
+(median of repeats; operands larger than L2 are rotated between repeats, so
+weights and KV pages come from HBM).  Reports achieved TFLOP/s or GB/s and
+the fraction of the measured peaks in MEASURED_PEAKS.json (HBM copy
+bandwidth, cuBLAS bf16 GEMM), plus torch.matmul (cuBLAS) on the same GEMM
+shapes as a library reference point.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+
+import torch
+
+
+def load_peaks():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+ITERS = [20]
+
+
+def timeit(fn, iters=None, warmup=5):
+    """Device time per call: `iters` calls (rotating operands) are captured in
+    a CUDA graph and replayed, so host launch cost never shows up in the
+    CUDA-event interval; median over 5 replays."""
+    iters = iters or ITERS[0]
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        fn(0)  # allocations of the first call happen outside the capture
+        with torch.cuda.graph(g, stream=s):
+            for i in range(iters):
+                fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) / iters)
+    return statistics.median(ts)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--json", default=None)
+    ap.add_argument("--only", default="")
+    ap.add_argument("--M", type=int, default=0, help="only this token count for GEMMs")
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    ITERS[0] = args.iters
+    from bloom_b200 import ops
+
+    hbm, tfl, src = load_peaks()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    t = args.tp
+    H, I, V, nq, nkv, hd = 4096, 14336, 128256, 32 // t, max(1, 8 // t), 128
+    rows = []
+
+    def report(name, ms, flops=None, bytes_=None, extra=None):
+        r = {"kernel": name, "ms": round(ms, 4)}
+        if flops:
+            r["tflops"] = round(flops / ms / 1e9, 1)
+            r["frac_bf16_peak"] = round(flops / ms / 1e9 / tfl, 3)
+        if bytes_:
+            r["gbs"] = round(bytes_ / ms / 1e6, 1)
+            r["frac_hbm_peak"] = round(bytes_ / ms / 1e6 / hbm, 3)
+        if extra:
+            r.update(extra)
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+
+    gemms = [("qkv", (nq + 2 * nkv) * hd, H), ("o_proj", H, nq * hd), ("gate_up", 2 * I // t, H),
+             ("down", H, I // t), ("lm_head", V // t, H)]
+    for M in ((args.M,) if args.M else (1, 64, 256, 2048, 8192)):
+        for name, N, K in gemms:
+            if args.only and args.only not in ("gemm", name, "gemm_" + name):
+                continue
+            if name == "lm_head" and M > 256:
+                continue
+            nrot = max(1, int(math.ceil(400e6 / (N * K * 2))))  # rotate weights beyond L2
+            ws = [torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02 for _ in range(nrot)]
+            x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+            epi = ops.EPI_SWIGLU if name == "gate_up" else ops.EPI_BF16
+            out = torch.empty(M, N // 2 if epi == ops.EPI_SWIGLU else N, device=dev, dtype=torch.bfloat16)
+            ms = timeit(lambda i=0: ops.gemm(x, ws[i % nrot], out, epi=epi))
+            flops = 2.0 * M * N * K
+            byt = N * K * 2 + M * K * 2 + out.numel() * 2
+            extra = {"M": M, "N": N, "K": K}
+            if M <= 512 and name in ("o_proj", "down"):
+                sp = ops.gemm_default_splits(M, N, K, 0)
+                if sp > 1:
+                    part = torch.empty(sp, M, N, device=dev, dtype=torch.float32)
+                    ms_sk = timeit(lambda i=0: ops.gemm(x, ws[i % nrot], part, epi=ops.EPI_PARTIAL_F32, splits=sp))
+                    extra["splitk"] = sp
+                    extra["splitk_ms"] = round(ms_sk, 4)
+            cms = timeit(lambda i=0: torch.matmul(x, ws[i % nrot].t()))
+            extra["cublas_ms"] = round(cms, 4)
+            report(f"gemm_{name}", ms, flops, byt, extra)
+            del ws
+
+    if not args.only or "attn" in args.only or "attention" in args.only:
+        # decode attention: 256 sequences, context U[512, 2304]
+        import random
+
+        rng = random.Random(0)
+        B = 256
+        lens = [rng.randint(512, 2304) for _ in range(B)]
+        MB = 2304 // 16
+        NB = sum((l + 15) // 16 for l in lens) + 8
+        L = 2
+        cache = torch.randn(L, NB, 2, nkv, 16, hd, device=dev, dtype=torch.bfloat16)
+        bt = torch.zeros(B, MB, dtype=torch.int32)
+        perm = torch.randperm(NB)
+        k = 0
+        for b, l in enumerate(lens):
+            nb = (l + 15) // 16
+            bt[b, :nb] = perm[k:k + nb]
+            k += nb
+        bt = bt.to(dev)
+        sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+        q = torch.randn(B, nq, hd, device=dev, dtype=torch.bfloat16)
+        o = torch.empty_like(q)
+        splits = ops.decode_attention_splits(B, nkv, MB, 0)
+        ws = torch.empty(ops.decode_workspace_numel(B, nkv, splits), device=dev)
+        kv_bytes = sum(lens) * nkv * hd * 2 * 2
+        ms = timeit(lambda i=0: ops.paged_decode_attention(q, cache, i % L, bt, sl, o, splits=splits, workspace=ws,
+                                                           scale=hd ** -0.5))
+        report("paged_decode_attention", ms, None, kv_bytes, {"B": B, "avg_ctx": sum(lens) / B, "splits": splits})
+        for Bs in (1, 8, 32):
+            sl2 = sl[:Bs].contiguous()
+            sp = ops.decode_attention_splits(Bs, nkv, MB, 0)
+            ws2 = torch.empty(ops.decode_workspace_numel(Bs, nkv, sp), device=dev)
+            ms = timeit(lambda i=0: ops.paged_decode_attention(q[:Bs], cache, i % L, bt[:Bs], sl2, o[:Bs], splits=sp,
+                                                               workspace=ws2, scale=hd ** -0.5))
+            report(f"paged_decode_attention_b{Bs}", ms, None, sum(lens[:Bs]) * nkv * hd * 4,
+                   {"B": Bs, "splits": sp})
+        # prefill attention: 4 sequences x 2048 tokens, causal
+        S, Lq = 4, 2048
+        NB2 = S * Lq // 16
+        cache2 = torch.randn(1, NB2, 2, nkv, 16, hd, device=dev, dtype=torch.bfloat16)
+        bt2 = torch.arange(NB2, dtype=torch.int32, device=dev).view(S, Lq // 16).contiguous()
+        cu = [i * Lq for i in range(S + 1)]
+        ctx = [Lq] * S
+        tseq, tstart = ops.prefill_tiles(cu, ctx)
+        q2 = torch.randn(S * Lq, nq, hd, device=dev, dtype=torch.bfloat16)
+        o2 = torch.empty_like(q2)
+        ctx_t = torch.tensor(ctx, dtype=torch.int32, device=dev)
+        cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+        ts_, tst = tseq.to(dev), tstart.to(dev)
+        ms = timeit(lambda i=0: ops.paged_prefill_attention(q2, cache2, 0, bt2, ctx_t, cu_t, ts_, tst, o2,
+                                                            scale=hd ** -0.5))
+        flops = S * 4.0 * Lq * Lq / 2 * hd * nq
+        report("paged_prefill_attention", ms, flops, None, {"seqs": S, "len": Lq})
+
+    if not args.only or "norm" in args.only:
+        for M in (256, 8192):
+            x = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+            r = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+            w = torch.ones(H, device=dev, dtype=torch.bfloat16)
+            out = torch.empty_like(x)
+            ms = timeit(lambda i=0: ops.add_rmsnorm(x, r, w, 1e-5, out))
+            report("add_rmsnorm", ms, None, M * H * 2 * 4, {"M": M})
+            qkv = torch.randn(M, (nq + 2 * nkv) * hd, device=dev, dtype=torch.bfloat16)
+            pos = torch.arange(M, device=dev, dtype=torch.int64)
+            slots = torch.arange(M, device=dev, dtype=torch.int32)
+            cache = torch.empty(1, M // 16 + 1, 2, nkv, 16, hd, device=dev, dtype=torch.bfloat16)
+            cs = ops.rope_cos_sin(8192, hd, 5e5, dev)
+            qo = torch.empty(M, nq, hd, device=dev, dtype=torch.bfloat16)
+            ms = timeit(lambda i=0: ops.rope_kv_write(qkv, pos, slots, cs, qo, cache, 0, nq, nkv))
+            report("rope_kv_write", ms, None, qkv.numel() * 4, {"M": M})
+        logits = torch.randn(256, V // t, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda i=0: ops.argmax(logits))
+        report("argmax", ms, None, logits.numel() * 2, {"B": 256})
+
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump({"peaks": {"hbm_gbs": hbm, "bf16_tflops": tfl, "source": src}, "rows": rows}, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

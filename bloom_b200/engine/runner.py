@@ -50,7 +50,8 @@ class ModelRunner:
         self.max_blocks = (max_model_len + self.block_size - 1) // self.block_size
         self.num_blocks = num_blocks
         cfg = self.cfg
-        self.kv_cache = torch.empty(cfg.num_layers, num_blocks, 2, model.nkv, self.block_size, cfg.head_dim,
+        # zero-filled: masked tail slots of a page are multiplied by p = 0, which must not meet NaN bit patterns
+        self.kv_cache = torch.zeros(cfg.num_layers, num_blocks, 2, model.nkv, self.block_size, cfg.head_dim,
                                     dtype=torch.bfloat16, device=self.device)
         rt = _rt()
         worst = rt.arena_layout(self.max_tokens, max_num_seqs, max_num_seqs,
@@ -136,10 +137,10 @@ class ModelRunner:
         rt = _rt()
         buckets = sorted(buckets or self.buckets, reverse=True)
         # a valid dummy step: every row reads one page of block 0, writes no KV
-        self.arena_host.zero_()
         for B in buckets:
             m = rt.arena_layout(B, B, 0, 0, B, self.max_blocks)
             h = self.arena_host
+            h[:m.used_words].zero_()  # regions of the previous bucket's layout must not leak in
             h[m.off_slot_mapping:m.off_slot_mapping + B] = -1
             h[m.off_decode_seq_lens:m.off_decode_seq_lens + B] = 1
             h[m.off_logits_rows:m.off_logits_rows + B] = torch.arange(B, dtype=torch.int32)

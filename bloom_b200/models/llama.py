@@ -289,10 +289,6 @@ class DecoderLM:
         residual = ops.embedding(s.input_ids, self.embed)
         x = ops.rmsnorm(residual, self.layers[0]["ln1"], eps)
         qkv_dim = (self.nq + 2 * self.nkv) * cfg.head_dim
-        # split-K for the row-parallel GEMMs when the grid would be small (decode)
-        small = T <= 512
-        o_splits = ops.gemm_default_splits(T, H, self.nq * cfg.head_dim, dev.index) if small else 1
-        d_splits = ops.gemm_default_splits(T, H, self.inter, dev.index) if small and not cfg.is_moe else 1
         for li, lay in enumerate(self.layers):
             qkv = ops.gemm(x, lay["qkv"], bias=lay.get("qkv_b"))
             q = torch.empty(T, self.nq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
@@ -307,19 +303,13 @@ class DecoderLM:
                 ops.paged_prefill_attention(q[Bd:], kv_cache, li, s.prefill_block_table, s.prefill_ctx_lens,
                                             s.prefill_cu_q, s.tile_seq, s.tile_start, attn[Bd:], scale=self.scale)
             a2 = attn.view(T, self.nq * cfg.head_dim)
-            if o_splits > 1 and self.tp.size == 1:
-                o = ops.gemm(a2, lay["o"], epi=ops.EPI_PARTIAL_F32, splits=o_splits)
-            else:
-                o = self._reduce(ops.gemm(a2, lay["o"]))
+            o = self._reduce(ops.gemm(a2, lay["o"]))
             x = ops.add_rmsnorm(o, residual, lay["ln2"], eps)
             if self.moe is not None:
                 d = self._reduce(self.moe.forward(li, x))
             else:
                 act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU)
-                if d_splits > 1 and self.tp.size == 1:
-                    d = ops.gemm(act, lay["down"], epi=ops.EPI_PARTIAL_F32, splits=d_splits)
-                else:
-                    d = self._reduce(ops.gemm(act, lay["down"]))
+                d = self._reduce(ops.gemm(act, lay["down"]))
             nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
             x = ops.add_rmsnorm(d, residual, nxt, eps)
         return x.index_select(0, s.logits_rows)

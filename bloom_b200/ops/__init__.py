@@ -56,7 +56,7 @@ def gemm(
     epi: int = EPI_BF16,
     bias: Optional[torch.Tensor] = None,
     resid: Optional[torch.Tensor] = None,
-    splits: int = 1,
+    splits: Optional[int] = None,
 ) -> torch.Tensor:
     """y = x @ w.T on tcgen05 (x [M,K] bf16, w [N,K] bf16) with a fused epilogue.
 
@@ -64,8 +64,19 @@ def gemm(
     per 32 rows (see `interleave_gate_up`) and returns silu(gate) * up [M, N/2].
     epi=EPI_PARTIAL_F32 returns split-K partial sums f32 [splits, M, N] that
     `add_rmsnorm` reduces.
+
+    splits=None picks split-K automatically for small M (decode batches): the
+    K range is split across CTAs so every SM streams weights, and the last
+    split to finish each tile sums the fp32 partials and runs the epilogue.
     """
     M, N = x.shape[0], w.shape[0]
+    if splits is None:
+        splits = 1
+        if epi != EPI_PARTIAL_F32 and 0 < M <= 512:
+            splits = _C().gemm_default_splits(M, N, x.shape[1], x.device.index)
+    fix_ws = fix_cnt = None
+    if splits > 1 and epi != EPI_PARTIAL_F32:
+        fix_ws, fix_cnt = _fixup_buffers(x.device, _C().gemm_fixup_ws_floats(M, N, splits))
     if out is None:
         if epi == EPI_SWIGLU:
             out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
@@ -75,9 +86,27 @@ def gemm(
             out = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
         else:
             out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index))
+    _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt)
     _count()
     return out
+
+
+_FIXUP: dict = {}
+
+
+def _fixup_buffers(device: torch.device, floats: int):
+    """Per-device split-K fixup workspace (fp32 partial tiles, L2-resident) and
+    per-tile arrival counters (zeroed once; every launch leaves them zero)."""
+    key = device.index
+    ws, cnt = _FIXUP.get(key, (None, None))
+    if ws is None or ws.numel() < floats:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("gemm split-K workspace must be sized before CUDA graph capture")
+        ws = torch.empty(max(floats, 8 << 20), dtype=torch.float32, device=device)
+        if cnt is None:
+            cnt = torch.zeros(1 << 16, dtype=torch.int32, device=device)
+        _FIXUP[key] = (ws, cnt)
+    return ws, cnt
 
 
 def gemm_default_splits(M: int, N: int, K: int, device: int = 0) -> int:

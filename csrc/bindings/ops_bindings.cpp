@@ -13,6 +13,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &bloom::gemm_out, "y = x @ w^T on tcgen05 with fused epilogue");
   m.def("gemm_pick_bn", &bloom::gemm_pick_bn);
   m.def("gemm_default_splits", &bloom::gemm_default_splits);
+  m.def("gemm_fixup_ws_floats", &bloom::gemm_fixup_ws_floats);
   m.def("rmsnorm", &bloom::rmsnorm);
   m.def("add_rmsnorm", &bloom::add_rmsnorm);
   m.def("layernorm", &bloom::layernorm);

@@ -14,9 +14,14 @@ enum GemmEpilogue : int {
   kEpiResidual = 4,    // out bf16 [M, N] = acc + resid
 };
 
+// splits > 1 with a non-partial epilogue: split-K where the last-arriving CTA
+// of each output tile sums the fp32 partials (fix_ws, L2-resident) and runs
+// the fused epilogue; fix_count holds one self-resetting counter per tile.
 void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
-              const torch::Tensor& status);
+              const torch::Tensor& status, const c10::optional<torch::Tensor>& fix_ws,
+              const c10::optional<torch::Tensor>& fix_count);
+int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits);
 int gemm_pick_bn(int M);
 int gemm_default_splits(int M, int N, int K, int device);
 

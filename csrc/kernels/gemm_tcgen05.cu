@@ -43,6 +43,9 @@ struct Args {
   long ldr;
   const __nv_bfloat16* bias;
   int* status;
+  float* fix_ws;     // split-K fixup: [tiles, splits, BN, 128] fp32 partial accumulators
+  int* fix_count;    // split-K fixup: (arrived, written) counters per output tile (self-resetting)
+  int fixup;         // 1: splits > 1 with the last-arriving CTA reducing and running the epilogue
 };
 
 template <int BN>
@@ -62,9 +65,12 @@ __device__ __forceinline__ void decode_tile(const Args& a, int t, int& feat_tile
   feat_tile = rest / a.num_tok_tiles;
 }
 
-template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(const Args& a, uint32_t taddr, int feat_tile, int tok_tile, int split,
-                                              int row, int lane) {
+// Runs the fused epilogue of one output tile.  `load(c, v)` supplies the fp32
+// accumulator of columns [c, c+16) for this thread's row (feature), either
+// straight from TMEM or as the sum of the split-K partials.
+template <int BN, int EPI, typename Loader>
+__device__ __forceinline__ void epilogue_tile(const Args& a, int feat_tile, int tok_tile, int split, int row,
+                                              int lane, Loader&& load) {
   const int tok0 = tok_tile * BN;
   if constexpr (EPI == kEpiSwiGLU) {
     // Weight rows are interleaved per 32-row group: 16 gate rows then the 16
@@ -76,8 +82,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, uint32_t taddr, int
     for (int c = 0; c < BN; c += 16) {
       if (tok0 + c >= a.M) break;
       float v[16];
-      tmem_ld_32x32b_x16(taddr + c, v);
-      tmem_wait_ld();
+      load(c, v);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const float up = __shfl_down_sync(0xffffffffu, v[j], 16);
@@ -95,8 +100,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, uint32_t taddr, int
     for (int c = 0; c < BN; c += 16) {
       if (tok0 + c >= a.M) break;
       float v[16];
-      tmem_ld_32x32b_x16(taddr + c, v);
-      tmem_wait_ld();
+      load(c, v);
       if (!fvalid) continue;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -115,6 +119,24 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, uint32_t taddr, int
       }
     }
   }
+}
+
+// Named barrier of the four epilogue warps (threads 64..191).
+__device__ __forceinline__ void epi_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Same barrier, returning whether any epilogue thread passed `pred` = true, so
+// the four warps always leave the tile loop together (no warp can be left
+// waiting at a later named barrier after another one gave up).
+__device__ __forceinline__ bool epi_barrier_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return r != 0;
 }
 
 template <int BN, int EPI>
@@ -251,18 +273,113 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int q = warp & 3;  // a warp may only touch TMEM lanes [32*(warp%4), +32)
     const int row = q * 32 + lane;
+    __shared__ int fix_last;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int ft, tt, sp;
       decode_tile(a, t, ft, tt, sp);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status, kStatusGemmTimeout)) break;
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status, kStatusGemmTimeout);
+      if (epi_barrier_or(!ok)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      epilogue_tile<BN, EPI>(a, taddr, ft, tt, sp, row, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      auto from_tmem = [&](int c, float (&v)[16]) {
+        tmem_ld_32x32b_x16(taddr + c, v);
+        tmem_wait_ld();
+      };
+      if (!a.fixup) {
+        epilogue_tile<BN, EPI>(a, ft, tt, sp, row, lane, from_tmem);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      } else {
+        // split-K fixup.  Splits arrive in completion order; the last one to
+        // arrive keeps its accumulator in TMEM and waits (bounded) only for the
+        // splits that already arrived and are writing their fp32 partials to
+        // the L2-resident workspace, so no CTA ever waits on one that may not
+        // be running.  It then sums the partials and runs the fused epilogue.
+        const long tile_id = (long)ft * a.num_tok_tiles + tt;
+        int* arrive = a.fix_count + 2 * tile_id;
+        int* written = arrive + 1;
+        if (threadIdx.x == 64) fix_last = atomicAdd(arrive, 1);
+        epi_barrier();
+        const int slot = fix_last;  // arrival index (read before anyone rewrites fix_last)
+        const bool last = (slot == a.splits - 1);
+        // partial layout per (tile, slot): [BN/4][128 rows] float4, coalesced across a warp
+        float4* ws4 = reinterpret_cast<float4*>(a.fix_ws) + (tile_id * a.splits) * (BN / 4) * BM;
+        const int tok0 = tt * BN;
+        bool timed_out = false;
+        if (!last) {
+          float4* mine = ws4 + (long)slot * (BN / 4) * BM + row;
+          for (int c = 0; c < BN; c += 16) {
+            if (tok0 + c >= a.M) break;
+            float v[16];
+            from_tmem(c, v);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              __stcg(mine + (long)((c >> 2) + j) * BM, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+          __threadfence();
+          epi_barrier();
+          if (threadIdx.x == 64) atomicAdd(written, 1);
+        } else {
+          if (threadIdx.x == 64) {
+            const uint64_t t0 = globaltimer_ns();
+            while (true) {
+              int w;
+              asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(w) : "l"(written) : "memory");
+              if (w >= a.splits - 1) break;
+              if (globaltimer_ns() - t0 > kLocalWaitTimeoutNs) {
+                atomicOr(a.status, kStatusGemmTimeout);
+                timed_out = true;
+                break;
+              }
+            }
+          }
+          timed_out = epi_barrier_or(timed_out);
+          __threadfence();
+          if (!timed_out) {
+            const float4* parts = ws4 + row;
+            auto summed = [&](int c, float (&v)[16]) {
+              float4 acc4[4] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f),
+                                make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+              for (int s2 = 0; s2 < a.splits - 1; ++s2) {
+                const float4* p = parts + ((long)s2 * (BN / 4) + (c >> 2)) * BM;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float4 q4 = __ldcg(p + (long)j * BM);
+                  acc4[j].x += q4.x;
+                  acc4[j].y += q4.y;
+                  acc4[j].z += q4.z;
+                  acc4[j].w += q4.w;
+                }
+              }
+              from_tmem(c, v);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                v[4 * j] += acc4[j].x;
+                v[4 * j + 1] += acc4[j].y;
+                v[4 * j + 2] += acc4[j].z;
+                v[4 * j + 3] += acc4[j].w;
+              }
+            };
+            epilogue_tile<BN, EPI>(a, ft, tt, sp, row, lane, summed);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+          epi_barrier();
+          if (threadIdx.x == 64) {  // leave the counters at zero for the next launch
+            *arrive = 0;
+            *written = 0;
+          }
+        }
+        epi_barrier();  // fix_last is rewritten by the next tile
+        if (timed_out) break;
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -318,19 +435,26 @@ int gemm_tiles(int M, int N, int epi) {
   return ntok * ((nrows + gemm::BM - 1) / gemm::BM);
 }
 
+int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits) {
+  const int bn = gemm_pick_bn(int(M));
+  const int64_t tiles = ((M + bn - 1) / bn) * ((N + gemm::BM - 1) / gemm::BM);
+  return tiles * splits * bn * gemm::BM;
+}
+
 int gemm_default_splits(int M, int N, int K, int device) {
   const int tiles = gemm_tiles(M, N, kEpiPartialF32);
   const int num_kb = (K + gemm::BK - 1) / gemm::BK;
   const int sms = num_sms(device);
   if (tiles >= sms) return 1;
-  int splits = (sms + tiles - 1) / tiles;
-  splits = std::min(splits, std::max(1, num_kb / 4));
+  int splits = sms / tiles;  // whole waves only
+  splits = std::min(splits, std::max(1, num_kb / 8));
   return std::max(1, std::min(splits, 16));
 }
 
 void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
-              const torch::Tensor& status) {
+              const torch::Tensor& status, const c10::optional<torch::Tensor>& fix_ws,
+              const c10::optional<torch::Tensor>& fix_count) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "gemm: tensors must be on CUDA");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: x and w must be bf16");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm: x [M,K], w [N,K]");
@@ -358,6 +482,9 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.ldr = 0;
   a.bias = nullptr;
   a.status = status.data_ptr<int>();
+  a.fix_ws = nullptr;
+  a.fix_count = nullptr;
+  a.fixup = 0;
 
   switch (epi) {
     case kEpiBF16:
@@ -388,6 +515,24 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
       break;
     default:
       TORCH_CHECK(false, "gemm: unknown epilogue ", epi);
+  }
+  if (epi != kEpiPartialF32 && splits > 1) {
+    // split-K with in-kernel fixup (last arriving split reduces + runs the epilogue)
+    int s = std::min<int>(int(splits), a.num_kb);
+    a.kb_per_split = (a.num_kb + s - 1) / s;
+    a.splits = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;
+    if (a.splits > 1) {
+      TORCH_CHECK(fix_ws.has_value() && fix_count.has_value(), "gemm split-K fixup needs a workspace");
+      const int64_t tiles = (int64_t)a.num_feat_tiles * a.num_tok_tiles;
+      TORCH_CHECK(fix_ws->scalar_type() == at::kFloat &&
+                      fix_ws->numel() >= tiles * a.splits * bn * gemm::BM,
+                  "gemm fixup workspace too small: need ", tiles * a.splits * bn * gemm::BM, " floats");
+      TORCH_CHECK(fix_count->scalar_type() == at::kInt && fix_count->numel() >= 2 * tiles,
+                  "gemm fixup counters too small");
+      a.fix_ws = fix_ws->data_ptr<float>();
+      a.fix_count = fix_count->data_ptr<int>();
+      a.fixup = 1;
+    }
   }
   if (bias.has_value() && bias->defined()) {
     TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N, "gemm: bias must be bf16 [N]");

@@ -84,6 +84,77 @@ __global__ void add_rmsnorm_kernel(const void* __restrict__ delta, int S, long l
     out[row * ldo + i] = __float2bfloat16(buf[i] * inv * __bfloat162float(w[i]));
 }
 
+// Vectorised variants: one 16-byte vector (8 x bf16) per thread, the row held
+// in registers (H <= 8192, H % 8 == 0, 16-byte aligned rows).
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 t = __bfloat1622float2(h[k]);
+    f[2 * k] = t.x;
+    f[2 * k + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 f32_to_bf16x8(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+  return u;
+}
+
+template <int kMode>  // 0: plain rmsnorm(x); 1: residual += bf16 delta; 2: residual += sum of f32 partials
+__global__ void rmsnorm_vec_kernel(const void* __restrict__ delta, int S, long ldd, __nv_bfloat16* __restrict__ resid,
+                                   long ldr, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                   long ldo, int M, int H, float eps) {
+  __shared__ float red[33];
+  const long row = blockIdx.x;
+  const int i = threadIdx.x * 8;
+  const bool active = i < H;
+  float v[8];
+  float ss = 0.f;
+  if (active) {
+    uint4 r = *reinterpret_cast<const uint4*>(resid + row * ldr + i);
+    bf16x8_to_f32(r, v);
+    if constexpr (kMode == 1) {
+      float d[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(delta) + row * ldd + i), d);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] += d[k];
+    } else if constexpr (kMode == 2) {
+      const float* dp = reinterpret_cast<const float*>(delta);
+      for (int sidx = 0; sidx < S; ++sidx) {
+        const float4 a = *reinterpret_cast<const float4*>(dp + ((long)sidx * M + row) * H + i);
+        const float4 b = *reinterpret_cast<const float4*>(dp + ((long)sidx * M + row) * H + i + 4);
+        v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+        v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+      }
+    }
+    if constexpr (kMode != 0) {
+      // the residual stream is stored in bf16 (the checkpoint dtype); normalise the rounded value
+      const uint4 nb = f32_to_bf16x8(v);
+      *reinterpret_cast<uint4*>(resid + row * ldr + i) = nb;
+      bf16x8_to_f32(nb, v);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+  }
+  const float tot = block_sum(ss, red);
+  const float inv = rsqrtf(tot / H + eps);
+  if (active) {
+    float wf[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(w + i), wf);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = v[k] * inv * wf[k];
+    *reinterpret_cast<uint4*>(out + row * ldo + i) = f32_to_bf16x8(v);
+  }
+}
+
+bool vec_ok(int H, const void* p, long ld) {
+  return (H % 8 == 0) && H <= 8192 && (reinterpret_cast<uintptr_t>(p) % 16 == 0) && (ld % 8 == 0);
+}
+int vec_threads(int H) { return ((H / 8 + 31) / 32) * 32; }
+
 // LayerNorm with optional residual input (x + resid), affine.
 __global__ void layernorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
                                  const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b,
@@ -135,12 +206,13 @@ __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, long
                                      const int* __restrict__ slots, const float* __restrict__ cos_sin,
                                      __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
                                      long layer_stride, int nq, int nkv, const __nv_bfloat16* __restrict__ qn,
-                                     const __nv_bfloat16* __restrict__ kn, float eps) {
+                                     const __nv_bfloat16* __restrict__ kn, float eps, long max_pos) {
   constexpr int D = 128;
   const long t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
-  const long p = pos[t];
+  long p = pos[t];
+  p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);  // the table bounds every read
   const int slot = slots != nullptr ? slots[t] : -1;
   const float* cs = cos_sin + p * D;
   const __nv_bfloat16* row = qkv + t * ldq;
@@ -192,6 +264,15 @@ void rmsnorm(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out,
   const int M = x.size(0), H = x.size(1);
   if (M == 0) return;
   const at::cuda::CUDAGuard g(x.device());
+  if (vec_ok(H, x.data_ptr(), x.stride(0)) && vec_ok(H, out.data_ptr(), out.stride(0))) {
+    // plain rmsnorm: read x through the "residual" slot, no write-back
+    rmsnorm_vec_kernel<0><<<M, vec_threads(H), 0, at::cuda::getCurrentCUDAStream()>>>(
+        nullptr, 0, 0, reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+        out.stride(0), M, H, float(eps));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   rmsnorm_kernel<<<M, kNormThreads, H * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
@@ -207,6 +288,26 @@ void add_rmsnorm(const torch::Tensor& delta, torch::Tensor& residual, const torc
   const at::cuda::CUDAGuard g(residual.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const size_t sm = H * sizeof(float);
+  const bool vec = vec_ok(H, residual.data_ptr(), residual.stride(0)) && vec_ok(H, out.data_ptr(), out.stride(0)) &&
+                   vec_ok(H, delta.data_ptr(), delta.dim() == 2 ? delta.stride(0) : H);
+  if (vec) {
+    if (delta.scalar_type() == at::kFloat) {
+      TORCH_CHECK(delta.is_contiguous() && delta.numel() % ((int64_t)M * H) == 0, "add_rmsnorm: f32 partials [S,M,H]");
+      rmsnorm_vec_kernel<2><<<M, vec_threads(H), 0, stream>>>(
+          delta.data_ptr(), int(delta.numel() / ((int64_t)M * H)), H,
+          reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), residual.stride(0),
+          reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+          out.stride(0), M, H, float(eps));
+    } else {
+      TORCH_CHECK(delta.scalar_type() == at::kBFloat16 && delta.stride(1) == 1, "add_rmsnorm: delta bf16 [M,H]");
+      rmsnorm_vec_kernel<1><<<M, vec_threads(H), 0, stream>>>(
+          delta.data_ptr(), 1, delta.stride(0), reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
+          residual.stride(0), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), M, H, float(eps));
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   if (delta.scalar_type() == at::kFloat) {
     TORCH_CHECK(delta.is_contiguous() && delta.numel() % ((int64_t)M * H) == 0, "add_rmsnorm: f32 partials [S,M,H]");
     const int S = delta.numel() / ((int64_t)M * H);
@@ -280,7 +381,7 @@ void rope_kv_write(const torch::Tensor& qkv, const torch::Tensor& positions, con
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),
       slot_mapping.data_ptr<int>(), cos_sin.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(kv_cache.data_ptr()), layer_stride, int(num_q_heads), int(num_kv_heads), qn,
-      kn, float(eps));
+      kn, float(eps), cos_sin.size(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

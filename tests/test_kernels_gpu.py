@@ -246,3 +246,37 @@ def test_sampling_distribution():
                    torch.zeros(n, device="cuda", dtype=torch.int64))
     freq = torch.bincount(s.long(), minlength=V).float() / n
     assert (freq - probs).abs().max().item() < 0.03
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(1, 384, 1024, 3), (64, 4096, 4096, 4), (256, 6144, 4096, 3),
+                                          (200, 512, 2048, 5), (512, 1000, 4160, 2)])
+@pytest.mark.parametrize("epi", ["bf16", "swiglu", "residual"])
+def test_gemm_splitk_fixup(M, N, K, splits, epi):
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(M + N + K)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    if epi == "swiglu":
+        N = (N // 32) * 32
+        g = torch.randn(N // 2, K, device="cuda", dtype=torch.bfloat16) * 0.05
+        u = torch.randn(N // 2, K, device="cuda", dtype=torch.bfloat16) * 0.05
+        w = ops.interleave_gate_up(g, u)
+        for _ in range(2):  # twice: the per-tile counters must be left at zero
+            y = ops.gemm(x, w, epi=ops.EPI_SWIGLU, splits=splits)
+            assert rel_err(y, ref.swiglu(ref.gemm(x, g), ref.gemm(x, u))) < 1.5e-2
+        return
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    if epi == "bf16":
+        for _ in range(2):
+            assert rel_err(ops.gemm(x, w, splits=splits), ref.gemm(x, w)) < 1e-2
+    else:
+        r = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+        yr = ops.gemm(x, w, epi=ops.EPI_RESIDUAL, resid=r, splits=splits)
+        assert rel_err(yr, ref.gemm(x, w) + r.float()) < 1e-2
+
+
+def test_gemm_auto_splits_decode_shapes():
+    ops, ref = _ops(), _ref()
+    for M, N, K in [(256, 4096, 14336), (8, 6144, 4096)]:
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+        assert rel_err(ops.gemm(x, w), ref.gemm(x, w)) < 1e-2

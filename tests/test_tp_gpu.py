@@ -1,0 +1,37 @@
+"""Tensor parallel end-to-end on 2+ GPUs (NCCL baseline and fused NVLink paths)."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(n, mode, graphs="graphs", model="tiny-tp", port=29611):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE=os.environ.get("NCCL_NVLS_ENABLE", "1"))
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={port}",
+           os.path.join(ROOT, "tests", "tp_worker.py"), mode, graphs, model]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads(lines[-1])
+    assert res["ok"] and res["ranks_agree"] and res["status"] == 0, res
+    return res
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_tp_nccl(n):
+    _run(n, "nccl", port=29611 + n)
+
+
+@pytest.mark.parametrize("n", [2, 8])
+def test_tp_nccl_eager(n):
+    _run(n, "nccl", graphs="eager", port=29631 + n)
