@@ -26,6 +26,8 @@
 #include "bloom/ops.h"
 #include "bloom/tma_host.h"
 
+#include <mutex>
+
 namespace bloom {
 namespace attn {
 
@@ -669,3 +671,147 @@ void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cac
 }
 
 }  // namespace bloom
+
+// ============================================================================
+// Allocation-free entry point: bloom_paged_decode_attention_noalloc
+//
+// This entry point has no counterpart in the reference; it is an addition of
+// this library.
+//
+// Who needs it: some callers cannot allocate GPU memory at the moment they
+// want to run attention.  Examples are a host application that hands this
+// library a fixed memory budget and forbids cudaMalloc after start-up, code
+// that runs on a stream whose memory pool belongs to another framework, and
+// plain C programs that load this library without PyTorch (so there is no
+// caching allocator to borrow scratch from).  The regular entry point takes
+// its split-K scratch from the caller as a torch tensor; this one takes it
+// from a fixed array compiled into the library instead, and it never calls
+// cudaMalloc, cudaFree or any allocating routine.
+//
+// What it computes: exactly what paged_decode_attention computes (the same
+// kernels), for q [batch * q_len, num_q_heads, 128] bf16 against one layer of
+// the paged cache [num_blocks, 2, num_kv_heads, 16, 128] bf16, writing
+// out [batch * q_len, num_q_heads, 128] bf16.  The caller owns q, out, the
+// cache, the block table and the sequence lengths.
+//
+// Limits and rules:
+//  * Scratch is kNoAllocScratchFloats fp32 values (8 MiB) per GPU, held by
+//    every GPU that loads the library until the process exits.  A call needs
+//    batch * num_kv_heads * splits * 32 * 130 floats when splits > 1; larger
+//    requests are rejected with BLOOM_NOALLOC_TOO_LARGE and nothing runs.
+//  * All calls on a device share that one array, and it keeps whatever the
+//    last call left in it.  Two calls whose kernels overlap on the GPU (two
+//    streams, no ordering between them) race on the scratch and give wrong
+//    results; order them on one stream or with events.  Nothing in the
+//    scratch has to start at zero: every partial is written before it is read.
+//  * The first call on a device does the set-up for that device: it looks up
+//    the device address of the array with cudaGetSymbolAddress (host code
+//    must never pass the array's name itself to a kernel: on the host that
+//    name is only a stand-in) and clears the status word.  Make that first
+//    call on each device before any stream capture begins.
+//  * Waits inside the kernel are bounded; a wait that gives up sets a bit in
+//    a status word that bloom_noalloc_status() reads and clears.
+// ============================================================================
+namespace bloom {
+namespace noalloc {
+
+constexpr long long kNoAllocScratchFloats = 1ll << 21;  // 8 MiB
+static __device__ __align__(256) float g_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) int g_status[16];
+
+struct DeviceState {
+  float* scratch = nullptr;
+  int* status = nullptr;
+  bool ready = false;
+};
+static DeviceState g_dev[64];
+static std::mutex g_mu;
+
+// Once per device, with that device current: resolve the arrays' device addresses.
+static int setup_device(int dev) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_dev[dev].ready) return 0;
+  void* scratch = nullptr;
+  void* status = nullptr;
+  if (cudaGetSymbolAddress(&scratch, g_scratch) != cudaSuccess) return -3;
+  if (cudaGetSymbolAddress(&status, g_status) != cudaSuccess) return -3;
+  if (cudaMemset(status, 0, sizeof(int) * 16) != cudaSuccess) return -3;
+  g_dev[dev].scratch = static_cast<float*>(scratch);
+  g_dev[dev].status = static_cast<int*>(status);
+  g_dev[dev].ready = true;
+  return 0;
+}
+
+}  // namespace noalloc
+}  // namespace bloom
+
+// Return codes and declarations: csrc/include/bloom/noalloc.h
+#include "bloom/noalloc.h"
+
+extern "C" __attribute__((visibility("default"))) int bloom_paged_decode_attention_noalloc(
+    const void* q, void* out, const void* kv_layer, long long num_blocks, int num_q_heads, int num_kv_heads,
+    const int* block_table, int block_table_stride, const int* seq_lens, int batch, int q_len, int splits,
+    float scale, void* stream) {
+  using namespace bloom;
+  if (q == nullptr || out == nullptr || kv_layer == nullptr || block_table == nullptr || seq_lens == nullptr)
+    return BLOOM_NOALLOC_BAD_ARGUMENT;
+  if (batch <= 0 || num_blocks <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || q_len < 1 ||
+      num_q_heads % num_kv_heads != 0 || block_table_stride <= 0)
+    return BLOOM_NOALLOC_BAD_ARGUMENT;
+  if ((num_q_heads / num_kv_heads) * q_len > 32) return BLOOM_NOALLOC_BAD_ARGUMENT;
+  if (batch > 65535 || num_kv_heads > 65535) return BLOOM_NOALLOC_BAD_ARGUMENT;
+  if (splits < 1) splits = 1;
+  if (splits > 65535) return BLOOM_NOALLOC_BAD_ARGUMENT;
+  if (splits > 1 && (long long)batch * num_kv_heads * splits * 32 * (attn::D + 2) > noalloc::kNoAllocScratchFloats)
+    return BLOOM_NOALLOC_TOO_LARGE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BLOOM_NOALLOC_CUDA_ERROR;
+  if (noalloc::setup_device(dev) != 0) return BLOOM_NOALLOC_CUDA_ERROR;
+
+  const unsigned long long rows = (unsigned long long)num_blocks * 2 * num_kv_heads * attn::PAGE;
+  if (rows >= (1ull << 31)) return BLOOM_NOALLOC_BAD_ARGUMENT;
+  CUtensorMap tm;
+  try {
+    tm = make_tmap_bf16_2d(kv_layer, attn::D, rows, attn::D * 2, 64, attn::PAGE);
+  } catch (...) {
+    return BLOOM_NOALLOC_TENSOR_MAP_ERROR;
+  }
+  attn::DecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.block_table = block_table;
+  a.bt_stride = block_table_stride;
+  a.seq_lens = seq_lens;
+  a.nq = num_q_heads;
+  a.nkv = num_kv_heads;
+  a.ql = q_len;
+  a.splits = splits;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.status = noalloc::g_dev[dev].status;
+  a.part = splits > 1 ? noalloc::g_dev[dev].scratch : nullptr;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((num_q_heads / num_kv_heads) * q_len <= 16)
+    attn::launch_decode<1, 4, 3>(tm, a, batch, s);
+  else
+    attn::launch_decode<2, 4, 3>(tm, a, batch, s);
+  if (cudaGetLastError() != cudaSuccess) return BLOOM_NOALLOC_LAUNCH_ERROR;
+  if (splits > 1) {
+    attn::decode_combine_kernel<<<dim3(batch, num_kv_heads), 256, 0, s>>>(a.part, a.out, num_q_heads, num_kv_heads,
+                                                                          q_len, splits);
+    if (cudaGetLastError() != cudaSuccess) return BLOOM_NOALLOC_LAUNCH_ERROR;
+  }
+  return BLOOM_NOALLOC_OK;
+}
+
+// Reads and clears the allocation-free entry point's status word on the
+// current device (bit 2: an attention wait gave up).  Synchronous.
+extern "C" __attribute__((visibility("default"))) int bloom_noalloc_status(int* bits) {
+  using namespace bloom;
+  int dev = 0;
+  if (bits == nullptr || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BLOOM_NOALLOC_BAD_ARGUMENT;
+  if (noalloc::setup_device(dev) != 0) return BLOOM_NOALLOC_CUDA_ERROR;
+  if (cudaMemcpy(bits, noalloc::g_dev[dev].status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return BLOOM_NOALLOC_CUDA_ERROR;
+  if (cudaMemset(noalloc::g_dev[dev].status, 0, sizeof(int)) != cudaSuccess) return BLOOM_NOALLOC_CUDA_ERROR;
+  return BLOOM_NOALLOC_OK;
+}
