@@ -130,7 +130,7 @@ def main():
     ap.add_argument("--prompt-max", type=int, default=2048)
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
-    ap.add_argument("--comm", default=os.environ.get("BLOOM_COMM", "nccl"), choices=["nccl", "fused"])
+    ap.add_argument("--comm", default=os.environ.get("BLOOM_COMM", "fused"), choices=["nccl", "fused"])
     ap.add_argument("--no-graphs", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -152,7 +152,8 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     group = dist.group.WORLD if world > 1 else None
-    comm = Communicator(rank, world, dev, group, mode=args.comm)
+    comm = Communicator(rank, world, dev, group, mode=args.comm, max_tokens=max(args.max_batched_tokens, args.requests),
+                        hidden=preset(args.model).hidden_size)
     tp = TPInfo(rank=rank, size=world, group=group, comm=comm)
 
     cfg = preset(args.model)

@@ -19,6 +19,8 @@ class ExtensionMissing(RuntimeError):
 def _load(name: str):
     if name in _cache:
         return _cache[name]
+    import torch  # noqa: F401  (loads libc10/libtorch that the extensions link against)
+
     try:
         mod = importlib.import_module(f"bloom_b200.{name}")
     except ImportError as e:  # pragma: no cover - depends on the build state

@@ -278,6 +278,17 @@ class DecoderLM:
             return t
         return self.tp.comm.all_reduce(t)
 
+    def _row_parallel_norm(self, inp: torch.Tensor, w_mat: torch.Tensor, residual: torch.Tensor,
+                           norm_w: torch.Tensor, eps: float) -> torch.Tensor:
+        """x = rmsnorm(residual += inp @ w_mat^T summed over TP ranks) * norm_w."""
+        fused = self.tp.comm.fused if (self.tp.size > 1 and self.tp.comm is not None) else None
+        if fused is not None:
+            T = inp.shape[0]
+            ops.gemm(inp, w_mat, fused.partial(T))
+            return fused.allreduce_rmsnorm(T, residual, norm_w, eps)
+        d = self._reduce(ops.gemm(inp, w_mat))
+        return ops.add_rmsnorm(d, residual, norm_w, eps)
+
     def forward(self, s: StepInputs, kv_cache: torch.Tensor) -> torch.Tensor:
         """Returns the final-normed hidden states of the logits rows [NL, H] (bf16)."""
         cfg = self.cfg
@@ -303,15 +314,14 @@ class DecoderLM:
                 ops.paged_prefill_attention(q[Bd:], kv_cache, li, s.prefill_block_table, s.prefill_ctx_lens,
                                             s.prefill_cu_q, s.tile_seq, s.tile_start, attn[Bd:], scale=self.scale)
             a2 = attn.view(T, self.nq * cfg.head_dim)
-            o = self._reduce(ops.gemm(a2, lay["o"]))
-            x = ops.add_rmsnorm(o, residual, lay["ln2"], eps)
+            x = self._row_parallel_norm(a2, lay["o"], residual, lay["ln2"], eps)
+            nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
             if self.moe is not None:
                 d = self._reduce(self.moe.forward(li, x))
+                x = ops.add_rmsnorm(d, residual, nxt, eps)
             else:
                 act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU)
-                d = self._reduce(ops.gemm(act, lay["down"]))
-            nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
-            x = ops.add_rmsnorm(d, residual, nxt, eps)
+                x = self._row_parallel_norm(act, lay["down"], residual, nxt, eps)
         return x.index_select(0, s.logits_rows)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:

@@ -25,7 +25,8 @@ from .. import ops
 
 
 class Communicator:
-    def __init__(self, rank: int, size: int, device: torch.device, group=None, mode: str = "nccl"):
+    def __init__(self, rank: int, size: int, device: torch.device, group=None, mode: str = "nccl",
+                 max_tokens: int = 8192, hidden: int = 4096, timeout_s: float = 5.0):
         self.rank = rank
         self.size = size
         self.device = device
@@ -35,7 +36,8 @@ class Communicator:
         if mode == "fused" and size > 1:
             from .fused import FusedComm
 
-            self.fused = FusedComm(rank, size, device, group)
+            self.fused = FusedComm(rank, size, device, group, max_tokens=max_tokens, hidden=hidden,
+                                   timeout_s=timeout_s)
 
     # ------------------------------------------------------------ collectives
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:

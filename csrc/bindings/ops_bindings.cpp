@@ -1,4 +1,5 @@
 // pybind11 surface of bloom_b200._C (CUDA kernels for sm_100a).
+#include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include "bloom/ops.h"
@@ -25,4 +26,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_rows", &bloom::argmax_rows);
   m.def("sample_rows", &bloom::sample_rows);
   m.def("status_tensor", &bloom::status_tensor);
+  m.def("tp_flag_words", &bloom::tp_flag_words);
+  m.def("tp_allreduce_rmsnorm", &bloom::tp_allreduce_rmsnorm);
+  m.def("tp_allgather_rows", &bloom::tp_allgather_rows);
+  m.def("tp_barrier", &bloom::tp_barrier);
 }

@@ -34,6 +34,7 @@ py::dict metrics_dict(const PoolMetrics& m) {
 }  // namespace
 
 void register_cpu_ops(py::module_& m);  // csrc/runtime/cpu_ops.cpp
+void register_gguf(py::module_& m);     // csrc/runtime/gguf.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 host runtime: KV block manager, in-flight batching scheduler, CPU kernels";
@@ -180,4 +181,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("reset_prefix_cache", [](Scheduler& s) { s.blocks().reset_prefix_cache(); });
 
   register_cpu_ops(m);
+  register_gguf(m);
 }

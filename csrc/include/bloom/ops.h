@@ -61,6 +61,18 @@ void sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, 
                  const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
                  torch::Tensor& out);
 
+// Tensor-parallel collectives over peer memory (pointers are device addresses
+// valid in this process, one per rank: the local buffer and the peer mappings).
+int64_t tp_flag_words();
+void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::vector<int64_t>& x_ptrs,
+                          const std::vector<int64_t>& flag_ptrs, int64_t rank, torch::Tensor& residual,
+                          const torch::Tensor& w, double eps, int64_t T, double timeout_s,
+                          const torch::Tensor& status);
+void tp_allgather_rows(const torch::Tensor& src, const std::vector<int64_t>& dst_ptrs,
+                       const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t T, double timeout_s,
+                       const torch::Tensor& status);
+void tp_barrier(const std::vector<int64_t>& flag_ptrs, int64_t rank, double timeout_s, const torch::Tensor& status);
+
 // Status word.
 torch::Tensor status_tensor(int64_t device);
 

@@ -35,3 +35,13 @@ def test_tp_nccl(n):
 @pytest.mark.parametrize("n", [2, 8])
 def test_tp_nccl_eager(n):
     _run(n, "nccl", graphs="eager", port=29631 + n)
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_tp_fused(n):
+    _run(n, "fused", port=29651 + n)
+
+
+@pytest.mark.parametrize("n", [2, 8])
+def test_tp_fused_eager(n):
+    _run(n, "fused", graphs="eager", port=29671 + n)

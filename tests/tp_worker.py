@@ -27,7 +27,8 @@ def main():
     dev = torch.device("cuda", local)
     cfg = preset(name)
     w = random_weights(cfg, seed=3, std=0.08, device=dev)
-    comm = Communicator(rank, world, dev, dist.group.WORLD, mode)
+    comm = Communicator(rank, world, dev, dist.group.WORLD, mode, max_tokens=512, hidden=cfg.hidden_size,
+                        timeout_s=10.0)
     model = DecoderLM(cfg, TPInfo(rank, world, dist.group.WORLD, comm), dev)
     model.shard_full(w)
     eng = LLMEngine(model, EngineConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=512,
