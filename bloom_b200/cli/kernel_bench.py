@@ -70,6 +70,7 @@ def main():
     ap.add_argument("--only", default="")
     ap.add_argument("--M", type=int, default=0, help="only this token count for GEMMs")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--autotune", action="store_true", help="pick token tile / split-K by measurement first")
     args = ap.parse_args()
     ITERS[0] = args.iters
     from bloom_b200 import ops
@@ -107,10 +108,15 @@ def main():
             x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
             epi = ops.EPI_SWIGLU if name == "gate_up" else ops.EPI_BF16
             out = torch.empty(M, N // 2 if epi == ops.EPI_SWIGLU else N, device=dev, dtype=torch.bfloat16)
+            if args.autotune and M <= 512:
+                ops.gemm_autotune([(N, K, epi == ops.EPI_SWIGLU)], [M], dev)
             ms = timeit(lambda i=0: ops.gemm(x, ws[i % nrot], out, epi=epi))
             flops = 2.0 * M * N * K
             byt = N * K * 2 + M * K * 2 + out.numel() * 2
             extra = {"M": M, "N": N, "K": K}
+            tuned = ops.GEMM_TUNED.get((ops._m_bucket(M), N, K, epi == ops.EPI_SWIGLU)) if M <= 512 else None
+            if tuned:
+                extra["bn_splits"] = list(tuned)
             if M <= 512 and name in ("o_proj", "down"):
                 sp = ops.gemm_default_splits(M, N, K, 0)
                 if sp > 1:

@@ -80,6 +80,7 @@ class EngineConfig:
     enable_prefix_caching: bool = True
     chunked_prefill: bool = True
     use_cuda_graphs: bool = True
+    autotune: bool = True
     seed: int = 0
 
 
@@ -107,6 +108,10 @@ class LLMEngine:
         self.scheduler = rt.Scheduler(sc, ec.num_blocks, 16, ec.enable_prefix_caching)
         self.runner = ModelRunner(model, ec.num_blocks, ec.max_num_seqs, ec.max_num_batched_tokens,
                                   ec.max_model_len, ec.use_cuda_graphs)
+        if ec.autotune and dev.type == "cuda":
+            from .. import ops
+
+            ops.gemm_autotune(model.gemm_shapes(), self.runner.buckets + [ec.max_num_seqs], dev)
         self.scheduler.set_arena(self.runner.arena_host, self.runner.max_tokens, ec.max_num_seqs,
                                  self.runner.max_blocks)
         if ec.use_cuda_graphs:

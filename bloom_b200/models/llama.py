@@ -260,6 +260,16 @@ class DecoderLM:
         self.cos_sin = ops.rope_cos_sin(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, self.device,
                                         cfg.rope_scaling)
 
+    def gemm_shapes(self):
+        """(N, K, swiglu) of every distinct projection, for the GEMM autotuner."""
+        cfg = self.cfg
+        hd = cfg.head_dim
+        shapes = {((self.nq + 2 * self.nkv) * hd, cfg.hidden_size, False), (cfg.hidden_size, self.nq * hd, False),
+                  (self.vocab_local, cfg.hidden_size, False)}
+        if not cfg.is_moe:
+            shapes |= {(2 * self.inter, cfg.hidden_size, True), (cfg.hidden_size, self.inter, False)}
+        return sorted(shapes)
+
     def weight_bytes(self) -> int:
         n = 0
         for lay in self.layers:

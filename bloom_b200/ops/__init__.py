@@ -57,6 +57,7 @@ def gemm(
     bias: Optional[torch.Tensor] = None,
     resid: Optional[torch.Tensor] = None,
     splits: Optional[int] = None,
+    bn: Optional[int] = None,
 ) -> torch.Tensor:
     """y = x @ w.T on tcgen05 (x [M,K] bf16, w [N,K] bf16) with a fused epilogue.
 
@@ -70,13 +71,20 @@ def gemm(
     split to finish each tile sums the fp32 partials and runs the epilogue.
     """
     M, N = x.shape[0], w.shape[0]
+    K = x.shape[1]
+    if splits is None and bn is None:
+        tuned = GEMM_TUNED.get((_m_bucket(M), N, K, epi == EPI_SWIGLU)) if M <= 512 else None
+        if tuned is not None:
+            bn, splits = tuned
+    if bn is None:
+        bn = 0
     if splits is None:
         splits = 1
         if epi != EPI_PARTIAL_F32 and 0 < M <= 512:
-            splits = _C().gemm_default_splits(M, N, x.shape[1], x.device.index)
+            splits = _C().gemm_default_splits(M, N, K, x.device.index)
     fix_ws = fix_cnt = None
     if splits > 1 and epi != EPI_PARTIAL_F32:
-        fix_ws, fix_cnt = _fixup_buffers(x.device, _C().gemm_fixup_ws_floats(M, N, splits))
+        fix_ws, fix_cnt = _fixup_buffers(x.device, _C().gemm_fixup_ws_floats(M, N, splits, bn))
     if out is None:
         if epi == EPI_SWIGLU:
             out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
@@ -86,10 +94,67 @@ def gemm(
             out = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
         else:
             out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt)
+    _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt, bn)
     _count()
     return out
 
+
+# (M bucket, N, K, swiglu) -> (token tile, split-K) chosen by measurement (see gemm_autotune)
+GEMM_TUNED: dict = {}
+_M_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512)
+
+
+def _m_bucket(M: int) -> int:
+    for b in _M_BUCKETS:
+        if M <= b:
+            return b
+    return M
+
+
+def gemm_autotune(shapes, Ms, device=None, reps: int = 3) -> dict:
+    """Time (token tile, split-K) candidates for every (M, N, K, swiglu) and keep
+    the fastest; `shapes` = [(N, K, swiglu)], `Ms` = batch sizes (<= 512).
+    Timing: CUDA events around `reps` back-to-back launches after a warm-up."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    for (N, K, swiglu) in shapes:
+        w = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
+        for M in sorted(set(_m_bucket(m) for m in Ms if 0 < m <= 512)):
+            key = (M, N, K, swiglu)
+            if key in GEMM_TUNED:
+                continue
+            x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+            epi = EPI_SWIGLU if swiglu else EPI_BF16
+            out = torch.empty(M, N // 2 if swiglu else N, device=dev, dtype=torch.bfloat16)
+            best = None
+            nkb = (K + 63) // 64
+            for bn in (16, 32, 64, 128, 256):
+                if bn < M and M // bn > 8 or bn >= 2 * M and bn > 16:
+                    continue
+                tiles = ((N + 127) // 128) * ((M + bn - 1) // bn)
+                for sp in (1, 2, 3, 4, 6, 8, 12, 16):
+                    if sp > 1 and (tiles * sp > 2 * sms or nkb // sp < 4):
+                        continue
+                    try:
+                        gemm(x, w, out, epi=epi, bn=bn, splits=sp)
+                        torch.cuda.synchronize(dev)
+                        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        # keep the GPU busy while the host queues the launches, so the
+                        # event interval holds device time only
+                        torch.cuda._sleep(2_000_000)
+                        a.record()
+                        for _ in range(reps):
+                            gemm(x, w, out, epi=epi, bn=bn, splits=sp)
+                        b.record()
+                        b.synchronize()
+                        ms = a.elapsed_time(b) / reps
+                    except RuntimeError:
+                        continue
+                    if best is None or ms < best[0]:
+                        best = (ms, bn, sp)
+            if best is not None:
+                GEMM_TUNED[key] = (best[1], best[2])
+    return GEMM_TUNED
 
 _FIXUP: dict = {}
 

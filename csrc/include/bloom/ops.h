@@ -20,8 +20,8 @@ enum GemmEpilogue : int {
 void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
               const torch::Tensor& status, const c10::optional<torch::Tensor>& fix_ws,
-              const c10::optional<torch::Tensor>& fix_count);
-int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits);
+              const c10::optional<torch::Tensor>& fix_count, int64_t bn_override);
+int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits, int64_t bn_override);
 int gemm_pick_bn(int M);
 int gemm_default_splits(int M, int N, int K, int device);
 

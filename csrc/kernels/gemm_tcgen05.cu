@@ -435,8 +435,8 @@ int gemm_tiles(int M, int N, int epi) {
   return ntok * ((nrows + gemm::BM - 1) / gemm::BM);
 }
 
-int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits) {
-  const int bn = gemm_pick_bn(int(M));
+int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits, int64_t bn_override) {
+  const int bn = bn_override > 0 ? int(bn_override) : gemm_pick_bn(int(M));
   const int64_t tiles = ((M + bn - 1) / bn) * ((N + gemm::BM - 1) / gemm::BM);
   return tiles * splits * bn * gemm::BM;
 }
@@ -454,7 +454,7 @@ int gemm_default_splits(int M, int N, int K, int device) {
 void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
               const torch::Tensor& status, const c10::optional<torch::Tensor>& fix_ws,
-              const c10::optional<torch::Tensor>& fix_count) {
+              const c10::optional<torch::Tensor>& fix_count, int64_t bn_override) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "gemm: tensors must be on CUDA");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: x and w must be bf16");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm: x [M,K], w [N,K]");
@@ -466,7 +466,13 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   const at::cuda::CUDAGuard guard(x.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 
-  const int bn = gemm_pick_bn(M);
+  int bn = gemm_pick_bn(M);
+  if (bn_override > 0) {
+    TORCH_CHECK(bn_override == 16 || bn_override == 32 || bn_override == 64 || bn_override == 128 ||
+                    bn_override == 256,
+                "gemm: token tile must be 16, 32, 64, 128 or 256");
+    bn = int(bn_override);
+  }
   gemm::Args a;
   a.M = M;
   a.N = N;
