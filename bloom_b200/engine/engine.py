@@ -38,6 +38,7 @@ class SamplingParams:
     min_tokens: int = 0
     ignore_eos: bool = False
     stop_token_ids: List[int] = field(default_factory=list)
+    json_mode: bool = False
 
     def to_native(self, default_seed: int):
         sp = _rt().SamplingParams()
@@ -118,6 +119,8 @@ class LLMEngine:
             self.scheduler.set_decode_buckets(sorted(self.runner.buckets))
             self.runner.capture_graphs()
         self.requests: Dict[int, RequestOutput] = {}
+        self.constraints: Dict[int, object] = {}
+        self.tokenizer = None  # set by the pipeline; needed for JSON-mode constraints
         self._seed_counter = ec.seed
         self.step_times: List[float] = []
 
@@ -146,9 +149,15 @@ class LLMEngine:
         rid = self.scheduler.add_request([int(t) for t in prompt_token_ids], params.to_native(self._seed_counter),
                                          priority)
         self.requests[rid] = RequestOutput(rid, list(prompt_token_ids), arrival_time=time.perf_counter())
+        if params.json_mode and self.tokenizer is not None:
+            from .structured import JsonConstraint, vocab_strings
+
+            self.constraints[rid] = JsonConstraint(vocab_strings(self.tokenizer, self.cfg.vocab_size),
+                                                   list(params.stop_token_ids) + list(self.cfg.eos_token_ids))
         return rid
 
     def abort(self, request_id: int) -> bool:
+        self.constraints.pop(request_id, None)
         ok = self.scheduler.abort(request_id)
         r = self.requests.get(request_id)
         if ok and r is not None:
@@ -167,6 +176,8 @@ class LLMEngine:
         if meta.num_tokens == 0:
             return []
         sampled = self.runner.execute(meta)
+        if self.constraints:
+            self._apply_constraints(sampled, meta)
         events = self.scheduler.update(sampled, meta.num_real_logits)
         now = time.perf_counter()
         out = []
@@ -178,13 +189,30 @@ class LLMEngine:
                 r.first_token_time = now
                 r.num_cached_tokens = 0
             r.token_ids.append(tok)
+            c = self.constraints.get(rid)
+            if c is not None:
+                c.advance(tok)
             if finished:
+                self.constraints.pop(rid, None)
                 r.finished = True
                 r.finish_reason = FINISH_REASONS.get(reason, "stop")
                 r.finish_time = now
             out.append(r)
         self.step_times.append(now - t0)
         return out
+
+    def _apply_constraints(self, sampled, meta) -> None:
+        """JSON mode: replace the sampled token of constrained rows by the best
+        candidate (top-256 logits) that keeps the output valid JSON."""
+        ids = self.scheduler.sampling_ids()
+        rows = [(i, sid) for i, sid in enumerate(ids) if sid in self.constraints]
+        if not rows or self.runner.last_logits is None or self.model.tp.size > 1:
+            return
+        logits = self.runner.last_logits
+        idx = torch.tensor([i for i, _ in rows], device=logits.device)
+        top = torch.topk(logits.index_select(0, idx).float(), k=min(256, logits.shape[1]), dim=1).indices.cpu()
+        for (row, sid), cand in zip(rows, top.tolist()):
+            sampled[row] = self.constraints[sid].choose(cand, int(sampled[row]))
 
     def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None,
                  on_token: Optional[Callable[[RequestOutput], None]] = None) -> List[RequestOutput]:

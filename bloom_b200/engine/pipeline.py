@@ -182,6 +182,7 @@ class InferencePipeline:
             dm.shard_full(load_weights(man))
         llm = LLMEngine(dm, EngineConfig(max_num_seqs=max_num_seqs, max_num_batched_tokens=max(ctx, 2048),
                                          max_model_len=ctx, use_cuda_graphs=use_cuda_graphs))
+        llm.tokenizer = tok
         spec = None
         if speculative in ("ngram", "draft"):
             from .speculative import make_speculator

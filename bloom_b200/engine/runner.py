@@ -73,6 +73,7 @@ class ModelRunner:
             ws = max(ws, ops.decode_workspace_numel(b, model.nkv, s))
         self.decode_ws = torch.empty(ws, dtype=torch.float32, device=self.device)
         self.graphs: Dict[int, tuple] = {}
+        self.last_logits: Optional[torch.Tensor] = None
         import os as _os
 
         self.check_finite = _os.environ.get("BLOOM_CHECK_FINITE", "0") == "1"
@@ -187,6 +188,7 @@ class ModelRunner:
                 rows = bad.nonzero().flatten().tolist()
                 raise FloatingPointError(f"non-finite logits in rows {rows} (T={m.num_tokens}, decode={m.num_decode}, "
                                          f"prefill={m.num_prefill})")
+        self.last_logits = logits
         toks = self._sample(logits, m, m.all_greedy)
         NL = m.num_logits
         self.sampled_host[:NL].copy_(toks[:NL], non_blocking=True)

@@ -1,0 +1,90 @@
+"""Structured output: JSON mode (response_format json_object / json_schema).
+
+Each constrained request carries a JSON recogniser (C++ `JsonDfa` in
+bloom_b200._runtime).  After the GPU forward of a step, the top-256 logits of
+the constrained rows are read back; the first candidate that keeps the
+output a valid JSON prefix is emitted, end-of-sequence only once the document
+is complete, and if no candidate qualifies the unconstrained token is kept
+(reference: executor/candle.rs:2584-3243 -- autocomplete_json, JsonDfa,
+filter_logits_by_grammar with top-256 candidates and EOS gating).
+`repair_json` closes an unfinished document (open strings and containers)
+when generation stops on the token limit.
+"""
+from __future__ import annotations
+
+import json
+from typing import Dict, List, Optional
+
+from .._ext import runtime as _rt
+
+TOPK = 256
+_VOCAB_CACHE: Dict[int, List[str]] = {}
+
+
+def vocab_strings(tokenizer, n: int) -> List[str]:
+    key = id(tokenizer)
+    v = _VOCAB_CACHE.get(key)
+    if v is None or len(v) < n:
+        v = [tokenizer.decode([i], skip_special_tokens=False) for i in range(n)]
+        _VOCAB_CACHE[key] = v
+    return v
+
+
+class JsonConstraint:
+    def __init__(self, vocab: List[str], eos: List[int]):
+        self.dfa = _rt().JsonDfa()
+        self.vocab = vocab
+        self.eos = list(eos)
+
+    def choose(self, candidates: List[int], fallback: int) -> int:
+        t = self.dfa.pick(candidates, self.vocab, self.eos)
+        return fallback if t < 0 else t
+
+    def advance(self, token: int) -> None:
+        if token in self.eos or not (0 <= token < len(self.vocab)):
+            return
+        self.dfa.feed(self.vocab[token])
+
+
+def constrain_params(params, response_format: dict, pipeline) -> None:
+    params.json_mode = True
+
+
+def repair_json(text: str) -> str:
+    """Close an unfinished JSON document; valid documents are returned unchanged."""
+    try:
+        json.loads(text)
+        return text
+    except ValueError:
+        pass
+    stack: List[str] = []
+    in_str = esc = False
+    start = text.find("{") if "{" in text else text.find("[")
+    if start < 0:
+        return "{}"
+    body = text[start:]
+    for c in body:
+        if in_str:
+            if esc:
+                esc = False
+            elif c == "\\":
+                esc = True
+            elif c == '"':
+                in_str = False
+            continue
+        if c == '"':
+            in_str = True
+        elif c in "{[":
+            stack.append("}" if c == "{" else "]")
+        elif c in "}]" and stack:
+            stack.pop()
+    out = body + ('"' if in_str else "")
+    out = out.rstrip().rstrip(",").rstrip(":")
+    if out.endswith(","):
+        out = out[:-1]
+    out += "".join(reversed(stack))
+    try:
+        json.loads(out)
+        return out
+    except ValueError:
+        return "{}"

@@ -26,6 +26,7 @@ EPI_F32 = 1
 EPI_SWIGLU = 2
 EPI_PARTIAL_F32 = 3
 EPI_RESIDUAL = 4
+EPI_GELU = 5
 
 
 def status(device: Optional[int] = None) -> torch.Tensor:
@@ -323,5 +324,30 @@ def sample(logits, temperature, top_p, top_k, seeds, offsets, out: Optional[torc
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
     _C().sample_rows(logits, temperature, top_p, top_k, seeds, offsets, out)
+    _count()
+    return out
+
+
+# ---------------------------------------------------------------- encoder (BERT)
+def bert_embed_ln(ids, pos, types, word, pemb, temb, g, b, eps: float, out=None):
+    if out is None:
+        out = torch.empty(ids.numel(), word.shape[1], dtype=torch.bfloat16, device=ids.device)
+    _C().bert_embed_ln(ids, pos, types, word, pemb, temb, g, b, out, eps)
+    _count()
+    return out
+
+
+def varlen_attention(qkv, cu_seqlens, num_heads: int, head_dim: int, max_len: int, scale: float, out=None):
+    if out is None:
+        out = torch.empty(qkv.shape[0], num_heads * head_dim, dtype=torch.bfloat16, device=qkv.device)
+    _C().varlen_attention(qkv, cu_seqlens, out, num_heads, head_dim, max_len, scale)
+    _count()
+    return out
+
+
+def mean_pool_l2(x, cu_seqlens, normalize: bool = True, out=None):
+    if out is None:
+        out = torch.empty(cu_seqlens.numel() - 1, x.shape[1], dtype=torch.float32, device=x.device)
+    _C().mean_pool_l2(x, cu_seqlens, out, normalize)
     _count()
     return out

@@ -1,0 +1,69 @@
+"""bloom_server: python -m bloom_b200.server --model PATH|PRESET [--host 127.0.0.1 --port 3000]
+
+Flags follow the reference server CLI (crates/server/src/cli.rs:18-327):
+--host/--port (127.0.0.1:3000), --max-concurrent 4, --context-size 2048,
+--api-key (repeatable; also BLOOM_API_KEYS comma-separated), --cors-origin,
+--device, --speculative/--draft-model/--num-speculative-tokens, --doctor
+(side-effect-free environment report).  --tp N runs tensor parallel when the
+server is launched with torchrun (rank 0 serves HTTP; other ranks follow).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+
+def build_parser():
+    ap = argparse.ArgumentParser(prog="bloom_server")
+    ap.add_argument("--model", "-m")
+    ap.add_argument("--host", default=os.environ.get("BLOOM_HOST", "127.0.0.1"))
+    ap.add_argument("--port", type=int, default=int(os.environ.get("BLOOM_PORT", "3000")))
+    ap.add_argument("--max-concurrent", type=int, default=4)
+    ap.add_argument("--context-size", type=int, default=2048)
+    ap.add_argument("--api-key", action="append", default=[])
+    ap.add_argument("--cors-origin", action="append", default=[])
+    ap.add_argument("--device", choices=["cpu", "gpu"], default="gpu")
+    ap.add_argument("--speculative", choices=["none", "ngram", "draft"], default="none")
+    ap.add_argument("--draft-model")
+    ap.add_argument("--num-speculative-tokens", type=int, default=5)
+    ap.add_argument("--model-id")
+    ap.add_argument("--doctor", action="store_true")
+    ap.add_argument("--enable-ifb", action="store_true", default=True,
+                    help="in-flight batching (always on for the GPU engine)")
+    return ap
+
+
+def main(argv=None) -> int:
+    args = build_parser().parse_args(argv)
+    if args.doctor:
+        from ..utils.doctor import doctor_report
+
+        print(json.dumps(doctor_report(args.model), indent=2))
+        return 0
+    if not args.model:
+        print("error: --model is required", file=sys.stderr)
+        return 2
+    keys = list(args.api_key) + [k for k in os.environ.get("BLOOM_API_KEYS", "").split(",") if k]
+    if args.host not in ("127.0.0.1", "localhost", "::1") and not keys:
+        print("error: refusing to listen on a non-loopback address without --api-key", file=sys.stderr)
+        return 2
+    from ..engine.pipeline import InferencePipeline
+    from .app import ServerSettings, create_app
+
+    pipe = InferencePipeline.load(args.model, device=args.device, context_size=args.context_size,
+                                  speculative=args.speculative, draft_model=args.draft_model,
+                                  num_speculative_tokens=args.num_speculative_tokens,
+                                  max_num_seqs=max(4, args.max_concurrent))
+    mid = args.model_id or os.path.basename(str(args.model).rstrip("/"))
+    app = create_app(pipe, ServerSettings(model_id=mid, api_keys=keys, context_size=pipe.context_size,
+                                          max_concurrent=args.max_concurrent, cors_origins=args.cors_origin))
+    import uvicorn
+
+    uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,760 @@
+"""OpenAI- and Ollama-compatible HTTP server (FastAPI / uvicorn).
+
+Routes (reference route table crates/server/src/lib.rs:2139-2244, 1811-1888):
+  GET  /health  /ready (bloom.readiness v3)  /metrics (Prometheus)
+  GET  /v1/models  /v1/models/{model}  /v1/observability  /v1/kv-cache-stats  /v1/backends
+  POST /v1/chat/completions  /v1/completions  /v1/responses  /v1/embeddings  /v1/rerank
+  GET  /v1/responses/{id}  /v1/responses/{id}/input_items
+  POST /v1/cancel/{request_id}
+  Ollama: GET /api/version /api/tags /api/ps, POST /api/show /api/chat /api/generate /api/embed /api/embeddings
+
+Behaviour kept from the reference (README.md:494-664, lib.rs:141-189):
+  * request limits (messages, stop sequences, max_tokens, embedding inputs, rerank documents, body size);
+  * a full request semaphore answers 429 with `Retry-After: 1`;
+  * every /v1 and /api response carries `x-request-id` (echoed when the client sent a valid one)
+    and `Cache-Control: no-store`;
+  * OpenAI-shaped errors on /v1, Ollama-shaped errors on /api, protocol-shaped 404/405;
+  * chat streams start with an assistant-role chunk; `stream_options.include_usage` adds a final
+    usage chunk before `data: [DONE]`; Ollama streams NDJSON;
+  * stop sequences are filtered across deltas (never leak a partial match);
+  * optional bearer API keys (`--api-key`), loopback-only unless keys are configured.
+"""
+from __future__ import annotations
+
+import asyncio
+import base64
+import json
+import re
+import struct
+import time
+import uuid
+from collections import OrderedDict
+from typing import Any, Dict, List, Optional
+
+from fastapi import FastAPI, Request
+from fastapi.responses import JSONResponse, PlainTextResponse, Response, StreamingResponse
+
+from ..engine.chat_template import render
+from ..engine.text import Detokenizer, StopSequenceFilter
+from .metrics import Metrics
+from .runtime import ServingRuntime
+
+MAX_CHAT_MESSAGES = 2048
+MAX_CHAT_CONTENT_BYTES = 768 * 1024
+MAX_GENERATED_TOKENS = 32768
+MAX_STOP_SEQUENCES = 4
+MAX_STOP_SEQUENCE_CHARS = 1024
+MAX_EMBEDDING_INPUTS = 256
+MAX_RERANK_DOCUMENTS = 256
+MAX_BODY_BYTES = 16 * 1024 * 1024
+MAX_REQUEST_ID_CHARS = 128
+READINESS_VERSION = 3
+SERVER_VERSION = "0.1.0"
+_RID = re.compile(r"^[A-Za-z0-9._:\-]{1,128}$")
+
+
+class APIError(Exception):
+    def __init__(self, status: int, message: str, type_: str = "invalid_request_error", param: Optional[str] = None,
+                 code: Optional[str] = None, headers: Optional[dict] = None):
+        super().__init__(message)
+        self.status, self.message, self.type, self.param, self.code = status, message, type_, param, code
+        self.headers = headers or {}
+
+
+def _openai_error(e: APIError) -> JSONResponse:
+    return JSONResponse({"error": {"message": e.message, "type": e.type, "param": e.param, "code": e.code}},
+                        status_code=e.status, headers=e.headers)
+
+
+def _ollama_error(e: APIError) -> JSONResponse:
+    return JSONResponse({"error": e.message}, status_code=e.status, headers=e.headers)
+
+
+class ResponseStore:
+    """Process-local store of /v1/responses results: 256 records FIFO, 24 h
+    (reference crates/server/src/response_store.rs:15-70)."""
+
+    def __init__(self, cap: int = 256, ttl_s: float = 24 * 3600):
+        self.cap, self.ttl = cap, ttl_s
+        self.items: "OrderedDict[str, tuple]" = OrderedDict()
+
+    def put(self, rid: str, resp: dict, inputs: list) -> None:
+        self.items[rid] = (time.time(), resp, inputs)
+        while len(self.items) > self.cap:
+            self.items.popitem(last=False)
+
+    def get(self, rid: str):
+        v = self.items.get(rid)
+        if v is None or time.time() - v[0] > self.ttl:
+            return None
+        return v
+
+
+class ServerSettings:
+    def __init__(self, model_id: str = "model", api_keys: Optional[List[str]] = None, context_size: int = 2048,
+                 max_concurrent: int = 4, allow_non_loopback: bool = False, cors_origins: Optional[List[str]] = None):
+        self.model_id = model_id
+        self.api_keys = list(api_keys or [])
+        self.context_size = context_size
+        self.max_concurrent = max_concurrent
+        self.allow_non_loopback = allow_non_loopback
+        self.cors_origins = cors_origins or []
+
+
+def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Optional[ServingRuntime] = None) -> FastAPI:
+    st = settings or ServerSettings()
+    metrics = Metrics()
+    rt = runtime or ServingRuntime(pipeline, st.model_id, st.max_concurrent, metrics)
+    rt.metrics = metrics
+    store = ResponseStore()
+    app = FastAPI(title="bloom_b200", version=SERVER_VERSION, docs_url=None, redoc_url=None, openapi_url=None)
+    app.state.runtime = rt
+    app.state.metrics = metrics
+    started = time.time()
+    is_embedding = getattr(pipeline, "is_embedding", False)
+
+    # ------------------------------------------------------------ middleware
+    @app.middleware("http")
+    async def envelope(request: Request, call_next):
+        path = request.url.path
+        api = path.startswith("/v1") or path.startswith("/api")
+        rid = request.headers.get("x-request-id")
+        if not rid or not _RID.match(rid):
+            rid = uuid.uuid4().hex
+        request.state.request_id = rid
+        if api and st.api_keys:
+            auth = request.headers.get("authorization", "")
+            tok = auth[7:] if auth.lower().startswith("bearer ") else None
+            if tok not in st.api_keys:
+                e = APIError(401, "invalid or missing API key", "authentication_error",
+                             headers={"WWW-Authenticate": 'Bearer realm="Bloom"'})
+                resp = _ollama_error(e) if path.startswith("/api") else _openai_error(e)
+                resp.headers["x-request-id"] = rid
+                resp.headers["cache-control"] = "no-store"
+                return resp
+        cl = request.headers.get("content-length")
+        if cl is not None and cl.isdigit() and int(cl) > MAX_BODY_BYTES:
+            e = APIError(413, "request body too large")
+            resp = _ollama_error(e) if path.startswith("/api") else _openai_error(e)
+        else:
+            metrics.requests_total += 1
+            resp = await call_next(request)
+        if api:
+            resp.headers["x-request-id"] = rid
+            resp.headers["cache-control"] = "no-store"
+        origin = request.headers.get("origin")
+        if origin and origin in st.cors_origins:
+            resp.headers["access-control-allow-origin"] = origin
+            resp.headers["vary"] = "Origin"
+        return resp
+
+    @app.exception_handler(APIError)
+    async def api_error(request: Request, e: APIError):
+        metrics.errors_total += 1
+        return _ollama_error(e) if request.url.path.startswith("/api") else _openai_error(e)
+
+    from starlette.exceptions import HTTPException as StarletteHTTPException
+
+    @app.exception_handler(StarletteHTTPException)
+    async def http_error(request: Request, e: StarletteHTTPException):
+        msg = "not found" if e.status_code == 404 else ("method not allowed" if e.status_code == 405 else str(e.detail))
+        err = APIError(e.status_code, msg, "invalid_request_error" if e.status_code != 404 else "not_found_error")
+        if request.url.path.startswith("/api"):
+            return _ollama_error(err)
+        return _openai_error(err)
+
+    from fastapi.exceptions import RequestValidationError
+
+    @app.exception_handler(RequestValidationError)
+    async def validation_error(request: Request, e: RequestValidationError):
+        err = APIError(400, f"invalid request: {e.errors()[:1]}")
+        return _ollama_error(err) if request.url.path.startswith("/api") else _openai_error(err)
+
+    async def body(request: Request) -> dict:
+        try:
+            d = await request.json()
+        except Exception:
+            raise APIError(400, "request body must be JSON")
+        if not isinstance(d, dict):
+            raise APIError(400, "request body must be a JSON object")
+        return d
+
+    # ------------------------------------------------------------ helpers
+    def check_model(name: Optional[str]) -> None:
+        if name not in (None, "", st.model_id) and not st.model_id.endswith(str(name)):
+            raise APIError(404, f"model {name!r} is not loaded", "not_found_error", "model", "model_not_found")
+
+    def sampling(d: dict, default_max: int = 128):
+        from ..engine.engine import SamplingParams
+
+        mt = d.get("max_completion_tokens", d.get("max_tokens", d.get("max_output_tokens", default_max)))
+        if mt is None:
+            mt = default_max
+        if not isinstance(mt, int) or mt < 1 or mt > MAX_GENERATED_TOKENS:
+            raise APIError(400, f"max_tokens must be an integer in [1, {MAX_GENERATED_TOKENS}]", param="max_tokens")
+        temp = d.get("temperature", 0.7)
+        top_p = d.get("top_p", 0.9)
+        if not isinstance(temp, (int, float)) or not 0 <= temp <= 2:
+            raise APIError(400, "temperature must be in [0, 2]", param="temperature")
+        if not isinstance(top_p, (int, float)) or not 0 < top_p <= 1:
+            raise APIError(400, "top_p must be in (0, 1]", param="top_p")
+        seed = d.get("seed")
+        return SamplingParams(max_tokens=mt, temperature=float(temp), top_p=float(top_p), seed=seed,
+                              top_k=int(d.get("top_k", 0) or 0))
+
+    def stops(d: dict) -> List[str]:
+        s = d.get("stop")
+        if s is None:
+            return []
+        if isinstance(s, str):
+            s = [s]
+        if not isinstance(s, list) or len(s) > MAX_STOP_SEQUENCES or any(
+                not isinstance(x, str) or len(x) > MAX_STOP_SEQUENCE_CHARS for x in s):
+            raise APIError(400, f"stop must be a string or up to {MAX_STOP_SEQUENCES} strings", param="stop")
+        return s
+
+    def messages_of(d: dict) -> List[Dict[str, str]]:
+        msgs = d.get("messages")
+        if not isinstance(msgs, list) or not msgs:
+            raise APIError(400, "messages must be a non-empty array", param="messages")
+        if len(msgs) > MAX_CHAT_MESSAGES:
+            raise APIError(400, f"at most {MAX_CHAT_MESSAGES} messages", param="messages")
+        out, total = [], 0
+        for m in msgs:
+            if not isinstance(m, dict) or m.get("role") not in ("system", "user", "assistant", "tool", "developer"):
+                raise APIError(400, "each message needs a role of system, user, assistant or tool", param="messages")
+            c = m.get("content", "")
+            if isinstance(c, list):
+                c = "".join(p.get("text", "") for p in c if isinstance(p, dict) and p.get("type") in ("text", "input_text"))
+            if c is None:
+                c = ""
+            if not isinstance(c, str):
+                raise APIError(400, "message content must be a string or text parts", param="messages")
+            total += len(c.encode("utf-8"))
+            role = "system" if m["role"] == "developer" else m["role"]
+            out.append({"role": role, "content": c})
+        if total > MAX_CHAT_CONTENT_BYTES:
+            raise APIError(413, "message content too large", param="messages")
+        return out
+
+    def prompt_ids_for(msgs: List[Dict[str, str]], raw_prompt: Optional[str] = None) -> List[int]:
+        if raw_prompt is not None:
+            ids = pipeline.tokenizer.encode(raw_prompt)
+        else:
+            ids = pipeline.tokenizer.encode(render(msgs, pipeline.template))
+        if not ids:
+            ids = [1]
+        if len(ids) >= st.context_size:
+            raise APIError(400, f"prompt has {len(ids)} tokens; the context window is {st.context_size}",
+                           param="messages", code="context_length_exceeded")
+        return ids
+
+    def with_eos(params):
+        eos = pipeline.eos_ids() if hasattr(pipeline, "eos_ids") else []
+        params.stop_token_ids = list(set(params.stop_token_ids) | set(eos))
+        return params
+
+    async def token_stream(msgs, params, stop_list, request: Request, raw_prompt: Optional[str] = None):
+        """Yields (delta_text, finished, reason); handles admission, cancellation, stop strings."""
+        if not rt.try_acquire():
+            raise APIError(429, "server is at capacity; retry shortly", "rate_limit_error",
+                           headers={"Retry-After": "1"})
+        metrics.in_flight += 1
+        sub = None
+        try:
+            ids = prompt_ids_for(msgs, raw_prompt)
+            params.max_tokens = min(params.max_tokens, st.context_size - len(ids) - 1)
+            with_eos(params)
+            sub = rt.submit(ids, params, messages=None if rt.engine is not None else (raw_prompt or msgs),
+                            request_id=request.state.request_id)
+            detok = Detokenizer(pipeline.tokenizer)
+            filt = StopSequenceFilter(stop_list)
+            eos = set(pipeline.eos_ids()) if hasattr(pipeline, "eos_ids") else set()
+            yield {"prompt_tokens": len(ids)}
+            while True:
+                item = await sub.queue.get()
+                if item.error:
+                    raise APIError(500, item.error, "server_error")
+                delta = ""
+                if item.token is not None and item.token not in eos:
+                    delta = detok.add(item.token)
+                elif item.text is not None:
+                    delta = item.text
+                out, stopped = filt.push(delta) if delta else ("", False)
+                if stopped:
+                    if not item.finished:
+                        rt.cancel(sub.id)
+                    yield (out, True, "stop")
+                    return
+                if item.finished:
+                    out += filt.flush()
+                    reason = item.reason if item.reason in ("stop", "length") else "stop"
+                    yield (out, True, reason)
+                    return
+                if out:
+                    yield (out, False, None)
+                if await request.is_disconnected():
+                    rt.cancel(sub.id)
+                    return
+        finally:
+            metrics.in_flight -= 1
+            rt.release()
+
+    # ------------------------------------------------------------ health / readiness / metrics
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
+    @app.get("/ready")
+    async def ready():
+        ok = rt.ready and rt.available_permits > 0
+        snap = {"schema_version": READINESS_VERSION, "object": "bloom.readiness", "protocol_version": READINESS_VERSION,
+                "minimum_ui_protocol_version": READINESS_VERSION, "maximum_ui_protocol_version": READINESS_VERSION,
+                "server_version": SERVER_VERSION, "status": "ready" if ok else "busy", "progress": 100,
+                "model": st.model_id, "loading": False, "load_error": None,
+                "input_modalities": ["Text"], "model_tasks": ["embedding"] if is_embedding else ["chat", "completion"],
+                "context_window": st.context_size, "in_flight_requests": rt.in_flight,
+                "available_permits": rt.available_permits, "memory_pressure_high": False,
+                "ram_utilization": _ram_utilization()}
+        return JSONResponse(snap, status_code=200 if ok else 503)
+
+    @app.get("/metrics")
+    async def prom():
+        kv = _kv_stats(pipeline)
+        return PlainTextResponse(metrics.render(kv), media_type="text/plain; version=0.0.4")
+
+    @app.get("/v1/observability")
+    async def observability():
+        return {"object": "bloom.observability", "schema_version": 1, "uptime_seconds": time.time() - started,
+                "model": st.model_id, "metrics": metrics.snapshot(), "kv_cache": _kv_stats(pipeline),
+                "runtime": {"in_flight_requests": rt.in_flight, "available_permits": rt.available_permits,
+                            "engine": getattr(pipeline, "engine_name", "unknown")}}
+
+    @app.get("/v1/kv-cache-stats")
+    async def kv_stats():
+        return {"object": "kv_cache_stats", "pool": _kv_stats(pipeline), "cachemesh": _cachemesh_stats(pipeline)}
+
+    @app.get("/v1/backends")
+    async def backends():
+        from ..engine.registry import default_registry
+
+        return {"object": "list", "data": default_registry().describe()}
+
+    @app.post("/v1/cancel/{request_id}")
+    async def cancel(request_id: str):
+        if not rt.cancel(request_id):
+            raise APIError(404, f"no in-flight request {request_id}", "not_found_error")
+        return {"id": request_id, "object": "cancellation", "cancelled": True}
+
+    # ------------------------------------------------------------ models
+    def model_card():
+        return {"id": st.model_id, "object": "model", "created": int(started), "owned_by": "bloom_b200"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [model_card()]}
+
+    @app.get("/v1/models/{model:path}")
+    async def model(model: str):
+        check_model(model)
+        return model_card()
+
+    # ------------------------------------------------------------ chat / completions
+    @app.post("/v1/chat/completions")
+    async def chat(request: Request):
+        if is_embedding:
+            raise APIError(400, "the loaded model is an embedding model", param="model")
+        d = await body(request)
+        check_model(d.get("model"))
+        msgs = messages_of(d)
+        params = sampling(d)
+        stop_list = stops(d)
+        rf = d.get("response_format")
+        if rf and rf.get("type") in ("json_object", "json_schema"):
+            from ..engine.structured import constrain_params
+
+            constrain_params(params, rf, pipeline)
+        cid = "chatcmpl-" + uuid.uuid4().hex[:24]
+        created = int(time.time())
+        stream = bool(d.get("stream"))
+        include_usage = bool((d.get("stream_options") or {}).get("include_usage"))
+        gen = token_stream(msgs, params, stop_list, request)
+        first = await gen.__anext__()  # admission / validation errors surface before streaming starts
+        ptoks = first["prompt_tokens"]
+        if not stream:
+            text, reason, n = [], "stop", 0
+            async for out, fin, r in gen:
+                text.append(out)
+                n += 1
+                if fin:
+                    reason = r
+            content = "".join(text)
+            metrics.tokens_generated += n
+            msg = {"role": "assistant", "content": content}
+            if rf and rf.get("type") in ("json_object", "json_schema"):
+                from ..engine.structured import repair_json
+
+                msg["content"] = repair_json(content)
+            return {"id": cid, "object": "chat.completion", "created": created, "model": st.model_id,
+                    "choices": [{"index": 0, "message": msg, "logprobs": None, "finish_reason": reason}],
+                    "usage": {"prompt_tokens": ptoks, "completion_tokens": n, "total_tokens": ptoks + n}}
+
+        async def sse():
+            def chunk(delta, reason=None):
+                return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": st.model_id,
+                        "choices": [{"index": 0, "delta": delta, "logprobs": None, "finish_reason": reason}]}
+
+            yield f"data: {json.dumps(chunk({'role': 'assistant', 'content': ''}))}\n\n"
+            n = 0
+            reason = "stop"
+            try:
+                async for out, fin, r in gen:
+                    n += 1
+                    if out:
+                        yield f"data: {json.dumps(chunk({'content': out}))}\n\n"
+                    if fin:
+                        reason = r
+                        break
+            except APIError as e:
+                yield f"data: {json.dumps({'error': {'message': e.message, 'type': e.type}})}\n\n"
+                yield "data: [DONE]\n\n"
+                return
+            metrics.tokens_generated += n
+            yield f"data: {json.dumps(chunk({}, reason))}\n\n"
+            if include_usage:
+                u = {"id": cid, "object": "chat.completion.chunk", "created": created, "model": st.model_id,
+                     "choices": [], "usage": {"prompt_tokens": ptoks, "completion_tokens": n,
+                                              "total_tokens": ptoks + n}}
+                yield f"data: {json.dumps(u)}\n\n"
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(sse(), media_type="text/event-stream")
+
+    @app.post("/v1/completions")
+    async def completions(request: Request):
+        if is_embedding:
+            raise APIError(400, "the loaded model is an embedding model", param="model")
+        d = await body(request)
+        check_model(d.get("model"))
+        prompt = d.get("prompt")
+        if isinstance(prompt, list):
+            prompt = "".join(p for p in prompt if isinstance(p, str))
+        if not isinstance(prompt, str):
+            raise APIError(400, "prompt must be a string", param="prompt")
+        params = sampling(d, 16)
+        stop_list = stops(d)
+        cid = "cmpl-" + uuid.uuid4().hex[:24]
+        created = int(time.time())
+        gen = token_stream([{"role": "user", "content": prompt}], params, stop_list, request, raw_prompt=prompt)
+        first = await gen.__anext__()
+        ptoks = first["prompt_tokens"]
+        if not d.get("stream"):
+            text, reason, n = [], "stop", 0
+            async for out, fin, r in gen:
+                text.append(out)
+                n += 1
+                if fin:
+                    reason = r
+            metrics.tokens_generated += n
+            return {"id": cid, "object": "text_completion", "created": created, "model": st.model_id,
+                    "choices": [{"index": 0, "text": "".join(text), "logprobs": None, "finish_reason": reason}],
+                    "usage": {"prompt_tokens": ptoks, "completion_tokens": n, "total_tokens": ptoks + n}}
+
+        async def sse():
+            n = 0
+            async for out, fin, r in gen:
+                n += 1
+                c = {"id": cid, "object": "text_completion", "created": created, "model": st.model_id,
+                     "choices": [{"index": 0, "text": out, "logprobs": None, "finish_reason": r if fin else None}]}
+                yield f"data: {json.dumps(c)}\n\n"
+                if fin:
+                    break
+            metrics.tokens_generated += n
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(sse(), media_type="text/event-stream")
+
+    # ------------------------------------------------------------ responses API
+    @app.post("/v1/responses")
+    async def responses(request: Request):
+        d = await body(request)
+        check_model(d.get("model"))
+        inp = d.get("input")
+        msgs = []
+        if d.get("instructions"):
+            msgs.append({"role": "system", "content": str(d["instructions"])})
+        if isinstance(inp, str):
+            msgs.append({"role": "user", "content": inp})
+        elif isinstance(inp, list):
+            msgs += messages_of({"messages": [m for m in inp if isinstance(m, dict) and "role" in m]})
+        else:
+            raise APIError(400, "input must be a string or a list of messages", param="input")
+        params = sampling(d)
+        rid = "resp_" + uuid.uuid4().hex[:24]
+        mid = "msg_" + uuid.uuid4().hex[:24]
+        created = int(time.time())
+        gen = token_stream(msgs, params, [], request)
+        first = await gen.__anext__()
+        ptoks = first["prompt_tokens"]
+
+        def final(text, n, status="completed"):
+            return {"id": rid, "object": "response", "created_at": created, "status": status, "model": st.model_id,
+                    "output": [{"type": "message", "id": mid, "status": "completed", "role": "assistant",
+                                "content": [{"type": "output_text", "text": text, "annotations": []}]}],
+                    "usage": {"input_tokens": ptoks, "output_tokens": n, "total_tokens": ptoks + n}}
+
+        if not d.get("stream"):
+            text, n = [], 0
+            async for out, fin, r in gen:
+                text.append(out)
+                n += 1
+            resp = final("".join(text), n)
+            store.put(rid, resp, msgs)
+            metrics.tokens_generated += n
+            return resp
+
+        async def sse():
+            seq = 0
+
+            def ev(kind, payload):
+                nonlocal seq
+                seq += 1
+                payload = dict(payload, type=kind, sequence_number=seq)
+                return f"event: {kind}\ndata: {json.dumps(payload)}\n\n"
+
+            yield ev("response.created", {"response": dict(final("", 0, "in_progress"), output=[])})
+            text, n = [], 0
+            async for out, fin, r in gen:
+                n += 1
+                if out:
+                    text.append(out)
+                    yield ev("response.output_text.delta", {"item_id": mid, "output_index": 0, "content_index": 0,
+                                                            "delta": out})
+                if fin:
+                    break
+            full = "".join(text)
+            yield ev("response.output_text.done", {"item_id": mid, "output_index": 0, "content_index": 0, "text": full})
+            resp = final(full, n)
+            store.put(rid, resp, msgs)
+            metrics.tokens_generated += n
+            yield ev("response.completed", {"response": resp})
+
+        return StreamingResponse(sse(), media_type="text/event-stream")
+
+    @app.get("/v1/responses/{rid}")
+    async def get_response(rid: str):
+        v = store.get(rid)
+        if v is None:
+            raise APIError(404, f"response {rid} not found", "not_found_error")
+        return v[1]
+
+    @app.get("/v1/responses/{rid}/input_items")
+    async def get_inputs(rid: str):
+        v = store.get(rid)
+        if v is None:
+            raise APIError(404, f"response {rid} not found", "not_found_error")
+        items = [{"type": "message", "role": m["role"], "content": [{"type": "input_text", "text": m["content"]}]}
+                 for m in v[2]]
+        return {"object": "list", "data": items}
+
+    # ------------------------------------------------------------ embeddings / rerank
+    def embed(texts: List[str], dims: Optional[int] = None) -> List[List[float]]:
+        if not is_embedding:
+            raise APIError(400, "the loaded model does not produce embeddings", param="model")
+        return pipeline.embedder.embed(texts, dimensions=dims)
+
+    @app.post("/v1/embeddings")
+    async def embeddings(request: Request):
+        d = await body(request)
+        check_model(d.get("model"))
+        inp = d.get("input")
+        if isinstance(inp, str):
+            inp = [inp]
+        if not isinstance(inp, list) or not inp or len(inp) > MAX_EMBEDDING_INPUTS or \
+                not all(isinstance(x, str) and x for x in inp):
+            raise APIError(400, f"input must be a non-empty string or 1..{MAX_EMBEDDING_INPUTS} non-empty strings",
+                           param="input")
+        dims = d.get("dimensions")
+        if dims is not None and (not isinstance(dims, int) or dims < 1):
+            raise APIError(400, "dimensions must be a positive integer", param="dimensions")
+        vecs = await asyncio.get_running_loop().run_in_executor(None, embed, inp, dims)
+        fmt = d.get("encoding_format", "float")
+        data = []
+        for i, v in enumerate(vecs):
+            e = base64.b64encode(struct.pack(f"<{len(v)}f", *v)).decode() if fmt == "base64" else v
+            data.append({"object": "embedding", "index": i, "embedding": e})
+        n = sum(len(x.split()) for x in inp)
+        return {"object": "list", "data": data, "model": st.model_id, "usage": {"prompt_tokens": n, "total_tokens": n}}
+
+    @app.post("/v1/rerank")
+    async def rerank(request: Request):
+        d = await body(request)
+        q = d.get("query")
+        docs = d.get("documents")
+        if not isinstance(q, str) or not q:
+            raise APIError(400, "query must be a non-empty string", param="query")
+        if not isinstance(docs, list) or not docs or len(docs) > MAX_RERANK_DOCUMENTS:
+            raise APIError(400, f"documents must hold 1..{MAX_RERANK_DOCUMENTS} items", param="documents")
+        texts = [x if isinstance(x, str) else (x or {}).get("text", "") for x in docs]
+        vecs = await asyncio.get_running_loop().run_in_executor(None, embed, [q] + texts, None)
+        qv = vecs[0]
+        scores = [sum(a * b for a, b in zip(qv, v)) for v in vecs[1:]]
+        order = sorted(range(len(scores)), key=lambda i: (-scores[i], i))  # stable ties by index
+        top = d.get("top_n") or len(order)
+        res = [{"index": i, "relevance_score": scores[i], "document": {"text": texts[i]}} for i in order[:top]]
+        return {"object": "list", "model": st.model_id, "results": res}
+
+    # ------------------------------------------------------------ Ollama adapter
+    @app.get("/api/version")
+    async def o_version():
+        return {"version": SERVER_VERSION}
+
+    def o_model():
+        return {"name": st.model_id, "model": st.model_id, "modified_at": _iso(started), "size": 0,
+                "digest": uuid.uuid5(uuid.NAMESPACE_URL, st.model_id).hex,
+                "details": {"format": "bloom", "family": getattr(pipeline.cfg, "arch", ""),
+                            "parameter_size": "", "quantization_level": ""}}
+
+    @app.get("/api/tags")
+    async def o_tags():
+        return {"models": [o_model()]}
+
+    @app.get("/api/ps")
+    async def o_ps():
+        return {"models": [dict(o_model(), expires_at=_iso(time.time() + 300), size_vram=0)]}
+
+    @app.post("/api/show")
+    async def o_show(request: Request):
+        d = await body(request)
+        check_model(d.get("model") or d.get("name"))
+        cfg = pipeline.cfg
+        return {"modelfile": "", "parameters": "", "template": pipeline.template,
+                "details": o_model()["details"],
+                "model_info": {"general.architecture": cfg.arch, "context_length": st.context_size,
+                               "embedding_length": cfg.hidden_size, "block_count": cfg.num_layers}}
+
+    def o_params(d: dict):
+        opts = d.get("options") or {}
+        m = {"max_tokens": opts.get("num_predict", 128), "temperature": opts.get("temperature", 0.8),
+             "top_p": opts.get("top_p", 0.9), "seed": opts.get("seed"), "top_k": opts.get("top_k", 0)}
+        if m["max_tokens"] in (None, -1):
+            m["max_tokens"] = 128
+        return sampling(m), stops({"stop": opts.get("stop")})
+
+    async def o_generate_common(request: Request, msgs, raw_prompt, chat_mode: bool, d: dict):
+        params, stop_list = o_params(d)
+        t0 = time.time()
+        gen = token_stream(msgs, params, stop_list, request, raw_prompt=raw_prompt)
+        first = await gen.__anext__()
+        ptoks = first["prompt_tokens"]
+
+        def piece(text, done, reason=None, n=0):
+            base = {"model": st.model_id, "created_at": _iso(time.time()), "done": done}
+            if chat_mode:
+                base["message"] = {"role": "assistant", "content": text}
+            else:
+                base["response"] = text
+            if done:
+                dur = int((time.time() - t0) * 1e9)
+                base.update(done_reason=reason or "stop", total_duration=dur, load_duration=0,
+                            prompt_eval_count=ptoks, eval_count=n, eval_duration=dur)
+            return base
+
+        if d.get("stream", True):
+            async def nd():
+                n = 0
+                async for out, fin, r in gen:
+                    n += 1
+                    if out:
+                        yield json.dumps(piece(out, False)) + "\n"
+                    if fin:
+                        yield json.dumps(piece("", True, r, n)) + "\n"
+                        break
+                metrics.tokens_generated += n
+
+            return StreamingResponse(nd(), media_type="application/x-ndjson")
+        text, n, reason = [], 0, "stop"
+        async for out, fin, r in gen:
+            text.append(out)
+            n += 1
+            if fin:
+                reason = r
+        metrics.tokens_generated += n
+        res = piece("".join(text), True, reason, n)
+        return res
+
+    @app.post("/api/chat")
+    async def o_chat(request: Request):
+        d = await body(request)
+        check_model(d.get("model"))
+        msgs = messages_of({"messages": d.get("messages")})
+        return await o_generate_common(request, msgs, None, True, d)
+
+    @app.post("/api/generate")
+    async def o_generate(request: Request):
+        d = await body(request)
+        check_model(d.get("model"))
+        p = d.get("prompt")
+        if not isinstance(p, str):
+            raise APIError(400, "prompt must be a string")
+        if d.get("raw"):
+            return await o_generate_common(request, [{"role": "user", "content": p}], p, False, d)
+        msgs = ([{"role": "system", "content": d["system"]}] if d.get("system") else []) + \
+            [{"role": "user", "content": p}]
+        return await o_generate_common(request, msgs, None, False, d)
+
+    @app.post("/api/embed")
+    async def o_embed(request: Request):
+        d = await body(request)
+        check_model(d.get("model"))
+        inp = d.get("input")
+        if isinstance(inp, str):
+            inp = [inp]
+        if not isinstance(inp, list) or not inp or len(inp) > MAX_EMBEDDING_INPUTS:
+            raise APIError(400, "input must be a string or a list of strings")
+        vecs = await asyncio.get_running_loop().run_in_executor(None, embed, inp, d.get("dimensions"))
+        return {"model": st.model_id, "embeddings": vecs}
+
+    @app.post("/api/embeddings")
+    async def o_embeddings(request: Request):
+        d = await body(request)
+        p = d.get("prompt")
+        if not isinstance(p, str) or not p:
+            raise APIError(400, "prompt must be a non-empty string")
+        vecs = await asyncio.get_running_loop().run_in_executor(None, embed, [p], None)
+        return {"embedding": vecs[0]}
+
+    return app
+
+
+def _iso(t: float) -> str:
+    return time.strftime("%Y-%m-%dT%H:%M:%S", time.gmtime(t)) + f".{int((t % 1) * 1e6):06d}Z"
+
+
+def _ram_utilization() -> float:
+    try:
+        tot = avail = None
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemTotal:"):
+                    tot = int(line.split()[1])
+                elif line.startswith("MemAvailable:"):
+                    avail = int(line.split()[1])
+        if tot and avail is not None:
+            return round(1.0 - avail / tot, 4)
+    except OSError:
+        pass
+    return 0.0
+
+
+def _kv_stats(pipeline) -> dict:
+    llm = getattr(pipeline, "llm", None)
+    if llm is None:
+        return {"total_blocks": 0, "free_blocks": 0, "active_blocks": 0, "cached_blocks": 0, "hits": 0, "misses": 0,
+                "evictions": 0, "reuses": 0}
+    return llm.kv_metrics()
+
+
+def _cachemesh_stats(pipeline) -> dict:
+    mesh = getattr(getattr(pipeline, "llm", None), "cachemesh", None)
+    return mesh.metrics() if mesh is not None else {"enabled": False}

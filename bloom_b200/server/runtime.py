@@ -1,0 +1,209 @@
+"""Serving runtime: one engine thread drives in-flight batching for every HTTP request.
+
+HTTP handlers call `submit()` and consume an async stream of token ids; the
+engine thread admits new requests into the C++ scheduler between steps, runs
+`LLMEngine.step()` (one batched forward for all running requests) and pushes
+each new token to its request's asyncio queue.  Detokenisation and stop-string
+filtering run on the handler side, so the engine loop never waits on Python
+text work.  Cancellation (client disconnect, /v1/cancel/{id}) aborts the
+request in the scheduler before the next step, which frees its KV blocks.
+
+The reference's IFB path instead kept a separate model wrapper per request and
+looped over them one at a time (crates/server/src/lib.rs:2796-3063, worker
+loop stepping every 5 ms); CPU and echo pipelines here keep that simpler
+one-request-at-a-time execution in a worker thread.
+"""
+from __future__ import annotations
+
+import asyncio
+import itertools
+import queue
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional
+
+_ids = itertools.count(1)
+
+
+@dataclass
+class StreamItem:
+    token: Optional[int] = None
+    text: Optional[str] = None  # used by non-engine pipelines (already detokenised)
+    finished: bool = False
+    reason: Optional[str] = None
+    error: Optional[str] = None
+
+
+@dataclass
+class Submission:
+    id: str
+    prompt_ids: List[int]
+    params: Any
+    loop: asyncio.AbstractEventLoop
+    queue: asyncio.Queue
+    created: float = field(default_factory=time.time)
+    engine_rid: Optional[int] = None
+    cancelled: bool = False
+    first_token_at: Optional[float] = None
+    n_tokens: int = 0
+    messages: Any = None
+
+
+class ServingRuntime:
+    def __init__(self, pipeline, model_id: str, max_concurrent: int = 4, metrics=None):
+        self.pipe = pipeline
+        self.model_id = model_id
+        self.max_concurrent = max_concurrent
+        self.metrics = metrics
+        self.in_flight = 0
+        self._lock = threading.Lock()
+        self._pending: "queue.Queue[Submission]" = queue.Queue()
+        self._cancel: "queue.Queue[str]" = queue.Queue()
+        self._by_id: Dict[str, Submission] = {}
+        self._by_rid: Dict[int, Submission] = {}
+        self._stop = threading.Event()
+        self._wake = threading.Event()
+        self.ready = True
+        self.engine = getattr(pipeline, "llm", None)
+        self._thread = threading.Thread(target=self._loop, name="bloom-engine", daemon=True)
+        self._thread.start()
+
+    # ------------------------------------------------------------ admission
+    def try_acquire(self) -> bool:
+        with self._lock:
+            if self.in_flight >= self.max_concurrent:
+                return False
+            self.in_flight += 1
+            return True
+
+    def release(self) -> None:
+        with self._lock:
+            self.in_flight = max(0, self.in_flight - 1)
+
+    @property
+    def available_permits(self) -> int:
+        return max(0, self.max_concurrent - self.in_flight)
+
+    def submit(self, prompt_ids: List[int], params, messages=None, request_id: Optional[str] = None) -> Submission:
+        loop = asyncio.get_running_loop()
+        sub = Submission(request_id or f"req-{next(_ids)}", list(prompt_ids), params, loop, asyncio.Queue(),
+                         messages=messages)
+        with self._lock:
+            self._by_id[sub.id] = sub
+        self._pending.put(sub)
+        self._wake.set()
+        return sub
+
+    def cancel(self, request_id: str) -> bool:
+        with self._lock:
+            sub = self._by_id.get(request_id)
+        if sub is None:
+            return False
+        sub.cancelled = True
+        self._cancel.put(request_id)
+        self._wake.set()
+        return True
+
+    def shutdown(self) -> None:
+        self._stop.set()
+        self._wake.set()
+        self._thread.join(timeout=10)
+
+    # ------------------------------------------------------------ engine thread
+    def _emit(self, sub: Submission, item: StreamItem) -> None:
+        sub.loop.call_soon_threadsafe(sub.queue.put_nowait, item)
+
+    def _finish(self, sub: Submission) -> None:
+        with self._lock:
+            self._by_id.pop(sub.id, None)
+            if sub.engine_rid is not None:
+                self._by_rid.pop(sub.engine_rid, None)
+
+    def _loop(self) -> None:
+        if self.engine is None:
+            return self._loop_blocking()
+        eng = self.engine
+        while not self._stop.is_set():
+            while True:
+                try:
+                    rid = self._cancel.get_nowait()
+                except queue.Empty:
+                    break
+                with self._lock:
+                    sub = self._by_id.get(rid)
+                if sub is not None and sub.engine_rid is not None:
+                    eng.abort(sub.engine_rid)
+                    self._emit(sub, StreamItem(finished=True, reason="abort"))
+                    self._finish(sub)
+            while True:
+                try:
+                    sub = self._pending.get_nowait()
+                except queue.Empty:
+                    break
+                if sub.cancelled:
+                    self._emit(sub, StreamItem(finished=True, reason="abort"))
+                    self._finish(sub)
+                    continue
+                try:
+                    rid = eng.add_request(sub.prompt_ids, sub.params)
+                except Exception as e:  # prompt too long etc.
+                    self._emit(sub, StreamItem(finished=True, reason="error", error=str(e)))
+                    self._finish(sub)
+                    continue
+                sub.engine_rid = rid
+                with self._lock:
+                    self._by_rid[rid] = sub
+            if not eng.has_unfinished():
+                self._wake.wait(timeout=0.05)
+                self._wake.clear()
+                continue
+            try:
+                outs = eng.step()
+            except Exception as e:  # a failed step fails every request in it (reference mod.rs:1862-1907)
+                with self._lock:
+                    subs = list(self._by_rid.values())
+                for sub in subs:
+                    eng.abort(sub.engine_rid)
+                    self._emit(sub, StreamItem(finished=True, reason="error", error=f"engine step failed: {e}"))
+                    self._finish(sub)
+                continue
+            now = time.time()
+            for r in outs:
+                sub = self._by_rid.get(r.request_id)
+                if sub is None:
+                    continue
+                if sub.first_token_at is None:
+                    sub.first_token_at = now
+                    if self.metrics is not None:
+                        self.metrics.observe_ttft(now - sub.created)
+                sub.n_tokens += 1
+                self._emit(sub, StreamItem(token=r.token_ids[-1], finished=r.finished, reason=r.finish_reason))
+                if r.finished:
+                    eng.requests.pop(r.request_id, None)
+                    self._finish(sub)
+
+    def _loop_blocking(self) -> None:
+        """CPU / echo pipelines: one request at a time, text deltas."""
+        while not self._stop.is_set():
+            try:
+                sub = self._pending.get(timeout=0.05)
+            except queue.Empty:
+                continue
+            try:
+                reason = "length"
+                for delta in self.pipe.run_stream(sub.messages if sub.messages is not None else "", sub.params,
+                                                  prompt_ids=sub.prompt_ids if sub.messages is None else None):
+                    if sub.cancelled:
+                        reason = "abort"
+                        break
+                    if sub.first_token_at is None:
+                        sub.first_token_at = time.time()
+                    sub.n_tokens += 1
+                    self._emit(sub, StreamItem(text=delta))
+                if reason != "abort" and self.pipe.last_generated_tokens < sub.params.max_tokens:
+                    reason = "stop"
+                self._emit(sub, StreamItem(finished=True, reason=reason))
+            except Exception as e:
+                self._emit(sub, StreamItem(finished=True, reason="error", error=str(e)))
+            self._finish(sub)

@@ -11,6 +11,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("EPI_SWIGLU") = int(bloom::kEpiSwiGLU);
   m.attr("EPI_PARTIAL_F32") = int(bloom::kEpiPartialF32);
   m.attr("EPI_RESIDUAL") = int(bloom::kEpiResidual);
+  m.attr("EPI_GELU") = int(bloom::kEpiGelu);
   m.def("gemm_out", &bloom::gemm_out, "y = x @ w^T on tcgen05 with fused epilogue");
   m.def("gemm_pick_bn", &bloom::gemm_pick_bn);
   m.def("gemm_default_splits", &bloom::gemm_default_splits);
@@ -26,6 +27,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_rows", &bloom::argmax_rows);
   m.def("sample_rows", &bloom::sample_rows);
   m.def("status_tensor", &bloom::status_tensor);
+  m.def("bert_embed_ln", &bloom::bert_embed_ln);
+  m.def("varlen_attention", &bloom::varlen_attention);
+  m.def("mean_pool_l2", &bloom::mean_pool_l2);
   m.def("tp_flag_words", &bloom::tp_flag_words);
   m.def("tp_allreduce_rmsnorm", &bloom::tp_allreduce_rmsnorm);
   m.def("tp_allgather_rows", &bloom::tp_allgather_rows);

@@ -35,6 +35,7 @@ py::dict metrics_dict(const PoolMetrics& m) {
 
 void register_cpu_ops(py::module_& m);  // csrc/runtime/cpu_ops.cpp
 void register_gguf(py::module_& m);     // csrc/runtime/gguf.cpp
+void register_json(py::module_& m);     // csrc/runtime/json_dfa.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 host runtime: KV block manager, in-flight batching scheduler, CPU kernels";
@@ -177,9 +178,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              const Sequence* q = s.find(id);
              return q == nullptr ? 0 : q->num_cached_prefix;
            })
+      .def("sampling_ids", &Scheduler::sampling_ids)
       .def("kv_metrics", [](Scheduler& s) { return metrics_dict(s.blocks().metrics()); })
       .def("reset_prefix_cache", [](Scheduler& s) { s.blocks().reset_prefix_cache(); });
 
   register_cpu_ops(m);
   register_gguf(m);
+  register_json(m);
 }

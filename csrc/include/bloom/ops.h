@@ -12,6 +12,7 @@ enum GemmEpilogue : int {
   kEpiSwiGLU = 2,      // w rows interleaved (16 gate | 16 up) per 32 rows; out bf16 [M, N/2] = silu(g) * u
   kEpiPartialF32 = 3,  // split-K: out f32 [splits, M, N] partial sums
   kEpiResidual = 4,    // out bf16 [M, N] = acc + resid
+  kEpiGelu = 5,        // out bf16 [M, N] = gelu_erf(acc + bias)
 };
 
 // splits > 1 with a non-partial epilogue: split-K where the last-arriving CTA
@@ -72,6 +73,14 @@ void tp_allgather_rows(const torch::Tensor& src, const std::vector<int64_t>& dst
                        const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t T, double timeout_s,
                        const torch::Tensor& status);
 void tp_barrier(const std::vector<int64_t>& flag_ptrs, int64_t rank, double timeout_s, const torch::Tensor& status);
+
+// Encoder (BERT) kernels.
+void bert_embed_ln(const torch::Tensor& ids, const torch::Tensor& pos, const c10::optional<torch::Tensor>& types,
+                   const torch::Tensor& word, const torch::Tensor& pemb, const torch::Tensor& temb,
+                   const torch::Tensor& g, const torch::Tensor& b, torch::Tensor& out, double eps);
+void varlen_attention(const torch::Tensor& qkv, const torch::Tensor& cu_seqlens, torch::Tensor& out, int64_t num_heads,
+                      int64_t head_dim, int64_t max_len, double scale);
+void mean_pool_l2(const torch::Tensor& x, const torch::Tensor& cu_seqlens, torch::Tensor& out, bool normalize);
 
 // Status word.
 torch::Tensor status_tensor(int64_t device);

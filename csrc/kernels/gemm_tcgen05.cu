@@ -94,7 +94,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, int feat_tile, int 
     const int f = feat_tile * BM + row;
     const bool fvalid = f < a.N;
     float bias = 0.f;
-    if constexpr (EPI == kEpiBF16 || EPI == kEpiF32) {
+    if constexpr (EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiGelu) {
       if (a.bias != nullptr && fvalid) bias = __bfloat162float(a.bias[f]);
     }
     for (int c = 0; c < BN; c += 16) {
@@ -115,6 +115,10 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, int feat_tile, int 
         } else if constexpr (EPI == kEpiResidual) {
           const float r = __bfloat162float(a.resid[(long)tok * a.ldr + f]);
           reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] = __float2bfloat16(v[j] + r);
+        } else if constexpr (EPI == kEpiGelu) {
+          const float x = v[j] + bias;
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] =
+              __float2bfloat16(0.5f * x * (1.f + erff(x * 0.7071067811865476f)));
         }
       }
     }
@@ -513,6 +517,9 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
       TORCH_CHECK(a.splits == s, "gemm partial: split count ", s, " not realisable for K=", K);
       break;
     }
+    case kEpiGelu:
+      TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(-1) == N, "gemm gelu: out must be bf16 [M,N]");
+      break;
     case kEpiResidual:
       TORCH_CHECK(resid.has_value(), "gemm residual epilogue needs resid");
       TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(-1) == N, "gemm: out must be bf16 [M,N]");
@@ -555,6 +562,7 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
     case kEpiSwiGLU: gemm::dispatch_bn<kEpiSwiGLU>(bn, tmA, tmB, a, grid, stream); break;
     case kEpiPartialF32: gemm::dispatch_bn<kEpiPartialF32>(bn, tmA, tmB, a, grid, stream); break;
     case kEpiResidual: gemm::dispatch_bn<kEpiResidual>(bn, tmA, tmB, a, grid, stream); break;
+    case kEpiGelu: gemm::dispatch_bn<kEpiGelu>(bn, tmA, tmB, a, grid, stream); break;
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -138,6 +138,13 @@ class Scheduler {
   const Sequence* find(int64_t id) const;
   const SchedulerConfig& config() const { return cfg_; }
   int64_t total_preemptions() const { return total_preemptions_; }
+  // Sequence ids of the sampling rows of the last scheduled step, in row order.
+  std::vector<int64_t> sampling_ids() const {
+    std::vector<int64_t> v;
+    v.reserve(last_sampling_.size());
+    for (const Sequence* s : last_sampling_) v.push_back(s->id);
+    return v;
+  }
 
  private:
   void preempt(Sequence* s);

@@ -95,3 +95,22 @@ def test_engine_sampling_reproducible():
     a = eng.generate([p], sp)[0].token_ids
     b = eng.generate([p], sp)[0].token_ids
     assert a == b and len(a) == 10
+
+
+def test_engine_json_mode_constrained_decoding():
+    import json as _json
+
+    from bloom_b200._ext import runtime
+    from bloom_b200.engine.engine import SamplingParams
+    from bloom_b200.engine.structured import repair_json
+    from bloom_b200.engine.text import Tokenizer
+
+    cfg, w, eng = _build("tiny-llama", graphs=False)
+    tok = Tokenizer(None)
+    eng.tokenizer = tok
+    out = eng.generate([[5, 6, 7]], SamplingParams(max_tokens=24, temperature=0.8, seed=3, json_mode=True,
+                                                    ignore_eos=True))[0]
+    text = tok.decode(out.token_ids)
+    d = runtime().JsonDfa()
+    assert d.feed(text), text  # every emitted token kept a valid JSON prefix
+    _json.loads(repair_json(text))

@@ -1,0 +1,193 @@
+"""HTTP surface (OpenAI + Ollama) on the deterministic echo model, in-process.
+
+Mirrors the reference's in-process router tests (crates/server/src/lib.rs
+tests with tower::ServiceExt::oneshot): protocol shapes, streaming framing,
+limits, 429 + Retry-After, request ids, cache headers, protocol-shaped
+404/405, authentication, Ollama NDJSON.
+"""
+import json
+import math
+
+import pytest
+from fastapi.testclient import TestClient
+
+from bloom_b200.engine.pipeline import EchoPipeline
+from bloom_b200.server.app import ServerSettings, create_app
+
+
+class FakeEmbedder:
+    def embed(self, texts, normalize=True, dimensions=None):
+        out = []
+        for t in texts:
+            v = [float((hash(t) >> (4 * i)) % 17 - 8) + (1.0 if w in t else 0.0)
+                 for i, w in enumerate(["cat", "dog", "sun", "car", "tea", "sky", "red", "big"])]
+            if dimensions:
+                v = v[:dimensions]
+            n = math.sqrt(sum(x * x for x in v)) or 1.0
+            out.append([x / n for x in v])
+        return out
+
+
+class EmbedPipeline(EchoPipeline):
+    def __init__(self):
+        super().__init__()
+        self.cfg.arch = "bert"
+        self.embedder = FakeEmbedder()
+
+    @property
+    def is_embedding(self):
+        return True
+
+
+@pytest.fixture(scope="module")
+def client():
+    app = create_app(EchoPipeline(), ServerSettings(model_id="echo", max_concurrent=4))
+    with TestClient(app) as c:
+        yield c
+
+
+def test_health_ready_metrics(client):
+    assert client.get("/health").json() == {"status": "ok"}
+    r = client.get("/ready").json()
+    assert r["object"] == "bloom.readiness" and r["protocol_version"] == 3
+    assert r["minimum_ui_protocol_version"] == 3 and r["maximum_ui_protocol_version"] == 3
+    m = client.get("/metrics")
+    assert m.status_code == 200 and "bloom_requests_total" in m.text
+
+
+def test_models_and_unknown_model(client):
+    d = client.get("/v1/models").json()
+    assert d["object"] == "list" and d["data"][0]["id"] == "echo"
+    r = client.post("/v1/chat/completions", json={"model": "other", "messages": [{"role": "user", "content": "x"}]})
+    assert r.status_code == 404 and r.json()["error"]["code"] == "model_not_found"
+
+
+def test_chat_non_stream(client):
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hello there"}]})
+    assert r.status_code == 200
+    d = r.json()
+    assert d["object"] == "chat.completion"
+    assert d["choices"][0]["message"] == {"role": "assistant", "content": "echo: hello there"}
+    assert d["usage"]["completion_tokens"] > 0
+    assert r.headers["cache-control"] == "no-store" and r.headers["x-request-id"]
+
+
+def test_chat_stream_framing_and_usage(client):
+    with client.stream("POST", "/v1/chat/completions", json={
+            "messages": [{"role": "user", "content": "a b c"}], "stream": True,
+            "stream_options": {"include_usage": True}}) as r:
+        lines = [l for l in r.iter_lines() if l]
+    assert lines[-1] == "data: [DONE]"
+    chunks = [json.loads(l[6:]) for l in lines[:-1]]
+    assert chunks[0]["choices"][0]["delta"] == {"role": "assistant", "content": ""}
+    text = "".join(c["choices"][0]["delta"].get("content", "") for c in chunks if c["choices"])
+    assert text == "echo: a b c"
+    assert chunks[-1]["choices"] == [] and chunks[-1]["usage"]["completion_tokens"] > 0
+    assert any(c["choices"] and c["choices"][0]["finish_reason"] for c in chunks)
+
+
+def test_stop_sequence_never_leaks(client):
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "one two three four"}],
+                                                  "stop": ["three"]})
+    d = r.json()
+    assert d["choices"][0]["message"]["content"] == "echo: one two "
+    assert d["choices"][0]["finish_reason"] == "stop"
+
+
+def test_max_tokens_length(client):
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "a b c d e f"}],
+                                                  "max_tokens": 2})
+    d = r.json()
+    assert d["choices"][0]["finish_reason"] == "length"
+
+
+@pytest.mark.parametrize("bad", [{"temperature": 5}, {"top_p": 0}, {"max_tokens": 0}, {"max_tokens": 40000},
+                                 {"stop": ["a", "b", "c", "d", "e"]}, {"messages": []}])
+def test_validation_errors(client, bad):
+    body = {"messages": [{"role": "user", "content": "x"}]}
+    body.update(bad)
+    r = client.post("/v1/chat/completions", json=body)
+    assert r.status_code == 400
+    assert "message" in r.json()["error"]
+
+
+def test_request_id_echo(client):
+    r = client.get("/v1/models", headers={"x-request-id": "abc-123"})
+    assert r.headers["x-request-id"] == "abc-123"
+
+
+def test_protocol_shaped_404_405(client):
+    r = client.get("/v1/nope")
+    assert r.status_code == 404 and "error" in r.json() and isinstance(r.json()["error"], dict)
+    r = client.get("/api/nope")
+    assert r.status_code == 404 and isinstance(r.json()["error"], str)
+    r = client.get("/v1/chat/completions")
+    assert r.status_code == 405
+
+
+def test_completions_and_responses(client):
+    r = client.post("/v1/completions", json={"prompt": "hi you", "max_tokens": 10}).json()
+    assert r["object"] == "text_completion" and r["choices"][0]["text"] == "echo: hi you"
+    r = client.post("/v1/responses", json={"input": "ping", "instructions": "be brief"}).json()
+    assert r["object"] == "response" and r["status"] == "completed"
+    assert r["output"][0]["content"][0]["text"] == "echo: ping"
+    got = client.get(f"/v1/responses/{r['id']}").json()
+    assert got["id"] == r["id"]
+    items = client.get(f"/v1/responses/{r['id']}/input_items").json()
+    assert items["data"][-1]["content"][0]["text"] == "ping"
+    assert client.get("/v1/responses/resp_missing").status_code == 404
+
+
+def test_responses_stream_events(client):
+    with client.stream("POST", "/v1/responses", json={"input": "x y", "stream": True}) as r:
+        events = [l[7:] for l in r.iter_lines() if l.startswith("event: ")]
+    assert events[0] == "response.created" and events[-1] == "response.completed"
+    assert "response.output_text.delta" in events
+
+
+def test_capacity_429():
+    app = create_app(EchoPipeline(), ServerSettings(model_id="echo", max_concurrent=0))
+    with TestClient(app) as c:
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}]})
+        assert r.status_code == 429 and r.headers["retry-after"] == "1"
+
+
+def test_api_key_auth():
+    app = create_app(EchoPipeline(), ServerSettings(model_id="echo", api_keys=["s3cret"]))
+    with TestClient(app) as c:
+        r = c.get("/v1/models")
+        assert r.status_code == 401 and "Bearer" in r.headers["www-authenticate"]
+        assert c.get("/v1/models", headers={"Authorization": "Bearer s3cret"}).status_code == 200
+        assert c.get("/health").status_code == 200
+
+
+def test_ollama_surface(client):
+    assert "version" in client.get("/api/version").json()
+    assert client.get("/api/tags").json()["models"][0]["name"] == "echo"
+    with client.stream("POST", "/api/chat", json={"model": "echo", "messages": [{"role": "user", "content": "q w"}]}) as r:
+        rows = [json.loads(l) for l in r.iter_lines() if l]
+    assert rows[-1]["done"] is True and rows[-1]["done_reason"] in ("stop", "length")
+    assert "".join(x["message"]["content"] for x in rows) == "echo: q w"
+    g = client.post("/api/generate", json={"model": "echo", "prompt": "z", "stream": False}).json()
+    assert g["done"] and g["response"] == "echo: z"
+
+
+def test_embeddings_and_rerank():
+    app = create_app(EmbedPipeline(), ServerSettings(model_id="mini"))
+    with TestClient(app) as c:
+        d = c.post("/v1/embeddings", json={"input": ["the cat", "a dog"]}).json()
+        assert d["object"] == "list" and len(d["data"]) == 2
+        v = d["data"][0]["embedding"]
+        assert abs(sum(x * x for x in v) - 1.0) < 1e-6
+        d2 = c.post("/v1/embeddings", json={"input": "x", "dimensions": 4}).json()
+        assert len(d2["data"][0]["embedding"]) == 4
+        b = c.post("/v1/embeddings", json={"input": "x", "encoding_format": "base64"}).json()
+        assert isinstance(b["data"][0]["embedding"], str)
+        assert c.post("/v1/embeddings", json={"input": ["x"] * 257}).status_code == 400
+        rr = c.post("/v1/rerank", json={"query": "cat", "documents": ["dog", "cat", "sun"], "top_n": 2}).json()
+        assert len(rr["results"]) == 2
+        scores = [x["relevance_score"] for x in rr["results"]]
+        assert scores == sorted(scores, reverse=True)
+        e = c.post("/api/embed", json={"model": "mini", "input": ["a", "b"]}).json()
+        assert len(e["embeddings"]) == 2
+        assert c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}]}).status_code == 400
