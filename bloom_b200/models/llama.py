@@ -184,7 +184,10 @@ class DecoderLM:
         self.lm_head = lm[r * V // t:(r + 1) * V // t].contiguous()
         if "lm_head.weight" in full:
             del full["lm_head.weight"]
-        moe_full = {}
+        if cfg.is_moe:
+            from .qwen3_moe import MoEBlock
+
+            self.moe = MoEBlock(self)
         for i in range(cfg.num_layers):
             p = f"model.layers.{i}."
             lay = {
@@ -214,12 +217,8 @@ class DecoderLM:
                 lay[p + "mlp.down_proj.weight"] = randn(H, cfg.intermediate_size)
             self._install_layer(i, lay)
             if cfg.is_moe:
-                moe_full.update({k: v for k, v in lay.items() if ".mlp." in k})
+                self.moe.add_layer(i, lay)
             del lay
-        if cfg.is_moe:
-            from .qwen3_moe import MoEBlock
-
-            self.moe = MoEBlock(self, moe_full)
         self._finish()
 
     def _install_layer(self, i: int, lay: Dict[str, torch.Tensor]) -> None:
@@ -327,8 +326,13 @@ class DecoderLM:
             x = self._row_parallel_norm(a2, lay["o"], residual, lay["ln2"], eps)
             nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
             if self.moe is not None:
-                d = self._reduce(self.moe.forward(li, x))
-                x = ops.add_rmsnorm(d, residual, nxt, eps)
+                fused = self.tp.comm.fused if (self.tp.size > 1 and self.tp.comm is not None) else None
+                if fused is not None:
+                    self.moe.forward(li, x, out=fused.partial(T))
+                    x = fused.allreduce_rmsnorm(T, residual, nxt, eps)
+                else:
+                    d = self._reduce(self.moe.forward(li, x))
+                    x = ops.add_rmsnorm(d, residual, nxt, eps)
             else:
                 act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU)
                 x = self._row_parallel_norm(act, lay["down"], residual, nxt, eps)

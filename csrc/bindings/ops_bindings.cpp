@@ -14,6 +14,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("EPI_GELU") = int(bloom::kEpiGelu);
   m.def("gemm_out", &bloom::gemm_out, "y = x @ w^T on tcgen05 with fused epilogue");
   m.def("gemm_pick_bn", &bloom::gemm_pick_bn);
+  m.def("gemm_grouped_out", &bloom::gemm_grouped_out);
+  m.def("moe_route", &bloom::moe_route);
+  m.def("moe_plan", &bloom::moe_plan);
+  m.def("moe_gather", &bloom::moe_gather);
+  m.def("moe_combine", &bloom::moe_combine);
   m.def("gemm_default_splits", &bloom::gemm_default_splits);
   m.def("gemm_fixup_ws_floats", &bloom::gemm_fixup_ws_floats);
   m.def("rmsnorm", &bloom::rmsnorm);

@@ -26,6 +26,19 @@ int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits, int64_t bn_ov
 int gemm_pick_bn(int M);
 int gemm_default_splits(int M, int N, int K, int device);
 
+void gemm_grouped_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
+                      const torch::Tensor& tiles, const torch::Tensor& num_tiles, int64_t rows_per_group, int64_t bn,
+                      const torch::Tensor& status);
+
+// Mixture of experts.
+void moe_route(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0, int64_t e_local,
+               torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& counts);
+void moe_plan(torch::Tensor& counts, torch::Tensor& offsets, int64_t bn, int64_t ft_gu, int64_t ft_d,
+              torch::Tensor& tiles_gu, torch::Tensor& n_gu, torch::Tensor& tiles_d, torch::Tensor& n_d);
+void moe_gather(const torch::Tensor& x, int64_t e0, int64_t e_local, const torch::Tensor& topk_ids,
+                const torch::Tensor& slot, const torch::Tensor& offsets, torch::Tensor& pos, torch::Tensor& xs);
+void moe_combine(const torch::Tensor& ys, const torch::Tensor& pos, const torch::Tensor& topk_w, torch::Tensor& out);
+
 // Normalisation.
 void rmsnorm(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, double eps);
 // residual += sum_s delta[s] (delta is bf16 [M,H] or f32 [S,M,H]); out = rmsnorm(residual) * w

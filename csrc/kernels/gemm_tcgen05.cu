@@ -46,6 +46,16 @@ struct Args {
   float* fix_ws;     // split-K fixup: [tiles, splits, BN, 128] fp32 partial accumulators
   int* fix_count;    // split-K fixup: (arrived, written) counters per output tile (self-resetting)
   int fixup;         // 1: splits > 1 with the last-arriving CTA reducing and running the epilogue
+  // grouped mode (MoE experts): a device-built tile list replaces the regular
+  // tile grid.  tiles[i] = (group, feat_tile, first token row, token row limit),
+  // the A operand of group g starts at row g * rows_per_group.
+  const int4* tiles;
+  const int* num_tiles_dev;
+  int rows_per_group;
+};
+
+struct Tile {
+  int ft, tt, sp, tok0, tok_end, arow;
 };
 
 template <int BN>
@@ -68,10 +78,32 @@ __device__ __forceinline__ void decode_tile(const Args& a, int t, int& feat_tile
 // Runs the fused epilogue of one output tile.  `load(c, v)` supplies the fp32
 // accumulator of columns [c, c+16) for this thread's row (feature), either
 // straight from TMEM or as the sum of the split-K partials.
+template <int BN>
+__device__ __forceinline__ Tile get_tile(const Args& a, int t) {
+  Tile r;
+  if (a.tiles != nullptr) {
+    const int4 d = a.tiles[t];
+    r.ft = d.y;
+    r.tt = 0;
+    r.sp = 0;
+    r.tok0 = d.z;
+    r.tok_end = d.w;
+    r.arow = d.x * a.rows_per_group + d.y * BM;
+  } else {
+    decode_tile(a, t, r.ft, r.tt, r.sp);
+    r.tok0 = r.tt * BN;
+    r.tok_end = a.M;
+    r.arow = r.ft * BM;
+  }
+  return r;
+}
+
 template <int BN, int EPI, typename Loader>
-__device__ __forceinline__ void epilogue_tile(const Args& a, int feat_tile, int tok_tile, int split, int row,
-                                              int lane, Loader&& load) {
-  const int tok0 = tok_tile * BN;
+__device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int row, int lane, Loader&& load) {
+  const int tok0 = tl.tok0;
+  const int tok_end = tl.tok_end;
+  const int feat_tile = tl.ft;
+  const int split = tl.sp;
   if constexpr (EPI == kEpiSwiGLU) {
     // Weight rows are interleaved per 32-row group: 16 gate rows then the 16
     // matching up rows, so gate and up of one feature sit in lanes l and l+16.
@@ -80,14 +112,14 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, int feat_tile, int 
     const bool writer = (lane < 16) && (f < nout);
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
     for (int c = 0; c < BN; c += 16) {
-      if (tok0 + c >= a.M) break;
+      if (tok0 + c >= tok_end) break;
       float v[16];
       load(c, v);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const float up = __shfl_down_sync(0xffffffffu, v[j], 16);
         const int tok = tok0 + c + j;
-        if (writer && tok < a.M) out[(long)tok * a.ldo + f] = __float2bfloat16(silu(v[j]) * up);
+        if (writer && tok < tok_end) out[(long)tok * a.ldo + f] = __float2bfloat16(silu(v[j]) * up);
       }
     }
   } else {
@@ -98,14 +130,14 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, int feat_tile, int 
       if (a.bias != nullptr && fvalid) bias = __bfloat162float(a.bias[f]);
     }
     for (int c = 0; c < BN; c += 16) {
-      if (tok0 + c >= a.M) break;
+      if (tok0 + c >= tok_end) break;
       float v[16];
       load(c, v);
       if (!fvalid) continue;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int tok = tok0 + c + j;
-        if (tok >= a.M) break;
+        if (tok >= tok_end) break;
         if constexpr (EPI == kEpiBF16) {
           reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] = __float2bfloat16(v[j] + bias);
         } else if constexpr (EPI == kEpiF32) {
@@ -189,7 +221,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total = a.num_feat_tiles * a.num_tok_tiles * a.splits;
+  const int total = a.tiles != nullptr ? *a.num_tiles_dev : a.num_feat_tiles * a.num_tok_tiles * a.splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -200,9 +232,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t issued_mask = 0, issued_par = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int ft, tt, sp;
-        decode_tile(a, t, ft, tt, sp);
-        const int kb0 = sp * a.kb_per_split;
+        const Tile tl = get_tile<BN>(a, t);
+        const int kb0 = tl.sp * a.kb_per_split;
         const int kb1 = min(kb0 + a.kb_per_split, a.num_kb);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.status, kStatusGemmTimeout)) {
@@ -210,8 +241,8 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-          tma_load_2d_hint(sA + stage * C::kABytes, &tmA, &full[stage], kb * BK, ft * BM, pol_w);
-          tma_load_2d_hint(sB + stage * C::kBBytes, &tmB, &full[stage], kb * BK, tt * BN, pol_x);
+          tma_load_2d_hint(sA + stage * C::kABytes, &tmA, &full[stage], kb * BK, tl.arow, pol_w);
+          tma_load_2d_hint(sB + stage * C::kBBytes, &tmB, &full[stage], kb * BK, tl.tok0, pol_x);
           issued_mask |= 1u << stage;
           issued_par = phase ? (issued_par | (1u << stage)) : (issued_par & ~(1u << stage));
           if (++stage == C::kStages) {
@@ -234,9 +265,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t acc_phase = 0;
       bool ok = true, issued_any = false;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int ft, tt, sp;
-        decode_tile(a, t, ft, tt, sp);
-        const int kb0 = sp * a.kb_per_split;
+        const Tile tl = get_tile<BN>(a, t);
+        const int kb0 = tl.sp * a.kb_per_split;
         const int kb1 = min(kb0 + a.kb_per_split, a.num_kb);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, a.status, kStatusGemmTimeout)) {
           ok = false;
@@ -281,8 +311,8 @@ __global__ void __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      int ft, tt, sp;
-      decode_tile(a, t, ft, tt, sp);
+      const Tile tl = get_tile<BN>(a, t);
+      const int ft = tl.ft, tt = tl.tt, sp = tl.sp;
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status, kStatusGemmTimeout);
       if (epi_barrier_or(!ok)) break;
       tc_fence_after();
@@ -292,7 +322,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_ld();
       };
       if (!a.fixup) {
-        epilogue_tile<BN, EPI>(a, ft, tt, sp, row, lane, from_tmem);
+        epilogue_tile<BN, EPI>(a, tl, row, lane, from_tmem);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -370,7 +400,7 @@ __global__ void __launch_bounds__(192, 1)
                 v[4 * j + 3] += acc4[j].w;
               }
             };
-            epilogue_tile<BN, EPI>(a, ft, tt, sp, row, lane, summed);
+            epilogue_tile<BN, EPI>(a, tl, row, lane, summed);
           }
           tc_fence_before();
           __syncwarp();
@@ -495,6 +525,9 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.fix_ws = nullptr;
   a.fix_count = nullptr;
   a.fixup = 0;
+  a.tiles = nullptr;
+  a.num_tiles_dev = nullptr;
+  a.rows_per_group = 0;
 
   switch (epi) {
     case kEpiBF16:
@@ -554,7 +587,7 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
 
   const CUtensorMap tmA = make_tmap_bf16_2d(w.data_ptr(), K, N, w.stride(0) * 2, gemm::BK, gemm::BM);
   const CUtensorMap tmB = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, bn);
-  const int total = a.num_feat_tiles * a.num_tok_tiles * a.splits;
+  const int total = a.tiles != nullptr ? *a.num_tiles_dev : a.num_feat_tiles * a.num_tok_tiles * a.splits;
   const int grid = std::min(total, num_sms(x.get_device()));
   switch (epi) {
     case kEpiBF16: gemm::dispatch_bn<kEpiBF16>(bn, tmA, tmB, a, grid, stream); break;
@@ -564,6 +597,48 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
     case kEpiResidual: gemm::dispatch_bn<kEpiResidual>(bn, tmA, tmB, a, grid, stream); break;
     case kEpiGelu: gemm::dispatch_bn<kEpiGelu>(bn, tmA, tmB, a, grid, stream); break;
   }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bloom
+
+namespace bloom {
+
+// Grouped GEMM for MoE experts: out[r] = x[r] @ w[g]^T for the rows r of every
+// tile in the device-built list (g = tile.x); w is [G * rows_per_group, K].
+void gemm_grouped_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
+                      const torch::Tensor& tiles, const torch::Tensor& num_tiles, int64_t rows_per_group, int64_t bn,
+                      const torch::Tensor& status) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "grouped gemm: bf16");
+  TORCH_CHECK(epi == kEpiBF16 || epi == kEpiSwiGLU, "grouped gemm: bf16 or SwiGLU epilogue");
+  TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4, "tiles int32 [n, 4]");
+  TORCH_CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256, "grouped gemm: bad token tile");
+  const int M = x.size(0), K = x.size(1);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  gemm::Args a{};
+  a.M = M;
+  a.N = int(rows_per_group);
+  a.K = K;
+  a.num_kb = (K + gemm::BK - 1) / gemm::BK;
+  a.kb_per_split = a.num_kb;
+  a.splits = 1;
+  a.num_feat_tiles = 1;
+  a.num_tok_tiles = 1;
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.status = status.data_ptr<int>();
+  a.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
+  a.num_tiles_dev = num_tiles.data_ptr<int>();
+  a.rows_per_group = int(rows_per_group);
+  const CUtensorMap tmA = make_tmap_bf16_2d(w.data_ptr(), K, w.size(0), w.stride(0) * 2, gemm::BK, gemm::BM);
+  const CUtensorMap tmB = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, int(bn));
+  const int grid = num_sms(x.get_device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (epi == kEpiSwiGLU)
+    gemm::dispatch_bn<kEpiSwiGLU>(int(bn), tmA, tmB, a, grid, stream);
+  else
+    gemm::dispatch_bn<kEpiBF16>(int(bn), tmA, tmB, a, grid, stream);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

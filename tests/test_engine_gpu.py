@@ -38,7 +38,7 @@ def _check_greedy(cfg, w, prompt, generated):
         assert gap <= 0.03 * spread + 1e-4, f"step {j}: token {tok} gap {gap} spread {spread}"
 
 
-@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2"])
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-moe"])
 @pytest.mark.parametrize("graphs", [False, True])
 def test_engine_greedy_matches_reference(name, graphs):
     from bloom_b200.engine.engine import SamplingParams
@@ -114,3 +114,21 @@ def test_engine_json_mode_constrained_decoding():
     d = runtime().JsonDfa()
     assert d.feed(text), text  # every emitted token kept a valid JSON prefix
     _json.loads(repair_json(text))
+
+
+def test_moe_routing_kernels_match_reference():
+    """Router top-k, grouped expert GEMMs and combine vs the dense fp32 MoE oracle."""
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.llama import DecoderLM
+    from bloom_b200.models.reference import moe_mlp, random_weights
+
+    cfg = preset("tiny-moe")
+    w = random_weights(cfg, seed=7, std=0.08, device="cuda")
+    m = DecoderLM(cfg, device="cuda")
+    m.shard_full(w)
+    for T in (1, 5, 64, 300):
+        x = torch.randn(T, cfg.hidden_size, device="cuda", dtype=torch.bfloat16)
+        got = m.moe.forward(0, x)
+        exp = moe_mlp(cfg, w, "model.layers.0.", x.float())
+        err = ((got.float() - exp).norm() / exp.norm()).item()
+        assert err < 2e-2, (T, err)

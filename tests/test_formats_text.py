@@ -1,0 +1,253 @@
+"""CPU tests: GGUF / safetensors / manifest formats, chat templates, text
+utilities, JSON recogniser, engine registry, CPU decoder vs the fp32 oracle."""
+import json
+import os
+
+import pytest
+import torch
+
+from bloom_b200.models.config import preset
+from bloom_b200.models.reference import random_weights
+
+
+# ---------------------------------------------------------------- GGUF
+@pytest.fixture(scope="module")
+def tiny_gguf(tmp_path_factory):
+    from bloom_b200.formats.gguf import GGML_Q8_0, write_decoder_gguf
+
+    cfg = preset("tiny-llama")
+    w = random_weights(cfg, seed=0, std=0.08)
+    p = str(tmp_path_factory.mktemp("gguf") / "tiny.gguf")
+    write_decoder_gguf(p, cfg, w, GGML_Q8_0)
+    return cfg, w, p
+
+
+def test_gguf_roundtrip_and_config(tiny_gguf):
+    from bloom_b200.formats.gguf import GGUFFile, config_from_gguf, load_hf_weights
+
+    cfg, w, p = tiny_gguf
+    g = GGUFFile(p)
+    assert g.version == 3 and g.arch == "llama" and g.primary_dtype() == "Q8_0"
+    c2 = config_from_gguf(g)
+    for k in ("hidden_size", "num_layers", "num_heads", "num_kv_heads", "head_dim", "intermediate_size"):
+        assert getattr(c2, k) == getattr(cfg, k)
+    w2 = load_hf_weights(g)
+    for k, v in w.items():
+        if v.dim() == 2:
+            err = ((w2[k].float() - v.float()).norm() / v.float().norm()).item()
+            assert err < 0.01, (k, err)  # Q8_0 rounding only; RoPE permutation undone exactly
+
+
+def test_gguf_q4_0_blocks():
+    from bloom_b200._ext import runtime
+
+    x = torch.randn(4096) * 0.1
+    raw = runtime().quantize_q4_0(x)
+    assert raw.numel() == 4096 // 32 * 18
+    y = runtime().dequant_q4_0(raw, 4096)
+    assert ((y - x).norm() / x.norm()).item() < 0.12
+
+
+def test_q8_0_matmul_matches_float():
+    from bloom_b200._ext import runtime
+
+    rt = runtime()
+    w = torch.randn(96, 256) * 0.05
+    x = torch.randn(3, 256)
+    y = rt.q8_0_matmul(x, rt.quantize_q8_0(w), 96, 256)
+    ref = x @ w.t()
+    assert ((y - ref).norm() / ref.norm()).item() < 0.02
+
+
+def test_bad_gguf_rejected(tmp_path):
+    from bloom_b200.formats.gguf import GGUFFile
+
+    p = tmp_path / "bad.gguf"
+    p.write_bytes(b"NOPE" + b"\0" * 64)
+    with pytest.raises(Exception):
+        GGUFFile(str(p))
+
+
+# ---------------------------------------------------------------- safetensors + manifest
+def test_safetensors_single_and_sharded(tmp_path):
+    from bloom_b200.formats.safetensors_io import (SafetensorsError, load_state_dict, resolve_shards, save_file,
+                                                    save_sharded)
+
+    t = {"a": torch.randn(4, 8).to(torch.bfloat16), "b": torch.arange(10, dtype=torch.int64)}
+    d1 = tmp_path / "single"
+    d1.mkdir()
+    save_file(t, str(d1 / "model.safetensors"))
+    sd = load_state_dict(str(d1))
+    assert torch.equal(sd["a"], t["a"]) and torch.equal(sd["b"], t["b"])
+    d2 = tmp_path / "sharded"
+    d2.mkdir()
+    names = save_sharded({f"w{i}": torch.randn(64, 64) for i in range(6)}, str(d2), 40_000)
+    assert len(names) > 1 and len(resolve_shards(str(d2))) == len(names)
+    os.remove(d2 / names[0])
+    with pytest.raises(SafetensorsError):
+        resolve_shards(str(d2))
+
+
+def test_safetensors_header_validation(tmp_path):
+    import struct
+
+    from bloom_b200.formats.safetensors_io import SafetensorsError, read_header
+
+    hdr = json.dumps({"x": {"dtype": "F32", "shape": [4], "data_offsets": [0, 32]}}).encode()
+    p = tmp_path / "bad.safetensors"
+    p.write_bytes(struct.pack("<Q", len(hdr)) + hdr + b"\0" * 16)
+    with pytest.raises(SafetensorsError):
+        read_header(str(p))
+
+
+def test_manifest_paths(tiny_gguf, tmp_path):
+    from bloom_b200.formats.manifest import ManifestError, estimate_memory, load_manifest, manifest_from_dict
+    from bloom_b200.formats.safetensors_io import save_file
+    from bloom_b200.models.config import to_hf_config
+
+    cfg, w, p = tiny_gguf
+    m = load_manifest(p)
+    assert m.family == "Llama" and m.primary_dtype == "Q8" and m.files[0].format == "Gguf"
+    hf = tmp_path / "hf"
+    hf.mkdir()
+    save_file(w, str(hf / "model.safetensors"))
+    (hf / "config.json").write_text(json.dumps(to_hf_config(cfg)))
+    (hf / "tokenizer.json").write_text("{}")
+    m2 = load_manifest(str(hf))
+    assert m2.primary_dtype == "BF16" and m2.parameters["num_hidden_layers"] == cfg.num_layers
+    (hf / "bloom.json").write_text(m2.to_json())
+    m3 = load_manifest(str(hf))
+    assert m3.id == m2.id
+    with pytest.raises(ManifestError):
+        manifest_from_dict({"id": "x"})
+    est = estimate_memory(m2, 4096, concurrent_seqs=8, tp=2)
+    assert est.kv_bytes_per_token == 2 * cfg.num_layers * cfg.num_kv_heads * cfg.head_dim * 2
+    assert est.fits
+
+
+def test_llama3_8b_memory_estimate_for_b200():
+    from bloom_b200.formats.manifest import ModelManifest, estimate_memory
+
+    c = preset("llama3-8b")
+    man = ModelManifest(id="l8", family="Llama", version="1", io_schema={"inputs": ["Text"], "outputs": ["Text"]},
+                        memory_profile={}, primary_dtype="BF16",
+                        parameters={"num_hidden_layers": 32, "hidden_size": 4096, "intermediate_size": 14336,
+                                    "vocab_size": 128256, "num_key_value_heads": 8, "head_dim": 128})
+    e1 = estimate_memory(man, 2304, concurrent_seqs=256, tp=1)
+    e8 = estimate_memory(man, 2304, concurrent_seqs=256, tp=8)
+    assert e1.kv_bytes_per_token == 128 * 1024  # 128 KiB per token across layers
+    assert e1.fits and e8.per_gpu_bytes < e1.per_gpu_bytes / 4
+
+
+# ---------------------------------------------------------------- templates / text
+def test_chat_templates():
+    from bloom_b200.engine.chat_template import classify_template, render, select_template
+
+    msgs = [{"role": "system", "content": "S"}, {"role": "user", "content": "U"}]
+    assert render(msgs, "chatml") == "<|im_start|>system\nS<|im_end|>\n<|im_start|>user\nU<|im_end|>\n<|im_start|>assistant\n"
+    assert render(msgs, "llama3").startswith("<|begin_of_text|><|start_header_id|>system<|end_header_id|>\n\nS<|eot_id|>")
+    assert render(msgs, "llama2") == "<s>[INST] <<SYS>>\nS\n<</SYS>>\n\nU [/INST]"
+    assert render([{"role": "user", "content": "U"}], "smollm2").startswith("<|im_start|>system\nYou are a helpful AI")
+    assert render(msgs, "qwen3-no-think").endswith("<think>\n\n</think>\n\n")
+    assert render(msgs, "gemma").endswith("<start_of_turn>model\n")
+    assert classify_template("{{'<|start_header_id|>'}}") == "llama3"
+    assert classify_template("<|im_start|>") == "chatml"
+    assert select_template("qwen", "qwen3") == "qwen3-no-think"
+
+
+def test_stop_filter_holds_partial_matches():
+    from bloom_b200.engine.text import StopSequenceFilter
+
+    f = StopSequenceFilter(["END"])
+    out = []
+    for d in ["ab", "cE", "N", "Dxyz"]:
+        o, stopped = f.push(d)
+        out.append(o)
+        if stopped:
+            break
+    assert "".join(out) == "abc" and stopped
+    f2 = StopSequenceFilter(["END"])
+    assert f2.push("xE")[0] == "x"
+    assert f2.push("y")[0] == "Ey"
+
+
+def test_detokenizer_incremental_utf8():
+    from bloom_b200.engine.text import Detokenizer, Tokenizer
+
+    tok = Tokenizer(None)
+    d = Detokenizer(tok)
+    s = "héllo ☃ world"
+    out = "".join(d.add(t) for t in tok.encode(s))
+    assert out == s
+
+
+def test_json_recogniser_and_repair():
+    from bloom_b200._ext import runtime
+    from bloom_b200.engine.structured import repair_json
+
+    rt = runtime()
+    d = rt.JsonDfa()
+    assert d.feed('{"a": [1, 2.5e3, true, null, "x\\u00e9"], ')
+    assert not d.can_feed("}")  # a key must follow the comma
+    assert d.feed('"b": {}}')
+    assert d.complete()
+    assert not rt.JsonDfa().feed("{'a': 1}")
+    assert not rt.JsonDfa().feed('{"a": 01}')
+    assert rt.is_valid_json('[1, {"k": "v"}]')
+    d2 = rt.JsonDfa()
+    assert d2.pick([5, 6], ['"', "{", "", "", "", "x", "{"], [7]) == 6
+    assert json.loads(repair_json('{"a": [1, 2, {"b": "hel')) == {"a": [1, 2, {"b": "hel"}]}
+    assert repair_json('{"ok": 1}') == '{"ok": 1}'
+
+
+def test_registry_routing():
+    from bloom_b200.engine.registry import FALLBACK, NATIVE, UNSUPPORTED, default_registry
+
+    r = default_registry()
+    assert r.route("Llama", "Safetensors", "BF16", "gpu") == ("b200", NATIVE)
+    assert r.route("Llama", "Gguf", "Q8", "gpu") == ("b200", FALLBACK)
+    assert r.route("Llama", "Gguf", "Q8", "cpu") == ("cpu", NATIVE)
+    assert r.route("Whisper", "Gguf", "Q8", "cpu")[1] == UNSUPPORTED
+    assert any(e["name"] == "b200" and e["max_tp"] == 8 for e in r.describe())
+
+
+# ---------------------------------------------------------------- CPU engine
+def test_cpu_decoder_matches_oracle_on_gguf(tiny_gguf):
+    from bloom_b200.engine.cpu_engine import CpuDecoder
+    from bloom_b200.formats.gguf import GGUFFile, load_hf_weights
+    from bloom_b200.models.reference import forward_logits
+
+    cfg, w, p = tiny_gguf
+    dec = CpuDecoder.from_gguf(p)
+    prompt = [5, 17, 99, 3, 250]
+    toks = list(dec.generate(prompt, 8, temperature=0.0, ignore_eos=True))
+    assert len(toks) == 8
+    wq = load_hf_weights(GGUFFile(p), dtype=torch.float32)
+    logits = forward_logits(cfg, wq, prompt + toks)
+    for j, t in enumerate(toks):
+        row = logits[len(prompt) - 1 + j]
+        assert (row.max() - row[t]).item() <= 0.05 * (row.max() - row.median()).item() + 1e-3
+
+
+def test_cli_inspect_and_echo_pipeline(tiny_gguf, capsys):
+    from bloom_b200.cli.infer import main
+    from bloom_b200.engine.engine import SamplingParams
+    from bloom_b200.engine.pipeline import InferencePipeline
+
+    cfg, w, p = tiny_gguf
+    assert main(["--model", p, "--inspect"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    for k in ("model_path", "selected_engine", "selected_engine_maturity", "context_size", "manifest",
+              "memory_estimate", "engines", "notes"):
+        assert k in out
+    pipe = InferencePipeline.load("echo")
+    assert pipe.run("hello", SamplingParams(max_tokens=10)) == "echo: hello"
+
+
+def test_cli_cpu_generation(tiny_gguf, capsys):
+    from bloom_b200.cli.infer import main
+
+    cfg, w, p = tiny_gguf
+    rc = main(["--model", p, "--device", "cpu", "--prompt", "hi", "--max-tokens", "4", "--temperature", "0",
+               "--raw", "--quiet"])
+    assert rc == 0

@@ -45,3 +45,8 @@ def test_tp_fused(n):
 @pytest.mark.parametrize("n", [2, 8])
 def test_tp_fused_eager(n):
     _run(n, "fused", graphs="eager", port=29671 + n)
+
+
+@pytest.mark.parametrize("n", [2, 8])
+def test_ep_moe_fused(n):
+    _run(n, "fused", model="tiny-moe-tp", port=29691 + n)
