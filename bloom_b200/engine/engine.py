@@ -83,6 +83,9 @@ class EngineConfig:
     use_cuda_graphs: bool = True
     autotune: bool = True
     seed: int = 0
+    # speculative decoding: proposals verified per sequence and step (0 = off);
+    # attach a proposer with LLMEngine.attach_speculator / make_speculator
+    spec_len: int = 0
 
 
 class LLMEngine:
@@ -106,13 +109,15 @@ class LLMEngine:
         sc.max_model_len = ec.max_model_len
         sc.chunked_prefill = ec.chunked_prefill
         sc.eos_token_ids = list(self.cfg.eos_token_ids)
+        sc.spec_len = int(ec.spec_len)
         self.scheduler = rt.Scheduler(sc, ec.num_blocks, 16, ec.enable_prefix_caching)
         self.runner = ModelRunner(model, ec.num_blocks, ec.max_num_seqs, ec.max_num_batched_tokens,
-                                  ec.max_model_len, ec.use_cuda_graphs)
+                                  ec.max_model_len, ec.use_cuda_graphs, spec_len=int(ec.spec_len))
         if ec.autotune and dev.type == "cuda":
             from .. import ops
 
-            ops.gemm_autotune(model.gemm_shapes(), self.runner.buckets + [ec.max_num_seqs], dev)
+            ql = self.runner.q_len
+            ops.gemm_autotune(model.gemm_shapes(), [b * ql for b in self.runner.buckets + [ec.max_num_seqs]], dev)
         self.scheduler.set_arena(self.runner.arena_host, self.runner.max_tokens, ec.max_num_seqs,
                                  self.runner.max_blocks)
         if ec.use_cuda_graphs:
@@ -123,6 +128,12 @@ class LLMEngine:
         self.tokenizer = None  # set by the pipeline; needed for JSON-mode constraints
         self._seed_counter = ec.seed
         self.step_times: List[float] = []
+        self.speculator = None
+
+    def attach_speculator(self, spec) -> None:
+        if int(spec.k) != int(self.econf.spec_len):
+            raise ValueError(f"speculator proposes {spec.k} tokens but the engine verifies {self.econf.spec_len}")
+        self.speculator = spec
 
     # ------------------------------------------------------------ construction helpers
     @staticmethod
@@ -158,6 +169,8 @@ class LLMEngine:
 
     def abort(self, request_id: int) -> bool:
         self.constraints.pop(request_id, None)
+        if self.speculator is not None:
+            self.speculator.forget(request_id)
         ok = self.scheduler.abort(request_id)
         r = self.requests.get(request_id)
         if ok and r is not None:
@@ -172,6 +185,10 @@ class LLMEngine:
     def step(self) -> List[RequestOutput]:
         """One engine step; returns the requests that received a token."""
         t0 = time.perf_counter()
+        if self.speculator is not None:
+            self.speculator.propose(self)
+            for rid in self.constraints:
+                self.scheduler.set_draft(rid, [])
         meta = self.scheduler.schedule()
         if meta.num_tokens == 0:
             return []
@@ -194,6 +211,8 @@ class LLMEngine:
                 c.advance(tok)
             if finished:
                 self.constraints.pop(rid, None)
+                if self.speculator is not None:
+                    self.speculator.forget(rid)
                 r.finished = True
                 r.finish_reason = FINISH_REASONS.get(reason, "stop")
                 r.finish_time = now
@@ -205,7 +224,8 @@ class LLMEngine:
         """JSON mode: replace the sampled token of constrained rows by the best
         candidate (top-256 logits) that keeps the output valid JSON."""
         ids = self.scheduler.sampling_ids()
-        rows = [(i, sid) for i, sid in enumerate(ids) if sid in self.constraints]
+        # first row of each request only (constrained requests get no proposals)
+        rows = [(i, sid) for i, sid in enumerate(ids) if sid in self.constraints and (i == 0 or ids[i - 1] != sid)]
         if not rows or self.runner.last_logits is None or self.model.tp.size > 1:
             return
         logits = self.runner.last_logits

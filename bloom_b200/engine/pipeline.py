@@ -180,8 +180,9 @@ class InferencePipeline:
             dm.random_init(0)
         else:
             dm.shard_full(load_weights(man))
+        spec_len = nspec if speculative in ("ngram", "draft") else 0
         llm = LLMEngine(dm, EngineConfig(max_num_seqs=max_num_seqs, max_num_batched_tokens=max(ctx, 2048),
-                                         max_model_len=ctx, use_cuda_graphs=use_cuda_graphs))
+                                         max_model_len=ctx, use_cuda_graphs=use_cuda_graphs, spec_len=spec_len))
         llm.tokenizer = tok
         spec = None
         if speculative in ("ngram", "draft"):
@@ -229,9 +230,7 @@ class InferencePipeline:
         if self.cpu is not None:
             toks = self.cpu.generate(ids, max_new, params.temperature, params.top_p, params.seed, eos,
                                      params.ignore_eos)
-        elif self.spec is not None:
-            toks = self.spec.generate(ids, max_new, params, eos)
-        else:
+        else:  # speculation, when configured, is attached to the engine itself
             from dataclasses import replace
 
             p2 = replace(params, max_tokens=max_new, stop_token_ids=list(set(params.stop_token_ids) | set(eos)))

@@ -40,14 +40,17 @@ class ModelRunner:
         max_model_len: int = 4096,
         use_cuda_graphs: bool = True,
         graph_buckets: Optional[List[int]] = None,
+        spec_len: int = 0,
     ):
         self.model = model
         self.cfg = model.cfg
         self.device = model.device
         self.block_size = 16
         self.max_num_seqs = max_num_seqs
-        self.max_tokens = max(max_num_batched_tokens, max_num_seqs)
-        self.max_blocks = (max_model_len + self.block_size - 1) // self.block_size
+        self.q_len = spec_len + 1  # token rows per decode sequence (verify rows when speculating)
+        self.max_tokens = max(max_num_batched_tokens, max_num_seqs * self.q_len)
+        # verify rows may run spec_len positions past the last token
+        self.max_blocks = (max_model_len + spec_len + self.block_size - 1) // self.block_size
         self.num_blocks = num_blocks
         cfg = self.cfg
         # zero-filled: masked tail slots of a page are multiplied by p = 0, which must not meet NaN bit patterns
@@ -55,11 +58,12 @@ class ModelRunner:
                                     dtype=torch.bfloat16, device=self.device)
         rt = _rt()
         worst = rt.arena_layout(self.max_tokens, max_num_seqs, max_num_seqs,
-                                self.max_tokens // 64 + max_num_seqs, max_num_seqs, self.max_blocks)
+                                self.max_tokens // 64 + max_num_seqs, self.max_tokens + max_num_seqs,
+                                self.max_blocks)
         self.arena_words = worst.used_words
         self.arena_host = torch.zeros(self.arena_words, dtype=torch.int32).pin_memory()
         self.arena_dev = torch.zeros(self.arena_words, dtype=torch.int32, device=self.device)
-        self.sampled_host = torch.zeros(max(max_num_seqs, 1), dtype=torch.int32).pin_memory()
+        self.sampled_host = torch.zeros(self.max_tokens + max_num_seqs, dtype=torch.int32).pin_memory()
         self.buckets = [b for b in (graph_buckets or DEFAULT_BUCKETS) if b <= max_num_seqs]
         if max_num_seqs not in self.buckets:
             self.buckets.append(max_num_seqs)
@@ -67,10 +71,14 @@ class ModelRunner:
         # decode attention split-K workspace, sized for the largest need over buckets
         ws = 1
         self.decode_splits: Dict[int, int] = {}
+        self.head_chunks = ops.decode_head_chunks(model.nq, model.nkv, self.q_len)
+        if self.head_chunks == 0:
+            raise ValueError(f"speculation length {spec_len} does not fit the decode attention kernel")
+        vkh = model.nkv * self.head_chunks  # CTAs per sequence and split
         for b in range(1, max_num_seqs + 1):  # eager steps may have any decode count
-            s = ops.decode_attention_splits(b, model.nkv, self.max_blocks, self.device.index)
+            s = ops.decode_attention_splits(b, vkh, self.max_blocks, self.device.index)
             self.decode_splits[b] = s
-            ws = max(ws, ops.decode_workspace_numel(b, model.nkv, s))
+            ws = max(ws, ops.decode_workspace_numel(b, vkh, s))
         self.decode_ws = torch.empty(ws, dtype=torch.float32, device=self.device)
         self.graphs: Dict[int, tuple] = {}
         self.last_logits: Optional[torch.Tensor] = None
@@ -92,8 +100,8 @@ class ModelRunner:
         MB = self.max_blocks
         splits = 1
         if Bd:
-            splits = self.decode_splits.get(Bd) or ops.decode_attention_splits(Bd, self.model.nkv, MB,
-                                                                              self.device.index)
+            splits = self.decode_splits.get(Bd) or ops.decode_attention_splits(
+                Bd, self.model.nkv * self.head_chunks, MB, self.device.index)
         return StepInputs(
             input_ids=self._v(m.off_input_ids, T),
             positions=self._v(m.off_positions, T, torch.int64),
@@ -110,12 +118,15 @@ class ModelRunner:
             tile_seq=self._v(m.off_tile_seq, NT) if Sp else None,
             tile_start=self._v(m.off_tile_start, NT) if Sp else None,
             logits_rows=self._v(m.off_logits_rows, NL),
+            decode_q_len=m.decode_q_len,
         )
 
     def sampling_views(self, m):
         NL = m.num_logits
+        draft = self._v(m.off_draft_ids, NL) if self.q_len > 1 else None
         return (self._v(m.off_temperature, NL, torch.float32), self._v(m.off_top_p, NL, torch.float32),
-                self._v(m.off_top_k, NL), self._v(m.off_seeds, NL, torch.int64), self._v(m.off_offsets, NL, torch.int64))
+                self._v(m.off_top_k, NL), self._v(m.off_seeds, NL, torch.int64), self._v(m.off_offsets, NL, torch.int64),
+                draft)
 
     # ------------------------------------------------------------ sampling
     def _sample(self, logits: torch.Tensor, m, greedy: bool) -> torch.Tensor:
@@ -138,13 +149,18 @@ class ModelRunner:
         rt = _rt()
         buckets = sorted(buckets or self.buckets, reverse=True)
         # a valid dummy step: every row reads one page of block 0, writes no KV
+        ql = self.q_len
         for B in buckets:
-            m = rt.arena_layout(B, B, 0, 0, B, self.max_blocks)
+            T = B * ql
+            m = rt.arena_layout(T, B, 0, 0, T, self.max_blocks, ql)
             h = self.arena_host
             h[:m.used_words].zero_()  # regions of the previous bucket's layout must not leak in
-            h[m.off_slot_mapping:m.off_slot_mapping + B] = -1
-            h[m.off_decode_seq_lens:m.off_decode_seq_lens + B] = 1
-            h[m.off_logits_rows:m.off_logits_rows + B] = torch.arange(B, dtype=torch.int32)
+            h[m.off_slot_mapping:m.off_slot_mapping + T] = -1
+            h[m.off_decode_seq_lens:m.off_decode_seq_lens + B] = ql
+            pos = h[m.off_positions:m.off_positions + 2 * T].view(torch.int64)
+            pos.copy_(torch.arange(ql, dtype=torch.int64).repeat(B))
+            h[m.off_logits_rows:m.off_logits_rows + T] = torch.arange(T, dtype=torch.int32)
+            h[m.off_draft_ids:m.off_draft_ids + T] = -1
             self.arena_dev[:m.used_words].copy_(self.arena_host[:m.used_words])
             s = self.views(m)
             torch.cuda.synchronize(self.device)

@@ -5,7 +5,8 @@ Per layer and step (T tokens: decode rows first, then chunked-prefill rows):
 
     qkv   = gemm(x, W_qkv) (+bias)                      tcgen05 GEMM
     q     = rope_kv_write(qkv) -> paged KV pages         RoPE (+q/k RMSNorm) fused with the KV write
-    attn  = paged_decode_attention(q[:Bd]) | paged_prefill_attention(q[Bd:])
+    attn  = paged_decode_attention(q[:Bd*ql]) | paged_prefill_attention(q[Bd*ql:])
+            (ql = 1 + proposals per sequence when verifying speculative tokens)
     o     = gemm(attn, W_o)                              (split-K fp32 partials on small batches)
     x     = add_rmsnorm(o -> residual)                   [tensor parallel: reduce across ranks]
     act   = gemm(x, W_gate_up, epilogue=SwiGLU)          gate/up rows interleaved, SwiGLU in the epilogue
@@ -303,6 +304,7 @@ class DecoderLM:
         cfg = self.cfg
         T = s.input_ids.shape[0]
         Bd = s.num_decode
+        Td = Bd * s.decode_q_len  # decode / verify token rows come first
         H = cfg.hidden_size
         eps = cfg.rms_norm_eps
         dev = self.device
@@ -316,12 +318,12 @@ class DecoderLM:
                               lay.get("q_norm"), lay.get("k_norm"), eps)
             attn = torch.empty_like(q)
             if Bd > 0:
-                ops.paged_decode_attention(q[:Bd], kv_cache, li, s.decode_block_table, s.decode_seq_lens, attn[:Bd],
+                ops.paged_decode_attention(q[:Td], kv_cache, li, s.decode_block_table, s.decode_seq_lens, attn[:Td],
                                            q_len=s.decode_q_len, splits=s.decode_splits,
                                            workspace=s.decode_workspace, scale=self.scale)
             if s.num_prefill > 0:
-                ops.paged_prefill_attention(q[Bd:], kv_cache, li, s.prefill_block_table, s.prefill_ctx_lens,
-                                            s.prefill_cu_q, s.tile_seq, s.tile_start, attn[Bd:], scale=self.scale)
+                ops.paged_prefill_attention(q[Td:], kv_cache, li, s.prefill_block_table, s.prefill_ctx_lens,
+                                            s.prefill_cu_q, s.tile_seq, s.tile_start, attn[Td:], scale=self.scale)
             a2 = attn.view(T, self.nq * cfg.head_dim)
             x = self._row_parallel_norm(a2, lay["o"], residual, lay["ln2"], eps)
             nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm

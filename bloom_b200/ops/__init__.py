@@ -272,15 +272,28 @@ def decode_attention_splits(batch: int, num_kv_heads: int, max_pages: int, devic
     return _C().decode_attention_splits(batch, num_kv_heads, max_pages, device)
 
 
-def decode_workspace_numel(batch: int, num_kv_heads: int, splits: int) -> int:
-    return batch * num_kv_heads * splits * 32 * 130 if splits > 1 else 1
+def decode_head_chunks(num_q_heads: int, num_kv_heads: int, q_len: int) -> int:
+    """CTAs per KV head of decode/verify attention: the smallest divisor hc of
+    the group size G with (G / hc) * q_len <= 32 packed MMA rows (0: none)."""
+    if num_kv_heads <= 0 or q_len < 1 or num_q_heads % num_kv_heads:
+        return 0
+    G = num_q_heads // num_kv_heads
+    for hc in range(1, G + 1):
+        if G % hc == 0 and (G // hc) * q_len <= 32:
+            return hc
+    return 0
+
+
+def decode_workspace_numel(batch: int, num_kv_heads: int, splits: int, head_chunks: int = 1) -> int:
+    return batch * num_kv_heads * head_chunks * splits * 32 * 130 if splits > 1 else 1
 
 
 def paged_decode_attention(q, kv_cache, layer, block_table, seq_lens, out, *, q_len: int = 1, splits: int = 1,
                            workspace: Optional[torch.Tensor] = None, scale: float):
     if workspace is None:
+        hc = decode_head_chunks(q.shape[-2], kv_cache.shape[3], q_len)
         workspace = torch.empty(
-            decode_workspace_numel(seq_lens.shape[0], kv_cache.shape[3], splits), dtype=torch.float32,
+            decode_workspace_numel(seq_lens.shape[0], kv_cache.shape[3], splits, hc), dtype=torch.float32,
             device=q.device)
     _C().paged_decode_attention(q, kv_cache, layer, block_table, seq_lens, out, q_len, splits, workspace, scale,
                                 status(q.device.index))
@@ -320,10 +333,16 @@ def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
     return out
 
 
-def sample(logits, temperature, top_p, top_k, seeds, offsets, out: Optional[torch.Tensor] = None):
+def sample(logits, temperature, top_p, top_k, seeds, offsets, draft=None, out: Optional[torch.Tensor] = None):
+    """Per-row temperature / top-k / top-p sampling (greedy rows: argmax).  With
+    `draft` (int32 per row, -1 = none) stochastic rows verify their proposal by
+    rejection sampling (accept with p(draft), else sample with it removed)."""
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
-    _C().sample_rows(logits, temperature, top_p, top_k, seeds, offsets, out)
+    if draft is None:
+        _C().sample_rows(logits, temperature, top_p, top_k, seeds, offsets, out)
+    else:
+        _C().verify_sample_rows(logits, temperature, top_p, top_k, seeds, offsets, draft, out)
     _count()
     return out
 

@@ -94,11 +94,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readwrite("max_num_batched_tokens", &SchedulerConfig::max_num_batched_tokens)
       .def_readwrite("max_model_len", &SchedulerConfig::max_model_len)
       .def_readwrite("chunked_prefill", &SchedulerConfig::chunked_prefill)
-      .def_readwrite("eos_token_ids", &SchedulerConfig::eos_token_ids);
+      .def_readwrite("eos_token_ids", &SchedulerConfig::eos_token_ids)
+      .def_readwrite("spec_len", &SchedulerConfig::spec_len);
 
   py::class_<StepMeta>(m, "StepMeta")
       .def_readonly("num_tokens", &StepMeta::num_tokens)
       .def_readonly("num_decode", &StepMeta::num_decode)
+      .def_readonly("decode_q_len", &StepMeta::decode_q_len)
       .def_readonly("num_real_decode", &StepMeta::num_real_decode)
       .def_readonly("num_prefill", &StepMeta::num_prefill)
       .def_readonly("num_tiles", &StepMeta::num_tiles)
@@ -121,12 +123,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readonly("off_top_k", &StepMeta::off_top_k)
       .def_readonly("off_temperature", &StepMeta::off_temperature)
       .def_readonly("off_top_p", &StepMeta::off_top_p)
+      .def_readonly("off_draft_ids", &StepMeta::off_draft_ids)
       .def_readonly("off_seeds", &StepMeta::off_seeds)
       .def_readonly("off_offsets", &StepMeta::off_offsets)
       .def_readonly("used_words", &StepMeta::used_words);
 
   m.def("arena_layout", &arena_layout, py::arg("T"), py::arg("Bd"), py::arg("Sp"), py::arg("NT"), py::arg("NL"),
-        py::arg("MB"));
+        py::arg("MB"), py::arg("q_len") = 1);
+  m.def("ngram_propose", &ngram_propose, py::arg("tokens"), py::arg("k"), py::arg("max_order") = 4,
+        py::arg("min_order") = 1);
 
   py::class_<Scheduler>(m, "Scheduler")
       .def(py::init<const SchedulerConfig&, int, int, bool>(), py::arg("config"), py::arg("num_blocks"),
@@ -141,7 +146,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
             a.max_seqs = max_seqs;
             a.max_blocks = max_blocks;
             const StepMeta worst = arena_layout(max_tokens, max_seqs, max_seqs, max_tokens / 64 + max_seqs,
-                                                max_seqs, max_blocks);
+                                                max_tokens + max_seqs, max_blocks);
             TORCH_CHECK(worst.used_words <= a.capacity, "arena too small: need ", worst.used_words, " words");
             s.set_arena(a);
           },
@@ -179,6 +184,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              return q == nullptr ? 0 : q->num_cached_prefix;
            })
       .def("sampling_ids", &Scheduler::sampling_ids)
+      .def("decode_candidates", &Scheduler::decode_candidates)
+      .def("set_draft", &Scheduler::set_draft)
+      .def("propose_ngram", &Scheduler::propose_ngram, py::arg("max_order") = 4, py::arg("min_order") = 1)
+      .def("set_tail", &Scheduler::set_tail)
+      .def("spec_stats",
+           [](const Scheduler& s) {
+             py::dict d;
+             d["verify_groups"] = s.spec_steps();
+             d["proposed"] = s.spec_proposed();
+             d["accepted"] = s.spec_accepted();
+             return d;
+           })
       .def("kv_metrics", [](Scheduler& s) { return metrics_dict(s.blocks().metrics()); })
       .def("reset_prefix_cache", [](Scheduler& s) { s.blocks().reset_prefix_cache(); });
 

@@ -68,12 +68,24 @@ void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cac
                              const torch::Tensor& tile_start, torch::Tensor& out, double scale, bool causal,
                              const torch::Tensor& status);
 int64_t decode_attention_splits(int64_t batch, int64_t num_kv_heads, int64_t max_pages, int64_t device);
+// CTAs per KV head for decode/verify attention: the smallest divisor hc of
+// G = q heads per KV head with (G / hc) * q_len <= 32 (0 if none).
+int64_t decode_head_chunks(int64_t num_q_heads, int64_t num_kv_heads, int64_t q_len);
 
 // Sampling.
 void argmax_rows(const torch::Tensor& logits, torch::Tensor& out);
 void sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
                  const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
                  torch::Tensor& out);
+// Sampling with speculative verification.  Row b carries a proposal
+// draft[b] (-1: none).  Greedy rows return the argmax.  Stochastic rows accept
+// the proposal with probability p(draft) under the row's temperature/top-k/
+// top-p distribution, otherwise draw from that distribution with the proposal
+// removed (rejection sampling with a deterministic proposal; exact for the
+// target distribution).  A row without a proposal samples as sample_rows.
+void verify_sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
+                        const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
+                        const torch::Tensor& draft, torch::Tensor& out);
 
 // Tensor-parallel collectives over peer memory (pointers are device addresses
 // valid in this process, one per rank: the local buffer and the peer mappings).

@@ -72,8 +72,9 @@ struct DecodeArgs {
   const int* block_table;
   int bt_stride;
   const int* seq_lens;  // kv length per sequence, including the ql new tokens
-  float* part;          // [B, nkv, splits, 32, 130] (o[128], m, l)
+  float* part;          // [B, nkv * hc, splits, 32, 130] (o[128], m, l)
   int nq, nkv, ql, splits;
+  int hc;               // CTAs per KV head, each taking G / hc of its q heads (G * ql > 32)
   float scale_log2;
   int* status;
 };
@@ -83,10 +84,11 @@ template <int MT, int NWARPS, int NST>
 __global__ void __launch_bounds__(NWARPS * 32)
     decode_kernel(const __grid_constant__ CUtensorMap tmKV, const DecodeArgs a) {
   constexpr int kStageBytes = 2 * PAGE * D * 2;  // K + V page = 8 KiB
-  const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
+  const int b = blockIdx.x, vkh = blockIdx.y, split = blockIdx.z;
+  const int kh = vkh / a.hc;  // KV head whose pages this CTA streams
   const int warp = warp_id(), lane = lane_id();
   const int g = lane >> 2, t4 = lane & 3;
-  const int G = a.nq / a.nkv;
+  const int G = a.nq / (a.nkv * a.hc);  // q heads handled by this CTA: vkh * G ...
   const int R = a.ql * G;
 
   extern __shared__ uint8_t smem_raw[];
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
       const __nv_bfloat16* qrow = nullptr;
       if (r < R) {
         const int qi = r / G, hh = r - qi * G;
-        qrow = a.q + ((long)(b * a.ql + qi) * a.nq + kh * G + hh) * D;
+        qrow = a.q + ((long)(b * a.ql + qi) * a.nq + vkh * G + hh) * D;
       }
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
@@ -304,9 +306,9 @@ __global__ void __launch_bounds__(NWARPS * 32)
     }
     if (a.splits == 1) {
       const int qi = r / G, hh = r - qi * G;
-      a.out[((long)(b * a.ql + qi) * a.nq + kh * G + hh) * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+      a.out[((long)(b * a.ql + qi) * a.nq + vkh * G + hh) * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
     } else {
-      float* pr = a.part + ((((long)b * a.nkv + kh) * a.splits + split) * 32 + r) * RS;
+      float* pr = a.part + ((((long)b * a.nkv * a.hc + vkh) * a.splits + split) * 32 + r) * RS;
       pr[d] = O;
       if (d == 0) {
         pr[D] = M;
@@ -568,11 +570,19 @@ void launch_decode(const CUtensorMap& tm, const DecodeArgs& a, int B, cudaStream
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     configured |= uint64_t(1) << dev;
   }
-  dim3 grid(B, a.nkv, a.splits);
+  dim3 grid(B, a.nkv * a.hc, a.splits);
   kern<<<grid, NWARPS * 32, smem, stream>>>(tm, a);
 }
 
 }  // namespace attn
+
+int64_t decode_head_chunks(int64_t num_q_heads, int64_t num_kv_heads, int64_t q_len) {
+  if (num_kv_heads <= 0 || q_len < 1 || num_q_heads % num_kv_heads) return 0;
+  const int64_t G = num_q_heads / num_kv_heads;
+  for (int64_t hc = 1; hc <= G; ++hc)
+    if (G % hc == 0 && (G / hc) * q_len <= 32) return hc;
+  return 0;
+}
 
 int64_t decode_attention_splits(int64_t batch, int64_t num_kv_heads, int64_t max_pages, int64_t device) {
   const int64_t ctas = batch * num_kv_heads;
@@ -597,7 +607,8 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
   const int nkv = kv_cache.size(3);
   TORCH_CHECK(nq % nkv == 0, "decode: nq must be a multiple of nkv");
   const int G = nq / nkv;
-  TORCH_CHECK(q_len >= 1 && G * q_len <= 32, "decode: (q heads per kv head) * q_len must be <= 32");
+  const int hc = int(decode_head_chunks(nq, nkv, q_len));
+  TORCH_CHECK(hc > 0, "decode: no split of the ", G, " q heads per kv head fits 32 rows at q_len ", q_len);
   TORCH_CHECK(q.numel() / (nq * attn::D) == B * q_len, "decode: q rows must equal batch * q_len");
   const at::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -611,24 +622,27 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
   a.nq = nq;
   a.nkv = nkv;
   a.ql = int(q_len);
+  a.hc = hc;
   a.splits = std::max<int>(1, int(splits));
   a.scale_log2 = float(scale * 1.4426950408889634);
   a.status = status.data_ptr<int>();
   a.part = nullptr;
   if (a.splits > 1) {
     TORCH_CHECK(workspace.scalar_type() == at::kFloat &&
-                    workspace.numel() >= (int64_t)B * nkv * a.splits * 32 * (attn::D + 2),
+                    workspace.numel() >= (int64_t)B * nkv * hc * a.splits * 32 * (attn::D + 2),
                 "decode: workspace too small");
     a.part = workspace.data_ptr<float>();
   }
   const CUtensorMap tm = attn::kv_tmap(kv_cache, layer);
-  if (G * q_len <= 16)
+  if ((G / hc) * q_len <= 16)
     attn::launch_decode<1, 4, 3>(tm, a, B, stream);
   else
     attn::launch_decode<2, 4, 3>(tm, a, B, stream);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (a.splits > 1) {
-    attn::decode_combine_kernel<<<dim3(B, nkv), 256, 0, stream>>>(a.part, a.out, nq, nkv, a.ql, a.splits);
+    // each (kv head, head chunk) pair acts as its own "kv head" of G / hc q heads
+    attn::decode_combine_kernel<<<dim3(B, nkv * hc), 256, 0, stream>>>(a.part, a.out, nq, nkv * hc, a.ql,
+                                                                      a.splits);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -785,6 +799,7 @@ extern "C" __attribute__((visibility("default"))) int bloom_paged_decode_attenti
   a.nq = num_q_heads;
   a.nkv = num_kv_heads;
   a.ql = q_len;
+  a.hc = 1;
   a.splits = splits;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.status = noalloc::g_dev[dev].status;

@@ -128,7 +128,7 @@ template <typename T>
 __global__ void sample_kernel(const T* __restrict__ logits, long ld, int V, const float* __restrict__ temp,
                               const float* __restrict__ top_p, const int* __restrict__ top_k,
                               const int64_t* __restrict__ seeds, const int64_t* __restrict__ offsets,
-                              int* __restrict__ out) {
+                              const int* __restrict__ draft, int* __restrict__ out) {
   __shared__ float red[33];
   const int b = blockIdx.x;
   const T* row = logits + (long)b * ld;
@@ -191,14 +191,35 @@ __global__ void sample_kernel(const T* __restrict__ logits, long ld, int V, cons
       lo = l0;
     }
   }
-  // Gumbel-max over kept tokens
   const uint32_t k0 = static_cast<uint32_t>(seeds[b]), k1 = static_cast<uint32_t>(static_cast<uint64_t>(seeds[b]) >> 32);
   const uint64_t off = static_cast<uint64_t>(offsets[b]);
+  // Speculative proposal: accept with probability p(d) of the kept,
+  // renormalised distribution; on rejection d leaves the support, which is
+  // the residual max(0, p - q) for a proposal q that is one-hot on d.
+  int excluded = -1;
+  const int d = draft ? draft[b] : -1;
+  if (d >= 0 && d < V) {
+    float zk = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float l = to_f(row[i]);
+      if (l >= lo) zk += __expf((l - mx) * inv_t);
+    }
+    zk = block_sum_f<T>(zk, red);
+    const float ld = to_f(row[d]);
+    const float pd = (ld >= lo && zk > 0.f) ? __expf((ld - mx) * inv_t) / zk : 0.f;
+    const U4 r = philox4x32_10(U4{0xffffffffu, static_cast<uint32_t>(off), static_cast<uint32_t>(off >> 32), 0xacce97edu}, k0, k1);
+    if (u01(r.x) < pd) {
+      if (threadIdx.x == 0) out[b] = d;
+      return;
+    }
+    excluded = d;
+  }
+  // Gumbel-max over kept tokens
   float best = -INFINITY;
-  int bi = amax;
+  int bi = amax != excluded ? amax : -1;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float l = to_f(row[i]);
-    if (l < lo) continue;
+    if (l < lo || i == excluded) continue;
     const U4 r = philox4x32_10(U4{static_cast<uint32_t>(i), static_cast<uint32_t>(off), static_cast<uint32_t>(off >> 32), 0x5eed5eedu}, k0, k1);
     const float gumbel = -__logf(-__logf(u01(r.x)));
     argmax_combine(best, bi, l * inv_t + gumbel, i);
@@ -225,7 +246,7 @@ __global__ void sample_kernel(const T* __restrict__ logits, long ld, int V, cons
       const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
       argmax_combine(best, bi, v2, i2);
     }
-    if (threadIdx.x == 0) out[b] = bi;
+    if (threadIdx.x == 0) out[b] = (bi >= 0 && bi < V) ? bi : amax;
   }
 }
 
@@ -246,28 +267,46 @@ void argmax_rows(const torch::Tensor& logits, torch::Tensor& out) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
-                 const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
-                 torch::Tensor& out) {
+namespace {
+void launch_sample(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
+                   const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
+                   const int* draft, torch::Tensor& out) {
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: logits [B, V]");
   const int B = logits.size(0), V = logits.size(1);
   if (B == 0) return;
   TORCH_CHECK(temperature.scalar_type() == at::kFloat && top_p.scalar_type() == at::kFloat, "sample: f32 params");
   TORCH_CHECK(top_k.scalar_type() == at::kInt && seeds.scalar_type() == at::kLong && offsets.scalar_type() == at::kLong,
               "sample: top_k int32, seeds/offsets int64");
+  TORCH_CHECK(temperature.numel() >= B && top_p.numel() >= B && top_k.numel() >= B && seeds.numel() >= B &&
+                  offsets.numel() >= B && out.numel() >= B,
+              "sample: per-row parameters shorter than the logits rows");
   const at::cuda::CUDAGuard g(logits.device());
   auto s = at::cuda::getCurrentCUDAStream();
   if (logits.scalar_type() == at::kFloat)
     sample_kernel<float><<<B, kThreads, 0, s>>>(logits.data_ptr<float>(), logits.stride(0), V,
                                                  temperature.data_ptr<float>(), top_p.data_ptr<float>(),
                                                  top_k.data_ptr<int>(), seeds.data_ptr<int64_t>(),
-                                                 offsets.data_ptr<int64_t>(), out.data_ptr<int>());
+                                                 offsets.data_ptr<int64_t>(), draft, out.data_ptr<int>());
   else
     sample_kernel<__nv_bfloat16><<<B, kThreads, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0), V, temperature.data_ptr<float>(),
-        top_p.data_ptr<float>(), top_k.data_ptr<int>(), seeds.data_ptr<int64_t>(), offsets.data_ptr<int64_t>(),
+        top_p.data_ptr<float>(), top_k.data_ptr<int>(), seeds.data_ptr<int64_t>(), offsets.data_ptr<int64_t>(), draft,
         out.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+}  // namespace
+
+void sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
+                 const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
+                 torch::Tensor& out) {
+  launch_sample(logits, temperature, top_p, top_k, seeds, offsets, nullptr, out);
+}
+
+void verify_sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
+                        const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
+                        const torch::Tensor& draft, torch::Tensor& out) {
+  TORCH_CHECK(draft.scalar_type() == at::kInt && draft.numel() >= logits.size(0), "verify: draft int32 [B]");
+  launch_sample(logits, temperature, top_p, top_k, seeds, offsets, draft.data_ptr<int>(), out);
 }
 
 torch::Tensor status_tensor(int64_t device) {

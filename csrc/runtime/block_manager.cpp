@@ -162,6 +162,17 @@ void BlockManager::truncate(std::vector<int32_t>& table, std::vector<uint64_t>& 
     }
   }
   const int full = num_tokens / block_size_;
+  if (static_cast<int>(table.size()) > full) {
+    // the kept partial tail block will be written again: it may no longer
+    // stand for a full cached prefix, and it must not be shared
+    const int b = table[full];
+    if (refcount_[b] > 1) throw std::logic_error("truncate: cannot cut into a block shared by another sequence");
+    if (block_hash_[b] != 0) {
+      auto f = by_hash_.find(block_hash_[b]);
+      if (f != by_hash_.end() && f->second == b) by_hash_.erase(f);
+      block_hash_[b] = 0;
+    }
+  }
   if (static_cast<int>(hashes.size()) > full) hashes.resize(full);
 }
 

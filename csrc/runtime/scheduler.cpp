@@ -78,6 +78,7 @@ StepMeta Scheduler::schedule() {
   if (arena_.base == nullptr) throw std::runtime_error("Scheduler: arena not set");
   StepMeta m;
   const int bs = bm_.block_size();
+  const int ql = cfg_.spec_len > 0 ? cfg_.spec_len + 1 : 1;
   int budget = std::min(cfg_.max_num_batched_tokens, arena_.max_tokens);
   last_sampling_.clear();
   last_scheduled_.clear();
@@ -96,8 +97,8 @@ StepMeta Scheduler::schedule() {
     if (s->status != SeqStatus::Running) continue;  // preempted earlier in this loop
     const int need = static_cast<int>(s->tokens.size()) - s->num_computed;
     if (need != 1) continue;
-    if (budget <= 0 || static_cast<int>(decodes.size()) >= arena_.max_seqs) break;
-    bool ok = bm_.ensure_capacity(s->table, s->num_computed + 1);
+    if (budget < ql || static_cast<int>(decodes.size()) >= arena_.max_seqs) break;
+    bool ok = bm_.ensure_capacity(s->table, s->num_computed + ql);
     while (!ok) {
       // preempt the most recently admitted running sequence not yet scheduled
       Sequence* victim = nullptr;
@@ -109,7 +110,7 @@ StepMeta Scheduler::schedule() {
       if (victim == nullptr) break;
       preempt(victim);
       ++m.num_preempted;
-      ok = bm_.ensure_capacity(s->table, s->num_computed + 1);
+      ok = bm_.ensure_capacity(s->table, s->num_computed + ql);
     }
     if (!ok) {
       preempt(s);
@@ -117,7 +118,7 @@ StepMeta Scheduler::schedule() {
       continue;
     }
     decodes.push_back(s);
-    budget -= 1;
+    budget -= ql;
   }
 
   // 2) partially prefilled running sequences (chunked prefill continues)
@@ -158,7 +159,7 @@ StepMeta Scheduler::schedule() {
     s->status = SeqStatus::Running;
     s->admitted_once = true;
     running_.push_back(s);
-    if (len == 1 && need == 1) {
+    if (len == 1 && need == 1 && ql == 1) {
       decodes.push_back(s);
     } else {
       prefills.push_back({s, s->num_computed, len});
@@ -173,7 +174,7 @@ StepMeta Scheduler::schedule() {
   for (auto& p : prefills) T_pref += p.len;
   int ntiles = 0;
   for (auto& p : prefills) ntiles += (p.len + 63) / 64;
-  int nl_real = Bd;
+  int nl_real = Bd * ql;
   for (auto& p : prefills)
     if (p.start + p.len == static_cast<int>(p.s->tokens.size())) ++nl_real;
   if (prefills.empty() && Bd > 0) {
@@ -183,11 +184,11 @@ StepMeta Scheduler::schedule() {
         break;
       }
   }
-  const int T = Bd + T_pref;
-  const int NL = nl_real + (Bd - real_decode);
+  const int T = Bd * ql + T_pref;
+  const int NL = nl_real + (Bd - real_decode) * ql;
   const int mb = arena_.max_blocks;
   m = [&] {
-    StepMeta lay = arena_layout(T, Bd, static_cast<int>(prefills.size()), ntiles, NL, mb);
+    StepMeta lay = arena_layout(T, Bd, static_cast<int>(prefills.size()), ntiles, NL, mb, ql);
     lay.num_preempted = m.num_preempted;
     return lay;
   }();
@@ -209,19 +210,27 @@ StepMeta Scheduler::schedule() {
   float* topp = reinterpret_cast<float*>(A + m.off_top_p);
   int64_t* seeds = reinterpret_cast<int64_t*>(A + m.off_seeds);
   int64_t* offs = reinterpret_cast<int64_t*>(A + m.off_offsets);
+  int32_t* drafts = A + m.off_draft_ids;
+  row_draft_.clear();
+  row_group_.clear();
 
   int t = 0;
   int nsample = 0;
   m.all_greedy = true;
-  auto add_sample = [&](Sequence* s, int row) {
+  auto add_sample = [&](Sequence* s, int row, int32_t draft, int group, int extra_offset) {
     lrows[nsample] = row;
     temp[nsample] = s ? s->sp.temperature : 0.f;
     topp[nsample] = s ? s->sp.top_p : 1.f;
     topk[nsample] = s ? s->sp.top_k : 0;
     seeds[nsample] = s ? s->sp.seed : 0;
-    offs[nsample] = s ? s->num_generated() : 0;
+    offs[nsample] = s ? s->num_generated() + extra_offset : 0;
+    drafts[nsample] = draft;
     if (s && s->sp.temperature > 0.f) m.all_greedy = false;
-    if (s) last_sampling_.push_back(s);
+    if (s) {
+      last_sampling_.push_back(s);
+      row_draft_.push_back(draft);
+      row_group_.push_back(group);
+    }
     ++nsample;
   };
   for (int i = 0; i < Bd; ++i) {
@@ -229,24 +238,32 @@ StepMeta Scheduler::schedule() {
     if (i < real_decode) {
       Sequence* s = decodes[i];
       const int pos = s->num_computed;
-      input_ids[t] = s->tokens[pos];
-      positions[t] = pos;
-      slots[t] = s->table[pos / bs] * bs + pos % bs;
       const int nb = static_cast<int>(s->table.size());
       if (nb > mb) throw std::runtime_error("Scheduler: block table wider than the arena");
       std::copy(s->table.begin(), s->table.end(), row_bt);
-      dsl[i] = pos + 1;
-      m.max_decode_blocks = std::max(m.max_decode_blocks, (pos + bs) / bs);
-      add_sample(s, t);
-    } else {  // padding row: reads one page of block 0, writes no KV, result ignored
-      input_ids[t] = 0;
-      positions[t] = 0;
-      slots[t] = -1;
+      dsl[i] = pos + ql;
+      m.max_decode_blocks = std::max(m.max_decode_blocks, (pos + ql + bs - 1) / bs);
+      const int nd = std::min<int>(static_cast<int>(s->draft.size()), ql - 1);
+      for (int j = 0; j < ql; ++j) {
+        const int p = pos + j;
+        input_ids[t] = j == 0 ? s->tokens[pos] : (j - 1 < nd ? s->draft[j - 1] : 0);
+        positions[t] = p;
+        slots[t] = s->table[p / bs] * bs + p % bs;
+        add_sample(s, t, j < nd ? s->draft[j] : -1, ql, j);
+        ++t;
+      }
+      s->verifying = ql > 1;
+    } else {  // padding rows: read one page of block 0, write no KV, results ignored
+      for (int j = 0; j < ql; ++j) {
+        input_ids[t] = 0;
+        positions[t] = j;
+        slots[t] = -1;
+        add_sample(nullptr, t, -1, ql, 0);
+        ++t;
+      }
       row_bt[0] = 0;
-      dsl[i] = 1;
-      add_sample(nullptr, t);
+      dsl[i] = ql;
     }
-    ++t;
   }
   pcu[0] = 0;
   struct TileOrder {
@@ -271,7 +288,7 @@ StepMeta Scheduler::schedule() {
     pcu[j + 1] = pcu[j] + p.len;
     for (int r = 0; r < p.len; r += 64) tiles.push_back({static_cast<int>(j), r, p.start + std::min(r + 64, p.len)});
     s->num_computed = p.start + p.len;
-    if (s->num_computed == static_cast<int>(s->tokens.size())) add_sample(s, t - 1);
+    if (s->num_computed == static_cast<int>(s->tokens.size())) add_sample(s, t - 1, -1, 1, 0);
   }
   // heavy tiles (long kv extent) first for load balance
   std::stable_sort(tiles.begin(), tiles.end(), [](const TileOrder& a, const TileOrder& b) { return a.extent > b.extent; });
@@ -279,15 +296,16 @@ StepMeta Scheduler::schedule() {
     tseq[i] = tiles[i].seq;
     tstart[i] = tiles[i].start;
   }
-  for (Sequence* s : decodes) s->num_computed += 1;
+  for (Sequence* s : decodes) s->num_computed += ql;  // provisional for verify rows: update() rolls back
   for (Sequence* s : decodes) last_scheduled_.push_back(s);
   for (auto& p : prefills) last_scheduled_.push_back(p.s);
   m.num_real_decode = real_decode;
   m.num_real_logits = static_cast<int>(last_sampling_.size());
+  m.decode_q_len = ql;
   return m;
 }
 
-StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB) {
+StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB, int q_len) {
   StepMeta m;
   int64_t off = 0;
   auto take = [&](int64_t words) {
@@ -311,6 +329,7 @@ StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB) {
   m.off_top_k = take(NL);
   m.off_temperature = take(NL);
   m.off_top_p = take(NL);
+  m.off_draft_ids = take(NL);
   align2();
   m.off_seeds = take(2 * int64_t(NL));
   m.off_offsets = take(2 * int64_t(NL));
@@ -321,7 +340,19 @@ StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB) {
   m.num_prefill = Sp;
   m.num_tiles = NT;
   m.num_logits = NL;
+  m.decode_q_len = q_len;
   return m;
+}
+
+FinishReason Scheduler::stop_reason(const Sequence& s, int32_t tok) const {
+  const bool length =
+      s.num_generated() >= s.sp.max_tokens || static_cast<int>(s.tokens.size()) >= cfg_.max_model_len;
+  bool eos = false;
+  if (!s.sp.ignore_eos)
+    for (int32_t e : cfg_.eos_token_ids) eos |= (tok == e);
+  for (int32_t e : s.sp.stop_token_ids) eos |= (tok == e);
+  return (eos && s.num_generated() >= s.sp.min_tokens) ? FinishReason::Stop
+                                                      : (length ? FinishReason::Length : FinishReason::Stop);
 }
 
 std::vector<Event> Scheduler::update(const int32_t* sampled, int n) {
@@ -329,30 +360,71 @@ std::vector<Event> Scheduler::update(const int32_t* sampled, int n) {
   if (n < static_cast<int>(last_sampling_.size()))
     throw std::invalid_argument("Scheduler::update: fewer sampled tokens than sampling rows");
   n = static_cast<int>(last_sampling_.size());
-  for (Sequence* s : last_scheduled_) bm_.commit_full_blocks(s->tokens, s->num_computed, s->table, s->hashes);
-  for (int i = 0; i < n; ++i) {
+  for (Sequence* s : last_scheduled_)
+    if (!s->verifying) bm_.commit_full_blocks(s->tokens, s->num_computed, s->table, s->hashes);
+  int i = 0;
+  while (i < n) {
     Sequence* s = last_sampling_[i];
-    if (s->status != SeqStatus::Running) continue;  // aborted meanwhile
-    const int32_t tok = sampled[i];
-    s->tokens.push_back(tok);
-    const bool stop = is_stop(*s, tok);
+    const int g = s->verifying ? row_group_[i] : 1;
+    if (s->status != SeqStatus::Running) {  // aborted meanwhile
+      i += g;
+      continue;
+    }
+    if (!s->verifying) {
+      const int32_t tok = sampled[i];
+      s->tokens.push_back(tok);
+      const bool stop = is_stop(*s, tok);
+      FinishReason r = FinishReason::None;
+      if (stop) {
+        r = stop_reason(*s, tok);
+        running_.erase(std::remove(running_.begin(), running_.end(), s), running_.end());
+        finish(s, r);
+      }
+      ev.push_back({s->id, tok, stop, static_cast<int>(r)});
+      ++i;
+      continue;
+    }
+    // Verify group: rows i .. i+g-1 sampled positions pos .. pos+g-1.  Row j
+    // agrees with its proposal => proposal j accepted; the first row that
+    // disagrees (or the bonus row) supplies the one new token.  For greedy
+    // rows the sample is the argmax; for stochastic rows the sampler already
+    // did the accept / residual draw, so equality is the acceptance test.
+    const int pos = s->num_computed - g;
+    int acc = 0;
+    while (acc < g - 1 && sampled[i + acc] == row_draft_[i + acc]) ++acc;
+    bool stopped = false;
     FinishReason r = FinishReason::None;
-    if (stop) {
-      const bool length = s->num_generated() >= s->sp.max_tokens ||
-                          static_cast<int>(s->tokens.size()) >= cfg_.max_model_len;
-      bool eos = false;
-      if (!s->sp.ignore_eos)
-        for (int32_t e : cfg_.eos_token_ids) eos |= (tok == e);
-      for (int32_t e : s->sp.stop_token_ids) eos |= (tok == e);
-      r = (eos && s->num_generated() >= s->sp.min_tokens) ? FinishReason::Stop
-                                                          : (length ? FinishReason::Length : FinishReason::Stop);
+    for (int j = 0; j <= acc; ++j) {
+      const int32_t tok = sampled[i + j];
+      s->tokens.push_back(tok);
+      const bool stop = is_stop(*s, tok);
+      if (stop) r = stop_reason(*s, tok);
+      ev.push_back({s->id, tok, stop, static_cast<int>(r)});
+      if (stop) {
+        stopped = true;
+        break;
+      }
+    }
+    s->num_computed = std::min<int>(pos + 1 + acc, static_cast<int>(s->tokens.size()));
+    ++spec_steps_;
+    spec_proposed_ += s->draft.empty() ? 0 : std::min<int>(static_cast<int>(s->draft.size()), g - 1);
+    spec_accepted_ += acc;
+    s->verifying = false;
+    s->draft.clear();
+    bm_.commit_full_blocks(s->tokens, s->num_computed, s->table, s->hashes);
+    if (stopped) {
       running_.erase(std::remove(running_.begin(), running_.end(), s), running_.end());
       finish(s, r);
+    } else {
+      bm_.truncate(s->table, s->hashes, static_cast<int>(s->tokens.size()));  // blocks of rejected rows
     }
-    ev.push_back({s->id, tok, stop, static_cast<int>(r)});
+    i += g;
   }
+  for (Sequence* s : last_scheduled_) s->verifying = false;
   last_sampling_.clear();
   last_scheduled_.clear();
+  row_draft_.clear();
+  row_group_.clear();
   // drop finished sequences
   for (auto it = seqs_.begin(); it != seqs_.end();) {
     if (it->second->status == SeqStatus::Finished)
@@ -361,6 +433,69 @@ std::vector<Event> Scheduler::update(const int32_t* sampled, int n) {
       ++it;
   }
   return ev;
+}
+
+// ---------------------------------------------------------------- speculation
+std::vector<int64_t> Scheduler::decode_candidates() const {
+  std::vector<int64_t> v;
+  for (const Sequence* s : running_)
+    if (static_cast<int>(s->tokens.size()) - s->num_computed == 1) v.push_back(s->id);
+  return v;
+}
+
+bool Scheduler::set_draft(int64_t id, const std::vector<int32_t>& draft) {
+  auto it = seqs_.find(id);
+  if (it == seqs_.end() || it->second->status == SeqStatus::Finished) return false;
+  Sequence* s = it->second.get();
+  s->draft.assign(draft.begin(), draft.begin() + std::min<size_t>(draft.size(), std::max(cfg_.spec_len, 0)));
+  return true;
+}
+
+int Scheduler::propose_ngram(int max_order, int min_order) {
+  int n = 0;
+  for (Sequence* s : running_) {
+    if (static_cast<int>(s->tokens.size()) - s->num_computed != 1) continue;
+    s->draft = ngram_propose(s->tokens, cfg_.spec_len, max_order, min_order);
+    n += !s->draft.empty();
+  }
+  return n;
+}
+
+bool Scheduler::set_tail(int64_t id, int keep_len, const std::vector<int32_t>& tail) {
+  auto it = seqs_.find(id);
+  if (it == seqs_.end() || it->second->status == SeqStatus::Finished) return false;
+  Sequence* s = it->second.get();
+  if (keep_len < s->num_prompt || keep_len > static_cast<int>(s->tokens.size())) return false;
+  if (keep_len + static_cast<int>(tail.size()) >= cfg_.max_model_len) return false;
+  s->tokens.resize(keep_len);
+  s->tokens.insert(s->tokens.end(), tail.begin(), tail.end());
+  if (s->num_computed > keep_len) s->num_computed = keep_len;
+  if (s->status == SeqStatus::Running) bm_.truncate(s->table, s->hashes, s->num_computed);
+  s->draft.clear();
+  return true;
+}
+
+std::vector<int32_t> ngram_propose(const std::vector<int32_t>& tokens, int k, int max_order, int min_order) {
+  std::vector<int32_t> out;
+  const int n = static_cast<int>(tokens.size());
+  if (k <= 0) return out;
+  min_order = std::max(1, min_order);
+  for (int order = std::min(max_order, n - 1); order >= min_order; --order) {
+    const int32_t* suf = tokens.data() + n - order;
+    // most recent earlier occurrence whose continuation exists
+    for (int start = n - order - 1; start >= 0; --start) {
+      if (tokens[start] != suf[0]) continue;
+      bool eq = true;
+      for (int j = 1; j < order && eq; ++j) eq = tokens[start + j] == suf[j];
+      if (!eq) continue;
+      // the continuation runs on into the proposal itself, so a repeating
+      // span proposes its period again (from + j - n < j always)
+      const int from = start + order;
+      for (int j = 0; j < k; ++j) out.push_back(from + j < n ? tokens[from + j] : out[from + j - n]);
+      return out;
+    }
+  }
+  return out;
 }
 
 }  // namespace rt

@@ -56,8 +56,10 @@ struct Sequence {
   FinishReason finish = FinishReason::None;
   int priority = 0;
   int64_t order = 0;
+  std::vector<int32_t> draft;  // speculative proposals for the next verify step
   int num_preemptions = 0;
   bool admitted_once = false;
+  bool verifying = false;  // scheduled as a verify group in the current step
   int num_generated() const { return static_cast<int>(tokens.size()) - num_prompt; }
 };
 
@@ -67,6 +69,10 @@ struct SchedulerConfig {
   int max_model_len = 4096;
   bool chunked_prefill = true;
   std::vector<int32_t> eos_token_ids;
+  // Speculative decoding: every decode row becomes a verify row of
+  // spec_len + 1 tokens (the last sampled token followed by spec_len
+  // proposals; missing proposals are padded and always rejected).  0 = off.
+  int spec_len = 0;
 };
 
 // The scheduler writes each step's metadata into ONE pinned int32 arena in a
@@ -79,7 +85,11 @@ struct SchedulerConfig {
 //   prefill_ctx_lens[Sp] prefill_cu_q[Sp + 1] prefill_block_table[Sp * MB]
 //   tile_seq[NT] tile_start[NT]
 //   logits_rows[NL] top_k[NL] temperature[NL] (f32) top_p[NL] (f32)
-//   seeds[NL] (int64, aligned) offsets[NL] (int64)
+//   draft_ids[NL] seeds[NL] (int64, aligned) offsets[NL] (int64)
+// With speculation on, the decode region holds Bd * q_len token rows
+// (q_len = spec_len + 1 consecutive positions per sequence) and every one of
+// them is a sampling row; draft_ids[row] is the proposal that row's sample is
+// checked against (-1: none, i.e. the bonus row or a padded proposal).
 struct Arena {
   int32_t* base = nullptr;
   int64_t capacity = 0;    // words
@@ -91,6 +101,7 @@ struct Arena {
 struct StepMeta {
   int num_tokens = 0;   // T (including decode padding)
   int num_decode = 0;   // Bd (including padding)
+  int decode_q_len = 1; // token rows per decode sequence (spec_len + 1 when speculating)
   int num_real_decode = 0;
   int num_prefill = 0;  // Sp
   int num_tiles = 0;    // NT
@@ -104,12 +115,19 @@ struct StepMeta {
   int64_t off_decode_seq_lens = 0, off_decode_block_table = 0;
   int64_t off_prefill_ctx_lens = 0, off_prefill_cu_q = 0, off_prefill_block_table = 0;
   int64_t off_tile_seq = 0, off_tile_start = 0;
-  int64_t off_logits_rows = 0, off_top_k = 0, off_temperature = 0, off_top_p = 0, off_seeds = 0, off_offsets = 0;
+  int64_t off_logits_rows = 0, off_top_k = 0, off_temperature = 0, off_top_p = 0, off_draft_ids = 0, off_seeds = 0,
+          off_offsets = 0;
   int64_t used_words = 0;
 };
 
 // Packed layout for the given row counts (shared by the scheduler and the runner).
-StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB);
+StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB, int q_len = 1);
+
+// Prompt-lookup (n-gram) proposal: the longest suffix of `tokens` of length
+// max_order down to min_order that also occurs earlier; returns the k tokens
+// that followed its most recent earlier occurrence, continuing periodically
+// past the end of the sequence (empty if no suffix recurs).
+std::vector<int32_t> ngram_propose(const std::vector<int32_t>& tokens, int k, int max_order, int min_order);
 
 struct Event {
   int64_t seq_id;
@@ -134,10 +152,27 @@ class Scheduler {
   StepMeta schedule();
   std::vector<Event> update(const int32_t* sampled, int n);
 
+  // ---- speculative decoding
+  // Running sequences whose next step is a decode (verify) row, in running order.
+  std::vector<int64_t> decode_candidates() const;
+  // Proposals for the next step (at most spec_len are used); false if unknown.
+  bool set_draft(int64_t id, const std::vector<int32_t>& draft);
+  // n-gram proposals for every decode candidate; returns how many got one.
+  int propose_ngram(int max_order, int min_order);
+  // Replace the token tail: keep the first keep_len tokens, append tail.  KV
+  // beyond keep_len is dropped (num_computed clamps).  Used to re-synchronise
+  // a draft model's mirror sequence with the target after verification.
+  // Blocks this sequence shares with others may not be cut into.
+  bool set_tail(int64_t id, int keep_len, const std::vector<int32_t>& tail);
+
   BlockManager& blocks() { return bm_; }
   const Sequence* find(int64_t id) const;
   const SchedulerConfig& config() const { return cfg_; }
   int64_t total_preemptions() const { return total_preemptions_; }
+  // speculation counters: verify groups, proposals offered, proposals accepted
+  int64_t spec_steps() const { return spec_steps_; }
+  int64_t spec_proposed() const { return spec_proposed_; }
+  int64_t spec_accepted() const { return spec_accepted_; }
   // Sequence ids of the sampling rows of the last scheduled step, in row order.
   std::vector<int64_t> sampling_ids() const {
     std::vector<int64_t> v;
@@ -149,6 +184,7 @@ class Scheduler {
  private:
   void preempt(Sequence* s);
   bool is_stop(const Sequence& s, int32_t tok) const;
+  FinishReason stop_reason(const Sequence& s, int32_t tok) const;
   void finish(Sequence* s, FinishReason r);
 
   SchedulerConfig cfg_;
@@ -159,10 +195,13 @@ class Scheduler {
   std::deque<Sequence*> waiting_;
   std::vector<Sequence*> running_;
   std::vector<Sequence*> last_sampling_;
+  std::vector<int32_t> row_draft_;  // per sampling row: proposal to check (-1 none)
+  std::vector<int32_t> row_group_;  // per sampling row: rows in its verify group (1 for plain rows)
   std::vector<Sequence*> last_scheduled_;
   int64_t next_id_ = 1;
   int64_t next_order_ = 0;
   int64_t total_preemptions_ = 0;
+  int64_t spec_steps_ = 0, spec_proposed_ = 0, spec_accepted_ = 0;
 };
 
 }  // namespace rt

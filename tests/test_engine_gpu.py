@@ -132,3 +132,95 @@ def test_moe_routing_kernels_match_reference():
         exp = moe_mlp(cfg, w, "model.layers.0.", x.float())
         err = ((got.float() - exp).norm() / exp.norm()).item()
         assert err < 2e-2, (T, err)
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_ngram_speculation_greedy(graphs):
+    """n-gram proposals verified in the batched step: greedy outputs still
+    follow the oracle, and a repetitive prompt gets proposals accepted."""
+    from bloom_b200.engine.engine import EngineConfig, LLMEngine, SamplingParams
+    from bloom_b200.engine.speculative import NgramSpeculator
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.llama import DecoderLM
+    from bloom_b200.models.reference import random_weights
+
+    cfg = preset("tiny-llama")
+    w = random_weights(cfg, seed=3, std=0.08, device="cuda")
+    model = DecoderLM(cfg, device="cuda")
+    model.shard_full(w)
+    eng = LLMEngine(model, EngineConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=512,
+                                        num_blocks=256, use_cuda_graphs=graphs, spec_len=4))
+    eng.attach_speculator(NgramSpeculator(4, 3))
+    torch.manual_seed(5)
+    period = torch.randint(3, cfg.vocab_size, (7,)).tolist()
+    prompts = [period * 6, torch.randint(3, cfg.vocab_size, (23,)).tolist(), [9]]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=20, temperature=0.0, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        assert len(o.token_ids) == 20
+        _check_greedy(cfg, w, p, o.token_ids)
+    st = eng.speculator.stats(eng)
+    assert st["verify_groups"] > 0 and st["proposed"] > 0
+    from bloom_b200 import ops
+
+    assert int(ops.status()[0].item()) == 0
+    if graphs:
+        assert eng.runner.stats["graph_steps"] > 0
+
+
+def test_draft_model_speculation_same_weights():
+    """A draft identical to the target proposes what the target would emit:
+    nearly every proposal is accepted and the outputs follow the oracle."""
+    from bloom_b200.engine.engine import EngineConfig, LLMEngine, SamplingParams
+    from bloom_b200.engine.speculative import DraftModelSpeculator
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.llama import DecoderLM
+    from bloom_b200.models.reference import random_weights
+
+    cfg = preset("tiny-llama")
+    w = random_weights(cfg, seed=3, std=0.08, device="cuda")
+
+    def engine(spec_len, mlen, prefix):
+        m = DecoderLM(cfg, device="cuda")
+        m.shard_full(w)
+        return LLMEngine(m, EngineConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=mlen,
+                                         num_blocks=256, use_cuda_graphs=True, spec_len=spec_len,
+                                         enable_prefix_caching=prefix))
+
+    eng = engine(3, 512, True)
+    draft = engine(0, 520, False)
+    eng.attach_speculator(DraftModelSpeculator(draft, 3))
+    torch.manual_seed(6)
+    prompts = [torch.randint(3, cfg.vocab_size, (n,)).tolist() for n in (4, 30, 77)]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=24, temperature=0.0, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        assert len(o.token_ids) == 24
+        _check_greedy(cfg, w, p, o.token_ids)
+    st = eng.speculator.stats(eng)
+    assert st["acceptance_rate"] > 0.8, st
+    assert st["tokens_per_verify"] > 3.0, st
+
+
+def test_speculation_sampled_runs():
+    """Stochastic sampling with proposals: valid tokens, reproducible per seed."""
+    from bloom_b200.engine.engine import SamplingParams
+    from bloom_b200.engine.speculative import NgramSpeculator
+
+    outs = []
+    for _ in range(2):
+        from bloom_b200.engine.engine import EngineConfig, LLMEngine
+        from bloom_b200.models.config import preset
+        from bloom_b200.models.llama import DecoderLM
+        from bloom_b200.models.reference import random_weights
+
+        cfg = preset("tiny-llama")
+        w = random_weights(cfg, seed=3, std=0.08, device="cuda")
+        m = DecoderLM(cfg, device="cuda")
+        m.shard_full(w)
+        eng = LLMEngine(m, EngineConfig(max_num_seqs=4, max_num_batched_tokens=256, max_model_len=512,
+                                        num_blocks=128, use_cuda_graphs=False, spec_len=3))
+        eng.attach_speculator(NgramSpeculator(3, 2))
+        o = eng.generate([[5, 6, 7] * 5], SamplingParams(max_tokens=16, temperature=0.8, top_p=0.95, seed=11,
+                                                          ignore_eos=True))
+        assert len(o[0].token_ids) == 16 and all(0 <= t < cfg.vocab_size for t in o[0].token_ids)
+        outs.append(o[0].token_ids)
+    assert outs[0] == outs[1]

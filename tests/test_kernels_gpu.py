@@ -149,7 +149,8 @@ def test_rope_kv_write(qk_norm):
     assert cache[0].abs().sum().item() == 0  # other layer untouched
 
 
-@pytest.mark.parametrize("nq,nkv,q_len", [(32, 8, 1), (8, 8, 1), (16, 2, 1), (32, 8, 4), (8, 1, 4)])
+@pytest.mark.parametrize("nq,nkv,q_len", [(32, 8, 1), (8, 8, 1), (16, 2, 1), (32, 8, 4), (8, 1, 4), (8, 1, 5),
+                                          (32, 8, 5), (64, 8, 3)])
 @pytest.mark.parametrize("splits", [1, 3])
 def test_paged_decode_attention(nq, nkv, q_len, splits):
     ops, ref = _ops(), _ref()
@@ -233,6 +234,35 @@ def test_argmax_and_sampling():
     assert logits[4, int(s[4])].float().item() >= third  # ties with the 3rd value are kept too
     s2 = ops.sample(logits, temp, top_p, top_k, seeds, offs)
     assert torch.equal(s, s2)  # reproducible stream
+
+
+def test_verify_sampling_is_exact():
+    """Rejection sampling against a fixed proposal keeps the target
+    distribution: accept d with p(d), else sample p with d removed."""
+    ops = _ops()
+    V = 48
+    probs = torch.softmax(torch.randn(V, device="cuda") * 1.5, 0)
+    d = int(probs.argsort()[-3])  # a proposal of middling probability
+    n = 40000
+    logits = probs.log().unsqueeze(0).repeat(n, 1).contiguous()
+    draft = torch.full((n,), d, dtype=torch.int32, device="cuda")
+    s = ops.sample(logits, torch.ones(n, device="cuda"), torch.ones(n, device="cuda"),
+                   torch.zeros(n, device="cuda", dtype=torch.int32), torch.arange(n, device="cuda"),
+                   torch.zeros(n, device="cuda", dtype=torch.int64), draft)
+    freq = torch.bincount(s.long(), minlength=V).float() / n
+    assert abs(freq[d].item() - probs[d].item()) < 0.015
+    assert (freq - probs).abs().max().item() < 0.015
+    # greedy rows ignore the proposal and return the argmax
+    t0 = torch.zeros(n, device="cuda")
+    g = ops.sample(logits[:8], t0[:8], torch.ones(8, device="cuda"), torch.zeros(8, device="cuda", dtype=torch.int32),
+                   torch.arange(8, device="cuda"), torch.zeros(8, device="cuda", dtype=torch.int64), draft[:8])
+    assert (g.long() == probs.argmax()).all()
+    # no proposal (-1) samples as usual; top-p excluding the proposal rejects it surely
+    tp = torch.full((n,), 0.3, device="cuda")
+    dlow = torch.full((n,), int(probs.argmin()), dtype=torch.int32, device="cuda")
+    s3 = ops.sample(logits, torch.ones(n, device="cuda"), tp, torch.zeros(n, device="cuda", dtype=torch.int32),
+                    torch.arange(n, device="cuda"), torch.zeros(n, device="cuda", dtype=torch.int64), dlow)
+    assert not (s3 == dlow).any()
 
 
 def test_sampling_distribution():

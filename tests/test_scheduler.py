@@ -26,7 +26,7 @@ def make(rt, num_blocks=64, max_seqs=8, budget=64, max_len=512, prefix=True, chu
     s = rt.Scheduler(cfg, num_blocks, 16, prefix)
     mb = (max_len + 15) // 16
     worst = rt.arena_layout(max(budget, max_seqs), max_seqs, max_seqs, max(budget, max_seqs) // 64 + max_seqs,
-                            max_seqs, mb)
+                            max(budget, max_seqs) + max_seqs, mb)
     arena = torch.zeros(worst.used_words, dtype=torch.int32)
     s.set_arena(arena, max(budget, max_seqs), max_seqs, mb)
     if buckets:
