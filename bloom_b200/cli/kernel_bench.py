@@ -32,12 +32,19 @@ def load_peaks():
 
 
 ITERS = [20]
+PROFILE = [False]
 
 
 def timeit(fn, iters=None, warmup=5):
     """Device time per call: `iters` calls (rotating operands) are captured in
     a CUDA graph and replayed, so host launch cost never shows up in the
-    CUDA-event interval; median over 5 replays."""
+    CUDA-event interval; median over 5 replays.  In profile mode (--ncu) the
+    op is only launched three times, eagerly, for a profiler to capture."""
+    if PROFILE[0]:
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        return float("nan")
     iters = iters or ITERS[0]
     for _ in range(warmup):
         fn()
@@ -71,8 +78,11 @@ def main():
     ap.add_argument("--M", type=int, default=0, help="only this token count for GEMMs")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--autotune", action="store_true", help="pick token tile / split-K by measurement first")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profile mode: launch each selected kernel 3 times eagerly, no timing, no cuBLAS runs")
     args = ap.parse_args()
     ITERS[0] = args.iters
+    PROFILE[0] = args.ncu
     from bloom_b200 import ops
 
     hbm, tfl, src = load_peaks()
@@ -117,15 +127,16 @@ def main():
             tuned = ops.GEMM_TUNED.get((ops._m_bucket(M), N, K, epi == ops.EPI_SWIGLU)) if M <= 512 else None
             if tuned:
                 extra["bn_splits"] = list(tuned)
-            if M <= 512 and name in ("o_proj", "down"):
+            if M <= 512 and name in ("o_proj", "down") and not args.ncu:
                 sp = ops.gemm_default_splits(M, N, K, 0)
                 if sp > 1:
                     part = torch.empty(sp, M, N, device=dev, dtype=torch.float32)
                     ms_sk = timeit(lambda i=0: ops.gemm(x, ws[i % nrot], part, epi=ops.EPI_PARTIAL_F32, splits=sp))
                     extra["splitk"] = sp
                     extra["splitk_ms"] = round(ms_sk, 4)
-            cms = timeit(lambda i=0: torch.matmul(x, ws[i % nrot].t()))
-            extra["cublas_ms"] = round(cms, 4)
+            if not args.ncu:
+                cms = timeit(lambda i=0: torch.matmul(x, ws[i % nrot].t()))
+                extra["cublas_ms"] = round(cms, 4)
             report(f"gemm_{name}", ms, flops, byt, extra)
             del ws
 
@@ -157,7 +168,7 @@ def main():
         ms = timeit(lambda i=0: ops.paged_decode_attention(q, cache, i % L, bt, sl, o, splits=splits, workspace=ws,
                                                            scale=hd ** -0.5))
         report("paged_decode_attention", ms, None, kv_bytes, {"B": B, "avg_ctx": sum(lens) / B, "splits": splits})
-        for Bs in (1, 8, 32):
+        for Bs in (() if args.ncu else (1, 8, 32)):
             sl2 = sl[:Bs].contiguous()
             sp = ops.decode_attention_splits(Bs, nkv, MB, 0)
             ws2 = torch.empty(ops.decode_workspace_numel(Bs, nkv, sp), device=dev)
@@ -202,6 +213,50 @@ def main():
         logits = torch.randn(256, V // t, device=dev, dtype=torch.bfloat16)
         ms = timeit(lambda i=0: ops.argmax(logits))
         report("argmax", ms, None, logits.numel() * 2, {"B": 256})
+
+    if not args.only or "sample" in args.only:
+        # stochastic verify sampling: 64 sequences x (4 proposals + bonus) rows, temperature 0.8, top-p 0.9
+        R = 320
+        logits = torch.randn(R, V // t, device=dev, dtype=torch.bfloat16) * 3
+        temp = torch.full((R,), 0.8, device=dev)
+        topp = torch.full((R,), 0.9, device=dev)
+        topk = torch.zeros(R, dtype=torch.int32, device=dev)
+        seeds = torch.arange(R, dtype=torch.int64, device=dev)
+        offs = torch.zeros(R, dtype=torch.int64, device=dev)
+        draft = torch.randint(0, V // t, (R,), dtype=torch.int32, device=dev)
+        ms = timeit(lambda i=0: ops.sample(logits, temp, topp, topk, seeds, offs, draft))
+        report("verify_sample", ms, None, logits.numel() * 2, {"rows": R})
+
+    if not args.only or "moe" in args.only:
+        # Qwen3-30B-A3B expert FFN at EP=8: 16 local experts, 128 tokens x top-8, H 2048, I 768
+        from bloom_b200.models.config import preset
+        from bloom_b200.models.llama import DecoderLM, TPInfo
+        from bloom_b200.models.qwen3_moe import MoEBlock
+
+        cfg = preset("qwen3-moe-30b-a3b")
+        cfg.num_layers = 1
+
+        class _Shell:  # the MoE block only needs cfg / tp / device from its model
+            pass
+
+        sh = _Shell()
+        sh.cfg, sh.device = cfg, dev
+        sh.tp = TPInfo(rank=0, size=8)
+        E, Hm, Im = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
+        full = {"model.layers.0.mlp.gate.weight": torch.randn(E, Hm, device=dev, dtype=torch.bfloat16) * 0.02,
+                "model.layers.0.mlp.experts.gate_proj": torch.randn(E, Im, Hm, device=dev, dtype=torch.bfloat16) * 0.02,
+                "model.layers.0.mlp.experts.up_proj": torch.randn(E, Im, Hm, device=dev, dtype=torch.bfloat16) * 0.02,
+                "model.layers.0.mlp.experts.down_proj": torch.randn(E, Hm, Im, device=dev, dtype=torch.bfloat16) * 0.02}
+        blk = MoEBlock(sh, full)
+        del full
+        for Tm in (128, 4096):
+            x = torch.randn(Tm, Hm, device=dev, dtype=torch.bfloat16)
+            out = torch.empty_like(x)
+            ms = timeit(lambda i=0: blk.forward(0, x, out))
+            El = E // 8
+            wbytes = El * 3 * Im * Hm * 2
+            flops = 2.0 * Tm * cfg.num_experts_per_tok / 8 * 3 * Im * Hm
+            report("moe_layer_ep8", ms, flops, wbytes, {"tokens": Tm, "local_experts": El})
 
     if args.json:
         with open(args.json, "w") as f:

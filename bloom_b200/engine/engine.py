@@ -230,9 +230,11 @@ class LLMEngine:
             return
         logits = self.runner.last_logits
         idx = torch.tensor([i for i, _ in rows], device=logits.device)
-        top = torch.topk(logits.index_select(0, idx).float(), k=min(256, logits.shape[1]), dim=1).indices.cpu()
-        for (row, sid), cand in zip(rows, top.tolist()):
-            sampled[row] = self.constraints[sid].choose(cand, int(sampled[row]))
+        sel = logits.index_select(0, idx).float()
+        top = torch.topk(sel, k=min(256, logits.shape[1]), dim=1).indices.cpu()
+        for j, ((row, sid), cand) in enumerate(zip(rows, top.tolist())):
+            full = (lambda j=j: torch.argsort(sel[j], descending=True).cpu().tolist())
+            sampled[row] = self.constraints[sid].choose(cand, int(sampled[row]), full)
 
     def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None,
                  on_token: Optional[Callable[[RequestOutput], None]] = None) -> List[RequestOutput]:

@@ -4,7 +4,8 @@ Each constrained request carries a JSON recogniser (C++ `JsonDfa` in
 bloom_b200._runtime).  After the GPU forward of a step, the top-256 logits of
 the constrained rows are read back; the first candidate that keeps the
 output a valid JSON prefix is emitted, end-of-sequence only once the document
-is complete, and if no candidate qualifies the unconstrained token is kept
+is complete; if no top candidate qualifies the whole vocabulary is searched
+in logit order, and end-of-sequence closes the output when nothing fits
 (reference: executor/candle.rs:2584-3243 -- autocomplete_json, JsonDfa,
 filter_logits_by_grammar with top-256 candidates and EOS gating).
 `repair_json` closes an unfinished document (open strings and containers)
@@ -36,9 +37,17 @@ class JsonConstraint:
         self.vocab = vocab
         self.eos = list(eos)
 
-    def choose(self, candidates: List[int], fallback: int) -> int:
+    def choose(self, candidates: List[int], fallback: int, full_order=None) -> int:
+        """First candidate that keeps the document a valid JSON prefix.  When
+        none of the top candidates qualifies, `full_order()` (the whole
+        vocabulary by descending logit) is searched; if still nothing fits,
+        the document is ended with the first end-of-sequence id."""
         t = self.dfa.pick(candidates, self.vocab, self.eos)
-        return fallback if t < 0 else t
+        if t < 0 and full_order is not None:
+            t = self.dfa.pick(full_order(), self.vocab, self.eos)
+        if t < 0:
+            return self.eos[0] if self.eos else fallback
+        return t
 
     def advance(self, token: int) -> None:
         if token in self.eos or not (0 <= token < len(self.vocab)):

@@ -30,6 +30,7 @@ def build_parser():
     ap.add_argument("--num-speculative-tokens", type=int, default=5)
     ap.add_argument("--model-id")
     ap.add_argument("--doctor", action="store_true")
+    ap.add_argument("--doctor-format", choices=["text", "json"], default="text")
     ap.add_argument("--enable-ifb", action="store_true", default=True,
                     help="in-flight batching (always on for the GPU engine)")
     return ap
@@ -40,8 +41,17 @@ def main(argv=None) -> int:
     if args.doctor:
         from ..utils.doctor import doctor_report
 
-        print(json.dumps(doctor_report(args.model), indent=2))
-        return 0
+        keys = list(args.api_key) + [k for k in os.environ.get("BLOOM_API_KEYS", "").split(",") if k]
+        rep = doctor_report(args.model, speculative=args.speculative, draft_model=args.draft_model,
+                            context_size=args.context_size, max_concurrent=args.max_concurrent, host=args.host,
+                            api_keys=keys)
+        if args.doctor_format == "json":
+            print(json.dumps(rep, indent=2))
+        else:
+            from ..utils.doctor import render_text
+
+            print(render_text(rep), end="")
+        return 1 if rep["status"] == "fail" else 0
     if not args.model:
         print("error: --model is required", file=sys.stderr)
         return 2

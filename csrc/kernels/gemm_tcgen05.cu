@@ -24,6 +24,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include "bloom/common.cuh"
 #include "bloom/ops.h"
 #include "bloom/tma_host.h"
@@ -52,6 +54,10 @@ struct Args {
   const int4* tiles;
   const int* num_tiles_dev;
   int rows_per_group;
+  // L2 policy of the weight (A) tiles: 0 evict-first (each weight tile is
+  // read by one token tile: decode), 1 normal (several token tiles re-read it
+  // while it is hot: prefill), 2 evict-last.
+  int wpol;
 };
 
 struct Tile {
@@ -225,7 +231,8 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_w = a.wpol == 0 ? l2_policy_evict_first()
+                                         : (a.wpol == 2 ? l2_policy_evict_last() : l2_policy_evict_normal());
       const uint64_t pol_x = l2_policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
@@ -528,6 +535,14 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.tiles = nullptr;
   a.num_tiles_dev = nullptr;
   a.rows_per_group = 0;
+  a.wpol = a.num_tok_tiles > 1 ? 1 : 0;
+  {
+    static const int env_wpol = [] {
+      const char* e = std::getenv("BLOOM_GEMM_WPOL");
+      return e ? std::atoi(e) : -1;
+    }();
+    if (env_wpol >= 0 && env_wpol <= 2) a.wpol = env_wpol;
+  }
 
   switch (epi) {
     case kEpiBF16:
@@ -631,6 +646,7 @@ void gemm_grouped_out(const torch::Tensor& x, const torch::Tensor& w, torch::Ten
   a.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
   a.num_tiles_dev = num_tiles.data_ptr<int>();
   a.rows_per_group = int(rows_per_group);
+  a.wpol = 0;
   const CUtensorMap tmA = make_tmap_bf16_2d(w.data_ptr(), K, w.size(0), w.stride(0) * 2, gemm::BK, gemm::BM);
   const CUtensorMap tmB = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, int(bn));
   const int grid = num_sms(x.get_device());
