@@ -175,11 +175,13 @@ class InferencePipeline:
         from .engine import EngineConfig, LLMEngine
         from ..models.llama import DecoderLM
 
-        dm = DecoderLM(cfg, tp_info, None)
         if man is None:
+            dm = DecoderLM(cfg, tp_info, None)
             dm.random_init(0)
         else:
-            dm.shard_full(load_weights(man))
+            from ..formats.loader import load_decoder
+
+            dm = load_decoder(model, tp_info, None)
         spec_len = nspec if speculative in ("ngram", "draft") else 0
         llm = LLMEngine(dm, EngineConfig(max_num_seqs=max_num_seqs, max_num_batched_tokens=max(ctx, 2048),
                                          max_model_len=ctx, use_cuda_graphs=use_cuda_graphs, spec_len=spec_len))

@@ -56,8 +56,13 @@ def load_decoder(path: str, tp=None, device=None):
 
     man = load_manifest(path)
     cfg = model_config(man)
-    w = load_weights(man)
     model = DecoderLM(cfg, tp, device)
+    gg = [f for f in man.files if f.format == "Gguf"]
+    if gg and (tp is None or tp.size == 1) and man.primary_dtype in ("Q8", "Q4"):
+        # Q8_0 / Q4_0 projections stay block-quantised on the GPU (qgemv / dequant + tcgen05)
+        model.load_gguf(os.path.join(man.root, gg[0].name), quantized=True)
+        return model
+    w = load_weights(man)
     model.shard_full(w)
     return model
 

@@ -158,6 +158,88 @@ class DecoderLM:
             self.moe = MoEBlock(self, full)
         self._finish()
 
+    def load_gguf(self, path: str, quantized: bool = True) -> None:
+        """Install a GGUF decoder (TP=1).  With `quantized`, the Q8_0 / Q4_0
+        projection weights stay block-quantised in HBM (bit-exact GGUF blocks,
+        rows reordered exactly as the float path: q/k RoPE rows un-permuted,
+        q|k|v concatenated, gate/up interleaved); norms, embeddings and other
+        types are dequantised to bf16."""
+        import numpy as np
+
+        from ..formats.gguf import GGUFFile, gguf_name_to_hf, unpermute_qk
+
+        assert self.tp.size == 1, "quantised GGUF weights are served at TP=1"
+        g = GGUFFile(path)
+        cfg, dev, bf = self.cfg, self.device, torch.bfloat16
+        lin = ("q_proj.weight", "k_proj.weight", "v_proj.weight", "o_proj.weight", "gate_proj.weight",
+               "up_proj.weight", "down_proj.weight")
+        rows: Dict[str, tuple] = {}
+        full: Dict[str, torch.Tensor] = {}
+        for name, t in g.tensors.items():
+            hf = gguf_name_to_hf(name)
+            if hf is None:
+                continue
+            if quantized and hf.endswith(lin) and t.type_name in ("Q8_0", "Q4_0"):
+                N, K = t.shape
+                r = torch.from_numpy(np.ascontiguousarray(g.raw(name))).view(N, -1)
+                if g.arch == "llama" and (name.endswith("attn_q.weight") or name.endswith("attn_k.weight")):
+                    r = unpermute_qk(r, g._heads_for(name)).contiguous()
+                rows[hf] = (t.type_name, r, K)
+            else:
+                full[hf] = g.tensor(name)
+        self.embed = full["model.embed_tokens.weight"].to(dev, bf).contiguous()
+        self.final_norm = full["model.norm.weight"].to(dev, bf).contiguous()
+        self.lm_head = full.get("lm_head.weight", full["model.embed_tokens.weight"]).to(dev, bf).contiguous()
+
+        def weight(name):
+            if name in rows:
+                kind, r, K = rows[name]
+                return ops.QWeight.from_rows(kind, r, K, dev)
+            return full[name].to(dev, bf).contiguous()
+
+        def cat_rows(names):
+            if all(n in rows for n in names) and len({rows[n][0] for n in names}) == 1:
+                kind, K = rows[names[0]][0], rows[names[0]][2]
+                return ops.QWeight.from_rows(kind, torch.cat([rows[n][1] for n in names], 0), K, dev)
+            return torch.cat([(weight(n).dequantize() if n in rows else weight(n)) for n in names], 0).contiguous()
+
+        self.layers = []
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            layer = {"ln1": full[p + "input_layernorm.weight"].to(dev, bf).contiguous(),
+                     "ln2": full[p + "post_attention_layernorm.weight"].to(dev, bf).contiguous(),
+                     "qkv": cat_rows([p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight",
+                                      p + "self_attn.v_proj.weight"]),
+                     "o": weight(p + "self_attn.o_proj.weight")}
+            if cfg.qkv_bias:
+                layer["qkv_b"] = torch.cat([full[p + f"self_attn.{x}_proj.bias"] for x in "qkv"]).to(dev, bf)
+            if cfg.qk_norm:
+                layer["q_norm"] = full[p + "self_attn.q_norm.weight"].to(dev, bf).contiguous()
+                layer["k_norm"] = full[p + "self_attn.k_norm.weight"].to(dev, bf).contiguous()
+            gn, un = p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"
+            if gn in rows and un in rows and rows[gn][0] == rows[un][0]:
+                kind, K = rows[gn][0], rows[gn][2]
+                layer["gate_up"] = ops.QWeight.from_rows(kind, ops.interleave_gate_up(rows[gn][1], rows[un][1]), K, dev)
+            else:
+                gw = weight(gn)
+                uw = weight(un)
+                gw = gw.dequantize() if isinstance(gw, ops.QWeight) else gw
+                uw = uw.dequantize() if isinstance(uw, ops.QWeight) else uw
+                layer["gate_up"] = ops.interleave_gate_up(gw, uw)
+            layer["down"] = weight(p + "mlp.down_proj.weight")
+            self.layers.append(layer)
+        self._finish()
+
+    def quantize_weights(self, kind: str = "Q8_0") -> None:
+        """Re-store the projection weights as GGUF blocks on the device (round
+        to nearest), e.g. to serve a bf16 checkpoint in Q8_0 / Q4_0."""
+        assert self.tp.size == 1
+        for lay in self.layers:
+            for k in ("qkv", "o", "gate_up", "down"):
+                if k in lay and not isinstance(lay[k], ops.QWeight):
+                    lay[k] = ops.QWeight.quantize(lay[k], kind, self.device)
+        torch.cuda.empty_cache()
+
     def random_init(self, seed: int = 0, std: float = 0.02) -> None:
         """N(0, std) weights (norms = 1) generated as full tensors from one seeded
         stream and then sharded, so every TP size holds the same model."""
@@ -273,7 +355,7 @@ class DecoderLM:
     def weight_bytes(self) -> int:
         n = 0
         for lay in self.layers:
-            n += sum(t.numel() * t.element_size() for t in lay.values())
+            n += sum(t.nbytes() if isinstance(t, ops.QWeight) else t.numel() * t.element_size() for t in lay.values())
         for t in (self.embed, self.final_norm, self.lm_head):
             if t is not None:
                 n += t.numel() * t.element_size()

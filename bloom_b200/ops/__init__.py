@@ -6,7 +6,7 @@ the call raises.  The fp32 oracles for tests live in `bloom_b200.ops.reference`.
 """
 from __future__ import annotations
 
-from typing import Optional
+from typing import Dict, Optional
 
 import torch
 
@@ -49,6 +49,83 @@ def check_status(device: Optional[int] = None) -> int:
 
 
 # ---------------------------------------------------------------- GEMM
+class QWeight:
+    """A GGUF Q8_0 / Q4_0 weight [N, K] kept block-quantised on the device:
+    `qs` int8 [N, K] (Q8_0) or uint8 [N, K/2] (Q4_0, the GGUF nibble order) and
+    `scales` fp16 [N, K/32] -- the GGUF blocks split into two aligned planes,
+    bit-exact.  `gemm` runs it through qgemv (M <= 8) or dequantises into a
+    bf16 scratch for the tcgen05 GEMM."""
+
+    KINDS = {"Q8_0": 0, "Q4_0": 1}
+    BLOCK_BYTES = {"Q8_0": 34, "Q4_0": 18}
+
+    def __init__(self, kind: str, qs: torch.Tensor, scales: torch.Tensor, K: int):
+        self.kind = kind
+        self.kid = self.KINDS[kind]
+        self.qs = qs
+        self.scales = scales
+        self.K = int(K)
+        self.shape = (int(scales.shape[0]), self.K)
+        self.device = qs.device
+
+    @classmethod
+    def from_rows(cls, kind: str, rows: torch.Tensor, K: int, device) -> "QWeight":
+        """rows: uint8 [N, K/32 * block_bytes] -- whole GGUF blocks per row."""
+        bb = cls.BLOCK_BYTES[kind]
+        N = rows.shape[0]
+        blocks = rows.reshape(N, K // 32, bb)
+        scales = blocks[:, :, :2].contiguous().view(torch.float16).reshape(N, K // 32)
+        q = blocks[:, :, 2:].contiguous()
+        qs = q.view(torch.int8).reshape(N, K) if kind == "Q8_0" else q.reshape(N, K // 2)
+        return cls(kind, qs.to(device), scales.to(device), K)
+
+    @classmethod
+    def quantize(cls, w: torch.Tensor, kind: str, device) -> "QWeight":
+        """Round-to-nearest GGUF blocks of a float weight (CPU quantiser)."""
+        from .._ext import runtime
+
+        wf = w.detach().float().cpu().contiguous()
+        N, K = wf.shape
+        raw = runtime().quantize_q8_0(wf.view(-1)) if kind == "Q8_0" else runtime().quantize_q4_0(wf.view(-1))
+        return cls.from_rows(kind, raw.view(N, -1), K, device)
+
+    def dequantize(self, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(self.shape, dtype=torch.bfloat16, device=self.device)
+        _C().qdequant(self.qs, self.scales, self.kid, out)
+        _count()
+        return out
+
+    def nbytes(self) -> int:
+        return self.qs.numel() * self.qs.element_size() + self.scales.numel() * 2
+
+
+_DEQ_SCRATCH: Dict[int, torch.Tensor] = {}
+
+
+def _dequant_scratch(w: "QWeight") -> torch.Tensor:
+    n = w.shape[0] * w.shape[1]
+    key = w.device.index or 0
+    buf = _DEQ_SCRATCH.get(key)
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(n, dtype=torch.bfloat16, device=w.device)
+        _DEQ_SCRATCH[key] = buf
+    return buf[:n].view(w.shape)
+
+
+def _qgemm(x, w: "QWeight", out, epi, bias, resid, splits, bn):
+    M = x.shape[0]
+    N = w.shape[0]
+    if M <= 8 and bias is None and epi in (EPI_BF16, EPI_SWIGLU, EPI_RESIDUAL):
+        if out is None:
+            out = torch.empty(M, N // 2 if epi == EPI_SWIGLU else N, dtype=torch.bfloat16, device=x.device)
+        _C().qgemv(x.contiguous(), w.qs, w.scales, w.kid, out, epi, resid)
+        _count()
+        return out
+    wb = w.dequantize(_dequant_scratch(w))
+    return gemm(x, wb, out, epi=epi, bias=bias, resid=resid, splits=splits, bn=bn)
+
+
 def gemm(
     x: torch.Tensor,
     w: torch.Tensor,
@@ -71,6 +148,8 @@ def gemm(
     K range is split across CTAs so every SM streams weights, and the last
     split to finish each tile sums the fp32 partials and runs the epilogue.
     """
+    if isinstance(w, QWeight):
+        return _qgemm(x, w, out, epi, bias, resid, splits, bn)
     M, N = x.shape[0], w.shape[0]
     K = x.shape[1]
     if splits is None and bn is None:

@@ -33,6 +33,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_rows", &bloom::argmax_rows);
   m.def("sample_rows", &bloom::sample_rows);
   m.def("verify_sample_rows", &bloom::verify_sample_rows);
+  m.def("qgemv", &bloom::qgemv, py::arg("x"), py::arg("qs"), py::arg("scales"), py::arg("kind"), py::arg("out"),
+        py::arg("epi"), py::arg("resid") = py::none());
+  m.def("qdequant", &bloom::qdequant);
   m.def("status_tensor", &bloom::status_tensor);
   m.def("bert_embed_ln", &bloom::bert_embed_ln);
   m.def("varlen_attention", &bloom::varlen_attention);

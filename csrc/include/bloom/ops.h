@@ -83,6 +83,13 @@ void sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, 
 // top-p distribution, otherwise draw from that distribution with the proposal
 // removed (rejection sampling with a deterministic proposal; exact for the
 // target distribution).  A row without a proposal samples as sample_rows.
+// GGUF Q8_0 (kind 0) / Q4_0 (kind 1) weights kept quantised on the device
+// (quant plane + fp16 scale plane [N, K/32]).  qgemv: M <= 8 tokens with a
+// bf16, SwiGLU (interleaved rows) or residual epilogue; qdequant: bf16 [N, K].
+void qgemv(const torch::Tensor& x, const torch::Tensor& qs, const torch::Tensor& scales, int64_t kind,
+           torch::Tensor& out, int64_t epi, const c10::optional<torch::Tensor>& resid);
+void qdequant(const torch::Tensor& qs, const torch::Tensor& scales, int64_t kind, torch::Tensor& out);
+
 void verify_sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
                         const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
                         const torch::Tensor& draft, torch::Tensor& out);

@@ -205,7 +205,8 @@ def test_registry_routing():
 
     r = default_registry()
     assert r.route("Llama", "Safetensors", "BF16", "gpu") == ("b200", NATIVE)
-    assert r.route("Llama", "Gguf", "Q8", "gpu") == ("b200", FALLBACK)
+    assert r.route("Llama", "Gguf", "Q8", "gpu") == ("b200", NATIVE)  # block-quantised GPU kernels
+    assert r.route("Llama", "Safetensors", "F32", "gpu") == ("b200", FALLBACK)
     assert r.route("Llama", "Gguf", "Q8", "cpu") == ("cpu", NATIVE)
     assert r.route("Whisper", "Gguf", "Q8", "cpu")[1] == UNSUPPORTED
     assert any(e["name"] == "b200" and e["max_tp"] == 8 for e in r.describe())
