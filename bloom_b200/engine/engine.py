@@ -86,6 +86,12 @@ class EngineConfig:
     # speculative decoding: proposals verified per sequence and step (0 = off);
     # attach a proposer with LLMEngine.attach_speculator / make_speculator
     spec_len: int = 0
+    # CacheMesh: pinned host bytes for evicted prefix blocks (0 = off) and an
+    # optional directory of block files below it
+    cachemesh_l2_bytes: int = 0
+    cachemesh_l3_dir: str = ""
+    cachemesh_l3_blocks: int = 0
+    cachemesh_namespace: Optional[str] = None
 
 
 class LLMEngine:
@@ -120,6 +126,9 @@ class LLMEngine:
             ops.gemm_autotune(model.gemm_shapes(), [b * ql for b in self.runner.buckets + [ec.max_num_seqs]], dev)
         self.scheduler.set_arena(self.runner.arena_host, self.runner.max_tokens, ec.max_num_seqs,
                                  self.runner.max_blocks)
+        if ec.cachemesh_l2_bytes > 0:
+            self.runner.enable_cachemesh(self.scheduler, ec.cachemesh_l2_bytes, ec.cachemesh_l3_dir,
+                                         ec.cachemesh_l3_blocks, ec.cachemesh_namespace or self._namespace())
         if ec.use_cuda_graphs:
             self.scheduler.set_decode_buckets(sorted(self.runner.buckets))
             self.runner.capture_graphs()
@@ -190,6 +199,8 @@ class LLMEngine:
             for rid in self.constraints:
                 self.scheduler.set_draft(rid, [])
         meta = self.scheduler.schedule()
+        if self.runner.l2 is not None:
+            self.runner.apply_kv_copies(self.scheduler.take_restores(), self.scheduler.take_offloads())
         if meta.num_tokens == 0:
             return []
         sampled = self.runner.execute(meta)
@@ -260,7 +271,26 @@ class LLMEngine:
                 return
 
     def kv_metrics(self) -> dict:
-        return dict(self.scheduler.kv_metrics())
+        d = dict(self.scheduler.kv_metrics())
+        mesh = dict(self.scheduler.cachemesh_metrics())
+        if mesh:
+            d["cachemesh"] = mesh
+        return d
+
+    def _namespace(self) -> str:
+        """Model + KV layout + a fingerprint of the weights: L3 files of another
+        model or another set of weights never match."""
+        import hashlib
+
+        m, cfg = self.model, self.cfg
+        h = hashlib.sha256()
+        for lay in m.layers[:4]:
+            w = lay["qkv"]
+            w = w.scales if hasattr(w, "scales") else w
+            h.update(w.reshape(-1)[:256].float().cpu().numpy().tobytes())
+        h.update(m.embed.reshape(-1)[:256].float().cpu().numpy().tobytes())
+        return (f"{cfg.name or cfg.arch}-L{cfg.num_layers}-kv{m.nkv}-hd{cfg.head_dim}-tp{m.tp.rank}of{m.tp.size}-"
+                f"{h.hexdigest()[:16]}")
 
     def shutdown(self) -> None:
         self.runner.release_graphs()

@@ -86,7 +86,35 @@ class ModelRunner:
 
         self.check_finite = _os.environ.get("BLOOM_CHECK_FINITE", "0") == "1"
         self.graph_pool = None
+        self.l2 = None
         self.stats = {"steps": 0, "graph_steps": 0, "eager_steps": 0, "tokens": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+
+    # ------------------------------------------------------------ CacheMesh tiers
+    def kv_block_bytes(self) -> int:
+        return kv_block_bytes(self.model, self.block_size)
+
+    def enable_cachemesh(self, scheduler, l2_bytes: int, l3_dir: str = "", l3_max_blocks: int = 0,
+                         namespace: str = "default") -> None:
+        """Pinned host slots (L2) and optional files (L3) below the HBM prefix
+        cache; the scheduler queues the block copies, `apply_kv_copies` issues them."""
+        bb = self.kv_block_bytes()
+        slots = max(1, int(l2_bytes) // bb)
+        self.l2 = torch.empty(slots * bb, dtype=torch.uint8).pin_memory()
+        cfg = self.cfg
+        self.l2_view = self.l2.view(torch.bfloat16).view(slots, cfg.num_layers, 2, self.model.nkv, self.block_size,
+                                                         cfg.head_dim)
+        scheduler.enable_cachemesh(self.l2, bb, l3_dir, int(l3_max_blocks), namespace)
+
+    def apply_kv_copies(self, restores, offloads) -> None:
+        """Host -> HBM restores first (a slot may be reused by an offload of
+        the same step), then HBM -> host offloads; both on the step's stream,
+        ahead of the forward that may overwrite an offloaded block."""
+        for blk, slot in restores:
+            self.kv_cache[:, blk].copy_(self.l2_view[slot], non_blocking=True)
+        for blk, slot in offloads:
+            self.l2_view[slot].copy_(self.kv_cache[:, blk], non_blocking=True)
+        self.stats["kv_restores"] = self.stats.get("kv_restores", 0) + len(restores)
+        self.stats["kv_offloads"] = self.stats.get("kv_offloads", 0) + len(offloads)
 
     # ------------------------------------------------------------ views
     def _v(self, off: int, n: int, dtype=torch.int32) -> torch.Tensor:

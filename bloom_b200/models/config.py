@@ -194,6 +194,11 @@ PRESETS = {
                                rope_theta=1000000.0, max_position_embeddings=1024, qk_norm=True, num_experts=16,
                                num_experts_per_tok=4, moe_intermediate_size=128, eos_token_ids=[2],
                                name="tiny-moe-tp"),
+    # head_dim 64 (the 1B draft and SmolLM2 layouts)
+    "tiny-hd64": ModelConfig(arch="llama", vocab_size=512, hidden_size=256, num_layers=2, num_heads=8,
+                             num_kv_heads=2, head_dim=64, intermediate_size=512, rms_norm_eps=1e-5,
+                             rope_theta=10000.0, max_position_embeddings=1024, tie_word_embeddings=True,
+                             eos_token_ids=[2], name="tiny-hd64"),
     "tiny-moe": ModelConfig(arch="qwen3_moe", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
                             num_kv_heads=2, head_dim=128, intermediate_size=512, rms_norm_eps=1e-6,
                             rope_theta=1000000.0, max_position_embeddings=1024, qk_norm=True, num_experts=8,

@@ -184,6 +184,53 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              return q == nullptr ? 0 : q->num_cached_prefix;
            })
       .def("sampling_ids", &Scheduler::sampling_ids)
+      .def(
+          "enable_cachemesh",
+          [](Scheduler& s, const torch::Tensor& l2, int64_t block_bytes, const std::string& l3_dir,
+             int64_t l3_max_blocks, const std::string& ns) {
+            TORCH_CHECK(l2.device().is_cpu() && l2.scalar_type() == at::kByte && l2.is_contiguous(),
+                        "cachemesh: L2 must be a contiguous uint8 host tensor (pinned)");
+            TORCH_CHECK(block_bytes > 0 && l2.numel() % block_bytes == 0, "cachemesh: L2 size not a block multiple");
+            CacheMeshConfig c;
+            c.l2_slots = l2.numel() / block_bytes;
+            c.block_bytes = block_bytes;
+            c.l3_dir = l3_dir;
+            c.l3_max_blocks = l3_max_blocks;
+            c.name_space = ns;
+            s.enable_cachemesh(c, l2.data_ptr<uint8_t>());
+          },
+          py::arg("l2"), py::arg("block_bytes"), py::arg("l3_dir") = "", py::arg("l3_max_blocks") = 0,
+          py::arg("namespace") = "default", py::keep_alive<1, 2>())
+      .def("take_offloads",
+           [](Scheduler& s) {
+             std::vector<std::pair<int, int>> v;
+             for (auto& c : s.blocks().take_offloads()) v.emplace_back(c.block, c.slot);
+             return v;
+           })
+      .def("take_restores",
+           [](Scheduler& s) {
+             std::vector<std::pair<int, int>> v;
+             for (auto& c : s.blocks().take_restores()) v.emplace_back(c.block, c.slot);
+             return v;
+           })
+      .def("cachemesh_metrics",
+           [](Scheduler& s) {
+             py::dict d;
+             if (s.cachemesh() == nullptr) return d;
+             const CacheMeshMetrics m = s.cachemesh()->metrics();
+             d["l2_used"] = m.l2_used;
+             d["l2_capacity"] = m.l2_capacity;
+             d["l3_used"] = m.l3_used;
+             d["l3_capacity"] = m.l3_capacity;
+             d["offloads"] = m.offloads;
+             d["l2_hits"] = m.l2_hits;
+             d["l3_hits"] = m.l3_hits;
+             d["misses"] = m.misses;
+             d["l2_evictions"] = m.l2_evictions;
+             d["l3_writes"] = m.l3_writes;
+             d["l3_evictions"] = m.l3_evictions;
+             return d;
+           })
       .def("decode_candidates", &Scheduler::decode_candidates)
       .def("set_draft", &Scheduler::set_draft)
       .def("propose_ngram", &Scheduler::propose_ngram, py::arg("max_order") = 4, py::arg("min_order") = 1)

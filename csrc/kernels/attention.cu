@@ -5,6 +5,8 @@
 // with 2D TMA tiles (box 64 dims x 16 tokens, 128-byte swizzle) so the
 // ldmatrix reads that feed the tensor cores are bank-conflict free.
 //
+// head_dim 128 or 64 (template parameter D).
+//
 // Decode / speculative verify (q_len 1..8): one CTA per (sequence, KV head,
 // split); the q heads of a GQA group and the q positions of the request are
 // packed into the 16-row M dimension of m16n8k16 MMAs, so every KV page is
@@ -80,7 +82,7 @@ struct DecodeArgs {
 };
 
 // Row r of the packed M dimension -> (q position qi, head-in-group hh).
-template <int MT, int NWARPS, int NST>
+template <int D, int MT, int NWARPS, int NST>
 __global__ void __launch_bounds__(NWARPS * 32)
     decode_kernel(const __grid_constant__ CUtensorMap tmKV, const DecodeArgs a) {
   constexpr int kStageBytes = 2 * PAGE * D * 2;  // K + V page = 8 KiB
@@ -120,18 +122,19 @@ __global__ void __launch_bounds__(NWARPS * 32)
     const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
     const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
     uint8_t* st = wsm + s * kStageBytes;
+    constexpr int kPageB = PAGE * D * 2;  // one page of one KV head: 2 KiB boxes of 64 dims
     mbar_arrive_expect_tx(&bars[s], kStageBytes);
     tma_load_2d(st, &tmKV, &bars[s], 0, rowK);
-    tma_load_2d(st + 2048, &tmKV, &bars[s], 64, rowK);
-    tma_load_2d(st + 4096, &tmKV, &bars[s], 0, rowV);
-    tma_load_2d(st + 6144, &tmKV, &bars[s], 64, rowV);
+    if constexpr (D == 128) tma_load_2d(st + 2048, &tmKV, &bars[s], 64, rowK);
+    tma_load_2d(st + kPageB, &tmKV, &bars[s], 0, rowV);
+    if constexpr (D == 128) tma_load_2d(st + kPageB + 2048, &tmKV, &bars[s], 64, rowV);
   };
   if (lane == 0) {
     for (int i = 0; i < NST && i < my_n; ++i) issue(i);
   }
 
   // Q fragments (A operand), rows beyond R are zero.
-  uint32_t qf[MT][8][4];
+  uint32_t qf[MT][D / 16][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -143,7 +146,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
         qrow = a.q + ((long)(b * a.ql + qi) * a.nq + vkh * G + hh) * D;
       }
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
+      for (int ks = 0; ks < D / 16; ++ks) {
         const int d = ks * 16 + 2 * t4;
         qf[mt][ks][hr] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
         qf[mt][ks][hr + 2] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
@@ -152,13 +155,13 @@ __global__ void __launch_bounds__(NWARPS * 32)
   }
 
   float m_run[MT][2], l_run[MT][2];
-  float o[MT][16][4];
+  float o[MT][D / 8][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
     m_run[mt][0] = m_run[mt][1] = kNegBig;
     l_run[mt][0] = l_run[mt][1] = 0.f;
 #pragma unroll
-    for (int n = 0; n < 16; ++n) o[mt][n][0] = o[mt][n][1] = o[mt][n][2] = o[mt][n][3] = 0.f;
+    for (int n = 0; n < D / 8; ++n) o[mt][n][0] = o[mt][n][1] = o[mt][n][2] = o[mt][n][3] = 0.f;
   }
   // causal limit per packed row: kv index must be <= kv_len - ql + qi
   int limit[MT][2];
@@ -175,7 +178,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
     const int s = i % NST;
     if (!mbar_wait(&bars[s], (i / NST) & 1, &abort_flag, a.status, kStatusAttnTimeout)) break;
     const uint32_t sK = smem_u32(wsm + s * kStageBytes);
-    const uint32_t sV = sK + 4096;
+    const uint32_t sV = sK + PAGE * D * 2;
     const int tok_base = (first + i * NWARPS) * PAGE;
 
     float sc[MT][2][4];
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < D / 32; ++j) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         uint32_t b0, b1, b2, b3;
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
         }
         l_run[mt][hr] = l_run[mt][hr] * alpha + ps;
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
+        for (int n = 0; n < D / 8; ++n) {
           o[mt][n][2 * hr] *= alpha;
           o[mt][n][2 * hr + 1] *= alpha;
         }
@@ -238,7 +241,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
     }
 
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < D / 16; ++j) {
       uint32_t b0, b1, b2, b3;
       ldsm_x4_t(page_addr(sV, (lane & 7) + 8 * ((lane >> 3) & 1), 16 * j + 8 * (lane >> 4)), b0, b1, b2, b3);
 #pragma unroll
@@ -280,7 +283,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
     for (int hr = 0; hr < 2; ++hr) {
       const int r = mt * 16 + g + 8 * hr;
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
+      for (int n = 0; n < D / 8; ++n) {
         wbuf[r * RS + 8 * n + 2 * t4] = o[mt][n][2 * hr];
         wbuf[r * RS + 8 * n + 2 * t4 + 1] = o[mt][n][2 * hr + 1];
       }
@@ -318,6 +321,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
   }
 }
 
+template <int D>
 __global__ void decode_combine_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ out, int nq,
                                       int nkv, int ql, int splits) {
   constexpr int RS = D + 2;
@@ -359,9 +363,11 @@ struct PrefillArgs {
 constexpr int kPfWarps = 4;
 constexpr int kPfRows = 16 * kPfWarps;  // 64 query rows per CTA
 constexpr int kPfKv = 64;               // kv tokens per tile (4 pages)
-constexpr int kPfStageBytes = 2 * kPfKv * D * 2;  // K + V = 32 KiB
+template <int D>
+constexpr int pf_stage_bytes() { return 2 * kPfKv * D * 2; }  // K + V tile: 32 KiB at D = 128
 constexpr int kPfStages = 2;
 
+template <int D>
 __global__ void __launch_bounds__(kPfWarps * 32)
     prefill_kernel(const __grid_constant__ CUtensorMap tmKV, const PrefillArgs a) {
   const int tile = blockIdx.x, h = blockIdx.y;
@@ -379,6 +385,9 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kPfStageBytes = pf_stage_bytes<D>();
+  constexpr int kHalf = kPfKv * D * 2;   // K (or V) part of a stage
+  constexpr int kPageB = PAGE * D * 2;   // one page of one KV head
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPfStages * kPfStageBytes);
   __shared__ int abort_flag;
 
@@ -404,17 +413,17 @@ __global__ void __launch_bounds__(kPfWarps * 32)
       const int blk = bt[page < n_pages ? page : 0];
       const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
       const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
-      tma_load_2d(st + pg * 4096, &tmKV, &bars[s], 0, rowK);
-      tma_load_2d(st + pg * 4096 + 2048, &tmKV, &bars[s], 64, rowK);
-      tma_load_2d(st + 16384 + pg * 4096, &tmKV, &bars[s], 0, rowV);
-      tma_load_2d(st + 16384 + pg * 4096 + 2048, &tmKV, &bars[s], 64, rowV);
+      tma_load_2d(st + pg * kPageB, &tmKV, &bars[s], 0, rowK);
+      if constexpr (D == 128) tma_load_2d(st + pg * kPageB + 2048, &tmKV, &bars[s], 64, rowK);
+      tma_load_2d(st + kHalf + pg * kPageB, &tmKV, &bars[s], 0, rowV);
+      if constexpr (D == 128) tma_load_2d(st + kHalf + pg * kPageB + 2048, &tmKV, &bars[s], 64, rowV);
     }
   };
   if (threadIdx.x == 0)
     for (int kt = 0; kt < kPfStages && kt < n_kt; ++kt) issue(kt);
 
   // Q fragments for rows row0 + 16*warp + {g, g+8}
-  uint32_t qf[8][4];
+  uint32_t qf[D / 16][4];
   int qpos[2];
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
@@ -423,7 +432,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
     qpos[hr] = valid ? (a.causal ? ctx - q_len + lr : ctx - 1) : -1;
     const __nv_bfloat16* qrow = valid ? a.q + ((long)(q_begin + lr) * a.nq + h) * D : nullptr;
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
+    for (int ks = 0; ks < D / 16; ++ks) {
       const int d = ks * 16 + 2 * t4;
       qf[ks][hr] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
       qf[ks][hr + 2] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
@@ -431,9 +440,9 @@ __global__ void __launch_bounds__(kPfWarps * 32)
   }
 
   float m_run[2] = {kNegBig, kNegBig}, l_run[2] = {0.f, 0.f};
-  float o[16][4];
+  float o[D / 8][4];
 #pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
   int kt = 0;
   bool ok = true;
@@ -447,7 +456,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
       break;
     }
     const uint32_t sK = smem_u32(smem + s * kPfStageBytes);
-    const uint32_t sV = sK + 16384;
+    const uint32_t sV = sK + kHalf;
     const int kv0 = kt * kPfKv;
     // skip whole tiles above the diagonal for this warp
     const bool warp_active = (qpos[0] >= kv0) || (qpos[1] >= kv0);
@@ -458,9 +467,9 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const int tok = 8 * nt + (lane & 7);
-        const uint32_t pbase = sK + (tok >> 4) * 4096;
+        const uint32_t pbase = sK + (tok >> 4) * kPageB;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < D / 32; ++j) {
           uint32_t b0, b1, b2, b3;
           ldsm_x4(page_addr(pbase, tok & 15, 32 * j + 8 * (lane >> 3)), b0, b1, b2, b3);
           mma_bf16_16816(sc[nt], qf[2 * j], b0, b1);
@@ -497,7 +506,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
           }
         l_run[hr] = l_run[hr] * alpha + ps;
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
+        for (int n = 0; n < D / 8; ++n) {
           o[n][2 * hr] *= alpha;
           o[n][2 * hr + 1] *= alpha;
         }
@@ -511,9 +520,9 @@ __global__ void __launch_bounds__(kPfWarps * 32)
       }
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const uint32_t pbase = sV + kk * 4096;
+        const uint32_t pbase = sV + kk * kPageB;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < D / 16; ++j) {
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(page_addr(pbase, (lane & 7) + 8 * ((lane >> 3) & 1), 16 * j + 8 * (lane >> 4)), b0, b1, b2, b3);
           mma_bf16_16816(o[2 * j], pa[kk], b0, b1);
@@ -541,7 +550,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = a.out + ((long)(q_begin + lr) * a.nq + h) * D;
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
+      for (int n = 0; n < D / 8; ++n) {
         *reinterpret_cast<uint32_t*>(orow + 8 * n + 2 * t4) = pack_bf16(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
       }
     }
@@ -549,20 +558,25 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 }
 
 CUtensorMap kv_tmap(const torch::Tensor& kv_cache, int64_t layer) {
-  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(2) == 2 && kv_cache.size(4) == PAGE && kv_cache.size(5) == D,
-              "kv_cache must be [L, NB, 2, KVH, 16, 128]");
+  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(2) == 2 && kv_cache.size(4) == PAGE &&
+                  (kv_cache.size(5) == 128 || kv_cache.size(5) == 64),
+              "kv_cache must be [L, NB, 2, KVH, 16, 128 or 64]");
   TORCH_CHECK(kv_cache.is_contiguous() && kv_cache.scalar_type() == at::kBFloat16, "kv_cache contiguous bf16");
   const uint64_t rows = (uint64_t)kv_cache.size(1) * 2 * kv_cache.size(3) * PAGE;
   TORCH_CHECK(rows < (1ull << 31), "kv_cache too many rows per layer for int32 TMA coordinates");
   const auto* base = reinterpret_cast<const __nv_bfloat16*>(kv_cache.data_ptr()) + layer * kv_cache.stride(0);
-  return make_tmap_bf16_2d(base, D, rows, D * 2, 64, PAGE);
+  const int hd = int(kv_cache.size(5));
+  return make_tmap_bf16_2d(base, hd, rows, hd * 2, 64, PAGE);
 }
 
-template <int MT, int NWARPS, int NST>
+template <int D, int MT, int NWARPS, int NST>
 void launch_decode(const CUtensorMap& tm, const DecodeArgs& a, int B, cudaStream_t stream) {
-  constexpr int smem = NWARPS * NST * 8192 + NWARPS * NST * 8 + 1024;
-  static_assert(NWARPS * NST * 8192 >= NWARPS * MT * 16 * (D + 2) * 4, "merge buffer must fit in the stage ring");
-  auto kern = decode_kernel<MT, NWARPS, NST>;
+  constexpr int kStage = 2 * PAGE * D * 2;
+  constexpr int ring = NWARPS * NST * kStage > NWARPS * MT * 16 * (D + 2) * 4 ? NWARPS * NST * kStage
+                                                                              : NWARPS * MT * 16 * (D + 2) * 4;
+  static_assert(ring == NWARPS * NST * kStage, "the cross-warp merge buffer must fit in the stage ring");
+  constexpr int smem = ring + NWARPS * NST * 8 + 1024;
+  auto kern = decode_kernel<D, MT, NWARPS, NST>;
   static uint64_t configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -598,7 +612,10 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
                             const torch::Tensor& block_table, const torch::Tensor& seq_lens, torch::Tensor& out,
                             int64_t q_len, int64_t splits, torch::Tensor& workspace, double scale,
                             const torch::Tensor& status) {
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(-1) == attn::D, "decode: q [T,nq,128]");
+  const int hd = int(q.size(-1));
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && (hd == 128 || hd == 64),
+              "decode: q [T, nq, 128 or 64] bf16");
+  TORCH_CHECK(kv_cache.size(5) == hd, "decode: q and kv_cache head_dim differ");
   TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.stride(1) == 1, "decode: block_table int32");
   TORCH_CHECK(seq_lens.scalar_type() == at::kInt, "decode: seq_lens int32");
   const int B = seq_lens.size(0);
@@ -609,7 +626,7 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
   const int G = nq / nkv;
   const int hc = int(decode_head_chunks(nq, nkv, q_len));
   TORCH_CHECK(hc > 0, "decode: no split of the ", G, " q heads per kv head fits 32 rows at q_len ", q_len);
-  TORCH_CHECK(q.numel() / (nq * attn::D) == B * q_len, "decode: q rows must equal batch * q_len");
+  TORCH_CHECK(q.numel() / (nq * hd) == B * q_len, "decode: q rows must equal batch * q_len");
   const at::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 
@@ -629,20 +646,28 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
   a.part = nullptr;
   if (a.splits > 1) {
     TORCH_CHECK(workspace.scalar_type() == at::kFloat &&
-                    workspace.numel() >= (int64_t)B * nkv * hc * a.splits * 32 * (attn::D + 2),
+                    workspace.numel() >= (int64_t)B * nkv * hc * a.splits * 32 * (hd + 2),
                 "decode: workspace too small");
     a.part = workspace.data_ptr<float>();
   }
   const CUtensorMap tm = attn::kv_tmap(kv_cache, layer);
-  if ((G / hc) * q_len <= 16)
-    attn::launch_decode<1, 4, 3>(tm, a, B, stream);
-  else
-    attn::launch_decode<2, 4, 3>(tm, a, B, stream);
+  const bool mt1 = (G / hc) * q_len <= 16;
+  if (hd == 128) {
+    if (mt1) attn::launch_decode<128, 1, 4, 3>(tm, a, B, stream);
+    else attn::launch_decode<128, 2, 4, 3>(tm, a, B, stream);
+  } else {
+    if (mt1) attn::launch_decode<64, 1, 4, 3>(tm, a, B, stream);
+    else attn::launch_decode<64, 2, 4, 3>(tm, a, B, stream);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (a.splits > 1) {
     // each (kv head, head chunk) pair acts as its own "kv head" of G / hc q heads
-    attn::decode_combine_kernel<<<dim3(B, nkv * hc), 256, 0, stream>>>(a.part, a.out, nq, nkv * hc, a.ql,
-                                                                      a.splits);
+    if (hd == 128)
+      attn::decode_combine_kernel<128><<<dim3(B, nkv * hc), 256, 0, stream>>>(a.part, a.out, nq, nkv * hc, a.ql,
+                                                                             a.splits);
+    else
+      attn::decode_combine_kernel<64><<<dim3(B, nkv * hc), 256, 0, stream>>>(a.part, a.out, nq, nkv * hc, a.ql,
+                                                                            a.splits);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -652,7 +677,10 @@ void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cac
                              const torch::Tensor& cu_seqlens_q, const torch::Tensor& tile_seq,
                              const torch::Tensor& tile_start, torch::Tensor& out, double scale, bool causal,
                              const torch::Tensor& status) {
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(-1) == attn::D, "prefill: q [T,nq,128]");
+  const int hd = int(q.size(-1));
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && (hd == 128 || hd == 64),
+              "prefill: q [T, nq, 128 or 64] bf16");
+  TORCH_CHECK(kv_cache.size(5) == hd, "prefill: q and kv_cache head_dim differ");
   const int n_tiles = tile_seq.size(0);
   if (n_tiles == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
@@ -672,15 +700,20 @@ void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cac
   a.causal = causal ? 1 : 0;
   a.status = status.data_ptr<int>();
   const CUtensorMap tm = attn::kv_tmap(kv_cache, layer);
-  constexpr int smem = attn::kPfStages * attn::kPfStageBytes + 64 + 1024;
+  constexpr int smem128 = attn::kPfStages * attn::pf_stage_bytes<128>() + 64 + 1024;
+  constexpr int smem64 = attn::kPfStages * attn::pf_stage_bytes<64>() + 64 + 1024;
   static uint64_t configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!((configured >> dev) & 1u)) {
-    cudaFuncSetAttribute(attn::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(attn::prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem128);
+    cudaFuncSetAttribute(attn::prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem64);
     configured |= uint64_t(1) << dev;
   }
-  attn::prefill_kernel<<<dim3(n_tiles, a.nq), attn::kPfWarps * 32, smem, stream>>>(tm, a);
+  if (hd == 128)
+    attn::prefill_kernel<128><<<dim3(n_tiles, a.nq), attn::kPfWarps * 32, smem128, stream>>>(tm, a);
+  else
+    attn::prefill_kernel<64><<<dim3(n_tiles, a.nq), attn::kPfWarps * 32, smem64, stream>>>(tm, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -806,12 +839,12 @@ extern "C" __attribute__((visibility("default"))) int bloom_paged_decode_attenti
   a.part = splits > 1 ? noalloc::g_dev[dev].scratch : nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((num_q_heads / num_kv_heads) * q_len <= 16)
-    attn::launch_decode<1, 4, 3>(tm, a, batch, s);
+    attn::launch_decode<attn::D, 1, 4, 3>(tm, a, batch, s);
   else
-    attn::launch_decode<2, 4, 3>(tm, a, batch, s);
+    attn::launch_decode<attn::D, 2, 4, 3>(tm, a, batch, s);
   if (cudaGetLastError() != cudaSuccess) return BLOOM_NOALLOC_LAUNCH_ERROR;
   if (splits > 1) {
-    attn::decode_combine_kernel<<<dim3(batch, num_kv_heads), 256, 0, s>>>(a.part, a.out, num_q_heads, num_kv_heads,
+    attn::decode_combine_kernel<attn::D><<<dim3(batch, num_kv_heads), 256, 0, s>>>(a.part, a.out, num_q_heads, num_kv_heads,
                                                                           q_len, splits);
     if (cudaGetLastError() != cudaSuccess) return BLOOM_NOALLOC_LAUNCH_ERROR;
   }

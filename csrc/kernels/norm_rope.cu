@@ -202,57 +202,60 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
 // qkv row layout: [q heads | k heads | v heads] x 128.
 // cos_sin: [max_pos, 128] f32 = [cos(0..63) | sin(0..63)].
 // kv cache: [L, NB, 2, KVH, 16, 128].
+template <int D>
 __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, long ldq, const int64_t* __restrict__ pos,
                                      const int* __restrict__ slots, const float* __restrict__ cos_sin,
                                      __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
                                      long layer_stride, int nq, int nkv, const __nv_bfloat16* __restrict__ qn,
                                      const __nv_bfloat16* __restrict__ kn, float eps, long max_pos) {
-  constexpr int D = 128;
+  constexpr int NV = D / 32;  // values per lane: dims lane + 32 i
   const long t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   long p = pos[t];
   p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);  // the table bounds every read
   const int slot = slots != nullptr ? slots[t] : -1;
-  const float* cs = cos_sin + p * D;
+  const float* cs = cos_sin + p * D;  // [cos(D/2) | sin(D/2)]
   const __nv_bfloat16* row = qkv + t * ldq;
   for (int h = warp; h < nq + 2 * nkv; h += nwarps) {
     const __nv_bfloat16* src = row + (long)h * D;
-    float v[4];
+    float v[NV];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(src[lane + 32 * i]);
+    for (int i = 0; i < NV; ++i) v[i] = __bfloat162float(src[lane + 32 * i]);
     const bool is_q = h < nq;
     const bool is_k = !is_q && h < nq + nkv;
     if (is_q || is_k) {
       const __nv_bfloat16* nw = is_q ? qn : kn;
       if (nw != nullptr) {
-        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) ss += v[i] * v[i];
         ss = warp_sum(ss);
         const float inv = rsqrtf(ss / D + eps);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = v[i] * inv * __bfloat162float(nw[lane + 32 * i]);
+        for (int i = 0; i < NV; ++i) v[i] = v[i] * inv * __bfloat162float(nw[lane + 32 * i]);
       }
-      // pairs (lane, lane+64) and (lane+32, lane+96)
+      // rotate-half pairs (d, d + D/2)
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
+      for (int i = 0; i < NV / 2; ++i) {
         const int d = lane + 32 * i;
-        const float c = cs[d], s = cs[64 + d];
-        const float x1 = v[i], x2 = v[i + 2];
+        const float c = cs[d], s = cs[D / 2 + d];
+        const float x1 = v[i], x2 = v[i + NV / 2];
         v[i] = x1 * c - x2 * s;
-        v[i + 2] = x2 * c + x1 * s;
+        v[i + NV / 2] = x2 * c + x1 * s;
       }
     }
     if (is_q) {
       __nv_bfloat16* dst = q_out + (t * nq + h) * D;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
+      for (int i = 0; i < NV; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
     } else if (slot >= 0) {
       const int kvsel = is_k ? 0 : 1;
       const int kh = is_k ? h - nq : h - nq - nkv;
       const long blk = slot >> 4, off = slot & 15;
       __nv_bfloat16* dst = cache + layer_stride + (((blk * 2 + kvsel) * nkv + kh) * 16 + off) * D;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
+      for (int i = 0; i < NV; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
     }
   }
 }
@@ -361,12 +364,13 @@ void rope_kv_write(const torch::Tensor& qkv, const torch::Tensor& positions, con
                    int64_t num_q_heads, int64_t num_kv_heads, const c10::optional<torch::Tensor>& q_norm,
                    const c10::optional<torch::Tensor>& k_norm, double eps) {
   TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "rope: qkv bf16 [T, *]");
-  TORCH_CHECK(qkv.size(1) >= (num_q_heads + 2 * num_kv_heads) * 128, "rope: head_dim must be 128");
+  const int hd = int(kv_cache.size(5));
+  TORCH_CHECK(hd == 128 || hd == 64, "rope: head_dim must be 128 or 64");
+  TORCH_CHECK(qkv.size(1) >= (num_q_heads + 2 * num_kv_heads) * hd, "rope: qkv narrower than the heads");
   TORCH_CHECK(positions.scalar_type() == at::kLong, "rope: positions int64");
   TORCH_CHECK(slot_mapping.scalar_type() == at::kInt, "rope: slot_mapping int32");
-  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == 128, "rope: cos_sin f32 [P,128]");
-  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(5) == 128 && kv_cache.size(3) == num_kv_heads,
-              "rope: kv_cache [L,NB,2,KVH,16,128]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == hd, "rope: cos_sin f32 [P, head_dim]");
+  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(3) == num_kv_heads, "rope: kv_cache [L,NB,2,KVH,16,head_dim]");
   const int T = qkv.size(0);
   if (T == 0) return;
   const at::cuda::CUDAGuard g(qkv.device());
@@ -377,7 +381,8 @@ void rope_kv_write(const torch::Tensor& qkv, const torch::Tensor& positions, con
   const __nv_bfloat16* kn = (k_norm.has_value() && k_norm->defined())
                                 ? reinterpret_cast<const __nv_bfloat16*>(k_norm->data_ptr())
                                 : nullptr;
-  rope_kv_write_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  auto kern = hd == 128 ? rope_kv_write_kernel<128> : rope_kv_write_kernel<64>;
+  kern<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),
       slot_mapping.data_ptr<int>(), cos_sin.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(kv_cache.data_ptr()), layer_stride, int(num_q_heads), int(num_kv_heads), qn,

@@ -57,6 +57,10 @@ int BlockManager::take_block() {
     lru_.erase(victim);
     in_lru_[b] = 0;
     if (block_hash_[b] != 0) {
+      if (mesh_ != nullptr) {  // keep the prefix one tier down
+        const int slot = mesh_->reserve_offload(block_hash_[b]);
+        if (slot >= 0) offloads_.push_back({b, slot});
+      }
       auto f = by_hash_.find(block_hash_[b]);
       if (f != by_hash_.end() && f->second == b) by_hash_.erase(f);
       block_hash_[b] = 0;
@@ -78,8 +82,24 @@ int BlockManager::match_prefix(const std::vector<int32_t>& tokens, int max_token
     const uint64_t h = chain_hash(prev, tokens.data() + i * block_size_, block_size_);
     auto it = by_hash_.find(h);
     if (it == by_hash_.end()) {
-      ++misses_;
-      break;
+      // HBM miss: the block may still be one tier down
+      const int slot = (mesh_ != nullptr && mesh_->contains(h)) ? mesh_->lookup(h) : -1;
+      const int nb = slot >= 0 ? take_block() : -1;
+      if (nb < 0) {
+        ++misses_;
+        break;
+      }
+      refcount_[nb] = 1;
+      block_uses_[nb] = 1;
+      block_hash_[nb] = h;
+      by_hash_[h] = nb;
+      restores_.push_back({nb, slot});
+      ++hits_;
+      table.push_back(nb);
+      hashes.push_back(h);
+      prev = h;
+      ++matched;
+      continue;
     }
     const int b = it->second;
     touch_lru(b);

@@ -16,6 +16,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include "cachemesh.h"
+
 namespace bloom {
 namespace rt {
 
@@ -66,6 +68,19 @@ class BlockManager {
   void reset_prefix_cache();
 
   PoolMetrics metrics() const;
+
+  // ---- CacheMesh (host / file tiers below the HBM prefix cache)
+  void set_cachemesh(CacheMesh* mesh) { mesh_ = mesh; }
+  CacheMesh* cachemesh() const { return mesh_; }
+  struct Copy {
+    int32_t block;
+    int32_t slot;
+  };
+  // Copies queued since the last call: HBM block -> host slot (evicted
+  // prefix blocks) and host slot -> HBM block (prefix restored from L2/L3).
+  // Restores must be issued before offloads (a slot may be reused).
+  std::vector<Copy> take_offloads() { return std::move(offloads_); }
+  std::vector<Copy> take_restores() { return std::move(restores_); }
   int refcount(int block) const { return refcount_[block]; }
 
   static uint64_t chain_hash(uint64_t prev, const int32_t* toks, int n);
@@ -86,6 +101,8 @@ class BlockManager {
   std::vector<std::list<int32_t>::iterator> lru_pos_;
   std::vector<uint8_t> in_lru_;
   int64_t hits_ = 0, misses_ = 0, evictions_ = 0, reuses_ = 0;
+  CacheMesh* mesh_ = nullptr;
+  std::vector<Copy> offloads_, restores_;
 };
 
 }  // namespace rt

@@ -76,6 +76,7 @@ bool Scheduler::is_stop(const Sequence& s, int32_t tok) const {
 
 StepMeta Scheduler::schedule() {
   if (arena_.base == nullptr) throw std::runtime_error("Scheduler: arena not set");
+  if (mesh_) mesh_->begin_step();
   StepMeta m;
   const int bs = bm_.block_size();
   const int ql = cfg_.spec_len > 0 ? cfg_.spec_len + 1 : 1;

@@ -166,6 +166,13 @@ class Scheduler {
   bool set_tail(int64_t id, int keep_len, const std::vector<int32_t>& tail);
 
   BlockManager& blocks() { return bm_; }
+  // Host (L2) and file (L3) tiers under the prefix cache; l2_base holds
+  // cfg.l2_slots * cfg.block_bytes bytes of pinned memory owned by the caller.
+  void enable_cachemesh(const CacheMeshConfig& cfg, uint8_t* l2_base) {
+    mesh_ = std::make_unique<CacheMesh>(cfg, l2_base);
+    bm_.set_cachemesh(mesh_.get());
+  }
+  CacheMesh* cachemesh() { return mesh_.get(); }
   const Sequence* find(int64_t id) const;
   const SchedulerConfig& config() const { return cfg_; }
   int64_t total_preemptions() const { return total_preemptions_; }
@@ -189,6 +196,7 @@ class Scheduler {
 
   SchedulerConfig cfg_;
   BlockManager bm_;
+  std::unique_ptr<CacheMesh> mesh_;
   Arena arena_;
   std::vector<int> buckets_;
   std::unordered_map<int64_t, std::unique_ptr<Sequence>> seqs_;

@@ -38,7 +38,7 @@ def _check_greedy(cfg, w, prompt, generated):
         assert gap <= 0.03 * spread + 1e-4, f"step {j}: token {tok} gap {gap} spread {spread}"
 
 
-@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-moe"])
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen3", "tiny-qwen2", "tiny-moe", "tiny-hd64"])
 @pytest.mark.parametrize("graphs", [False, True])
 def test_engine_greedy_matches_reference(name, graphs):
     from bloom_b200.engine.engine import SamplingParams
@@ -224,3 +224,34 @@ def test_speculation_sampled_runs():
         assert len(o[0].token_ids) == 16 and all(0 <= t < cfg.vocab_size for t in o[0].token_ids)
         outs.append(o[0].token_ids)
     assert outs[0] == outs[1]
+
+
+def test_cachemesh_restores_evicted_prefix(tmp_path):
+    """Prefix blocks evicted from HBM come back from pinned host memory (L2)
+    or files (L3) and give the same greedy continuation."""
+    from bloom_b200.engine.engine import EngineConfig, LLMEngine, SamplingParams
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.llama import DecoderLM
+    from bloom_b200.models.reference import random_weights
+
+    cfg = preset("tiny-llama")
+    w = random_weights(cfg, seed=3, std=0.08, device="cuda")
+    m = DecoderLM(cfg, device="cuda")
+    m.shard_full(w)
+    from bloom_b200.engine.runner import kv_block_bytes
+
+    eng = LLMEngine(m, EngineConfig(max_num_seqs=4, max_num_batched_tokens=256, max_model_len=256, num_blocks=12,
+                                    use_cuda_graphs=False, autotune=False,
+                                    cachemesh_l2_bytes=3 * kv_block_bytes(m), cachemesh_l3_dir=str(tmp_path),
+                                    cachemesh_l3_blocks=64))
+    torch.manual_seed(9)
+    sp = SamplingParams(max_tokens=6, temperature=0.0, ignore_eos=True)
+    a = torch.randint(3, cfg.vocab_size, (70,)).tolist()
+    first = eng.generate([a], sp)[0].token_ids
+    for _ in range(4):  # fill HBM with other prompts: A's cached blocks are evicted
+        eng.generate([torch.randint(3, cfg.vocab_size, (70,)).tolist()], sp)
+    again = eng.generate([a], sp)[0]
+    mesh = eng.kv_metrics()["cachemesh"]
+    assert mesh["offloads"] > 0 and mesh["l2_hits"] + mesh["l3_hits"] > 0, mesh
+    assert again.token_ids == first
+    assert eng.runner.stats["kv_restores"] > 0

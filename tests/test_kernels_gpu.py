@@ -120,9 +120,10 @@ def _make_cache(L, NB, KVH, D=128):
 
 
 @pytest.mark.parametrize("qk_norm", [False, True])
-def test_rope_kv_write(qk_norm):
+@pytest.mark.parametrize("D", [128, 64])
+def test_rope_kv_write(qk_norm, D):
     ops, ref = _ops(), _ref()
-    T, nq, nkv, D = 19, 4, 2, 128
+    T, nq, nkv = 19, 4, 2
     cache = torch.zeros(2, 8, 2, nkv, 16, D, device="cuda", dtype=torch.bfloat16)
     qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda", dtype=torch.bfloat16)
     pos = torch.randint(0, 500, (T,), device="cuda", dtype=torch.int64)
@@ -152,11 +153,12 @@ def test_rope_kv_write(qk_norm):
 @pytest.mark.parametrize("nq,nkv,q_len", [(32, 8, 1), (8, 8, 1), (16, 2, 1), (32, 8, 4), (8, 1, 4), (8, 1, 5),
                                           (32, 8, 5), (64, 8, 3)])
 @pytest.mark.parametrize("splits", [1, 3])
-def test_paged_decode_attention(nq, nkv, q_len, splits):
+@pytest.mark.parametrize("D", [128, 64])
+def test_paged_decode_attention(nq, nkv, q_len, splits, D):
     ops, ref = _ops(), _ref()
     torch.manual_seed(1)
-    L, NB, D, MB = 2, 300, 128, 64
-    cache = _make_cache(L, NB, nkv)
+    L, NB, MB = 2, 300, 64
+    cache = _make_cache(L, NB, nkv, D)
     lens = [1, 17, 200, 513, 35, 1000][: 4 if q_len > 1 else 6]
     lens = [max(l, q_len) for l in lens]
     B = len(lens)
@@ -180,12 +182,13 @@ def test_paged_decode_attention(nq, nkv, q_len, splits):
 
 
 @pytest.mark.parametrize("causal", [True, False])
-def test_paged_prefill_attention(causal):
+@pytest.mark.parametrize("D", [128, 64])
+def test_paged_prefill_attention(causal, D):
     ops, ref = _ops(), _ref()
     torch.manual_seed(2)
-    L, NB, D, MB = 1, 200, 128, 64
+    L, NB, MB = 1, 200, 64
     nq, nkv = 8, 2
-    cache = _make_cache(L, NB, nkv)
+    cache = _make_cache(L, NB, nkv, D)
     # (prefix already cached, new query tokens)
     seqs = [(0, 5), (0, 64), (32, 100), (16, 1), (100, 250)]
     Sp = len(seqs)

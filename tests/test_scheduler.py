@@ -255,3 +255,55 @@ def test_many_requests_complete(rt):
                 done.add(e[0])
     assert done == set(ids)
     assert s.kv_metrics()["active_blocks"] == 0
+
+
+def test_cachemesh_offload_restore_and_l3(rt, tmp_path):
+    """Evicted prefix blocks go to host slots (L2), spill to files (L3) and come
+    back on a later prefix hit; the scheduler queues the copies for the runner."""
+    s, arena, mb = make(rt, num_blocks=6, max_seqs=4, budget=64, prefix=True)
+    bb = 64
+    l2 = torch.zeros(2 * bb, dtype=torch.uint8)  # two host slots
+    s.enable_cachemesh(l2, bb, str(tmp_path), 8, "unit")
+    import collections
+
+    hbm = collections.defaultdict(lambda: torch.zeros(bb, dtype=torch.uint8))  # simulated device blocks
+
+    def step():
+        m = s.schedule()
+        for blk, slot in s.take_restores():  # host -> device first
+            hbm[blk] = l2[slot * bb:(slot + 1) * bb].clone()
+        for blk, slot in s.take_offloads():
+            l2[slot * bb:(slot + 1) * bb] = hbm[blk]
+        # "forward": every block this step wrote gets a pattern of its first token
+        ev = s.update(torch.full((max(m.num_logits, 1),), 7, dtype=torch.int32), m.num_real_logits)
+        return m, ev
+
+    def run(prompt):
+        rid = s.add_request(prompt, params(rt, max_tokens=1))
+        while s.has_unfinished():
+            m, _ = step()
+        return rid
+
+    a = list(range(100, 133))  # two full blocks + 1
+    # device content of A's blocks = a recognisable pattern written at prefill
+    s.add_request(a, params(rt, max_tokens=1))
+    m = s.schedule()
+    assert not s.take_offloads() and not s.take_restores()
+    bt = region(arena, m.off_prefill_block_table, mb).tolist()
+    for j, blk in enumerate(bt[:3]):
+        hbm[blk] = torch.full((bb,), 10 + j, dtype=torch.uint8)
+    s.update(torch.full((m.num_logits,), 7, dtype=torch.int32), m.num_real_logits)
+    # other prompts evict A's cached blocks (6 HBM blocks in total)
+    for base in (200, 300, 400):
+        run(list(range(base, base + 33)))
+    mm = s.cachemesh_metrics()
+    assert mm["offloads"] >= 2 and mm["l3_writes"] >= 1  # 2 host slots: older blocks spilled to files
+    # A again: its two full blocks come back from L2 / L3 with their bytes
+    s.add_request(a, params(rt, max_tokens=1))
+    m = s.schedule()
+    rest = s.take_restores()
+    assert len(rest) == 2
+    for j, (blk, slot) in enumerate(rest):
+        assert int(l2[slot * bb]) == 10 + j
+    s.take_offloads()
+    assert s.cachemesh_metrics()["l2_hits"] + s.cachemesh_metrics()["l3_hits"] == 2
