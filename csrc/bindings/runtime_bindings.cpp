@@ -36,6 +36,7 @@ py::dict metrics_dict(const PoolMetrics& m) {
 void register_cpu_ops(py::module_& m);  // csrc/runtime/cpu_ops.cpp
 void register_gguf(py::module_& m);     // csrc/runtime/gguf.cpp
 void register_json(py::module_& m);     // csrc/runtime/json_dfa.cpp
+void register_plugin(py::module_& m);   // csrc/runtime/plugin_loader.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 host runtime: KV block manager, in-flight batching scheduler, CPU kernels";
@@ -249,4 +250,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_cpu_ops(m);
   register_gguf(m);
   register_json(m);
+  register_plugin(m);
 }
