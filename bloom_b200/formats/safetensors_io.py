@@ -137,6 +137,12 @@ def load_state_dict(model_dir: str, names: Optional[Iterable[str]] = None) -> Di
     return out
 
 
+def load_file(path: str) -> Dict[str, object]:
+    """All tensors of one .safetensors file."""
+    f = SafetensorsFile(path)
+    return {k: f.get(k) for k in f.keys()}
+
+
 def save_file(tensors: Dict[str, object], path: str, metadata: Optional[Dict[str, str]] = None) -> None:
     import torch
 

@@ -37,6 +37,7 @@ void register_cpu_ops(py::module_& m);  // csrc/runtime/cpu_ops.cpp
 void register_gguf(py::module_& m);     // csrc/runtime/gguf.cpp
 void register_json(py::module_& m);     // csrc/runtime/json_dfa.cpp
 void register_plugin(py::module_& m);   // csrc/runtime/plugin_loader.cpp
+void register_quantize(py::module_& m); // csrc/runtime/quantize.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 host runtime: KV block manager, in-flight batching scheduler, CPU kernels";
@@ -251,4 +252,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_gguf(m);
   register_json(m);
   register_plugin(m);
+  register_quantize(m);
 }
