@@ -372,3 +372,29 @@ def test_gguf_decoder_on_gpu_matches_oracle(tmp_path):
         for j, t in enumerate(o.token_ids):
             row = logits[len(pr) - 1 + j]
             assert (row.max() - row[t]).item() <= 0.03 * (row.max() - row.median()).item() + 1e-4
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 4096, 4096), (3000, 6272, 1024), (4096, 4736, 2048)])
+@pytest.mark.parametrize("epi", ["bf16", "swiglu", "resid"])
+def test_gemm_cta_pair_large_m(M, N, K, epi):
+    """Large unsplit GEMMs take the 2-CTA (cta_group::2) path: check it
+    against fp32, including ragged M / N edges."""
+    ops = _ops()
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    if epi == "swiglu":
+        N2 = (N // 32) * 32
+        w = w[:N2].contiguous()
+        out = ops.gemm(x, w, epi=ops.EPI_SWIGLU, splits=1)
+        g, u = ops.deinterleave_gate_up(w)
+        exp = torch.nn.functional.silu(x.float() @ g.float().t()) * (x.float() @ u.float().t())
+    elif epi == "resid":
+        r = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+        out = ops.gemm(x, w, epi=ops.EPI_RESIDUAL, resid=r, splits=1)
+        exp = x.float() @ w.float().t() + r.float()
+    else:
+        out = ops.gemm(x, w, splits=1)
+        exp = x.float() @ w.float().t()
+    assert rel_err(out, exp) < 1e-2
+    assert int(ops.status()[0].item()) == 0
