@@ -31,6 +31,8 @@ def build_parser():
     ap.add_argument("--model-id")
     ap.add_argument("--doctor", action="store_true")
     ap.add_argument("--doctor-format", choices=["text", "json"], default="text")
+    ap.add_argument("--comm", choices=["fused", "nccl"], default="fused",
+                    help="tensor-parallel collectives (torchrun launches): fused NVLink kernels or NCCL")
     ap.add_argument("--enable-ifb", action="store_true", default=True,
                     help="in-flight batching (always on for the GPU engine)")
     return ap
@@ -61,17 +63,42 @@ def main(argv=None) -> int:
         return 2
     from ..engine.pipeline import InferencePipeline
     from .app import ServerSettings, create_app
+    from .runtime import ServingRuntime, TPControl, follower_loop
 
+    tp_info, ctrl = None, None
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:  # launched by torchrun: tensor parallel over the ranks
+        from ..models.llama import TPInfo
+        from ..models.config import PRESETS, preset
+        from ..parallel.comm import Communicator, init_distributed
+        import torch
+        import torch.distributed as dist
+
+        rank, world, local = init_distributed("nccl")
+        dev = torch.device("cuda", local)
+        hidden = preset(args.model).hidden_size if args.model in PRESETS else 8192
+        comm = Communicator(rank, world, dev, dist.group.WORLD, mode=args.comm,
+                            max_tokens=max(args.context_size, 8192), hidden=hidden)
+        tp_info = TPInfo(rank=rank, size=world, group=dist.group.WORLD, comm=comm)
+        ctrl = TPControl()
     pipe = InferencePipeline.load(args.model, device=args.device, context_size=args.context_size,
                                   speculative=args.speculative, draft_model=args.draft_model,
                                   num_speculative_tokens=args.num_speculative_tokens,
-                                  max_num_seqs=max(4, args.max_concurrent))
+                                  max_num_seqs=max(4, args.max_concurrent), tp_info=tp_info)
+    if ctrl is not None and ctrl.rank != 0:
+        follower_loop(pipe.llm, ctrl)  # returns when rank 0 shuts down
+        return 0
     mid = args.model_id or os.path.basename(str(args.model).rstrip("/"))
-    app = create_app(pipe, ServerSettings(model_id=mid, api_keys=keys, context_size=pipe.context_size,
-                                          max_concurrent=args.max_concurrent, cors_origins=args.cors_origin))
+    settings = ServerSettings(model_id=mid, api_keys=keys, context_size=pipe.context_size,
+                              max_concurrent=args.max_concurrent, cors_origins=args.cors_origin)
+    runtime = ServingRuntime(pipe, mid, args.max_concurrent, ctrl=ctrl) if ctrl is not None else None
+    app = create_app(pipe, settings, runtime)
     import uvicorn
 
-    uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    try:
+        uvicorn.run(app, host=args.host, port=args.port, log_level="warning")
+    finally:
+        if runtime is not None:
+            runtime.shutdown()
     return 0
 
 

@@ -199,8 +199,11 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         if not isinstance(top_p, (int, float)) or not 0 < top_p <= 1:
             raise APIError(400, "top_p must be in (0, 1]", param="top_p")
         seed = d.get("seed")
+        mn = d.get("min_tokens", 0) or 0  # extension: no end-of-sequence before this many tokens
+        if not isinstance(mn, int) or mn < 0:
+            raise APIError(400, "min_tokens must be a non-negative integer", param="min_tokens")
         return SamplingParams(max_tokens=mt, temperature=float(temp), top_p=float(top_p), seed=seed,
-                              top_k=int(d.get("top_k", 0) or 0))
+                              top_k=int(d.get("top_k", 0) or 0), min_tokens=min(mn, mt))
 
     def stops(d: dict) -> List[str]:
         s = d.get("stop")
@@ -254,15 +257,23 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         params.stop_token_ids = list(set(params.stop_token_ids) | set(eos))
         return params
 
-    async def token_stream(msgs, params, stop_list, request: Request, raw_prompt: Optional[str] = None):
-        """Yields (delta_text, finished, reason); handles admission, cancellation, stop strings."""
+    async def token_stream(msgs, params, stop_list, request: Request, raw_prompt: Optional[str] = None,
+                           prompt_ids: Optional[List[int]] = None, counter: Optional[dict] = None):
+        """Yields (delta_text, finished, reason); handles admission, cancellation, stop strings.
+        `counter["tokens"]` (if given) counts generated tokens."""
         if not rt.try_acquire():
             raise APIError(429, "server is at capacity; retry shortly", "rate_limit_error",
                            headers={"Retry-After": "1"})
         metrics.in_flight += 1
         sub = None
         try:
-            ids = prompt_ids_for(msgs, raw_prompt)
+            if prompt_ids is not None:
+                ids = list(prompt_ids)
+                if len(ids) >= st.context_size:
+                    raise APIError(400, f"prompt has {len(ids)} tokens; the context window is {st.context_size}",
+                                   param="prompt", code="context_length_exceeded")
+            else:
+                ids = prompt_ids_for(msgs, raw_prompt)
             params.max_tokens = min(params.max_tokens, st.context_size - len(ids) - 1)
             with_eos(params)
             sub = rt.submit(ids, params, messages=None if rt.engine is not None else (raw_prompt or msgs),
@@ -275,6 +286,8 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                 item = await sub.queue.get()
                 if item.error:
                     raise APIError(500, item.error, "server_error")
+                if counter is not None and (item.token is not None or item.text):
+                    counter["tokens"] = counter.get("tokens", 0) + 1
                 delta = ""
                 if item.token is not None and item.token not in eos:
                     delta = detok.add(item.token)
@@ -437,15 +450,24 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         d = await body(request)
         check_model(d.get("model"))
         prompt = d.get("prompt")
-        if isinstance(prompt, list):
+        token_prompt = None
+        if isinstance(prompt, list) and prompt and all(isinstance(p, int) and not isinstance(p, bool) for p in prompt):
+            token_prompt = prompt  # OpenAI form: the prompt as token ids
+            vocab = getattr(getattr(pipeline, "cfg", None), "vocab_size", None)
+            if vocab and any(p < 0 or p >= vocab for p in token_prompt):
+                raise APIError(400, "prompt token id out of the vocabulary", param="prompt")
+            prompt = ""
+        elif isinstance(prompt, list):
             prompt = "".join(p for p in prompt if isinstance(p, str))
         if not isinstance(prompt, str):
-            raise APIError(400, "prompt must be a string", param="prompt")
+            raise APIError(400, "prompt must be a string or a list of token ids", param="prompt")
         params = sampling(d, 16)
         stop_list = stops(d)
         cid = "cmpl-" + uuid.uuid4().hex[:24]
         created = int(time.time())
-        gen = token_stream([{"role": "user", "content": prompt}], params, stop_list, request, raw_prompt=prompt)
+        counter = {"tokens": 0}
+        gen = token_stream([{"role": "user", "content": prompt}], params, stop_list, request, raw_prompt=prompt,
+                           prompt_ids=token_prompt, counter=counter)
         first = await gen.__anext__()
         ptoks = first["prompt_tokens"]
         if not d.get("stream"):
@@ -455,6 +477,7 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                 n += 1
                 if fin:
                     reason = r
+            n = counter["tokens"] or n
             metrics.tokens_generated += n
             return {"id": cid, "object": "text_completion", "created": created, "model": st.model_id,
                     "choices": [{"index": 0, "text": "".join(text), "logprobs": None, "finish_reason": reason}],

@@ -50,8 +50,45 @@ class Submission:
     messages: Any = None
 
 
+class TPControl:
+    """Keeps the engines of tensor-parallel ranks in lockstep.  Rank 0 (the
+    HTTP process) publishes, before every engine step, the requests it admits
+    and aborts; the other ranks apply the same calls in the same order (so the
+    replicated C++ schedulers assign the same ids and schedule the same rows)
+    and step with it.  Messages travel over a gloo (CPU) process group; an
+    idle rank 0 sends a heartbeat every second."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group if group is not None else dist.new_group(backend="gloo")
+        self.rank = dist.get_rank()
+
+    def exchange(self, msg=None):
+        obj = [msg]
+        self.dist.broadcast_object_list(obj, src=0, group=self.group)
+        return obj[0]
+
+
+def follower_loop(engine, ctrl: TPControl) -> None:
+    """Ranks > 0: apply rank 0's admissions / aborts and step in lockstep."""
+    while True:
+        msg = ctrl.exchange(None)
+        if msg.get("stop"):
+            return
+        for prompt, params in msg.get("add", []):
+            engine.add_request(prompt, params)
+        for rid in msg.get("abort", []):
+            engine.abort(rid)
+        if msg.get("step"):
+            for r in engine.step():
+                if r.finished:
+                    engine.requests.pop(r.request_id, None)
+
+
 class ServingRuntime:
-    def __init__(self, pipeline, model_id: str, max_concurrent: int = 4, metrics=None):
+    def __init__(self, pipeline, model_id: str, max_concurrent: int = 4, metrics=None, ctrl: Optional[TPControl] = None):
         self.pipe = pipeline
         self.model_id = model_id
         self.max_concurrent = max_concurrent
@@ -65,6 +102,7 @@ class ServingRuntime:
         self._stop = threading.Event()
         self._wake = threading.Event()
         self.ready = True
+        self.ctrl = ctrl
         self.engine = getattr(pipeline, "llm", None)
         self._thread = threading.Thread(target=self._loop, name="bloom-engine", daemon=True)
         self._thread.start()
@@ -109,6 +147,8 @@ class ServingRuntime:
         self._stop.set()
         self._wake.set()
         self._thread.join(timeout=10)
+        if self.ctrl is not None and self.engine is not None:
+            self.ctrl.exchange({"stop": True})
 
     # ------------------------------------------------------------ engine thread
     def _emit(self, sub: Submission, item: StreamItem) -> None:
@@ -124,7 +164,10 @@ class ServingRuntime:
         if self.engine is None:
             return self._loop_blocking()
         eng = self.engine
+        ctrl = self.ctrl
+        last_beat = time.time()
         while not self._stop.is_set():
+            msg = {"add": [], "abort": []}
             while True:
                 try:
                     rid = self._cancel.get_nowait()
@@ -134,6 +177,7 @@ class ServingRuntime:
                     sub = self._by_id.get(rid)
                 if sub is not None and sub.engine_rid is not None:
                     eng.abort(sub.engine_rid)
+                    msg["abort"].append(sub.engine_rid)
                     self._emit(sub, StreamItem(finished=True, reason="abort"))
                     self._finish(sub)
             while True:
@@ -151,10 +195,15 @@ class ServingRuntime:
                     self._emit(sub, StreamItem(finished=True, reason="error", error=str(e)))
                     self._finish(sub)
                     continue
+                msg["add"].append((list(sub.prompt_ids), sub.params))
                 sub.engine_rid = rid
                 with self._lock:
                     self._by_rid[rid] = sub
-            if not eng.has_unfinished():
+            msg["step"] = eng.has_unfinished()
+            if ctrl is not None and (msg["add"] or msg["abort"] or msg["step"] or time.time() - last_beat > 1.0):
+                ctrl.exchange(msg)  # the other ranks repeat these calls before the same step
+                last_beat = time.time()
+            if not msg["step"]:
                 self._wake.wait(timeout=0.05)
                 self._wake.clear()
                 continue
@@ -169,7 +218,11 @@ class ServingRuntime:
                     self._finish(sub)
                 continue
             now = time.time()
-            for r in outs:
+            seen = set()
+            for r in outs:  # a request appears once per token of the step (speculation: several)
+                if r.request_id in seen:
+                    continue
+                seen.add(r.request_id)
                 sub = self._by_rid.get(r.request_id)
                 if sub is None:
                     continue
@@ -177,8 +230,12 @@ class ServingRuntime:
                     sub.first_token_at = now
                     if self.metrics is not None:
                         self.metrics.observe_ttft(now - sub.created)
-                sub.n_tokens += 1
-                self._emit(sub, StreamItem(token=r.token_ids[-1], finished=r.finished, reason=r.finish_reason))
+                new = r.token_ids[sub.n_tokens:]
+                for j, tok in enumerate(new):
+                    last = j == len(new) - 1
+                    self._emit(sub, StreamItem(token=tok, finished=r.finished and last,
+                                               reason=r.finish_reason if last else None))
+                sub.n_tokens += len(new)
                 if r.finished:
                     eng.requests.pop(r.request_id, None)
                     self._finish(sub)
