@@ -217,7 +217,10 @@ def main():
     value = out_tokens / total_dev_s
     e2e = out_tokens / total_host_s
     line = {
-        "metric": "decode tok/s/box (max over ranks) & p50 TTFT, Llama-3-8B-shape bf16, TP=1/2/4/8",
+        "metric": ("decode tok/s/box (max over ranks) & p50 TTFT, Llama-3-8B-shape bf16, TP=1/2/4/8"
+                   if args.model == "llama3-8b" else
+                   f"decode tok/s/box (max over ranks) & p50 TTFT, {args.model} bf16, "
+                   f"{'EP' if cfg.is_moe else 'TP'}={world}"),
         "value": round(value, 1),
         "unit": "output tokens/s (whole box)",
         "n_gpus": world,
@@ -233,12 +236,15 @@ def main():
         "p90_ttft_ms": round(sorted(ttfts)[int(0.9 * (len(ttfts) - 1))], 1),
         "mean_tbt_ms": round(statistics.mean(tbts), 2) if tbts else None,
         "config": {
-            "model": f"{args.model} (hidden 4096, 32 layers, 32/8 heads, FFN 14336, vocab 128256)",
+            "model": (f"{args.model} (hidden {cfg.hidden_size}, {cfg.num_layers} layers, {cfg.num_heads}/"
+                      f"{cfg.num_kv_heads} heads, " + (f"{cfg.num_experts} experts top-{cfg.num_experts_per_tok} "
+                                                       f"FFN {cfg.moe_intermediate_size}" if cfg.is_moe else
+                                                       f"FFN {cfg.intermediate_size}") + f", vocab {cfg.vocab_size})"),
             "global_batch": args.requests,
             "seq_len": f"prompt U[{args.prompt_min},{args.prompt_max}] + {args.output_len} output",
-            "parallelism": f"tp{world}",
+            "parallelism": (f"ep{world}+tp{world}-attention" if cfg.is_moe and world > 1 else f"tp{world}"),
             "comm": args.comm if world > 1 else "none",
-            "step": "one full serving run of the 256-request workload",
+            "step": f"one full serving run of the {args.requests}-request workload",
             "cache": "inputs larger than L2 (16 GB weights / tp, tens of GB of KV pages per run)",
             "kv_block": 16,
             "max_num_batched_tokens": args.max_batched_tokens,

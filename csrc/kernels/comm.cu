@@ -111,8 +111,10 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return r;
 }
 
-// grid: one CTA per owned row (rows_per_rank CTAs); block: H/8 threads (one 16-byte vector each)
-__global__ void tp_allreduce_rmsnorm_kernel(const ARArgs a) {
+// grid: a fixed number of CTAs striding over the owned rows; block: H/8 threads
+// (one 16-byte vector each; up to 1024 threads at H = 8192, so the kernel is
+// held to the 64 registers a 1024-thread block can have)
+__global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs a) {
   __shared__ float red[33];
   __shared__ int ok_s, last_s;
   __shared__ uint32_t epoch_s;
