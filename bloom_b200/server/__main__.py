@@ -31,6 +31,8 @@ def build_parser():
     ap.add_argument("--model-id")
     ap.add_argument("--doctor", action="store_true")
     ap.add_argument("--doctor-format", choices=["text", "json"], default="text")
+    ap.add_argument("--models-dir", default=os.environ.get("BLOOM_MODELS_DIR"),
+                    help="catalog for /v1/model-management (list, preflight, switch, unload, remove)")
     ap.add_argument("--comm", choices=["fused", "nccl"], default="fused",
                     help="tensor-parallel collectives (torchrun launches): fused NVLink kernels or NCCL")
     ap.add_argument("--enable-ifb", action="store_true", default=True,
@@ -89,9 +91,13 @@ def main(argv=None) -> int:
         return 0
     mid = args.model_id or os.path.basename(str(args.model).rstrip("/"))
     settings = ServerSettings(model_id=mid, api_keys=keys, context_size=pipe.context_size,
-                              max_concurrent=args.max_concurrent, cors_origins=args.cors_origin)
+                              max_concurrent=args.max_concurrent, cors_origins=args.cors_origin,
+                              models_dir=args.models_dir)
     runtime = ServingRuntime(pipe, mid, args.max_concurrent, ctrl=ctrl) if ctrl is not None else None
     app = create_app(pipe, settings, runtime)
+    if ctrl is None:  # model switching re-loads on this process's device (not offered under tensor parallel)
+        app.state.model_loader = lambda path: InferencePipeline.load(
+            path, device=args.device, context_size=args.context_size, max_num_seqs=max(4, args.max_concurrent))
     import uvicorn
 
     try:

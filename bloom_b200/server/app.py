@@ -24,6 +24,7 @@ from __future__ import annotations
 import asyncio
 import base64
 import json
+import os
 import re
 import struct
 import time
@@ -90,15 +91,36 @@ class ResponseStore:
         return v
 
 
+class _Ref:
+    """Attribute proxy to a swappable object (the served pipeline / runtime)."""
+
+    def __init__(self, obj):
+        object.__setattr__(self, "_obj", obj)
+
+    def __getattr__(self, k):
+        return getattr(object.__getattribute__(self, "_obj"), k)
+
+    def __setattr__(self, k, v):
+        setattr(object.__getattribute__(self, "_obj"), k, v)
+
+    def swap(self, obj) -> None:
+        object.__setattr__(self, "_obj", obj)
+
+    def get(self):
+        return object.__getattribute__(self, "_obj")
+
+
 class ServerSettings:
     def __init__(self, model_id: str = "model", api_keys: Optional[List[str]] = None, context_size: int = 2048,
-                 max_concurrent: int = 4, allow_non_loopback: bool = False, cors_origins: Optional[List[str]] = None):
+                 max_concurrent: int = 4, allow_non_loopback: bool = False, cors_origins: Optional[List[str]] = None,
+                 models_dir: Optional[str] = None):
         self.model_id = model_id
         self.api_keys = list(api_keys or [])
         self.context_size = context_size
         self.max_concurrent = max_concurrent
         self.allow_non_loopback = allow_non_loopback
         self.cors_origins = cors_origins or []
+        self.models_dir = models_dir if models_dir is not None else os.environ.get("BLOOM_MODELS_DIR")
 
 
 def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Optional[ServingRuntime] = None) -> FastAPI:
@@ -106,12 +128,16 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
     metrics = Metrics()
     rt = runtime or ServingRuntime(pipeline, st.model_id, st.max_concurrent, metrics)
     rt.metrics = metrics
+    # model management swaps the served pipeline / runtime behind these handles
+    pipeline = _Ref(pipeline)
+    rt = _Ref(rt)
     store = ResponseStore()
     app = FastAPI(title="bloom_b200", version=SERVER_VERSION, docs_url=None, redoc_url=None, openapi_url=None)
     app.state.runtime = rt
     app.state.metrics = metrics
     started = time.time()
-    is_embedding = getattr(pipeline, "is_embedding", False)
+    def is_embedding() -> bool:
+        return bool(getattr(pipeline, "is_embedding", False))
 
     # ------------------------------------------------------------ middleware
     @app.middleware("http")
@@ -261,6 +287,8 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                            prompt_ids: Optional[List[int]] = None, counter: Optional[dict] = None):
         """Yields (delta_text, finished, reason); handles admission, cancellation, stop strings.
         `counter["tokens"]` (if given) counts generated tokens."""
+        if not state["loaded"]:
+            raise APIError(503, "no model is loaded (model management unloaded it)", "server_error")
         if not rt.try_acquire():
             raise APIError(429, "server is at capacity; retry shortly", "rate_limit_error",
                            headers={"Retry-After": "1"})
@@ -325,7 +353,7 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                 "minimum_ui_protocol_version": READINESS_VERSION, "maximum_ui_protocol_version": READINESS_VERSION,
                 "server_version": SERVER_VERSION, "status": "ready" if ok else "busy", "progress": 100,
                 "model": st.model_id, "loading": False, "load_error": None,
-                "input_modalities": ["Text"], "model_tasks": ["embedding"] if is_embedding else ["chat", "completion"],
+                "input_modalities": ["Text"], "model_tasks": ["embedding"] if is_embedding() else ["chat", "completion"],
                 "context_window": st.context_size, "in_flight_requests": rt.in_flight,
                 "available_permits": rt.available_permits, "memory_pressure_high": False,
                 "ram_utilization": _ram_utilization()}
@@ -375,7 +403,7 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
     # ------------------------------------------------------------ chat / completions
     @app.post("/v1/chat/completions")
     async def chat(request: Request):
-        if is_embedding:
+        if is_embedding():
             raise APIError(400, "the loaded model is an embedding model", param="model")
         d = await body(request)
         check_model(d.get("model"))
@@ -445,7 +473,7 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
 
     @app.post("/v1/completions")
     async def completions(request: Request):
-        if is_embedding:
+        if is_embedding():
             raise APIError(400, "the loaded model is an embedding model", param="model")
         d = await body(request)
         check_model(d.get("model"))
@@ -582,7 +610,7 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
 
     # ------------------------------------------------------------ embeddings / rerank
     def embed(texts: List[str], dims: Optional[int] = None) -> List[List[float]]:
-        if not is_embedding:
+        if not is_embedding():
             raise APIError(400, "the loaded model does not produce embeddings", param="model")
         return pipeline.embedder.embed(texts, dimensions=dims)
 
@@ -628,6 +656,100 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         return {"object": "list", "model": st.model_id, "results": res}
 
     # ------------------------------------------------------------ Ollama adapter
+    # ------------------------------------------------------------ model management (operator API)
+    from .catalog import ModelCatalog
+
+    catalog = ModelCatalog(st.models_dir)
+    state = {"loaded": True}
+
+    def require_catalog():
+        if catalog.root is None:
+            raise APIError(404, "no models directory is configured (--models-dir / BLOOM_MODELS_DIR)",
+                           "not_found_error")
+
+    @app.get("/v1/model-management/models")
+    async def mm_list():
+        require_catalog()
+        return {"object": "list", "data": catalog.entries(), "active": st.model_id if state["loaded"] else None}
+
+    @app.post("/v1/model-management/preflight")
+    async def mm_preflight(request: Request):
+        require_catalog()
+        d = await body(request)
+        try:
+            return catalog.preflight(str(d.get("model", "")), int(d.get("context_size", st.context_size)),
+                                     int(d.get("max_concurrent", st.max_concurrent)), int(d.get("tp", 1)))
+        except KeyError:
+            raise APIError(404, f"model {d.get('model')!r} is not in the catalog", "not_found_error", "model",
+                           "model_not_found")
+
+    @app.post("/v1/model-management/switch")
+    async def mm_switch(request: Request):
+        require_catalog()
+        d = await body(request)
+        e = catalog.find(str(d.get("model", "")))
+        if e is None or not e.get("valid"):
+            raise APIError(404, f"model {d.get('model')!r} is not a loadable catalog entry", "not_found_error",
+                           "model", "model_not_found")
+        loader = getattr(app.state, "model_loader", None)
+        if loader is None:
+            raise APIError(501, "this server was started without a model loader", "server_error")
+        if rt.in_flight:
+            raise APIError(409, "requests are in flight; retry when idle", "conflict")
+        import asyncio
+
+        new_pipe = await asyncio.get_running_loop().run_in_executor(None, loader, e["path"])
+        old = rt.get()
+        st.model_id = str(e["id"])
+        st.context_size = int(getattr(new_pipe, "context_size", st.context_size))
+        new_rt = ServingRuntime(new_pipe, st.model_id, st.max_concurrent, metrics)
+        pipeline.swap(new_pipe)
+        rt.swap(new_rt)
+        state["loaded"] = True
+        old.shutdown()
+        return {"status": "switched", "model": st.model_id}
+
+    @app.post("/v1/model-management/unload")
+    async def mm_unload():
+        if rt.in_flight:
+            raise APIError(409, "requests are in flight; retry when idle", "conflict")
+        state["loaded"] = False
+        return {"status": "unloaded", "model": st.model_id}
+
+    @app.delete("/v1/model-management/models/{model_id}")
+    async def mm_remove(model_id: str, confirm: bool = False):
+        require_catalog()
+        if not confirm:
+            raise APIError(400, "removing model files needs ?confirm=true", param="confirm")
+        if model_id == st.model_id and state["loaded"]:
+            raise APIError(409, "the active model cannot be removed; switch or unload first", "conflict")
+        try:
+            catalog.remove(model_id)
+        except KeyError:
+            raise APIError(404, f"model {model_id!r} is not in the catalog", "not_found_error", "model",
+                           "model_not_found")
+        return {"status": "removed", "model": model_id}
+
+    @app.post("/api/pull")
+    async def ollama_pull(request: Request):
+        return _ollama_error(APIError(501, "model downloads are not available in this offline build; copy the "
+                                           "model package into the models directory instead"))
+
+    @app.delete("/api/delete")
+    async def ollama_delete(request: Request):
+        try:
+            require_catalog()
+            d = await body(request)
+            name = str(d.get("model") or d.get("name") or "")
+            if name == st.model_id and state["loaded"]:
+                raise APIError(409, "the active model cannot be removed")
+            catalog.remove(name)
+        except APIError as e:
+            return _ollama_error(e)
+        except KeyError:
+            return _ollama_error(APIError(404, f"model '{name}' not found"))
+        return JSONResponse({})
+
     @app.get("/api/version")
     async def o_version():
         return {"version": SERVER_VERSION}

@@ -252,3 +252,15 @@ def test_cli_cpu_generation(tiny_gguf, capsys):
     rc = main(["--model", p, "--device", "cpu", "--prompt", "hi", "--max-tokens", "4", "--temperature", "0",
                "--raw", "--quiet"])
     assert rc == 0
+
+
+def test_inspect_gguf_cli(tiny_gguf, capsys):
+    from bloom_b200.cli.inspect_gguf import main
+
+    cfg, w, p = tiny_gguf
+    assert main([p, "--json", "--limit", "3"]) == 0
+    d = json.loads(capsys.readouterr().out)
+    assert d["architecture"] == "llama" and d["version"] == 3 and len(d["tensors"]) == 3
+    assert d["tensor_count"] > 3 and d["primary_dtype"] == "Q8_0"
+    assert main([p]) == 0 and "GGUF v3" in capsys.readouterr().out
+    assert main([p + ".missing"]) == 1

@@ -191,3 +191,37 @@ def test_embeddings_and_rerank():
         e = c.post("/api/embed", json={"model": "mini", "input": ["a", "b"]}).json()
         assert len(e["embeddings"]) == 2
         assert c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}]}).status_code == 400
+
+
+def test_model_management(tmp_path):
+    """Catalog list / preflight / switch / unload / remove on a models directory."""
+    from bloom_b200.formats.gguf import GGML_Q8_0, write_decoder_gguf
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.reference import random_weights
+
+    cfg = preset("tiny-llama")
+    write_decoder_gguf(str(tmp_path / "tiny.gguf"), cfg, random_weights(cfg, seed=0, std=0.08), GGML_Q8_0)
+    (tmp_path / "broken").mkdir()
+    (tmp_path / "spare.gguf").write_bytes((tmp_path / "tiny.gguf").read_bytes())
+    app = create_app(EchoPipeline(), ServerSettings(model_id="echo", models_dir=str(tmp_path)))
+    from bloom_b200.engine.pipeline import InferencePipeline
+
+    app.state.model_loader = lambda path: InferencePipeline.load(path, device="cpu", context_size=256)
+    with TestClient(app) as c:
+        d = c.get("/v1/model-management/models").json()
+        ids = {e["id"]: e for e in d["data"]}
+        assert ids["tiny.gguf"]["valid"] and ids["tiny.gguf"]["primary_dtype"] == "Q8" and not ids["broken"]["valid"]
+        pf = c.post("/v1/model-management/preflight", json={"model": "tiny.gguf", "context_size": 256}).json()
+        assert pf["fits"] is True and pf["model"] == "tiny.gguf"
+        assert c.post("/v1/model-management/preflight", json={"model": "nope"}).status_code == 404
+        r = c.post("/v1/model-management/switch", json={"model": "tiny.gguf"})
+        assert r.status_code == 200 and r.json()["model"] == "tiny.gguf"
+        out = c.post("/v1/completions", json={"prompt": "hi", "max_tokens": 3, "temperature": 0}).json()
+        assert out["model"] == "tiny.gguf" and out["usage"]["completion_tokens"] >= 1
+        assert c.delete("/v1/model-management/models/tiny.gguf?confirm=true").status_code == 409
+        assert c.delete("/v1/model-management/models/spare.gguf").status_code == 400
+        assert c.delete("/v1/model-management/models/spare.gguf?confirm=true").json()["status"] == "removed"
+        assert not (tmp_path / "spare.gguf").exists()
+        assert c.post("/v1/model-management/unload").json()["status"] == "unloaded"
+        assert c.post("/v1/completions", json={"prompt": "hi", "max_tokens": 3}).status_code == 503
+        assert c.post("/api/pull", json={"model": "x"}).status_code == 501
