@@ -6,6 +6,7 @@ the call raises.  The fp32 oracles for tests live in `bloom_b200.ops.reference`.
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, Optional
 
 import torch
@@ -384,15 +385,22 @@ def paged_decode_attention(q, kv_cache, layer, block_table, seq_lens, out, *, q_
     return out
 
 
+_PREFILL_TC = os.environ.get("BLOOM_PREFILL_TC", "1") != "0"
+
+
 def paged_prefill_attention(q, kv_cache, layer, block_table, ctx_lens, cu_seqlens_q, tile_seq, tile_start, out, *,
                             scale: float, causal: bool = True):
-    _C().paged_prefill_attention(q, kv_cache, layer, block_table, ctx_lens, cu_seqlens_q, tile_seq, tile_start, out,
-                                 scale, causal, status(q.device.index))
+    """Causal (or full) attention of chunked-prefill query rows over the paged
+    cache; tiles are 128 query rows (see `prefill_tiles`).  head_dim 128 runs
+    on tcgen05 (S and O in TMEM), head_dim 64 on the mma.sync kernel."""
+    fn = _C().paged_prefill_attention_tc if (_PREFILL_TC and q.shape[-1] == 128) else _C().paged_prefill_attention
+    fn(q, kv_cache, layer, block_table, ctx_lens, cu_seqlens_q, tile_seq, tile_start, out, scale, causal,
+       status(q.device.index))
     _count()
     return out
 
 
-def prefill_tiles(cu_seqlens_q, ctx_lens, tile_rows: int = 64):
+def prefill_tiles(cu_seqlens_q, ctx_lens, tile_rows: int = 128):
     """Host helper: (tile_seq, tile_start) int32 lists for paged_prefill_attention."""
     seqs, starts, ext = [], [], []
     cu = [int(v) for v in cu_seqlens_q]

@@ -30,6 +30,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_prefill_attention", &bloom::paged_prefill_attention);
   m.def("decode_attention_splits", &bloom::decode_attention_splits);
   m.def("decode_head_chunks", &bloom::decode_head_chunks);
+  m.def("paged_prefill_attention_tc", &bloom::paged_prefill_attention_tc);
   m.def("argmax_rows", &bloom::argmax_rows);
   m.def("sample_rows", &bloom::sample_rows);
   m.def("verify_sample_rows", &bloom::verify_sample_rows);

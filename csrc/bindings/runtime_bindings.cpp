@@ -38,6 +38,7 @@ void register_gguf(py::module_& m);     // csrc/runtime/gguf.cpp
 void register_json(py::module_& m);     // csrc/runtime/json_dfa.cpp
 void register_plugin(py::module_& m);   // csrc/runtime/plugin_loader.cpp
 void register_quantize(py::module_& m); // csrc/runtime/quantize.cpp
+void register_admission(py::module_& m); // csrc/runtime/admission.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 host runtime: KV block manager, in-flight batching scheduler, CPU kernels";
@@ -253,4 +254,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_json(m);
   register_plugin(m);
   register_quantize(m);
+  register_admission(m);
 }

@@ -67,6 +67,13 @@ void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cac
                              const torch::Tensor& cu_seqlens_q, const torch::Tensor& tile_seq,
                              const torch::Tensor& tile_start, torch::Tensor& out, double scale, bool causal,
                              const torch::Tensor& status);
+// Same contract on tcgen05 (S and O in TMEM), head_dim 128, 128-row tiles
+// (tile_start in steps of 128 within a sequence).
+void paged_prefill_attention_tc(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                                const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
+                                const torch::Tensor& cu_seqlens_q, const torch::Tensor& tile_seq,
+                                const torch::Tensor& tile_start, torch::Tensor& out, double scale, bool causal,
+                                const torch::Tensor& status);
 int64_t decode_attention_splits(int64_t batch, int64_t num_kv_heads, int64_t max_pages, int64_t device);
 // CTAs per KV head for decode/verify attention: the smallest divisor hc of
 // G = q heads per KV head with (G / hc) * q_len <= 32 (0 if none).

@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
   const int G = a.nq / a.nkv;
   const int kh = h / G;
   const int s_idx = a.tile_seq[tile];
-  const int row0 = a.tile_start[tile];
+  const int row0 = a.tile_start[tile] + kPfRows * blockIdx.z;  // 128-row tiles run as two 64-row halves
   const int q_begin = a.cu_q[s_idx];
   const int q_len = a.cu_q[s_idx + 1] - q_begin;
   const int ctx = a.ctx_lens[s_idx];
@@ -711,9 +711,9 @@ void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cac
     configured |= uint64_t(1) << dev;
   }
   if (hd == 128)
-    attn::prefill_kernel<128><<<dim3(n_tiles, a.nq), attn::kPfWarps * 32, smem128, stream>>>(tm, a);
+    attn::prefill_kernel<128><<<dim3(n_tiles, a.nq, 2), attn::kPfWarps * 32, smem128, stream>>>(tm, a);
   else
-    attn::prefill_kernel<64><<<dim3(n_tiles, a.nq), attn::kPfWarps * 32, smem64, stream>>>(tm, a);
+    attn::prefill_kernel<64><<<dim3(n_tiles, a.nq, 2), attn::kPfWarps * 32, smem64, stream>>>(tm, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

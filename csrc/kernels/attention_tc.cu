@@ -1,0 +1,414 @@
+// Paged prefill attention on the 5th-generation tensor cores (tcgen05).
+//
+// One CTA = 128 query rows of one q head (a 128-row prefill tile); KV in
+// 128-token tiles (8 pages) double-buffered through TMA.  Per KV tile:
+//   S = Q K^T      tcgen05.mma M=128 N=128 K=128, S accumulates in TMEM
+//   softmax        4 warps, thread t owns query row t: tcgen05.ld its S row,
+//                  online max / sum in the log2 domain, P = exp2(S - m) as bf16
+//                  into shared memory (the K-major A operand of the next MMA)
+//   O += P V       tcgen05.mma M=128 N=128 K=128, O stays in TMEM; V is read
+//                  as an MN-major B operand straight from the TMA tile
+// The running max is lazy (FlashAttention-4 style): O and the row sum are
+// rescaled only when a row's max grows by more than 8 (a factor 256 in the
+// exp2 domain, safe in fp32), so TMEM read-modify-writes of O are rare.
+//
+// Shared memory layout of a K or V tile: two 16 KB regions (head dims 0-63 and
+// 64-127) of 128 token rows x 128 bytes with the 128-byte swizzle; page p of
+// the tile lands at rows 16p..16p+15 (one 2 KB TMA box per region), so token
+// rows are uniformly 128 bytes apart across pages.
+//
+// Warp roles: warps 0-3 softmax and epilogue (thread 0 also issues the MMAs),
+// warp 4 TMA producer and TMEM owner.  Every wait is bounded (status bit +
+// return).  Reference behaviour: causal GQA attention over the paged cache
+// (scheduler/paged_cache.rs:565-748).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "bloom/common.cuh"
+#include "bloom/ops.h"
+#include "bloom/tma_host.h"
+
+namespace bloom {
+namespace attn_tc {
+
+constexpr int D = 128;
+constexpr int PAGE = 16;
+constexpr int kRows = 128;                 // query rows per CTA
+constexpr int kKv = 128;                   // kv tokens per tile
+constexpr int kRegion = kKv * 64 * 2;      // 16 KB: one 64-dim half of a K or V tile
+constexpr int kQBytes = kRows * D * 2;     // 32 KB
+constexpr int kPBytes = kRows * kKv * 2;   // 32 KB
+constexpr int kStageBytes = 4 * kRegion;   // K (2 regions) + V (2 regions) = 64 KB
+constexpr int kStages = 2;
+constexpr int kThreads = 160;
+constexpr int kSmem = kQBytes + kPBytes + kStages * kStageBytes + 256 + 1024;
+constexpr int kTmemCols = 256;             // S [0,128) + O [128,256)
+constexpr float kLazy = 8.f;               // rescale threshold (log2 units)
+
+struct Args {
+  const __nv_bfloat16* q;  // [T, nq, 128]
+  __nv_bfloat16* out;      // [T, nq, 128]
+  const int* block_table;
+  int bt_stride;
+  const int* ctx_lens;
+  const int* cu_q;
+  const int* tile_seq;
+  const int* tile_start;   // first query row of a 128-row tile (local to the sequence)
+  int nq, nkv;
+  float scale_log2;
+  int causal;
+  int* status;
+};
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// MN-major operand (the contiguous dimension is N): 64-element atoms of 8 K-rows.
+// lbo = byte stride between 64-element atoms along N, sbo = between 8-row groups along K.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+__host__ __device__ constexpr uint32_t idesc_bf16_bmn(int M, int N) { return umma_idesc_bf16(M, N) | (1u << 16); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier that also reports whether any softmax thread passed `pred`
+__device__ __forceinline__ bool named_sync_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmKV, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sP = smem + kQBytes;
+  uint8_t* sKV = sP + kPBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * kStageBytes);
+  uint64_t* full = bars;            // [kStages]
+  uint64_t* empty = bars + 2;       // [kStages]
+  uint64_t* s_done = bars + 4;
+  uint64_t* o_done = bars + 5;
+  uint64_t* drain = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int warp = warp_id(), lane = lane_id();
+  const int G = a.nq / a.nkv;
+  const int kh = h / G;
+  const int s_idx = a.tile_seq[tile];
+  const int row0 = a.tile_start[tile];
+  const int q_begin = a.cu_q[s_idx];
+  const int q_len = a.cu_q[s_idx + 1] - q_begin;
+  const int ctx = a.ctx_lens[s_idx];
+  const int* bt = a.block_table + (long)s_idx * a.bt_stride;
+  const int n_pages = (ctx + PAGE - 1) / PAGE;
+  const int last_row = min(row0 + kRows, q_len) - 1;
+  const int kv_end = a.causal ? min(ctx, ctx - q_len + last_row + 1) : ctx;
+  const int n_kt = (kv_end + kKv - 1) / kKv;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(s_done, 1);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tS = tmem_base, tO = tmem_base + 128;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      for (int j = 0; j < n_kt && ok; ++j) {
+        const int s = j % kStages;
+        if (!mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1u, abort_flag, a.status, kStatusAttnTimeout)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = sKV + s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+#pragma unroll 1
+        for (int pg = 0; pg < kKv / PAGE; ++pg) {
+          const int page = j * (kKv / PAGE) + pg;
+          const int blk = bt[page < n_pages ? page : 0];
+          const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
+          const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
+          tma_load_2d(st + pg * 2048, &tmKV, &full[s], 0, rowK);
+          tma_load_2d(st + kRegion + pg * 2048, &tmKV, &full[s], 64, rowK);
+          tma_load_2d(st + 2 * kRegion + pg * 2048, &tmKV, &full[s], 0, rowV);
+          tma_load_2d(st + 3 * kRegion + pg * 2048, &tmKV, &full[s], 64, rowV);
+        }
+        ++issued;
+      }
+      if (!ok) {  // wait (bounded) for the loads already in flight before leaving
+        for (int j = max(0, issued - kStages); j < issued; ++j) mbar_drain(&full[j % kStages], (j / kStages) & 1);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax warps
+    const int t = threadIdx.x;  // query row of the tile, = TMEM lane
+    const int lr = row0 + t;
+    const bool valid = lr < q_len;
+    // rows past the chunk keep a finite softmax (no masking) and are not stored
+    const int qpos = valid ? (a.causal ? ctx - q_len + lr : ctx - 1) : ctx - 1;
+    {  // Q row -> shared memory in the K-major SW128 layout (two 64-dim regions)
+      const uint4* src = reinterpret_cast<const uint4*>(a.q + ((long)(q_begin + (valid ? lr : 0)) * a.nq + h) * D);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
+        const int region = c >> 3, chunk = c & 7;
+        *reinterpret_cast<uint4*>(sQ + region * (kRows * 128) + t * 128 + ((chunk ^ (t & 7)) << 4)) = v;
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    named_sync_softmax();
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    constexpr uint32_t idS = umma_idesc_bf16(128, kKv);
+    constexpr uint32_t idO = idesc_bf16_bmn(128, D);
+    float m = -INFINITY, l = 0.f;
+    bool failed = false;
+    int j = 0;
+    for (; j < n_kt; ++j) {
+      const int s = j % kStages;
+      // ---- S = Q K^T (issued by thread 0 once the tile has landed)
+      if (t == 0) {
+        bool ok = mbar_wait(&full[s], (j / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t kb = smem_u32(sKV + s * kStageBytes);
+          const uint32_t qb = smem_u32(sQ);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ad = umma_desc_sw128(qb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
+            const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * kRegion) + 2 * (kk & 3);
+            umma_f16(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(s_done);
+        } else {
+          failed = true;
+        }
+      }
+      if (named_sync_or(failed)) {
+        failed = true;
+        break;
+      }
+      if (!mbar_wait(s_done, j & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
+      if (named_sync_or(failed)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      // ---- softmax of this row over the tile
+      float sv[kKv];
+#pragma unroll
+      for (int c = 0; c < kKv; c += 16) {
+        float v16[16];
+        tmem_ld_32x32b_x16(tS + lane_off + c, v16);
+        tmem_wait_ld();  // registers are valid only after the wait
+#pragma unroll
+        for (int q = 0; q < 16; ++q) sv[c + q] = v16[q];
+      }
+      const int kv0 = j * kKv;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKv; ++c) {
+        const int idx = kv0 + c;
+        float v = sv[c] * a.scale_log2;
+        if (idx > qpos || idx >= ctx) v = -INFINITY;
+        sv[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      // the previous P V must be done before P is rewritten and before O is rescaled
+      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
+      if (named_sync_or(failed)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const float m_new = fmaxf(m, mx);
+      const bool grow = (m_new > m + kLazy) || j == 0;
+      const float alpha = (grow && j > 0) ? exp2f(m - m_new) : 1.f;
+      if (__any_sync(0xffffffffu, grow && j > 0)) {  // warp-collective TMEM read-modify-write of O
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          float o16[16];
+          tmem_ld_32x32b_x16(tO + lane_off + c, o16);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o16[q] *= alpha;
+          tmem_st_32x32b_x16(tO + lane_off + c, o16);
+        }
+        tmem_wait_st();
+      }
+      if (grow) {
+        l *= alpha;
+        m = m_new;
+      }
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < kKv; c += 8) {
+        float p8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          p8[q] = exp2f(sv[c + q] - m);
+          ps += p8[q];
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(p8[0], p8[1]);
+        pk.y = pack_bf16x2(p8[2], p8[3]);
+        pk.z = pack_bf16x2(p8[4], p8[5]);
+        pk.w = pack_bf16x2(p8[6], p8[7]);
+        const int cc = c >> 3, region = cc >> 3, chunk = cc & 7;
+        *reinterpret_cast<uint4*>(sP + region * (kRows * 128) + t * 128 + ((chunk ^ (t & 7)) << 4)) = pk;
+      }
+      l += ps;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      named_sync_softmax();
+      // ---- O += P V
+      if (t == 0) {
+        tc_fence_after();
+        const uint32_t pb = smem_u32(sP);
+        const uint32_t vb = smem_u32(sKV + s * kStageBytes + 2 * kRegion);
+#pragma unroll
+        for (int kk = 0; kk < kKv / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(pb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
+          const uint64_t bd = umma_desc_sw128_mn(vb + kk * 16 * 128, kRegion, 1024);
+          umma_f16(tO, ad, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done);
+        umma_commit(&empty[s]);
+      }
+    }
+    if (!failed && n_kt > 0) {
+      if (!mbar_wait(o_done, (n_kt - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
+    }
+    if (named_sync_or(failed)) failed = true;
+    if (failed) {
+      if (t == 0) {  // let the tensor pipe finish what was issued before TMEM is freed
+        umma_commit(drain);
+        mbar_drain(drain, 0);
+      }
+    } else if (n_kt > 0) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = a.out + ((long)(q_begin + (valid ? lr : 0)) * a.nq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 16) {
+        float o16[16];
+        tmem_ld_32x32b_x16(tO + lane_off + c, o16);
+        tmem_wait_ld();
+        if (valid) {
+          uint4 w0, w1;
+          w0.x = pack_bf16x2(o16[0] * inv, o16[1] * inv);
+          w0.y = pack_bf16x2(o16[2] * inv, o16[3] * inv);
+          w0.z = pack_bf16x2(o16[4] * inv, o16[5] * inv);
+          w0.w = pack_bf16x2(o16[6] * inv, o16[7] * inv);
+          w1.x = pack_bf16x2(o16[8] * inv, o16[9] * inv);
+          w1.y = pack_bf16x2(o16[10] * inv, o16[11] * inv);
+          w1.z = pack_bf16x2(o16[12] * inv, o16[13] * inv);
+          w1.w = pack_bf16x2(o16[14] * inv, o16[15] * inv);
+          *reinterpret_cast<uint4*>(orow + c) = w0;
+          *reinterpret_cast<uint4*>(orow + c + 8) = w1;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace attn_tc
+
+void paged_prefill_attention_tc(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                                const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
+                                const torch::Tensor& cu_seqlens_q, const torch::Tensor& tile_seq,
+                                const torch::Tensor& tile_start, torch::Tensor& out, double scale, bool causal,
+                                const torch::Tensor& status) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(-1) == attn_tc::D,
+              "prefill_tc: q [T, nq, 128] bf16");
+  TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(5) == attn_tc::D && kv_cache.size(4) == attn_tc::PAGE &&
+                  kv_cache.is_contiguous(),
+              "prefill_tc: kv_cache [L, NB, 2, KVH, 16, 128]");
+  const int n_tiles = tile_seq.size(0);
+  if (n_tiles == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  attn_tc::Args a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_stride = block_table.stride(0);
+  a.ctx_lens = ctx_lens.data_ptr<int>();
+  a.cu_q = cu_seqlens_q.data_ptr<int>();
+  a.tile_seq = tile_seq.data_ptr<int>();
+  a.tile_start = tile_start.data_ptr<int>();
+  a.nq = q.size(-2);
+  a.nkv = kv_cache.size(3);
+  a.scale_log2 = float(scale * 1.4426950408889634);
+  a.causal = causal ? 1 : 0;
+  a.status = status.data_ptr<int>();
+  const uint64_t rows = (uint64_t)kv_cache.size(1) * 2 * kv_cache.size(3) * attn_tc::PAGE;
+  TORCH_CHECK(rows < (1ull << 31), "prefill_tc: kv_cache too many rows per layer for int32 TMA coordinates");
+  const auto* base = reinterpret_cast<const __nv_bfloat16*>(kv_cache.data_ptr()) + layer * kv_cache.stride(0);
+  const CUtensorMap tm = make_tmap_bf16_2d(base, attn_tc::D, rows, attn_tc::D * 2, 64, attn_tc::PAGE);
+  static uint64_t configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((configured >> dev) & 1u)) {
+    cudaFuncSetAttribute(attn_tc::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_tc::kSmem);
+    configured |= uint64_t(1) << dev;
+  }
+  attn_tc::prefill_tc_kernel<<<dim3(n_tiles, a.nq), attn_tc::kThreads, attn_tc::kSmem, stream>>>(tm, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bloom

@@ -174,7 +174,7 @@ StepMeta Scheduler::schedule() {
   int T_pref = 0;
   for (auto& p : prefills) T_pref += p.len;
   int ntiles = 0;
-  for (auto& p : prefills) ntiles += (p.len + 63) / 64;
+  for (auto& p : prefills) ntiles += (p.len + 127) / 128;  // 128 query rows per attention tile
   int nl_real = Bd * ql;
   for (auto& p : prefills)
     if (p.start + p.len == static_cast<int>(p.s->tokens.size())) ++nl_real;
@@ -287,7 +287,8 @@ StepMeta Scheduler::schedule() {
     std::copy(s->table.begin(), s->table.end(), pbt + static_cast<int64_t>(j) * mb);
     pctx[j] = p.start + p.len;
     pcu[j + 1] = pcu[j] + p.len;
-    for (int r = 0; r < p.len; r += 64) tiles.push_back({static_cast<int>(j), r, p.start + std::min(r + 64, p.len)});
+    for (int r = 0; r < p.len; r += 128)
+      tiles.push_back({static_cast<int>(j), r, p.start + std::min(r + 128, p.len)});
     s->num_computed = p.start + p.len;
     if (s->num_computed == static_cast<int>(s->tokens.size())) add_sample(s, t - 1, -1, 1, 0);
   }

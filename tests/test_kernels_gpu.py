@@ -398,3 +398,59 @@ def test_gemm_cta_pair_large_m(M, N, K, epi):
         exp = x.float() @ w.float().t()
     assert rel_err(out, exp) < 1e-2
     assert int(ops.status()[0].item()) == 0
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(256, 6144, 4096, 64), (200, 28672, 1024, 32), (96, 8192, 512, 32)])
+@pytest.mark.parametrize("epi", ["bf16", "swiglu"])
+def test_gemm_cta_pair_small_token_tiles(M, N, K, bn, epi):
+    """Decode-sized batches on the CTA-pair kernel with 32 / 64-token tiles."""
+    ops = _ops()
+    torch.manual_seed(3)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    if epi == "swiglu":
+        out = ops.gemm(x, w, epi=ops.EPI_SWIGLU, splits=1, bn=bn)
+        g, u = ops.deinterleave_gate_up(w)
+        exp = torch.nn.functional.silu(x.float() @ g.float().t()) * (x.float() @ u.float().t())
+    else:
+        out = ops.gemm(x, w, splits=1, bn=bn)
+        exp = x.float() @ w.float().t()
+    assert rel_err(out, exp) < 1e-2
+    assert int(ops.status()[0].item()) == 0
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_tc_matches_reference_long(causal):
+    """tcgen05 prefill attention (S/O in TMEM, lazy rescaling) on long chunks
+    with cached prefixes and GQA, against fp32 and the mma.sync kernel."""
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(5)
+    L, NB, D, MB = 1, 600, 128, 160
+    nq, nkv = 16, 4
+    cache = _make_cache(L, NB, nkv, D)
+    seqs = [(0, 700), (1000, 300), (37, 129), (0, 1), (500, 128)]
+    bt = torch.zeros(len(seqs), MB, dtype=torch.int32)
+    perm = torch.randperm(NB)
+    k, ctx, cu = 0, [], [0]
+    for j, (pre, ql) in enumerate(seqs):
+        c = pre + ql
+        nb = (c + 15) // 16
+        bt[j, :nb] = perm[k:k + nb]
+        k += nb
+        ctx.append(c)
+        cu.append(cu[-1] + ql)
+    q = torch.randn(cu[-1], nq, D, device="cuda", dtype=torch.bfloat16)
+    tseq, tstart = ops.prefill_tiles(cu, ctx)
+    args = (cache, 0, bt.cuda(), torch.tensor(ctx, dtype=torch.int32, device="cuda"),
+            torch.tensor(cu, dtype=torch.int32, device="cuda"), tseq.cuda(), tstart.cuda())
+    out_tc = torch.zeros_like(q)
+    out_mma = torch.zeros_like(q)
+    C = ops._C()
+    C.paged_prefill_attention_tc(q, *args, out_tc, 1 / math.sqrt(D), causal, ops.status())
+    C.paged_prefill_attention(q, *args, out_mma, 1 / math.sqrt(D), causal, ops.status())
+    for j, (pre, ql) in enumerate(seqs):
+        kk, vv = ref.gather_paged(cache, 0, bt[j].cuda(), ctx[j])
+        exp = ref.attention(q[cu[j]:cu[j + 1]], kk, vv, causal=causal, q_offset=pre, scale=1 / math.sqrt(D))
+        assert rel_err(out_tc[cu[j]:cu[j + 1]], exp) < 2e-2, j
+        assert rel_err(out_mma[cu[j]:cu[j + 1]], exp) < 2e-2, j
+    assert int(ops.status()[0].item()) == 0
