@@ -121,6 +121,10 @@ class ServerSettings:
         self.allow_non_loopback = allow_non_loopback
         self.cors_origins = cors_origins or []
         self.models_dir = models_dir if models_dir is not None else os.environ.get("BLOOM_MODELS_DIR")
+        # per-model token buckets (prompt + max_tokens per request), off unless BLOOM_RATE_LIMIT=1
+        self.rate_limit = os.environ.get("BLOOM_RATE_LIMIT", "0") == "1"
+        self.rate_limit_burst = float(os.environ.get("BLOOM_RATE_LIMIT_BURST", "32768"))
+        self.rate_limit_rate = float(os.environ.get("BLOOM_RATE_LIMIT_RATE", "200"))
 
 
 def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Optional[ServingRuntime] = None) -> FastAPI:
@@ -128,12 +132,16 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
     metrics = Metrics()
     rt = runtime or ServingRuntime(pipeline, st.model_id, st.max_concurrent, metrics)
     rt.metrics = metrics
+    from .._ext import runtime as _native
+
+    limiter = _native().RateLimiter(st.rate_limit, st.rate_limit_burst, st.rate_limit_rate)
     # model management swaps the served pipeline / runtime behind these handles
     pipeline = _Ref(pipeline)
     rt = _Ref(rt)
     store = ResponseStore()
     app = FastAPI(title="bloom_b200", version=SERVER_VERSION, docs_url=None, redoc_url=None, openapi_url=None)
     app.state.runtime = rt
+    app.state.rate_limiter = limiter
     app.state.metrics = metrics
     started = time.time()
     def is_embedding() -> bool:
@@ -289,6 +297,13 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         `counter["tokens"]` (if given) counts generated tokens."""
         if not state["loaded"]:
             raise APIError(503, "no model is loaded (model management unloaded it)", "server_error")
+        want = (len(prompt_ids) if prompt_ids is not None else 0) + int(getattr(params, "max_tokens", 0) or 0)
+        ok, wait = limiter.try_acquire(st.model_id, float(max(1, want)), time.monotonic())
+        if not ok:
+            import math
+
+            raise APIError(429, f"token rate limit exceeded for {st.model_id}; retry in {wait:.1f} s",
+                           "rate_limit_error", headers={"Retry-After": str(max(1, math.ceil(wait)))})
         if not rt.try_acquire():
             raise APIError(429, "server is at capacity; retry shortly", "rate_limit_error",
                            headers={"Retry-After": "1"})

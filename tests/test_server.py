@@ -225,3 +225,16 @@ def test_model_management(tmp_path):
         assert c.post("/v1/model-management/unload").json()["status"] == "unloaded"
         assert c.post("/v1/completions", json={"prompt": "hi", "max_tokens": 3}).status_code == 503
         assert c.post("/api/pull", json={"model": "x"}).status_code == 501
+
+
+def test_token_rate_limit(monkeypatch):
+    monkeypatch.setenv("BLOOM_RATE_LIMIT", "1")
+    monkeypatch.setenv("BLOOM_RATE_LIMIT_BURST", "100")
+    monkeypatch.setenv("BLOOM_RATE_LIMIT_RATE", "1")
+    app = create_app(EchoPipeline(), ServerSettings(model_id="echo"))
+    with TestClient(app) as c:
+        ok = c.post("/v1/completions", json={"prompt": "a", "max_tokens": 90})
+        assert ok.status_code == 200
+        r = c.post("/v1/completions", json={"prompt": "b", "max_tokens": 90})
+        assert r.status_code == 429 and int(r.headers["retry-after"]) >= 1
+        assert app.state.rate_limiter.throttled == 1
