@@ -17,8 +17,13 @@
 // the tile lands at rows 16p..16p+15 (one 2 KB TMA box per region), so token
 // rows are uniformly 128 bytes apart across pages.
 //
-// Warp roles: warps 0-3 softmax and epilogue (thread 0 also issues the MMAs),
-// warp 4 TMA producer and TMEM owner.  Every wait is bounded (status bit +
+// S is double-buffered in TMEM and K and V have separate TMA rings, so the
+// tensor cores compute S(j+1) = Q K(j+1)^T while the softmax warps work on
+// tile j, and P(j) V(j) runs while the next softmax starts.
+// Warp roles: warps 0-7 softmax and epilogue, two threads per query row
+// (warps w and w+4 read the same TMEM lanes, columns 0-63 and 64-127; the row
+// max and sum are combined through shared memory); thread 0 also issues the
+// MMAs; warp 8 is the TMA producer and TMEM owner.  Every wait is bounded (status bit +
 // return).  Reference behaviour: causal GQA attention over the paged cache
 // (scheduler/paged_cache.rs:565-748).
 #include <ATen/cuda/CUDAContext.h>
@@ -39,11 +44,12 @@ constexpr int kKv = 128;                   // kv tokens per tile
 constexpr int kRegion = kKv * 64 * 2;      // 16 KB: one 64-dim half of a K or V tile
 constexpr int kQBytes = kRows * D * 2;     // 32 KB
 constexpr int kPBytes = kRows * kKv * 2;   // 32 KB
-constexpr int kStageBytes = 4 * kRegion;   // K (2 regions) + V (2 regions) = 64 KB
-constexpr int kStages = 2;
-constexpr int kThreads = 160;
-constexpr int kSmem = kQBytes + kPBytes + kStages * kStageBytes + 256 + 1024;
-constexpr int kTmemCols = 256;             // S [0,128) + O [128,256)
+constexpr int kTileBytes = 2 * kRegion;    // one K or V tile = 32 KB
+constexpr int kStages = 2;                 // separate K and V rings of kStages tiles each
+constexpr int kSoftmaxThreads = 256;      // two threads per query row (64 columns each)
+constexpr int kThreads = kSoftmaxThreads + 32;
+constexpr int kSmem = kQBytes + kPBytes + 2 * kStages * kTileBytes + 256 + 1024;
+constexpr int kTmemCols = 512;             // S0 [0,128), S1 [128,256), O [256,384)
 constexpr float kLazy = 8.f;               // rescale threshold (log2 units)
 
 struct Args {
@@ -91,14 +97,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 // named barrier that also reports whether any softmax thread passed `pred`
 __device__ __forceinline__ bool named_sync_or(bool pred) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred pi, po;\n\t"
       "setp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.or.pred po, 1, 128, pi;\n\t"
+      "bar.red.or.pred po, 1, 256, pi;\n\t"
       "selp.u32 %0, 1, 0, po;\n\t}"
       : "=r"(r)
       : "r"(static_cast<uint32_t>(pred))
@@ -112,14 +118,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sP = smem + kQBytes;
-  uint8_t* sKV = sP + kPBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * kStageBytes);
-  uint64_t* full = bars;            // [kStages]
-  uint64_t* empty = bars + 2;       // [kStages]
-  uint64_t* s_done = bars + 4;
-  uint64_t* o_done = bars + 5;
-  uint64_t* drain = bars + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  uint8_t* sK = sP + kPBytes;                       // K ring
+  uint8_t* sV = sK + kStages * kTileBytes;          // V ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * kTileBytes);
+  uint64_t* fullK = bars;           // [kStages]
+  uint64_t* emptyK = bars + 2;
+  uint64_t* fullV = bars + 4;
+  uint64_t* emptyV = bars + 6;
+  uint64_t* s_done = bars + 8;      // [2]: one per S buffer
+  uint64_t* o_done = bars + 10;
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tile = blockIdx.x, h = blockIdx.y;
@@ -139,16 +148,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&fullK[s], 1);
+      mbar_init(&emptyK[s], 1);
+      mbar_init(&fullV[s], 1);
+      mbar_init(&emptyV[s], 1);
     }
-    mbar_init(s_done, 1);
+    mbar_init(&s_done[0], 1);
+    mbar_init(&s_done[1], 1);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -156,112 +168,136 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tS = tmem_base, tO = tmem_base + 128;
+  const uint32_t tO = tmem_base + 256;  // S buffers at tmem_base + 128 * (j % 2)
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       bool ok = true;
-      int issued = 0;
-      for (int j = 0; j < n_kt && ok; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1u, abort_flag, a.status, kStatusAttnTimeout)) {
+      int issuedK = 0, issuedV = 0;
+      auto load_tile = [&](int jt, uint8_t* dst, uint64_t* bar, int kv) {
+        mbar_arrive_expect_tx(bar, kTileBytes);
+#pragma unroll 1
+        for (int pg = 0; pg < kKv / PAGE; ++pg) {
+          const int page = jt * (kKv / PAGE) + pg;
+          const int blk = bt[page < n_pages ? page : 0];
+          const int row = ((blk * 2 + kv) * a.nkv + kh) * PAGE;
+          tma_load_2d(dst + pg * 2048, &tmKV, bar, 0, row);
+          tma_load_2d(dst + kRegion + pg * 2048, &tmKV, bar, 64, row);
+        }
+      };
+      for (int jt = 0; jt < n_kt && ok; ++jt) {
+        const int s = jt % kStages;
+        const uint32_t par = ((jt / kStages) & 1) ^ 1u;
+        if (!mbar_wait(&emptyK[s], par, abort_flag, a.status, kStatusAttnTimeout)) {
           ok = false;
           break;
         }
-        uint8_t* st = sKV + s * kStageBytes;
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
-#pragma unroll 1
-        for (int pg = 0; pg < kKv / PAGE; ++pg) {
-          const int page = j * (kKv / PAGE) + pg;
-          const int blk = bt[page < n_pages ? page : 0];
-          const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
-          const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
-          tma_load_2d(st + pg * 2048, &tmKV, &full[s], 0, rowK);
-          tma_load_2d(st + kRegion + pg * 2048, &tmKV, &full[s], 64, rowK);
-          tma_load_2d(st + 2 * kRegion + pg * 2048, &tmKV, &full[s], 0, rowV);
-          tma_load_2d(st + 3 * kRegion + pg * 2048, &tmKV, &full[s], 64, rowV);
+        load_tile(jt, sK + s * kTileBytes, &fullK[s], 0);
+        ++issuedK;
+        if (!mbar_wait(&emptyV[s], par, abort_flag, a.status, kStatusAttnTimeout)) {
+          ok = false;
+          break;
         }
-        ++issued;
+        load_tile(jt, sV + s * kTileBytes, &fullV[s], 1);
+        ++issuedV;
       }
       if (!ok) {  // wait (bounded) for the loads already in flight before leaving
-        for (int j = max(0, issued - kStages); j < issued; ++j) mbar_drain(&full[j % kStages], (j / kStages) & 1);
+        for (int jt = max(0, issuedK - kStages); jt < issuedK; ++jt)
+          mbar_drain(&fullK[jt % kStages], (jt / kStages) & 1);
+        for (int jt = max(0, issuedV - kStages); jt < issuedV; ++jt)
+          mbar_drain(&fullV[jt % kStages], (jt / kStages) & 1);
       }
     }
   } else {
     // ---------------------------------------------------------------- softmax warps
-    const int t = threadIdx.x;  // query row of the tile, = TMEM lane
+    __shared__ float red_m[kSoftmaxThreads], red_l[kSoftmaxThreads];
+    const int t = threadIdx.x & (kRows - 1);  // query row of the tile, = TMEM lane
+    const int half = threadIdx.x >> 7;        // columns [64 * half, 64 * half + 64)
+    const int cb = half * 64;
+    const bool leader = threadIdx.x == 0;     // issues the MMAs
     const int lr = row0 + t;
     const bool valid = lr < q_len;
     // rows past the chunk keep a finite softmax (no masking) and are not stored
     const int qpos = valid ? (a.causal ? ctx - q_len + lr : ctx - 1) : ctx - 1;
-    {  // Q row -> shared memory in the K-major SW128 layout (two 64-dim regions)
+    {  // this thread's half of the Q row -> shared memory, K-major SW128 (region = half)
       const uint4* src = reinterpret_cast<const uint4*>(a.q + ((long)(q_begin + (valid ? lr : 0)) * a.nq + h) * D);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
-        const int region = c >> 3, chunk = c & 7;
-        *reinterpret_cast<uint4*>(sQ + region * (kRows * 128) + t * 128 + ((chunk ^ (t & 7)) << 4)) = v;
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = valid ? src[half * 8 + c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sQ + half * (kRows * 128) + t * 128 + ((c ^ (t & 7)) << 4)) = v;
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     named_sync_softmax();
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     constexpr uint32_t idS = umma_idesc_bf16(128, kKv);
     constexpr uint32_t idO = idesc_bf16_bmn(128, D);
     float m = -INFINITY, l = 0.f;
     bool failed = false;
     int j = 0;
-    for (; j < n_kt; ++j) {
-      const int s = j % kStages;
-      // ---- S = Q K^T (issued by thread 0 once the tile has landed)
-      if (t == 0) {
-        bool ok = mbar_wait(&full[s], (j / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t kb = smem_u32(sKV + s * kStageBytes);
-          const uint32_t qb = smem_u32(sQ);
+    // S(jt) = Q K(jt)^T into S buffer jt % 2 (leader only)
+    auto issue_s = [&](int jt) -> bool {
+      const int sk = jt % kStages;
+      if (!mbar_wait(&fullK[sk], (jt / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout)) return false;
+      tc_fence_after();
+      const uint32_t kb = smem_u32(sK + sk * kTileBytes);
+      const uint32_t qb = smem_u32(sQ);
+      const uint32_t tS = tmem_base + 128u * static_cast<uint32_t>(jt & 1);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t ad = umma_desc_sw128(qb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
-            const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * kRegion) + 2 * (kk & 3);
-            umma_f16(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(s_done);
-        } else {
-          failed = true;
-        }
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint64_t ad = umma_desc_sw128(qb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
+        const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * kRegion) + 2 * (kk & 3);
+        umma_f16(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
       }
+      umma_commit(&s_done[jt & 1]);
+      umma_commit(&emptyK[sk]);
+      return true;
+    };
+    if (leader && n_kt > 0 && !issue_s(0)) failed = true;
+    for (; j < n_kt; ++j) {
+      // ---- S(j+1) on the tensor cores while this tile's softmax runs
+      if (leader && !failed && j + 1 < n_kt && !issue_s(j + 1)) failed = true;
       if (named_sync_or(failed)) {
         failed = true;
         break;
       }
-      if (!mbar_wait(s_done, j & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
+      if (!mbar_wait(&s_done[j & 1], (j >> 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
       if (named_sync_or(failed)) {
         failed = true;
         break;
       }
       tc_fence_after();
-      // ---- softmax of this row over the tile
-      float sv[kKv];
+      // ---- this thread's 64 columns of its row
+      float sv[64];
+      const uint32_t sbase = tmem_base + 128u * static_cast<uint32_t>(j & 1) + lane_off + cb;
 #pragma unroll
-      for (int c = 0; c < kKv; c += 16) {
+      for (int c = 0; c < 64; c += 16) {
         float v16[16];
-        tmem_ld_32x32b_x16(tS + lane_off + c, v16);
+        tmem_ld_32x32b_x16(sbase + c, v16);
         tmem_wait_ld();  // registers are valid only after the wait
 #pragma unroll
         for (int q = 0; q < 16; ++q) sv[c + q] = v16[q];
       }
-      const int kv0 = j * kKv;
+      const int kv0 = j * kKv + cb;
       float mx = -INFINITY;
+      if (kv0 + 63 <= qpos && kv0 + 63 < ctx) {  // the whole half is visible: no masking
 #pragma unroll
-      for (int c = 0; c < kKv; ++c) {
-        const int idx = kv0 + c;
-        float v = sv[c] * a.scale_log2;
-        if (idx > qpos || idx >= ctx) v = -INFINITY;
-        sv[c] = v;
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < 64; ++c) {
+          sv[c] *= a.scale_log2;
+          mx = fmaxf(mx, sv[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const int idx = kv0 + c;
+          float v = sv[c] * a.scale_log2;
+          if (idx > qpos || idx >= ctx) v = -INFINITY;
+          sv[c] = v;
+          mx = fmaxf(mx, v);
+        }
       }
+      red_m[threadIdx.x] = mx;
       // the previous P V must be done before P is rewritten and before O is rescaled
       if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
       if (named_sync_or(failed)) {
@@ -269,18 +305,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      mx = fmaxf(mx, red_m[threadIdx.x ^ 128]);  // the row max over both halves
       const float m_new = fmaxf(m, mx);
-      const bool grow = (m_new > m + kLazy) || j == 0;
+      const bool grow = (m_new > m + kLazy) || j == 0;  // identical in both threads of a row
       const float alpha = (grow && j > 0) ? exp2f(m - m_new) : 1.f;
       if (__any_sync(0xffffffffu, grow && j > 0)) {  // warp-collective TMEM read-modify-write of O
 #pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
+        for (int c = 0; c < 64; c += 16) {
           float o16[16];
-          tmem_ld_32x32b_x16(tO + lane_off + c, o16);
+          tmem_ld_32x32b_x16(tO + lane_off + cb + c, o16);
           tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 16; ++q) o16[q] *= alpha;
-          tmem_st_32x32b_x16(tO + lane_off + c, o16);
+          tmem_st_32x32b_x16(tO + lane_off + cb + c, o16);
         }
         tmem_wait_st();
       }
@@ -290,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float ps = 0.f;
 #pragma unroll
-      for (int c = 0; c < kKv; c += 8) {
+      for (int c = 0; c < 64; c += 8) {
         float p8[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -302,45 +339,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk.y = pack_bf16x2(p8[2], p8[3]);
         pk.z = pack_bf16x2(p8[4], p8[5]);
         pk.w = pack_bf16x2(p8[6], p8[7]);
-        const int cc = c >> 3, region = cc >> 3, chunk = cc & 7;
-        *reinterpret_cast<uint4*>(sP + region * (kRows * 128) + t * 128 + ((chunk ^ (t & 7)) << 4)) = pk;
+        const int chunk = c >> 3;
+        *reinterpret_cast<uint4*>(sP + half * (kRows * 128) + t * 128 + ((chunk ^ (t & 7)) << 4)) = pk;
       }
       l += ps;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       named_sync_softmax();
       // ---- O += P V
-      if (t == 0) {
-        tc_fence_after();
-        const uint32_t pb = smem_u32(sP);
-        const uint32_t vb = smem_u32(sKV + s * kStageBytes + 2 * kRegion);
+      if (leader) {
+        const int sv_ = j % kStages;
+        if (mbar_wait(&fullV[sv_], (j / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout)) {
+          tc_fence_after();
+          const uint32_t pb = smem_u32(sP);
+          const uint32_t vb = smem_u32(sV + sv_ * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < kKv / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(pb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
-          const uint64_t bd = umma_desc_sw128_mn(vb + kk * 16 * 128, kRegion, 1024);
-          umma_f16(tO, ad, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kKv / 16; ++kk) {
+            const uint64_t ad = umma_desc_sw128(pb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
+            const uint64_t bd = umma_desc_sw128_mn(vb + kk * 16 * 128, kRegion, 1024);
+            umma_f16(tO, ad, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(o_done);
+          umma_commit(&emptyV[sv_]);
+        } else {
+          failed = true;
         }
-        umma_commit(o_done);
-        umma_commit(&empty[s]);
       }
     }
     if (!failed && n_kt > 0) {
       if (!mbar_wait(o_done, (n_kt - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
     }
+    red_l[threadIdx.x] = l;
     if (named_sync_or(failed)) failed = true;
     if (failed) {
-      if (t == 0) {  // let the tensor pipe finish what was issued before TMEM is freed
+      if (leader) {  // let the tensor pipe finish what was issued before TMEM is freed
         umma_commit(drain);
         mbar_drain(drain, 0);
       }
     } else if (n_kt > 0) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = a.out + ((long)(q_begin + (valid ? lr : 0)) * a.nq + h) * D;
+      const float lt = l + red_l[threadIdx.x ^ 128];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      __nv_bfloat16* orow = a.out + ((long)(q_begin + (valid ? lr : 0)) * a.nq + h) * D + cb;
 #pragma unroll 1
-      for (int c = 0; c < D; c += 16) {
+      for (int c = 0; c < 64; c += 16) {
         float o16[16];
-        tmem_ld_32x32b_x16(tO + lane_off + c, o16);
+        tmem_ld_32x32b_x16(tO + lane_off + cb + c, o16);
         tmem_wait_ld();
         if (valid) {
           uint4 w0, w1;
@@ -360,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }

@@ -59,7 +59,15 @@ struct Args {
   // while it is hot: prefill), 2 evict-last.
   int wpol;
   int tok_group;  // token tiles per raster group (see decode_tile)
+  // optional timeline (%globaltimer ns) of each CTA's first work item:
+  // [entry, setup done, first stage landed, last MMA issued, accumulator seen
+  // by the epilogue, epilogue done, 0, 0] x gridDim.x
+  unsigned long long* trace;
 };
+
+__device__ __forceinline__ void trace_mark(const Args& a, int slot) {
+  if (a.trace != nullptr) a.trace[blockIdx.x * 8 + slot] = globaltimer_ns();
+}
 
 struct Tile {
   int ft, tt, sp, tok0, tok_end, arow;
@@ -212,6 +220,7 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = lane_id();
 
   if (threadIdx.x == 0) {
+    trace_mark(a, 0);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -236,6 +245,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) trace_mark(a, 1);
 
   const int total = a.tiles != nullptr ? *a.num_tiles_dev : a.num_feat_tiles * a.num_tok_tiles * a.splits;
 
@@ -297,6 +307,7 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
+          if (!issued_any) trace_mark(a, 2);
           const uint64_t adesc = umma_desc_sw128(smem_u32(sA + stage * C::kABytes));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + stage * C::kBBytes));
 #pragma unroll
@@ -304,6 +315,7 @@ __global__ void __launch_bounds__(192, 1)
             // advance 16 bf16 = 32 bytes along K inside the 128-byte swizzle atom
             umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
+          if (t == blockIdx.x && kb == kb1 - 1) trace_mark(a, 3);
           issued_any = true;
           umma_commit(&empty[stage]);
           if (++stage == C::kStages) {
@@ -333,6 +345,8 @@ __global__ void __launch_bounds__(192, 1)
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, a.status, kStatusGemmTimeout);
       if (epi_barrier_or(!ok)) break;
       tc_fence_after();
+      const bool first_item = t == blockIdx.x;
+      if (first_item && threadIdx.x == 64) trace_mark(a, 4);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       auto from_tmem = [&](int c, float (&v)[16]) {
         tmem_ld_32x32b_x16(taddr + c, v);
@@ -431,6 +445,10 @@ __global__ void __launch_bounds__(192, 1)
         epi_barrier();  // fix_last is rewritten by the next tile
         if (timed_out) break;
       }
+      if (first_item) {
+        epi_barrier();
+        if (threadIdx.x == 64) trace_mark(a, 5);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -508,7 +526,8 @@ struct Cfg2 {
   static constexpr int kABytes = BM * BK * 2;         // this CTA's 128 weight rows
   static constexpr int kBBytes = (BN / 2) * BK * 2;   // this CTA's half of the tokens
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+  // deep rings for small (decode) token tiles: more k-blocks in flight per SM
+  static constexpr int kStages = (200 * 1024) / kStageBytes > 12 ? 12 : (200 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
 };
@@ -759,6 +778,19 @@ void dispatch_bn(int bn, const CUtensorMap& tmA, const CUtensorMap& tmB, const A
 
 }  // namespace gemm
 
+// Timeline buffer for the next plain (non-pair) GEMM launches; see Args::trace.
+static unsigned long long* g_gemm_trace = nullptr;
+
+void gemm_set_trace(const c10::optional<torch::Tensor>& buf) {
+  if (buf.has_value() && buf->defined()) {
+    TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 8 * 1024,
+                "gemm trace: int64 CUDA tensor of >= 8192 elements");
+    g_gemm_trace = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+  } else {
+    g_gemm_trace = nullptr;
+  }
+}
+
 int gemm_pick_bn(int M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
@@ -835,6 +867,7 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.num_tiles_dev = nullptr;
   a.rows_per_group = 0;
   a.wpol = a.num_tok_tiles > 1 ? 1 : 0;
+  a.trace = g_gemm_trace;
   // 8 token tiles per raster group: measured on M=8192 prefill GEMMs (N 4096-28672,
   // K 4096-14336) as 10-15 % faster than one group, with 2.3x fewer DRAM reads
   a.tok_group = std::min(a.num_tok_tiles, 8);
@@ -917,7 +950,7 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
       return e ? std::atoi(e) : 1;
     }();
     const int pair_tiles = ((N + 2 * gemm::BM - 1) / (2 * gemm::BM)) * a.num_tok_tiles;
-    if (env_pair && a.splits == 1 && epi != kEpiPartialF32 && (bn == 256 || bn == 128) && pair_tiles >= 74) {
+    if (env_pair && a.splits == 1 && epi != kEpiPartialF32 && bn >= 32 && pair_tiles >= 74) {
       const CUtensorMap tmB2 = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, bn / 2);
       int done = 0;
       if (bn == 256) {
@@ -928,13 +961,27 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
           case kEpiResidual: done = gemm::launch_pair<256, kEpiResidual>(tmA, tmB2, a, pair_tiles, stream); break;
           case kEpiGelu: done = gemm::launch_pair<256, kEpiGelu>(tmA, tmB2, a, pair_tiles, stream); break;
         }
-      } else {
+      } else if (bn == 128) {
         switch (epi) {
           case kEpiBF16: done = gemm::launch_pair<128, kEpiBF16>(tmA, tmB2, a, pair_tiles, stream); break;
           case kEpiF32: done = gemm::launch_pair<128, kEpiF32>(tmA, tmB2, a, pair_tiles, stream); break;
           case kEpiSwiGLU: done = gemm::launch_pair<128, kEpiSwiGLU>(tmA, tmB2, a, pair_tiles, stream); break;
           case kEpiResidual: done = gemm::launch_pair<128, kEpiResidual>(tmA, tmB2, a, pair_tiles, stream); break;
           case kEpiGelu: done = gemm::launch_pair<128, kEpiGelu>(tmA, tmB2, a, pair_tiles, stream); break;
+        }
+      } else if (bn == 64) {  // decode-sized batches: more CTA pairs instead of split-K
+        switch (epi) {
+          case kEpiBF16: done = gemm::launch_pair<64, kEpiBF16>(tmA, tmB2, a, pair_tiles, stream); break;
+          case kEpiSwiGLU: done = gemm::launch_pair<64, kEpiSwiGLU>(tmA, tmB2, a, pair_tiles, stream); break;
+          case kEpiResidual: done = gemm::launch_pair<64, kEpiResidual>(tmA, tmB2, a, pair_tiles, stream); break;
+          default: break;
+        }
+      } else {
+        switch (epi) {
+          case kEpiBF16: done = gemm::launch_pair<32, kEpiBF16>(tmA, tmB2, a, pair_tiles, stream); break;
+          case kEpiSwiGLU: done = gemm::launch_pair<32, kEpiSwiGLU>(tmA, tmB2, a, pair_tiles, stream); break;
+          case kEpiResidual: done = gemm::launch_pair<32, kEpiResidual>(tmA, tmB2, a, pair_tiles, stream); break;
+          default: break;
         }
       }
       if (done) {
@@ -990,6 +1037,7 @@ void gemm_grouped_out(const torch::Tensor& x, const torch::Tensor& w, torch::Ten
   a.rows_per_group = int(rows_per_group);
   a.wpol = 0;
   a.tok_group = 1;
+  a.trace = nullptr;
   const CUtensorMap tmA = make_tmap_bf16_2d(w.data_ptr(), K, w.size(0), w.stride(0) * 2, gemm::BK, gemm::BM);
   const CUtensorMap tmB = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, int(bn));
   const int grid = num_sms(x.get_device());
