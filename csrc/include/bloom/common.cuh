@@ -237,4 +237,21 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel of the
+// stream is still running; griddep_wait() blocks until that kernel has
+// completed and its memory is visible, so everything before it may only touch
+// memory the previous kernel neither writes nor reads (weights).
+// griddep_launch_dependents() lets the next such kernel start early.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace bloom

@@ -61,8 +61,12 @@ struct Args {
   int tok_group;  // token tiles per raster group (see decode_tile)
   // optional timeline (%globaltimer ns) of each CTA's first work item:
   // [entry, setup done, first stage landed, last MMA issued, accumulator seen
-  // by the epilogue, epilogue done, 0, 0] x gridDim.x
+  // by the epilogue, epilogue done (cluster split-K: slice parked), cluster
+  // reduction done, 0] x gridDim.x
   unsigned long long* trace;
+  int vec;     // output / residual rows allow 16-byte vector access
+  int csplit;  // > 1: cluster split-K, one tile per cluster of csplit CTAs (one K-slice each)
+  int pdl;     // launched with programmatic stream serialization (weights prefetched before the wait)
 };
 
 __device__ __forceinline__ void trace_mark(const Args& a, int slot) {
@@ -99,9 +103,6 @@ __device__ __forceinline__ void decode_tile(const Args& a, int t, int& feat_tile
   tok_tile = g * a.tok_group + (in - feat_tile * gsize);
 }
 
-// Runs the fused epilogue of one output tile.  `load(c, v)` supplies the fp32
-// accumulator of columns [c, c+16) for this thread's row (feature), either
-// straight from TMEM or as the sum of the split-K partials.
 template <int BN>
 __device__ __forceinline__ Tile get_tile(const Args& a, int t) {
   Tile r;
@@ -122,61 +123,136 @@ __device__ __forceinline__ Tile get_tile(const Args& a, int t) {
   return r;
 }
 
+// Per-warp transpose scratch of the epilogue: 16 tokens x 32 features fp32,
+// rows padded to 36 floats (conflict-free row writes and float4 column reads).
+constexpr int kScrStride = 36;
+constexpr int kScrFloats = 16 * kScrStride;
+
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* dst, const float (&x)[8], int n, bool vec) {
+  if (vec && n >= 8) {
+    uint4 w;
+    w.x = pack_bf16x2(x[0], x[1]);
+    w.y = pack_bf16x2(x[2], x[3]);
+    w.z = pack_bf16x2(x[4], x[5]);
+    w.w = pack_bf16x2(x[6], x[7]);
+    *reinterpret_cast<uint4*>(dst) = w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < n) dst[k] = __float2bfloat16(x[k]);
+  }
+}
+__device__ __forceinline__ void store8_f32(float* dst, const float (&x)[8], int n, bool vec) {
+  if (vec && n >= 8) {
+    reinterpret_cast<float4*>(dst)[0] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(x[4], x[5], x[6], x[7]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < n) dst[k] = x[k];
+  }
+}
+
+// Runs the fused epilogue of columns [cbeg, cend) of one output tile.
+// `load(c, v)` supplies the fp32 accumulator of columns [c, c+16) for this
+// thread's row (feature): straight from TMEM, or summed over split-K partials.
+// The accumulator holds one feature per lane and one token per column, the
+// output is token-major, so each 32-feature x 16-token block is transposed
+// through the warp's scratch and written as 16-byte vectors (8 features of one
+// token per lane) instead of 2-byte scalars.
 template <int BN, int EPI, typename Loader>
-__device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int row, int lane, Loader&& load) {
+__device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int q, int lane, float* scr, int cbeg,
+                                              int cend, Loader&& load) {
   const int tok0 = tl.tok0;
   const int tok_end = tl.tok_end;
-  const int feat_tile = tl.ft;
-  const int split = tl.sp;
   if constexpr (EPI == kEpiSwiGLU) {
     // Weight rows are interleaved per 32-row group: 16 gate rows then the 16
     // matching up rows, so gate and up of one feature sit in lanes l and l+16.
     const int nout = a.N / 2;
-    const int f = feat_tile * (BM / 2) + (row >> 5) * 16 + (row & 15);
-    const bool writer = (lane < 16) && (f < nout);
+    const int r = lane >> 1, fo = (lane & 1) * 8;
+    const int f = tl.ft * (BM / 2) + q * 16 + fo;
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-    for (int c = 0; c < BN; c += 16) {
+    for (int c = cbeg; c < cend; c += 16) {
       if (tok0 + c >= tok_end) break;
       float v[16];
       load(c, v);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const float up = __shfl_down_sync(0xffffffffu, v[j], 16);
-        const int tok = tok0 + c + j;
-        if (writer && tok < tok_end) out[(long)tok * a.ldo + f] = __float2bfloat16(silu(v[j]) * up);
+        scr[j * kScrStride + lane] = silu(v[j]) * up;  // lanes >= 16 write unused columns
       }
+      __syncwarp();
+      const int tok = tok0 + c + r;
+      if (tok < tok_end && f < nout) {
+        float x[8];
+        *reinterpret_cast<float4*>(x) = *reinterpret_cast<const float4*>(scr + r * kScrStride + fo);
+        *reinterpret_cast<float4*>(x + 4) = *reinterpret_cast<const float4*>(scr + r * kScrStride + fo + 4);
+        store8_bf16(out + (long)tok * a.ldo + f, x, nout - f, a.vec);
+      }
+      __syncwarp();
     }
   } else {
-    const int f = feat_tile * BM + row;
-    const bool fvalid = f < a.N;
-    float bias = 0.f;
+    const int fo = (lane & 3) * 8;
+    const int f = tl.ft * BM + q * 32 + fo;
+    const int nf = a.N - f;  // features of this lane's group of 8 inside the matrix
+    float bias[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) bias[k] = 0.f;
     if constexpr (EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiGelu) {
-      if (a.bias != nullptr && fvalid) bias = __bfloat162float(a.bias[f]);
+      if (a.bias != nullptr) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k < nf) bias[k] = __bfloat162float(a.bias[f + k]);
+      }
     }
-    for (int c = 0; c < BN; c += 16) {
+    for (int c = cbeg; c < cend; c += 16) {
       if (tok0 + c >= tok_end) break;
       float v[16];
       load(c, v);
-      if (!fvalid) continue;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int tok = tok0 + c + j;
-        if (tok >= tok_end) break;
+      for (int j = 0; j < 16; ++j) scr[j * kScrStride + lane] = v[j];
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int r = (lane >> 2) + 8 * i;
+        const int tok = tok0 + c + r;
+        if (tok >= tok_end || nf <= 0) continue;
+        float x[8];
+        *reinterpret_cast<float4*>(x) = *reinterpret_cast<const float4*>(scr + r * kScrStride + fo);
+        *reinterpret_cast<float4*>(x + 4) = *reinterpret_cast<const float4*>(scr + r * kScrStride + fo + 4);
         if constexpr (EPI == kEpiBF16) {
-          reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] = __float2bfloat16(v[j] + bias);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) x[k] += bias[k];
+          store8_bf16(reinterpret_cast<__nv_bfloat16*>(a.out) + (long)tok * a.ldo + f, x, nf, a.vec);
         } else if constexpr (EPI == kEpiF32) {
-          reinterpret_cast<float*>(a.out)[(long)tok * a.ldo + f] = v[j] + bias;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) x[k] += bias[k];
+          store8_f32(reinterpret_cast<float*>(a.out) + (long)tok * a.ldo + f, x, nf, a.vec);
         } else if constexpr (EPI == kEpiPartialF32) {
-          reinterpret_cast<float*>(a.out)[((long)split * a.M + tok) * a.N + f] = v[j];
+          store8_f32(reinterpret_cast<float*>(a.out) + ((long)tl.sp * a.M + tok) * a.N + f, x, nf, a.vec);
         } else if constexpr (EPI == kEpiResidual) {
-          const float r = __bfloat162float(a.resid[(long)tok * a.ldr + f]);
-          reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] = __float2bfloat16(v[j] + r);
+          const __nv_bfloat16* rp = a.resid + (long)tok * a.ldr + f;
+          if (a.vec && nf >= 8) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(rp);
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] += __bfloat162float(rb[k]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              if (k < nf) x[k] += __bfloat162float(rp[k]);
+          }
+          store8_bf16(reinterpret_cast<__nv_bfloat16*>(a.out) + (long)tok * a.ldo + f, x, nf, a.vec);
         } else if constexpr (EPI == kEpiGelu) {
-          const float x = v[j] + bias;
-          reinterpret_cast<__nv_bfloat16*>(a.out)[(long)tok * a.ldo + f] =
-              __float2bfloat16(0.5f * x * (1.f + erff(x * 0.7071067811865476f)));
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float y = x[k] + bias[k];
+            x[k] = 0.5f * y * (1.f + erff(y * 0.7071067811865476f));
+          }
+          store8_bf16(reinterpret_cast<__nv_bfloat16*>(a.out) + (long)tok * a.ldo + f, x, nf, a.vec);
         }
       }
+      __syncwarp();
     }
   }
 }
@@ -199,6 +275,37 @@ __device__ __forceinline__ bool epi_barrier_or(bool pred) {
   return r != 0;
 }
 
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Asynchronous 16-byte store into a cluster peer's shared memory that counts
+// its bytes on the peer's mbarrier (complete_tx).
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float x, float y, float z, float w,
+                                            uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   cluster_addr),
+               "f"(x), "f"(y), "f"(z), "f"(w), "r"(cluster_bar)
+               : "memory");
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Args a) {
@@ -213,8 +320,11 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull = bars + 2 * C::kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* recv = drain + 1;  // cluster split-K: the peers' partial slices have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ __align__(16) float epi_scr[4 * kScrFloats];
+  bool csplit_armed = false;  // epilogue thread passed the first cluster barrier
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -230,6 +340,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&tempty[i], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(recv, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -258,17 +369,35 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_par = 0;
       bool ok = true;
+      // Under programmatic dependent launch the weight tiles of the first
+      // k-blocks are requested before waiting for the previous kernel (they
+      // do not depend on it); the activation tiles follow after the wait.
+      int pre = 0;
+      if (a.pdl) {
+        if (static_cast<int>(blockIdx.x) < total) {
+          const Tile tl = get_tile<BN>(a, blockIdx.x);
+          const int kb0 = tl.sp * a.kb_per_split;
+          pre = min(C::kStages, min(kb0 + a.kb_per_split, a.num_kb) - kb0);
+          for (int i = 0; i < pre; ++i) {
+            mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+            tma_load_2d_hint(sA + i * C::kABytes, &tmA, &full[i], (kb0 + i) * BK, tl.arow, pol_w);
+          }
+        }
+        griddep_wait();
+      }
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const Tile tl = get_tile<BN>(a, t);
         const int kb0 = tl.sp * a.kb_per_split;
         const int kb1 = min(kb0 + a.kb_per_split, a.num_kb);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.status, kStatusGemmTimeout)) {
-            ok = false;
-            break;
+          if (!(t == static_cast<int>(blockIdx.x) && kb - kb0 < pre)) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, a.status, kStatusGemmTimeout)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+            tma_load_2d_hint(sA + stage * C::kABytes, &tmA, &full[stage], kb * BK, tl.arow, pol_w);
           }
-          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-          tma_load_2d_hint(sA + stage * C::kABytes, &tmA, &full[stage], kb * BK, tl.arow, pol_w);
           tma_load_2d_hint(sB + stage * C::kBBytes, &tmB, &full[stage], kb * BK, tl.tok0, pol_x);
           issued_mask |= 1u << stage;
           issued_par = phase ? (issued_par | (1u << stage)) : (issued_par & ~(1u << stage));
@@ -282,6 +411,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int s = 0; s < C::kStages; ++s)
           if ((issued_mask >> s) & 1u) mbar_drain(&full[s], (issued_par >> s) & 1u);
       }
+      griddep_launch_dependents();
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -336,9 +466,11 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int q = warp & 3;  // a warp may only touch TMEM lanes [32*(warp%4), +32)
     const int row = q * 32 + lane;
+    float* scr = epi_scr + q * kScrFloats;
     __shared__ int fix_last;
     int acc = 0;
     uint32_t acc_phase = 0;
+    if (a.pdl) griddep_wait();  // outputs, residuals and fixup state belong to the stream order
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile tl = get_tile<BN>(a, t);
       const int ft = tl.ft, tt = tl.tt, sp = tl.sp;
@@ -352,8 +484,73 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_32x32b_x16(taddr + c, v);
         tmem_wait_ld();
       };
-      if (!a.fixup) {
-        epilogue_tile<BN, EPI>(a, tl, row, lane, from_tmem);
+      if (a.csplit > 1) {
+        // cluster split-K.  CTA r of the cluster owns token columns
+        // [r * per, (r + 1) * per) of the tile.  Every CTA writes the other
+        // owners' columns of its K-slice accumulator to an L2-resident
+        // workspace (fp32 as [column / 4][row] float4, so each warp store
+        // covers 512 contiguous bytes), the cluster barrier
+        // publishes them, and each owner fetches its S-1 incoming slices with
+        // one bulk copy into its (idle) ring memory, adds them to its own
+        // columns straight from TMEM and runs the epilogue.  The reduction
+        // runs in all S CTAs at once; the cluster guarantees they are resident.
+        const int S = a.csplit;
+        const int rank = static_cast<int>(cluster_ctarank());
+        const int per = ((BN / 16 + S - 1) / S) * 16;
+        const int cb = min(BN, rank * per), ce = min(BN, (rank + 1) * per);
+        const long slab = (long)BM * per;  // floats of one (owner, source) slice
+        float* wtile = a.fix_ws + ((long)tl.ft * a.num_tok_tiles + tl.tt) * S * (S - 1) * slab;
+        for (int i2 = 1; i2 < S; ++i2) {
+          const int d = rank + i2 < S ? rank + i2 : rank + i2 - S;  // stagger the destinations
+          const int cbd = min(BN, d * per), ced = min(BN, (d + 1) * per);
+          const int slot = rank < d ? rank : rank - 1;
+          float4* dst = reinterpret_cast<float4*>(wtile + (d * (S - 1) + slot) * slab) + row;
+          for (int c = cbd; c < ced; c += 16) {
+            if (tl.tok0 + c >= tl.tok_end) break;
+            float v[16];
+            from_tmem(c, v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              __stcg(dst + (((c - cbd) >> 2) + k) * BM,
+                     make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+          }
+        }
+        const uint32_t bytes = static_cast<uint32_t>((S - 1) * slab * 4);
+        if (threadIdx.x == 64) mbar_arrive_expect_tx(recv, bytes);
+        __threadfence();
+        if (threadIdx.x == 64) trace_mark(a, 5);
+        cluster_sync_all();  // the peers' slices of this CTA's columns are in L2
+        csplit_armed = true;
+        if (threadIdx.x == 64) trace_mark(a, 7);
+        if (threadIdx.x == 64) {
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // generic writes -> bulk-copy reads
+          bulk_load(smem, wtile + (long)rank * (S - 1) * slab, bytes, recv);
+        }
+        const bool got = mbar_wait(recv, 0, abort_flag, a.status, kStatusGemmTimeout);
+        if (!epi_barrier_or(!got)) {
+          const float4* mine = reinterpret_cast<const float4*>(smem) + row;
+          auto summed = [&](int c, float (&v)[16]) {
+            from_tmem(c, v);
+            for (int sl = 0; sl < S - 1; ++sl) {
+              const float4* p = mine + sl * (slab / 4) + ((c - cb) >> 2) * BM;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float4 x = p[k * BM];
+                v[4 * k] += x.x;
+                v[4 * k + 1] += x.y;
+                v[4 * k + 2] += x.z;
+                v[4 * k + 3] += x.w;
+              }
+            }
+          };
+          epilogue_tile<BN, EPI>(a, tl, q, lane, scr, cb, ce, summed);
+          if (threadIdx.x == 64) trace_mark(a, 6);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      } else if (!a.fixup) {
+        epilogue_tile<BN, EPI>(a, tl, q, lane, scr, 0, BN, from_tmem);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -431,7 +628,7 @@ __global__ void __launch_bounds__(192, 1)
                 v[4 * j + 3] += acc4[j].w;
               }
             };
-            epilogue_tile<BN, EPI>(a, tl, row, lane, summed);
+            epilogue_tile<BN, EPI>(a, tl, q, lane, scr, 0, BN, summed);
           }
           tc_fence_before();
           __syncwarp();
@@ -445,7 +642,7 @@ __global__ void __launch_bounds__(192, 1)
         epi_barrier();  // fix_last is rewritten by the next tile
         if (timed_out) break;
       }
-      if (first_item) {
+      if (first_item && a.csplit <= 1) {
         epi_barrier();
         if (threadIdx.x == 64) trace_mark(a, 5);
       }
@@ -454,6 +651,9 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
 
+  // every thread of the cluster takes part in the split-K cluster barrier
+  // (epilogue warps that reached their tile took it above)
+  if (a.csplit > 1 && !csplit_armed) cluster_sync_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -471,19 +671,6 @@ __global__ void __launch_bounds__(192, 1)
 // tile.  Every TMA load is a plain (non-multicast) load into the issuing
 // CTA's own shared memory that signals the leader's full barrier; the
 // leader's MMA completion is committed separately to each CTA's barrier.
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* tm, uint32_t leader_bar, int x, int y,
                                                  uint64_t hint) {
   asm volatile(
@@ -548,6 +735,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ __align__(16) float epi_scr[4 * kScrFloats];
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -702,7 +890,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_32x32b_x16(taddr + c, v);
         tmem_wait_ld();
       };
-      epilogue_tile<BN, EPI>(a, tl, row, lane, from_tmem);
+      epilogue_tile<BN, EPI>(a, tl, q, lane, epi_scr + q * kScrFloats, 0, BN, from_tmem);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
@@ -762,7 +950,83 @@ void launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const Args& a, int g
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
     configured |= uint64_t(1) << dev;
   }
-  kern<<<grid, 192, Cfg<BN>::kSmem, stream>>>(tmA, tmB, a);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (a.pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (a.csplit > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = a.csplit;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = Cfg<BN>::kSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, a));
+}
+
+// Clusters of `cs` one-CTA GEMM blocks that can be resident at once (0 if a
+// cluster launch is unavailable); cached per device, token tile and size.
+template <int BN>
+int max_active_clusters(int cs) {
+  static int cache[64][9];
+  static bool init[64][9];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cs < 1 || cs > 8 || dev >= 64) return 0;
+  if (!init[dev][cs]) {
+    auto kern = gemm_tn_kernel<BN, kEpiBF16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(cs * 16, 1, 1);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = Cfg<BN>::kSmem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 0) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cache[dev][cs] = n;
+    init[dev][cs] = true;
+  }
+  return cache[dev][cs];
+}
+
+// Shared-memory ring bytes of the one-CTA kernel (the cluster split-K receive area).
+int ring_bytes_bn(int bn) {
+  switch (bn) {
+    case 16: return Cfg<16>::kStages * Cfg<16>::kStageBytes;
+    case 32: return Cfg<32>::kStages * Cfg<32>::kStageBytes;
+    case 64: return Cfg<64>::kStages * Cfg<64>::kStageBytes;
+    case 128: return Cfg<128>::kStages * Cfg<128>::kStageBytes;
+    default: return Cfg<256>::kStages * Cfg<256>::kStageBytes;
+  }
+}
+
+int max_active_clusters_bn(int bn, int cs) {
+  switch (bn) {
+    case 16: return max_active_clusters<16>(cs);
+    case 32: return max_active_clusters<32>(cs);
+    case 64: return max_active_clusters<64>(cs);
+    case 128: return max_active_clusters<128>(cs);
+    default: return max_active_clusters<256>(cs);
+  }
 }
 
 template <int EPI>
@@ -791,6 +1055,10 @@ void gemm_set_trace(const c10::optional<torch::Tensor>& buf) {
   }
 }
 
+int gemm_max_active_clusters(int64_t bn, int64_t cluster_size) {
+  return gemm::max_active_clusters_bn(int(bn), int(cluster_size));
+}
+
 int gemm_pick_bn(int M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
@@ -810,7 +1078,10 @@ int gemm_tiles(int M, int N, int epi) {
 int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits, int64_t bn_override) {
   const int bn = bn_override > 0 ? int(bn_override) : gemm_pick_bn(int(M));
   const int64_t tiles = ((M + bn - 1) / bn) * ((N + gemm::BM - 1) / gemm::BM);
-  return tiles * splits * bn * gemm::BM;
+  // last-arriver fixup: one partial tile per split; cluster split-K: S-1
+  // column slices per owner
+  const int64_t per = ((bn / 16 + splits - 1) / splits) * 16;
+  return std::max(tiles * splits * bn * gemm::BM, tiles * splits * (splits - 1) * gemm::BM * per);
 }
 
 int gemm_default_splits(int M, int N, int K, int device) {
@@ -868,6 +1139,22 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.rows_per_group = 0;
   a.wpol = a.num_tok_tiles > 1 ? 1 : 0;
   a.trace = g_gemm_trace;
+  a.csplit = 1;
+  {
+    static const int env_pdl = [] {
+      const char* e = std::getenv("BLOOM_PDL");
+      return e ? std::atoi(e) : 1;
+    }();
+    a.pdl = env_pdl;
+  }
+  {
+    // 16-byte vector stores need aligned rows: 8 bf16 / 4 fp32 elements
+    const int esz = out.element_size();
+    a.vec = (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0) && ((a.ldo * esz) % 16 == 0) &&
+            (epi == kEpiPartialF32 ? (N * 4) % 16 == 0 : true);
+    if (epi == kEpiResidual && resid.has_value())
+      a.vec = a.vec && reinterpret_cast<uintptr_t>(resid->data_ptr()) % 16 == 0 && (resid->stride(0) * 2) % 16 == 0;
+  }
   // 8 token tiles per raster group: measured on M=8192 prefill GEMMs (N 4096-28672,
   // K 4096-14336) as 10-15 % faster than one group, with 2.3x fewer DRAM reads
   a.tok_group = std::min(a.num_tok_tiles, 8);
@@ -919,12 +1206,29 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
     default:
       TORCH_CHECK(false, "gemm: unknown epilogue ", epi);
   }
+  static const int env_csplit = [] {
+    const char* e = std::getenv("BLOOM_GEMM_CSPLIT");
+    return e ? std::atoi(e) : 1;
+  }();
   if (epi != kEpiPartialF32 && splits > 1) {
-    // split-K with in-kernel fixup (last arriving split reduces + runs the epilogue)
+    // split-K: the K-slices of one tile run as one thread-block cluster and
+    // reduce through distributed shared memory (up to 8 slices), otherwise
+    // with an in-kernel fixup (the last arriving split reduces + runs the epilogue)
     int s = std::min<int>(int(splits), a.num_kb);
     a.kb_per_split = (a.num_kb + s - 1) / s;
     a.splits = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;
-    if (a.splits > 1) {
+    // clusters only when every tile's cluster is resident at once (a second
+    // wave of clusters would double the kernel time)
+    const int per = ((bn / 16 + a.splits - 1) / a.splits) * 16;
+    const int64_t recv_bytes = (int64_t)(a.splits - 1) * gemm::BM * per * 4;
+    const int64_t tiles = (int64_t)a.num_feat_tiles * a.num_tok_tiles;
+    if (a.splits > 1 && a.splits <= 8 && env_csplit && recv_bytes <= gemm::ring_bytes_bn(bn) &&
+        tiles <= gemm::max_active_clusters_bn(bn, a.splits) && fix_ws.has_value() &&
+        fix_ws->scalar_type() == at::kFloat &&
+        fix_ws->numel() >= tiles * a.splits * (a.splits - 1) * gemm::BM * per) {
+      a.csplit = a.splits;
+      a.fix_ws = fix_ws->data_ptr<float>();
+    } else if (a.splits > 1) {
       TORCH_CHECK(fix_ws.has_value() && fix_count.has_value(), "gemm split-K fixup needs a workspace");
       const int64_t tiles = (int64_t)a.num_feat_tiles * a.num_tok_tiles;
       TORCH_CHECK(fix_ws->scalar_type() == at::kFloat &&
@@ -991,8 +1295,9 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
     }
   }
   const CUtensorMap tmB = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, bn);
-  const int total = a.tiles != nullptr ? *a.num_tiles_dev : a.num_feat_tiles * a.num_tok_tiles * a.splits;
-  const int grid = std::min(total, num_sms(x.get_device()));
+  const int total = a.num_feat_tiles * a.num_tok_tiles * a.splits;
+  // cluster split-K runs one tile per cluster (grid = all tiles); otherwise persistent
+  const int grid = a.csplit > 1 ? total : std::min(total, num_sms(x.get_device()));
   switch (epi) {
     case kEpiBF16: gemm::dispatch_bn<kEpiBF16>(bn, tmA, tmB, a, grid, stream); break;
     case kEpiF32: gemm::dispatch_bn<kEpiF32>(bn, tmA, tmB, a, grid, stream); break;
@@ -1038,6 +1343,9 @@ void gemm_grouped_out(const torch::Tensor& x, const torch::Tensor& w, torch::Ten
   a.wpol = 0;
   a.tok_group = 1;
   a.trace = nullptr;
+  a.csplit = 1;
+  a.pdl = 0;  // the tile list is written by the previous kernel
+  a.vec = reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0 && (out.stride(0) * 2) % 16 == 0;
   const CUtensorMap tmA = make_tmap_bf16_2d(w.data_ptr(), K, w.size(0), w.stride(0) * 2, gemm::BK, gemm::BM);
   const CUtensorMap tmB = make_tmap_bf16_2d(x.data_ptr(), K, M, x.stride(0) * 2, gemm::BK, int(bn));
   const int grid = num_sms(x.get_device());

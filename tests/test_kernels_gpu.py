@@ -307,6 +307,36 @@ def test_gemm_splitk_fixup(M, N, K, splits, epi):
         assert rel_err(yr, ref.gemm(x, w) + r.float()) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K,splits", [(64, 1024, 8192, 12), (256, 2048, 8192, 16)])
+def test_gemm_splitk_global_fixup(M, N, K, splits):
+    """More K-slices than a thread-block cluster holds: the global-memory fixup path."""
+    ops, ref = _ops(), _ref()
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    for _ in range(2):
+        assert rel_err(ops.gemm(x, w, splits=splits), ref.gemm(x, w)) < 1e-2
+
+
+@pytest.mark.parametrize("M", [3, 77, 256])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_gemm_unaligned_output_rows(M, splits):
+    """Output rows that are not 16-byte aligned and N not a multiple of 8 take the scalar stores."""
+    ops, ref = _ops(), _ref()
+    N, K = 100, 1024
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    b = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    big = torch.zeros(M, N + 3, device="cuda", dtype=torch.bfloat16)
+    out = big[:, 1:N + 1]
+    ops.gemm(x, w, out, bias=b if splits == 1 else None, splits=splits)
+    want = ref.gemm(x, w, b) if splits == 1 else ref.gemm(x, w)
+    assert rel_err(out, want) < 1e-2
+    assert big[:, 0].abs().max().item() == 0 and big[:, N + 1:].abs().max().item() == 0
+    r = torch.randn(M, N + 5, device="cuda", dtype=torch.bfloat16)[:, 2:N + 2]
+    yr = ops.gemm(x, w, epi=ops.EPI_RESIDUAL, resid=r, splits=splits)
+    assert rel_err(yr, ref.gemm(x, w) + r.float()) < 1e-2
+
+
 def test_gemm_auto_splits_decode_shapes():
     ops, ref = _ops(), _ref()
     for M, N, K in [(256, 4096, 14336), (8, 6144, 4096)]:
