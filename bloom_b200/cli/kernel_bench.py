@@ -70,6 +70,42 @@ def timeit(fn, iters=None, warmup=5):
     return statistics.median(ts)
 
 
+def sweep_gemm(ops, name, M, N, K, epi, x, ws, out, nrot, *, trace, report):
+    """Every (token tile, split-K) pair of one GEMM shape: device time per call
+    (CUDA graph of back-to-back calls, rotating weights), or with `trace` the
+    per-CTA timeline of one launch on a cold weight copy: entry, first stage
+    landed, accumulator ready, epilogue done (cluster split-K: slices written),
+    cluster barrier passed, reduction + epilogue done; min / median / max in
+    microseconds from the first CTA's entry (%globaltimer ticks ~0.26 us)."""
+    for bn in (64, 128, 256):
+        for sp in (1, 2, 3, 4, 6, 8):
+            if K // 64 // sp < 2:
+                continue
+            extra = {"M": M, "N": N, "K": K, "bn": bn, "splits": sp}
+            if trace:
+                tr = torch.zeros(8 * 1024, dtype=torch.int64, device=x.device)
+                for i in range(3):
+                    ops.gemm(x, ws[i % nrot], out, epi=epi, bn=bn, splits=sp)
+                torch.cuda.synchronize()
+                ops._C().gemm_set_trace(tr)
+                ops.gemm(x, ws[3 % nrot], out, epi=epi, bn=bn, splits=sp)
+                torch.cuda.synchronize()
+                ops._C().gemm_set_trace(None)
+                t = tr.view(-1, 8).cpu()
+                t = t[t[:, 0] > 0].double()
+                rel = (t - t[:, 0].min()) / 1000.0
+                names = {0: "entry", 2: "first_stage", 4: "acc_ready", 5: "written", 7: "cluster_barrier",
+                         6: "reduced"}
+                for c, nm in names.items():
+                    if (t[:, c] > 0).all():
+                        extra[nm + "_us"] = [round(float(torch.quantile(rel[:, c], p)), 2) for p in (0.0, 0.5, 1.0)]
+                extra["ctas"] = int(t.shape[0])
+                report(f"gemm_{name}_trace", float("nan"), None, None, extra)
+            else:
+                ms = timeit(lambda i=0: ops.gemm(x, ws[i % nrot], out, epi=epi, bn=bn, splits=sp))
+                report(f"gemm_{name}_sweep", ms, 2.0 * M * N * K, N * K * 2 + M * K * 2, extra)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tp", type=int, default=1)
@@ -78,6 +114,10 @@ def main():
     ap.add_argument("--M", type=int, default=0, help="only this token count for GEMMs")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--autotune", action="store_true", help="pick token tile / split-K by measurement first")
+    ap.add_argument("--sweep", action="store_true",
+                    help="GEMMs: time every (token tile, split-K) pair at the chosen --M instead of the default pick")
+    ap.add_argument("--trace", action="store_true",
+                    help="GEMMs: per-CTA %%globaltimer phases of one launch per (token tile, split-K) pair")
     ap.add_argument("--ncu", action="store_true",
                     help="profile mode: launch each selected kernel 3 times eagerly, no timing, no cuBLAS runs")
     args = ap.parse_args()
@@ -118,6 +158,10 @@ def main():
             x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
             epi = ops.EPI_SWIGLU if name == "gate_up" else ops.EPI_BF16
             out = torch.empty(M, N // 2 if epi == ops.EPI_SWIGLU else N, device=dev, dtype=torch.bfloat16)
+            if args.sweep or args.trace:
+                sweep_gemm(ops, name, M, N, K, epi, x, ws, out, nrot, trace=args.trace, report=report)
+                del ws
+                continue
             if args.autotune and M <= 512:
                 ops.gemm_autotune([(N, K, epi == ops.EPI_SWIGLU)], [M], dev)
             ms = timeit(lambda i=0: ops.gemm(x, ws[i % nrot], out, epi=epi))

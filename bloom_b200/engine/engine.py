@@ -92,6 +92,35 @@ class EngineConfig:
     cachemesh_l3_dir: str = ""
     cachemesh_l3_blocks: int = 0
     cachemesh_namespace: Optional[str] = None
+    # long-context policy: "full", "sliding_window:<tokens>",
+    # "context_shift:<max_context_tokens>:<shift_tokens>" or
+    # "compact_inactive:<target_free_blocks>"
+    long_context_policy: str = "full"
+
+
+LONG_CONTEXT_POLICIES = {"full": 0, "sliding_window": 1, "context_shift": 2, "compact_inactive": 3}
+
+
+def apply_long_context_policy(sc, spec: str) -> None:
+    """Parse a policy string into the scheduler config's lc_* fields."""
+    parts = (spec or "full").strip().lower().split(":")
+    kind = parts[0]
+    if kind not in LONG_CONTEXT_POLICIES:
+        raise ValueError(f"unknown long-context policy {spec!r} (full, sliding_window:N, context_shift:MAX:SHIFT, "
+                         "compact_inactive:N)")
+    args = [int(a) for a in parts[1:]]
+    need = {"full": 0, "sliding_window": 1, "context_shift": 2, "compact_inactive": 1}[kind]
+    if len(args) != need or any(a < 0 for a in args):
+        raise ValueError(f"long-context policy {spec!r} takes {need} non-negative integer argument(s)")
+    sc.lc_policy = LONG_CONTEXT_POLICIES[kind]
+    if kind == "sliding_window":
+        if args[0] == 0:
+            raise ValueError("sliding_window needs a window of at least one token")
+        sc.lc_window_tokens = args[0]
+    elif kind == "context_shift":
+        sc.lc_max_context, sc.lc_shift = args
+    elif kind == "compact_inactive":
+        sc.lc_target_free = args[0]
 
 
 class LLMEngine:
@@ -116,6 +145,7 @@ class LLMEngine:
         sc.chunked_prefill = ec.chunked_prefill
         sc.eos_token_ids = list(self.cfg.eos_token_ids)
         sc.spec_len = int(ec.spec_len)
+        apply_long_context_policy(sc, ec.long_context_policy)
         self.scheduler = rt.Scheduler(sc, ec.num_blocks, 16, ec.enable_prefix_caching)
         self.runner = ModelRunner(model, ec.num_blocks, ec.max_num_seqs, ec.max_num_batched_tokens,
                                   ec.max_model_len, ec.use_cuda_graphs, spec_len=int(ec.spec_len))

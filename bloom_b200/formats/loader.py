@@ -27,15 +27,18 @@ def model_config(man: ModelManifest) -> ModelConfig:
         return from_hf_config(json.load(f))
 
 
-def load_weights(man: ModelManifest) -> dict:
+def load_weights(man: ModelManifest, device=None) -> dict:
     gg = [f for f in man.files if f.format == "Gguf"]
     if gg:
         from .gguf import GGUFFile, load_hf_weights
 
         return load_hf_weights(GGUFFile(os.path.join(man.root, gg[0].name)))
+    from .quant_config import QuantizationConfig, dequantize_checkpoint
     from .safetensors_io import load_state_dict
 
     sd = load_state_dict(man.root)
+    # AWQ / GPTQ / bitsandbytes 4-bit checkpoints: packed layers -> bf16 weights
+    sd = dequantize_checkpoint(sd, QuantizationConfig.from_model_dir(man.root), device)
     # HF checkpoints of MoE models keep experts as separate tensors: stack them
     out = {}
     experts = {}
@@ -62,7 +65,7 @@ def load_decoder(path: str, tp=None, device=None):
         # Q8_0 / Q4_0 projections stay block-quantised on the GPU (qgemv / dequant + tcgen05)
         model.load_gguf(os.path.join(man.root, gg[0].name), quantized=True)
         return model
-    w = load_weights(man)
+    w = load_weights(man, device if torch.cuda.is_available() else None)
     model.shard_full(w)
     return model
 

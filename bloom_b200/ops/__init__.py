@@ -180,6 +180,90 @@ def gemm(
     return out
 
 
+# ---------------------------------------------------------------- quantised formats (quant_formats.cu)
+
+
+def dequant_int4_flat(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor, n: int,
+                      g_idx: Optional[torch.Tensor] = None, dtype=torch.bfloat16) -> torch.Tensor:
+    """AWQ (g_idx None: groups of 128 elements) / GPTQ (group = g_idx[id]) int4
+    in the flat packing -> [n] of `dtype` (bf16, fp16 or fp32)."""
+    out = torch.empty(n, dtype=dtype, device=qweight.device)
+    _C().int4_flat_dequant(qweight.contiguous().view(torch.int32), scales.float().contiguous(),
+                           qzeros.contiguous().view(torch.int32),
+                           None if g_idx is None else g_idx.to(torch.int32).contiguous(), out)
+    _count()
+    return out
+
+
+def dequant_gptq(qweight, qzeros, scales, g_idx) -> torch.Tensor:
+    """GPTQ checkpoint tensors -> W [N, K] bf16 (nn.Linear layout)."""
+    N = qweight.shape[1]
+    K = qweight.shape[0] * 8
+    out = torch.empty(N, K, dtype=torch.bfloat16, device=qweight.device)
+    _C().gptq_dequant(qweight.contiguous(), qzeros.contiguous(), scales.half().contiguous(),
+                      g_idx.to(torch.int32).contiguous(), out)
+    _count()
+    return out
+
+
+def dequant_awq(qweight, qzeros, scales, group: int) -> torch.Tensor:
+    """AWQ GEMM-format checkpoint tensors -> W [N, K] bf16."""
+    K, N = qweight.shape[0], qweight.shape[1] * 8
+    out = torch.empty(N, K, dtype=torch.bfloat16, device=qweight.device)
+    _C().awq_dequant(qweight.contiguous(), qzeros.contiguous(), scales.half().contiguous(), int(group), out)
+    _count()
+    return out
+
+
+def dequant_bnb4(packed: torch.Tensor, scale: torch.Tensor, block: int, nf4: bool = True) -> torch.Tensor:
+    """bitsandbytes NF4 / FP4 codes (uint8, high nibble first) -> bf16 [2 * bytes]."""
+    out = torch.empty(packed.numel() * 2, dtype=torch.bfloat16, device=packed.device)
+    _C().bnb4_dequant(packed.contiguous().view(torch.uint8).flatten(), scale.float().contiguous().flatten(),
+                      int(block), bool(nf4), out)
+    _count()
+    return out
+
+
+def kv_quantize(x: torch.Tensor, kind: str = "int8"):
+    """Per-row 8-bit KV quantisation of bf16 [rows, cols]: (codes uint8, fp32 scale per row);
+    kind "int8" (symmetric, /127) or "fp8" (e4m3, /448)."""
+    q = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    s = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    _C().kv_row_quant(x.contiguous(), q, s, kind == "fp8")
+    _count()
+    return q, s
+
+
+def kv_dequantize(q: torch.Tensor, scales: torch.Tensor, kind: str = "int8") -> torch.Tensor:
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    _C().kv_row_dequant(q.contiguous(), scales.float().contiguous(), out, kind == "fp8")
+    _count()
+    return out
+
+
+MROPE_SECTIONS_QWEN_VL = (24, 20, 20)  # temporal / height / width split of head_dim 128 / 2
+
+
+def mrope_cos_sin(position_ids: torch.Tensor, head_dim: int, theta: float = 1_000_000.0):
+    """cos / sin planes [3, B, S, D] (fp32) for 3-D position ids [3, B, S]
+    (temporal, height, width; text tokens repeat one position in all three)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device=position_ids.device) / head_dim))
+    f = position_ids.float()[..., None] * inv  # [3, B, S, D/2]
+    emb = torch.cat([f, f], dim=-1)
+    return emb.cos().contiguous(), emb.sin().contiguous()
+
+
+def mrope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+          sections=MROPE_SECTIONS_QWEN_VL):
+    """Multimodal rotary embedding of q [B, H, S, D] and k [B, KVH, S, D]
+    (fp32 or bf16) with cos / sin [3, B, S, D]; returns (q_out, k_out)."""
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    _C().mrope(q.contiguous(), k.contiguous(), cos.float().contiguous(), sin.float().contiguous(), qo, ko,
+               int(sections[0]), int(sections[1]), int(sections[2]))
+    _count(2)
+    return qo, ko
+
+
 # (M bucket, N, K, swiglu) -> (token tile, split-K) chosen by measurement (see gemm_autotune)
 GEMM_TUNED: dict = {}
 _M_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512)

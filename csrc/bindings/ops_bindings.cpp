@@ -39,6 +39,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qgemv", &bloom::qgemv, py::arg("x"), py::arg("qs"), py::arg("scales"), py::arg("kind"), py::arg("out"),
         py::arg("epi"), py::arg("resid") = py::none());
   m.def("qdequant", &bloom::qdequant);
+  m.def("int4_flat_dequant", &bloom::int4_flat_dequant, py::arg("qweight"), py::arg("scales"), py::arg("qzeros"),
+        py::arg("g_idx"), py::arg("out"), "AWQ (g_idx None) / GPTQ int4 in the flat layout");
+  m.def("gptq_dequant", &bloom::gptq_dequant, "GPTQ checkpoint tensors -> W [N, K] bf16");
+  m.def("awq_dequant", &bloom::awq_dequant, "AWQ GEMM-format checkpoint tensors -> W [N, K] bf16");
+  m.def("bnb4_dequant", &bloom::bnb4_dequant, "bitsandbytes NF4 / FP4 codes -> bf16");
+  m.def("kv_row_quant", &bloom::kv_row_quant, "per-row int8 / e4m3 quantisation");
+  m.def("kv_row_dequant", &bloom::kv_row_dequant, "per-row int8 / e4m3 dequantisation");
+  m.def("mrope", &bloom::mrope, "multimodal rotary embedding on q [B,H,S,D], k [B,KVH,S,D]");
   m.def("status_tensor", &bloom::status_tensor);
   m.def("bert_embed_ln", &bloom::bert_embed_ln);
   m.def("varlen_attention", &bloom::varlen_attention);

@@ -98,7 +98,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readwrite("max_model_len", &SchedulerConfig::max_model_len)
       .def_readwrite("chunked_prefill", &SchedulerConfig::chunked_prefill)
       .def_readwrite("eos_token_ids", &SchedulerConfig::eos_token_ids)
-      .def_readwrite("spec_len", &SchedulerConfig::spec_len);
+      .def_readwrite("spec_len", &SchedulerConfig::spec_len)
+      .def_readwrite("lc_policy", &SchedulerConfig::lc_policy)
+      .def_readwrite("lc_window_tokens", &SchedulerConfig::lc_window_tokens)
+      .def_readwrite("lc_max_context", &SchedulerConfig::lc_max_context)
+      .def_readwrite("lc_shift", &SchedulerConfig::lc_shift)
+      .def_readwrite("lc_target_free", &SchedulerConfig::lc_target_free);
 
   py::class_<StepMeta>(m, "StepMeta")
       .def_readonly("num_tokens", &StepMeta::num_tokens)
@@ -157,6 +162,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("set_decode_buckets", &Scheduler::set_decode_buckets)
       .def("add_request", &Scheduler::add_request, py::arg("prompt"), py::arg("params"), py::arg("priority") = 0)
       .def("abort", &Scheduler::abort)
+      .def("maintain_long_context", &Scheduler::maintain_long_context)
+      .def("visible_blocks", &Scheduler::visible_blocks)
       .def("has_unfinished", &Scheduler::has_unfinished)
       .def_property_readonly("num_waiting", &Scheduler::num_waiting)
       .def_property_readonly("num_running", &Scheduler::num_running)

@@ -99,6 +99,22 @@ void qgemv(const torch::Tensor& x, const torch::Tensor& qs, const torch::Tensor&
            torch::Tensor& out, int64_t epi, const c10::optional<torch::Tensor>& resid);
 void qdequant(const torch::Tensor& qs, const torch::Tensor& scales, int64_t kind, torch::Tensor& out);
 
+// Non-GGUF weight formats and 8-bit KV rows (quant_formats.cu).
+void int4_flat_dequant(const torch::Tensor& qweight, const torch::Tensor& scales, const torch::Tensor& qzeros,
+                       const c10::optional<torch::Tensor>& g_idx, torch::Tensor& out);
+void gptq_dequant(const torch::Tensor& qweight, const torch::Tensor& qzeros, const torch::Tensor& scales,
+                  const torch::Tensor& g_idx, torch::Tensor& out);
+void awq_dequant(const torch::Tensor& qweight, const torch::Tensor& qzeros, const torch::Tensor& scales,
+                 int64_t group, torch::Tensor& out);
+void bnb4_dequant(const torch::Tensor& packed, const torch::Tensor& scale, int64_t block, bool nf4,
+                  torch::Tensor& out);
+void kv_row_quant(const torch::Tensor& x, torch::Tensor& q, torch::Tensor& scales, bool fp8);
+void kv_row_dequant(const torch::Tensor& q, const torch::Tensor& scales, torch::Tensor& out, bool fp8);
+
+// Multimodal rotary embedding (mrope.cu): cos / sin fp32 [3, B, S, D].
+void mrope(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& cos, const torch::Tensor& sin,
+           torch::Tensor& q_out, torch::Tensor& k_out, int64_t sec0, int64_t sec1, int64_t sec2);
+
 void verify_sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
                         const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
                         const torch::Tensor& draft, torch::Tensor& out);

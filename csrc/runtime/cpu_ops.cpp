@@ -231,9 +231,45 @@ torch::Tensor q8_0_matmul(const torch::Tensor& x, const torch::Tensor& wraw, int
   return y;
 }
 
+// Multimodal rotary embedding on the host (the CPU counterpart of
+// csrc/kernels/mrope.cu; reference: crates/tilelang/scripts/generate_kernel.py:
+// 264-338).  x [B, H, S, D] f32, cos / sin [3, B, S, D] f32; the half
+// dimension is cut into sections (s0, s1, s2) taken from the temporal, height
+// and width position planes; rotate-half pairs channel c with c + D/2.
+torch::Tensor mrope_cpu(const torch::Tensor& x, const torch::Tensor& cos, const torch::Tensor& sin, int64_t s0,
+                        int64_t s1, int64_t s2) {
+  TORCH_CHECK(x.dim() == 4 && x.scalar_type() == at::kFloat, "mrope_cpu: x f32 [B, H, S, D]");
+  const int64_t B = x.size(0), H = x.size(1), S = x.size(2), D = x.size(3), half = D / 2;
+  TORCH_CHECK(D % 2 == 0 && s0 >= 0 && s1 >= 0 && s2 >= 0 && s0 + s1 + s2 == half, "mrope_cpu: sections");
+  TORCH_CHECK(cos.scalar_type() == at::kFloat && cos.dim() == 4 && cos.size(0) == 3 && cos.size(1) == B &&
+                  cos.size(2) == S && cos.size(3) == D && sin.sizes() == cos.sizes(),
+              "mrope_cpu: cos / sin f32 [3, B, S, D]");
+  const torch::Tensor xc = x.contiguous(), cc = cos.contiguous(), sc = sin.contiguous();
+  torch::Tensor out = torch::empty_like(xc);
+  const float* xp = xc.data_ptr<float>();
+  const float* cp = cc.data_ptr<float>();
+  const float* sp = sc.data_ptr<float>();
+  float* op = out.data_ptr<float>();
+  const int64_t plane = B * S * D;
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t h = 0; h < H; ++h)
+      for (int64_t s = 0; s < S; ++s) {
+        const float* xr = xp + ((b * H + h) * S + s) * D;
+        float* orow = op + ((b * H + h) * S + s) * D;
+        for (int64_t c = 0; c < half; ++c) {
+          const int64_t comp = c < s0 ? 0 : (c < s0 + s1 ? 1 : 2);
+          const int64_t cb = comp * plane + (b * S + s) * D;
+          orow[c] = xr[c] * cp[cb + c] - xr[c + half] * sp[cb + c];
+          orow[c + half] = xr[c + half] * cp[cb + c + half] + xr[c] * sp[cb + c + half];
+        }
+      }
+  return out;
+}
+
 }  // namespace
 
 void register_cpu_ops(py::module_& m) {
+  m.def("mrope_cpu", &mrope_cpu, "multimodal rotary embedding of x [B,H,S,D] (f32, host)");
   m.def("dequant_q8_0", &dequant_q8_0, "GGUF Q8_0 blocks -> f32");
   m.def("dequant_q4_0", &dequant_q4_0, "GGUF Q4_0 blocks -> f32");
   m.def("quantize_q8_0", &quantize_q8_0, "f32 -> GGUF Q8_0 blocks");

@@ -74,9 +74,36 @@ bool Scheduler::is_stop(const Sequence& s, int32_t tok) const {
   return false;
 }
 
+int lc_window_blocks(const SchedulerConfig& c, int block_size, int total_blocks) {
+  auto to_blocks = [&](int tokens) { return tokens <= 0 || block_size <= 0 ? 0 : (tokens + block_size - 1) / block_size; };
+  switch (c.lc_policy) {
+    case 1:
+      return to_blocks(c.lc_window_tokens);
+    case 2:
+      return to_blocks(std::max(std::max(0, c.lc_max_context - c.lc_shift), block_size));
+    default:
+      return total_blocks;
+  }
+}
+
+std::vector<int32_t> Scheduler::visible_blocks(const std::vector<int32_t>& table) const {
+  const int n = static_cast<int>(table.size());
+  const int w = lc_window_blocks(cfg_, bm_.block_size(), n);
+  if (w >= n) return table;
+  return std::vector<int32_t>(table.end() - w, table.end());
+}
+
+int Scheduler::maintain_long_context() {
+  if (cfg_.lc_policy != 3) return 0;
+  const PoolMetrics pm = bm_.metrics();
+  const int need = cfg_.lc_target_free - static_cast<int>(pm.free_blocks);
+  return need > 0 ? bm_.evict_cached(need) : 0;
+}
+
 StepMeta Scheduler::schedule() {
   if (arena_.base == nullptr) throw std::runtime_error("Scheduler: arena not set");
   if (mesh_) mesh_->begin_step();
+  maintain_long_context();
   StepMeta m;
   const int bs = bm_.block_size();
   const int ql = cfg_.spec_len > 0 ? cfg_.spec_len + 1 : 1;
@@ -215,6 +242,13 @@ StepMeta Scheduler::schedule() {
   row_draft_.clear();
   row_group_.clear();
 
+  // first block attention sees: the policy's window over the blocks covering
+  // the context, never starting after the first token of this step
+  auto window_start = [&](int ctx, int first) {
+    const int nb = (ctx + bs - 1) / bs;
+    const int w = lc_window_blocks(cfg_, bs, nb);
+    return std::max(0, std::min(nb - w, first / bs));
+  };
   int t = 0;
   int nsample = 0;
   m.all_greedy = true;
@@ -241,9 +275,10 @@ StepMeta Scheduler::schedule() {
       const int pos = s->num_computed;
       const int nb = static_cast<int>(s->table.size());
       if (nb > mb) throw std::runtime_error("Scheduler: block table wider than the arena");
-      std::copy(s->table.begin(), s->table.end(), row_bt);
-      dsl[i] = pos + ql;
-      m.max_decode_blocks = std::max(m.max_decode_blocks, (pos + ql + bs - 1) / bs);
+      const int w0 = window_start(pos + ql, pos);
+      std::copy(s->table.begin() + w0, s->table.end(), row_bt);
+      dsl[i] = pos + ql - w0 * bs;
+      m.max_decode_blocks = std::max(m.max_decode_blocks, (pos + ql + bs - 1) / bs - w0);
       const int nd = std::min<int>(static_cast<int>(s->draft.size()), ql - 1);
       for (int j = 0; j < ql; ++j) {
         const int p = pos + j;
@@ -284,11 +319,12 @@ StepMeta Scheduler::schedule() {
     }
     const int nb = static_cast<int>(s->table.size());
     if (nb > mb) throw std::runtime_error("Scheduler: block table wider than the arena");
-    std::copy(s->table.begin(), s->table.end(), pbt + static_cast<int64_t>(j) * mb);
-    pctx[j] = p.start + p.len;
+    const int w0 = window_start(p.start + p.len, p.start);
+    std::copy(s->table.begin() + w0, s->table.end(), pbt + static_cast<int64_t>(j) * mb);
+    pctx[j] = p.start + p.len - w0 * bs;
     pcu[j + 1] = pcu[j] + p.len;
     for (int r = 0; r < p.len; r += 128)
-      tiles.push_back({static_cast<int>(j), r, p.start + std::min(r + 128, p.len)});
+      tiles.push_back({static_cast<int>(j), r, p.start - w0 * bs + std::min(r + 128, p.len)});
     s->num_computed = p.start + p.len;
     if (s->num_computed == static_cast<int>(s->tokens.size())) add_sample(s, t - 1, -1, 1, 0);
   }

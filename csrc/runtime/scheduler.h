@@ -73,7 +73,23 @@ struct SchedulerConfig {
   // spec_len + 1 tokens (the last sampled token followed by spec_len
   // proposals; missing proposals are padded and always rejected).  0 = off.
   int spec_len = 0;
+  // Long-context policy (reference: scheduler/paged_cache.rs:58-90, 443-464).
+  // Full: attention sees every block.  SlidingWindow: only the blocks of the
+  // last lc_window_tokens tokens.  ContextShift: only the blocks of the last
+  // max(lc_max_context - lc_shift, block) tokens.  CompactInactive: all
+  // blocks visible; before each step cached blocks no sequence holds are
+  // evicted until lc_target_free blocks are free.  Visibility is per step
+  // and whole blocks; the window never starts inside the tokens of the
+  // current step, so every query still sees its own position.
+  int lc_policy = 0;  // 0 full, 1 sliding window, 2 context shift, 3 compact inactive
+  int lc_window_tokens = 0;
+  int lc_max_context = 0;
+  int lc_shift = 0;
+  int lc_target_free = 0;
 };
+
+// Blocks of a table of `total_blocks` that a policy keeps visible.
+int lc_window_blocks(const SchedulerConfig& c, int block_size, int total_blocks);
 
 // The scheduler writes each step's metadata into ONE pinned int32 arena in a
 // packed layout, so the runner moves it to the device with a single copy.
@@ -150,6 +166,11 @@ class Scheduler {
   int num_running() const { return static_cast<int>(running_.size()); }
 
   StepMeta schedule();
+  // Policy maintenance outside the forward pass (CompactInactive); returns
+  // the number of cache blocks freed.  schedule() runs it first.
+  int maintain_long_context();
+  // Block ids of a table visible to attention under the policy.
+  std::vector<int32_t> visible_blocks(const std::vector<int32_t>& table) const;
   std::vector<Event> update(const int32_t* sampled, int n);
 
   // ---- speculative decoding

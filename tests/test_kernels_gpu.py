@@ -484,3 +484,81 @@ def test_prefill_tc_matches_reference_long(causal):
         assert rel_err(out_tc[cu[j]:cu[j + 1]], exp) < 2e-2, j
         assert rel_err(out_mma[cu[j]:cu[j + 1]], exp) < 2e-2, j
     assert int(ops.status()[0].item()) == 0
+
+
+# ---------------------------------------------------------------- quantised formats (quant_formats.cu)
+
+
+def test_int4_flat_dequant_matches_reference():
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(3)
+    n = 128 * 37 + 40
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, ((n + 7) // 8,), dtype=torch.int32)
+    sc = torch.rand(n // 128 + 1) + 0.1
+    qz = torch.randint(-2 ** 31, 2 ** 31 - 1, ((n // 128 + 1 + 7) // 8,), dtype=torch.int32)
+    got = ops.dequant_int4_flat(qw.cuda(), sc.cuda(), qz.cuda(), n, dtype=torch.float32).cpu()
+    assert torch.allclose(got, ref.dequant_int4_flat(qw, sc, qz, n), atol=1e-5)
+    gi = torch.randint(0, sc.numel() + 3, (n - 5,), dtype=torch.int32)  # some groups and ids out of range -> 0
+    got = ops.dequant_int4_flat(qw.cuda(), sc.cuda(), qz.cuda(), n, g_idx=gi.cuda(), dtype=torch.float32).cpu()
+    assert torch.allclose(got, ref.dequant_int4_flat(qw, sc, qz, n, g_idx=gi), atol=1e-5)
+
+
+@pytest.mark.parametrize("K,N,G", [(256, 128, 128), (4096, 512, 128), (512, 64, 32)])
+def test_gptq_awq_dequant_and_gemm(K, N, G):
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(K + N)
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32)
+    qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // G, N // 8), dtype=torch.int32)
+    sc = (torch.rand(K // G, N) * 0.01 + 0.001).half()
+    gi = (torch.arange(K) // G).to(torch.int32)[torch.randperm(K)]  # act-order: permuted groups
+    w = ops.dequant_gptq(qw.cuda(), qz.cuda(), sc.cuda(), gi.cuda())
+    assert w.shape == (N, K) and rel_err(w.float().cpu(), ref.dequant_gptq(qw, qz, sc, gi)) < 5e-3
+    aw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, N // 8), dtype=torch.int32)
+    w2 = ops.dequant_awq(aw.cuda(), qz.cuda(), sc.cuda(), G)
+    assert rel_err(w2.float().cpu(), ref.dequant_awq(aw, qz, sc, G)) < 5e-3
+    x = torch.randn(33, K, device="cuda", dtype=torch.bfloat16)
+    assert rel_err(ops.gemm(x, w2), ref.gemm(x, w2)) < 1e-2
+
+
+@pytest.mark.parametrize("nf4", [True, False])
+def test_bnb4_dequant(nf4):
+    ops, ref = _ops(), _ref()
+    packed = torch.randint(0, 256, (64 * 100 + 32,), dtype=torch.uint8)
+    scale = torch.rand(packed.numel() * 2 // 64 + 1) + 0.5
+    got = ops.dequant_bnb4(packed.cuda(), scale.cuda(), 64, nf4=nf4).float().cpu()
+    assert rel_err(got, ref.dequant_bnb4(packed, scale, 64, nf4=nf4)) < 5e-3
+    g = ops.dequant_bnb4(torch.tensor([23, 240], dtype=torch.uint8, device="cuda"),
+                         torch.tensor([2.0], device="cuda"), 4, nf4=nf4).float().cpu()
+    want = [-1.3923834, 0.0, 2.0, -2.0] if nf4 else [0.125, 6.0, -6.0, 0.0]
+    assert torch.allclose(g, torch.tensor(want), atol=1e-2)
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8"])
+def test_kv_row_quant_roundtrip(kind):
+    ops, ref = _ops(), _ref()
+    x = torch.randn(1000, 1024, device="cuda", dtype=torch.bfloat16)
+    x[7] = 0
+    q, s = ops.kv_quantize(x, kind)
+    y = ops.kv_dequantize(q, s, kind)
+    assert s[7].item() == 1.0 and (y[7] == 0).all()
+    err = (y.float() - x.float()).abs().max(dim=1).values / x.float().abs().max(dim=1).values.clamp_min(1e-6)
+    assert err.max().item() < (0.01 if kind == "int8" else 0.07)
+    if kind == "int8":
+        qr, sr = ref.kv_quantize_int8(x.float().cpu())
+        assert torch.allclose(s.cpu(), sr, rtol=1e-6)
+        assert (q.cpu().view(torch.int8).int() - qr.int()).abs().max().item() <= 1
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mrope_cuda_matches_reference(dtype):
+    ops, ref = _ops(), _ref()
+    torch.manual_seed(2)
+    B, H, KVH, S, D = 2, 8, 2, 37, 128
+    q = torch.randn(B, H, S, D, device="cuda", dtype=dtype)
+    k = torch.randn(B, KVH, S, D, device="cuda", dtype=dtype)
+    pos = torch.randint(0, 4096, (3, B, S), device="cuda")
+    cos, sin = ops.mrope_cos_sin(pos, D)
+    qo, ko = ops.mrope(q, k, cos, sin)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert rel_err(qo.float().cpu(), ref.mrope(q.float().cpu(), cos.cpu(), sin.cpu())) < tol
+    assert rel_err(ko.float().cpu(), ref.mrope(k.float().cpu(), cos.cpu(), sin.cpu())) < tol

@@ -307,3 +307,65 @@ def test_cachemesh_offload_restore_and_l3(rt, tmp_path):
         assert int(l2[slot * bb]) == 10 + j
     s.take_offloads()
     assert s.cachemesh_metrics()["l2_hits"] + s.cachemesh_metrics()["l3_hits"] == 2
+
+
+def make_lc(rt, policy, **kw):
+    from bloom_b200.engine.engine import apply_long_context_policy
+
+    s, arena, mb = make(rt, **kw)
+    cfg = rt.SchedulerConfig()
+    cfg.max_num_seqs = kw.get("max_seqs", 8)
+    cfg.max_num_batched_tokens = kw.get("budget", 64)
+    cfg.max_model_len = kw.get("max_len", 512)
+    cfg.eos_token_ids = [2]
+    apply_long_context_policy(cfg, policy)
+    s = rt.Scheduler(cfg, kw.get("num_blocks", 64), 16, kw.get("prefix", True))
+    s.set_arena(arena, max(cfg.max_num_batched_tokens, cfg.max_num_seqs), cfg.max_num_seqs, mb)
+    return s, arena, mb
+
+
+def test_long_context_visible_blocks(rt):
+    # reference paged_cache.rs:1165-1187 with 16-token blocks
+    s, _, _ = make_lc(rt, "sliding_window:32")
+    assert s.visible_blocks([1, 2, 3, 4]) == [3, 4]
+    s, _, _ = make_lc(rt, "context_shift:64:16")
+    assert s.visible_blocks([10, 11, 12, 13, 14]) == [12, 13, 14]
+    s, _, _ = make_lc(rt, "full")
+    assert s.visible_blocks([1, 2, 3]) == [1, 2, 3]
+    with pytest.raises(ValueError):
+        make_lc(rt, "sliding_window")
+    with pytest.raises(ValueError):
+        make_lc(rt, "bogus:3")
+
+
+def test_sliding_window_block_tables(rt):
+    s, arena, mb = make_lc(rt, "sliding_window:32", budget=64, prefix=False)
+    s.add_request(list(range(3, 103)), params(rt, max_tokens=3))
+    m, _ = run_step(s, arena)  # prefill tokens 0..63: the window never starts inside the step
+    assert region(arena, m.off_prefill_ctx_lens, 1).tolist() == [64]
+    full = region(arena, m.off_prefill_block_table, mb).tolist()
+    m, _ = run_step(s, arena)  # tokens 64..99: blocks 4.. visible, context counted from block 4
+    assert region(arena, m.off_prefill_ctx_lens, 1).tolist() == [100 - 64]
+    bt = region(arena, m.off_prefill_block_table, 3).tolist()
+    pos = region(arena, m.off_positions, m.num_tokens, torch.int64).tolist()
+    slots = region(arena, m.off_slot_mapping, m.num_tokens).tolist()
+    assert pos[0] == 64  # rotary positions and KV slots stay absolute
+    assert not set(bt) & set(full[:4])  # the first four blocks are outside the window
+    assert all(slots[k] // 16 == bt[p // 16 - 4] for k, p in enumerate(pos))  # table starts at block 4
+    table = bt
+    m, _ = run_step(s, arena)  # decode at position 100: the last two blocks (32 tokens window)
+    assert m.num_decode == 1
+    assert region(arena, m.off_decode_seq_lens, 1).tolist() == [101 - 80]
+    assert region(arena, m.off_decode_block_table, 2).tolist() == table[1:3]
+
+
+def test_compact_inactive_releases_cached_blocks(rt):
+    s, arena, _ = make_lc(rt, "compact_inactive:8", num_blocks=8, budget=64)
+    s.add_request(list(range(500, 540)), params(rt, max_tokens=1))
+    while s.has_unfinished():
+        run_step(s, arena)
+    before = s.kv_metrics()
+    assert before["cached_blocks"] >= 2  # full prompt blocks stay in the prefix cache
+    assert s.maintain_long_context() == before["cached_blocks"]
+    after = s.kv_metrics()
+    assert after["free_blocks"] == 8 and after["active_blocks"] == 0
