@@ -26,6 +26,7 @@ last-position lm_head).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional
 
@@ -33,6 +34,10 @@ import torch
 
 from .. import ops
 from .config import ModelConfig
+
+# Row-parallel GEMMs push their partial rows to the owning ranks from the
+# epilogue (reduce-scatter fused into the GEMM); 0 keeps the pull variant.
+_TP_PUSH = os.environ.get("BLOOM_TP_PUSH", "1") != "0"
 
 
 @dataclass
@@ -376,8 +381,9 @@ class DecoderLM:
         fused = self.tp.comm.fused if (self.tp.size > 1 and self.tp.comm is not None) else None
         if fused is not None:
             T = inp.shape[0]
-            ops.gemm(inp, w_mat, fused.partial(T))
-            return fused.allreduce_rmsnorm(T, residual, norm_w, eps)
+            push = _TP_PUSH and isinstance(w_mat, torch.Tensor)
+            ops.gemm(inp, w_mat, fused.partial(T), push=fused.push_args(T) if push else None)
+            return fused.allreduce_rmsnorm(T, residual, norm_w, eps, pushed=push)
         d = self._reduce(ops.gemm(inp, w_mat))
         return ops.add_rmsnorm(d, residual, norm_w, eps)
 

@@ -137,6 +137,7 @@ def gemm(
     resid: Optional[torch.Tensor] = None,
     splits: Optional[int] = None,
     bn: Optional[int] = None,
+    push=None,
 ) -> torch.Tensor:
     """y = x @ w.T on tcgen05 (x [M,K] bf16, w [N,K] bf16) with a fused epilogue.
 
@@ -144,6 +145,11 @@ def gemm(
     per 32 rows (see `interleave_gate_up`) and returns silu(gate) * up [M, N/2].
     epi=EPI_PARTIAL_F32 returns split-K partial sums f32 [splits, M, N] that
     `add_rmsnorm` reduces.
+
+    push=(peer buffer pointers, rank, rows per rank) turns the bf16 epilogue
+    into a tensor-parallel reduce-scatter: token row t is stored into rank
+    t // rows's buffer at slot [rank][t % rows] over NVLink (see
+    parallel.fused.FusedComm.push_args); `out` then only fixes the shape.
 
     splits=None picks split-K automatically for small M (decode batches): the
     K range is split across CTAs so every SM streams weights, and the last
@@ -175,7 +181,12 @@ def gemm(
             out = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
         else:
             out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt, bn)
+    if push is not None:
+        ptrs, rank, rows = push
+        _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt, bn,
+                      list(ptrs), int(rank), int(rows))
+    else:
+        _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt, bn)
     _count()
     return out
 

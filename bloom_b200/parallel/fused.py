@@ -5,10 +5,14 @@ every rank's allocation into every process: the plumbing); all data movement
 and synchronisation is done by this repository's kernels (csrc/kernels/comm.cu)
 with 16-byte P2P loads/stores and bounded flag waits.
 
-Per row-parallel GEMM the model calls `allreduce_rmsnorm`: the GEMM writes its
-partial sums into `partial(T)`, and one kernel reduce-scatters them, adds the
-residual, applies RMSNorm and all-gathers the result into `x(T)` on every
-rank, which is the next GEMM's input.
+Per row-parallel GEMM the model calls `allreduce_rmsnorm`.  Dense layers run
+the GEMM with `push_args(T)`: its epilogue stores each finished output tile
+row straight into the owning rank's buffer over NVLink (the reduce-scatter
+is fused into the tcgen05 GEMM and overlaps its remaining tiles), and one
+kernel sums the local slots, adds the residual, applies RMSNorm and
+all-gathers the result into `x(T)` on every rank, which is the next GEMM's
+input.  Other producers (MoE) write `partial(T)` locally and the same kernel
+pulls the peers' rows instead.
 """
 from __future__ import annotations
 
@@ -32,7 +36,8 @@ class FusedComm:
         self.max_tokens = max_tokens
         self.hidden = hidden
         n = max_tokens * hidden
-        self._P = symm.empty(n, dtype=torch.bfloat16, device=device)
+        # pushed partials use [world][ceil(T / world)][H] slots: up to world - 1 rows more than T
+        self._P = symm.empty(n + world * hidden, dtype=torch.bfloat16, device=device)
         self._X = symm.empty(n, dtype=torch.bfloat16, device=device)
         fw = int(_C().tp_flag_words())
         self._F = symm.empty(fw, dtype=torch.int32, device=device)
@@ -42,7 +47,7 @@ class FusedComm:
         hX = symm.rendezvous(self._X, self.group)
         hF = symm.rendezvous(self._F, self.group)
         self._handles = (hP, hX, hF)
-        self.p_ptrs = [hP.get_buffer(r, (n,), torch.bfloat16, 0).data_ptr() for r in range(world)]
+        self.p_ptrs = [hP.get_buffer(r, (n + world * hidden,), torch.bfloat16, 0).data_ptr() for r in range(world)]
         self.x_ptrs = [hX.get_buffer(r, (n,), torch.bfloat16, 0).data_ptr() for r in range(world)]
         self.f_ptrs = [hF.get_buffer(r, (fw,), torch.int32, 0).data_ptr() for r in range(world)]
         dist.barrier(group=self.group)
@@ -55,13 +60,19 @@ class FusedComm:
         assert T <= self.max_tokens
         return self._P[:T * self.hidden].view(T, self.hidden)
 
+    def push_args(self, T: int):
+        """(peer buffers, this rank, rows per rank) for ops.gemm(push=...): the
+        GEMM writes token row t into rank t // rows's buffer, slot [rank][t % rows]."""
+        return self.p_ptrs, self.rank, (T + self.world - 1) // self.world
+
     def x(self, T: int) -> torch.Tensor:
         """[T, H] bf16 view of this rank's all-gathered input buffer."""
         return self._X[:T * self.hidden].view(T, self.hidden)
 
-    def allreduce_rmsnorm(self, T: int, residual: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    def allreduce_rmsnorm(self, T: int, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                          pushed: bool = False) -> torch.Tensor:
         _C().tp_allreduce_rmsnorm(self.p_ptrs, self.x_ptrs, self.f_ptrs, self.rank, residual, w, eps, T,
-                                  self.timeout_s, ops.status(self.device.index))
+                                  self.timeout_s, ops.status(self.device.index), pushed)
         ops._count()
         return self.x(T)
 

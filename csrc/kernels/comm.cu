@@ -77,6 +77,11 @@ struct ARArgs {
   float eps;
   uint64_t timeout_ns;
   int* status;
+  // 1: the row-parallel GEMM already pushed every rank's partial rows of this
+  // rank's slice into the local buffer as [world][rows_per_rank][H] slots
+  // (reduce-scatter fused into the GEMM epilogue); phase B then reads local
+  // memory only.  0: partials are [T, H] in each rank's own buffer (pulled).
+  int pushed;
 };
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
@@ -149,8 +154,11 @@ __global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs
 #pragma unroll
       for (int r = 0; r < kMaxRanks; ++r)
         if (r < a.world)
-          parts[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.partial.p[r]) +
-                                                     (long)row * a.H + i);
+          parts[r] = a.pushed ? *reinterpret_cast<const uint4*>(
+                                    reinterpret_cast<const __nv_bfloat16*>(a.partial.p[a.rank]) +
+                                    ((long)r * a.rows_per_rank + lr) * a.H + i)
+                              : *reinterpret_cast<const uint4*>(
+                                    reinterpret_cast<const __nv_bfloat16*>(a.partial.p[r]) + (long)row * a.H + i);
 #pragma unroll
       for (int r = 0; r < kMaxRanks; ++r)
         if (r < a.world) {
@@ -271,7 +279,7 @@ int64_t tp_flag_words() { return comm::kFlagWords; }
 void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::vector<int64_t>& x_ptrs,
                           const std::vector<int64_t>& flag_ptrs, int64_t rank, torch::Tensor& residual,
                           const torch::Tensor& w, double eps, int64_t T, double timeout_s,
-                          const torch::Tensor& status) {
+                          const torch::Tensor& status, bool pushed) {
   const int world = static_cast<int>(partial_ptrs.size());
   TORCH_CHECK(x_ptrs.size() == partial_ptrs.size() && flag_ptrs.size() == partial_ptrs.size(), "rank count mismatch");
   TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.is_contiguous(), "residual bf16 contiguous");
@@ -293,6 +301,7 @@ void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::v
   a.eps = float(eps);
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   a.status = status.data_ptr<int>();
+  a.pushed = pushed ? 1 : 0;
   const int threads = ((H / 8 + 31) / 32) * 32;
   // a fixed, fully resident grid striding over the owned rows keeps the number
   // of flag waits and remote ready-signals independent of the batch size

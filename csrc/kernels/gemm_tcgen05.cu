@@ -67,7 +67,23 @@ struct Args {
   int vec;     // output / residual rows allow 16-byte vector access
   int csplit;  // > 1: cluster split-K, one tile per cluster of csplit CTAs (one K-slice each)
   int pdl;     // launched with programmatic stream serialization (weights prefetched before the wait)
+  // Tensor-parallel reduce-scatter push (bf16 epilogue only): token row t is
+  // owned by rank t / push_rows; its partial sum goes straight to that rank's
+  // buffer over NVLink, into slot [push_rank][t % push_rows] of its
+  // [world][push_rows][ldo] layout, while the rest of the GEMM runs.
+  unsigned long long push[8];
+  int push_world, push_rank, push_rows;
 };
+
+// Row `tok` of the bf16 output: local, or the owner's slot for this rank (push).
+__device__ __forceinline__ __nv_bfloat16* out_row_bf16(const Args& a, int tok) {
+  if (a.push_world > 0) {
+    const int owner = tok / a.push_rows;
+    const int lr = tok - owner * a.push_rows;
+    return reinterpret_cast<__nv_bfloat16*>(a.push[owner]) + ((long)a.push_rank * a.push_rows + lr) * a.ldo;
+  }
+  return reinterpret_cast<__nv_bfloat16*>(a.out) + (long)tok * a.ldo;
+}
 
 __device__ __forceinline__ void trace_mark(const Args& a, int slot) {
   if (a.trace != nullptr) a.trace[blockIdx.x * 8 + slot] = globaltimer_ns();
@@ -223,7 +239,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int
         if constexpr (EPI == kEpiBF16) {
 #pragma unroll
           for (int k = 0; k < 8; ++k) x[k] += bias[k];
-          store8_bf16(reinterpret_cast<__nv_bfloat16*>(a.out) + (long)tok * a.ldo + f, x, nf, a.vec);
+          store8_bf16(out_row_bf16(a, tok) + f, x, nf, a.vec);
         } else if constexpr (EPI == kEpiF32) {
 #pragma unroll
           for (int k = 0; k < 8; ++k) x[k] += bias[k];
@@ -654,6 +670,8 @@ __global__ void __launch_bounds__(192, 1)
   // every thread of the cluster takes part in the split-K cluster barrier
   // (epilogue warps that reached their tile took it above)
   if (a.csplit > 1 && !csplit_armed) cluster_sync_all();
+  // pushed rows are performed at system scope before the kernel completes
+  if (a.push_world > 0 && warp >= 2) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -899,6 +917,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
 
+  if (a.push_world > 0 && warp >= 2) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // no remote arrival or MMA into this CTA is outstanding past this point
@@ -1097,7 +1116,8 @@ int gemm_default_splits(int M, int N, int K, int device) {
 void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int64_t epi,
               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
               const torch::Tensor& status, const c10::optional<torch::Tensor>& fix_ws,
-              const c10::optional<torch::Tensor>& fix_count, int64_t bn_override) {
+              const c10::optional<torch::Tensor>& fix_count, int64_t bn_override,
+              const std::vector<int64_t>& push_ptrs, int64_t push_rank, int64_t push_rows) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "gemm: tensors must be on CUDA");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: x and w must be bf16");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm: x [M,K], w [N,K]");
@@ -1140,6 +1160,25 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.wpol = a.num_tok_tiles > 1 ? 1 : 0;
   a.trace = g_gemm_trace;
   a.csplit = 1;
+  a.push_world = 0;
+  a.push_rank = 0;
+  a.push_rows = 0;
+  for (int r = 0; r < 8; ++r) a.push[r] = 0;
+  if (!push_ptrs.empty()) {
+    TORCH_CHECK(epi == kEpiBF16 && !bias.has_value(), "gemm push: plain bf16 epilogue only");
+    TORCH_CHECK(push_ptrs.size() <= 8 && push_rank >= 0 && push_rank < (int64_t)push_ptrs.size(),
+                "gemm push: up to 8 ranks");
+    TORCH_CHECK(push_rows > 0 && push_rows * (int64_t)push_ptrs.size() >= M, "gemm push: rows per rank cover M");
+    TORCH_CHECK(out.dim() == 2 && out.size(1) == N && out.stride(1) == 1 && out.stride(0) == N,
+                "gemm push: out [M, N] contiguous rows (the peers' slot pitch)");
+    for (size_t r = 0; r < push_ptrs.size(); ++r) {
+      TORCH_CHECK(push_ptrs[r] % 16 == 0, "gemm push: peer buffers must be 16-byte aligned");
+      a.push[r] = static_cast<unsigned long long>(push_ptrs[r]);
+    }
+    a.push_world = static_cast<int>(push_ptrs.size());
+    a.push_rank = static_cast<int>(push_rank);
+    a.push_rows = static_cast<int>(push_rows);
+  }
   {
     static const int env_pdl = [] {
       const char* e = std::getenv("BLOOM_PDL");

@@ -266,9 +266,92 @@ torch::Tensor mrope_cpu(const torch::Tensor& x, const torch::Tensor& cos, const 
   return out;
 }
 
+// Small host kernels kept as CPU oracles (the reference generates them as
+// TileLang C++: crates/tilelang/scripts/generate_kernel.py:7-102): elementwise
+// add, row-major matmul, softmax of a vector, and single-head attention with
+// an online (running max / running sum) softmax.
+torch::Tensor oracle_vector_add(const torch::Tensor& a, const torch::Tensor& b) {
+  TORCH_CHECK(a.scalar_type() == at::kFloat && b.scalar_type() == at::kFloat && a.numel() == b.numel(),
+              "vector_add: two f32 tensors of one size");
+  const torch::Tensor ac = a.contiguous(), bc = b.contiguous();
+  torch::Tensor c = torch::empty_like(ac);
+  const float* pa = ac.data_ptr<float>();
+  const float* pb = bc.data_ptr<float>();
+  float* pc = c.data_ptr<float>();
+  for (int64_t i = 0; i < ac.numel(); ++i) pc[i] = pa[i] + pb[i];
+  return c;
+}
+
+torch::Tensor oracle_matmul(const torch::Tensor& a, const torch::Tensor& b) {
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(0) && a.scalar_type() == at::kFloat &&
+                  b.scalar_type() == at::kFloat,
+              "matmul: f32 [m, k] @ [k, n]");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(1);
+  const torch::Tensor ac = a.contiguous(), bc = b.contiguous();
+  torch::Tensor c = torch::zeros({M, N}, a.options());
+  const float* pa = ac.data_ptr<float>();
+  const float* pb = bc.data_ptr<float>();
+  float* pc = c.data_ptr<float>();
+  for (int64_t i = 0; i < M; ++i)
+    for (int64_t k = 0; k < K; ++k) {
+      const float x = pa[i * K + k];
+      for (int64_t j = 0; j < N; ++j) pc[i * N + j] += x * pb[k * N + j];
+    }
+  return c;
+}
+
+torch::Tensor oracle_softmax(const torch::Tensor& x) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.numel() > 0, "softmax: non-empty f32");
+  const torch::Tensor xc = x.contiguous();
+  torch::Tensor y = torch::empty_like(xc);
+  const float* px = xc.data_ptr<float>();
+  float* py = y.data_ptr<float>();
+  const int64_t n = xc.numel();
+  float mx = px[0];
+  for (int64_t i = 1; i < n; ++i) mx = std::max(mx, px[i]);
+  double sum = 0.0;
+  for (int64_t i = 0; i < n; ++i) sum += std::exp(static_cast<double>(px[i] - mx));
+  for (int64_t i = 0; i < n; ++i) py[i] = static_cast<float>(std::exp(static_cast<double>(px[i] - mx)) / sum);
+  return y;
+}
+
+torch::Tensor oracle_attention(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v) {
+  TORCH_CHECK(q.dim() == 2 && k.sizes() == q.sizes() && v.sizes() == q.sizes() && q.scalar_type() == at::kFloat,
+              "attention: f32 q, k, v [seq, head_dim]");
+  const int64_t S = q.size(0), D = q.size(1);
+  const torch::Tensor qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
+  torch::Tensor o = torch::zeros_like(qc);
+  const float* pq = qc.data_ptr<float>();
+  const float* pk = kc.data_ptr<float>();
+  const float* pv = vc.data_ptr<float>();
+  float* po = o.data_ptr<float>();
+  const float scale = 1.0f / std::sqrt(static_cast<float>(D));
+  for (int64_t r = 0; r < S; ++r) {
+    float m = -INFINITY, l = 0.f;
+    float* orow = po + r * D;
+    for (int64_t j = 0; j < S; ++j) {
+      float dot = 0.f;
+      for (int64_t d = 0; d < D; ++d) dot += pq[r * D + d] * pk[j * D + d];
+      const float s = dot * scale;
+      const float mn = std::max(m, s);
+      const float alpha = std::exp(m - mn);  // rescales what was accumulated under the old max
+      const float p = std::exp(s - mn);
+      l = l * alpha + p;
+      for (int64_t d = 0; d < D; ++d) orow[d] = orow[d] * alpha + p * pv[j * D + d];
+      m = mn;
+    }
+    for (int64_t d = 0; d < D; ++d) orow[d] /= l;
+  }
+  return o;
+}
+
 }  // namespace
 
 void register_cpu_ops(py::module_& m) {
+  m.def("oracle_vector_add", &oracle_vector_add, "c = a + b (f32, host)");
+  m.def("oracle_matmul", &oracle_matmul, "c = a @ b (f32 row-major, host)");
+  m.def("oracle_softmax", &oracle_softmax, "softmax of a f32 vector (host)");
+  m.def("oracle_attention", &oracle_attention, "single-head attention with online softmax (f32, host)");
   m.def("mrope_cpu", &mrope_cpu, "multimodal rotary embedding of x [B,H,S,D] (f32, host)");
   m.def("dequant_q8_0", &dequant_q8_0, "GGUF Q8_0 blocks -> f32");
   m.def("dequant_q4_0", &dequant_q4_0, "GGUF Q4_0 blocks -> f32");

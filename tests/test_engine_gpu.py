@@ -20,7 +20,8 @@ def _build(name, std=0.08, graphs=True, **kw):
     model.shard_full(w)
     ec = EngineConfig(max_num_seqs=kw.get("max_num_seqs", 16), max_num_batched_tokens=kw.get("budget", 512),
                       max_model_len=512, num_blocks=kw.get("num_blocks", 256), use_cuda_graphs=graphs,
-                      enable_prefix_caching=kw.get("prefix", True))
+                      enable_prefix_caching=kw.get("prefix", True),
+                      long_context_policy=kw.get("policy", "full"))
     return cfg, w, LLMEngine(model, ec)
 
 
@@ -255,3 +256,25 @@ def test_cachemesh_restores_evicted_prefix(tmp_path):
     assert mesh["offloads"] > 0 and mesh["l2_hits"] + mesh["l3_hits"] > 0, mesh
     assert again.token_ids == first
     assert eng.runner.stats["kv_restores"] > 0
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_sliding_window_policy(graphs):
+    """A window covering the whole context changes nothing; a 32-token window
+    attends to the last two blocks only and still decodes (finite logits,
+    no kernel timeouts)."""
+    from bloom_b200 import ops
+    from bloom_b200.engine.engine import SamplingParams
+
+    torch.manual_seed(1)
+    sp = SamplingParams(max_tokens=10, temperature=0.0, ignore_eos=True)
+    cfg, w, eng = _build("tiny-llama", graphs=graphs, policy="sliding_window:512")
+    prompts = [torch.randint(3, cfg.vocab_size, (n,)).tolist() for n in (100, 37, 3)]
+    outs = eng.generate(prompts, sp)
+    for p, o in zip(prompts, outs):
+        _check_greedy(cfg, w, p, o.token_ids)
+    _, _, small = _build("tiny-llama", graphs=graphs, policy="sliding_window:32", budget=64)
+    outs2 = small.generate(prompts, sp)
+    assert all(len(o.token_ids) == 10 and all(0 <= t < cfg.vocab_size for t in o.token_ids) for o in outs2)
+    _check_greedy(cfg, w, prompts[2], outs2[2].token_ids)  # 3 + 10 tokens fit in the window
+    assert int(ops.status()[0].item()) == 0

@@ -562,3 +562,25 @@ def test_mrope_cuda_matches_reference(dtype):
     tol = 1e-5 if dtype == torch.float32 else 1e-2
     assert rel_err(qo.float().cpu(), ref.mrope(q.float().cpu(), cos.cpu(), sin.cpu())) < tol
     assert rel_err(ko.float().cpu(), ref.mrope(k.float().cpu(), cos.cpu(), sin.cpu())) < tol
+
+
+@pytest.mark.parametrize("M,splits", [(7, 1), (256, 1), (256, 3), (1000, 1)])
+def test_gemm_push_slots(M, splits):
+    """Reduce-scatter push addressing, emulated with two local buffers as the
+    two ranks' receive buffers: row t lands in buffer t // rows at slot
+    [rank][t % rows]; nothing else is written."""
+    ops, ref = _ops(), _ref()
+    N, K, world, rank = 512, 1024, 2, 1
+    rows = (M + world - 1) // world
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    bufs = [torch.zeros(world * rows + 1, N, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ops.gemm(x, w, out, splits=splits, push=([b.data_ptr() for b in bufs], rank, rows))
+    want = ref.gemm(x, w)
+    for t0 in range(0, M, rows):
+        owner = t0 // rows
+        got = bufs[owner][rank * rows: rank * rows + min(rows, M - t0)]
+        assert rel_err(got, want[t0: t0 + got.shape[0]]) < 1e-2
+        assert bufs[owner][: rank * rows].abs().max().item() == 0
+        assert bufs[owner][rank * rows + got.shape[0]:].abs().max().item() == 0

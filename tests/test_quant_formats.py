@@ -149,3 +149,19 @@ def test_mrope_cpu_matches_torch_restatement():
     c1, s1 = ops.mrope_cos_sin(p1, D)
     plain = x * c1[0][:, None] + torch.cat([-x[..., D // 2:], x[..., :D // 2]], -1) * s1[0][:, None]
     assert torch.allclose(rt.mrope_cpu(x, c1, s1, 24, 20, 20), plain, atol=1e-5)
+
+
+def test_cpu_oracle_kernels():
+    from bloom_b200._ext import runtime
+
+    rt = runtime()
+    torch.manual_seed(4)
+    a, b = torch.randn(1000), torch.randn(1000)
+    assert torch.allclose(rt.oracle_vector_add(a, b), a + b)
+    A, B = torch.randn(17, 33), torch.randn(33, 9)
+    assert torch.allclose(rt.oracle_matmul(A, B), A @ B, atol=1e-4)
+    x = torch.randn(257) * 5
+    assert torch.allclose(rt.oracle_softmax(x), torch.softmax(x, 0), atol=1e-6)
+    q, k, v = torch.randn(3, 40, 64).unbind(0)
+    want = torch.softmax(q @ k.t() / 8.0, dim=-1) @ v
+    assert torch.allclose(rt.oracle_attention(q, k, v), want, atol=1e-4)
