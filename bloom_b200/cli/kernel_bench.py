@@ -93,6 +93,10 @@ def sweep_gemm(ops, name, M, N, K, epi, x, ws, out, nrot, *, trace, report):
                 ops._C().gemm_set_trace(None)
                 t = tr.view(-1, 8).cpu()
                 t = t[t[:, 0] > 0].double()
+                if t.shape[0] == 0:  # the 2-CTA kernel ran (it records no timeline)
+                    extra["note"] = "2-CTA kernel, no timeline"
+                    report(f"gemm_{name}_trace", float("nan"), None, None, extra)
+                    continue
                 rel = (t - t[:, 0].min()) / 1000.0
                 names = {0: "entry", 2: "first_stage", 4: "acc_ready", 5: "written", 7: "cluster_barrier",
                          6: "reduced"}
@@ -237,6 +241,26 @@ def main():
                                                             scale=hd ** -0.5))
         flops = S * 4.0 * Lq * Lq / 2 * hd * nq
         report("paged_prefill_attention", ms, flops, None, {"seqs": S, "len": Lq})
+        if args.trace:
+            # per-CTA phase profile of one launch: thread 0's clock64 cycles per kv tile
+            ctas = int(ts_.numel()) * nq
+            tr = torch.zeros(ctas * 16, dtype=torch.int64, device=dev)
+            ops._C().attn_tc_set_trace(tr)
+            ops.paged_prefill_attention(q2, cache2, 0, bt2, ctx_t, cu_t, ts_, tst, o2, scale=hd ** -0.5)
+            torch.cuda.synchronize()
+            ops._C().attn_tc_set_trace(None)
+            t = tr.view(ctas, 16).cpu().double()
+            t = t[t[:, 0] > 0]
+            nkt = t[:, 10].sum().item()
+            names = ["issue_S_next", "barrier", "wait_S", "load_S_rowmax", "wait_PV_prev", "exp_P_store",
+                     "issue_PV"]
+            extra = {"ctas": int(t.shape[0]), "kv_tiles": int(nkt),
+                     "loop_cycles_per_tile": round(t[:, 2].sum().item() / max(nkt, 1), 1),
+                     "launch_us": round((t[:, 1].max() - t[:, 0].min()).item() / 1000.0, 2),
+                     "cta_us_median": round(float((t[:, 1] - t[:, 0]).median()) / 1000.0, 2)}
+            for k, nm in enumerate(names):
+                extra[nm + "_cycles_per_tile"] = round(t[:, 3 + k].sum().item() / max(nkt, 1), 1)
+            report("paged_prefill_attention_profile", float("nan"), None, None, extra)
 
     if not args.only or "norm" in args.only:
         for M in (256, 8192):

@@ -65,6 +65,14 @@ struct Args {
   float scale_log2;
   int causal;
   int* status;
+  // optional per-CTA profile (CTA = blockIdx.y * gridDim.x + blockIdx.x, 16
+  // words each, CTAs past trace_ctas skipped): [0] %globaltimer at entry,
+  // [1] at exit, [2] clock64 cycles of the kv loop, [3..9] cycles of thread 0
+  // per loop phase summed over kv tiles: S(j+1) issue incl. its K wait, first
+  // barrier, S(j) wait, S load + row max, P V(j-1) wait, exp + P store +
+  // barrier, P V(j) issue incl. its V wait; [10] kv tiles
+  unsigned long long* trace;
+  int trace_ctas;
 };
 
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const float (&v)[16]) {
@@ -127,6 +135,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tile = blockIdx.x, h = blockIdx.y;
+  const long cta = (long)blockIdx.y * gridDim.x + blockIdx.x;
+  unsigned long long* tr = (a.trace != nullptr && cta < a.trace_ctas) ? a.trace + cta * 16 : nullptr;
+  if (tr != nullptr && threadIdx.x == 0) tr[0] = globaltimer_ns();
   const int warp = warp_id(), lane = lane_id();
   const int G = a.nq / a.nkv;
   const int kh = h / G;
@@ -231,6 +242,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f;
     bool failed = false;
     int j = 0;
+    long long ph[7] = {0, 0, 0, 0, 0, 0, 0};
+    long long tprev = clock64();
+    const long long tloop = tprev;
+    auto lap = [&](int k) {  // thread 0's time in phase k since the previous lap
+      if (tr != nullptr && threadIdx.x == 0) {
+        const long long t1 = clock64();
+        ph[k] += t1 - tprev;
+        tprev = t1;
+      }
+    };
     // S(jt) = Q K(jt)^T into S buffer jt % 2 (leader only)
     auto issue_s = [&](int jt) -> bool {
       const int sk = jt % kStages;
@@ -253,15 +274,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; j < n_kt; ++j) {
       // ---- S(j+1) on the tensor cores while this tile's softmax runs
       if (leader && !failed && j + 1 < n_kt && !issue_s(j + 1)) failed = true;
+      lap(0);
       if (named_sync_or(failed)) {
         failed = true;
         break;
       }
+      lap(1);
       if (!mbar_wait(&s_done[j & 1], (j >> 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
       if (named_sync_or(failed)) {
         failed = true;
         break;
       }
+      lap(2);
       tc_fence_after();
       // ---- this thread's 64 columns of its row
       float sv[64];
@@ -293,12 +317,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       red_m[threadIdx.x] = mx;
+      lap(3);
       // the previous P V must be done before P is rewritten and before O is rescaled
       if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
       if (named_sync_or(failed)) {
         failed = true;
         break;
       }
+      lap(4);
       tc_fence_after();
       mx = fmaxf(mx, red_m[threadIdx.x ^ 128]);  // the row max over both halves
       const float m_new = fmaxf(m, mx);
@@ -341,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       named_sync_softmax();
+      lap(5);
       // ---- O += P V
       if (leader) {
         const int sv_ = j % kStages;
@@ -360,6 +387,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           failed = true;
         }
       }
+      lap(6);
+    }
+    if (tr != nullptr && threadIdx.x == 0) {
+      tr[2] = static_cast<unsigned long long>(clock64() - tloop);
+      for (int k = 0; k < 7; ++k) tr[3 + k] = static_cast<unsigned long long>(ph[k]);
+      tr[10] = static_cast<unsigned long long>(n_kt);
     }
     if (!failed && n_kt > 0) {
       if (!mbar_wait(o_done, (n_kt - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
@@ -403,9 +436,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (tr != nullptr && threadIdx.x == 0) tr[1] = globaltimer_ns();
 }
 
 }  // namespace attn_tc
+
+// Per-CTA profile buffer of the next prefill launches (see Args::trace).
+static unsigned long long* g_attn_tc_trace = nullptr;
+static int g_attn_tc_trace_ctas = 0;
+
+void attn_tc_set_trace(const c10::optional<torch::Tensor>& buf) {
+  if (buf.has_value() && buf->defined()) {
+    TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong, "attn trace: int64 CUDA tensor");
+    g_attn_tc_trace = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    g_attn_tc_trace_ctas = static_cast<int>(buf->numel() / 16);
+  } else {
+    g_attn_tc_trace = nullptr;
+    g_attn_tc_trace_ctas = 0;
+  }
+}
 
 void paged_prefill_attention_tc(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
                                 const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
@@ -435,6 +484,8 @@ void paged_prefill_attention_tc(const torch::Tensor& q, const torch::Tensor& kv_
   a.scale_log2 = float(scale * 1.4426950408889634);
   a.causal = causal ? 1 : 0;
   a.status = status.data_ptr<int>();
+  a.trace = g_attn_tc_trace;
+  a.trace_ctas = g_attn_tc_trace_ctas;
   const uint64_t rows = (uint64_t)kv_cache.size(1) * 2 * kv_cache.size(3) * attn_tc::PAGE;
   TORCH_CHECK(rows < (1ull << 31), "prefill_tc: kv_cache too many rows per layer for int32 TMA coordinates");
   const auto* base = reinterpret_cast<const __nv_bfloat16*>(kv_cache.data_ptr()) + layer * kv_cache.stride(0);
