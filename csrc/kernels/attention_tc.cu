@@ -70,7 +70,8 @@ struct Args {
   // [1] at exit, [2] clock64 cycles of the kv loop, [3..9] cycles of thread 0
   // per loop phase summed over kv tiles: S(j+1) issue incl. its K wait, first
   // barrier, S(j) wait, S load + row max, P V(j-1) wait, exp + P store +
-  // barrier, P V(j) issue incl. its V wait; [10] kv tiles
+  // barrier, P V(j) issue incl. its V wait; [10] kv tiles; [11] / [12] cycles
+  // of the K / V tile waits inside [3] / [9]
   unsigned long long* trace;
   int trace_ctas;
 };
@@ -181,32 +182,65 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       bool ok = true;
       int issuedK = 0, issuedV = 0;
-      auto load_tile = [&](int jt, uint8_t* dst, uint64_t* bar, int kv) {
-        mbar_arrive_expect_tx(bar, kTileBytes);
-#pragma unroll 1
+      // Block ids of a kv tile's 8 pages: independent loads issued together
+      // (one memory latency per tile, not one per page); the next K tile's
+      // ids are fetched right after its predecessor's copies are issued, so
+      // their latency hides behind the ring waits.
+      auto fetch_ids = [&](int jt, int (&ids)[kKv / PAGE]) {
+#pragma unroll
         for (int pg = 0; pg < kKv / PAGE; ++pg) {
           const int page = jt * (kKv / PAGE) + pg;
-          const int blk = bt[page < n_pages ? page : 0];
-          const int row = ((blk * 2 + kv) * a.nkv + kh) * PAGE;
+          ids[pg] = __ldg(bt + (page < n_pages ? page : 0));
+        }
+      };
+      auto load_tile = [&](const int (&ids)[kKv / PAGE], uint8_t* dst, uint64_t* bar, int kv) {
+        mbar_arrive_expect_tx(bar, kTileBytes);
+#pragma unroll
+        for (int pg = 0; pg < kKv / PAGE; ++pg) {
+          const int row = ((ids[pg] * 2 + kv) * a.nkv + kh) * PAGE;
           tma_load_2d(dst + pg * 2048, &tmKV, bar, 0, row);
           tma_load_2d(dst + kRegion + pg * 2048, &tmKV, bar, 64, row);
         }
       };
-      for (int jt = 0; jt < n_kt && ok; ++jt) {
-        const int s = jt % kStages;
-        const uint32_t par = ((jt / kStages) & 1) ^ 1u;
-        if (!mbar_wait(&emptyK[s], par, abort_flag, a.status, kStatusAttnTimeout)) {
-          ok = false;
-          break;
+      int idsK[kKv / PAGE], idsV[kKv / PAGE];
+      if (n_kt > 0) fetch_ids(0, idsK);
+      // K and V rings advance independently: a K tile is requested as soon as
+      // its slot is free (S of the tile two back done), without queueing
+      // behind the V tile whose slot waits for an older P V; V never runs
+      // ahead of K.  Bounded: no progress for kLocalWaitTimeoutNs -> error.
+      uint64_t t_prog = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ok && (issuedK < n_kt || issuedV < n_kt)) {
+        bool progressed = false;
+        if (issuedK < n_kt) {
+          const int s = issuedK % kStages;
+          if (mbar_try_wait(&emptyK[s], ((issuedK / kStages) & 1) ^ 1u)) {
+            load_tile(idsK, sK + s * kTileBytes, &fullK[s], 0);
+            ++issuedK;
+            if (issuedK < n_kt) fetch_ids(issuedK, idsK);
+            progressed = true;
+          }
         }
-        load_tile(jt, sK + s * kTileBytes, &fullK[s], 0);
-        ++issuedK;
-        if (!mbar_wait(&emptyV[s], par, abort_flag, a.status, kStatusAttnTimeout)) {
-          ok = false;
-          break;
+        if (issuedV < issuedK) {
+          const int s = issuedV % kStages;
+          if (mbar_try_wait(&emptyV[s], ((issuedV / kStages) & 1) ^ 1u)) {
+            fetch_ids(issuedV, idsV);  // the K tile of the same index read these ids: cache hits
+            load_tile(idsV, sV + s * kTileBytes, &fullV[s], 1);
+            ++issuedV;
+            progressed = true;
+          }
         }
-        load_tile(jt, sV + s * kTileBytes, &fullV[s], 1);
-        ++issuedV;
+        if (progressed) {
+          t_prog = globaltimer_ns();
+        } else if ((++spins & 31u) == 0) {
+          if (*abort_flag) {
+            ok = false;
+          } else if (globaltimer_ns() - t_prog > kLocalWaitTimeoutNs) {
+            *abort_flag = 1;
+            atomicOr(a.status, kStatusAttnTimeout);
+            ok = false;
+          }
+        }
       }
       if (!ok) {  // wait (bounded) for the loads already in flight before leaving
         for (int jt = max(0, issuedK - kStages); jt < issuedK; ++jt)
@@ -243,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool failed = false;
     int j = 0;
     long long ph[7] = {0, 0, 0, 0, 0, 0, 0};
+    long long wK = 0, wV = 0;  // thread 0's cycles waiting for K / V tiles to land
     long long tprev = clock64();
     const long long tloop = tprev;
     auto lap = [&](int k) {  // thread 0's time in phase k since the previous lap
@@ -255,7 +290,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // S(jt) = Q K(jt)^T into S buffer jt % 2 (leader only)
     auto issue_s = [&](int jt) -> bool {
       const int sk = jt % kStages;
+      const long long tw = tr != nullptr ? clock64() : 0;
       if (!mbar_wait(&fullK[sk], (jt / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout)) return false;
+      if (tr != nullptr) wK += clock64() - tw;
       tc_fence_after();
       const uint32_t kb = smem_u32(sK + sk * kTileBytes);
       const uint32_t qb = smem_u32(sQ);
@@ -371,7 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- O += P V
       if (leader) {
         const int sv_ = j % kStages;
-        if (mbar_wait(&fullV[sv_], (j / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout)) {
+        const long long tw = tr != nullptr ? clock64() : 0;
+        const bool vok = mbar_wait(&fullV[sv_], (j / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout);
+        if (tr != nullptr) wV += clock64() - tw;
+        if (vok) {
           tc_fence_after();
           const uint32_t pb = smem_u32(sP);
           const uint32_t vb = smem_u32(sV + sv_ * kTileBytes);
@@ -393,6 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tr[2] = static_cast<unsigned long long>(clock64() - tloop);
       for (int k = 0; k < 7; ++k) tr[3 + k] = static_cast<unsigned long long>(ph[k]);
       tr[10] = static_cast<unsigned long long>(n_kt);
+      tr[11] = static_cast<unsigned long long>(wK);
+      tr[12] = static_cast<unsigned long long>(wV);
     }
     if (!failed && n_kt > 0) {
       if (!mbar_wait(o_done, (n_kt - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
