@@ -260,8 +260,10 @@ def main():
                      "cta_us_median": round(float((t[:, 1] - t[:, 0]).median()) / 1000.0, 2)}
             for k, nm in enumerate(names):
                 extra[nm + "_cycles_per_tile"] = round(t[:, 3 + k].sum().item() / max(nkt, 1), 1)
-            extra["of_which_wait_K_cycles_per_tile"] = round(t[:, 11].sum().item() / max(nkt, 1), 1)
-            extra["of_which_wait_V_cycles_per_tile"] = round(t[:, 12].sum().item() / max(nkt, 1), 1)
+            extra["mma_warp_wait_K_cycles_per_tile"] = round(t[:, 11].sum().item() / max(nkt, 1), 1)
+            extra["mma_warp_wait_V_cycles_per_tile"] = round(t[:, 12].sum().item() / max(nkt, 1), 1)
+            extra["mma_warp_wait_QP_cycles_per_tile"] = round(t[:, 13].sum().item() / max(nkt, 1), 1)
+            extra["mma_warp_wait_Sfree_cycles_per_tile"] = round(t[:, 14].sum().item() / max(nkt, 1), 1)
             report("paged_prefill_attention_profile", float("nan"), None, None, extra)
 
     if not args.only or "norm" in args.only:

@@ -22,8 +22,8 @@
 // tile j, and P(j) V(j) runs while the next softmax starts.
 // Warp roles: warps 0-7 softmax and epilogue, two threads per query row
 // (warps w and w+4 read the same TMEM lanes, columns 0-63 and 64-127; the row
-// max and sum are combined through shared memory); thread 0 also issues the
-// MMAs; warp 8 is the TMA producer and TMEM owner.  Every wait is bounded (status bit +
+// max and sum are combined through shared memory); warp 8 is the TMA producer
+// and TMEM owner; warp 9 issues the MMAs.  Every wait is bounded (status bit +
 // return).  Reference behaviour: causal GQA attention over the paged cache
 // (scheduler/paged_cache.rs:565-748).
 #include <ATen/cuda/CUDAContext.h>
@@ -47,7 +47,7 @@ constexpr int kPBytes = kRows * kKv * 2;   // 32 KB
 constexpr int kTileBytes = 2 * kRegion;    // one K or V tile = 32 KB
 constexpr int kStages = 2;                 // separate K and V rings of kStages tiles each
 constexpr int kSoftmaxThreads = 256;      // two threads per query row (64 columns each)
-constexpr int kThreads = kSoftmaxThreads + 32;
+constexpr int kThreads = kSoftmaxThreads + 64;  // + TMA producer warp + MMA warp
 constexpr int kSmem = kQBytes + kPBytes + 2 * kStages * kTileBytes + 256 + 1024;
 constexpr int kTmemCols = 512;             // S0 [0,128), S1 [128,256), O [256,384)
 constexpr float kLazy = 8.f;               // rescale threshold (log2 units)
@@ -70,8 +70,8 @@ struct Args {
   // [1] at exit, [2] clock64 cycles of the kv loop, [3..9] cycles of thread 0
   // per loop phase summed over kv tiles: S(j+1) issue incl. its K wait, first
   // barrier, S(j) wait, S load + row max, P V(j-1) wait, exp + P store +
-  // barrier, P V(j) issue incl. its V wait; [10] kv tiles; [11] / [12] cycles
-  // of the K / V tile waits inside [3] / [9]
+  // barrier, P-ready signal; [10] kv tiles; MMA warp: [11] / [12] cycles
+  // waiting for K / V tiles, [13] for Q and P, [14] for a free S buffer
   unsigned long long* trace;
   int trace_ctas;
 };
@@ -132,7 +132,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_done = bars + 8;      // [2]: one per S buffer
   uint64_t* o_done = bars + 10;
   uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* s_free = bars + 12;     // [2]: the softmax has read S buffer b (one arrival per softmax warp)
+  uint64_t* p_ready = bars + 14;    // P of the current tile is in shared memory, O rescaled
+  uint64_t* q_ready = bars + 15;    // the Q tile is in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tile = blockIdx.x, h = blockIdx.y;
@@ -164,6 +167,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&s_done[1], 1);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
+    mbar_init(&s_free[0], kSoftmaxThreads / 32);
+    mbar_init(&s_free[1], kSoftmaxThreads / 32);
+    mbar_init(p_ready, 1);
+    mbar_init(q_ready, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -249,13 +256,83 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_drain(&fullV[jt % kStages], (jt / kStages) & 1);
       }
     }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    // One thread issues every tcgen05.mma: S(j+1) = Q K(j+1)^T goes into the
+    // free S buffer while the softmax of tile j runs, then O += P(j) V(j)
+    // once the softmax has written P(j).  An MMA issue blocks its thread while
+    // the tensor pipe drains its queue, so it lives in its own warp: the
+    // softmax warps never wait on it.
+    if (lane == 0) {
+      constexpr uint32_t idS = umma_idesc_bf16(128, kKv);
+      constexpr uint32_t idO = idesc_bf16_bmn(128, D);
+      bool ok = true, issued_any = false;
+      long long wK = 0, wV = 0, wP = 0, wF = 0;
+      auto timed_wait = [&](uint64_t* bar, uint32_t par, long long& acc) -> bool {
+        const long long tw = tr != nullptr ? clock64() : 0;
+        const bool r = mbar_wait(bar, par, abort_flag, a.status, kStatusAttnTimeout);
+        if (tr != nullptr) acc += clock64() - tw;
+        return r;
+      };
+      auto issue_s = [&](int jt) -> bool {
+        if (jt >= 2 && !timed_wait(&s_free[jt & 1], ((jt >> 1) - 1) & 1, wF)) return false;
+        const int sk = jt % kStages;
+        if (!timed_wait(&fullK[sk], (jt / kStages) & 1, wK)) return false;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(sK + sk * kTileBytes);
+        const uint32_t qb = smem_u32(sQ);
+        const uint32_t tS = tmem_base + 128u * static_cast<uint32_t>(jt & 1);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(qb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
+          const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * kRegion) + 2 * (kk & 3);
+          umma_f16(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
+        }
+        issued_any = true;
+        umma_commit(&s_done[jt & 1]);
+        umma_commit(&emptyK[sk]);
+        return true;
+      };
+      if (n_kt > 0) ok = timed_wait(q_ready, 0, wP) && issue_s(0);
+      for (int j = 0; j < n_kt && ok; ++j) {
+        if (j + 1 < n_kt && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        const int sv_ = j % kStages;
+        if (!timed_wait(p_ready, j & 1, wP) || !timed_wait(&fullV[sv_], (j / kStages) & 1, wV)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t pb = smem_u32(sP);
+        const uint32_t vb = smem_u32(sV + sv_ * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kKv / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(pb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
+          const uint64_t bd = umma_desc_sw128_mn(vb + kk * 16 * 128, kRegion, 1024);
+          umma_f16(tO, ad, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done);
+        umma_commit(&emptyV[sv_]);
+      }
+      if (!ok && issued_any) {  // let the tensor pipe finish what was issued before TMEM is freed
+        umma_commit(drain);
+        mbar_drain(drain, 0);
+      }
+      if (tr != nullptr) {
+        tr[11] = static_cast<unsigned long long>(wK);
+        tr[12] = static_cast<unsigned long long>(wV);
+        tr[13] = static_cast<unsigned long long>(wP);
+        tr[14] = static_cast<unsigned long long>(wF);
+      }
+    }
   } else {
     // ---------------------------------------------------------------- softmax warps
     __shared__ float red_m[kSoftmaxThreads], red_l[kSoftmaxThreads];
     const int t = threadIdx.x & (kRows - 1);  // query row of the tile, = TMEM lane
     const int half = threadIdx.x >> 7;        // columns [64 * half, 64 * half + 64)
     const int cb = half * 64;
-    const bool leader = threadIdx.x == 0;     // issues the MMAs
     const int lr = row0 + t;
     const bool valid = lr < q_len;
     // rows past the chunk keep a finite softmax (no masking) and are not stored
@@ -270,14 +347,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     named_sync_softmax();
+    if (threadIdx.x == 0) mbar_arrive(q_ready);
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    constexpr uint32_t idS = umma_idesc_bf16(128, kKv);
-    constexpr uint32_t idO = idesc_bf16_bmn(128, D);
     float m = -INFINITY, l = 0.f;
     bool failed = false;
     int j = 0;
     long long ph[7] = {0, 0, 0, 0, 0, 0, 0};
-    long long wK = 0, wV = 0;  // thread 0's cycles waiting for K / V tiles to land
     long long tprev = clock64();
     const long long tloop = tprev;
     auto lap = [&](int k) {  // thread 0's time in phase k since the previous lap
@@ -287,30 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tprev = t1;
       }
     };
-    // S(jt) = Q K(jt)^T into S buffer jt % 2 (leader only)
-    auto issue_s = [&](int jt) -> bool {
-      const int sk = jt % kStages;
-      const long long tw = tr != nullptr ? clock64() : 0;
-      if (!mbar_wait(&fullK[sk], (jt / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout)) return false;
-      if (tr != nullptr) wK += clock64() - tw;
-      tc_fence_after();
-      const uint32_t kb = smem_u32(sK + sk * kTileBytes);
-      const uint32_t qb = smem_u32(sQ);
-      const uint32_t tS = tmem_base + 128u * static_cast<uint32_t>(jt & 1);
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint64_t ad = umma_desc_sw128(qb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
-        const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * kRegion) + 2 * (kk & 3);
-        umma_f16(tS, ad, bd, idS, kk > 0 ? 1u : 0u);
-      }
-      umma_commit(&s_done[jt & 1]);
-      umma_commit(&emptyK[sk]);
-      return true;
-    };
-    if (leader && n_kt > 0 && !issue_s(0)) failed = true;
     for (; j < n_kt; ++j) {
-      // ---- S(j+1) on the tensor cores while this tile's softmax runs
-      if (leader && !failed && j + 1 < n_kt && !issue_s(j + 1)) failed = true;
       lap(0);
       if (named_sync_or(failed)) {
         failed = true;
@@ -335,6 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int q = 0; q < 16; ++q) sv[c + q] = v16[q];
       }
+      tc_fence_before();  // S(j) is in registers: its TMEM buffer may take S(j + 2)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[j & 1]);
       const int kv0 = j * kKv + cb;
       float mx = -INFINITY;
       if (kv0 + 63 <= qpos && kv0 + 63 < ctx) {  // the whole half is visible: no masking
@@ -405,48 +460,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       named_sync_softmax();
       lap(5);
-      // ---- O += P V
-      if (leader) {
-        const int sv_ = j % kStages;
-        const long long tw = tr != nullptr ? clock64() : 0;
-        const bool vok = mbar_wait(&fullV[sv_], (j / kStages) & 1, abort_flag, a.status, kStatusAttnTimeout);
-        if (tr != nullptr) wV += clock64() - tw;
-        if (vok) {
-          tc_fence_after();
-          const uint32_t pb = smem_u32(sP);
-          const uint32_t vb = smem_u32(sV + sv_ * kTileBytes);
-#pragma unroll
-          for (int kk = 0; kk < kKv / 16; ++kk) {
-            const uint64_t ad = umma_desc_sw128(pb + (kk >> 2) * (kRows * 128)) + 2 * (kk & 3);
-            const uint64_t bd = umma_desc_sw128_mn(vb + kk * 16 * 128, kRegion, 1024);
-            umma_f16(tO, ad, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(o_done);
-          umma_commit(&emptyV[sv_]);
-        } else {
-          failed = true;
-        }
-      }
+      // ---- the MMA warp may run O += P V
+      if (threadIdx.x == 0) mbar_arrive(p_ready);
       lap(6);
     }
     if (tr != nullptr && threadIdx.x == 0) {
       tr[2] = static_cast<unsigned long long>(clock64() - tloop);
       for (int k = 0; k < 7; ++k) tr[3 + k] = static_cast<unsigned long long>(ph[k]);
       tr[10] = static_cast<unsigned long long>(n_kt);
-      tr[11] = static_cast<unsigned long long>(wK);
-      tr[12] = static_cast<unsigned long long>(wV);
     }
     if (!failed && n_kt > 0) {
       if (!mbar_wait(o_done, (n_kt - 1) & 1, abort_flag, a.status, kStatusAttnTimeout)) failed = true;
     }
     red_l[threadIdx.x] = l;
     if (named_sync_or(failed)) failed = true;
-    if (failed) {
-      if (leader) {  // let the tensor pipe finish what was issued before TMEM is freed
-        umma_commit(drain);
-        mbar_drain(drain, 0);
-      }
-    } else if (n_kt > 0) {
+    if (!failed && n_kt > 0) {
       tc_fence_after();
       const float lt = l + red_l[threadIdx.x ^ 128];
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
