@@ -26,6 +26,9 @@ from __future__ import annotations
 import argparse
 import json
 import os
+
+# the fused collectives use plain peer loads / stores only: no NVLink multicast object
+os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
 import statistics
 import sys
 import threading
@@ -35,12 +38,32 @@ BASELINE_TOKS = None  # the reference publishes no GPU number for this config
 
 
 def reference_arm(args):
-    reason = ("reference is a Rust workspace (Cargo, candle 0.10, cudarc 0.19); no cargo/rustc and no offline crate "
-              "registry in this image, and pip cannot install it (not a Python project)")
-    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    if os.path.isdir(ref) and any(f.startswith("bloom") for f in os.listdir(ref)):
-        reason = "baseline/_ref holds no runnable reference engine: " + reason
+    """The reference is a Rust Cargo workspace (candle + cudarc).  This arm
+    looks for what building it would need -- a Rust toolchain, a vendored
+    crate registry, or an installed reference under baseline/_ref -- and
+    reports what it found; with none of them it prints the `unavailable`
+    line and exits 0."""
+    import glob
+    import shutil
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    found = {tool: shutil.which(tool) for tool in ("cargo", "rustc")}
+    registry = [p for p in (os.path.expanduser("~/.cargo/registry"), os.path.join(here, "baseline", "_ref", "vendor"))
+                if os.path.isdir(p)]
+    ref = os.path.join(here, "baseline", "_ref")
+    ref_files = sorted(os.path.basename(p) for p in glob.glob(os.path.join(ref, "*")))[:8]
+    engine_bins = [p for p in glob.glob(os.path.join(ref, "**", "bloom_infer*"), recursive=True) if os.access(p, os.X_OK)]
+    probe = (f"cargo={found['cargo'] or 'absent'}, rustc={found['rustc'] or 'absent'}, "
+             f"crate registry={'present' if registry else 'absent'}, "
+             f"baseline/_ref={'[' + ', '.join(ref_files) + ']' if ref_files else 'empty or absent'}, "
+             f"bloom_infer binary={'present' if engine_bins else 'absent'}")
     rank = int(os.environ.get("RANK", "0"))
+    if engine_bins or (found["cargo"] and registry):
+        reason = ("a Rust toolchain or reference binary was found, but this arm has no driver for the reference's "
+                  "engine on this metric (it has no tensor-parallel CUDA path to run): " + probe)
+    else:
+        reason = ("reference is a Rust workspace (Cargo, candle 0.10, cudarc 0.19) and cannot be built here; "
+                  "pip install of it fails (not a Python project); probe: " + probe)
     if rank == 0:
         print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
     return 0
@@ -132,6 +155,9 @@ def main():
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--comm", default=os.environ.get("BLOOM_COMM", "fused"), choices=["nccl", "fused"])
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--profile", default="",
+                    help="after the timed runs, profile one more (untimed) run with torch.profiler and write the "
+                         "per-kernel device-time table of every rank to PROFILE.rank<r>.json")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -265,6 +291,13 @@ def main():
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if args.profile:
+        from bloom_b200.utils.step_profile import profile_call
+
+        table = profile_call(one_run, dev)
+        table.update({"rank": rank, "n_gpus": world, "config": line["config"]})
+        with open(f"{args.profile}.rank{rank}.json", "w") as f:
+            json.dump(table, f, indent=1)
     eng.shutdown()
     if world > 1:
         dist.barrier()

@@ -55,7 +55,16 @@ class SamplingParams:
 
 GREEDY = SamplingParams(temperature=0.0, top_p=1.0)
 
-FINISH_REASONS = {0: None, 1: "stop", 2: "length", 3: "abort"}
+FINISH_REASONS = {0: None, 1: "stop", 2: "length", 3: "abort", 4: "error"}
+
+# Status-word bits (csrc/include/bloom/common.cuh StatusBits).
+STATUS_NAMES = {1: "GEMM pipeline wait timed out", 2: "attention wait timed out", 4: "cross-GPU wait timed out",
+                8: "bad kernel argument", 16: "MoE buffer overflow", 32: "communicator poisoned"}
+
+
+def describe_status(bits: int) -> str:
+    names = [n for b, n in STATUS_NAMES.items() if bits & b]
+    return f"kernel status 0x{bits:x} ({', '.join(names) or 'unknown'})"
 
 
 @dataclass
@@ -69,6 +78,7 @@ class RequestOutput:
     first_token_time: Optional[float] = None
     finish_time: Optional[float] = None
     num_cached_tokens: int = 0
+    error: Optional[str] = None  # set when finish_reason == "error"
 
 
 @dataclass
@@ -167,6 +177,7 @@ class LLMEngine:
         self.tokenizer = None  # set by the pipeline; needed for JSON-mode constraints
         self._seed_counter = ec.seed
         self.step_times: List[float] = []
+        self.failures: List[dict] = []  # steps failed by a kernel status error
         self.speculator = None
 
     def attach_speculator(self, spec) -> None:
@@ -234,6 +245,8 @@ class LLMEngine:
         if meta.num_tokens == 0:
             return []
         sampled = self.runner.execute(meta)
+        if self.runner.last_status:
+            return self._fail_step(self.runner.last_status)
         if self.constraints:
             self._apply_constraints(sampled, meta)
         events = self.scheduler.update(sampled, meta.num_real_logits)
@@ -259,6 +272,41 @@ class LLMEngine:
                 r.finish_time = now
             out.append(r)
         self.step_times.append(now - t0)
+        return out
+
+    def _fail_step(self, bits: int) -> List[RequestOutput]:
+        """A kernel of the step reported an error (the status word, combined over
+        all tensor-parallel ranks, so every rank takes this path in the same
+        step): no token of the step is emitted; every request the step
+        scheduled finishes with finish_reason "error" and releases its KV
+        blocks; requests outside the step continue.  A cross-GPU timeout also
+        drops the fused communicator (later steps run on NCCL) and re-captures
+        the CUDA graphs.  Reference: fail_scheduled_requests
+        (crates/engine/src/scheduler/mod.rs:1862-1907)."""
+        from .. import ops
+
+        msg = describe_status(bits)
+        ops.status(self.model.device.index).zero_()
+        now = time.perf_counter()
+        out = []
+        for rid in self.scheduler.fail_scheduled():
+            self.constraints.pop(rid, None)
+            if self.speculator is not None:
+                self.speculator.forget(rid)
+            r = self.requests.get(rid)
+            if r is None:
+                continue
+            r.finished = True
+            r.finish_reason = "error"
+            r.error = msg
+            r.finish_time = now
+            out.append(r)
+        self.failures.append({"time": now, "status": bits, "message": msg, "requests": [r.request_id for r in out]})
+        comm = self.model.tp.comm
+        if comm is not None and bits & comm.COMM_BITS and comm.poison():
+            self.runner.release_graphs()
+            if self.econf.use_cuda_graphs:
+                self.runner.capture_graphs()
         return out
 
     def _apply_constraints(self, sampled, meta) -> None:

@@ -3,7 +3,10 @@
 The C++ scheduler writes the step's metadata into a pinned arena; the runner
 copies the used part to the device in one transfer, runs the forward (a CUDA
 graph replay for decode-only steps padded to a batch bucket, eager kernels
-otherwise), samples on the GPU and reads back one int32 per sampling row.
+otherwise), samples on the GPU and reads back one int32 per sampling row
+plus the kernels' status word (the OR over all tensor-parallel ranks), in
+one device-to-host copy.  A nonzero status means the step's outputs cannot be
+trusted: the engine fails the step's requests instead of emitting tokens.
 
 Tensor parallel ranks run identical schedulers on identical inputs; sampled
 tokens are made identical across ranks (greedy: distributed argmax over the
@@ -63,7 +66,8 @@ class ModelRunner:
         self.arena_words = worst.used_words
         self.arena_host = torch.zeros(self.arena_words, dtype=torch.int32).pin_memory()
         self.arena_dev = torch.zeros(self.arena_words, dtype=torch.int32, device=self.device)
-        self.sampled_host = torch.zeros(self.max_tokens + max_num_seqs, dtype=torch.int32).pin_memory()
+        self.sampled_host = torch.zeros(self.max_tokens + max_num_seqs + 1, dtype=torch.int32).pin_memory()
+        self.last_status = 0
         self.buckets = [b for b in (graph_buckets or DEFAULT_BUCKETS) if b <= max_num_seqs]
         if max_num_seqs not in self.buckets:
             self.buckets.append(max_num_seqs)
@@ -158,11 +162,17 @@ class ModelRunner:
 
     # ------------------------------------------------------------ sampling
     def _sample(self, logits: torch.Tensor, m, greedy: bool) -> torch.Tensor:
+        """int32 [NL + 1]: sampled tokens, then the (rank-combined) status word."""
         tp = self.model.tp
         if tp.size == 1:
+            NL = logits.shape[0]
+            out = torch.empty(NL + 1, dtype=torch.int32, device=logits.device)
             if greedy:
-                return ops.argmax(logits)
-            return ops.sample(logits, *self.sampling_views(m))
+                ops.argmax(logits, out=out[:NL])
+            else:
+                ops.sample(logits, *self.sampling_views(m), out=out[:NL])
+            out[NL:].copy_(ops.status(self.device.index)[:1])
+            return out
         return tp.comm.sample_vocab_parallel(logits, greedy, self.sampling_views(m) if not greedy else None,
                                              self.model.vocab_local)
 
@@ -235,10 +245,11 @@ class ModelRunner:
         self.last_logits = logits
         toks = self._sample(logits, m, m.all_greedy)
         NL = m.num_logits
-        self.sampled_host[:NL].copy_(toks[:NL], non_blocking=True)
+        self.sampled_host[:NL + 1].copy_(toks[:NL + 1], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        self.last_status = int(self.sampled_host[NL])
         self.stats["steps"] += 1
         self.stats["tokens"] += m.num_tokens
         self.stats["h2d_bytes"] += 4 * used
-        self.stats["d2h_bytes"] += 4 * NL
+        self.stats["d2h_bytes"] += 4 * (NL + 1)
         return self.sampled_host

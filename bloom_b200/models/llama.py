@@ -309,6 +309,72 @@ class DecoderLM:
             del lay
         self._finish()
 
+    def random_init_flat(self, seed: int = 0, std: float = 0.02) -> None:
+        """N(0, std) weights (norms = 1) in this shard's final layout, drawn by
+        ONE normal fill over a flat buffer that every projection is a view of
+        (128-element aligned, so every view is a 16-byte aligned TMA operand).
+        Three device launches in all, instead of several per tensor; the
+        values differ from `random_init` and from one TP size to another.
+        Dense decoders only."""
+        if self.cfg.is_moe:
+            raise NotImplementedError("random_init_flat covers dense decoders; use random_init for MoE")
+        cfg, dev, bf = self.cfg, self.device, torch.bfloat16
+        H, hd = cfg.hidden_size, cfg.head_dim
+        qkv_rows = (self.nq + 2 * self.nkv) * hd
+        shapes = [("embed", (cfg.vocab_size, H))]
+        if not cfg.tie_word_embeddings:
+            shapes.append(("lm_head", (self.vocab_local, H)))
+        per_layer = [("qkv", (qkv_rows, H)), ("o", (H, self.nq * hd)), ("gate_up", (2 * self.inter, H)),
+                     ("down", (H, self.inter))]
+        if cfg.qkv_bias:
+            per_layer.append(("qkv_b", (qkv_rows,)))
+        for i in range(cfg.num_layers):
+            shapes += [(f"{i}.{n}", sh) for n, sh in per_layer]
+
+        def numel(sh):
+            n = 1
+            for d in sh:
+                n *= d
+            return n
+
+        align = 128
+        total = sum((numel(sh) + align - 1) // align * align for _, sh in shapes)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        flat = torch.empty(total, dtype=bf, device=dev).normal_(0.0, std, generator=g)
+        views: Dict[str, torch.Tensor] = {}
+        off = 0
+        for name, sh in shapes:
+            n = numel(sh)
+            views[name] = flat[off:off + n].view(sh)
+            off += (n + align - 1) // align * align
+        nnorm = (2 * cfg.num_layers + 1) * H + (2 * cfg.num_layers * hd if cfg.qk_norm else 0)
+        ones = torch.ones(nnorm, dtype=bf, device=dev)
+        self._flat = (flat, ones)
+        self.embed = views["embed"]
+        self.lm_head = views["lm_head"] if "lm_head" in views else views["embed"][
+            self.tp.rank * self.vocab_local:(self.tp.rank + 1) * self.vocab_local]
+        o = 0
+
+        def norm_w(n):
+            nonlocal o
+            t = ones[o:o + n]
+            o += n
+            return t
+
+        self.final_norm = norm_w(H)
+        self.layers = []
+        for i in range(cfg.num_layers):
+            lay = {"ln1": norm_w(H), "ln2": norm_w(H), "qkv": views[f"{i}.qkv"], "o": views[f"{i}.o"],
+                   "gate_up": views[f"{i}.gate_up"], "down": views[f"{i}.down"]}
+            if cfg.qkv_bias:
+                lay["qkv_b"] = views[f"{i}.qkv_b"]
+            if cfg.qk_norm:
+                lay["q_norm"] = norm_w(hd)
+                lay["k_norm"] = norm_w(hd)
+            self.layers.append(lay)
+        self._finish()
+
     def _install_layer(self, i: int, lay: Dict[str, torch.Tensor]) -> None:
         cfg, hd, bf = self.cfg, self.cfg.head_dim, torch.bfloat16
         r = self.tp.rank

@@ -13,21 +13,30 @@ kernel sums the local slots, adds the residual, applies RMSNorm and
 all-gathers the result into `x(T)` on every rank, which is the next GEMM's
 input.  Other producers (MoE) write `partial(T)` locally and the same kernel
 pulls the peers' rows instead.
+
+No kernel here uses an NVLink multicast object, so none is created: torch's
+symmetric memory would otherwise bind every rendezvoused buffer to one, and a
+rank that dies while bound to it can raise NVLink faults on its peers' GPUs.
+`TORCH_SYMM_MEM_DISABLE_MULTICAST=1` is set before the first allocation and
+every handle is checked to carry no multicast pointer.
 """
 from __future__ import annotations
 
+import os
 from typing import List, Optional
 
-import torch
-import torch.distributed as dist
+os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
 
-from .. import ops
-from .._ext import cuda as _C
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from .. import ops  # noqa: E402
+from .._ext import cuda as _C  # noqa: E402
 
 
 class FusedComm:
     def __init__(self, rank: int, world: int, device: torch.device, group=None, max_tokens: int = 8192,
-                 hidden: int = 4096, timeout_s: float = 5.0, extra_rows: int = 0):
+                 hidden: int = 4096, timeout_s: float = 5.0, extra_rows: int = 0, max_logit_rows: int = 0):
         import torch.distributed._symmetric_memory as symm
 
         self.rank, self.world, self.device = rank, world, device
@@ -42,11 +51,25 @@ class FusedComm:
         fw = int(_C().tp_flag_words())
         self._F = symm.empty(fw, dtype=torch.int32, device=device)
         self._F.zero_()
+        # greedy logits: (value, global index) pairs [world][rows + 1] (last entry: a rank's status word)
+        self.max_logit_rows = int(max_logit_rows or max_tokens)
+        ns = world * (self.max_logit_rows + 1) * 2
+        self._G = symm.empty(ns, dtype=torch.int32, device=device)
+        self._G.zero_()
         torch.cuda.synchronize(device)
         hP = symm.rendezvous(self._P, self.group)
         hX = symm.rendezvous(self._X, self.group)
         hF = symm.rendezvous(self._F, self.group)
-        self._handles = (hP, hX, hF)
+        hG = symm.rendezvous(self._G, self.group)
+        self._handles = (hP, hX, hF, hG)
+        self.g_ptrs = [hG.get_buffer(r, (ns,), torch.int32, 0).data_ptr() for r in range(world)]
+        self._full = None  # lazily: full-vocabulary logits rows for stochastic sampling
+        self.poisoned = False
+        for h in self._handles:
+            mc = getattr(h, "multicast_ptr", 0)
+            if mc:
+                raise RuntimeError("symmetric-memory buffer is bound to an NVLink multicast object although "
+                                   "TORCH_SYMM_MEM_DISABLE_MULTICAST=1; refusing to run the fused collectives")
         self.p_ptrs = [hP.get_buffer(r, (n + world * hidden,), torch.bfloat16, 0).data_ptr() for r in range(world)]
         self.x_ptrs = [hX.get_buffer(r, (n,), torch.bfloat16, 0).data_ptr() for r in range(world)]
         self.f_ptrs = [hF.get_buffer(r, (fw,), torch.int32, 0).data_ptr() for r in range(world)]
@@ -78,3 +101,43 @@ class FusedComm:
 
     def barrier(self) -> None:
         _C().tp_barrier(self.f_ptrs, self.rank, self.timeout_s, ops.status(self.device.index))
+
+    # ------------------------------------------------------------ last-layer logits
+    def argmax_gather(self, logits: torch.Tensor, vocab_offset: int, out: torch.Tensor) -> torch.Tensor:
+        """Greedy tokens of vocabulary-parallel logits in one kernel: local
+        argmax, (value, index) pairs stored into every rank over NVLink,
+        bounded flag exchange, reduction.  out: int32 [NL + 1]; out[NL] is the
+        OR of every rank's status word (all ranks read the same value)."""
+        _C().tp_argmax_gather(logits, int(vocab_offset), self.g_ptrs, self.max_logit_rows, self.f_ptrs, self.rank,
+                              out, self.timeout_s, ops.status(self.device.index))
+        ops._count()
+        return out
+
+    def gather_cols(self, logits: torch.Tensor, out_status: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary rows [NL, world * Vl] on every rank from the
+        [NL, Vl] shards (16-byte P2P stores); out_status[0] receives the OR of
+        every rank's status word.  The first call allocates the buffers on all
+        ranks at once (the ranks run identical schedules)."""
+        import torch.distributed._symmetric_memory as symm
+
+        NL, Vl = logits.shape
+        V = Vl * self.world
+        if self._full is None or self._full[1] < NL or self._full[2] != V:
+            rows = max(NL, self.max_logit_rows)
+            L = symm.empty(rows * V, dtype=torch.bfloat16, device=self.device)
+            S = symm.empty(self.world, dtype=torch.int32, device=self.device)
+            S.zero_()
+            torch.cuda.synchronize(self.device)
+            hL = symm.rendezvous(L, self.group)
+            hS = symm.rendezvous(S, self.group)
+            for h in (hL, hS):
+                if getattr(h, "multicast_ptr", 0):
+                    raise RuntimeError("symmetric-memory buffer is bound to an NVLink multicast object")
+            lp = [hL.get_buffer(r, (rows * V,), torch.bfloat16, 0).data_ptr() for r in range(self.world)]
+            sp = [hS.get_buffer(r, (self.world,), torch.int32, 0).data_ptr() for r in range(self.world)]
+            self._full = (L, rows, V, lp, sp, (hL, hS))
+        L, rows, V, lp, sp, _ = self._full
+        _C().tp_gather_cols(logits.contiguous(), lp, V, sp, self.f_ptrs, self.rank, out_status, self.timeout_s,
+                            ops.status(self.device.index))
+        ops._count()
+        return L[:NL * V].view(NL, V)

@@ -72,7 +72,10 @@ class TPControl:
 
 
 def follower_loop(engine, ctrl: TPControl) -> None:
-    """Ranks > 0: apply rank 0's admissions / aborts and step in lockstep."""
+    """Ranks > 0: apply rank 0's admissions / aborts and step in lockstep.
+    If rank 0 is gone, the exchange raises (connection closed, or the process
+    group's timeout) and so does this loop: the rank exits with an error
+    instead of waiting for a leader that never speaks again."""
     while True:
         msg = ctrl.exchange(None)
         if msg.get("stop"):
@@ -102,6 +105,7 @@ class ServingRuntime:
         self._stop = threading.Event()
         self._wake = threading.Event()
         self.ready = True
+        self.broken: Optional[str] = None  # set when a tensor-parallel peer was lost
         self.ctrl = ctrl
         self.engine = getattr(pipeline, "llm", None)
         self._thread = threading.Thread(target=self._loop, name="bloom-engine", daemon=True)
@@ -127,6 +131,9 @@ class ServingRuntime:
         loop = asyncio.get_running_loop()
         sub = Submission(request_id or f"req-{next(_ids)}", list(prompt_ids), params, loop, asyncio.Queue(),
                          messages=messages)
+        if self.broken is not None:
+            sub.queue.put_nowait(StreamItem(finished=True, reason="error", error=self.broken))
+            return sub
         with self._lock:
             self._by_id[sub.id] = sub
         self._pending.put(sub)
@@ -147,7 +154,7 @@ class ServingRuntime:
         self._stop.set()
         self._wake.set()
         self._thread.join(timeout=10)
-        if self.ctrl is not None and self.engine is not None:
+        if self.ctrl is not None and self.engine is not None and self.broken is None:
             self.ctrl.exchange({"stop": True})
 
     # ------------------------------------------------------------ engine thread
@@ -201,7 +208,11 @@ class ServingRuntime:
                     self._by_rid[rid] = sub
             msg["step"] = eng.has_unfinished()
             if ctrl is not None and (msg["add"] or msg["abort"] or msg["step"] or time.time() - last_beat > 1.0):
-                ctrl.exchange(msg)  # the other ranks repeat these calls before the same step
+                try:
+                    ctrl.exchange(msg)  # the other ranks repeat these calls before the same step
+                except Exception as e:  # a peer rank is gone (closed connection or process-group timeout)
+                    self._peer_lost(f"tensor-parallel peer lost: {e}")
+                    return
                 last_beat = time.time()
             if not msg["step"]:
                 self._wake.wait(timeout=0.05)
@@ -236,9 +247,33 @@ class ServingRuntime:
                     self._emit(sub, StreamItem(token=tok, finished=r.finished and last,
                                                reason=r.finish_reason if last else None))
                 sub.n_tokens += len(new)
+                if r.finished and not new:  # failed step (kernel status error): no token, an error item
+                    self._emit(sub, StreamItem(finished=True, reason=r.finish_reason,
+                                               error=getattr(r, "error", None)))
                 if r.finished:
                     eng.requests.pop(r.request_id, None)
                     self._finish(sub)
+
+    def _peer_lost(self, reason: str) -> None:
+        """No collective can complete any more: every in-flight and queued
+        request ends with an error, readiness goes false and new submissions
+        are refused with the same reason.  The engine is not stepped again."""
+        self.broken = reason
+        self.ready = False
+        with self._lock:
+            subs = list(self._by_id.values())
+        while True:
+            try:
+                subs.append(self._pending.get_nowait())
+            except queue.Empty:
+                break
+        seen = set()
+        for sub in subs:
+            if sub.id in seen:
+                continue
+            seen.add(sub.id)
+            self._emit(sub, StreamItem(finished=True, reason="error", error=reason))
+            self._finish(sub)
 
     def _loop_blocking(self) -> None:
         """CPU / echo pipelines: one request at a time, text deltas."""

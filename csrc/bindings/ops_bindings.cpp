@@ -61,4 +61,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("timeout_s"), py::arg("status"), py::arg("pushed") = false);
   m.def("tp_allgather_rows", &bloom::tp_allgather_rows);
   m.def("tp_barrier", &bloom::tp_barrier);
+  m.def("tp_argmax_gather", &bloom::tp_argmax_gather);
+  m.def("tp_gather_cols", &bloom::tp_gather_cols);
 }

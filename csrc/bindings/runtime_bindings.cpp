@@ -194,6 +194,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              return q == nullptr ? 0 : q->num_cached_prefix;
            })
       .def("sampling_ids", &Scheduler::sampling_ids)
+      .def("fail_scheduled", &Scheduler::fail_scheduled)
       .def(
           "enable_cachemesh",
           [](Scheduler& s, const torch::Tensor& l2, int64_t block_bytes, const std::string& l3_dir,

@@ -24,6 +24,9 @@ enum StatusBits : int {
   kStatusCommTimeout = 1 << 2,
   kStatusBadArgument = 1 << 3,
   kStatusMoeOverflow = 1 << 4,
+  // a fused collective found its communicator poisoned by an earlier timeout
+  // and did nothing (the host must fail the step and stop using it)
+  kStatusCommPoisoned = 1 << 5,
 };
 
 // Local (same-GPU) pipeline waits never legitimately take this long.

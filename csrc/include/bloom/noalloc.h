@@ -42,7 +42,9 @@ int bloom_paged_decode_attention_noalloc(const void* q, void* out, const void* k
                                          int block_table_stride, const int* seq_lens, int batch, int q_len,
                                          int splits, float scale, void* stream);
 
-/* Reads and clears the status word of the current device (synchronous). */
+/* Reads and clears the status word of the current device.  Synchronous: it
+ * waits for all work on the device first (every stream), so the bits of a
+ * call queued on a non-blocking stream are included.  Not during capture. */
 int bloom_noalloc_status(int* bits);
 
 #ifdef __cplusplus

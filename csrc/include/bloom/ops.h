@@ -132,6 +132,12 @@ void tp_allgather_rows(const torch::Tensor& src, const std::vector<int64_t>& dst
                        const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t T, double timeout_s,
                        const torch::Tensor& status);
 void tp_barrier(const std::vector<int64_t>& flag_ptrs, int64_t rank, double timeout_s, const torch::Tensor& status);
+void tp_argmax_gather(const torch::Tensor& logits, int64_t vocab_offset, const std::vector<int64_t>& slot_ptrs,
+                      int64_t max_rows, const std::vector<int64_t>& flag_ptrs, int64_t rank, torch::Tensor& out,
+                      double timeout_s, const torch::Tensor& status);
+void tp_gather_cols(const torch::Tensor& logits, const std::vector<int64_t>& dst_ptrs, int64_t dst_cols,
+                    const std::vector<int64_t>& stat_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t rank,
+                    torch::Tensor& out_status, double timeout_s, const torch::Tensor& status);
 
 // Encoder (BERT) kernels.
 void bert_embed_ln(const torch::Tensor& ids, const torch::Tensor& pos, const c10::optional<torch::Tensor>& types,

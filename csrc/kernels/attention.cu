@@ -852,12 +852,17 @@ extern "C" __attribute__((visibility("default"))) int bloom_paged_decode_attenti
 }
 
 // Reads and clears the allocation-free entry point's status word on the
-// current device (bit 2: an attention wait gave up).  Synchronous.
+// current device (bit 2: an attention wait gave up).  Synchronous: it first
+// waits for all work on the device (cudaDeviceSynchronize), so a call queued
+// on any stream -- a non-blocking stream or a per-thread default stream
+// included -- has finished and set its bits before the word is read.  Do not
+// call it while a stream of this device is being captured.
 extern "C" __attribute__((visibility("default"))) int bloom_noalloc_status(int* bits) {
   using namespace bloom;
   int dev = 0;
   if (bits == nullptr || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BLOOM_NOALLOC_BAD_ARGUMENT;
   if (noalloc::setup_device(dev) != 0) return BLOOM_NOALLOC_CUDA_ERROR;
+  if (cudaDeviceSynchronize() != cudaSuccess) return BLOOM_NOALLOC_CUDA_ERROR;
   if (cudaMemcpy(bits, noalloc::g_dev[dev].status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return BLOOM_NOALLOC_CUDA_ERROR;
   if (cudaMemset(noalloc::g_dev[dev].status, 0, sizeof(int)) != cudaSuccess) return BLOOM_NOALLOC_CUDA_ERROR;

@@ -21,6 +21,14 @@
 // kStatusCommTimeout in the caller's status word and the kernel returns, so a
 // dead peer can never hang this GPU.
 //
+// Poisoning: a timed-out wait also sets the local poison word.  From then on
+// every collective launch on this rank does nothing but set
+// kStatusCommPoisoned, and the epoch no longer advances, so a late peer can
+// never pair its epoch with a stale one here and read overwritten partials:
+// it times out on this rank's missing "done" flag and poisons itself too.
+// The host reads the status word after each step, fails the step's requests
+// and stops using the communicator (falls back to NCCL or rebuilds it).
+//
 // Replaces the reference's no-op CollectiveOps / TensorCollectiveOps
 // (crates/engine/src/core/parallelism.rs:105-178).
 #include <ATen/cuda/CUDAContext.h>
@@ -44,7 +52,8 @@ struct Peers {
 //   [8, 16)   done[src]    written by peer src: its all-gather stores into this rank are complete
 //   [16]      epoch        local: number of completed fused collectives
 //   [17]      cta counter  local: CTAs of the current launch that finished
-constexpr int kReady = 0, kDone = 8, kEpoch = 16, kCtaCount = 17;
+//   [18]      poison       local: nonzero once a wait of this rank timed out
+constexpr int kReady = 0, kDone = 8, kEpoch = 16, kCtaCount = 17, kPoison = 18;
 constexpr int kFlagWords = 32;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -55,6 +64,22 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+
+__device__ __forceinline__ bool poisoned(const uint32_t* my_flags) {
+  return *reinterpret_cast<const volatile uint32_t*>(my_flags + kPoison) != 0u;
+}
+__device__ __forceinline__ void poison(uint32_t* my_flags, int* status) {
+  *reinterpret_cast<volatile uint32_t*>(my_flags + kPoison) = 1u;
+  __threadfence();
+  atomicOr(status, kStatusCommTimeout);
+}
+
+// Launch-end bookkeeping shared by the collectives: the last CTA to finish
+// signals "done" to every peer, waits (bounded) for theirs and advances the
+// epoch -- unless the communicator is poisoned, in which case it only resets
+// the CTA counter.
+__device__ void finish_collective(uint32_t* my_flags, const uint64_t (&peer_flags)[8], int rank, int world,
+                                  uint32_t target, uint64_t timeout_ns, int* status, int* last_s);
 
 // Bounded wait until flags[base + r] >= target for every rank r.
 __device__ bool wait_flags(const uint32_t* flags, int base, int world, uint32_t target, uint64_t timeout_ns) {
@@ -126,9 +151,11 @@ __global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.flags.p[a.rank]);
   if (threadIdx.x == 0) {
     epoch_s = my_flags[kEpoch];
-    ok_s = 1;
+    ok_s = poisoned(my_flags) ? 0 : 1;
+    if (!ok_s) atomicOr(a.status, kStatusCommPoisoned);
   }
   __syncthreads();
+  if (!ok_s) return;  // poisoned communicator: touch nothing
   const uint32_t target = epoch_s + 1;
   // A. every CTA announces readiness (idempotent) so no CTA depends on another being scheduled
   if (threadIdx.x < a.world)
@@ -136,7 +163,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs
   if (threadIdx.x == 0) {
     if (!wait_flags(my_flags, kReady, a.world, target, a.timeout_ns)) {
       ok_s = 0;
-      atomicOr(a.status, kStatusCommTimeout);
+      poison(my_flags, a.status);
     }
   }
   __syncthreads();
@@ -193,20 +220,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs
   }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(reinterpret_cast<int*>(my_flags + kCtaCount), 1);
-    last_s = (prev == (int)gridDim.x - 1);
-  }
-  __syncthreads();
-  if (last_s && threadIdx.x == 0) {
-    my_flags[kCtaCount] = 0;
-    __threadfence_system();
-    for (int r = 0; r < a.world; ++r)
-      st_release_sys(reinterpret_cast<uint32_t*>(a.flags.p[r]) + kDone + a.rank, target);
-    if (!wait_flags(my_flags, kDone, a.world, target, a.timeout_ns)) atomicOr(a.status, kStatusCommTimeout);
-    my_flags[kEpoch] = target;  // stream order makes the next launch see it
-    __threadfence();
-  }
+  if (threadIdx.x == 0) finish_collective(my_flags, a.flags.p, a.rank, a.world, target, a.timeout_ns, a.status, &last_s);
 }
 
 // All-gather of row slices: rank r owns rows [r*rows_per_rank, ...) of src (local,
@@ -221,11 +235,16 @@ struct AGArgs {
 };
 
 __global__ void tp_allgather_rows_kernel(const AGArgs a) {
-  __shared__ int last_s;
+  __shared__ int last_s, ok_s;
   __shared__ uint32_t epoch_s;
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.flags.p[a.rank]);
-  if (threadIdx.x == 0) epoch_s = my_flags[kEpoch];
+  if (threadIdx.x == 0) {
+    epoch_s = my_flags[kEpoch];
+    ok_s = poisoned(my_flags) ? 0 : 1;
+    if (!ok_s) atomicOr(a.status, kStatusCommPoisoned);
+  }
   __syncthreads();
+  if (!ok_s) return;
   const uint32_t target = epoch_s + 1;
   const int r0 = a.rank * a.rows_per_rank;
   const int r1 = min(a.T, r0 + a.rows_per_rank);
@@ -239,30 +258,217 @@ __global__ void tp_allgather_rows_kernel(const AGArgs a) {
   }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(reinterpret_cast<int*>(my_flags + kCtaCount), 1);
-    last_s = (prev == (int)gridDim.x - 1);
-  }
-  __syncthreads();
-  if (last_s && threadIdx.x == 0) {
-    my_flags[kCtaCount] = 0;
-    __threadfence_system();
-    for (int r = 0; r < a.world; ++r)
-      st_release_sys(reinterpret_cast<uint32_t*>(a.flags.p[r]) + kDone + a.rank, target);
-    if (!wait_flags(my_flags, kDone, a.world, target, a.timeout_ns)) atomicOr(a.status, kStatusCommTimeout);
-    my_flags[kEpoch] = target;
-    __threadfence();
-  }
+  if (threadIdx.x == 0) finish_collective(my_flags, a.flags.p, a.rank, a.world, target, a.timeout_ns, a.status, &last_s);
 }
 
 // Stand-alone bounded barrier (used by tests of the timeout path and at start-up).
 __global__ void tp_barrier_kernel(Peers flags, int rank, int world, uint64_t timeout_ns, int* status) {
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(flags.p[rank]);
+  if (poisoned(my_flags)) {
+    atomicOr(status, kStatusCommPoisoned);
+    return;
+  }
   const uint32_t target = my_flags[kEpoch] + 1;
   __threadfence_system();
   for (int r = 0; r < world; ++r) st_release_sys(reinterpret_cast<uint32_t*>(flags.p[r]) + kDone + rank, target);
-  if (!wait_flags(my_flags, kDone, world, target, timeout_ns)) atomicOr(status, kStatusCommTimeout);
+  if (!wait_flags(my_flags, kDone, world, target, timeout_ns)) {
+    poison(my_flags, status);
+    return;
+  }
   my_flags[kEpoch] = target;
+}
+
+__device__ void finish_collective(uint32_t* my_flags, const uint64_t (&peer_flags)[8], int rank, int world,
+                                  uint32_t target, uint64_t timeout_ns, int* status, int* last_s) {
+  const int prev = atomicAdd(reinterpret_cast<int*>(my_flags + kCtaCount), 1);
+  *last_s = (prev == (int)gridDim.x - 1);
+  if (!*last_s) return;
+  my_flags[kCtaCount] = 0;
+  if (poisoned(my_flags)) return;  // a CTA of this launch timed out: no done signal, no epoch advance
+  __threadfence_system();
+  for (int r = 0; r < world; ++r) st_release_sys(reinterpret_cast<uint32_t*>(peer_flags[r]) + kDone + rank, target);
+  if (!wait_flags(my_flags, kDone, world, target, timeout_ns)) {
+    poison(my_flags, status);
+    return;
+  }
+  my_flags[kEpoch] = target;  // stream order makes the next launch see it
+  __threadfence();
+}
+
+// ---------------------------------------------------------------- last-layer logits
+// Status agreement: every rank's status word travels with its logits share, and
+// each rank writes the OR of all ranks' words next to the sampled tokens, so all
+// ranks see the same error bits after a step and fail the same requests.
+
+__device__ __forceinline__ void argmax_pair(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+struct ArgmaxGatherArgs {
+  Peers slots;  // per rank: uint2 [world][max_rows + 1]; entry [r][row] = (value bits, global index) from rank r,
+                // entry [r][max_rows] = rank r's status word
+  Peers flags;
+  const __nv_bfloat16* logits;  // local vocabulary shard [NL, ld]
+  long ld;
+  int Vl, vocab_offset;
+  int rank, world, NL, max_rows;
+  int* out;  // int32 [NL + 1]: greedy tokens, then the OR of every rank's status word
+  int* status;
+  uint64_t timeout_ns;
+};
+
+// One CTA per logits row: argmax over the local shard, the (value, index) pair
+// stored into every rank's slot array with 8-byte P2P stores; the last CTA to
+// finish exchanges "done" flags (bounded) and reduces the world pairs of every
+// row (largest value, lowest global index on ties: the single-GPU argmax rule).
+__global__ void __launch_bounds__(1024) tp_argmax_gather_kernel(const ArgmaxGatherArgs a) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ int ok_s, last_s;
+  __shared__ uint32_t epoch_s;
+  uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.flags.p[a.rank]);
+  if (threadIdx.x == 0) {
+    epoch_s = my_flags[kEpoch];
+    ok_s = poisoned(my_flags) ? 0 : 1;
+    if (!ok_s) {
+      atomicOr(a.status, kStatusCommPoisoned);
+      if (blockIdx.x == 0) a.out[a.NL] = atomicOr(a.status, 0);
+    }
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const uint32_t target = epoch_s + 1;
+  const int row = blockIdx.x;
+  const __nv_bfloat16* lr = a.logits + (long)row * a.ld;
+  float v = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int k = threadIdx.x; k < a.Vl; k += blockDim.x) argmax_pair(v, idx, __bfloat162float(lr[k]), k);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) argmax_pair(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = v;
+    si[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    v = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
+    idx = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+      argmax_pair(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+    // lanes 0..world-1 each store the pair into one rank's slots
+    if (threadIdx.x < a.world) {
+      const uint2 pr = make_uint2(__float_as_uint(v), static_cast<uint32_t>(idx + a.vocab_offset));
+      reinterpret_cast<uint2*>(a.slots.p[threadIdx.x])[(long)a.rank * (a.max_rows + 1) + row] = pr;
+      if (row == 0)
+        reinterpret_cast<uint2*>(a.slots.p[threadIdx.x])[(long)a.rank * (a.max_rows + 1) + a.max_rows] =
+            make_uint2(static_cast<uint32_t>(atomicOr(a.status, 0)), 0u);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(reinterpret_cast<int*>(my_flags + kCtaCount), 1);
+    last_s = (prev == (int)gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!last_s) return;
+  if (threadIdx.x == 0) {
+    my_flags[kCtaCount] = 0;
+    ok_s = 0;
+    if (!poisoned(my_flags)) {
+      __threadfence_system();
+      for (int r = 0; r < a.world; ++r)
+        st_release_sys(reinterpret_cast<uint32_t*>(a.flags.p[r]) + kDone + a.rank, target);
+      if (wait_flags(my_flags, kDone, a.world, target, a.timeout_ns)) {
+        ok_s = 1;
+        my_flags[kEpoch] = target;
+      } else {
+        poison(my_flags, a.status);
+      }
+    }
+  }
+  __syncthreads();
+  const uint2* mine = reinterpret_cast<const uint2*>(a.slots.p[a.rank]);
+  if (!ok_s) {
+    if (threadIdx.x == 0) a.out[a.NL] = atomicOr(a.status, 0);
+    return;
+  }
+  for (int r = threadIdx.x; r < a.NL; r += blockDim.x) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int q = 0; q < a.world; ++q) {
+      const volatile uint32_t* pr = reinterpret_cast<const volatile uint32_t*>(mine + (long)q * (a.max_rows + 1) + r);
+      argmax_pair(bv, bi, __uint_as_float(pr[0]), static_cast<int>(pr[1]));
+    }
+    a.out[r] = bi;
+  }
+  if (threadIdx.x == 0) {
+    int st = 0;
+    for (int q = 0; q < a.world; ++q)
+      st |= static_cast<int>(*reinterpret_cast<const volatile uint32_t*>(mine + (long)q * (a.max_rows + 1) + a.max_rows));
+    a.out[a.NL] = st | atomicOr(a.status, 0);
+  }
+}
+
+struct GatherColsArgs {
+  Peers dst;       // per rank: bf16 [max_rows, V] full-vocabulary logits
+  Peers stat;      // per rank: int32 [world] status words
+  Peers flags;
+  const uint4* src;  // local shard rows, 16-byte vectors
+  long src_ld16;     // source row stride in 16-byte vectors
+  int cols16;        // shard width in 16-byte vectors (Vl * 2 / 16)
+  long dst_ld16;     // destination row stride in 16-byte vectors (V * 2 / 16)
+  int rank, world, NL;
+  int* out_status;  // local int32: OR of every rank's status word
+  int* status;
+  uint64_t timeout_ns;
+};
+
+// Vocabulary-parallel logits -> full rows on every rank: each rank stores its
+// [NL, Vl] shard at columns [rank * Vl, (rank + 1) * Vl) of every rank's
+// buffer with 16-byte P2P stores; the stochastic sampler then runs locally on
+// identical rows with identical Philox streams, so the ranks agree.
+__global__ void __launch_bounds__(256) tp_gather_cols_kernel(const GatherColsArgs a) {
+  __shared__ int ok_s, last_s;
+  __shared__ uint32_t epoch_s;
+  uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.flags.p[a.rank]);
+  if (threadIdx.x == 0) {
+    epoch_s = my_flags[kEpoch];
+    ok_s = poisoned(my_flags) ? 0 : 1;
+    if (!ok_s) {
+      atomicOr(a.status, kStatusCommPoisoned);
+      if (blockIdx.x == 0) *a.out_status = atomicOr(a.status, 0);
+    }
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const uint32_t target = epoch_s + 1;
+  const long n = (long)a.NL * a.cols16;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < n; e += (long)gridDim.x * blockDim.x) {
+    const long r = e / a.cols16, c = e - r * a.cols16;
+    const uint4 v = a.src[r * a.src_ld16 + c];
+    const long off = r * a.dst_ld16 + (long)a.rank * a.cols16 + c;
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q)
+      if (q < a.world) reinterpret_cast<uint4*>(a.dst.p[q])[off] = v;
+  }
+  if (blockIdx.x == 0 && threadIdx.x < a.world)
+    reinterpret_cast<int*>(a.stat.p[threadIdx.x])[a.rank] = atomicOr(a.status, 0);
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) finish_collective(my_flags, a.flags.p, a.rank, a.world, target, a.timeout_ns, a.status, &last_s);
+  __syncthreads();
+  if (last_s && threadIdx.x == 0) {
+    int st = atomicOr(a.status, 0);
+    if (!poisoned(my_flags))
+      for (int q = 0; q < a.world; ++q) st |= reinterpret_cast<const volatile int*>(a.stat.p[a.rank])[q];
+    *a.out_status = st;
+  }
 }
 
 Peers to_peers(const std::vector<int64_t>& v) {
@@ -339,6 +545,68 @@ void tp_barrier(const std::vector<int64_t>& flag_ptrs, int64_t rank, double time
   comm::tp_barrier_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
       comm::to_peers(flag_ptrs), int(rank), int(flag_ptrs.size()), static_cast<uint64_t>(timeout_s * 1e9),
       status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void tp_argmax_gather(const torch::Tensor& logits, int64_t vocab_offset, const std::vector<int64_t>& slot_ptrs,
+                      int64_t max_rows, const std::vector<int64_t>& flag_ptrs, int64_t rank, torch::Tensor& out,
+                      double timeout_s, const torch::Tensor& status) {
+  const int world = static_cast<int>(slot_ptrs.size());
+  TORCH_CHECK(flag_ptrs.size() == slot_ptrs.size(), "rank count mismatch");
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1, "logits bf16 [NL, V]");
+  TORCH_CHECK(out.scalar_type() == at::kInt && out.numel() >= logits.size(0) + 1, "out int32 [NL + 1]");
+  const int NL = static_cast<int>(logits.size(0));
+  TORCH_CHECK(NL <= max_rows, "more logits rows than the slot array holds");
+  if (NL <= 0) return;
+  const at::cuda::CUDAGuard g(logits.device());
+  comm::ArgmaxGatherArgs a;
+  a.slots = comm::to_peers(slot_ptrs);
+  a.flags = comm::to_peers(flag_ptrs);
+  a.logits = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
+  a.ld = logits.stride(0);
+  a.Vl = static_cast<int>(logits.size(1));
+  a.vocab_offset = static_cast<int>(vocab_offset);
+  a.rank = int(rank);
+  a.world = world;
+  a.NL = NL;
+  a.max_rows = static_cast<int>(max_rows);
+  a.out = out.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
+  comm::tp_argmax_gather_kernel<<<NL, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void tp_gather_cols(const torch::Tensor& logits, const std::vector<int64_t>& dst_ptrs, int64_t dst_cols,
+                    const std::vector<int64_t>& stat_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t rank,
+                    torch::Tensor& out_status, double timeout_s, const torch::Tensor& status) {
+  const int world = static_cast<int>(dst_ptrs.size());
+  TORCH_CHECK(flag_ptrs.size() == dst_ptrs.size() && stat_ptrs.size() == dst_ptrs.size(), "rank count mismatch");
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1, "logits bf16 [NL, V]");
+  TORCH_CHECK((logits.size(1) * 2) % 16 == 0 && (logits.stride(0) * 2) % 16 == 0 && (dst_cols * 2) % 16 == 0,
+              "rows must be 16-byte multiples");
+  TORCH_CHECK(logits.size(1) * world == dst_cols, "shard width x ranks must equal the full row");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0, "logits must be 16-byte aligned");
+  const int NL = static_cast<int>(logits.size(0));
+  if (NL <= 0) return;
+  const at::cuda::CUDAGuard g(logits.device());
+  comm::GatherColsArgs a;
+  a.dst = comm::to_peers(dst_ptrs);
+  a.stat = comm::to_peers(stat_ptrs);
+  a.flags = comm::to_peers(flag_ptrs);
+  a.src = reinterpret_cast<const uint4*>(logits.data_ptr());
+  a.src_ld16 = logits.stride(0) * 2 / 16;
+  a.cols16 = static_cast<int>(logits.size(1) * 2 / 16);
+  a.dst_ld16 = dst_cols * 2 / 16;
+  a.rank = int(rank);
+  a.world = world;
+  a.NL = NL;
+  a.out_status = out_status.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
+  const long n = (long)NL * a.cols16;
+  const int blocks = int(std::min<long>(2 * 148, std::max<long>(1, (n + 255) / 256)));
+  comm::tp_gather_cols_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -473,6 +473,25 @@ std::vector<Event> Scheduler::update(const int32_t* sampled, int n) {
   return ev;
 }
 
+std::vector<int64_t> Scheduler::fail_scheduled() {
+  std::vector<int64_t> ids;
+  for (Sequence* s : last_scheduled_) {
+    if (s->status == SeqStatus::Finished) continue;
+    ids.push_back(s->id);
+    running_.erase(std::remove(running_.begin(), running_.end(), s), running_.end());
+    waiting_.erase(std::remove(waiting_.begin(), waiting_.end(), s), waiting_.end());
+    s->verifying = false;
+    s->draft.clear();
+    finish(s, FinishReason::Error);
+  }
+  last_sampling_.clear();
+  last_scheduled_.clear();
+  row_draft_.clear();
+  row_group_.clear();
+  for (int64_t id : ids) seqs_.erase(id);
+  return ids;
+}
+
 // ---------------------------------------------------------------- speculation
 std::vector<int64_t> Scheduler::decode_candidates() const {
   std::vector<int64_t> v;

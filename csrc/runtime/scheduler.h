@@ -41,7 +41,7 @@ struct SamplingParams {
 };
 
 enum class SeqStatus : int { Waiting = 0, Running = 1, Finished = 2 };
-enum class FinishReason : int { None = 0, Stop = 1, Length = 2, Aborted = 3 };
+enum class FinishReason : int { None = 0, Stop = 1, Length = 2, Aborted = 3, Error = 4 };
 
 struct Sequence {
   int64_t id = 0;
@@ -172,6 +172,13 @@ class Scheduler {
   // Block ids of a table visible to attention under the policy.
   std::vector<int32_t> visible_blocks(const std::vector<int32_t>& table) const;
   std::vector<Event> update(const int32_t* sampled, int n);
+  // The step scheduled last could not be trusted (a kernel reported an
+  // error): every sequence it scheduled finishes with FinishReason::Error and
+  // releases its KV blocks, and the step's sampling state is dropped.
+  // Returns the failed sequence ids.  Sequences that were not part of the
+  // step are untouched.  (Reference: fail_scheduled_requests,
+  // crates/engine/src/scheduler/mod.rs:1862-1907.)
+  std::vector<int64_t> fail_scheduled();
 
   // ---- speculative decoding
   // Running sequences whose next step is a decode (verify) row, in running order.

@@ -369,3 +369,31 @@ def test_compact_inactive_releases_cached_blocks(rt):
     assert s.maintain_long_context() == before["cached_blocks"]
     after = s.kv_metrics()
     assert after["free_blocks"] == 8 and after["active_blocks"] == 0
+
+
+def test_fail_scheduled_frees_kv_and_spares_others(rt):
+    """A step whose kernels reported an error: every sequence it scheduled
+    finishes with an error and releases its blocks; a waiting request that the
+    step did not include is untouched and runs afterwards (reference:
+    fail_scheduled_requests, scheduler/mod.rs:1862-1907)."""
+    s, arena, _ = make(rt, num_blocks=16, max_seqs=2, budget=64)
+    free0 = s.kv_metrics()["free_blocks"]
+    a = s.add_request(list(range(3, 40)), params(rt, max_tokens=4))
+    b = s.add_request(list(range(5, 30)), params(rt, max_tokens=4))
+    c = s.add_request(list(range(7, 20)), params(rt, max_tokens=4))  # max_seqs = 2: waits
+    m = s.schedule()
+    assert m.num_prefill == 2
+    failed = sorted(s.fail_scheduled())
+    assert failed == [a, b]
+    assert s.kv_metrics()["free_blocks"] == free0
+    assert s.num_running == 0 and s.num_waiting == 1
+    # the untouched request runs to completion
+    done = []
+    for _ in range(10):
+        if not s.has_unfinished():
+            break
+        _, ev = run_step(s, arena)
+        done += [e for e in ev if e[2]]
+    assert [e[0] for e in done] == [c]
+    km = s.kv_metrics()  # c's full blocks stay in the prefix cache
+    assert km["free_blocks"] + km["cached_blocks"] == free0

@@ -15,7 +15,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def _run(n, mode, graphs="graphs", model="tiny-tp", port=29611, extra_env=None):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE=os.environ.get("NCCL_NVLS_ENABLE", "1"), **(extra_env or {}))
+    env = dict(os.environ, NCCL_NVLS_ENABLE=os.environ.get("NCCL_NVLS_ENABLE", "1"),
+               TORCH_SYMM_MEM_DISABLE_MULTICAST="1", **(extra_env or {}))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={port}",
            os.path.join(ROOT, "tests", "tp_worker.py"), mode, graphs, model]
@@ -55,4 +56,4 @@ def test_ep_moe_fused(n):
 @pytest.mark.parametrize("n", [2])
 def test_tp_fused_pull_variant(n):
     """Row-parallel GEMMs write locally and the collective pulls (BLOOM_TP_PUSH=0)."""
-    _run(n, "fused", port=29671 + n, extra_env={"BLOOM_TP_PUSH": "0"})
+    _run(n, "fused", port=29711 + n, extra_env={"BLOOM_TP_PUSH": "0"})
