@@ -38,7 +38,8 @@ class SamplingParams:
     min_tokens: int = 0
     ignore_eos: bool = False
     stop_token_ids: List[int] = field(default_factory=list)
-    json_mode: bool = False
+    json_mode: bool = False  # constrain the output to a JSON object
+    json_schema: Optional[dict] = None  # ... that satisfies this JSON Schema (see engine.structured)
 
     def to_native(self, default_seed: int):
         sp = _rt().SamplingParams()
@@ -106,7 +107,21 @@ class EngineConfig:
     # "context_shift:<max_context_tokens>:<shift_tokens>" or
     # "compact_inactive:<target_free_blocks>"
     long_context_policy: str = "full"
+    # preemption when the KV pool cannot grow a running sequence: victim policy
+    # (newest, priority, oldest, kv_cost, aegaeon, lru, largest_first), a cap on
+    # preemptions per request (0 = none), priority preemption after a waiting
+    # request has waited this long (ms, < 0 = off), and the KV utilisation at
+    # which no new request is admitted (1.0 = off)
+    preemption_policy: str = "newest"
+    max_preemptions_per_request: int = 0
+    priority_preemption_ms: float = -1.0
+    kv_admission_threshold: float = 1.0
+    # swap preemption: pinned host bytes that preempted sequences' KV blocks are
+    # copied into (resumed without recompute); 0 = recompute preemption only
+    swap_space_bytes: int = 0
 
+
+VICTIM_POLICIES = {"newest": 0, "priority": 1, "oldest": 2, "kv_cost": 3, "aegaeon": 4, "lru": 5, "largest_first": 6}
 
 LONG_CONTEXT_POLICIES = {"full": 0, "sliding_window": 1, "context_shift": 2, "compact_inactive": 3}
 
@@ -156,6 +171,16 @@ class LLMEngine:
         sc.eos_token_ids = list(self.cfg.eos_token_ids)
         sc.spec_len = int(ec.spec_len)
         apply_long_context_policy(sc, ec.long_context_policy)
+        if ec.preemption_policy not in VICTIM_POLICIES:
+            raise ValueError(f"unknown preemption policy {ec.preemption_policy!r} ({', '.join(VICTIM_POLICIES)})")
+        if not 0.0 < ec.kv_admission_threshold <= 1.0:
+            raise ValueError("kv_admission_threshold must be in (0, 1]")
+        sc.victim_policy = VICTIM_POLICIES[ec.preemption_policy]
+        sc.max_preemptions_per_request = int(ec.max_preemptions_per_request)
+        sc.priority_preempt_ms = float(ec.priority_preemption_ms)
+        sc.kv_admission_threshold = float(ec.kv_admission_threshold)
+        swap_slots = int(ec.swap_space_bytes) // kv_block_bytes(model) if ec.swap_space_bytes > 0 else 0
+        sc.swap_slots = swap_slots
         self.scheduler = rt.Scheduler(sc, ec.num_blocks, 16, ec.enable_prefix_caching)
         self.runner = ModelRunner(model, ec.num_blocks, ec.max_num_seqs, ec.max_num_batched_tokens,
                                   ec.max_model_len, ec.use_cuda_graphs, spec_len=int(ec.spec_len))
@@ -166,6 +191,8 @@ class LLMEngine:
             ops.gemm_autotune(model.gemm_shapes(), [b * ql for b in self.runner.buckets + [ec.max_num_seqs]], dev)
         self.scheduler.set_arena(self.runner.arena_host, self.runner.max_tokens, ec.max_num_seqs,
                                  self.runner.max_blocks)
+        if swap_slots > 0:
+            self.runner.enable_swap(swap_slots)
         if ec.cachemesh_l2_bytes > 0:
             self.runner.enable_cachemesh(self.scheduler, ec.cachemesh_l2_bytes, ec.cachemesh_l3_dir,
                                          ec.cachemesh_l3_blocks, ec.cachemesh_namespace or self._namespace())
@@ -178,6 +205,7 @@ class LLMEngine:
         self._seed_counter = ec.seed
         self.step_times: List[float] = []
         self.failures: List[dict] = []  # steps failed by a kernel status error
+        self._mask_host = None  # constrained decoding: pinned token masks of one step
         self.speculator = None
 
     def attach_speculator(self, spec) -> None:
@@ -210,11 +238,12 @@ class LLMEngine:
         rid = self.scheduler.add_request([int(t) for t in prompt_token_ids], params.to_native(self._seed_counter),
                                          priority)
         self.requests[rid] = RequestOutput(rid, list(prompt_token_ids), arrival_time=time.perf_counter())
-        if params.json_mode and self.tokenizer is not None:
-            from .structured import JsonConstraint, vocab_strings
+        if (params.json_mode or params.json_schema is not None) and self.tokenizer is not None:
+            from .structured import SchemaConstraint, TokenVocab
 
-            self.constraints[rid] = JsonConstraint(vocab_strings(self.tokenizer, self.cfg.vocab_size),
-                                                   list(params.stop_token_ids) + list(self.cfg.eos_token_ids))
+            vocab = TokenVocab.get(self.tokenizer, self.cfg.vocab_size)
+            self.constraints[rid] = SchemaConstraint(vocab, params.json_schema,
+                                                     list(params.stop_token_ids) + list(self.cfg.eos_token_ids))
         return rid
 
     def abort(self, request_id: int) -> bool:
@@ -242,13 +271,19 @@ class LLMEngine:
         meta = self.scheduler.schedule()
         if self.runner.l2 is not None:
             self.runner.apply_kv_copies(self.scheduler.take_restores(), self.scheduler.take_offloads())
+        if self.econf.swap_space_bytes > 0:
+            ins, outs = self.scheduler.take_swap_ins(), self.scheduler.take_swap_outs()
+            if ins or outs:
+                self.runner.apply_swaps(ins, outs)
         if meta.num_tokens == 0:
             return []
-        sampled = self.runner.execute(meta)
+        if self.constraints:
+            logits = self.runner.launch(meta)
+            sampled = self.runner.finish(meta, logits, self._constraint_masks())  # masks built while the GPU runs
+        else:
+            sampled = self.runner.execute(meta)
         if self.runner.last_status:
             return self._fail_step(self.runner.last_status)
-        if self.constraints:
-            self._apply_constraints(sampled, meta)
         events = self.scheduler.update(sampled, meta.num_real_logits)
         now = time.perf_counter()
         out = []
@@ -309,21 +344,30 @@ class LLMEngine:
                 self.runner.capture_graphs()
         return out
 
-    def _apply_constraints(self, sampled, meta) -> None:
-        """JSON mode: replace the sampled token of constrained rows by the best
-        candidate (top-256 logits) that keeps the output valid JSON."""
+    def _constraint_masks(self):
+        """Allowed-token masks of this step's constrained sampling rows:
+        (rows int32 [R], mask int32 [R, words]) on the device, or None.  Each
+        constrained request has exactly one sampling row (it gets no
+        speculative proposals).  Host work: one cached trie walk per row."""
         ids = self.scheduler.sampling_ids()
-        # first row of each request only (constrained requests get no proposals)
         rows = [(i, sid) for i, sid in enumerate(ids) if sid in self.constraints and (i == 0 or ids[i - 1] != sid)]
-        if not rows or self.runner.last_logits is None or self.model.tp.size > 1:
-            return
-        logits = self.runner.last_logits
-        idx = torch.tensor([i for i, _ in rows], device=logits.device)
-        sel = logits.index_select(0, idx).float()
-        top = torch.topk(sel, k=min(256, logits.shape[1]), dim=1).indices.cpu()
-        for j, ((row, sid), cand) in enumerate(zip(rows, top.tolist())):
-            full = (lambda j=j: torch.argsort(sel[j], descending=True).cpu().tolist())
-            sampled[row] = self.constraints[sid].choose(cand, int(sampled[row]), full)
+        if not rows:
+            return None
+        words = next(iter(self.constraints.values())).words
+        R = len(rows)
+        if self._mask_host is None or self._mask_host.shape[0] < R or self._mask_host.shape[1] != words:
+            n = max(R, self.econf.max_num_seqs)
+            self._mask_host = torch.zeros(n, words, dtype=torch.int32).pin_memory()
+            self._mask_rows_host = torch.zeros(n, dtype=torch.int32).pin_memory()
+            self._mask_dev = torch.zeros(n, words, dtype=torch.int32, device=self.model.device)
+            self._mask_rows_dev = torch.zeros(n, dtype=torch.int32, device=self.model.device)
+        for j, (row, sid) in enumerate(rows):
+            self.constraints[sid].mask_into(self._mask_host[j])
+            self._mask_rows_host[j] = row
+        self._mask_dev[:R].copy_(self._mask_host[:R], non_blocking=True)
+        self._mask_rows_dev[:R].copy_(self._mask_rows_host[:R], non_blocking=True)
+        self.runner.stats["h2d_bytes"] += 4 * R * (words + 1)
+        return self._mask_rows_dev[:R], self._mask_dev[:R]
 
     def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None,
                  on_token: Optional[Callable[[RequestOutput], None]] = None) -> List[RequestOutput]:
@@ -347,6 +391,86 @@ class LLMEngine:
             if r.finished:
                 self.requests.pop(rid, None)
                 return
+
+    # ------------------------------------------------------------ KV state export / import
+    _BLOB_MAGIC = b"BLOOMKV1"
+
+    def export_state(self, request_id: int) -> bytes:
+        """Serialise a live request's KV cache and tokens (between steps) into
+        a blob: magic, header length, JSON header (model fingerprint, layout,
+        tokens, sampling parameters), then the request's KV pages as bf16
+        [blocks, layers, 2, kv_heads, 16, head_dim] (this rank's heads under
+        tensor parallelism).  `import_state` on an engine with the same model
+        and layout resumes it without recomputing the prefix.  Reference:
+        Model::export_state / import_state and StateBlob
+        (crates/engine/src/core/model.rs:11-21,215-238)."""
+        import json as _json
+        import struct
+
+        st = self.scheduler.export_sequence(int(request_id))
+        blocks = list(st["blocks"])
+        torch.cuda.synchronize(self.model.device)
+        if blocks:
+            idx = torch.tensor(blocks, dtype=torch.long, device=self.model.device)
+            pages = self.runner.kv_cache.index_select(1, idx).transpose(0, 1).contiguous().cpu()
+        else:
+            pages = torch.empty(0, dtype=torch.bfloat16)
+        sp = st["params"]
+        r = self.requests.get(int(request_id))
+        hdr = {"kind": "kv_cache", "model": self._namespace(), "num_layers": self.cfg.num_layers,
+               "kv_heads": self.model.nkv, "head_dim": self.cfg.head_dim, "block_size": 16, "dtype": "bf16",
+               "tp": [self.model.tp.rank, self.model.tp.size], "tokens": list(st["tokens"]),
+               "num_prompt": st["num_prompt"], "num_computed": st["num_computed"], "num_blocks": len(blocks),
+               "priority": st["priority"],
+               "params": {"max_tokens": sp.max_tokens, "temperature": sp.temperature, "top_p": sp.top_p,
+                          "top_k": sp.top_k, "seed": sp.seed, "min_tokens": sp.min_tokens,
+                          "ignore_eos": sp.ignore_eos, "stop_token_ids": list(sp.stop_token_ids)},
+               "arrival": r.arrival_time if r is not None else None}
+        h = _json.dumps(hdr, separators=(",", ":")).encode()
+        return self._BLOB_MAGIC + struct.pack("<I", len(h)) + h + pages.view(torch.uint8).numpy().tobytes()
+
+    def import_state(self, blob: bytes, params: Optional[SamplingParams] = None) -> int:
+        """Resume a request exported by `export_state`; returns its new id.
+        The blob's model fingerprint and KV layout must match this engine."""
+        import json as _json
+        import struct
+
+        if not blob.startswith(self._BLOB_MAGIC):
+            raise ValueError("not a bloom KV state blob")
+        n = struct.unpack("<I", blob[8:12])[0]
+        hdr = _json.loads(blob[12:12 + n])
+        want = {"model": self._namespace(), "num_layers": self.cfg.num_layers, "kv_heads": self.model.nkv,
+                "head_dim": self.cfg.head_dim, "block_size": 16, "dtype": "bf16",
+                "tp": [self.model.tp.rank, self.model.tp.size]}
+        for k, v in want.items():
+            if hdr.get(k) != v:
+                raise ValueError(f"KV state blob does not match this engine: {k} {hdr.get(k)!r} != {v!r}")
+        nb = int(hdr["num_blocks"])
+        payload = memoryview(blob)[12 + n:]
+        shape = (nb, self.cfg.num_layers, 2, self.model.nkv, 16, self.cfg.head_dim)
+        numel = 1
+        for d in shape:
+            numel *= d
+        if len(payload) != numel * 2:
+            raise ValueError(f"KV state blob payload has {len(payload)} bytes, expected {numel * 2}")
+        if params is None:
+            p = hdr["params"]
+            params = SamplingParams(max_tokens=p["max_tokens"], temperature=p["temperature"], top_p=p["top_p"],
+                                    top_k=p["top_k"], seed=p["seed"], min_tokens=p["min_tokens"],
+                                    ignore_eos=p["ignore_eos"], stop_token_ids=list(p["stop_token_ids"]))
+        self._seed_counter += 1
+        tokens = [int(t) for t in hdr["tokens"]]
+        rid, table = self.scheduler.import_sequence(tokens, int(hdr["num_prompt"]), int(hdr["num_computed"]),
+                                                    params.to_native(self._seed_counter), int(hdr["priority"]))
+        if nb:
+            pages = torch.frombuffer(bytearray(payload), dtype=torch.bfloat16).view(shape)
+            dev_pages = pages.to(self.model.device, non_blocking=False)
+            k = min(nb, len(table))
+            idx = torch.tensor(list(table[:k]), dtype=torch.long, device=self.model.device)
+            self.runner.kv_cache.index_copy_(1, idx, dev_pages[:k].transpose(0, 1).contiguous())
+        P = int(hdr["num_prompt"])
+        self.requests[rid] = RequestOutput(rid, tokens[:P], token_ids=tokens[P:], arrival_time=time.perf_counter())
+        return rid
 
     def kv_metrics(self) -> dict:
         d = dict(self.scheduler.kv_metrics())

@@ -120,6 +120,27 @@ class ModelRunner:
         self.stats["kv_restores"] = self.stats.get("kv_restores", 0) + len(restores)
         self.stats["kv_offloads"] = self.stats.get("kv_offloads", 0) + len(offloads)
 
+    # ------------------------------------------------------------ swap preemption
+    def enable_swap(self, slots: int) -> None:
+        """Pinned host slots (one KV block each, all layers) for swap preemption."""
+        bb = self.kv_block_bytes()
+        self.swap = torch.empty(max(1, slots) * bb, dtype=torch.uint8).pin_memory()
+        cfg = self.cfg
+        self.swap_view = self.swap.view(torch.bfloat16).view(max(1, slots), cfg.num_layers, 2, self.model.nkv,
+                                                             self.block_size, cfg.head_dim)
+
+    def apply_swaps(self, swap_ins, swap_outs) -> None:
+        """Swap-ins (host slot -> block) before swap-outs (block -> slot): a
+        slot freed by a swap-in may be reused by a swap-out of the same step.
+        Both are queued on the step's stream ahead of its forward, so a block
+        freed by a swap-out is copied before a new owner overwrites it."""
+        for blk, slot in swap_ins:
+            self.kv_cache[:, blk].copy_(self.swap_view[slot], non_blocking=True)
+        for blk, slot in swap_outs:
+            self.swap_view[slot].copy_(self.kv_cache[:, blk], non_blocking=True)
+        self.stats["swap_ins"] = self.stats.get("swap_ins", 0) + len(swap_ins)
+        self.stats["swap_outs"] = self.stats.get("swap_outs", 0) + len(swap_outs)
+
     # ------------------------------------------------------------ views
     def _v(self, off: int, n: int, dtype=torch.int32) -> torch.Tensor:
         if dtype == torch.int32 or dtype == torch.float32:
@@ -225,6 +246,11 @@ class ModelRunner:
     # ------------------------------------------------------------ step
     def execute(self, m) -> torch.Tensor:
         """Run one scheduled step; returns host int32 sampled tokens [num_logits]."""
+        return self.finish(m, self.launch(m))
+
+    def launch(self, m) -> torch.Tensor:
+        """Queue the step's arena copy and forward on the GPU; returns the
+        logits tensor without waiting (the host may prepare token masks meanwhile)."""
         used = m.used_words
         self.arena_dev[:used].copy_(self.arena_host[:used], non_blocking=True)
         graph = self.graphs.get(m.num_decode) if (m.num_prefill == 0 and m.num_decode > 0) else None
@@ -243,6 +269,15 @@ class ModelRunner:
                 raise FloatingPointError(f"non-finite logits in rows {rows} (T={m.num_tokens}, decode={m.num_decode}, "
                                          f"prefill={m.num_prefill})")
         self.last_logits = logits
+        return logits
+
+    def finish(self, m, logits: torch.Tensor, token_mask=None) -> torch.Tensor:
+        """Optional constrained-decoding masks (rows int32 [R], mask int32
+        [R, words] on the device), sampling, and the one device-to-host read
+        of the tokens and the status word."""
+        if token_mask is not None:
+            rows, mask = token_mask
+            ops.apply_token_mask(logits, rows, mask, self.model.tp.rank * self.model.vocab_local)
         toks = self._sample(logits, m, m.all_greedy)
         NL = m.num_logits
         self.sampled_host[:NL + 1].copy_(toks[:NL + 1], non_blocking=True)
@@ -250,6 +285,6 @@ class ModelRunner:
         self.last_status = int(self.sampled_host[NL])
         self.stats["steps"] += 1
         self.stats["tokens"] += m.num_tokens
-        self.stats["h2d_bytes"] += 4 * used
+        self.stats["h2d_bytes"] += 4 * m.used_words
         self.stats["d2h_bytes"] += 4 * (NL + 1)
         return self.sampled_host

@@ -519,6 +519,14 @@ def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
     return out
 
 
+def apply_token_mask(logits: torch.Tensor, rows: torch.Tensor, mask: torch.Tensor, col_offset: int = 0) -> None:
+    """Constrained decoding: set logits[rows[r], c] = -inf for every column c
+    whose token (col_offset + c) has no bit in mask[r] (int32 words, bit
+    t % 32 of word t // 32)."""
+    _C().apply_token_mask(logits, rows, mask, int(col_offset))
+    _count()
+
+
 def sample(logits, temperature, top_p, top_k, seeds, offsets, draft=None, out: Optional[torch.Tensor] = None):
     """Per-row temperature / top-k / top-p sampling (greedy rows: argmax).  With
     `draft` (int32 per row, -1 = none) stochastic rows verify their proposal by

@@ -256,6 +256,13 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
             raise APIError(400, "messages must be a non-empty array", param="messages")
         if len(msgs) > MAX_CHAT_MESSAGES:
             raise APIError(400, f"at most {MAX_CHAT_MESSAGES} messages", param="messages")
+        if any(isinstance(m, dict) and (m.get("tool_calls") or m.get("role") == "tool") for m in msgs):
+            from .tool_calling import ToolError, normalize_tool_history
+
+            try:
+                msgs = normalize_tool_history(msgs)
+            except ToolError as e:
+                raise APIError(400, str(e), param="messages") from None
         out, total = [], 0
         for m in msgs:
             if not isinstance(m, dict) or m.get("role") not in ("system", "user", "assistant", "tool", "developer"):
@@ -415,6 +422,34 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         check_model(model)
         return model_card()
 
+    # ------------------------------------------------------------ function tools
+    from .tool_calling import (ToolError, envelope_schema, finish_reason as tool_finish, parse_tool_output,
+                               protocol_instruction, tool_calls_json, tool_config)
+
+    def tool_setup(d: dict, msgs: List[Dict[str, str]], params, cfg=None):
+        """Parse tools / tool_choice; with tools active, append the protocol
+        instruction and constrain decoding to the JSON envelope."""
+        try:
+            if cfg is None:
+                cfg = tool_config(d.get("tools"), d.get("tool_choice"), d.get("parallel_tool_calls"))
+        except ToolError as e:
+            raise APIError(400, str(e), param="tools") from None
+        if cfg is None:
+            return None
+        msgs.append({"role": "system", "content": protocol_instruction(cfg)})
+        params.json_mode = True
+        params.json_schema = envelope_schema(cfg)
+        return cfg
+
+    def parse_tools_output(text: str, cfg):
+        from ..engine.structured import repair_json
+
+        try:
+            return parse_tool_output(repair_json(text), cfg)
+        except ToolError as e:
+            raise APIError(502, f"model output did not follow the function-calling protocol: {e}",
+                           "server_error") from None
+
     # ------------------------------------------------------------ chat / completions
     @app.post("/v1/chat/completions")
     async def chat(request: Request):
@@ -426,10 +461,14 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         params = sampling(d)
         stop_list = stops(d)
         rf = d.get("response_format")
-        if rf and rf.get("type") in ("json_object", "json_schema"):
-            from ..engine.structured import constrain_params
+        tools = tool_setup(d, msgs, params)
+        if rf is not None and tools is None:
+            from ..engine.structured import SchemaError, constrain_params
 
-            constrain_params(params, rf, pipeline)
+            try:
+                constrain_params(params, rf, pipeline)
+            except SchemaError as e:
+                raise APIError(400, str(e), param="response_format") from None
         cid = "chatcmpl-" + uuid.uuid4().hex[:24]
         created = int(time.time())
         stream = bool(d.get("stream"))
@@ -446,6 +485,15 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                     reason = r
             content = "".join(text)
             metrics.tokens_generated += n
+            if tools is not None:
+                parsed = parse_tools_output(content, tools)
+                msg = {"role": "assistant", "content": parsed.message}
+                if parsed.is_calls:
+                    msg["tool_calls"] = tool_calls_json(cid, parsed)
+                return {"id": cid, "object": "chat.completion", "created": created, "model": st.model_id,
+                        "choices": [{"index": 0, "message": msg, "logprobs": None,
+                                     "finish_reason": tool_finish(parsed, n, params.max_tokens)}],
+                        "usage": {"prompt_tokens": ptoks, "completion_tokens": n, "total_tokens": ptoks + n}}
             msg = {"role": "assistant", "content": content}
             if rf and rf.get("type") in ("json_object", "json_schema"):
                 from ..engine.structured import repair_json
@@ -463,14 +511,25 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
             yield f"data: {json.dumps(chunk({'role': 'assistant', 'content': ''}))}\n\n"
             n = 0
             reason = "stop"
+            buffered = []
             try:
                 async for out, fin, r in gen:
                     n += 1
-                    if out:
+                    if out and tools is not None:
+                        buffered.append(out)  # the envelope is parsed once complete
+                    elif out:
                         yield f"data: {json.dumps(chunk({'content': out}))}\n\n"
                     if fin:
                         reason = r
                         break
+                if tools is not None:
+                    parsed = parse_tools_output("".join(buffered), tools)
+                    delta = ({"tool_calls": tool_calls_json(cid, parsed, with_index=True)} if parsed.is_calls
+                             else {"content": parsed.message})
+                    metrics.tokens_generated += n
+                    yield f"data: {json.dumps(chunk(delta, tool_finish(parsed, n, params.max_tokens)))}\n\n"
+                    yield "data: [DONE]\n\n"
+                    return
             except APIError as e:
                 yield f"data: {json.dumps({'error': {'message': e.message, 'type': e.type}})}\n\n"
                 yield "data: [DONE]\n\n"
@@ -559,15 +618,36 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         rid = "resp_" + uuid.uuid4().hex[:24]
         mid = "msg_" + uuid.uuid4().hex[:24]
         created = int(time.time())
+        from .tool_calling import responses_tool_config
+
+        try:
+            rcfg, echoed_tools, echoed_choice = responses_tool_config(d.get("tools"), d.get("tool_choice"),
+                                                                      d.get("parallel_tool_calls"))
+        except ToolError as e:
+            raise APIError(400, str(e), param="tools") from None
+        tools = tool_setup(d, msgs, params, cfg=rcfg) if rcfg is not None else None
         gen = token_stream(msgs, params, [], request)
         first = await gen.__anext__()
         ptoks = first["prompt_tokens"]
 
         def final(text, n, status="completed"):
-            return {"id": rid, "object": "response", "created_at": created, "status": status, "model": st.model_id,
-                    "output": [{"type": "message", "id": mid, "status": "completed", "role": "assistant",
-                                "content": [{"type": "output_text", "text": text, "annotations": []}]}],
-                    "usage": {"input_tokens": ptoks, "output_tokens": n, "total_tokens": ptoks + n}}
+            output = [{"type": "message", "id": mid, "status": "completed", "role": "assistant",
+                       "content": [{"type": "output_text", "text": text, "annotations": []}]}]
+            if tools is not None and status == "completed":
+                parsed = parse_tools_output(text, tools)
+                if parsed.is_calls:
+                    output = [{"type": "function_call", "id": f"fc_{rid[5:]}_{i}", "call_id": cid_,
+                               "name": c["function"]["name"], "arguments": c["function"]["arguments"],
+                               "status": "completed"}
+                              for i, (c, cid_) in enumerate((c, c["id"]) for c in tool_calls_json(rid, parsed))]
+                else:
+                    output[0]["content"][0]["text"] = parsed.message
+            r = {"id": rid, "object": "response", "created_at": created, "status": status, "model": st.model_id,
+                 "output": output, "usage": {"input_tokens": ptoks, "output_tokens": n, "total_tokens": ptoks + n}}
+            if tools is not None or echoed_tools:
+                r.update(tools=echoed_tools, tool_choice=echoed_choice,
+                         parallel_tool_calls=bool(tools.parallel) if tools is not None else False)
+            return r
 
         if not d.get("stream"):
             text, n = [], 0
@@ -594,13 +674,19 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                 n += 1
                 if out:
                     text.append(out)
-                    yield ev("response.output_text.delta", {"item_id": mid, "output_index": 0, "content_index": 0,
-                                                            "delta": out})
+                    if tools is None:  # a function-calling envelope is reported once parsed
+                        yield ev("response.output_text.delta", {"item_id": mid, "output_index": 0,
+                                                                "content_index": 0, "delta": out})
                 if fin:
                     break
             full = "".join(text)
-            yield ev("response.output_text.done", {"item_id": mid, "output_index": 0, "content_index": 0, "text": full})
             resp = final(full, n)
+            if tools is None:
+                yield ev("response.output_text.done", {"item_id": mid, "output_index": 0, "content_index": 0,
+                                                       "text": full})
+            else:
+                for i, item in enumerate(resp["output"]):
+                    yield ev("response.output_item.done", {"output_index": i, "item": item})
             store.put(rid, resp, msgs)
             metrics.tokens_generated += n
             yield ev("response.completed", {"response": resp})

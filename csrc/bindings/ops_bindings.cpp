@@ -38,6 +38,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_head_chunks", &bloom::decode_head_chunks);
   m.def("paged_prefill_attention_tc", &bloom::paged_prefill_attention_tc);
   m.def("argmax_rows", &bloom::argmax_rows);
+  m.def("apply_token_mask", &bloom::apply_token_mask);
   m.def("sample_rows", &bloom::sample_rows);
   m.def("verify_sample_rows", &bloom::verify_sample_rows);
   m.def("qgemv", &bloom::qgemv, py::arg("x"), py::arg("qs"), py::arg("scales"), py::arg("kind"), py::arg("out"),

@@ -39,6 +39,7 @@ void register_json(py::module_& m);     // csrc/runtime/json_dfa.cpp
 void register_plugin(py::module_& m);   // csrc/runtime/plugin_loader.cpp
 void register_quantize(py::module_& m); // csrc/runtime/quantize.cpp
 void register_admission(py::module_& m); // csrc/runtime/admission.cpp
+void register_schema(py::module_& m);    // csrc/runtime/schema_matcher.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 host runtime: KV block manager, in-flight batching scheduler, CPU kernels";
@@ -99,6 +100,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readwrite("chunked_prefill", &SchedulerConfig::chunked_prefill)
       .def_readwrite("eos_token_ids", &SchedulerConfig::eos_token_ids)
       .def_readwrite("spec_len", &SchedulerConfig::spec_len)
+      .def_readwrite("victim_policy", &SchedulerConfig::victim_policy)
+      .def_readwrite("max_preemptions_per_request", &SchedulerConfig::max_preemptions_per_request)
+      .def_readwrite("priority_preempt_ms", &SchedulerConfig::priority_preempt_ms)
+      .def_readwrite("kv_admission_threshold", &SchedulerConfig::kv_admission_threshold)
+      .def_readwrite("swap_slots", &SchedulerConfig::swap_slots)
       .def_readwrite("lc_policy", &SchedulerConfig::lc_policy)
       .def_readwrite("lc_window_tokens", &SchedulerConfig::lc_window_tokens)
       .def_readwrite("lc_max_context", &SchedulerConfig::lc_max_context)
@@ -168,6 +174,34 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("num_waiting", &Scheduler::num_waiting)
       .def_property_readonly("num_running", &Scheduler::num_running)
       .def_property_readonly("total_preemptions", &Scheduler::total_preemptions)
+      .def_property_readonly("admissions_deferred", &Scheduler::admissions_deferred)
+      .def_property_readonly("priority_preemptions", &Scheduler::priority_preemptions)
+      .def("set_clock_ms", &Scheduler::set_clock_ms)
+      .def("take_swap_ins", &Scheduler::take_swap_ins)
+      .def("take_swap_outs", &Scheduler::take_swap_outs)
+      .def_property_readonly("free_swap_slots", &Scheduler::free_swap_slots)
+      .def_property_readonly("total_swap_outs", &Scheduler::total_swap_outs)
+      .def("export_sequence",
+           [](const Scheduler& s, int64_t id) {
+             const Scheduler::SeqState st = s.export_sequence(id);
+             py::dict d;
+             d["tokens"] = st.tokens;
+             d["num_prompt"] = st.num_prompt;
+             d["num_computed"] = st.num_computed;
+             d["blocks"] = st.blocks;
+             d["priority"] = st.priority;
+             d["params"] = st.sp;
+             return d;
+           })
+      .def("import_sequence", &Scheduler::import_sequence, py::arg("tokens"), py::arg("num_prompt"),
+           py::arg("num_computed"), py::arg("params"), py::arg("priority") = 0)
+      .def("now_ms", &Scheduler::now_ms)
+      .def("kv_utilization", &Scheduler::kv_utilization)
+      .def("num_preemptions",
+           [](const Scheduler& s, int64_t id) {
+             const Sequence* q = s.find(id);
+             return q == nullptr ? -1 : q->num_preemptions;
+           })
       .def("schedule", &Scheduler::schedule, py::call_guard<py::gil_scoped_release>())
       .def("update",
            [](Scheduler& s, const torch::Tensor& sampled, int n) {
@@ -263,4 +297,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_plugin(m);
   register_quantize(m);
   register_admission(m);
+  register_schema(m);
 }

@@ -85,6 +85,7 @@ int64_t decode_head_chunks(int64_t num_q_heads, int64_t num_kv_heads, int64_t q_
 
 // Sampling.
 void argmax_rows(const torch::Tensor& logits, torch::Tensor& out);
+void apply_token_mask(torch::Tensor& logits, const torch::Tensor& rows, const torch::Tensor& mask, int64_t col_offset);
 void sample_rows(const torch::Tensor& logits, const torch::Tensor& temperature, const torch::Tensor& top_p,
                  const torch::Tensor& top_k, const torch::Tensor& seeds, const torch::Tensor& offsets,
                  torch::Tensor& out);

@@ -432,6 +432,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
+// ---- constrained decoding: allowed-token masks from the host matcher
+// mask [R, words] uint32, bit (t % 32) of word (t / 32) = token t allowed;
+// rows[r] = the logits row of constraint r; this rank's logits hold the
+// vocabulary columns [col_offset, col_offset + Vl).  Disallowed logits become
+// -inf in place, so the ordinary argmax / sampler only picks allowed tokens.
+namespace {
+__global__ void apply_token_mask_kernel(__nv_bfloat16* __restrict__ logits, long ld, int Vl,
+                                        const int* __restrict__ rows, const uint32_t* __restrict__ mask, int words,
+                                        int col_offset) {
+  const int r = blockIdx.y;
+  __nv_bfloat16* lr = logits + (long)rows[r] * ld;
+  const uint32_t* mr = mask + (long)r * words;
+  const __nv_bfloat16 ninf = __ushort_as_bfloat16(0xFF80u);
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < Vl; c += gridDim.x * blockDim.x) {
+    const int t = c + col_offset;
+    const int w = t >> 5;
+    const bool ok = w < words && ((mr[w] >> (t & 31)) & 1u);
+    if (!ok) lr[c] = ninf;
+  }
+}
+}  // namespace
+
+void apply_token_mask(torch::Tensor& logits, const torch::Tensor& rows, const torch::Tensor& mask, int64_t col_offset) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
+              "apply_token_mask: logits bf16 [NL, V]");
+  TORCH_CHECK(rows.scalar_type() == at::kInt && rows.is_contiguous() && rows.is_cuda(), "apply_token_mask: rows int32");
+  TORCH_CHECK(mask.scalar_type() == at::kInt && mask.is_contiguous() && mask.dim() == 2 && mask.is_cuda(),
+              "apply_token_mask: mask int32 [R, words]");
+  const int R = static_cast<int>(rows.numel());
+  TORCH_CHECK(mask.size(0) >= R, "apply_token_mask: fewer mask rows than constrained rows");
+  if (R == 0) return;
+  const int Vl = static_cast<int>(logits.size(1));
+  const at::cuda::CUDAGuard g(logits.device());
+  const int bx = std::max(1, std::min(64, (Vl + 1023) / 1024));
+  apply_token_mask_kernel<<<dim3(bx, R), 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0), Vl, rows.data_ptr<int>(),
+      reinterpret_cast<const uint32_t*>(mask.data_ptr()), static_cast<int>(mask.size(1)), static_cast<int>(col_offset));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void argmax_rows(const torch::Tensor& logits, torch::Tensor& out) {
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "argmax: logits [B, V]");
   TORCH_CHECK(out.scalar_type() == at::kInt, "argmax: out int32");

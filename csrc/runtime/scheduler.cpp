@@ -7,7 +7,9 @@ namespace bloom {
 namespace rt {
 
 Scheduler::Scheduler(const SchedulerConfig& cfg, int num_blocks, int block_size, bool prefix_caching)
-    : cfg_(cfg), bm_(num_blocks, block_size, prefix_caching) {}
+    : cfg_(cfg), bm_(num_blocks, block_size, prefix_caching) {
+  for (int i = cfg.swap_slots - 1; i >= 0; --i) free_swap_.push_back(i);
+}
 
 int64_t Scheduler::add_request(const std::vector<int32_t>& prompt, const SamplingParams& sp, int priority) {
   if (prompt.empty()) throw std::invalid_argument("add_request: empty prompt");
@@ -20,6 +22,8 @@ int64_t Scheduler::add_request(const std::vector<int32_t>& prompt, const Samplin
   s->sp = sp;
   s->priority = priority;
   s->order = next_order_++;
+  s->arrival_ms = now_ms();
+  s->last_scheduled_ms = s->arrival_ms;
   Sequence* p = s.get();
   seqs_[p->id] = std::move(s);
   // higher priority first, FCFS inside a priority class
@@ -38,6 +42,9 @@ void Scheduler::finish(Sequence* s, FinishReason r) {
   s->status = SeqStatus::Finished;
   s->finish = r;
   bm_.release(s->table, s->hashes);
+  for (int32_t slot : s->swap_slots) free_swap_.push_back(slot);
+  s->swap_slots.clear();
+  s->swapped = false;
 }
 
 bool Scheduler::abort(int64_t id) {
@@ -52,14 +59,92 @@ bool Scheduler::abort(int64_t id) {
   return true;
 }
 
-void Scheduler::preempt(Sequence* s) {
+void Scheduler::preempt(Sequence* s, bool to_front) {
   running_.erase(std::remove(running_.begin(), running_.end(), s), running_.end());
+  const int bs = bm_.block_size();
+  const int keep = (s->num_computed + bs - 1) / bs;  // blocks holding computed KV
+  if (keep > 0 && static_cast<int>(free_swap_.size()) >= keep && keep <= static_cast<int>(s->table.size())) {
+    // swap: copy the computed blocks to host slots; the sequence keeps its progress
+    s->swap_slots.clear();
+    for (int b = 0; b < keep; ++b) {
+      const int32_t slot = free_swap_.back();
+      free_swap_.pop_back();
+      swap_out_q_.emplace_back(s->table[b], slot);
+      s->swap_slots.push_back(slot);
+    }
+    s->swapped = true;
+    ++total_swap_outs_;
+  } else {
+    s->num_computed = 0;
+  }
   bm_.release(s->table, s->hashes);
-  s->num_computed = 0;
   s->status = SeqStatus::Waiting;
   ++s->num_preemptions;
   ++total_preemptions_;
-  waiting_.push_front(s);
+  if (to_front) {
+    waiting_.push_front(s);
+    return;
+  }
+  // behind every waiting request of higher or equal priority
+  auto it = waiting_.begin();
+  while (it != waiting_.end() && (*it)->priority >= s->priority) ++it;
+  waiting_.insert(it, s);
+}
+
+double Scheduler::now_ms() const {
+  if (clock_override_ms_ >= 0.0) return clock_override_ms_;
+  using namespace std::chrono;
+  return duration<double, std::milli>(steady_clock::now().time_since_epoch()).count();
+}
+
+double Scheduler::kv_utilization() const {
+  const PoolMetrics pm = bm_.metrics();
+  return pm.total_blocks ? static_cast<double>(pm.active_blocks) / static_cast<double>(pm.total_blocks) : 1.0;
+}
+
+double Scheduler::victim_cost(const Sequence& s, double now) const {
+  const double kv = static_cast<double>(s.num_computed);
+  switch (static_cast<VictimPolicy>(cfg_.victim_policy)) {
+    case VictimPolicy::Priority:
+      return static_cast<double>(s.priority);
+    case VictimPolicy::Oldest:
+      return -static_cast<double>(s.num_generated());
+    case VictimPolicy::KvCost:
+      return kv;
+    case VictimPolicy::AegaeonScore: {
+      const double age_s = std::max(1e-3, (now - s.arrival_ms) / 1e3);
+      return age_s / std::max(1.0, kv);
+    }
+    case VictimPolicy::Lru:
+      return -(now - s.last_scheduled_ms);
+    case VictimPolicy::LargestFirst:
+      return -kv;
+    case VictimPolicy::Newest:
+    default:
+      return -static_cast<double>(s.order);
+  }
+}
+
+Sequence* Scheduler::pick_victim(const Sequence* requester, const std::vector<Sequence*>& scheduled) const {
+  const double now = now_ms();
+  const int cap = cfg_.max_preemptions_per_request;
+  Sequence* best = nullptr;
+  Sequence* best_capped = nullptr;
+  double bc = 0.0, bcc = 0.0;
+  auto better = [&](Sequence* cand, double c, Sequence* cur, double cur_c) {
+    return cur == nullptr || c < cur_c || (c == cur_c && cand->order > cur->order);
+  };
+  for (Sequence* r : running_) {
+    if (r == requester || r->status != SeqStatus::Running) continue;
+    if (std::find(scheduled.begin(), scheduled.end(), r) != scheduled.end()) continue;
+    const double c = victim_cost(*r, now);
+    if (cap > 0 && r->num_preemptions >= cap) {
+      if (better(r, c, best_capped, bcc)) best_capped = r, bcc = c;
+    } else if (better(r, c, best, bc)) {
+      best = r, bc = c;
+    }
+  }
+  return best ? best : best_capped;
 }
 
 bool Scheduler::is_stop(const Sequence& s, int32_t tok) const {
@@ -119,6 +204,29 @@ StepMeta Scheduler::schedule() {
   std::vector<Sequence*> decodes;
   std::vector<Prefill> prefills;
 
+  // 0) priority preemption (before anything is scheduled): the head of the
+  // wait queue outranks running sequences and has waited long enough, but the
+  // pool cannot hold its prompt -> lower-priority sequences give up their
+  // blocks (lowest priority, newest first) until it fits
+  if (cfg_.priority_preempt_ms >= 0.0 && !waiting_.empty()) {
+    Sequence* h = waiting_.front();
+    if (now_ms() - h->arrival_ms >= cfg_.priority_preempt_ms) {
+      const int need_blocks =
+          (static_cast<int>(h->tokens.size()) + bs - 1) / bs - static_cast<int>(h->table.size());
+      while (static_cast<int>(bm_.num_available()) < need_blocks) {
+        Sequence* v = nullptr;
+        for (Sequence* r : running_)
+          if (r->priority < h->priority &&
+              (v == nullptr || r->priority < v->priority || (r->priority == v->priority && r->order > v->order)))
+            v = r;
+        if (v == nullptr) break;
+        preempt(v, /*to_front=*/false);  // h stays at the head of the queue
+        ++m.num_preempted;
+        ++priority_preemptions_;
+      }
+    }
+  }
+
   // 1) decode rows: running sequences that need exactly their last token computed.
   const std::vector<Sequence*> snapshot = running_;
   for (Sequence* s : snapshot) {
@@ -128,14 +236,14 @@ StepMeta Scheduler::schedule() {
     if (budget < ql || static_cast<int>(decodes.size()) >= arena_.max_seqs) break;
     bool ok = bm_.ensure_capacity(s->table, s->num_computed + ql);
     while (!ok) {
-      // preempt the most recently admitted running sequence not yet scheduled
-      Sequence* victim = nullptr;
-      for (auto it = running_.rbegin(); it != running_.rend(); ++it)
-        if (*it != s && std::find(decodes.begin(), decodes.end(), *it) == decodes.end()) {
-          victim = *it;
-          break;
-        }
+      // preempt the policy's victim among running sequences not yet scheduled
+      // (the requester itself when the policy ranks it first)
+      Sequence* victim = pick_victim(s, decodes);
       if (victim == nullptr) break;
+      if (cfg_.victim_policy != static_cast<int>(VictimPolicy::Newest)) {
+        const double now = now_ms();
+        if (victim_cost(*s, now) < victim_cost(*victim, now)) break;
+      }
       preempt(victim);
       ++m.num_preempted;
       ok = bm_.ensure_capacity(s->table, s->num_computed + ql);
@@ -161,11 +269,16 @@ StepMeta Scheduler::schedule() {
     budget -= len;
   }
 
-  // 3) admit waiting sequences
+  // 3) admit waiting sequences (not while the KV pool is above the admission threshold)
+  if (!waiting_.empty() && cfg_.kv_admission_threshold < 1.0 && kv_utilization() >= cfg_.kv_admission_threshold &&
+      !(running_.empty() && decodes.empty() && prefills.empty())) {
+    ++admissions_deferred_;
+    budget = 0;
+  }
   while (!waiting_.empty() && budget > 0 && static_cast<int>(running_.size()) < cfg_.max_num_seqs &&
          static_cast<int>(prefills.size()) + static_cast<int>(decodes.size()) < arena_.max_seqs) {
     Sequence* s = waiting_.front();
-    if (s->table.empty()) {
+    if (s->table.empty() && !s->swapped) {
       // prefix reuse: whole cached blocks, always leaving the last token to compute
       const int max_cached = ((static_cast<int>(s->tokens.size()) - 1) / bs) * bs;
       s->num_computed = bm_.match_prefix(s->tokens, max_cached, s->table, s->hashes);
@@ -174,7 +287,8 @@ StepMeta Scheduler::schedule() {
     const int need = static_cast<int>(s->tokens.size()) - s->num_computed;
     int len = cfg_.chunked_prefill ? std::min(need, budget) : need;
     if (len > budget) break;
-    if (!bm_.ensure_capacity(s->table, s->num_computed + len)) {
+    const bool fits = bm_.ensure_capacity(s->table, s->num_computed + len);
+    if (!fits) {
       if (running_.empty() && decodes.empty() && prefills.empty()) {
         // nothing else holds blocks: this request can never fit
         waiting_.pop_front();
@@ -184,6 +298,15 @@ StepMeta Scheduler::schedule() {
       break;
     }
     waiting_.pop_front();
+    if (s->swapped) {
+      // swap in: the saved blocks go back into the first blocks of the new table
+      for (size_t b = 0; b < s->swap_slots.size(); ++b) {
+        swap_in_q_.emplace_back(s->table[b], s->swap_slots[b]);
+        free_swap_.push_back(s->swap_slots[b]);  // the runner copies swap-ins before any swap-out
+      }
+      s->swap_slots.clear();
+      s->swapped = false;
+    }
     s->status = SeqStatus::Running;
     s->admitted_once = true;
     running_.push_back(s);
@@ -334,6 +457,9 @@ StepMeta Scheduler::schedule() {
     tseq[i] = tiles[i].seq;
     tstart[i] = tiles[i].start;
   }
+  const double tnow = now_ms();
+  for (Sequence* s : decodes) s->last_scheduled_ms = tnow;
+  for (auto& p : prefills) p.s->last_scheduled_ms = tnow;
   for (Sequence* s : decodes) s->num_computed += ql;  // provisional for verify rows: update() rolls back
   for (Sequence* s : decodes) last_scheduled_.push_back(s);
   for (auto& p : prefills) last_scheduled_.push_back(p.s);
@@ -490,6 +616,54 @@ std::vector<int64_t> Scheduler::fail_scheduled() {
   row_group_.clear();
   for (int64_t id : ids) seqs_.erase(id);
   return ids;
+}
+
+Scheduler::SeqState Scheduler::export_sequence(int64_t id) const {
+  const Sequence* s = find(id);
+  if (s == nullptr || s->status == SeqStatus::Finished) throw std::invalid_argument("export_sequence: unknown id");
+  if (s->swapped) throw std::invalid_argument("export_sequence: sequence is swapped out; export it once resumed");
+  SeqState st;
+  st.tokens = s->tokens;
+  st.num_prompt = s->num_prompt;
+  // verify rows of a scheduled step are provisional: export between steps only
+  st.num_computed = s->num_computed;
+  const int bs = bm_.block_size();
+  const int nb = (st.num_computed + bs - 1) / bs;
+  st.blocks.assign(s->table.begin(), s->table.begin() + std::min<int>(nb, static_cast<int>(s->table.size())));
+  st.num_computed = std::min<int>(st.num_computed, static_cast<int>(st.blocks.size()) * bs);
+  st.sp = s->sp;
+  st.priority = s->priority;
+  return st;
+}
+
+std::pair<int64_t, std::vector<int32_t>> Scheduler::import_sequence(const std::vector<int32_t>& tokens,
+                                                                    int num_prompt, int num_computed,
+                                                                    const SamplingParams& sp, int priority) {
+  if (tokens.empty() || num_prompt < 1 || num_prompt > static_cast<int>(tokens.size()))
+    throw std::invalid_argument("import_sequence: bad token counts");
+  if (static_cast<int>(tokens.size()) >= cfg_.max_model_len)
+    throw std::invalid_argument("import_sequence: sequence longer than max_model_len");
+  // at least the last token is recomputed, so the first step samples from it
+  num_computed = std::max(0, std::min(num_computed, static_cast<int>(tokens.size()) - 1));
+  auto s = std::make_unique<Sequence>();
+  s->id = next_id_++;
+  s->tokens = tokens;
+  s->num_prompt = num_prompt;
+  s->num_computed = num_computed;
+  s->num_cached_prefix = num_computed;
+  s->sp = sp;
+  s->priority = priority;
+  s->order = next_order_++;
+  s->arrival_ms = now_ms();
+  s->last_scheduled_ms = s->arrival_ms;
+  if (num_computed > 0 && !bm_.ensure_capacity(s->table, num_computed))
+    throw std::runtime_error("import_sequence: no free KV blocks for the imported state");
+  Sequence* p = s.get();
+  seqs_[p->id] = std::move(s);
+  auto it = waiting_.end();
+  while (it != waiting_.begin() && (*(it - 1))->priority < priority) --it;
+  waiting_.insert(it, p);
+  return {p->id, p->table};
 }
 
 // ---------------------------------------------------------------- speculation

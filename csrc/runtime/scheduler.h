@@ -17,6 +17,7 @@
 // Stop conditions come from the model (EOS ids), never a hard-coded token id.
 #pragma once
 
+#include <chrono>
 #include <cstdint>
 #include <deque>
 #include <memory>
@@ -60,8 +61,29 @@ struct Sequence {
   int num_preemptions = 0;
   bool admitted_once = false;
   bool verifying = false;  // scheduled as a verify group in the current step
+  // swap preemption: host slots holding this sequence's first blocks while it waits
+  std::vector<int32_t> swap_slots;
+  bool swapped = false;
+  double arrival_ms = 0.0;          // scheduler clock at add_request
+  double last_scheduled_ms = 0.0;   // scheduler clock of the last step that ran it
   int num_generated() const { return static_cast<int>(tokens.size()) - num_prompt; }
 };
+
+// Which running sequence gives up its KV blocks when the pool cannot grow
+// another one (recompute preemption).  Lower cost is chosen first; ties go to
+// the most recently admitted sequence.
+//   Newest       most recently admitted (the default)
+//   Priority     lowest request priority           (reference PreemptionPolicy::Priority)
+//   Oldest       most generated tokens             (PreemptionPolicy::Oldest: cost = -generated)
+//   KvCost       fewest KV tokens (cheapest redo)  (PreemptionPolicy::KvCost)
+//   AegaeonScore age x value / KV tokens: young sessions holding much KV
+//                go first (priority_eviction.rs, Aegaeon section 5.2; value = 1)
+//   Lru          longest since last scheduled      (KvEvictionPolicy::Lru)
+//   LargestFirst most KV tokens                    (KvEvictionPolicy::LargestFirst)
+// (reference: crates/core/src/token_scheduling/preemption.rs:20-64,136-240,
+// priority_eviction.rs:38-74,173-312)
+enum class VictimPolicy : int { Newest = 0, Priority = 1, Oldest = 2, KvCost = 3, AegaeonScore = 4, Lru = 5,
+                                LargestFirst = 6 };
 
 struct SchedulerConfig {
   int max_num_seqs = 256;
@@ -81,6 +103,24 @@ struct SchedulerConfig {
   // evicted until lc_target_free blocks are free.  Visibility is per step
   // and whole blocks; the window never starts inside the tokens of the
   // current step, so every query still sees its own position.
+  // Preemption: victim policy (VictimPolicy), per-request cap (a sequence
+  // preempted this many times is not chosen again while another candidate
+  // exists; 0 = no cap), and priority preemption: a waiting request whose
+  // priority is above a running one and that has waited at least
+  // priority_preempt_ms (< 0: off) may preempt lower-priority sequences to
+  // get its KV blocks.
+  int victim_policy = 0;
+  int max_preemptions_per_request = 0;
+  double priority_preempt_ms = -1.0;
+  // KV admission threshold: no waiting request is admitted while the used
+  // fraction of the KV pool is at or above it (reference
+  // KvEvictionManager::check_admission, default 0.85 there; 1.0 = off here).
+  double kv_admission_threshold = 1.0;
+  // Swap preemption: host slots (one KV block each) that a preempted
+  // sequence's blocks are copied into instead of being recomputed later
+  // (0 = recompute preemption only; a victim whose blocks do not fit in the
+  // free slots is recomputed).
+  int swap_slots = 0;
   int lc_policy = 0;  // 0 full, 1 sliding window, 2 context shift, 3 compact inactive
   int lc_window_tokens = 0;
   int lc_max_context = 0;
@@ -204,6 +244,40 @@ class Scheduler {
   const Sequence* find(int64_t id) const;
   const SchedulerConfig& config() const { return cfg_; }
   int64_t total_preemptions() const { return total_preemptions_; }
+  int64_t admissions_deferred() const { return admissions_deferred_; }
+  int64_t priority_preemptions() const { return priority_preemptions_; }
+  // ---- swap preemption: block copies the runner issues before the step's
+  // forward, swap-ins (host slot -> block) first, then swap-outs (block -> slot)
+  std::vector<std::pair<int32_t, int32_t>> take_swap_ins() { return std::move(swap_in_q_); }
+  std::vector<std::pair<int32_t, int32_t>> take_swap_outs() { return std::move(swap_out_q_); }
+  int free_swap_slots() const { return static_cast<int>(free_swap_.size()); }
+  int64_t total_swap_outs() const { return total_swap_outs_; }
+
+  // ---- KV state export / import (reference Model::export_state /
+  // import_state, crates/engine/src/core/model.rs:215-238)
+  struct SeqState {
+    std::vector<int32_t> tokens;
+    int num_prompt = 0;
+    int num_computed = 0;         // tokens whose KV is in the blocks below
+    std::vector<int32_t> blocks;  // block ids holding those tokens, in order
+    SamplingParams sp;
+    int priority = 0;
+  };
+  // A running or waiting (not swapped) sequence's state; throws if unknown.
+  SeqState export_sequence(int64_t id) const;
+  // New waiting sequence that resumes from num_computed tokens of KV: its
+  // blocks are allocated now (returned in SeqState::blocks) and the caller
+  // copies the pages in before the next step.  Throws if the pool is full.
+  std::pair<int64_t, std::vector<int32_t>> import_sequence(const std::vector<int32_t>& tokens, int num_prompt,
+                                                           int num_computed, const SamplingParams& sp, int priority);
+
+  // Scheduler clock in milliseconds (steady clock; a test may pin it).
+  double now_ms() const;
+  void set_clock_ms(double ms) { clock_override_ms_ = ms; }
+  // Fraction of the KV pool held by sequences and the prefix cache's active blocks.
+  double kv_utilization() const;
+  // Cost of choosing `s` as the preemption victim under the configured policy.
+  double victim_cost(const Sequence& s, double now) const;
   // speculation counters: verify groups, proposals offered, proposals accepted
   int64_t spec_steps() const { return spec_steps_; }
   int64_t spec_proposed() const { return spec_proposed_; }
@@ -217,7 +291,12 @@ class Scheduler {
   }
 
  private:
-  void preempt(Sequence* s);
+  // Recompute preemption: release the blocks and requeue at the head of the
+  // wait queue (to_front) or behind the waiting requests of >= priority.
+  void preempt(Sequence* s, bool to_front = true);
+  // Lowest-cost running sequence that is not `requester` and not already in
+  // `scheduled`; sequences at the preemption cap only when nothing else is left.
+  Sequence* pick_victim(const Sequence* requester, const std::vector<Sequence*>& scheduled) const;
   bool is_stop(const Sequence& s, int32_t tok) const;
   FinishReason stop_reason(const Sequence& s, int32_t tok) const;
   void finish(Sequence* s, FinishReason r);
@@ -237,6 +316,12 @@ class Scheduler {
   int64_t next_id_ = 1;
   int64_t next_order_ = 0;
   int64_t total_preemptions_ = 0;
+  int64_t admissions_deferred_ = 0;
+  int64_t total_swap_outs_ = 0;
+  std::vector<int32_t> free_swap_;
+  std::vector<std::pair<int32_t, int32_t>> swap_in_q_, swap_out_q_;
+  int64_t priority_preemptions_ = 0;
+  double clock_override_ms_ = -1.0;
   int64_t spec_steps_ = 0, spec_proposed_ = 0, spec_accepted_ = 0;
 };
 

@@ -278,3 +278,33 @@ def test_sliding_window_policy(graphs):
     assert all(len(o.token_ids) == 10 and all(0 <= t < cfg.vocab_size for t in o.token_ids) for o in outs2)
     _check_greedy(cfg, w, prompts[2], outs2[2].token_ids)  # 3 + 10 tokens fit in the window
     assert int(ops.status()[0].item()) == 0
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+@pytest.mark.parametrize("temperature", [0.0, 0.9])
+def test_json_schema_constrained_decoding_random_weights(graphs, temperature):
+    """Random weights pick tokens at random; the device vocabulary mask must
+    still force every output to be a JSON document the schema accepts,
+    ended by end-of-sequence."""
+    import json
+
+    from bloom_b200.engine.engine import SamplingParams
+    from bloom_b200.engine.structured import validate_json_schema_subset
+    from bloom_b200.engine.text import Tokenizer
+
+    cfg, w, eng = _build("tiny-llama", graphs=graphs)
+    eng.tokenizer = Tokenizer(None)  # byte tokenizer: ids 3..258 are the bytes, 2 = end of sequence
+    schema = {"type": "object", "properties": {"a": {"enum": ["x", "yy"]}, "b": {"type": "boolean"},
+                                               "c": {"type": "null"}, "d": {"enum": [1, 22]}},
+              "required": ["a", "b", "c", "d"], "additionalProperties": False}
+    prompts = [[5, 6, 7], [9, 10, 11, 12, 13], [20] * 30]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=250, temperature=temperature, seed=7, json_schema=schema,
+                                                stop_token_ids=[2]))
+    for o in outs:
+        assert o.finish_reason == "stop", (o.finish_reason, o.token_ids)
+        body = bytes(t - 3 for t in o.token_ids if 3 <= t < 259).decode()
+        assert all(3 <= t < 259 or t == 2 for t in o.token_ids), o.token_ids
+        validate_json_schema_subset(json.loads(body), schema)
+    from bloom_b200 import ops
+
+    assert int(ops.status()[0].item()) == 0

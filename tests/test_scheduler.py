@@ -397,3 +397,203 @@ def test_fail_scheduled_frees_kv_and_spares_others(rt):
     assert [e[0] for e in done] == [c]
     km = s.kv_metrics()  # c's full blocks stay in the prefix cache
     assert km["free_blocks"] + km["cached_blocks"] == free0
+
+
+# ---------------------------------------------------------------- preemption policies
+def _policy_sched(rt, policy, cap=0, priorities=(0, 0, 0, 0), lens=(16, 16, 16, 16), blocks=8):
+    cfg = rt.SchedulerConfig()
+    cfg.max_num_seqs = 4
+    cfg.max_num_batched_tokens = 256
+    cfg.max_model_len = 512
+    cfg.eos_token_ids = [2]
+    cfg.victim_policy = {"newest": 0, "priority": 1, "oldest": 2, "kv_cost": 3, "aegaeon": 4, "lru": 5,
+                         "largest_first": 6}[policy]
+    cfg.max_preemptions_per_request = cap
+    s = rt.Scheduler(cfg, blocks, 16, False)
+    mb = 32
+    worst = rt.arena_layout(256, 4, 4, 256 // 64 + 4, 256 + 4, mb)
+    arena = torch.zeros(worst.used_words, dtype=torch.int32)
+    s.set_arena(arena, 256, 4, mb)
+    s.set_clock_ms(0.0)
+    ids = []
+    for i, (p, n) in enumerate(zip(priorities, lens)):
+        s.set_clock_ms(float(i) * 1000.0)  # arrivals 1 s apart
+        ids.append(s.add_request([3 + i] * n, params(rt, max_tokens=100, ignore_eos=True), p))
+    return s, arena, ids
+
+
+def _victim(rt, s, arena, ids, steps=40):
+    for _ in range(steps):
+        m = s.schedule()
+        sampled = torch.full((max(m.num_logits, 1),), 42, dtype=torch.int32)
+        s.update(sampled, m.num_real_logits)
+        if m.num_preempted:
+            return [i for i in ids if s.num_preemptions(i) > 0]
+    return []
+
+
+def test_victim_policies(rt):
+    # 9 blocks of 16 tokens, 4 sequences growing into their 3rd block: one preemption frees enough
+    s, arena, ids = _policy_sched(rt, "newest", blocks=9)
+    assert _victim(rt, s, arena, ids) == [ids[3]]
+    s, arena, ids = _policy_sched(rt, "priority", priorities=(5, 1, 9, 5), blocks=9)
+    assert _victim(rt, s, arena, ids) == [ids[1]]  # the lowest priority, even when it is the one asking
+    s, arena, ids = _policy_sched(rt, "kv_cost", lens=(20, 18, 17, 24), blocks=9)
+    assert _victim(rt, s, arena, ids) == [ids[2]]
+    s, arena, ids = _policy_sched(rt, "largest_first", lens=(20, 18, 17, 24), blocks=9)
+    assert _victim(rt, s, arena, ids) == [ids[3]]
+
+
+def test_aegaeon_score_prefers_young_large_sessions(rt):
+    """score = age x value / KV tokens: the youngest session holding the most KV goes first."""
+    s, arena, ids = _policy_sched(rt, "aegaeon", lens=(17, 17, 17, 30), blocks=9)
+    s.set_clock_ms(10_000.0)
+    assert _victim(rt, s, arena, ids) == [ids[3]]
+
+
+def test_preemption_cap_spares_capped_requests(rt):
+    """With a cap of 1, a sequence preempted once is only chosen again when no
+    other running sequence is left."""
+    s, arena, ids = _policy_sched(rt, "newest", cap=1, blocks=9)
+    first = _victim(rt, s, arena, ids)
+    assert first == [ids[3]]
+    for _ in range(200):
+        if not s.has_unfinished():
+            break
+        m = s.schedule()
+        sampled = torch.full((max(m.num_logits, 1),), 42, dtype=torch.int32)
+        s.update(sampled, m.num_real_logits)
+    counts = [s.num_preemptions(i) for i in ids]
+    assert all(c in (-1, 0, 1, 2) for c in counts)  # finished ids report -1
+
+
+def test_kv_admission_threshold_defers_new_requests(rt):
+    cfg = rt.SchedulerConfig()
+    cfg.max_num_seqs = 8
+    cfg.max_num_batched_tokens = 256
+    cfg.max_model_len = 512
+    cfg.kv_admission_threshold = 0.5
+    s = rt.Scheduler(cfg, 8, 16, False)
+    worst = rt.arena_layout(256, 8, 8, 256 // 64 + 8, 256 + 8, 32)
+    arena = torch.zeros(worst.used_words, dtype=torch.int32)
+    s.set_arena(arena, 256, 8, 32)
+    a = s.add_request([3] * 70, params(rt, max_tokens=4), 0)  # 5 of 8 blocks
+    m = s.schedule()
+    s.update(torch.full((max(m.num_logits, 1),), 42, dtype=torch.int32), m.num_real_logits)
+    assert s.kv_utilization() >= 0.5
+    b = s.add_request([4] * 5, params(rt, max_tokens=4), 0)
+    m = s.schedule()
+    assert m.num_prefill == 0 and s.num_waiting == 1 and s.admissions_deferred >= 1
+    s.update(torch.full((max(m.num_logits, 1),), 42, dtype=torch.int32), m.num_real_logits)
+    for _ in range(10):  # a finishes, its blocks free, b is admitted
+        if not s.has_unfinished():
+            break
+        m = s.schedule()
+        s.update(torch.full((max(m.num_logits, 1),), 42, dtype=torch.int32), m.num_real_logits)
+    assert not s.has_unfinished()
+
+
+def test_priority_preemption_after_wait_threshold(rt):
+    cfg = rt.SchedulerConfig()
+    cfg.max_num_seqs = 4
+    cfg.max_num_batched_tokens = 256
+    cfg.max_model_len = 512
+    cfg.priority_preempt_ms = 500.0
+    s = rt.Scheduler(cfg, 6, 16, False)
+    worst = rt.arena_layout(256, 4, 4, 256 // 64 + 4, 256 + 4, 32)
+    arena = torch.zeros(worst.used_words, dtype=torch.int32)
+    s.set_arena(arena, 256, 4, 32)
+    s.set_clock_ms(0.0)
+    low = s.add_request([3] * 90, params(rt, max_tokens=50, ignore_eos=True), 0)  # 6 blocks: the whole pool
+    m = s.schedule()
+    s.update(torch.full((max(m.num_logits, 1),), 42, dtype=torch.int32), m.num_real_logits)
+    high = s.add_request([4] * 20, params(rt, max_tokens=2, ignore_eos=True), 9)
+    s.set_clock_ms(100.0)  # waited 100 ms < 500 ms: no preemption yet
+    m = s.schedule()
+    assert m.num_preempted == 0 and s.num_waiting == 1
+    s.update(torch.full((max(m.num_logits, 1),), 42, dtype=torch.int32), m.num_real_logits)
+    s.set_clock_ms(700.0)
+    m = s.schedule()
+    assert m.num_preempted == 1 and s.priority_preemptions == 1
+    assert m.num_prefill == 1  # the high-priority request was admitted in the same step
+    assert s.num_preemptions(low) == 1 and s.num_waiting == 1
+
+
+# ---------------------------------------------------------------- swap preemption, state export / import
+def _sched(rt, blocks, swap_slots=0, max_seqs=4):
+    cfg = rt.SchedulerConfig()
+    cfg.max_num_seqs = max_seqs
+    cfg.max_num_batched_tokens = 256
+    cfg.max_model_len = 512
+    cfg.eos_token_ids = [2]
+    cfg.swap_slots = swap_slots
+    s = rt.Scheduler(cfg, blocks, 16, False)
+    worst = rt.arena_layout(256, max_seqs, max_seqs, 256 // 64 + max_seqs, 256 + max_seqs, 32)
+    arena = torch.zeros(worst.used_words, dtype=torch.int32)
+    s.set_arena(arena, 256, max_seqs, 32)
+    return s, arena
+
+
+def _step(s, tok=42):
+    m = s.schedule()
+    ev = s.update(torch.full((max(m.num_logits, 1),), tok, dtype=torch.int32), m.num_real_logits)
+    return m, ev
+
+
+def test_swap_preemption_keeps_progress(rt):
+    """Swapped-out victims keep their computed tokens: every slot swapped in
+    was swapped out before, no prompt token is ever prefilled twice (the
+    resumed sequences continue with decode rows), and all slots come back."""
+    s, arena = _sched(rt, blocks=9, swap_slots=16)
+    ids = [s.add_request([3 + i] * 16, params(rt, max_tokens=40, ignore_eos=True), 0) for i in range(4)]
+    held = set()
+    prefill_tokens = 0
+    swapped_in = 0
+    for _ in range(400):
+        if not s.has_unfinished():
+            break
+        m, _ = _step(s)
+        prefill_tokens += m.num_tokens - m.num_decode
+        for _, slot in s.take_swap_ins():
+            assert slot in held
+            held.discard(slot)
+            swapped_in += 1
+        for _, slot in s.take_swap_outs():
+            assert slot not in held
+            held.add(slot)
+    assert not s.has_unfinished()
+    assert s.total_swap_outs >= 1 and swapped_in >= 2
+    assert prefill_tokens == 4 * 16  # nothing recomputed
+    assert not held and s.free_swap_slots == 16
+
+
+def test_swap_falls_back_to_recompute_without_slots(rt):
+    s, arena = _sched(rt, blocks=9, swap_slots=1)  # a victim needs 2 slots
+    ids = [s.add_request([3 + i] * 16, params(rt, max_tokens=40, ignore_eos=True), 0) for i in range(4)]
+    for _ in range(40):
+        _step(s)
+        if s.total_preemptions:
+            break
+    assert s.total_preemptions == 1 and s.total_swap_outs == 0 and not s.take_swap_outs()
+
+
+def test_export_import_sequence(rt):
+    s, arena = _sched(rt, blocks=16)
+    a = s.add_request(list(range(3, 40)), params(rt, max_tokens=10, ignore_eos=True), 3)
+    for _ in range(3):
+        _step(s, 77)
+    st = s.export_sequence(a)
+    assert st["tokens"][-2:] == [77, 77] and st["num_prompt"] == 37 and st["priority"] == 3
+    assert st["num_computed"] == len(st["tokens"]) - 1 and len(st["blocks"]) == (st["num_computed"] + 15) // 16
+    free0 = s.kv_metrics()["free_blocks"]
+    b, table = s.import_sequence(st["tokens"], st["num_prompt"], st["num_computed"], st["params"], 3)
+    assert len(table) == len(st["blocks"]) and not set(table) & set(st["blocks"])
+    assert s.kv_metrics()["free_blocks"] == free0 - len(table)
+    m, ev = _step(s, 5)
+    # the imported sequence needs only its last token computed: a decode row
+    assert m.num_prefill == 0 and m.num_decode >= 2
+    assert [e[1] for e in ev if e[0] == b] == [5]
+    with pytest.raises(Exception):
+        s.export_sequence(12345)
+    with pytest.raises(Exception):
+        s.import_sequence([1] * 600, 1, 10, st["params"], 0)

@@ -238,3 +238,110 @@ def test_token_rate_limit(monkeypatch):
         r = c.post("/v1/completions", json={"prompt": "b", "max_tokens": 90})
         assert r.status_code == 429 and int(r.headers["retry-after"]) >= 1
         assert app.state.rate_limiter.throttled == 1
+
+
+# ---------------------------------------------------------------- function tools
+class ScriptedPipeline(EchoPipeline):
+    """Streams a fixed text regardless of the prompt (the model's 'answer')."""
+
+    answer = ""
+
+    def run_stream(self, messages, params, raw: bool = False, stop=None, prompt_ids=None):
+        self.last_prompt = messages
+        self.last_params = params
+        words = self.answer.split(" ")
+        self.last_generated_tokens = len(words)
+        for i, w in enumerate(words):
+            yield w if i == 0 else " " + w
+
+
+TOOLS = [{"type": "function", "function": {
+    "name": "get_weather", "description": "Get weather.",
+    "parameters": {"type": "object", "properties": {"city": {"type": "string"}}, "required": ["city"],
+                   "additionalProperties": False}}}]
+
+
+@pytest.fixture()
+def scripted():
+    pipe = ScriptedPipeline()
+    app = create_app(pipe, ServerSettings(model_id="echo", max_concurrent=4))
+    with TestClient(app) as c:
+        yield c, pipe
+
+
+def test_chat_tool_calls_non_stream_and_stream(scripted):
+    c, pipe = scripted
+    pipe.answer = '{"type": "function_calls", "calls": [{"name": "get_weather", "arguments": {"city": "Oslo"}}]}'
+    body = {"model": "echo", "messages": [{"role": "user", "content": "weather in Oslo?"}], "tools": TOOLS,
+            "max_tokens": 64}
+    r = c.post("/v1/chat/completions", json=body)
+    assert r.status_code == 200, r.text
+    ch = r.json()["choices"][0]
+    assert ch["finish_reason"] == "tool_calls" and ch["message"]["content"] is None
+    call = ch["message"]["tool_calls"][0]
+    assert call["type"] == "function" and call["function"]["name"] == "get_weather"
+    assert json.loads(call["function"]["arguments"]) == {"city": "Oslo"}
+    assert call["id"].startswith("call_")
+    # the request ran constrained to the envelope, with the protocol in the prompt
+    assert pipe.last_params.json_schema["properties"]["type"]["enum"] == ["message", "function_calls"]
+    assert "get_weather" in pipe.last_prompt[-1]["content"]
+    r = c.post("/v1/chat/completions", json=dict(body, stream=True))
+    events = [json.loads(l[6:]) for l in r.text.splitlines() if l.startswith("data: {")]
+    last = events[-1]["choices"][0]
+    assert last["finish_reason"] == "tool_calls" and last["delta"]["tool_calls"][0]["index"] == 0
+    assert r.text.rstrip().endswith("data: [DONE]")
+    # a plain message through the same protocol
+    pipe.answer = '{"type": "message", "content": "It is sunny."}'
+    ch = c.post("/v1/chat/completions", json=body).json()["choices"][0]
+    assert ch["finish_reason"] == "stop" and ch["message"]["content"] == "It is sunny."
+
+
+def test_chat_tool_protocol_errors(scripted):
+    c, pipe = scripted
+    base = {"model": "echo", "messages": [{"role": "user", "content": "x"}]}
+    r = c.post("/v1/chat/completions", json=dict(base, tools=[{"type": "function", "function": {"name": "a b"}}]))
+    assert r.status_code == 400 and "ASCII" in r.json()["error"]["message"]
+    r = c.post("/v1/chat/completions", json=dict(base, tool_choice="required"))
+    assert r.status_code == 400
+    pipe.answer = '{"type": "message", "content": "no"}'
+    r = c.post("/v1/chat/completions", json=dict(base, tools=TOOLS, tool_choice="required"))
+    assert r.status_code == 502 and "protocol" in r.json()["error"]["message"]
+    # history: a tool call must be answered before the conversation continues
+    call = {"id": "call_1", "type": "function", "function": {"name": "get_weather", "arguments": '{"city":"Oslo"}'}}
+    msgs = [{"role": "user", "content": "w?"}, {"role": "assistant", "content": None, "tool_calls": [call]},
+            {"role": "user", "content": "and?"}]
+    r = c.post("/v1/chat/completions", json=dict(base, messages=msgs, tools=TOOLS))
+    assert r.status_code == 400
+    msgs[2] = {"role": "tool", "tool_call_id": "call_1", "content": "sunny, 21 C"}
+    pipe.answer = '{"type": "message", "content": "Sunny."}'
+    r = c.post("/v1/chat/completions", json=dict(base, messages=msgs, tools=TOOLS))
+    assert r.status_code == 200 and r.json()["choices"][0]["message"]["content"] == "Sunny."
+    assert any("untrusted" in m["content"] for m in pipe.last_prompt)
+
+
+def test_response_format_schema_validation(scripted):
+    c, pipe = scripted
+    base = {"model": "echo", "messages": [{"role": "user", "content": "x"}]}
+    bad = {"type": "json_schema", "json_schema": {"name": "s", "schema": {"type": "object", "properties": {
+        "a": {"type": "string", "pattern": "x"}}}}}
+    r = c.post("/v1/chat/completions", json=dict(base, response_format=bad))
+    assert r.status_code == 400 and "pattern" in r.json()["error"]["message"]
+    good = {"type": "json_schema", "json_schema": {"name": "s", "schema": {"type": "object", "properties": {
+        "a": {"type": "string"}}, "required": ["a"]}}}
+    pipe.answer = '{"a": "b"}'
+    r = c.post("/v1/chat/completions", json=dict(base, response_format=good))
+    assert r.status_code == 200 and json.loads(r.json()["choices"][0]["message"]["content"]) == {"a": "b"}
+    assert pipe.last_params.json_schema == good["json_schema"]["schema"]
+
+
+def test_responses_api_function_call(scripted):
+    c, pipe = scripted
+    pipe.answer = '{"type": "function_calls", "calls": [{"name": "get_weather", "arguments": {"city": "Rome"}}]}'
+    flat = [dict(TOOLS[0]["function"], type="function")]
+    r = c.post("/v1/responses", json={"model": "echo", "input": "weather?", "tools": flat})
+    assert r.status_code == 200, r.text
+    d = r.json()
+    item = d["output"][0]
+    assert item["type"] == "function_call" and item["name"] == "get_weather"
+    assert json.loads(item["arguments"]) == {"city": "Rome"} and item["call_id"].startswith("call_")
+    assert d["tools"][0]["name"] == "get_weather" and d["tool_choice"] == "auto"
