@@ -263,6 +263,14 @@ class LLMEngine:
 
     def step(self) -> List[RequestOutput]:
         """One engine step; returns the requests that received a token."""
+        from ..utils.tracing import enabled, span
+
+        if enabled():
+            with span("engine.step", running=self.scheduler.num_running, waiting=self.scheduler.num_waiting):
+                return self._step()
+        return self._step()
+
+    def _step(self) -> List[RequestOutput]:
         t0 = time.perf_counter()
         if self.speculator is not None:
             self.speculator.propose(self)

@@ -251,7 +251,10 @@ class InferencePipeline:
             yield tail
 
     def run(self, messages, params, raw: bool = False, stop=None) -> str:
-        return "".join(self.run_stream(messages, params, raw, stop))
+        from ..utils.tracing import span
+
+        with span("pipeline.run", engine=self.engine_name):
+            return "".join(self.run_stream(messages, params, raw, stop))
 
     def run_embedding_batch(self, texts: List[str]) -> List[List[float]]:
         if self.embedder is None:

@@ -55,6 +55,13 @@ def load_weights(man: ModelManifest, device=None) -> dict:
 
 
 def load_decoder(path: str, tp=None, device=None):
+    from ..utils.tracing import span
+
+    with span("model.load", path=str(path)):
+        return _load_decoder(path, tp, device)
+
+
+def _load_decoder(path: str, tp=None, device=None):
     from ..models.llama import DecoderLM
 
     man = load_manifest(path)

@@ -381,17 +381,37 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                 "ram_utilization": _ram_utilization()}
         return JSONResponse(snap, status_code=200 if ok else 503)
 
+    def _sched_gauges() -> dict:
+        eng = getattr(pipeline, "llm", None)
+        sch = getattr(eng, "scheduler", None)
+        if sch is None:
+            return {}
+        return {"waiting_requests": sch.num_waiting, "running_requests": sch.num_running,
+                "preemptions_total": sch.total_preemptions, "admissions_deferred_total": sch.admissions_deferred,
+                "failed_steps_total": len(getattr(eng, "failures", []))}
+
+    def _memory():
+        from ..utils.telemetry import MemoryTelemetry
+
+        dev = getattr(getattr(pipeline, "llm", None), "model", None)
+        idx = [dev.device.index] if dev is not None and getattr(dev.device, "index", None) is not None else []
+        return MemoryTelemetry.snapshot(idx)
+
     @app.get("/metrics")
     async def prom():
         kv = _kv_stats(pipeline)
-        return PlainTextResponse(metrics.render(kv), media_type="text/plain; version=0.0.4")
+        return PlainTextResponse(metrics.render(kv, _sched_gauges(), _memory()),
+                                 media_type="text/plain; version=0.0.4")
 
     @app.get("/v1/observability")
     async def observability():
+        from ..utils import tracing
+
         return {"object": "bloom.observability", "schema_version": 1, "uptime_seconds": time.time() - started,
                 "model": st.model_id, "metrics": metrics.snapshot(), "kv_cache": _kv_stats(pipeline),
+                "scheduler": _sched_gauges(), "memory": _memory().to_dict(), "spans": tracing.stats(),
                 "runtime": {"in_flight_requests": rt.in_flight, "available_permits": rt.available_permits,
-                            "engine": getattr(pipeline, "engine_name", "unknown")}}
+                            "engine": getattr(pipeline, "engine_name", "unknown"), "broken": rt.broken}}
 
     @app.get("/v1/kv-cache-stats")
     async def kv_stats():

@@ -46,6 +46,7 @@ class Submission:
     engine_rid: Optional[int] = None
     cancelled: bool = False
     first_token_at: Optional[float] = None
+    last_token_at: Optional[float] = None
     n_tokens: int = 0
     messages: Any = None
 
@@ -225,6 +226,8 @@ class ServingRuntime:
                     subs = list(self._by_rid.values())
                 for sub in subs:
                     eng.abort(sub.engine_rid)
+                    if self.metrics is not None:
+                        self.metrics.observe_request(time.time() - sub.created, False, len(sub.prompt_ids))
                     self._emit(sub, StreamItem(finished=True, reason="error", error=f"engine step failed: {e}"))
                     self._finish(sub)
                 continue
@@ -242,6 +245,12 @@ class ServingRuntime:
                     if self.metrics is not None:
                         self.metrics.observe_ttft(now - sub.created)
                 new = r.token_ids[sub.n_tokens:]
+                if new and self.metrics is not None and sub.last_token_at is not None:
+                    self.metrics.observe_itl((now - sub.last_token_at) / len(new))
+                if new:
+                    sub.last_token_at = now
+                if r.finished and self.metrics is not None:
+                    self.metrics.observe_request(now - sub.created, r.finish_reason != "error", len(sub.prompt_ids))
                 for j, tok in enumerate(new):
                     last = j == len(new) - 1
                     self._emit(sub, StreamItem(token=tok, finished=r.finished and last,

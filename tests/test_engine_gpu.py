@@ -308,3 +308,61 @@ def test_json_schema_constrained_decoding_random_weights(graphs, temperature):
     from bloom_b200 import ops
 
     assert int(ops.status()[0].item()) == 0
+
+
+def test_export_import_state_resumes_identically():
+    """Export a running request's KV + tokens, import it into a second engine
+    with the same weights: greedy decoding continues with exactly the tokens
+    the first engine produces, without recomputing the prefix."""
+    from bloom_b200.engine.engine import SamplingParams
+
+    cfg, w, a = _build("tiny-llama", graphs=False)
+    _, _, b = _build("tiny-llama", graphs=False)
+    sp = SamplingParams(max_tokens=16, temperature=0.0, ignore_eos=True)
+    prompt = list(range(5, 45))
+    rid = a.add_request(prompt, sp)
+    for _ in range(6):
+        a.step()
+    blob = a.export_state(rid)
+    got_before = list(a.requests[rid].token_ids)
+    while a.has_unfinished():
+        a.step()
+    full_a = a.requests[rid].token_ids
+    rid_b = b.import_state(blob)
+    tokens_before = b.runner.stats["tokens"]
+    while b.has_unfinished():
+        b.step()
+    full_b = b.requests[rid_b].token_ids
+    assert full_b == full_a, (full_a, full_b)
+    assert full_b[:len(got_before)] == got_before
+    # only the last token of the imported state was recomputed, then one row per new token
+    assert b.runner.stats["tokens"] - tokens_before == 16 - len(got_before)
+    _check_greedy(cfg, w, prompt, full_a)
+    bad = blob[:12] + blob[12:].replace(b'"head_dim":128', b'"head_dim":64', 1)
+    with pytest.raises(ValueError):
+        b.import_state(bad)
+
+
+def test_swap_preemption_matches_reference():
+    """A KV pool too small for every request forces preemption; with swap
+    space the victims' blocks go to host memory and come back, and greedy
+    outputs still match the fp32 oracle."""
+    from bloom_b200.engine.engine import EngineConfig, LLMEngine, SamplingParams
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.llama import DecoderLM
+    from bloom_b200.models.reference import random_weights
+
+    cfg = preset("tiny-llama")
+    w = random_weights(cfg, seed=3, std=0.08, device="cuda")
+    model = DecoderLM(cfg, device="cuda")
+    model.shard_full(w)
+    eng = LLMEngine(model, EngineConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=512, num_blocks=24,
+                                        use_cuda_graphs=True, enable_prefix_caching=False,
+                                        swap_space_bytes=64 * 2 * 2 * 2 * 16 * 128 * 2 * 2))
+    torch.manual_seed(1)
+    prompts = [torch.randint(3, cfg.vocab_size, (40,)).tolist() for _ in range(6)]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=40, temperature=0.0, ignore_eos=True))
+    assert eng.scheduler.total_swap_outs > 0 and eng.runner.stats.get("swap_ins", 0) > 0
+    for p, o in zip(prompts, outs):
+        assert len(o.token_ids) == 40
+        _check_greedy(cfg, w, p, o.token_ids)

@@ -345,3 +345,42 @@ def test_responses_api_function_call(scripted):
     assert item["type"] == "function_call" and item["name"] == "get_weather"
     assert json.loads(item["arguments"]) == {"city": "Rome"} and item["call_id"].startswith("call_")
     assert d["tools"][0]["name"] == "get_weather" and d["tool_choice"] == "auto"
+
+
+def test_metrics_latency_memory_and_spans(client):
+    for _ in range(2):
+        client.post("/v1/chat/completions", json={"model": "echo", "messages": [{"role": "user", "content": "a b c"}]})
+    text = client.get("/metrics").text
+    for name in ("bloom_inter_token_latency_seconds_count", "bloom_request_latency_seconds", "bloom_uptime_seconds",
+                 "bloom_process_resident_memory_bytes", "bloom_system_memory_total_bytes",
+                 "bloom_memory_pressure_high", "bloom_requests_completed_total"):
+        assert name in text, name
+    obs = client.get("/v1/observability").json()
+    assert obs["memory"]["rss_bytes"] > 0 and obs["memory"]["total_ram_bytes"] > 0
+    assert "spans" in obs and obs["metrics"]["uptime_seconds"] >= 0
+
+
+def test_tracing_spans_and_chrome_trace(tmp_path, monkeypatch):
+    from bloom_b200.utils import tracing
+
+    monkeypatch.setattr(tracing, "_TRACE_PATH", str(tmp_path / "t.json"))
+    with tracing.span("unit.outer", k=1):
+        with tracing.span("unit.inner"):
+            pass
+    st = tracing.stats()
+    assert st["unit.outer"]["count"] >= 1 and st["unit.inner"]["seconds"] >= 0
+    path = tracing.flush()
+    ev = json.load(open(path))["traceEvents"]
+    names = [e["name"] for e in ev]
+    assert "unit.outer" in names and "unit.inner" in names
+    outer = [e for e in ev if e["name"] == "unit.outer"][-1]
+    assert outer["ph"] == "X" and outer["args"] == {"k": 1}
+
+
+def test_memory_telemetry_snapshot():
+    from bloom_b200.utils.telemetry import MemoryTelemetry
+
+    s = MemoryTelemetry.snapshot([])
+    assert s.rss_bytes > 0 and s.peak_rss_bytes >= s.rss_bytes and s.total_ram_bytes > s.rss_bytes
+    assert 0.0 <= s.ram_utilization <= 1.0 and "RAM rss" in s.summary()
+    assert s.to_dict()["high_pressure"] in (True, False)
