@@ -29,6 +29,12 @@ def build_parser():
     ap.add_argument("--draft-model")
     ap.add_argument("--num-speculative-tokens", type=int, default=5)
     ap.add_argument("--model-id")
+    ap.add_argument("--max-resident-models", type=int, default=int(os.environ.get("BLOOM_MAX_RESIDENT_MODELS", "1")),
+                    help="models kept loaded at once (requests select one with their `model` field)")
+    ap.add_argument("--memory-host-limit", type=int, default=0,
+                    help="host bytes all resident models may hold (0 = physical RAM)")
+    ap.add_argument("--memory-device-limit", type=int, default=0,
+                    help="device bytes all resident models may hold (0 = every GPU's memory)")
     ap.add_argument("--doctor", action="store_true")
     ap.add_argument("--doctor-format", choices=["text", "json"], default="text")
     ap.add_argument("--models-dir", default=os.environ.get("BLOOM_MODELS_DIR"),
@@ -92,7 +98,8 @@ def main(argv=None) -> int:
     mid = args.model_id or os.path.basename(str(args.model).rstrip("/"))
     settings = ServerSettings(model_id=mid, api_keys=keys, context_size=pipe.context_size,
                               max_concurrent=args.max_concurrent, cors_origins=args.cors_origin,
-                              models_dir=args.models_dir)
+                              models_dir=args.models_dir, pool_capacity=args.max_resident_models,
+                              memory_host_limit=args.memory_host_limit, memory_device_limit=args.memory_device_limit)
     runtime = ServingRuntime(pipe, mid, args.max_concurrent, ctrl=ctrl) if ctrl is not None else None
     app = create_app(pipe, settings, runtime)
     if ctrl is None:  # model switching re-loads on this process's device (not offered under tensor parallel)

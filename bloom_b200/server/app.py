@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import asyncio
 import base64
+import contextvars
 import json
 import os
 import re
@@ -91,30 +92,57 @@ class ResponseStore:
         return v
 
 
-class _Ref:
-    """Attribute proxy to a swappable object (the served pipeline / runtime)."""
+# The runtime-pool entry a request selected with its `model` field (set by
+# check_model inside the request's own task; None = the default model).
+_SELECTED: "contextvars.ContextVar" = contextvars.ContextVar("bloom_selected_runtime", default=None)
 
-    def __init__(self, obj):
+
+def _device_count() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count() if torch.cuda.is_available() else 0
+    except Exception:  # pragma: no cover
+        return 0
+
+
+class _Ref:
+    """Attribute proxy to the served pipeline / runtime: the entry this
+    request selected from the runtime pool, else the swappable default."""
+
+    def __init__(self, obj, attr: str):
         object.__setattr__(self, "_obj", obj)
+        object.__setattr__(self, "_attr", attr)
+
+    def _target(self):
+        e = _SELECTED.get()
+        if e is not None:
+            return getattr(e, object.__getattribute__(self, "_attr"))
+        return object.__getattribute__(self, "_obj")
 
     def __getattr__(self, k):
-        return getattr(object.__getattribute__(self, "_obj"), k)
+        return getattr(self._target(), k)
 
     def __setattr__(self, k, v):
-        setattr(object.__getattribute__(self, "_obj"), k, v)
+        setattr(self._target(), k, v)
 
     def swap(self, obj) -> None:
         object.__setattr__(self, "_obj", obj)
 
     def get(self):
-        return object.__getattribute__(self, "_obj")
+        return self._target()
 
 
 class ServerSettings:
     def __init__(self, model_id: str = "model", api_keys: Optional[List[str]] = None, context_size: int = 2048,
                  max_concurrent: int = 4, allow_non_loopback: bool = False, cors_origins: Optional[List[str]] = None,
-                 models_dir: Optional[str] = None):
+                 models_dir: Optional[str] = None, pool_capacity: int = 1, memory_host_limit: int = 0,
+                 memory_device_limit: int = 0):
         self.model_id = model_id
+        self.pool_capacity = int(pool_capacity)
+        # aggregate byte budgets over every resident model (0 = physical RAM / device memory)
+        self.memory_host_limit = int(memory_host_limit)
+        self.memory_device_limit = int(memory_device_limit)
         self.api_keys = list(api_keys or [])
         self.context_size = context_size
         self.max_concurrent = max_concurrent
@@ -126,6 +154,26 @@ class ServerSettings:
         self.rate_limit_burst = float(os.environ.get("BLOOM_RATE_LIMIT_BURST", "32768"))
         self.rate_limit_rate = float(os.environ.get("BLOOM_RATE_LIMIT_RATE", "200"))
 
+    @property
+    def model_id(self) -> str:
+        e = _SELECTED.get()
+        return e.key if e is not None else self._model_id
+
+    @model_id.setter
+    def model_id(self, v: str) -> None:
+        self._model_id = v
+
+    @property
+    def context_size(self) -> int:
+        e = _SELECTED.get()
+        if e is not None:
+            return int(getattr(e.pipeline, "context_size", self._context_size))
+        return self._context_size
+
+    @context_size.setter
+    def context_size(self, v: int) -> None:
+        self._context_size = int(v)
+
 
 def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Optional[ServingRuntime] = None) -> FastAPI:
     st = settings or ServerSettings()
@@ -135,9 +183,19 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
     from .._ext import runtime as _native
 
     limiter = _native().RateLimiter(st.rate_limit, st.rate_limit_burst, st.rate_limit_rate)
-    # model management swaps the served pipeline / runtime behind these handles
-    pipeline = _Ref(pipeline)
-    rt = _Ref(rt)
+    # model management swaps the served pipeline / runtime behind these handles;
+    # other resident models are selected per request through the runtime pool
+    from .runtime_pool import (Footprint, KeepAliveError, MemoryBudget, MemoryError_, RuntimeEntry, RuntimePool,
+                               parse_keep_alive)
+    from ..utils.telemetry import MemoryTelemetry
+
+    _mem = MemoryTelemetry.snapshot()
+    budget = MemoryBudget(st.memory_host_limit or max(1, _mem.total_ram_bytes),
+                          st.memory_device_limit or max(1, sum(d.total_bytes for d in _mem.devices) or 1 << 60))
+    pool = RuntimePool(max(1, st.pool_capacity))
+    pool.publish(RuntimeEntry(st.model_id, "", pipeline, rt), make_default=True)
+    pipeline = _Ref(pipeline, "pipeline")
+    rt = _Ref(rt, "runtime")
     store = ResponseStore()
     app = FastAPI(title="bloom_b200", version=SERVER_VERSION, docs_url=None, redoc_url=None, openapi_url=None)
     app.state.runtime = rt
@@ -215,8 +273,14 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
 
     # ------------------------------------------------------------ helpers
     def check_model(name: Optional[str]) -> None:
-        if name not in (None, "", st.model_id) and not st.model_id.endswith(str(name)):
+        """Select the resident model a request names (404 when none is)."""
+        if name in (None, "") or name == st._model_id or st._model_id.endswith(str(name)):
+            return
+        e = pool.select(str(name))
+        if e is None or e.key == pool.default_key:
             raise APIError(404, f"model {name!r} is not loaded", "not_found_error", "model", "model_not_found")
+        _SELECTED.set(e)
+        pool.touch(e.key)
 
     def sampling(d: dict, default_max: int = 128):
         from ..engine.engine import SamplingParams
@@ -819,23 +883,129 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
             raise APIError(409, "requests are in flight; retry when idle", "conflict")
         import asyncio
 
-        new_pipe = await asyncio.get_running_loop().run_in_executor(None, loader, e["path"])
-        old = rt.get()
-        st.model_id = str(e["id"])
-        st.context_size = int(getattr(new_pipe, "context_size", st.context_size))
-        new_rt = ServingRuntime(new_pipe, st.model_id, st.max_concurrent, metrics)
-        pipeline.swap(new_pipe)
-        rt.swap(new_rt)
+        entry = await load_entry(e, make_default=True)
+        st.model_id = entry.key
+        st.context_size = int(getattr(entry.pipeline, "context_size", st.context_size))
+        pipeline.swap(entry.pipeline)
+        rt.swap(entry.runtime)
         state["loaded"] = True
-        old.shutdown()
         return {"status": "switched", "model": st.model_id}
 
+    def footprint_of(e: dict) -> "Footprint":
+        """Memory the model will hold: the manifest estimate for the server's context and concurrency."""
+        try:
+            pf = catalog.preflight(str(e["id"]), st._context_size, st.max_concurrent)
+            total = int(pf.get("total_bytes", 0) or 0)
+        except Exception:  # noqa: BLE001 - an unestimable package is charged its file size
+            total = int(e.get("size_bytes", 0) or 0)
+        on_gpu = _device_count() > 0
+        return Footprint(host_bytes=0 if on_gpu else total, device_bytes=total if on_gpu else 0)
+
+    async def load_entry(e: dict, make_default: bool = False, keep_alive_s: Optional[float] = None) -> "RuntimeEntry":
+        """Load a catalog entry under a memory permit and publish it in the pool
+        (idle least-recently-used residents are evicted to make room)."""
+        loader = getattr(app.state, "model_loader", None)
+        if loader is None:
+            raise APIError(501, "this server was started without a model loader", "server_error")
+        key = str(e["id"])
+        fp = footprint_of(e)
+        old = pool.get(key)
+        if old is not None and old.permit is not None:
+            old.permit.release()  # a reload replaces the old generation's charge
+            old.permit = None
+        for v in pool.evict_for(budget, fp, protect=key):
+            metrics_evictions[0] += 1
+        try:
+            permit = budget.reserve(fp)
+        except MemoryError_ as ex:
+            raise APIError(507, f"model {key!r} does not fit the memory budget: {ex}", "server_error") from None
+        try:
+            new_pipe = await asyncio.get_running_loop().run_in_executor(None, loader, e["path"])
+        except Exception:
+            permit.release()
+            raise
+        entry = RuntimeEntry(key, str(e["path"]), new_pipe, ServingRuntime(new_pipe, key, st.max_concurrent, metrics),
+                             permit)
+        if keep_alive_s is not None:
+            entry.keep_alive_s = keep_alive_s
+        for r in pool.publish(entry, make_default=make_default):
+            if r is not entry:
+                r.retire()
+        pool.touch(key)
+        return entry
+
+    metrics_evictions = [0]
+
+    @app.post("/v1/model-management/load")
+    async def mm_load(request: Request):
+        """Make another catalog model resident next to the default one; requests
+        select it with their `model` field."""
+        require_catalog()
+        d = await body(request)
+        e = catalog.find(str(d.get("model", "")))
+        if e is None or not e.get("valid"):
+            raise APIError(404, f"model {d.get('model')!r} is not a loadable catalog entry", "not_found_error",
+                           "model", "model_not_found")
+        try:
+            ka = parse_keep_alive(d["keep_alive"]) if d.get("keep_alive") is not None else None
+        except KeepAliveError as ex:
+            raise APIError(400, str(ex), param="keep_alive") from None
+        entry = await load_entry(e, keep_alive_s=ka)
+        return {"status": "loaded", "model": entry.key, "resident": [x.key for x in pool.entries()]}
+
+    @app.get("/v1/model-management/residency")
+    async def mm_residency():
+        return {"object": "bloom.residency", "capacity": pool.capacity, "default": pool.default_key,
+                "memory_budget": budget.snapshot(), "evictions": metrics_evictions[0],
+                "models": [{"model": x.key, "default": x.key == pool.default_key, "source": x.source,
+                            "keep_alive_seconds": x.keep_alive_s,
+                            "expires_at": _iso(x.expires_at) if x.expires_at else None,
+                            "host_bytes": x.permit.footprint.host_bytes if x.permit else 0,
+                            "device_bytes": x.permit.footprint.device_bytes if x.permit else 0,
+                            "in_flight": getattr(x.runtime, "in_flight", 0)} for x in pool.entries()]}
+
     @app.post("/v1/model-management/unload")
-    async def mm_unload():
+    async def mm_unload(request: Request):
+        d = await body(request) if (await request.body()) else {}
+        key = d.get("model")
+        if key and key != st._model_id:
+            e = pool.get(str(key))
+            if e is None:
+                raise APIError(404, f"model {key!r} is not resident", "not_found_error", "model", "model_not_found")
+            if getattr(e.runtime, "in_flight", 0):
+                raise APIError(409, "requests are in flight; retry when idle", "conflict")
+            pool.remove(e.key)
+            e.retire()
+            return {"status": "unloaded", "model": e.key}
         if rt.in_flight:
             raise APIError(409, "requests are in flight; retry when idle", "conflict")
         state["loaded"] = False
         return {"status": "unloaded", "model": st.model_id}
+
+    async def expire_residents():
+        """Keep-alive deadlines: unload residents whose deadline passed."""
+        while True:
+            await asyncio.sleep(0.25)
+            for key in pool.expired():
+                if key == pool.default_key:
+                    e = pool.get(key)
+                    if e is not None:
+                        e.expires_at = None
+                    state["loaded"] = False
+                    continue
+                e = pool.remove(key)
+                if e is not None:
+                    e.retire()
+
+    @app.on_event("startup")
+    async def _start_expiry():
+        app.state.expiry_task = asyncio.get_running_loop().create_task(expire_residents())
+
+    @app.on_event("shutdown")
+    async def _stop_expiry():
+        t = getattr(app.state, "expiry_task", None)
+        if t is not None:
+            t.cancel()
 
     @app.delete("/v1/model-management/models/{model_id}")
     async def mm_remove(model_id: str, confirm: bool = False):
@@ -887,7 +1057,18 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
 
     @app.get("/api/ps")
     async def o_ps():
-        return {"models": [dict(o_model(), expires_at=_iso(time.time() + 300), size_vram=0)]}
+        out = []
+        for x in pool.entries():
+            if x.key == pool.default_key and not state["loaded"]:
+                continue
+            exp = x.expires_at if x.expires_at is not None else (
+                time.time() + 365 * 24 * 3600 if x.keep_alive_s < 0 else time.time() + x.keep_alive_s)
+            out.append({"name": x.key, "model": x.key, "size": (x.permit.footprint.host_bytes +
+                                                                x.permit.footprint.device_bytes) if x.permit else 0,
+                        "digest": uuid.uuid5(uuid.NAMESPACE_URL, x.key).hex, "expires_at": _iso(exp),
+                        "size_vram": x.permit.footprint.device_bytes if x.permit else 0,
+                        "details": {"format": "bloom", "family": getattr(x.pipeline.cfg, "arch", "")}})
+        return {"models": out}
 
     @app.post("/api/show")
     async def o_show(request: Request):
@@ -949,17 +1130,67 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         res = piece("".join(text), True, reason, n)
         return res
 
+    async def o_resident(d: dict):
+        """Ollama residency: the named model is made resident on demand (from
+        the catalog), its keep_alive deadline is re-armed after the request,
+        and an empty request with keep_alive only loads / unloads.  Returns
+        (keep_alive seconds, lifecycle response or None)."""
+        try:
+            ka = parse_keep_alive(d.get("keep_alive"))
+        except KeepAliveError as ex:
+            raise APIError(400, str(ex), param="keep_alive") from None
+        name = d.get("model") or d.get("name")
+        if name and pool.select(str(name)) is None and not (name == st._model_id or st._model_id.endswith(str(name))):
+            e = catalog.find(str(name)) if catalog.root else None
+            if e is None or not e.get("valid"):
+                raise APIError(404, f"model '{name}' not found", "not_found_error")
+            await load_entry(e, keep_alive_s=ka)
+        check_model(name)
+        key = st.model_id
+        empty = not d.get("messages") and not d.get("prompt")
+        if empty:
+            if ka == 0:
+                e = pool.get(key)
+                if e is not None and key != pool.default_key:
+                    pool.remove(key)
+                    e.retire()
+                else:
+                    state["loaded"] = False
+                return ka, {"model": key, "created_at": _iso(time.time()), "done": True, "done_reason": "unload"}
+            if key == pool.default_key:
+                state["loaded"] = True
+            pool.touch(key, ka)
+            return ka, {"model": key, "created_at": _iso(time.time()), "done": True, "done_reason": "load"}
+        return ka, None
+
     @app.post("/api/chat")
     async def o_chat(request: Request):
         d = await body(request)
-        check_model(d.get("model"))
+        ka, life = await o_resident(d)
+        if life is not None:
+            if life["done_reason"] == "load":
+                life["message"] = {"role": "assistant", "content": ""}
+            return life
         msgs = messages_of({"messages": d.get("messages")})
-        return await o_generate_common(request, msgs, None, True, d)
+        try:
+            return await o_generate_common(request, msgs, None, True, d)
+        finally:
+            pool.touch(st.model_id, ka)
 
     @app.post("/api/generate")
     async def o_generate(request: Request):
         d = await body(request)
-        check_model(d.get("model"))
+        ka, life = await o_resident(d)
+        if life is not None:
+            if life["done_reason"] == "load":
+                life["response"] = ""
+            return life
+        try:
+            return await o_generate_inner(request, d)
+        finally:
+            pool.touch(st.model_id, ka)
+
+    async def o_generate_inner(request: Request, d: dict):
         p = d.get("prompt")
         if not isinstance(p, str):
             raise APIError(400, "prompt must be a string")

@@ -47,7 +47,10 @@ def main():
             worst = max(worst, gap / max(spread, 1e-6))
             if gap > 0.03 * spread + 1e-4:
                 ok = False
-    toks = torch.tensor([t for o in outs for t in o.token_ids], device=dev)
+    # stochastic rows: the full-vocabulary rows are gathered from the shards
+    # (fused: one P2P kernel) and sampled with the same Philox stream on every rank
+    souts = eng.generate(prompts, SamplingParams(max_tokens=6, temperature=0.8, top_p=0.9, seed=11, ignore_eos=True))
+    toks = torch.tensor([t for o in outs + souts for t in o.token_ids], device=dev)
     allt = [torch.empty_like(toks) for _ in range(world)]
     dist.all_gather(allt, toks)
     same = all(torch.equal(allt[0], t) for t in allt)
