@@ -193,6 +193,12 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
     budget = MemoryBudget(st.memory_host_limit or max(1, _mem.total_ram_bytes),
                           st.memory_device_limit or max(1, sum(d.total_bytes for d in _mem.devices) or 1 << 60))
     pool = RuntimePool(max(1, st.pool_capacity))
+    # per-device accounting (C++ ResourceLedger): device -1 is host memory
+    ledger = _native().ResourceLedger()
+    ledger.add_device(-1, max(1, _mem.total_ram_bytes))
+    for _d in _mem.devices:
+        ledger.add_device(_d.index, _d.total_bytes)
+    ledger_stamp = [0]
     pool.publish(RuntimeEntry(st.model_id, "", pipeline, rt), make_default=True)
     pipeline = _Ref(pipeline, "pipeline")
     rt = _Ref(rt, "runtime")
@@ -300,8 +306,28 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         mn = d.get("min_tokens", 0) or 0  # extension: no end-of-sequence before this many tokens
         if not isinstance(mn, int) or mn < 0:
             raise APIError(400, "min_tokens must be a non-negative integer", param="min_tokens")
-        return SamplingParams(max_tokens=mt, temperature=float(temp), top_p=float(top_p), seed=seed,
-                              top_k=int(d.get("top_k", 0) or 0), min_tokens=min(mn, mt))
+        sp = SamplingParams(max_tokens=mt, temperature=float(temp), top_p=float(top_p), seed=seed,
+                            top_k=int(d.get("top_k", 0) or 0), min_tokens=min(mn, mt))
+        sp.segment = segment_of(d)
+        return sp
+
+    def segment_of(d: dict) -> int:
+        """Request class for admission: OpenAI service_tier "flex" / "batch" ->
+        background; "realtime" or Bloom's "segment" field by name; otherwise
+        foreground interactive."""
+        from .runtime import SEGMENTS
+
+        seg = d.get("segment")
+        if isinstance(seg, str):
+            if seg not in SEGMENTS:
+                raise APIError(400, f"segment must be one of {', '.join(SEGMENTS)}", param="segment")
+            return SEGMENTS[seg]
+        tier = d.get("service_tier")
+        if tier in ("flex", "batch"):
+            return SEGMENTS["background"]
+        if tier == "realtime":
+            return SEGMENTS["realtime"]
+        return SEGMENTS["foreground"]
 
     def stops(d: dict) -> List[str]:
         s = d.get("stop")
@@ -391,7 +417,7 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
             params.max_tokens = min(params.max_tokens, st.context_size - len(ids) - 1)
             with_eos(params)
             sub = rt.submit(ids, params, messages=None if rt.engine is not None else (raw_prompt or msgs),
-                            request_id=request.state.request_id)
+                            request_id=request.state.request_id, segment=getattr(params, "segment", 0))
             detok = Detokenizer(pipeline.tokenizer)
             filt = StopSequenceFilter(stop_list)
             eos = set(pipeline.eos_ids()) if hasattr(pipeline, "eos_ids") else set()
@@ -919,13 +945,26 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
             permit = budget.reserve(fp)
         except MemoryError_ as ex:
             raise APIError(507, f"model {key!r} does not fit the memory budget: {ex}", "server_error") from None
+        dev = 0 if fp.device_bytes else -1
+        ledger_stamp[0] += 1
+        ok, evicted = ledger.reserve(key, dev, fp.device_bytes or fp.host_bytes, 2 if make_default else 1,
+                                     ledger_stamp[0])
+        if not ok:
+            permit.release()
+            raise APIError(507, f"model {key!r} does not fit device {dev}'s free memory", "server_error")
+        for owner in evicted:  # lower-priority residents the ledger displaced
+            v = pool.remove(owner)
+            if v is not None:
+                v.retire()
+                metrics_evictions[0] += 1
         try:
             new_pipe = await asyncio.get_running_loop().run_in_executor(None, loader, e["path"])
         except Exception:
             permit.release()
+            ledger.release(key)
             raise
         entry = RuntimeEntry(key, str(e["path"]), new_pipe, ServingRuntime(new_pipe, key, st.max_concurrent, metrics),
-                             permit)
+                             permit, on_retire=[ledger.release])
         if keep_alive_s is not None:
             entry.keep_alive_s = keep_alive_s
         for r in pool.publish(entry, make_default=make_default):
@@ -957,6 +996,8 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
     async def mm_residency():
         return {"object": "bloom.residency", "capacity": pool.capacity, "default": pool.default_key,
                 "memory_budget": budget.snapshot(), "evictions": metrics_evictions[0],
+                "ledger": {str(dv): {"used_bytes": ledger.used(dv), "free_bytes": ledger.free_bytes(dv)}
+                           for dv in [-1] + [d.index for d in _mem.devices]},
                 "models": [{"model": x.key, "default": x.key == pool.default_key, "source": x.source,
                             "keep_alive_seconds": x.keep_alive_s,
                             "expires_at": _iso(x.expires_at) if x.expires_at else None,

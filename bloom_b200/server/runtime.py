@@ -49,6 +49,7 @@ class Submission:
     last_token_at: Optional[float] = None
     n_tokens: int = 0
     messages: Any = None
+    segment: int = 0  # 0 foreground, 1 realtime stream, 2 background batch, 3 maintenance
 
 
 class TPControl:
@@ -81,8 +82,8 @@ def follower_loop(engine, ctrl: TPControl) -> None:
         msg = ctrl.exchange(None)
         if msg.get("stop"):
             return
-        for prompt, params in msg.get("add", []):
-            engine.add_request(prompt, params)
+        for prompt, params, prio in msg.get("add", []):
+            engine.add_request(prompt, params, prio)
         for rid in msg.get("abort", []):
             engine.abort(rid)
         if msg.get("step"):
@@ -91,8 +92,47 @@ def follower_loop(engine, ctrl: TPControl) -> None:
                     engine.requests.pop(r.request_id, None)
 
 
+# request class -> engine scheduler priority (higher first); classes follow the
+# reference's BloomScheduler (scheduler/mod.rs:893-915): foreground interactive
+# > realtime stream > background batch > maintenance
+SEGMENT_PRIORITY = {0: 3, 1: 2, 2: 1, 3: 0}
+SEGMENTS = {"foreground": 0, "realtime": 1, "background": 2, "maintenance": 3}
+
+
+class ThermalMonitor:
+    """Reads the GPU's throttle reasons through NVML at most once a second:
+    thermal 3 (hardware thermal slowdown), 2 (software thermal slowdown) or 0."""
+
+    def __init__(self, device_index: Optional[int]):
+        self.h = None
+        self.last = 0.0
+        self.thermal = 0
+        if device_index is None:
+            return
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(int(device_index))
+        except Exception:
+            self.h = None
+
+    def poll(self, now: float) -> int:
+        if self.h is None or now - self.last < 1.0:
+            return self.thermal
+        self.last = now
+        try:
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            return self.thermal
+        self.thermal = 3 if r & 0x40 else (2 if r & 0x20 else 0)
+        return self.thermal
+
+
 class ServingRuntime:
-    def __init__(self, pipeline, model_id: str, max_concurrent: int = 4, metrics=None, ctrl: Optional[TPControl] = None):
+    def __init__(self, pipeline, model_id: str, max_concurrent: int = 4, metrics=None, ctrl: Optional[TPControl] = None,
+                 admit_per_step: int = 64):
         self.pipe = pipeline
         self.model_id = model_id
         self.max_concurrent = max_concurrent
@@ -109,6 +149,16 @@ class ServingRuntime:
         self.broken: Optional[str] = None  # set when a tensor-parallel peer was lost
         self.ctrl = ctrl
         self.engine = getattr(pipeline, "llm", None)
+        # admission order: weighted fair queueing over request classes (C++
+        # SegmentScheduler), at most `admit_per_step` new requests per engine
+        # step, fewer under thermal slowdown
+        from .._ext import runtime as _native
+
+        self.admit_per_step = max(1, int(admit_per_step))
+        self.segments = _native().SegmentScheduler(self.admit_per_step, True)
+        self._held: Dict[str, Submission] = {}
+        dev = getattr(getattr(self.engine, "model", None), "device", None)
+        self.thermal = ThermalMonitor(getattr(dev, "index", None) if dev is not None else None)
         self._thread = threading.Thread(target=self._loop, name="bloom-engine", daemon=True)
         self._thread.start()
 
@@ -128,10 +178,11 @@ class ServingRuntime:
     def available_permits(self) -> int:
         return max(0, self.max_concurrent - self.in_flight)
 
-    def submit(self, prompt_ids: List[int], params, messages=None, request_id: Optional[str] = None) -> Submission:
+    def submit(self, prompt_ids: List[int], params, messages=None, request_id: Optional[str] = None,
+               segment: int = 0) -> Submission:
         loop = asyncio.get_running_loop()
         sub = Submission(request_id or f"req-{next(_ids)}", list(prompt_ids), params, loop, asyncio.Queue(),
-                         messages=messages)
+                         messages=messages, segment=int(segment))
         if self.broken is not None:
             sub.queue.put_nowait(StreamItem(finished=True, reason="error", error=self.broken))
             return sub
@@ -193,21 +244,28 @@ class ServingRuntime:
                     sub = self._pending.get_nowait()
                 except queue.Empty:
                     break
+                self._held[sub.id] = sub
+                self.segments.submit(sub.id, sub.segment)
+            if self._held:
+                self.segments.set_conditions(self.thermal.poll(time.time()), 0)
+            for sid, cls in (self.segments.next_batch() if self._held else []):
+                sub = self._held.pop(sid)
                 if sub.cancelled:
                     self._emit(sub, StreamItem(finished=True, reason="abort"))
                     self._finish(sub)
                     continue
+                prio = SEGMENT_PRIORITY.get(cls, 0)
                 try:
-                    rid = eng.add_request(sub.prompt_ids, sub.params)
+                    rid = eng.add_request(sub.prompt_ids, sub.params, prio)
                 except Exception as e:  # prompt too long etc.
                     self._emit(sub, StreamItem(finished=True, reason="error", error=str(e)))
                     self._finish(sub)
                     continue
-                msg["add"].append((list(sub.prompt_ids), sub.params))
+                msg["add"].append((list(sub.prompt_ids), sub.params, prio))
                 sub.engine_rid = rid
                 with self._lock:
                     self._by_rid[rid] = sub
-            msg["step"] = eng.has_unfinished()
+            msg["step"] = eng.has_unfinished() or bool(self._held)
             if ctrl is not None and (msg["add"] or msg["abort"] or msg["step"] or time.time() - last_beat > 1.0):
                 try:
                     ctrl.exchange(msg)  # the other ranks repeat these calls before the same step
@@ -271,6 +329,8 @@ class ServingRuntime:
         self.ready = False
         with self._lock:
             subs = list(self._by_id.values())
+        subs += list(self._held.values())
+        self._held.clear()
         while True:
             try:
                 subs.append(self._pending.get_nowait())

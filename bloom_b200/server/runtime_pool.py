@@ -195,6 +195,8 @@ class RuntimeEntry:
         """Requests being served by this runtime right now."""
         return int(getattr(self.runtime, "in_flight", 0) or 0)
 
+    on_retire: List[Any] = field(default_factory=list)  # callbacks (key) run after shutdown
+
     def retire(self) -> None:
         try:
             self.runtime.shutdown()
@@ -202,6 +204,9 @@ class RuntimeEntry:
             if self.permit is not None:
                 self.permit.release()
                 self.permit = None
+            for cb in self.on_retire:
+                cb(self.key)
+            self.on_retire = []
 
 
 class RuntimePool:

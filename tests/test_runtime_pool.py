@@ -167,3 +167,68 @@ def test_ollama_keep_alive_load_unload_and_expiry(tmp_path):
         assert r.json()["done_reason"] == "unload"
         assert "m2.gguf" not in {m["name"] for m in c.get("/api/ps").json()["models"]}
         assert c.post("/api/generate", json={"model": "m1.gguf", "keep_alive": "5x"}).status_code == 400
+
+
+def test_residency_reports_ledger(tmp_path):
+    with TestClient(_server(tmp_path)) as c:
+        c.post("/v1/model-management/load", json={"model": "m1.gguf"})
+        led = c.get("/v1/model-management/residency").json()["ledger"]
+        assert sum(v["used_bytes"] for v in led.values()) > 0
+        c.post("/v1/model-management/unload", json={"model": "m1.gguf"})
+        led = c.get("/v1/model-management/residency").json()["ledger"]
+        assert sum(v["used_bytes"] for v in led.values()) == 0
+
+
+def test_segment_admission_order():
+    """Waiting requests are admitted by weighted fair queueing over request
+    classes (foreground 4 : realtime 3 : background 2 : maintenance 1) and
+    reach the engine with the class's priority."""
+    import asyncio
+
+    from bloom_b200.server.runtime import ServingRuntime
+
+    class Eng:
+        def __init__(self):
+            self.added, self.live, self.requests = [], {}, {}
+            self.n = 0
+
+        def add_request(self, prompt, params, priority=0):
+            self.n += 1
+            self.added.append((prompt[0], priority))
+            return self.n
+
+        def abort(self, rid):
+            pass
+
+        def has_unfinished(self):
+            return False
+
+        def step(self):
+            return []
+
+    class Pipe:
+        pass
+
+    p = Pipe()
+    p.llm = Eng()
+
+    async def go():
+        rt = ServingRuntime(p, "m", 64, admit_per_step=4)
+        rt._stop.set()  # hold the loop: submit everything first
+        rt._thread.join()
+        subs = [rt.submit([100 + i], None, segment=2) for i in range(4)] + \
+               [rt.submit([200 + i], None, segment=0) for i in range(4)]
+        rt._stop.clear()
+        import threading
+
+        rt._thread = threading.Thread(target=rt._loop, daemon=True)
+        rt._thread.start()
+        await asyncio.sleep(0.3)
+        rt.shutdown()
+        return p.llm.added
+
+    added = asyncio.run(go())
+    assert len(added) == 8
+    first = added[:4]  # one batch of 4: a weighted pass, foreground weight 4 > background 2
+    assert sum(1 for t, _ in first if t >= 200) >= 2
+    assert {pr for t, pr in added if t >= 200} == {3} and {pr for t, pr in added if t < 200} == {1}

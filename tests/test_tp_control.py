@@ -24,7 +24,7 @@ WORKER = textwrap.dedent(r'''
         """Each request gets 3 tokens over 2 steps (2 tokens in its first step: speculation)."""
         def __init__(self):
             self.log, self.next, self.live, self.requests = [], 1, {}, {}
-        def add_request(self, prompt, params):
+        def add_request(self, prompt, params, priority=0):
             rid = self.next; self.next += 1
             self.live[rid] = []; self.requests[rid] = None
             self.log.append(("add", rid, list(prompt)))
@@ -119,7 +119,7 @@ DYING = textwrap.dedent(r'''
         """Every request needs 1000 steps; rank 1's copy exits after its 3rd step."""
         def __init__(self, die_after=None):
             self.next, self.live, self.requests, self.steps, self.die_after = 1, {}, {}, 0, die_after
-        def add_request(self, prompt, params):
+        def add_request(self, prompt, params, priority=0):
             rid = self.next; self.next += 1
             self.live[rid] = []; self.requests[rid] = None
             return rid
