@@ -1062,6 +1062,62 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
                            "model_not_found")
         return {"status": "removed", "model": model_id}
 
+    # ------------------------------------------------------------ acquisition (offline subset)
+    def store():
+        require_catalog()
+        from .model_store import ModelStore
+
+        if not hasattr(app.state, "model_store"):
+            app.state.model_store = ModelStore(catalog.root)
+        return app.state.model_store
+
+    async def in_thread(fn, *a):
+        from .model_store import StoreError
+
+        try:
+            return await asyncio.get_running_loop().run_in_executor(None, fn, *a)
+        except StoreError as e:
+            raise APIError(400, str(e)) from None
+
+    @app.post("/v1/model-management/import")
+    async def mm_import(request: Request):
+        """Copy a local model file / package into the models directory with a
+        checksum record (optionally checked against an expected sha256)."""
+        d = await body(request)
+        if not isinstance(d.get("path"), str):
+            raise APIError(400, "import needs a local `path`", param="path")
+        return await in_thread(store().import_package, d["path"], d.get("model"), d.get("sha256"))
+
+    @app.post("/v1/model-management/record")
+    async def mm_record(request: Request):
+        d = await body(request)
+        return await in_thread(store().record, str(d.get("model", "")), str(d.get("source", "local")))
+
+    @app.post("/v1/model-management/verify")
+    async def mm_verify(request: Request):
+        d = await body(request)
+        mid = str(d.get("model", ""))
+        if mid == st._model_id and state["loaded"] and d.get("quarantine", True):
+            raise APIError(409, "the active model cannot be quarantined; switch or unload first", "conflict")
+        return await in_thread(store().verify, mid, bool(d.get("quarantine", True)))
+
+    @app.get("/v1/model-management/integrity")
+    async def mm_integrity():
+        return store().status
+
+    @app.get("/v1/model-management/inventory")
+    async def mm_inventory():
+        return store().inventory()
+
+    @app.post("/v1/model-management/inventory/reconcile")
+    async def mm_reconcile(request: Request):
+        d = await body(request)
+        return store().reconcile(d.get("inventory", d))
+
+    @app.get("/v1/model-management/quarantine")
+    async def mm_quarantine():
+        return {"object": "list", "data": store().quarantined()}
+
     @app.post("/api/pull")
     async def ollama_pull(request: Request):
         return _ollama_error(APIError(501, "model downloads are not available in this offline build; copy the "

@@ -36,6 +36,8 @@ class ModelCatalog:
         if not self.root or not os.path.isdir(self.root):
             return out
         for name in sorted(os.listdir(self.root)):
+            if name.startswith("."):  # store metadata, quarantine, imports in progress
+                continue
             path = os.path.join(self.root, name)
             if not (os.path.isdir(path) or name.endswith(".gguf")):
                 continue
