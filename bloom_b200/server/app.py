@@ -1063,7 +1063,7 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         return {"status": "removed", "model": model_id}
 
     # ------------------------------------------------------------ acquisition (offline subset)
-    def store():
+    def model_store():
         require_catalog()
         from .model_store import ModelStore
 
@@ -1086,12 +1086,12 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         d = await body(request)
         if not isinstance(d.get("path"), str):
             raise APIError(400, "import needs a local `path`", param="path")
-        return await in_thread(store().import_package, d["path"], d.get("model"), d.get("sha256"))
+        return await in_thread(model_store().import_package, d["path"], d.get("model"), d.get("sha256"))
 
     @app.post("/v1/model-management/record")
     async def mm_record(request: Request):
         d = await body(request)
-        return await in_thread(store().record, str(d.get("model", "")), str(d.get("source", "local")))
+        return await in_thread(model_store().record, str(d.get("model", "")), str(d.get("source", "local")))
 
     @app.post("/v1/model-management/verify")
     async def mm_verify(request: Request):
@@ -1099,24 +1099,24 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         mid = str(d.get("model", ""))
         if mid == st._model_id and state["loaded"] and d.get("quarantine", True):
             raise APIError(409, "the active model cannot be quarantined; switch or unload first", "conflict")
-        return await in_thread(store().verify, mid, bool(d.get("quarantine", True)))
+        return await in_thread(model_store().verify, mid, bool(d.get("quarantine", True)))
 
     @app.get("/v1/model-management/integrity")
     async def mm_integrity():
-        return store().status
+        return model_store().status
 
     @app.get("/v1/model-management/inventory")
     async def mm_inventory():
-        return store().inventory()
+        return model_store().inventory()
 
     @app.post("/v1/model-management/inventory/reconcile")
     async def mm_reconcile(request: Request):
         d = await body(request)
-        return store().reconcile(d.get("inventory", d))
+        return model_store().reconcile(d.get("inventory", d))
 
     @app.get("/v1/model-management/quarantine")
     async def mm_quarantine():
-        return {"object": "list", "data": store().quarantined()}
+        return {"object": "list", "data": model_store().quarantined()}
 
     @app.post("/api/pull")
     async def ollama_pull(request: Request):
