@@ -513,6 +513,61 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
 
         return {"object": "list", "data": default_registry().describe()}
 
+    # ------------------------------------------------------------ world-model loop
+    world_sessions: "OrderedDict[str, Any]" = OrderedDict()
+
+    @app.post("/v1/world/step")
+    async def world_step(request: Request):
+        """One observation -> state -> predicted futures -> action cycle.
+        Without `session` every call starts a fresh loop (the reference's
+        behaviour); with `session` the loop and its state cache persist
+        between calls (at most 64 sessions, least recently used dropped).
+        `engine`: "latent" (GPU latent dynamics, the default) or "mock"."""
+        from ..engine import world as W
+
+        d = await body(request)
+        try:
+            obs = [W.Observation.parse(o) for o in (d.get("observations") or [])]
+            horizon = d.get("horizon", 1)
+            if not isinstance(horizon, int) or not 0 <= horizon <= 64:
+                raise W.WorldError("horizon must be an integer in [0, 64]")
+            sid = d.get("session")
+            loop = world_sessions.get(sid) if sid else None
+            if loop is None:
+                cc = W.CacheConfig()
+                for k, v in (d.get("cache_config") or {}).items():
+                    if hasattr(cc, k) and v is not None:
+                        setattr(cc, k, type(getattr(cc, k))(v))
+                kind = d.get("engine", "latent")
+                sp = (d.get("action_schema") or {}).get("allowed_action_spaces") or ["robot_velocity"]
+                dim = (d.get("action_schema") or {}).get("action_dimensions", {}).get(sp[0], 2)
+                if kind == "mock":
+                    loop = W.WorldModelLoop(W.MockWorldModel(), W.MockPolicy(sp[0], dim), cc)
+                elif kind == "latent":
+                    loop = W.WorldModelLoop(W.LatentWorldModel(), W.LinearPolicy(action_space=sp[0], dim=dim), cc)
+                else:
+                    raise W.WorldError("engine must be latent or mock")
+                if sid:
+                    world_sessions[str(sid)] = loop
+                    while len(world_sessions) > 64:
+                        world_sessions.popitem(last=False)
+            elif sid:
+                world_sessions.move_to_end(str(sid))
+            loop.state_schema = d.get("state_schema")
+            loop.action_schema = d.get("action_schema")
+            if d.get("thermal_state") is not None and d.get("power_state") is not None:
+                loop.set_environment(str(d["thermal_state"]), str(d["power_state"]))
+            chunks = await asyncio.get_running_loop().run_in_executor(None, loop.step, obs, horizon)
+        except W.WorldError as e:
+            raise APIError(400, str(e), "invalid_observation_or_action") from None
+        if d.get("stream"):
+            async def sse():
+                for c in chunks:
+                    yield f"data: {json.dumps(c)}\n\n"
+
+            return StreamingResponse(sse(), media_type="text/event-stream")
+        return chunks
+
     @app.post("/v1/cancel/{request_id}")
     async def cancel(request_id: str):
         if not rt.cancel(request_id):
