@@ -313,3 +313,26 @@ class EchoPipeline(InferencePipeline):
         tail = filt.flush()
         if tail:
             yield tail
+
+    accepts_images = True
+
+    def run_multimodal(self, blocks, params) -> Iterator[str]:
+        """Echo of a multimodal request: its text, and each image's size."""
+        from .processor import decode_image
+        from .vl_pipeline import parse_blocks
+
+        parts = []
+        for kind, v in parse_blocks(blocks):
+            if kind == "Text":
+                parts.append(v)
+            elif kind == "Tokens":
+                parts.append(self.tokenizer.decode(v))
+            else:
+                img = decode_image(*v)
+                parts.append(f"[image {img.shape[1]}x{img.shape[0]}]")
+        words = ("echo: " + " ".join(parts)).split(" ")
+        n = min(len(words), max(1, getattr(params, "max_tokens", 128)))
+        self.last_generated_tokens = n
+        for i in range(n):
+            yield words[i] if i == 0 else " " + words[i]
+

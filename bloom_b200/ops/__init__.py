@@ -27,7 +27,8 @@ EPI_F32 = 1
 EPI_SWIGLU = 2
 EPI_PARTIAL_F32 = 3
 EPI_RESIDUAL = 4
-EPI_GELU = 5
+EPI_GELU = 5  # erf form
+EPI_GELU_TANH = 6  # tanh approximation ("gelu_pytorch_tanh")
 
 
 def status(device: Optional[int] = None) -> torch.Tensor:

@@ -513,6 +513,97 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
 
         return {"object": "list", "data": default_registry().describe()}
 
+    # ------------------------------------------------------------ multimodal
+    def _multipart(raw: bytes, ctype: str) -> Dict[str, tuple]:
+        """name -> (bytes, content type) of a multipart/form-data body."""
+        from email.parser import BytesParser
+        from email.policy import HTTP
+
+        msg = BytesParser(policy=HTTP).parsebytes(b"Content-Type: " + ctype.encode() + b"\r\n\r\n" + raw)
+        if not msg.is_multipart():
+            raise APIError(400, "expected a multipart/form-data upload")
+        out = {}
+        for part in msg.iter_parts():
+            name = part.get_param("name", header="content-disposition")
+            if name:
+                out[str(name)] = (part.get_payload(decode=True) or b"", part.get_content_type())
+        return out
+
+    async def _multimodal(request: Request, blocks, params):
+        from ..engine.processor import ProcessorError
+        from ..engine.vl_pipeline import parse_blocks
+
+        if not getattr(pipeline, "accepts_images", False):
+            raise APIError(400, "the loaded model does not accept multimodal input", param="model")
+        try:
+            parse_blocks(blocks)  # fail before streaming starts
+        except ProcessorError as e:
+            raise APIError(400, str(e), param="blocks") from None
+        if not rt.try_acquire():
+            raise APIError(429, "server is at capacity; retry shortly", "rate_limit_error", headers={"Retry-After": "1"})
+        loop = asyncio.get_running_loop()
+        q: "asyncio.Queue" = asyncio.Queue()
+        pipe = pipeline.get()
+
+        def work():
+            try:
+                for d in pipe.run_multimodal(blocks, params):
+                    loop.call_soon_threadsafe(q.put_nowait, ("delta", d))
+                loop.call_soon_threadsafe(q.put_nowait, ("end", None))
+            except Exception as e:  # noqa: BLE001 - reported in the stream
+                loop.call_soon_threadsafe(q.put_nowait, ("error", str(e)))
+
+        t0 = time.time()
+        loop.run_in_executor(None, work)
+
+        async def sse():
+            n = 0
+            try:
+                while True:
+                    kind, v = await q.get()
+                    if kind == "delta":
+                        n += 1
+                        yield f"data: {json.dumps({'TextDelta': v})}\n\n"
+                    elif kind == "error":
+                        yield f"data: {json.dumps({'error': {'message': v, 'type': 'server_error'}})}\n\n"
+                        return
+                    else:
+                        metrics.tokens_generated += n
+                        yield f"data: {json.dumps({'Metrics': {'compute_ms': int((time.time() - t0) * 1000)}})}\n\n"
+                        yield f"data: {json.dumps('End')}\n\n"
+                        return
+            finally:
+                rt.release()
+
+        return StreamingResponse(sse(), media_type="text/event-stream")
+
+    @app.post("/v1/multimodal/stream")
+    async def multimodal_stream(request: Request):
+        """InferenceRequest {"blocks": [...], "params": {max_tokens, temperature,
+        top_p, seed}} -> SSE of OutputChunks (TextDelta ..., Metrics, End)."""
+        d = await body(request)
+        check_model(d.get("model"))
+        return await _multimodal(request, d.get("blocks"), sampling(d.get("params") or {}, 128))
+
+    @app.post("/v1/multimodal/upload")
+    async def multimodal_upload(request: Request):
+        """multipart/form-data: prompt, image (image/png; JPEG is refused),
+        optional model and max_tokens -> the same SSE stream."""
+        raw = await request.body()
+        if len(raw) > 32 * 1024 * 1024:
+            raise APIError(413, "upload too large (32 MiB at most)")
+        parts = _multipart(raw, request.headers.get("content-type", ""))
+        if "model" in parts:
+            check_model(parts["model"][0].decode("utf-8", "replace"))
+        blocks = []
+        if "image" in parts:
+            data, mime = parts["image"]
+            blocks.append({"Image": {"bytes": base64.b64encode(data).decode(), "mime": mime}})
+        if "prompt" in parts:
+            blocks.append({"Text": parts["prompt"][0].decode("utf-8", "replace")})
+        p = {"max_tokens": int(parts["max_tokens"][0]) if "max_tokens" in parts else 512}
+        return await _multimodal(request, blocks, sampling(p, 512))
+
     # ------------------------------------------------------------ world-model loop
     world_sessions: "OrderedDict[str, Any]" = OrderedDict()
 

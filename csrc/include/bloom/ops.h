@@ -13,6 +13,7 @@ enum GemmEpilogue : int {
   kEpiPartialF32 = 3,  // split-K: out f32 [splits, M, N] partial sums
   kEpiResidual = 4,    // out bf16 [M, N] = acc + resid
   kEpiGelu = 5,        // out bf16 [M, N] = gelu_erf(acc + bias)
+  kEpiGeluTanh = 6,    // out bf16 [M, N] = gelu_tanh(acc + bias) (runs the kEpiGelu kernels with Args::gelu_tanh)
 };
 
 // splits > 1 with a non-partial epilogue: split-K where the last-arriving CTA

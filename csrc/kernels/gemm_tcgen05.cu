@@ -73,6 +73,7 @@ struct Args {
   // [world][push_rows][ldo] layout, while the rest of the GEMM runs.
   unsigned long long push[8];
   int push_world, push_rank, push_rows;
+  int gelu_tanh;  // kEpiGelu: 1 = tanh approximation, 0 = erf
 };
 
 // Row `tok` of the bf16 output: local, or the owner's slot for this rank (push).
@@ -263,7 +264,9 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const float y = x[k] + bias[k];
-            x[k] = 0.5f * y * (1.f + erff(y * 0.7071067811865476f));
+            // 0.7978845608 = sqrt(2 / pi), the tanh form's scale (Hendrycks & Gimpel, 2016)
+            x[k] = a.gelu_tanh ? 0.5f * y * (1.f + tanhf(0.7978845608028654f * (y + 0.044715f * y * y * y)))
+                               : 0.5f * y * (1.f + erff(y * 0.7071067811865476f));
           }
           store8_bf16(reinterpret_cast<__nv_bfloat16*>(a.out) + (long)tok * a.ldo + f, x, nf, a.vec);
         }
@@ -1126,6 +1129,8 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   TORCH_CHECK(w.size(1) == K, "gemm: K mismatch");
   TORCH_CHECK(K % 8 == 0, "gemm: K must be a multiple of 8");
   if (M == 0) return;
+  const bool gelu_tanh = epi == kEpiGeluTanh;
+  if (gelu_tanh) epi = kEpiGelu;
   const at::cuda::CUDAGuard guard(x.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 
@@ -1140,6 +1145,7 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.M = M;
   a.N = N;
   a.K = K;
+  a.gelu_tanh = gelu_tanh ? 1 : 0;
   a.num_kb = (K + gemm::BK - 1) / gemm::BK;
   a.num_feat_tiles = (N + gemm::BM - 1) / gemm::BM;
   a.num_tok_tiles = (M + bn - 1) / bn;

@@ -16,6 +16,7 @@
 #include <functional>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
@@ -249,3 +250,53 @@ void register_model_store(py::module_& m) {
       },
       py::arg("paths"), py::arg("threads") = 4, py::arg("progress") = std::function<bool(int64_t)>());
 }
+
+// ---------------------------------------------------------------- PNG scanline reconstruction
+// Reverses the five PNG filter types (None, Sub, Up, Average, Paeth; PNG
+// specification section 9) over the inflated IDAT stream of a non-interlaced
+// 8-bit image: `raw` holds h rows of (1 filter byte + w * bpp bytes).
+// The per-pixel dependency on the left neighbour makes this sequential per
+// row, so it runs here rather than in Python.
+namespace {
+inline uint8_t paeth(int a, int b, int c) {
+  const int p = a + b - c;
+  const int pa = std::abs(p - a), pb = std::abs(p - b), pc = std::abs(p - c);
+  if (pa <= pb && pa <= pc) return static_cast<uint8_t>(a);
+  if (pb <= pc) return static_cast<uint8_t>(b);
+  return static_cast<uint8_t>(c);
+}
+}  // namespace
+
+py::bytes png_unfilter(const py::bytes& raw_b, int h, int w, int bpp) {
+  const std::string raw(raw_b);
+  const size_t stride = static_cast<size_t>(w) * bpp;
+  if (h <= 0 || w <= 0 || bpp <= 0 || raw.size() < static_cast<size_t>(h) * (stride + 1))
+    throw std::invalid_argument("png_unfilter: truncated image data");
+  std::string out(static_cast<size_t>(h) * stride, '\0');
+  uint8_t* o = reinterpret_cast<uint8_t*>(&out[0]);
+  const uint8_t* r = reinterpret_cast<const uint8_t*>(raw.data());
+  for (int y = 0; y < h; ++y) {
+    const uint8_t ft = r[y * (stride + 1)];
+    const uint8_t* src = r + y * (stride + 1) + 1;
+    uint8_t* cur = o + y * stride;
+    const uint8_t* prev = y > 0 ? o + (y - 1) * stride : nullptr;
+    for (size_t x = 0; x < stride; ++x) {
+      const int a = x >= static_cast<size_t>(bpp) ? cur[x - bpp] : 0;
+      const int b = prev ? prev[x] : 0;
+      const int c = (prev && x >= static_cast<size_t>(bpp)) ? prev[x - bpp] : 0;
+      int v = src[x];
+      switch (ft) {
+        case 0: break;
+        case 1: v += a; break;
+        case 2: v += b; break;
+        case 3: v += (a + b) >> 1; break;
+        case 4: v += paeth(a, b, c); break;
+        default: throw std::invalid_argument("png_unfilter: unknown filter type");
+      }
+      cur[x] = static_cast<uint8_t>(v);
+    }
+  }
+  return py::bytes(out);
+}
+
+void register_image(py::module_& m) { m.def("png_unfilter", &png_unfilter); }

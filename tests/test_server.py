@@ -384,3 +384,30 @@ def test_memory_telemetry_snapshot():
     assert s.rss_bytes > 0 and s.peak_rss_bytes >= s.rss_bytes and s.total_ram_bytes > s.rss_bytes
     assert 0.0 <= s.ram_utilization <= 1.0 and "RAM rss" in s.summary()
     assert s.to_dict()["high_pressure"] in (True, False)
+
+
+def test_multimodal_stream_and_upload(client):
+    import base64
+    import sys
+    import os
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    import numpy as np
+    from test_processor_vl import png_bytes
+
+    img = np.random.default_rng(0).integers(0, 256, (12, 20, 3), dtype=np.uint8)
+    png = png_bytes(img, 4)
+    body = {"blocks": [{"Image": {"bytes": base64.b64encode(png).decode(), "mime": "image/png"}},
+                       {"Text": "what is this"}], "params": {"max_tokens": 64}}
+    r = client.post("/v1/multimodal/stream", json=body)
+    ev = [json.loads(l[6:]) for l in r.text.splitlines() if l.startswith("data: ")]
+    text = "".join(e["TextDelta"] for e in ev if isinstance(e, dict) and "TextDelta" in e)
+    assert text == "echo: [image 20x12] what is this" and ev[-1] == "End"
+    bad = client.post("/v1/multimodal/stream", json={"blocks": [{"Image": {"bytes": "AAAA", "mime": "image/jpeg"}},
+                                                                {"Image": {"bytes": "AAAA", "mime": "x"}}]})
+    assert bad.status_code == 400
+    files = {"image": ("a.png", png, "image/png"), "prompt": (None, "hi")}
+    r = client.post("/v1/multimodal/upload", files=files)
+    ev = [json.loads(l[6:]) for l in r.text.splitlines() if l.startswith("data: ")]
+    assert "".join(e["TextDelta"] for e in ev if isinstance(e, dict) and "TextDelta" in e) == \
+        "echo: [image 20x12] hi"
