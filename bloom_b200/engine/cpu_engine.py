@@ -40,11 +40,37 @@ class FLinear:
         return x.float() @ self.w.t()
 
 
+def _fuse(parts: List[object]) -> Optional[object]:
+    """Rows of several Q8_0 / fp32 linears with the same K as one linear."""
+    if all(isinstance(p, QLinear) for p in parts) and len({p.k for p in parts}) == 1:
+        return QLinear(torch.cat([p.raw.view(p.n, -1) for p in parts], 0).reshape(-1).contiguous(),
+                       sum(p.n for p in parts), parts[0].k)
+    if all(isinstance(p, FLinear) for p in parts) and len({p.w.shape[1] for p in parts}) == 1:
+        return FLinear(torch.cat([p.w for p in parts], 0))
+    return None
+
+
 class CpuDecoder:
     def __init__(self, cfg: ModelConfig, linears: Dict[str, object], dense: Dict[str, torch.Tensor]):
+        import os
+
+        # the native thread pool parallelises the matmuls; the PyTorch glue
+        # between them is tiny, and torch's own intra-op threads would only
+        # compete with the pool's workers for the cores
+        torch.set_num_threads(int(os.environ.get("BLOOM_TORCH_THREADS", "1")))
         self.cfg = cfg
         self.L = linears
         self.D = dense
+        # one matmul for q|k|v and one for gate|up per layer: the decode step is
+        # a chain of small matmuls, so fewer and larger ones run faster
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            qkv = _fuse([linears[p + f"self_attn.{x}_proj.weight"] for x in "qkv"])
+            if qkv is not None:
+                linears[p + "self_attn.qkv"] = qkv
+            gu = _fuse([linears[p + "mlp.gate_proj.weight"], linears[p + "mlp.up_proj.weight"]])
+            if gu is not None:
+                linears[p + "mlp.gate_up"] = gu
         self.cos_sin = rope_cos_sin(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta,
                                     scaling=cfg.rope_scaling)
 
@@ -107,9 +133,12 @@ class CpuDecoder:
         for i in range(c.num_layers):
             p = f"model.layers.{i}."
             h = R.rmsnorm(x, D[p + "input_layernorm.weight"], c.rms_norm_eps)
-            q = L[p + "self_attn.q_proj.weight"](h)
-            k = L[p + "self_attn.k_proj.weight"](h)
-            v = L[p + "self_attn.v_proj.weight"](h)
+            if p + "self_attn.qkv" in L:
+                q, k, v = L[p + "self_attn.qkv"](h).split([c.q_size, c.kv_size, c.kv_size], dim=-1)
+            else:
+                q = L[p + "self_attn.q_proj.weight"](h)
+                k = L[p + "self_attn.k_proj.weight"](h)
+                v = L[p + "self_attn.v_proj.weight"](h)
             if c.qkv_bias:
                 q = q + D[p + "self_attn.q_proj.bias"]
                 k = k + D[p + "self_attn.k_proj.bias"]
@@ -129,8 +158,11 @@ class CpuDecoder:
             a = R.attention(q, kk, vv, causal=True, q_offset=start).reshape(T, c.q_size)
             x = x + L[p + "self_attn.o_proj.weight"](a)
             h = R.rmsnorm(x, D[p + "post_attention_layernorm.weight"], c.rms_norm_eps)
-            g = L[p + "mlp.gate_proj.weight"](h)
-            u = L[p + "mlp.up_proj.weight"](h)
+            if p + "mlp.gate_up" in L:
+                g, u = L[p + "mlp.gate_up"](h).split([c.intermediate_size, c.intermediate_size], dim=-1)
+            else:
+                g = L[p + "mlp.gate_proj.weight"](h)
+                u = L[p + "mlp.up_proj.weight"](h)
             x = x + L[p + "mlp.down_proj.weight"](R.swiglu(g, u))
         cache["len"] = start + T
         h = R.rmsnorm(x[-1:], D["model.norm.weight"], c.rms_norm_eps)

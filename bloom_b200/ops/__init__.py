@@ -269,8 +269,9 @@ def mrope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor
           sections=MROPE_SECTIONS_QWEN_VL):
     """Multimodal rotary embedding of q [B, H, S, D] and k [B, KVH, S, D]
     (fp32 or bf16) with cos / sin [3, B, S, D]; returns (q_out, k_out)."""
+    q, k = q.contiguous(), k.contiguous()
     qo, ko = torch.empty_like(q), torch.empty_like(k)
-    _C().mrope(q.contiguous(), k.contiguous(), cos.float().contiguous(), sin.float().contiguous(), qo, ko,
+    _C().mrope(q, k, cos.float().contiguous(), sin.float().contiguous(), qo, ko,
                int(sections[0]), int(sections[1]), int(sections[2]))
     _count(2)
     return qo, ko

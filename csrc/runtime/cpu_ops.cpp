@@ -217,7 +217,7 @@ torch::Tensor q8_0_matmul(const torch::Tensor& x, const torch::Tensor& wraw, int
   auto y = torch::empty({M, N}, torch::kFloat);
   float* yp = y.data_ptr<float>();
   const uint8_t* w = wraw.data_ptr<uint8_t>();
-  parallel_for(N, [&](int64_t n0, int64_t n1) {
+  auto rows = [&](int64_t n0, int64_t n1) {
   for (int64_t n = n0; n < n1; ++n) {
     const uint8_t* wr = w + n * kb * Q8_BYTES;
     for (int64_t m = 0; m < M; ++m) {
@@ -227,7 +227,12 @@ torch::Tensor q8_0_matmul(const torch::Tensor& x, const torch::Tensor& wraw, int
       yp[m * N + n] = acc;
     }
   }
-  });
+  };
+  // below ~256 KB of weights one core finishes before a dispatch pays off
+  if (N * K * M < (int64_t(1) << 18))
+    rows(0, N);
+  else
+    parallel_for(N, rows);
   return y;
 }
 

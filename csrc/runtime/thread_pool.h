@@ -1,5 +1,10 @@
-// Minimal persistent worker pool for the host CPU kernels (no OpenMP runtime
-// is required at link time).
+// Persistent worker pool for the host CPU kernels (no OpenMP runtime is
+// required at link time).  A job is published by bumping an atomic
+// generation counter; workers spin on it for a short while (a decode step
+// issues its small matmuls back to back, so the next job usually arrives
+// within microseconds) and only then sleep on a condition variable, and the
+// caller spins on an atomic count of unfinished parts.  Dispatch therefore
+// costs about a cache-line round trip instead of two futex wake-ups.
 #pragma once
 
 #include <algorithm>
@@ -34,12 +39,13 @@ class ThreadPool {
 
   std::vector<std::thread> workers_;
   std::mutex mu_;
-  std::condition_variable cv_, done_cv_;
+  std::condition_variable cv_;
   const std::function<void(int64_t, int64_t)>* job_ = nullptr;
   int64_t job_n_ = 0;
-  int64_t generation_ = 0;
-  int pending_ = 0;
-  bool stop_ = false;
+  std::atomic<int64_t> generation_{0};
+  std::atomic<int> pending_{0};
+  std::atomic<bool> stop_{false};
+  std::atomic<int> sleepers_{0};
 };
 
 inline void parallel_for(int64_t n, const std::function<void(int64_t, int64_t)>& fn) {
