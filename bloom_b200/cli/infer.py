@@ -64,14 +64,15 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--backend", "--engine", dest="backend", default=None)
     ap.add_argument("--dtype", default=None)
     ap.add_argument("--context-size", "--ctx-size", dest="context_size", type=int)
-    ap.add_argument("--threads", type=int)
-    ap.add_argument("--batch-size", type=int)
-    ap.add_argument("--gpu-layers", type=int)
+    ap.add_argument("--threads", type=int, help="host CPU threads of the native kernels")
+    ap.add_argument("--batch-size", type=int, help="tokens per engine step (the prefill chunk)")
+    ap.add_argument("--gpu-layers", type=int,
+                    help="layers kept in HBM; the others stream from pinned host memory each step")
     ap.add_argument("--speculative", choices=["none", "ngram", "draft", "mtp"])
     ap.add_argument("--draft-model")
     ap.add_argument("--num-speculative-tokens", type=int)
     ap.add_argument("--speculative-ngram-order", type=int)
-    ap.add_argument("--image")
+    ap.add_argument("--image", help="PNG / PPM image for a vision-language model (a Qwen3-VL preset or package)")
     ap.add_argument("-i", "--interactive", action="store_true")
     ap.add_argument("--list-engines", action="store_true")
     ap.add_argument("--bench", action="store_true")
@@ -133,11 +134,14 @@ def main(argv: Optional[List[str]] = None) -> int:
         print(json.dumps(InferencePipeline.inspect(args.model, opts["context_size"], reg, tp=args.tp), indent=2))
         return 0
     t0 = time.perf_counter()
+    if args.image:
+        return run_image(args, opts)
     pipe = InferencePipeline.load(args.model, device=opts["device"], context_size=opts["context_size"], tp=args.tp,
                                   use_cuda_graphs=not args.no_cuda_graphs, template=args.template,
                                   speculative=opts["speculative"], draft_model=args.draft_model,
                                   num_speculative_tokens=opts["num_speculative_tokens"],
-                                  ngram_order=opts["speculative_ngram_order"])
+                                  ngram_order=opts["speculative_ngram_order"], gpu_layers=args.gpu_layers,
+                                  max_num_batched_tokens=args.batch_size, threads=args.threads)
     load_s = time.perf_counter() - t0
     if pipe.is_embedding:
         print("error: embedding models are served by the HTTP server (/v1/embeddings), not bloom_infer",
@@ -182,6 +186,33 @@ def main(argv: Optional[List[str]] = None) -> int:
         tps = gen / dur if dur > 0 else 0.0
         print(f"[load {load_s * 1e3:.0f} ms | ttft {(ttft or 0) * 1e3:.1f} ms | {gen} tokens | {tps:.2f} tok/s]",
               file=sys.stderr)
+    return 0
+
+
+def run_image(args, opts) -> int:
+    """Text + one image through the vision-language pipeline (streamed)."""
+    from ..engine.engine import SamplingParams
+    from ..engine.vl_pipeline import VisionLanguagePipeline
+    from ..models.qwen3_vl import PRESETS
+
+    if args.model not in PRESETS:
+        print(f"error: --image needs a vision-language model ({', '.join(PRESETS)})", file=sys.stderr)
+        return 2
+    t0 = time.perf_counter()
+    pipe = VisionLanguagePipeline.from_preset(args.model, context_size=opts["context_size"])
+    load_s = time.perf_counter() - t0
+    with open(args.image, "rb") as f:
+        data = f.read()
+    blocks = [{"Image": {"bytes": list(data), "mime": ""}}, {"Text": read_prompt(args) or ""}]
+    sp = SamplingParams(max_tokens=opts["max_tokens"], temperature=0.0)
+    t1 = time.perf_counter()
+    for d in pipe.run_multimodal(blocks, sp):
+        sys.stdout.write(d)
+        sys.stdout.flush()
+    sys.stdout.write("\n")
+    if not args.quiet:
+        print(f"[load {load_s * 1e3:.0f} ms | {pipe.last_generated_tokens} tokens in "
+              f"{(time.perf_counter() - t1) * 1e3:.0f} ms]", file=sys.stderr)
     return 0
 
 

@@ -89,7 +89,18 @@ class InferencePipeline:
     def load(model: str, device: str = "gpu", context_size: int = DEFAULT_CONTEXT_SIZE, tp: int = 1,
              use_cuda_graphs: bool = True, template: Optional[str] = None, strict: Optional[bool] = None,
              speculative: str = "none", draft_model: Optional[str] = None, num_speculative_tokens: int = 5,
-             ngram_order: int = 4, max_num_seqs: int = 64, tp_info=None) -> "InferencePipeline":
+             ngram_order: int = 4, max_num_seqs: int = 64, tp_info=None, gpu_layers: Optional[int] = None,
+             max_num_batched_tokens: Optional[int] = None, threads: Optional[int] = None) -> "InferencePipeline":
+        """`gpu_layers`: layers kept in HBM (the rest stream from pinned host
+        memory; default all, or BLOOM_GPU_LAYERS); `max_num_batched_tokens`:
+        tokens per engine step (the prefill chunk); `threads`: host CPU threads
+        of the native kernels."""
+        if threads:
+            from .._ext import runtime as _rt
+
+            _rt().set_num_threads(int(threads))
+        if gpu_layers is None and os.environ.get("BLOOM_GPU_LAYERS"):
+            gpu_layers = int(os.environ["BLOOM_GPU_LAYERS"])
         if strict is None:
             strict = os.environ.get("BLOOM_STRICT_MEMORY_BUDGET", "0") == "1"
         attempts = 0
@@ -101,7 +112,7 @@ class InferencePipeline:
             try:
                 return InferencePipeline._load_once(model, dev, ctx, tp, use_cuda_graphs, template, speculative,
                                                     draft_model, num_speculative_tokens, ngram_order, max_num_seqs,
-                                                    tp_info)
+                                                    tp_info, gpu_layers, max_num_batched_tokens)
             except Exception as e:  # degradation ladder on OOM only
                 if not _is_oom(e) or strict:
                     raise
@@ -119,7 +130,7 @@ class InferencePipeline:
 
     @staticmethod
     def _load_once(model, device, ctx, tp, use_cuda_graphs, template, speculative, draft_model, nspec, ngram_order,
-                   max_num_seqs, tp_info):
+                   max_num_seqs, tp_info, gpu_layers=None, max_num_batched_tokens=None):
         from ..formats.loader import load_tokenizer, load_weights, model_config
         from ..formats.manifest import load_manifest, verify_hashes
 
@@ -182,8 +193,11 @@ class InferencePipeline:
             from ..formats.loader import load_decoder
 
             dm = load_decoder(model, tp_info, None)
+        if gpu_layers is not None and gpu_layers < cfg.num_layers:
+            dm.place_layers(gpu_layers)
         spec_len = nspec if speculative in ("ngram", "draft") else 0
-        llm = LLMEngine(dm, EngineConfig(max_num_seqs=max_num_seqs, max_num_batched_tokens=max(ctx, 2048),
+        budget = int(max_num_batched_tokens) if max_num_batched_tokens else max(ctx, 2048)
+        llm = LLMEngine(dm, EngineConfig(max_num_seqs=max_num_seqs, max_num_batched_tokens=budget,
                                          max_model_len=ctx, use_cuda_graphs=use_cuda_graphs, spec_len=spec_len))
         llm.tokenizer = tok
         spec = None

@@ -71,7 +71,8 @@ class ModelRunner:
         self.buckets = [b for b in (graph_buckets or DEFAULT_BUCKETS) if b <= max_num_seqs]
         if max_num_seqs not in self.buckets:
             self.buckets.append(max_num_seqs)
-        self.use_cuda_graphs = use_cuda_graphs
+        # streamed (host-placed) layers order copies across two streams: eager steps only
+        self.use_cuda_graphs = use_cuda_graphs and not getattr(model, "offloaded", False)
         # decode attention split-K workspace, sized for the largest need over buckets
         ws = 1
         self.decode_splits: Dict[int, int] = {}

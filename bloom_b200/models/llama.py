@@ -408,6 +408,66 @@ class DecoderLM:
         else:
             self.layers[i] = layer
 
+    # ------------------------------------------------------------ layer placement
+    def place_layers(self, gpu_layers: int) -> None:
+        """Keep layers [0, gpu_layers) in HBM; the other layers' projection
+        weights move to pinned host memory and are streamed, one layer ahead,
+        into two HBM staging slots on a copy stream while the previous layer
+        computes (every layer still runs on this GPU's kernels).  For models
+        larger than the device memory left after the KV cache.  Reference:
+        LayerPlacementStrategy (crates/engine/src/core/memory.rs:484-533),
+        which computes the non-GPU layers on the CPU instead."""
+        n = len(self.layers)
+        g = max(0, min(int(gpu_layers), n))
+        self.host_layers = list(range(g, n))
+        if not self.host_layers:
+            return
+        keys = ("qkv", "o", "gate_up", "down")
+        for i in self.host_layers:
+            for k in keys:
+                t = self.layers[i].get(k)
+                if isinstance(t, torch.Tensor) and t.is_cuda:
+                    self.layers[i][k] = t.cpu().pin_memory()
+        ref = self.layers[self.host_layers[0]]
+        self._slots = [{k: torch.empty_like(ref[k], device=self.device) for k in keys if k in ref} for _ in range(2)]
+        self._copy_stream = torch.cuda.Stream(self.device)
+        self._ready = [torch.cuda.Event() for _ in range(2)]
+        self._done = [torch.cuda.Event() for _ in range(2)]
+        self._pending = -1  # host layer whose copy was issued ahead
+        torch.cuda.empty_cache()
+
+    @property
+    def offloaded(self) -> bool:
+        return bool(getattr(self, "host_layers", None))
+
+    def _stage(self, li: int) -> None:
+        """Queue the copy of host layer li into its slot (after the slot's last user finished)."""
+        j = self.host_layers.index(li)
+        s = j & 1
+        with torch.cuda.stream(self._copy_stream):
+            self._copy_stream.wait_event(self._done[s])
+            for k, dst in self._slots[s].items():
+                dst.copy_(self.layers[li][k], non_blocking=True)
+            self._ready[s].record(self._copy_stream)
+        self._pending = li
+
+    def _layer(self, li: int) -> Dict[str, torch.Tensor]:
+        lay = self.layers[li]
+        if not self.offloaded or li not in self.host_layers:
+            return lay
+        j = self.host_layers.index(li)
+        s = j & 1
+        if self._pending != li:
+            self._stage(li)
+        torch.cuda.current_stream(self.device).wait_event(self._ready[s])
+        if j + 1 < len(self.host_layers):
+            self._stage(self.host_layers[j + 1])
+        return dict(lay, **self._slots[s])
+
+    def _release(self, li: int) -> None:
+        if self.offloaded and li in self.host_layers:
+            self._done[self.host_layers.index(li) & 1].record(torch.cuda.current_stream(self.device))
+
     def _finish(self) -> None:
         cfg = self.cfg
         self.cos_sin = ops.rope_cos_sin(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, self.device,
@@ -465,7 +525,8 @@ class DecoderLM:
         residual = ops.embedding(s.input_ids, self.embed)
         x = ops.rmsnorm(residual, self.layers[0]["ln1"], eps)
         qkv_dim = (self.nq + 2 * self.nkv) * cfg.head_dim
-        for li, lay in enumerate(self.layers):
+        for li in range(len(self.layers)):
+            lay = self._layer(li)
             qkv = ops.gemm(x, lay["qkv"], bias=lay.get("qkv_b"))
             q = torch.empty(T, self.nq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
             ops.rope_kv_write(qkv, s.positions, s.slot_mapping, self.cos_sin, q, kv_cache, li, self.nq, self.nkv,
@@ -492,6 +553,7 @@ class DecoderLM:
             else:
                 act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU)
                 x = self._row_parallel_norm(act, lay["down"], residual, nxt, eps)
+            self._release(li)
         return x.index_select(0, s.logits_rows)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:

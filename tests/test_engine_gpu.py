@@ -366,3 +366,22 @@ def test_swap_preemption_matches_reference():
     for p, o in zip(prompts, outs):
         assert len(o.token_ids) == 40
         _check_greedy(cfg, w, p, o.token_ids)
+
+
+def test_streamed_layers_match_reference():
+    """Layers placed in host memory (streamed into HBM staging slots one layer
+    ahead) give the same greedy outputs as the all-HBM model."""
+    from bloom_b200.engine.engine import SamplingParams
+
+    cfg, w, eng = _build("tiny-llama", graphs=True)
+    m = eng.model
+    assert not m.offloaded
+    m.place_layers(1)
+    assert m.offloaded and m.host_layers == [1] and not m.layers[1]["qkv"].is_cuda
+    eng.runner.release_graphs()
+    eng.runner.use_cuda_graphs = False
+    torch.manual_seed(0)
+    prompts = [torch.randint(3, cfg.vocab_size, (n,)).tolist() for n in (5, 40)]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=10, temperature=0.0, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        _check_greedy(cfg, w, p, o.token_ids)
