@@ -136,12 +136,22 @@ def main(argv: Optional[List[str]] = None) -> int:
     t0 = time.perf_counter()
     if args.image:
         return run_image(args, opts)
-    pipe = InferencePipeline.load(args.model, device=opts["device"], context_size=opts["context_size"], tp=args.tp,
-                                  use_cuda_graphs=not args.no_cuda_graphs, template=args.template,
-                                  speculative=opts["speculative"], draft_model=args.draft_model,
-                                  num_speculative_tokens=opts["num_speculative_tokens"],
-                                  ngram_order=opts["speculative_ngram_order"], gpu_layers=args.gpu_layers,
-                                  max_num_batched_tokens=args.batch_size, threads=args.threads)
+    if args.backend in ("llamacpp", "script"):
+        from ..engine.external import ExternalPipeline, ExternalScriptEngine, ExternalServerEngine
+
+        eng = (ExternalServerEngine(args.model, device=opts["device"], context_size=opts["context_size"],
+                                    threads=args.threads) if args.backend == "llamacpp" else
+               ExternalScriptEngine(args.model))
+        pipe = ExternalPipeline(eng, template=args.template or "chatml", context_size=opts["context_size"])
+    else:
+        pipe = None
+    if pipe is None:
+        pipe = InferencePipeline.load(args.model, device=opts["device"], context_size=opts["context_size"], tp=args.tp,
+                                      use_cuda_graphs=not args.no_cuda_graphs, template=args.template,
+                                      speculative=opts["speculative"], draft_model=args.draft_model,
+                                      num_speculative_tokens=opts["num_speculative_tokens"],
+                                      ngram_order=opts["speculative_ngram_order"], gpu_layers=args.gpu_layers,
+                                      max_num_batched_tokens=args.batch_size, threads=args.threads)
     load_s = time.perf_counter() - t0
     if pipe.is_embedding:
         print("error: embedding models are served by the HTTP server (/v1/embeddings), not bloom_infer",

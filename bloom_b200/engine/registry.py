@@ -95,4 +95,14 @@ def default_registry() -> EngineRegistry:
     r.register(EngineCapability(
         name="echo", maturity="Experimental", devices=["cpu", "gpu"], families=["Echo"], formats=["Preset"],
         native_dtypes=["F32"]))
+    r.register(EngineCapability(
+        name="qwen3-vl", maturity="Experimental", devices=["gpu"], families=["QwenVL"], formats=["Preset", "Safetensors"],
+        native_dtypes=["BF16"], modalities=["Text", "Vision"]))
+    # external runtimes (explicit --backend only: their availability depends on binaries outside this build)
+    r.register(EngineCapability(
+        name="llamacpp", maturity="Beta", devices=["cpu", "gpu"], families=["*"], formats=["Gguf"],
+        native_dtypes=["F32", "F16", "BF16", "Q8", "Q4"]))
+    r.register(EngineCapability(
+        name="script", maturity="Experimental", devices=["cpu", "gpu"], families=["*"], formats=["Script"],
+        native_dtypes=["F32"], modalities=["Text", "Audio", "Vision"]))
     return r
