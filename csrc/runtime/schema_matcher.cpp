@@ -488,6 +488,7 @@ const std::vector<uint32_t>& SchemaMatcher::mask(const VocabTrie& trie, const st
 }  // namespace bloom
 
 // ---------------------------------------------------------------- Python surface
+#ifndef BLOOM_NO_PYTHON
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
@@ -537,3 +538,4 @@ void register_schema(py::module_& m) {
           },
           py::arg("trie"), py::arg("eos"), py::arg("out"));
 }
+#endif  // BLOOM_NO_PYTHON
