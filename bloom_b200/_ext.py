@@ -1,6 +1,7 @@
 """Loader for the in-tree native extensions.
 
-`cuda()` returns bloom_b200._C (sm_100a kernels).  On a machine with a GPU a
+`cuda()` returns bloom_b200._C (sm_100a kernels), or bloom_b200._C_checked
+(the same kernels built with index checks) when BLOOM_KERNEL_CHECKS=1.  On a machine with a GPU a
 missing or broken extension is an error, never a silent fallback: the engine
 only runs on its own kernels.  `runtime()` returns bloom_b200._runtime (host
 C++ runtime), which imports without a GPU.
@@ -33,7 +34,9 @@ def _load(name: str):
 
 
 def cuda():
-    return _load("_C")
+    import os
+
+    return _load("_C_checked" if os.environ.get("BLOOM_KERNEL_CHECKS", "0") == "1" else "_C")
 
 
 def runtime():

@@ -34,7 +34,9 @@ EPI_GELU_TANH = 6  # tanh approximation ("gelu_pytorch_tanh")
 def status(device: Optional[int] = None) -> torch.Tensor:
     """Per-device int32[16] status word that kernels OR error bits into
     (1: GEMM pipeline wait timed out, 2: attention wait timed out,
-    4: cross-GPU wait timed out, 8: bad argument, 16: MoE buffer overflow)."""
+    4: cross-GPU wait timed out, 8: bad argument, 16: MoE buffer overflow,
+    32: fused collective skipped on a poisoned communicator, 64: an index
+    check failed -- only the BLOOM_KERNEL_CHECKS=1 build checks)."""
     if device is None:
         device = torch.cuda.current_device()
     return _C().status_tensor(int(device))

@@ -19,6 +19,12 @@ symmetric memory would otherwise bind every rendezvoused buffer to one, and a
 rank that dies while bound to it can raise NVLink faults on its peers' GPUs.
 `TORCH_SYMM_MEM_DISABLE_MULTICAST=1` is set before the first allocation and
 every handle is checked to carry no multicast pointer.
+
+Every symmetric buffer carries a 4 KiB guard region before and after its
+data, filled with a fixed word pattern; kernels receive pointers to the data
+only.  `check_canaries()` counts guard words that no longer hold the pattern
+on this rank (a stray P2P store from any rank lands in some rank's guard),
+and the TP tests assert it is zero after every run.
 """
 from __future__ import annotations
 
@@ -33,6 +39,32 @@ import torch.distributed as dist  # noqa: E402
 from .. import ops  # noqa: E402
 from .._ext import cuda as _C  # noqa: E402
 
+CANARY_BYTES = 4096
+CANARY_WORD = 0x5AC3A55A  # as two bf16 halves: finite values, so a guard never reads as NaN
+
+
+def _guarded(symm, numel: int, dtype, device):
+    """(full symmetric tensor, data view, guard elements) with both guards filled."""
+    es = torch.empty(0, dtype=dtype).element_size()
+    g = CANARY_BYTES // es
+    full = symm.empty(numel + 2 * g, dtype=dtype, device=device)
+    words = full.view(torch.int32)
+    gw = CANARY_BYTES // 4
+    words[:gw].fill_(CANARY_WORD)
+    words[words.numel() - gw:].fill_(CANARY_WORD)
+    return full, full[g:g + numel], g
+
+
+def _bad_guard_words(full: torch.Tensor) -> int:
+    words = full.view(torch.int32)
+    gw = CANARY_BYTES // 4
+    return int((words[:gw] != CANARY_WORD).sum().item() + (words[words.numel() - gw:] != CANARY_WORD).sum().item())
+
+
+def _peer(handle, rank: int, full_numel: int, dtype, guard: int) -> int:
+    es = torch.empty(0, dtype=dtype).element_size()
+    return handle.get_buffer(rank, (full_numel,), dtype, 0).data_ptr() + guard * es
+
 
 class FusedComm:
     def __init__(self, rank: int, world: int, device: torch.device, group=None, max_tokens: int = 8192,
@@ -46,23 +78,24 @@ class FusedComm:
         self.hidden = hidden
         n = max_tokens * hidden
         # pushed partials use [world][ceil(T / world)][H] slots: up to world - 1 rows more than T
-        self._P = symm.empty(n + world * hidden, dtype=torch.bfloat16, device=device)
-        self._X = symm.empty(n, dtype=torch.bfloat16, device=device)
+        bf, i32 = torch.bfloat16, torch.int32
+        fP, self._P, gP = _guarded(symm, n + world * hidden, bf, device)
+        fX, self._X, gX = _guarded(symm, n, bf, device)
         fw = int(_C().tp_flag_words())
-        self._F = symm.empty(fw, dtype=torch.int32, device=device)
+        fF, self._F, gF = _guarded(symm, fw, i32, device)
         self._F.zero_()
         # greedy logits: (value, global index) pairs [world][rows + 1] (last entry: a rank's status word)
         self.max_logit_rows = int(max_logit_rows or max_tokens)
         ns = world * (self.max_logit_rows + 1) * 2
-        self._G = symm.empty(ns, dtype=torch.int32, device=device)
+        fG, self._G, gG = _guarded(symm, ns, i32, device)
         self._G.zero_()
+        self._guards = {"partial": fP, "x": fX, "flags": fF, "logit_pairs": fG}
         torch.cuda.synchronize(device)
-        hP = symm.rendezvous(self._P, self.group)
-        hX = symm.rendezvous(self._X, self.group)
-        hF = symm.rendezvous(self._F, self.group)
-        hG = symm.rendezvous(self._G, self.group)
+        hP = symm.rendezvous(fP, self.group)
+        hX = symm.rendezvous(fX, self.group)
+        hF = symm.rendezvous(fF, self.group)
+        hG = symm.rendezvous(fG, self.group)
         self._handles = (hP, hX, hF, hG)
-        self.g_ptrs = [hG.get_buffer(r, (ns,), torch.int32, 0).data_ptr() for r in range(world)]
         self._full = None  # lazily: full-vocabulary logits rows for stochastic sampling
         self.poisoned = False
         for h in self._handles:
@@ -70,10 +103,17 @@ class FusedComm:
             if mc:
                 raise RuntimeError("symmetric-memory buffer is bound to an NVLink multicast object although "
                                    "TORCH_SYMM_MEM_DISABLE_MULTICAST=1; refusing to run the fused collectives")
-        self.p_ptrs = [hP.get_buffer(r, (n + world * hidden,), torch.bfloat16, 0).data_ptr() for r in range(world)]
-        self.x_ptrs = [hX.get_buffer(r, (n,), torch.bfloat16, 0).data_ptr() for r in range(world)]
-        self.f_ptrs = [hF.get_buffer(r, (fw,), torch.int32, 0).data_ptr() for r in range(world)]
+        self.g_ptrs = [_peer(hG, r, fG.numel(), i32, gG) for r in range(world)]
+        self.p_ptrs = [_peer(hP, r, fP.numel(), bf, gP) for r in range(world)]
+        self.x_ptrs = [_peer(hX, r, fX.numel(), bf, gX) for r in range(world)]
+        self.f_ptrs = [_peer(hF, r, fF.numel(), i32, gF) for r in range(world)]
         dist.barrier(group=self.group)
+
+    def check_canaries(self) -> dict:
+        """Guard words of this rank's symmetric buffers that lost their pattern
+        (0 everywhere when no kernel wrote outside a buffer).  Synchronises."""
+        torch.cuda.synchronize(self.device)
+        return {k: _bad_guard_words(v) for k, v in self._guards.items()}
 
     def can_all_reduce(self, t: torch.Tensor) -> bool:
         return False  # the fused path is taken through allreduce_rmsnorm, not a bare all-reduce
@@ -124,17 +164,18 @@ class FusedComm:
         V = Vl * self.world
         if self._full is None or self._full[1] < NL or self._full[2] != V:
             rows = max(NL, self.max_logit_rows)
-            L = symm.empty(rows * V, dtype=torch.bfloat16, device=self.device)
-            S = symm.empty(self.world, dtype=torch.int32, device=self.device)
+            fL, L, gL = _guarded(symm, rows * V, torch.bfloat16, self.device)
+            fS, S, gS = _guarded(symm, self.world, torch.int32, self.device)
             S.zero_()
+            self._guards["logit_rows"], self._guards["logit_status"] = fL, fS
             torch.cuda.synchronize(self.device)
-            hL = symm.rendezvous(L, self.group)
-            hS = symm.rendezvous(S, self.group)
+            hL = symm.rendezvous(fL, self.group)
+            hS = symm.rendezvous(fS, self.group)
             for h in (hL, hS):
                 if getattr(h, "multicast_ptr", 0):
                     raise RuntimeError("symmetric-memory buffer is bound to an NVLink multicast object")
-            lp = [hL.get_buffer(r, (rows * V,), torch.bfloat16, 0).data_ptr() for r in range(self.world)]
-            sp = [hS.get_buffer(r, (self.world,), torch.int32, 0).data_ptr() for r in range(self.world)]
+            lp = [_peer(hL, r, fL.numel(), torch.bfloat16, gL) for r in range(self.world)]
+            sp = [_peer(hS, r, fS.numel(), torch.int32, gS) for r in range(self.world)]
             self._full = (L, rows, V, lp, sp, (hL, hS))
         L, rows, V, lp, sp, _ = self._full
         _C().tp_gather_cols(logits.contiguous(), lp, V, sp, self.f_ptrs, self.rank, out_status, self.timeout_s,

@@ -6,6 +6,12 @@
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 sm_100a kernels";
+#ifdef BLOOM_KERNEL_CHECKS
+  m.attr("KERNEL_CHECKS") = true;
+#else
+  m.attr("KERNEL_CHECKS") = false;
+#endif
+  m.attr("STATUS_INDEX_CHECK") = 1 << 6;  // kStatusIndexCheck in bloom/common.cuh
   m.attr("EPI_BF16") = int(bloom::kEpiBF16);
   m.attr("EPI_F32") = int(bloom::kEpiF32);
   m.attr("EPI_SWIGLU") = int(bloom::kEpiSwiGLU);

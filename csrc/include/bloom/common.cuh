@@ -27,7 +27,23 @@ enum StatusBits : int {
   // a fused collective found its communicator poisoned by an earlier timeout
   // and did nothing (the host must fail the step and stop using it)
   kStatusCommPoisoned = 1 << 5,
+  // an index read from a table (block id, cache slot, token id, expert row)
+  // was out of range; only builds with -DBLOOM_KERNEL_CHECKS look
+  kStatusIndexCheck = 1 << 6,
 };
+
+// Index checks compiled in by -DBLOOM_KERNEL_CHECKS (the bloom_b200._C_checked
+// extension): kcheck(ok, status) records a failed check in the status word
+// and returns ok, so the caller skips the access.  In the regular build it is
+// the constant true and costs nothing.
+#ifdef BLOOM_KERNEL_CHECKS
+__device__ __forceinline__ bool kcheck(bool ok, int* status) {
+  if (!ok && status != nullptr) atomicOr(status, kStatusIndexCheck);
+  return ok;
+}
+#else
+__device__ __forceinline__ constexpr bool kcheck(bool, int*) { return true; }
+#endif
 
 // Local (same-GPU) pipeline waits never legitimately take this long.
 constexpr uint64_t kLocalWaitTimeoutNs = 2000000000ull;  // 2 s

@@ -151,5 +151,15 @@ void mean_pool_l2(const torch::Tensor& x, const torch::Tensor& cu_seqlens, torch
 
 // Status word.
 torch::Tensor status_tensor(int64_t device);
+// Status word for kernels' index checks: only builds with -DBLOOM_KERNEL_CHECKS
+// pass one (the regular build passes nullptr and its kernels never look).
+inline int* check_word(int64_t device) {
+#ifdef BLOOM_KERNEL_CHECKS
+  return status_tensor(device).data_ptr<int>();
+#else
+  (void)device;
+  return nullptr;
+#endif
+}
 
 }  // namespace bloom

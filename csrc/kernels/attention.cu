@@ -79,6 +79,7 @@ struct DecodeArgs {
   int hc;               // CTAs per KV head, each taking G / hc of its q heads (G * ql > 32)
   float scale_log2;
   int* status;
+  int num_blocks;       // pages in the cache (index checks only)
 };
 
 // Row r of the packed M dimension -> (q position qi, head-in-group hh).
@@ -118,7 +119,8 @@ __global__ void __launch_bounds__(NWARPS * 32)
   auto issue = [&](int i) {
     const int s = i % NST;
     const int page = first + i * NWARPS;
-    const int blk = bt[page];
+    int blk = bt[page];
+    if (!kcheck(blk >= 0 && blk < a.num_blocks, a.status)) blk = 0;
     const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
     const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
     uint8_t* st = wsm + s * kStageBytes;
@@ -358,6 +360,7 @@ struct PrefillArgs {
   float scale_log2;
   int causal;
   int* status;
+  int num_blocks;          // pages in the cache (index checks only)
 };
 
 constexpr int kPfWarps = 4;
@@ -410,7 +413,8 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 #pragma unroll
     for (int pg = 0; pg < 4; ++pg) {
       const int page = kt * 4 + pg;
-      const int blk = bt[page < n_pages ? page : 0];
+      int blk = bt[page < n_pages ? page : 0];
+      if (!kcheck(blk >= 0 && blk < a.num_blocks, a.status)) blk = 0;
       const int rowK = ((blk * 2 + 0) * a.nkv + kh) * PAGE;
       const int rowV = ((blk * 2 + 1) * a.nkv + kh) * PAGE;
       tma_load_2d(st + pg * kPageB, &tmKV, &bars[s], 0, rowK);
@@ -643,6 +647,7 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
   a.splits = std::max<int>(1, int(splits));
   a.scale_log2 = float(scale * 1.4426950408889634);
   a.status = status.data_ptr<int>();
+  a.num_blocks = int(kv_cache.size(1));
   a.part = nullptr;
   if (a.splits > 1) {
     TORCH_CHECK(workspace.scalar_type() == at::kFloat &&
@@ -699,6 +704,7 @@ void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cac
   a.scale_log2 = float(scale * 1.4426950408889634);
   a.causal = causal ? 1 : 0;
   a.status = status.data_ptr<int>();
+  a.num_blocks = int(kv_cache.size(1));
   const CUtensorMap tm = attn::kv_tmap(kv_cache, layer);
   constexpr int smem128 = attn::kPfStages * attn::pf_stage_bytes<128>() + 64 + 1024;
   constexpr int smem64 = attn::kPfStages * attn::pf_stage_bytes<64>() + 64 + 1024;

@@ -65,6 +65,7 @@ struct Args {
   float scale_log2;
   int causal;
   int* status;
+  int num_blocks;          // pages in the cache (index checks only)
   // optional per-CTA profile (CTA = blockIdx.y * gridDim.x + blockIdx.x, 16
   // words each, CTAs past trace_ctas skipped): [0] %globaltimer at entry,
   // [1] at exit, [2] clock64 cycles of the kv loop, [3..9] cycles of thread 0
@@ -198,6 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int pg = 0; pg < kKv / PAGE; ++pg) {
           const int page = jt * (kKv / PAGE) + pg;
           ids[pg] = __ldg(bt + (page < n_pages ? page : 0));
+          if (!kcheck(ids[pg] >= 0 && ids[pg] < a.num_blocks, a.status)) ids[pg] = 0;
         }
       };
       auto load_tile = [&](const int (&ids)[kKv / PAGE], uint8_t* dst, uint64_t* bar, int kv) {
@@ -554,6 +556,7 @@ void paged_prefill_attention_tc(const torch::Tensor& q, const torch::Tensor& kv_
   a.scale_log2 = float(scale * 1.4426950408889634);
   a.causal = causal ? 1 : 0;
   a.status = status.data_ptr<int>();
+  a.num_blocks = int(kv_cache.size(1));
   a.trace = g_attn_tc_trace;
   a.trace_ctas = g_attn_tc_trace_ctas;
   const uint64_t rows = (uint64_t)kv_cache.size(1) * 2 * kv_cache.size(3) * attn_tc::PAGE;

@@ -141,7 +141,7 @@ __global__ void moe_plan_kernel(int* __restrict__ counts, int El, int* __restric
 __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int H, int K, int e0, int El,
                                   const int* __restrict__ topk_ids, const int* __restrict__ slot,
                                   const int* __restrict__ offsets, int* __restrict__ pos,
-                                  __nv_bfloat16* __restrict__ xs) {
+                                  __nv_bfloat16* __restrict__ xs, long xs_rows, int* status) {
   const int t = blockIdx.x;
   const uint4* src = reinterpret_cast<const uint4*>(x + (long)t * H);
   for (int j = 0; j < K; ++j) {
@@ -151,7 +151,15 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int H, in
       continue;
     }
     const int e = topk_ids[(long)t * K + j] - e0;
+    if (!kcheck(e >= 0 && e < El, status)) {
+      if (threadIdx.x == 0) pos[(long)t * K + j] = -1;
+      continue;
+    }
     const int r = offsets[e] + s;
+    if (!kcheck(r >= 0 && r < xs_rows, status)) {
+      if (threadIdx.x == 0) pos[(long)t * K + j] = -1;
+      continue;
+    }
     if (threadIdx.x == 0) pos[(long)t * K + j] = r;
     uint4* dst = reinterpret_cast<uint4*>(xs + (long)r * H);
     for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
@@ -159,13 +167,14 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int H, in
 }
 
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ ys, int H, int K, const int* __restrict__ pos,
-                                   const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out) {
+                                   const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out, long ys_rows,
+                                   int* status) {
   const int t = blockIdx.x;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     float acc = 0.f;
     for (int j = 0; j < K; ++j) {
       const int r = pos[(long)t * K + j];
-      if (r >= 0) acc += topk_w[(long)t * K + j] * __bfloat162float(ys[(long)r * H + i]);
+      if (r >= 0 && kcheck(r < ys_rows, status)) acc += topk_w[(long)t * K + j] * __bfloat162float(ys[(long)r * H + i]);
     }
     out[(long)t * H + i] = __float2bfloat16(acc);
   }
@@ -209,7 +218,8 @@ void moe_gather(const torch::Tensor& x, int64_t e0, int64_t e_local, const torch
   const at::cuda::CUDAGuard g(x.device());
   moe_gather_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), H, K, int(e0), int(e_local), topk_ids.data_ptr<int>(),
-      slot.data_ptr<int>(), offsets.data_ptr<int>(), pos.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()));
+      slot.data_ptr<int>(), offsets.data_ptr<int>(), pos.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()),
+      long(xs.numel() / H), check_word(x.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -219,7 +229,7 @@ void moe_combine(const torch::Tensor& ys, const torch::Tensor& pos, const torch:
   const at::cuda::CUDAGuard g(out.device());
   moe_combine_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr()), H, K, pos.data_ptr<int>(), topk_w.data_ptr<float>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), long(ys.numel() / H), check_word(out.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

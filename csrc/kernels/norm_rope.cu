@@ -182,10 +182,11 @@ __global__ void layernorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv
 }
 
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, long V,
-                                 int H, __nv_bfloat16* __restrict__ out) {
+                                 int H, __nv_bfloat16* __restrict__ out, int* status) {
   const long t = blockIdx.x;
   const long id = ids[t];
-  const bool ok = id >= 0 && id < V;
+  const bool ok = id >= 0 && id < V;  // always bounded: an unknown id embeds as zeros
+  if (threadIdx.x == 0) kcheck(ok, status);
   // 16-byte vectors when H is a multiple of 8
   if ((H & 7) == 0) {
     const uint4* src = reinterpret_cast<const uint4*>(table + (ok ? id : 0) * H);
@@ -207,14 +208,16 @@ __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, long
                                      const int* __restrict__ slots, const float* __restrict__ cos_sin,
                                      __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
                                      long layer_stride, int nq, int nkv, const __nv_bfloat16* __restrict__ qn,
-                                     const __nv_bfloat16* __restrict__ kn, float eps, long max_pos) {
+                                     const __nv_bfloat16* __restrict__ kn, float eps, long max_pos,
+                                     long cache_slots, int* status) {
   constexpr int NV = D / 32;  // values per lane: dims lane + 32 i
   const long t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   long p = pos[t];
   p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);  // the table bounds every read
-  const int slot = slots != nullptr ? slots[t] : -1;
+  int slot = slots != nullptr ? slots[t] : -1;
+  if (slot >= 0 && !kcheck(slot < cache_slots, status)) slot = -1;
   const float* cs = cos_sin + p * D;  // [cos(D/2) | sin(D/2)]
   const __nv_bfloat16* row = qkv + t * ldq;
   for (int h = warp; h < nq + 2 * nkv; h += nwarps) {
@@ -355,7 +358,7 @@ void embedding(const torch::Tensor& ids, const torch::Tensor& table, torch::Tens
   const at::cuda::CUDAGuard g(ids.device());
   embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), table.size(0), table.size(1),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), check_word(ids.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -386,7 +389,7 @@ void rope_kv_write(const torch::Tensor& qkv, const torch::Tensor& positions, con
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),
       slot_mapping.data_ptr<int>(), cos_sin.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(kv_cache.data_ptr()), layer_stride, int(num_q_heads), int(num_kv_heads), qn,
-      kn, float(eps), cos_sin.size(0));
+      kn, float(eps), cos_sin.size(0), kv_cache.size(1) * 16, check_word(qkv.device().index()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -6,6 +6,12 @@ Builds
   bloom_b200/_C        CUDA kernels, compiled for sm_100a only
   bloom_b200/_runtime  C++ host runtime (scheduler, KV block manager, GGUF,
                        CPU kernels); no CUDA dependency so it imports anywhere
+  bloom_b200/_C_checked  (BLOOM_BUILD=checked, in its own build folder:
+                       `--build-temp build/temp_checked`) the CUDA kernels with
+                       -DBLOOM_KERNEL_CHECKS: table indices (KV block ids, cache
+                       slots, token ids, expert rows) are checked, a bad one sets
+                       a status bit and its access is skipped.  Loaded instead of
+                       _C when BLOOM_KERNEL_CHECKS=1.
 """
 import glob
 import os
@@ -52,6 +58,16 @@ def extensions(which=("cuda", "runtime")):
                 cuda_sources(),
                 include_dirs=INC,
                 extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+            )
+        )
+    if "checked" in which:
+        exts.append(
+            CUDAExtension(
+                "bloom_b200._C_checked",
+                cuda_sources(),
+                include_dirs=INC,
+                extra_compile_args={"cxx": CXX_FLAGS + ["-DBLOOM_KERNEL_CHECKS"],
+                                    "nvcc": NVCC_FLAGS + ["-DBLOOM_KERNEL_CHECKS"]},
             )
         )
     if "runtime" in which:

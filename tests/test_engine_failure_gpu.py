@@ -42,6 +42,7 @@ def _fake_two_rank_fused(dev, T, H, timeout_s):
     fc.f_ptrs = [fc._F.data_ptr(), peerF.data_ptr()]
     fc.g_ptrs = [fc._G.data_ptr(), peerG.data_ptr()]
     fc._full = None
+    fc._guards = {}
     fc.poisoned = False
     fc._keep = keep
     return fc

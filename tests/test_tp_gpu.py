@@ -25,6 +25,7 @@ def _run(n, mode, graphs="graphs", model="tiny-tp", port=29611, extra_env=None):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads(lines[-1])
     assert res["ok"] and res["ranks_agree"] and res["status"] == 0, res
+    assert res["bad_guard_words"] == 0, res
     return res
 
 
@@ -40,7 +41,8 @@ def test_tp_nccl_eager(n):
 
 @pytest.mark.parametrize("n", [2, 4, 8])
 def test_tp_fused(n):
-    _run(n, "fused", port=29651 + n)
+    res = _run(n, "fused", port=29651 + n)
+    assert {"partial", "x", "flags", "logit_pairs", "logit_rows"} <= set(res["guards_checked"]), res
 
 
 @pytest.mark.parametrize("n", [2, 8])

@@ -55,13 +55,18 @@ def main():
     dist.all_gather(allt, toks)
     same = all(torch.equal(allt[0], t) for t in allt)
     status = int(ops.status(local)[0].item())
+    # guard words around every symmetric buffer: a stray P2P store by any rank shows up here
+    canaries = comm.fused.check_canaries() if comm.fused is not None else {}
+    bad = torch.tensor([sum(canaries.values())], device=dev)
+    dist.all_reduce(bad)
     eng.shutdown()
     if rank == 0:
         print(json.dumps({"ok": ok, "ranks_agree": same, "worst_gap": worst, "status": status,
-                          "graph_steps": eng.runner.stats["graph_steps"]}), flush=True)
+                          "graph_steps": eng.runner.stats["graph_steps"], "bad_guard_words": int(bad.item()),
+                          "guards_checked": sorted(canaries)}), flush=True)
     dist.barrier()
     dist.destroy_process_group()
-    sys.exit(0 if (ok and same and status == 0) else 1)
+    sys.exit(0 if (ok and same and status == 0 and int(bad.item()) == 0) else 1)
 
 
 if __name__ == "__main__":
