@@ -119,6 +119,10 @@ class EngineConfig:
     # swap preemption: pinned host bytes that preempted sequences' KV blocks are
     # copied into (resumed without recompute); 0 = recompute preemption only
     swap_space_bytes: int = 0
+    # deterministic replay: write every scheduler call, its clock and its
+    # result to this JSON-lines file ("{rank}" expands to the TP rank; also
+    # BLOOM_STEP_LOG); `python -m bloom_b200.engine.replay <file>` re-runs it
+    step_log: str = ""
 
 
 VICTIM_POLICIES = {"newest": 0, "priority": 1, "oldest": 2, "kv_cost": 3, "aegaeon": 4, "lru": 5, "largest_first": 6}
@@ -182,6 +186,13 @@ class LLMEngine:
         swap_slots = int(ec.swap_space_bytes) // kv_block_bytes(model) if ec.swap_space_bytes > 0 else 0
         sc.swap_slots = swap_slots
         self.scheduler = rt.Scheduler(sc, ec.num_blocks, 16, ec.enable_prefix_caching)
+        log = ec.step_log or os.environ.get("BLOOM_STEP_LOG", "")
+        if log:
+            from .replay import SchedulerRecorder
+
+            rank = model.tp.rank if getattr(model, "tp", None) is not None else 0
+            self.scheduler = SchedulerRecorder(self.scheduler, log.replace("{rank}", str(rank)), sc, ec.num_blocks,
+                                               16, ec.enable_prefix_caching)
         self.runner = ModelRunner(model, ec.num_blocks, ec.max_num_seqs, ec.max_num_batched_tokens,
                                   ec.max_model_len, ec.use_cuda_graphs, spec_len=int(ec.spec_len))
         if ec.autotune and dev.type == "cuda":
