@@ -17,11 +17,15 @@ from __future__ import annotations
 
 import asyncio
 import itertools
+import logging
+import os
 import queue
 import threading
 import time
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional
+
+log = logging.getLogger("bloom_b200.server.runtime")
 
 _ids = itertools.count(1)
 
@@ -58,7 +62,10 @@ class TPControl:
     and aborts; the other ranks apply the same calls in the same order (so the
     replicated C++ schedulers assign the same ids and schedule the same rows)
     and step with it.  Messages travel over a gloo (CPU) process group; an
-    idle rank 0 sends a heartbeat every second."""
+    idle rank 0 sends an empty message every second.  Independently, every
+    rank beats into the rendezvous store (parallel/heartbeat.py), so a rank
+    that died or stopped stepping is noticed within BLOOM_HEARTBEAT_STALE_S
+    (default 10 s) even while the exchange is blocked on it."""
 
     def __init__(self, group=None):
         import torch.distributed as dist
@@ -66,6 +73,18 @@ class TPControl:
         self.dist = dist
         self.group = group if group is not None else dist.new_group(backend="gloo")
         self.rank = dist.get_rank()
+        self.heartbeat = None
+
+    def start_heartbeat(self, on_lost) -> None:
+        from ..parallel.heartbeat import Heartbeat
+
+        store = self.dist.distributed_c10d._get_default_store()
+        self.heartbeat = Heartbeat(store, self.rank, self.dist.get_world_size(), on_lost,
+                                   stale_s=float(os.environ.get("BLOOM_HEARTBEAT_STALE_S", "10"))).start()
+
+    def tick(self) -> None:
+        if self.heartbeat is not None:
+            self.heartbeat.tick()
 
     def exchange(self, msg=None):
         obj = [msg]
@@ -78,9 +97,13 @@ def follower_loop(engine, ctrl: TPControl) -> None:
     If rank 0 is gone, the exchange raises (connection closed, or the process
     group's timeout) and so does this loop: the rank exits with an error
     instead of waiting for a leader that never speaks again."""
+    if getattr(ctrl, "heartbeat", None) is None and hasattr(ctrl, "start_heartbeat"):
+        ctrl.start_heartbeat(lambda r, why: log.error("tensor-parallel rank lost: %s", why))
     while True:
         msg = ctrl.exchange(None)
         if msg.get("stop"):
+            if getattr(ctrl, "heartbeat", None) is not None:
+                ctrl.heartbeat.stop()
             return
         for prompt, params, prio in msg.get("add", []):
             engine.add_request(prompt, params, prio)
@@ -90,6 +113,8 @@ def follower_loop(engine, ctrl: TPControl) -> None:
             for r in engine.step():
                 if r.finished:
                     engine.requests.pop(r.request_id, None)
+            if hasattr(ctrl, "tick"):
+                ctrl.tick()
 
 
 # request class -> engine scheduler priority (higher first); classes follow the
@@ -159,6 +184,8 @@ class ServingRuntime:
         self._held: Dict[str, Submission] = {}
         dev = getattr(getattr(self.engine, "model", None), "device", None)
         self.thermal = ThermalMonitor(getattr(dev, "index", None) if dev is not None else None)
+        if ctrl is not None and getattr(ctrl, "heartbeat", None) is None and hasattr(ctrl, "start_heartbeat"):
+            ctrl.start_heartbeat(lambda r, why: self._peer_lost(f"tensor-parallel peer lost: {why}"))
         self._thread = threading.Thread(target=self._loop, name="bloom-engine", daemon=True)
         self._thread.start()
 
@@ -208,6 +235,8 @@ class ServingRuntime:
         self._thread.join(timeout=10)
         if self.ctrl is not None and self.engine is not None and self.broken is None:
             self.ctrl.exchange({"stop": True})
+        if getattr(self.ctrl, "heartbeat", None) is not None:
+            self.ctrl.heartbeat.stop()
 
     # ------------------------------------------------------------ engine thread
     def _emit(self, sub: Submission, item: StreamItem) -> None:
@@ -277,8 +306,12 @@ class ServingRuntime:
                 self._wake.wait(timeout=0.05)
                 self._wake.clear()
                 continue
+            if self.broken is not None:  # the heartbeat reported a lost peer
+                return
             try:
                 outs = eng.step()
+                if ctrl is not None and hasattr(ctrl, "tick"):
+                    ctrl.tick()
             except Exception as e:  # a failed step fails every request in it (reference mod.rs:1862-1907)
                 with self._lock:
                     subs = list(self._by_rid.values())
@@ -325,6 +358,8 @@ class ServingRuntime:
         """No collective can complete any more: every in-flight and queued
         request ends with an error, readiness goes false and new submissions
         are refused with the same reason.  The engine is not stepped again."""
+        if self.broken is not None:
+            return
         self.broken = reason
         self.ready = False
         with self._lock:
