@@ -81,6 +81,8 @@ def main(argv=None) -> None:
     ap.add_argument("--ffn", type=int, default=14336)
     ap.add_argument("--iters", type=int, default=32)
     ap.add_argument("--out", default="")
+    ap.add_argument("--trace", action="store_true",
+                    help="also print the phase timeline of block 0 (entry, ready, rows written, done)")
     args = ap.parse_args(argv)
 
     from bloom_b200 import ops
@@ -125,6 +127,29 @@ def main(argv=None) -> None:
                                            args.iters), 0.0, ag_bytes)
         report("coll_pull", T, _time_graph(lambda: fc.allreduce_rmsnorm(T, r_T, norm_w, 1e-5, pushed=False),
                                            args.iters), 0.0, ag_bytes + rs_bytes)
+        if args.trace:
+            from bloom_b200._ext import cuda
+
+            cap = 64
+            tb = torch.zeros(cap * 4, dtype=torch.int64, device=dev)
+            cuda().tp_ar_set_trace(tb)
+            fn = (lambda: fc.allreduce_rmsnorm(T, r_T, norm_w, 1e-5, pushed=True))
+            _time_graph(fn, cap)
+            cuda().tp_ar_set_trace(None)
+            tr = tb.view(cap, 4).cpu().double()
+            ok = (tr > 0).all(1)
+            tr = tr[ok]
+            if tr.shape[0] > 2:
+                order = tr[:, 0].argsort()
+                tr = tr[order]
+                ph = {"ready_us": (tr[:, 1] - tr[:, 0]), "rows_us": (tr[:, 2] - tr[:, 1]),
+                      "done_us": (tr[:, 3] - tr[:, 2]), "period_us": (tr[1:, 0] - tr[:-1, 0])}
+                med = {k: round(float(v.median()) / 1000.0, 2) for k, v in ph.items()}
+                allm = [None] * world
+                dist.all_gather_object(allm, med)
+                if rank == 0:
+                    print(json.dumps({"case": "coll_push_trace", "world": world, "T": T, "per_rank": allm}),
+                          flush=True)
         buf = part[:T].clone()
         xo = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
 

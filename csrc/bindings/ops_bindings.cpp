@@ -31,6 +31,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_default_splits", &bloom::gemm_default_splits);
   m.def("gemm_max_active_clusters", &bloom::gemm_max_active_clusters, "resident clusters of the one-CTA GEMM");
   m.def("attn_tc_set_trace", &bloom::attn_tc_set_trace, "per-CTA phase profile of tcgen05 prefill launches (None = off)");
+  m.def("tp_ar_set_trace", &bloom::tp_ar_set_trace, "phase timeline of tp_allreduce_rmsnorm block 0 (None = off)");
   m.def("gemm_set_trace", &bloom::gemm_set_trace, "per-CTA %globaltimer timeline of plain GEMM launches (None = off)");
   m.def("gemm_fixup_ws_floats", &bloom::gemm_fixup_ws_floats);
   m.def("rmsnorm", &bloom::rmsnorm);

@@ -28,6 +28,7 @@ int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits, int64_t bn_ov
 int gemm_pick_bn(int M);
 int gemm_default_splits(int M, int N, int K, int device);
 void gemm_set_trace(const c10::optional<torch::Tensor>& buf);
+void tp_ar_set_trace(const c10::optional<torch::Tensor>& buf);
 void attn_tc_set_trace(const c10::optional<torch::Tensor>& buf);
 int gemm_max_active_clusters(int64_t bn, int64_t cluster_size);
 

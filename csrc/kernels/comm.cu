@@ -7,8 +7,12 @@
 //     B. for the token rows this rank owns, sums the partials of all ranks with
 //        16-byte P2P loads, adds the residual, applies RMSNorm,
 //     C. writes the normalised rows into every rank's input buffer with 16-byte
-//        P2P stores (the all-gather), then the last CTA waits (bounded) until
-//        every peer finished writing into this rank's buffer.
+//        P2P stores (the all-gather), then every block waits (bounded) until
+//        the same block of every peer finished writing into this rank's buffer.
+//   Each block synchronises only with the same block index on the peers (its
+//   own ready / done / epoch words), so a launch has no CTA counter and no
+//   serial last-CTA hand-off, and the kernel is launched with programmatic
+//   stream serialisation so its start overlaps the producing GEMM's tail.
 //   That is reduce-scatter + residual + RMSNorm + all-gather in one launch, and
 //   every byte crosses NVLink once per direction: 2 (t-1)/t * T * H * 2 bytes.
 //
@@ -54,7 +58,15 @@ struct Peers {
 //   [17]      cta counter  local: CTAs of the current launch that finished
 //   [18]      poison       local: nonzero once a wait of this rank timed out
 constexpr int kReady = 0, kDone = 8, kEpoch = 16, kCtaCount = 17, kPoison = 18;
-constexpr int kFlagWords = 32;
+// Per-block flags of tp_allreduce_rmsnorm (block b of a launch pairs only with
+// block b of every peer, so no CTA counter and no last-CTA hand-off):
+//   [kBlkReady + src * kMaxArBlocks + b]  written by peer src's block b: its partials are complete
+//   [kBlkDone  + src * kMaxArBlocks + b]  written by peer src's block b: its all-gather stores here are complete
+//   [kBlkEpoch + b]                       local: completed launches that had a block b
+constexpr int kMaxArBlocks = 2 * 148;
+constexpr int kBlkReady = 32, kBlkDone = kBlkReady + kMaxRanks * kMaxArBlocks,
+              kBlkEpoch = kBlkDone + kMaxRanks * kMaxArBlocks;
+constexpr int kFlagWords = ((kBlkEpoch + kMaxArBlocks + 63) / 64) * 64;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -92,6 +104,15 @@ __device__ bool wait_flags(const uint32_t* flags, int base, int world, uint32_t 
   return true;
 }
 
+// Bounded wait until *flag >= target.
+__device__ bool wait_flag(const uint32_t* flag, uint32_t target, uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys(flag) < target) {
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+  return true;
+}
+
 struct ARArgs {
   Peers partial;  // bf16 [T, H] partial sums, one buffer per rank
   Peers xout;     // bf16 [T, H] normalised output, one buffer per rank (all-gathered)
@@ -107,6 +128,11 @@ struct ARArgs {
   // (reduce-scatter fused into the GEMM epilogue); phase B then reads local
   // memory only.  0: partials are [T, H] in each rank's own buffer (pulled).
   int pushed;
+  // optional phase timeline of block 0 (tp_ar_set_trace): 4 %globaltimer
+  // stamps per launch -- entry, ready wait passed, rows written, done wait
+  // passed -- at [(epoch % trace_cap) * 4]
+  unsigned long long* trace;
+  int trace_cap;
 };
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
@@ -146,32 +172,48 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // held to the 64 registers a 1024-thread block can have)
 __global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs a) {
   __shared__ float red[33];
-  __shared__ int ok_s, last_s;
-  __shared__ uint32_t epoch_s;
+  __shared__ int ok_s, fail_s;
+  __shared__ uint32_t target_s;
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(a.flags.p[a.rank]);
+  const int blk = blockIdx.x;
+  // Launched with programmatic stream serialisation: nothing before this wait
+  // may read what an earlier kernel writes (the previous collective may still
+  // be finishing when the producing GEMM lets this launch start), so the
+  // poison word, this block's epoch, the partials and the residual are all
+  // read after it.
+  griddep_wait();
+  griddep_launch_dependents();  // the next GEMM may stage its weights meanwhile
   if (threadIdx.x == 0) {
-    epoch_s = my_flags[kEpoch];
     ok_s = poisoned(my_flags) ? 0 : 1;
+    fail_s = 0;
     if (!ok_s) atomicOr(a.status, kStatusCommPoisoned);
+    target_s = my_flags[kBlkEpoch + blk] + 1;
   }
   __syncthreads();
   if (!ok_s) return;  // poisoned communicator: touch nothing
-  const uint32_t target = epoch_s + 1;
-  // A. every CTA announces readiness (idempotent) so no CTA depends on another being scheduled
-  if (threadIdx.x < a.world)
-    st_release_sys(reinterpret_cast<uint32_t*>(a.flags.p[threadIdx.x]) + kReady + a.rank, target);
-  if (threadIdx.x == 0) {
-    if (!wait_flags(my_flags, kReady, a.world, target, a.timeout_ns)) {
-      ok_s = 0;
-      poison(my_flags, a.status);
-    }
+  const uint32_t target = target_s;
+  const bool tr = a.trace != nullptr && blk == 0 && threadIdx.x == 0;
+  unsigned long long* trs = tr ? a.trace + (target % a.trace_cap) * 4 : nullptr;
+  if (tr) trs[0] = globaltimer_ns();
+  // A. this block tells block `blk` of every rank that this rank's partials are
+  // complete (the producing GEMM finished before this launch), and thread r
+  // waits for rank r's signal: one flag pair per (block, rank), no CTA counter
+  if (threadIdx.x < a.world) {
+    const int r = threadIdx.x;
+    st_release_sys(reinterpret_cast<uint32_t*>(a.flags.p[r]) + kBlkReady + a.rank * kMaxArBlocks + blk, target);
+    if (!wait_flag(my_flags + kBlkReady + r * kMaxArBlocks + blk, target, a.timeout_ns)) fail_s = 1;
   }
   __syncthreads();
+  if (fail_s) {
+    if (threadIdx.x == 0) poison(my_flags, a.status);
+    return;
+  }
+  if (tr) trs[1] = globaltimer_ns();
   const int i = threadIdx.x * 8;
   const bool active = i < a.H;
   float wf[8];
   if (active) bf16x8_to_f32(*reinterpret_cast<const uint4*>(a.w + i), wf);
-  for (int lr = blockIdx.x; ok_s && lr < a.rows_per_rank; lr += gridDim.x) {
+  for (int lr = blk; lr < a.rows_per_rank; lr += gridDim.x) {
     const int row = a.rank * a.rows_per_rank + lr;
     if (row >= a.T) break;
     // B. reduce this rank's rows over all ranks' partials, residual add, RMSNorm
@@ -218,9 +260,24 @@ __global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs
           *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.xout.p[r]) + (long)row * a.H + i) = o;
     }
   }
-  __threadfence_system();
+  // D. the block's stores (all threads, ordered before the release by the
+  // barrier; release is cumulative) are announced to block `blk` of every
+  // rank, and thread r waits until rank r's block `blk` finished writing here.
+  // Every rank launches the same grid, so when all blocks pass, every row of
+  // this rank's input buffer has arrived.
   __syncthreads();
-  if (threadIdx.x == 0) finish_collective(my_flags, a.flags.p, a.rank, a.world, target, a.timeout_ns, a.status, &last_s);
+  if (tr) trs[2] = globaltimer_ns();
+  if (threadIdx.x < a.world) {
+    const int r = threadIdx.x;
+    st_release_sys(reinterpret_cast<uint32_t*>(a.flags.p[r]) + kBlkDone + a.rank * kMaxArBlocks + blk, target);
+    if (!wait_flag(my_flags + kBlkDone + r * kMaxArBlocks + blk, target, a.timeout_ns)) fail_s = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (fail_s) poison(my_flags, a.status);
+    else my_flags[kBlkEpoch + blk] = target;  // stream order makes the next launch see it
+    if (tr) trs[3] = globaltimer_ns();
+  }
 }
 
 // All-gather of row slices: rank r owns rows [r*rows_per_rank, ...) of src (local,
@@ -482,6 +539,19 @@ Peers to_peers(const std::vector<int64_t>& v) {
 
 int64_t tp_flag_words() { return comm::kFlagWords; }
 
+static unsigned long long* g_ar_trace = nullptr;
+static int g_ar_trace_cap = 0;
+void tp_ar_set_trace(const c10::optional<torch::Tensor>& buf) {
+  if (buf.has_value() && buf->defined()) {
+    TORCH_CHECK(buf->scalar_type() == at::kLong && buf->is_cuda() && buf->numel() >= 4, "trace: int64 [n * 4] CUDA");
+    g_ar_trace = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    g_ar_trace_cap = static_cast<int>(buf->numel() / 4);
+  } else {
+    g_ar_trace = nullptr;
+    g_ar_trace_cap = 0;
+  }
+}
+
 void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::vector<int64_t>& x_ptrs,
                           const std::vector<int64_t>& flag_ptrs, int64_t rank, torch::Tensor& residual,
                           const torch::Tensor& w, double eps, int64_t T, double timeout_s,
@@ -508,12 +578,27 @@ void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::v
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   a.status = status.data_ptr<int>();
   a.pushed = pushed ? 1 : 0;
+  a.trace = g_ar_trace;
+  a.trace_cap = g_ar_trace_cap;
   const int threads = ((H / 8 + 31) / 32) * 32;
   // a fixed, fully resident grid striding over the owned rows keeps the number
   // of flag waits and remote ready-signals independent of the batch size
-  const int blocks = std::max(1, std::min(a.rows_per_rank, 2 * 148));
-  comm::tp_allreduce_rmsnorm_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int blocks = std::max(1, std::min(a.rows_per_rank, comm::kMaxArBlocks));
+  static const int env_pdl = [] {
+    const char* e = std::getenv("BLOOM_PDL");
+    return e ? std::atoi(e) : 1;
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(blocks, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cfg.attrs = attr;
+  cfg.numAttrs = env_pdl ? 1 : 0;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, comm::tp_allreduce_rmsnorm_kernel, a));
 }
 
 void tp_allgather_rows(const torch::Tensor& src, const std::vector<int64_t>& dst_ptrs,
