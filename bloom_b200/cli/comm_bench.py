@@ -14,6 +14,11 @@ ranks (one JSON line per case, rank 0):
                Llama-3-8B shape) whose epilogue pushes rows to their owners,
                then coll_push
   <gemm>_nccl  the same GEMM into a local buffer, NCCL all-reduce, add_rmsnorm
+  mlp_chain    the tensor-parallel part of a decoder layer's second half:
+               o_proj (push) -> collective -> gate_up + SwiGLU -> down (push)
+               -> collective -> next qkv GEMM, with the all-gather waited
+               for in the collective (mlp_chain) or deferred to the GEMM that
+               reads the rows (mlp_chain_deferred), and on NCCL (mlp_chain_nccl)
 
 Each case is captured as a CUDA graph of `--iters` back-to-back ops and
 replayed (warm-up replays first); the time is CUDA events on the launching
@@ -104,6 +109,8 @@ def main(argv=None) -> None:
     fc.partial(Tmax).copy_(part)
     weights = {"o_proj": torch.randn(H, H // world, device=dev, dtype=torch.bfloat16, generator=g) * 0.02,
                "down": torch.randn(H, F // world, device=dev, dtype=torch.bfloat16, generator=g) * 0.02}
+    w_gu = torch.randn(2 * F // world, H, device=dev, dtype=torch.bfloat16, generator=g) * 0.02
+    w_qkv = torch.randn((H + 2 * H // 4) // world, H, device=dev, dtype=torch.bfloat16, generator=g) * 0.02
     acts = {k: torch.randn(Tmax, w.shape[1], device=dev, dtype=torch.bfloat16, generator=g) for k, w in weights.items()}
     results = []
 
@@ -174,6 +181,32 @@ def main(argv=None) -> None:
 
             report(f"{name}_fused", T, _time_graph(fused_op, args.iters), flops, ag_bytes + rs_bytes)
             report(f"{name}_nccl", T, _time_graph(nccl_op, args.iters), flops, ag_bytes + rs_bytes)
+        # decoder-layer chain with and without the deferred all-gather
+        x_o = acts["o_proj"][:T]
+        chain_flops = 2.0 * T * H * (H // world + 2 * F // world + F // world + w_qkv.shape[0])
+
+        def chain(defer):
+            ops.gemm(x_o, weights["o_proj"], fc.partial(T), push=fc.push_args(T))
+            x = fc.allreduce_rmsnorm(T, r_T, norm_w, 1e-5, pushed=True, defer=defer)
+            act = ops.gemm(x, w_gu, epi=ops.EPI_SWIGLU, wait=fc.wait_args() if defer else None)
+            ops.gemm(act, weights["down"], fc.partial(T), push=fc.push_args(T))
+            x = fc.allreduce_rmsnorm(T, r_T, norm_w, 1e-5, pushed=True, defer=defer)
+            ops.gemm(x, w_qkv, wait=fc.wait_args() if defer else None)
+
+        def chain_nccl():
+            y = ops.gemm(x_o, weights["o_proj"])
+            dist.all_reduce(y)
+            x = ops.add_rmsnorm(y, r_T, norm_w, 1e-5)
+            act = ops.gemm(x, w_gu, epi=ops.EPI_SWIGLU)
+            y = ops.gemm(act, weights["down"])
+            dist.all_reduce(y)
+            x = ops.add_rmsnorm(y, r_T, norm_w, 1e-5)
+            ops.gemm(x, w_qkv)
+
+        report("mlp_chain", T, _time_graph(lambda: chain(False), args.iters), chain_flops, 2 * (ag_bytes + rs_bytes))
+        report("mlp_chain_deferred", T, _time_graph(lambda: chain(True), args.iters), chain_flops,
+               2 * (ag_bytes + rs_bytes))
+        report("mlp_chain_nccl", T, _time_graph(chain_nccl, args.iters), chain_flops, 2 * (ag_bytes + rs_bytes))
     st = int(ops.status(local)[0].item())
     bad = sum(fc.check_canaries().values())
     if rank == 0:

@@ -38,6 +38,8 @@ from .config import ModelConfig
 # Row-parallel GEMMs push their partial rows to the owning ranks from the
 # epilogue (reduce-scatter fused into the GEMM); 0 keeps the pull variant.
 _TP_PUSH = os.environ.get("BLOOM_TP_PUSH", "1") != "0"
+# the fused all-gather leaves the wait for the peers' rows to the next GEMM
+_TP_DEFER = os.environ.get("BLOOM_TP_DEFER", "1") != "0"
 
 
 @dataclass
@@ -502,16 +504,22 @@ class DecoderLM:
         return self.tp.comm.all_reduce(t)
 
     def _row_parallel_norm(self, inp: torch.Tensor, w_mat: torch.Tensor, residual: torch.Tensor,
-                           norm_w: torch.Tensor, eps: float) -> torch.Tensor:
-        """x = rmsnorm(residual += inp @ w_mat^T summed over TP ranks) * norm_w."""
+                           norm_w: torch.Tensor, eps: float, wait=None, next_w=None):
+        """x = rmsnorm(residual += inp @ w_mat^T summed over TP ranks) * norm_w.
+
+        Returns (x, wait): with the fused collective and a bf16 `next_w` (the
+        weight of the GEMM that reads x next), the all-gather is deferred and
+        `wait` must be passed to that GEMM; otherwise wait is None."""
         fused = self.tp.comm.fused if (self.tp.size > 1 and self.tp.comm is not None) else None
         if fused is not None:
             T = inp.shape[0]
             push = _TP_PUSH and isinstance(w_mat, torch.Tensor)
-            ops.gemm(inp, w_mat, fused.partial(T), push=fused.push_args(T) if push else None)
-            return fused.allreduce_rmsnorm(T, residual, norm_w, eps, pushed=push)
-        d = self._reduce(ops.gemm(inp, w_mat))
-        return ops.add_rmsnorm(d, residual, norm_w, eps)
+            defer = _TP_DEFER and isinstance(next_w, torch.Tensor)
+            ops.gemm(inp, w_mat, fused.partial(T), push=fused.push_args(T) if push else None, wait=wait)
+            x = fused.allreduce_rmsnorm(T, residual, norm_w, eps, pushed=push, defer=defer)
+            return x, (fused.wait_args() if defer else None)
+        d = self._reduce(ops.gemm(inp, w_mat, wait=wait))
+        return ops.add_rmsnorm(d, residual, norm_w, eps), None
 
     def forward(self, s: StepInputs, kv_cache: torch.Tensor) -> torch.Tensor:
         """Returns the final-normed hidden states of the logits rows [NL, H] (bf16)."""
@@ -525,9 +533,12 @@ class DecoderLM:
         residual = ops.embedding(s.input_ids, self.embed)
         x = ops.rmsnorm(residual, self.layers[0]["ln1"], eps)
         qkv_dim = (self.nq + 2 * self.nkv) * cfg.head_dim
-        for li in range(len(self.layers)):
+        wait = None  # a deferred all-gather the next GEMM must wait for
+        L = len(self.layers)
+        for li in range(L):
             lay = self._layer(li)
-            qkv = ops.gemm(x, lay["qkv"], bias=lay.get("qkv_b"))
+            qkv = ops.gemm(x, lay["qkv"], bias=lay.get("qkv_b"), wait=wait)
+            wait = None
             q = torch.empty(T, self.nq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
             ops.rope_kv_write(qkv, s.positions, s.slot_mapping, self.cos_sin, q, kv_cache, li, self.nq, self.nkv,
                               lay.get("q_norm"), lay.get("k_norm"), eps)
@@ -540,7 +551,8 @@ class DecoderLM:
                 ops.paged_prefill_attention(q[Td:], kv_cache, li, s.prefill_block_table, s.prefill_ctx_lens,
                                             s.prefill_cu_q, s.tile_seq, s.tile_start, attn[Td:], scale=self.scale)
             a2 = attn.view(T, self.nq * cfg.head_dim)
-            x = self._row_parallel_norm(a2, lay["o"], residual, lay["ln2"], eps)
+            x, wait = self._row_parallel_norm(a2, lay["o"], residual, lay["ln2"], eps,
+                                              next_w=lay.get("gate_up") if self.moe is None else None)
             nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
             if self.moe is not None:
                 fused = self.tp.comm.fused if (self.tp.size > 1 and self.tp.comm is not None) else None
@@ -551,8 +563,11 @@ class DecoderLM:
                     d = self._reduce(self.moe.forward(li, x))
                     x = ops.add_rmsnorm(d, residual, nxt, eps)
             else:
-                act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU)
-                x = self._row_parallel_norm(act, lay["down"], residual, nxt, eps)
+                act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU, wait=wait)
+                wait = None
+                # the next layer's qkv GEMM can take the wait unless its layer is streamed in
+                nq_w = self.layers[li + 1].get("qkv") if (li + 1 < L and not self.offloaded) else None
+                x, wait = self._row_parallel_norm(act, lay["down"], residual, nxt, eps, next_w=nq_w)
             self._release(li)
         return x.index_select(0, s.logits_rows)
 

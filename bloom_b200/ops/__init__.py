@@ -141,6 +141,7 @@ def gemm(
     splits: Optional[int] = None,
     bn: Optional[int] = None,
     push=None,
+    wait=None,
 ) -> torch.Tensor:
     """y = x @ w.T on tcgen05 (x [M,K] bf16, w [N,K] bf16) with a fused epilogue.
 
@@ -154,11 +155,17 @@ def gemm(
     t // rows's buffer at slot [rank][t % rows] over NVLink (see
     parallel.fused.FusedComm.push_args); `out` then only fixes the shape.
 
+    wait=(flag block pointer, timeout s) makes the producer wait, before its
+    first activation tile, for the rows of a deferred tensor-parallel
+    all-gather (parallel.fused.FusedComm.wait_args).
+
     splits=None picks split-K automatically for small M (decode batches): the
     K range is split across CTAs so every SM streams weights, and the last
     split to finish each tile sums the fp32 partials and runs the epilogue.
     """
     if isinstance(w, QWeight):
+        if wait is not None:
+            raise ValueError("gemm: wait= needs a bf16 weight (the quantised kernels do not wait)")
         return _qgemm(x, w, out, epi, bias, resid, splits, bn)
     M, N = x.shape[0], w.shape[0]
     K = x.shape[1]
@@ -184,10 +191,11 @@ def gemm(
             out = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
         else:
             out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    if push is not None:
-        ptrs, rank, rows = push
+    if push is not None or wait is not None:
+        ptrs, rank, rows = push if push is not None else ([], 0, 0)
+        wf, wt = wait if wait is not None else (0, 5.0)
         _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt, bn,
-                      list(ptrs), int(rank), int(rows))
+                      list(ptrs), int(rank), int(rows), int(wf), float(wt))
     else:
         _C().gemm_out(x, w, out, epi, resid, bias, splits, status(x.device.index), fix_ws, fix_cnt, bn)
     _count()

@@ -133,11 +133,19 @@ class FusedComm:
         return self._X[:T * self.hidden].view(T, self.hidden)
 
     def allreduce_rmsnorm(self, T: int, residual: torch.Tensor, w: torch.Tensor, eps: float,
-                          pushed: bool = False) -> torch.Tensor:
+                          pushed: bool = False, defer: bool = False) -> torch.Tensor:
+        """defer=True: the kernel does not wait for the peers' rows; the next
+        reader of x(T) must be an ops.gemm given wait=self.wait_args(), which
+        waits for them before its first activation tile (the wait overlaps the
+        collective's exit and the GEMM's weight prefetch)."""
         _C().tp_allreduce_rmsnorm(self.p_ptrs, self.x_ptrs, self.f_ptrs, self.rank, residual, w, eps, T,
-                                  self.timeout_s, ops.status(self.device.index), pushed)
+                                  self.timeout_s, ops.status(self.device.index), pushed, defer)
         ops._count()
         return self.x(T)
+
+    def wait_args(self):
+        """(this rank's flag block, timeout) for ops.gemm(wait=...)."""
+        return self.f_ptrs[self.rank], self.timeout_s
 
     def barrier(self) -> None:
         _C().tp_barrier(self.f_ptrs, self.rank, self.timeout_s, ops.status(self.device.index))

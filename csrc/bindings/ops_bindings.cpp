@@ -21,7 +21,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &bloom::gemm_out, "y = x @ w^T on tcgen05 with fused epilogue", py::arg("x"), py::arg("w"),
         py::arg("out"), py::arg("epi"), py::arg("resid"), py::arg("bias"), py::arg("splits"), py::arg("status"),
         py::arg("fix_ws"), py::arg("fix_count"), py::arg("bn_override"),
-        py::arg("push_ptrs") = std::vector<int64_t>{}, py::arg("push_rank") = 0, py::arg("push_rows") = 0);
+        py::arg("push_ptrs") = std::vector<int64_t>{}, py::arg("push_rank") = 0, py::arg("push_rows") = 0,
+        py::arg("wait_flags") = 0, py::arg("wait_timeout_s") = 5.0);
   m.def("gemm_pick_bn", &bloom::gemm_pick_bn);
   m.def("gemm_grouped_out", &bloom::gemm_grouped_out);
   m.def("moe_route", &bloom::moe_route);
@@ -66,7 +67,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_flag_words", &bloom::tp_flag_words);
   m.def("tp_allreduce_rmsnorm", &bloom::tp_allreduce_rmsnorm, py::arg("partial_ptrs"), py::arg("x_ptrs"),
         py::arg("flag_ptrs"), py::arg("rank"), py::arg("residual"), py::arg("w"), py::arg("eps"), py::arg("T"),
-        py::arg("timeout_s"), py::arg("status"), py::arg("pushed") = false);
+        py::arg("timeout_s"), py::arg("status"), py::arg("pushed") = false, py::arg("defer_done") = false);
   m.def("tp_allgather_rows", &bloom::tp_allgather_rows);
   m.def("tp_barrier", &bloom::tp_barrier);
   m.def("tp_argmax_gather", &bloom::tp_argmax_gather);

@@ -45,6 +45,26 @@ __device__ __forceinline__ bool kcheck(bool ok, int* status) {
 __device__ __forceinline__ constexpr bool kcheck(bool, int*) { return true; }
 #endif
 
+// Words of a rank's tensor-parallel flag block (bloom_b200.parallel.fused)
+// that kernels outside comm.cu also touch: the poison word, and the counter
+// and expectation of a deferred all-gather (see wait_deferred_rows).
+constexpr int kFlagPoison = 18, kFlagDoneCount = 19, kFlagDoneExpect = 20;
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Consumer side of a deferred all-gather: a tensor-parallel collective that
+// does not wait for its peers' rows leaves that wait to the kernel that reads
+// them.  Every block of every rank adds 1 to this rank's done counter after
+// its rows are stored here; the collective also raised the expectation by its
+// number of blocks x ranks.  Waits (bounded) until the counter reaches the
+// expectation (wrap-around safe).  A timeout poisons the communicator and
+// sets kStatusCommTimeout; the caller goes on (the step is failed by the host).
+__device__ __forceinline__ bool wait_deferred_rows(uint32_t* flags, uint64_t timeout_ns, int* status);
+
 // Local (same-GPU) pipeline waits never legitimately take this long.
 constexpr uint64_t kLocalWaitTimeoutNs = 2000000000ull;  // 2 s
 
@@ -271,6 +291,23 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ bool wait_deferred_rows(uint32_t* flags, uint64_t timeout_ns, int* status) {
+  if (flags == nullptr) return true;
+  volatile uint32_t* vf = flags;
+  if (vf[kFlagPoison] != 0u) return true;  // the step fails anyway; do not wait
+  const uint32_t expect = vf[kFlagDoneExpect];
+  const uint64_t t0 = globaltimer_ns();
+  while (static_cast<int>(ld_acquire_sys_u32(flags + kFlagDoneCount) - expect) < 0) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      vf[kFlagPoison] = 1u;
+      __threadfence();
+      atomicOr(status, kStatusCommTimeout);
+      return false;
+    }
+  }
+  return true;
 }
 
 }  // namespace bloom

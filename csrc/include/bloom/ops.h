@@ -23,7 +23,8 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
               const torch::Tensor& status, const c10::optional<torch::Tensor>& fix_ws,
               const c10::optional<torch::Tensor>& fix_count, int64_t bn_override,
-              const std::vector<int64_t>& push_ptrs = {}, int64_t push_rank = 0, int64_t push_rows = 0);
+              const std::vector<int64_t>& push_ptrs = {}, int64_t push_rank = 0, int64_t push_rows = 0,
+              int64_t wait_flags = 0, double wait_timeout_s = 5.0);
 int64_t gemm_fixup_ws_floats(int64_t M, int64_t N, int64_t splits, int64_t bn_override);
 int gemm_pick_bn(int M);
 int gemm_default_splits(int M, int N, int K, int device);
@@ -130,7 +131,7 @@ int64_t tp_flag_words();
 void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::vector<int64_t>& x_ptrs,
                           const std::vector<int64_t>& flag_ptrs, int64_t rank, torch::Tensor& residual,
                           const torch::Tensor& w, double eps, int64_t T, double timeout_s,
-                          const torch::Tensor& status, bool pushed = false);
+                          const torch::Tensor& status, bool pushed = false, bool defer_done = false);
 void tp_allgather_rows(const torch::Tensor& src, const std::vector<int64_t>& dst_ptrs,
                        const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t T, double timeout_s,
                        const torch::Tensor& status);

@@ -57,7 +57,10 @@ struct Peers {
 //   [16]      epoch        local: number of completed fused collectives
 //   [17]      cta counter  local: CTAs of the current launch that finished
 //   [18]      poison       local: nonzero once a wait of this rank timed out
-constexpr int kReady = 0, kDone = 8, kEpoch = 16, kCtaCount = 17, kPoison = 18;
+//   [19]      done count   written by every peer block of a deferred all-gather (red.add)
+//   [20]      done expect  local: done count the next reader of the rows waits for
+constexpr int kReady = 0, kDone = 8, kEpoch = 16, kCtaCount = 17, kPoison = kFlagPoison;
+static_assert(kFlagDoneCount == 19 && kFlagDoneExpect == 20, "flag block layout");
 // Per-block flags of tp_allreduce_rmsnorm (block b of a launch pairs only with
 // block b of every peer, so no CTA counter and no last-CTA hand-off):
 //   [kBlkReady + src * kMaxArBlocks + b]  written by peer src's block b: its partials are complete
@@ -133,6 +136,10 @@ struct ARArgs {
   // passed -- at [(epoch % trace_cap) * 4]
   unsigned long long* trace;
   int trace_cap;
+  // 1: do not wait for the peers' rows here; every block adds 1 to every
+  // rank's done count after its stores, and the next kernel that reads the
+  // rows (a GEMM given wait_flags) waits for the count instead
+  int defer_done;
 };
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
@@ -267,6 +274,18 @@ __global__ void __launch_bounds__(1024) tp_allreduce_rmsnorm_kernel(const ARArgs
   // this rank's input buffer has arrived.
   __syncthreads();
   if (tr) trs[2] = globaltimer_ns();
+  if (a.defer_done) {
+    if (threadIdx.x < a.world) {
+      uint32_t* cnt = reinterpret_cast<uint32_t*>(a.flags.p[threadIdx.x]) + kFlagDoneCount;
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+    }
+    if (threadIdx.x == 0) {
+      if (blk == 0) my_flags[kFlagDoneExpect] += gridDim.x * a.world;  // read after this launch completes
+      my_flags[kBlkEpoch + blk] = target;
+      if (tr) trs[3] = globaltimer_ns();
+    }
+    return;
+  }
   if (threadIdx.x < a.world) {
     const int r = threadIdx.x;
     st_release_sys(reinterpret_cast<uint32_t*>(a.flags.p[r]) + kBlkDone + a.rank * kMaxArBlocks + blk, target);
@@ -555,7 +574,7 @@ void tp_ar_set_trace(const c10::optional<torch::Tensor>& buf) {
 void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::vector<int64_t>& x_ptrs,
                           const std::vector<int64_t>& flag_ptrs, int64_t rank, torch::Tensor& residual,
                           const torch::Tensor& w, double eps, int64_t T, double timeout_s,
-                          const torch::Tensor& status, bool pushed) {
+                          const torch::Tensor& status, bool pushed, bool defer_done) {
   const int world = static_cast<int>(partial_ptrs.size());
   TORCH_CHECK(x_ptrs.size() == partial_ptrs.size() && flag_ptrs.size() == partial_ptrs.size(), "rank count mismatch");
   TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.is_contiguous(), "residual bf16 contiguous");
@@ -578,6 +597,7 @@ void tp_allreduce_rmsnorm(const std::vector<int64_t>& partial_ptrs, const std::v
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   a.status = status.data_ptr<int>();
   a.pushed = pushed ? 1 : 0;
+  a.defer_done = defer_done ? 1 : 0;
   a.trace = g_ar_trace;
   a.trace_cap = g_ar_trace_cap;
   const int threads = ((H / 8 + 31) / 32) * 32;

@@ -74,6 +74,11 @@ struct Args {
   unsigned long long push[8];
   int push_world, push_rank, push_rows;
   int gelu_tanh;  // kEpiGelu: 1 = tanh approximation, 0 = erf
+  // Activations written by a deferred tensor-parallel all-gather: before the
+  // first activation tile, the producer waits (bounded) until every peer's
+  // rows arrived (wait_deferred_rows on this rank's flag block); nullptr = none
+  uint32_t* wait_flags;
+  uint64_t wait_timeout_ns;
 };
 
 // Row `tok` of the bf16 output: local, or the owner's slot for this rank (push).
@@ -404,6 +409,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         griddep_wait();
       }
+      wait_deferred_rows(a.wait_flags, a.wait_timeout_ns, a.status);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const Tile tl = get_tile<BN>(a, t);
         const int kb0 = tl.sp * a.kb_per_split;
@@ -812,6 +818,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_par = 0;
       bool ok = true;
+      wait_deferred_rows(a.wait_flags, a.wait_timeout_ns, a.status);
       for (int t = pair; t < total && ok; t += npairs) {
         int ft2, tt;
         tile_of(t, ft2, tt);
@@ -1120,7 +1127,8 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& bias, int64_t splits,
               const torch::Tensor& status, const c10::optional<torch::Tensor>& fix_ws,
               const c10::optional<torch::Tensor>& fix_count, int64_t bn_override,
-              const std::vector<int64_t>& push_ptrs, int64_t push_rank, int64_t push_rows) {
+              const std::vector<int64_t>& push_ptrs, int64_t push_rank, int64_t push_rows, int64_t wait_flags,
+              double wait_timeout_s) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "gemm: tensors must be on CUDA");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm: x and w must be bf16");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm: x [M,K], w [N,K]");
@@ -1169,6 +1177,8 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   a.push_world = 0;
   a.push_rank = 0;
   a.push_rows = 0;
+  a.wait_flags = reinterpret_cast<uint32_t*>(static_cast<uintptr_t>(wait_flags));
+  a.wait_timeout_ns = static_cast<uint64_t>(wait_timeout_s * 1e9);
   for (int r = 0; r < 8; ++r) a.push[r] = 0;
   if (!push_ptrs.empty()) {
     TORCH_CHECK(epi == kEpiBF16 && !bias.has_value(), "gemm push: plain bf16 epilogue only");
