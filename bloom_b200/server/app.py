@@ -63,6 +63,62 @@ class APIError(Exception):
         self.headers = headers or {}
 
 
+_EXPOSED = "x-request-id, retry-after, www-authenticate"
+_LOOPBACK_HOSTS = ("127.0.0.1", "localhost", "[::1]", "::1")
+
+
+def _split_origin(value: str):
+    """(scheme, host, port) of a serialized browser origin, or None."""
+    m = re.match(r"^(https?)://([^/:?#\s]+|\[[0-9a-fA-F:]+\])(?::(\d{1,5}))?$", value.strip())
+    if not m:
+        return None
+    scheme, host, port = m.group(1), m.group(2).lower(), m.group(3)
+    return scheme, host, int(port) if port else (443 if scheme == "https" else 80)
+
+
+def origin_permitted(origins: List[str], loopback_listener: bool, origin_values: List[str], host_header: str) -> bool:
+    """Browser-origin policy of the HTTP server.  No Origin header: a
+    non-browser client, allowed.  Several Origin headers or an unparsable one
+    ("null" included): refused.  `origins` ["*"] allows any origin, a list
+    allows exactly those; otherwise only same-origin pages: an http origin
+    whose host:port equals the request's Host, and a loopback host when the
+    server listens on loopback only (DNS rebinding).  Reference:
+    crates/server/src/lib.rs:283-320 (BrowserOriginGuard::permits)."""
+    if not origin_values:
+        return True
+    if len(origin_values) > 1:
+        return False
+    o = _split_origin(origin_values[0])
+    if o is None:
+        return False
+    if "*" in origins:
+        return True
+    if origin_values[0].strip().rstrip("/") in [x.rstrip("/") for x in origins]:
+        return True
+    scheme, host, port = o
+    if scheme != "http":
+        return False
+    if loopback_listener and host not in _LOOPBACK_HOSTS:
+        return False
+    h = _split_origin("http://" + host_header.strip()) if host_header else None
+    return h is not None and (h[1], h[2]) == (host, port)
+
+
+def _cors_headers(resp, origins: List[str], origin: str) -> None:
+    """Allowed cross-origin answer: "*" policy -> any origin; an exact list ->
+    the configured origin the request matched (or the first one for a
+    same-origin request); same-origin only -> no CORS header."""
+    if "*" in origins:
+        resp.headers["access-control-allow-origin"] = "*"
+    elif origins:
+        o = origin.strip().rstrip("/")
+        resp.headers["access-control-allow-origin"] = o if o in [x.rstrip("/") for x in origins] else origins[0]
+        resp.headers["vary"] = "Origin"
+    else:
+        return
+    resp.headers["access-control-expose-headers"] = _EXPOSED
+
+
 def _openai_error(e: APIError) -> JSONResponse:
     return JSONResponse({"error": {"message": e.message, "type": e.type, "param": e.param, "code": e.code}},
                         status_code=e.status, headers=e.headers)
@@ -220,6 +276,20 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         if not rid or not _RID.match(rid):
             rid = uuid.uuid4().hex
         request.state.request_id = rid
+        origins = request.headers.getlist("origin")
+        if not origin_permitted(st.cors_origins, not st.allow_non_loopback, origins, request.headers.get("host", "")):
+            e = APIError(403, "The browser origin is not allowed by the Bloom server policy.", "invalid_request_error")
+            resp = _ollama_error(e) if path.startswith("/api") else _openai_error(e)
+            resp.headers["x-request-id"] = rid
+            resp.headers["cache-control"] = "no-store"
+            return resp
+        if request.method == "OPTIONS" and origins and request.headers.get("access-control-request-method"):
+            resp = Response(status_code=204)
+            _cors_headers(resp, st.cors_origins, origins[0])
+            resp.headers["access-control-allow-methods"] = "*"
+            resp.headers["access-control-allow-headers"] = request.headers.get("access-control-request-headers", "*")
+            resp.headers["x-request-id"] = rid
+            return resp
         if api and st.api_keys:
             auth = request.headers.get("authorization", "")
             tok = auth[7:] if auth.lower().startswith("bearer ") else None
@@ -240,10 +310,8 @@ def create_app(pipeline, settings: Optional[ServerSettings] = None, runtime: Opt
         if api:
             resp.headers["x-request-id"] = rid
             resp.headers["cache-control"] = "no-store"
-        origin = request.headers.get("origin")
-        if origin and origin in st.cors_origins:
-            resp.headers["access-control-allow-origin"] = origin
-            resp.headers["vary"] = "Origin"
+        if origins:
+            _cors_headers(resp, st.cors_origins, origins[0])
         return resp
 
     @app.exception_handler(APIError)

@@ -411,3 +411,78 @@ def test_multimodal_stream_and_upload(client):
     ev = [json.loads(l[6:]) for l in r.text.splitlines() if l.startswith("data: ")]
     assert "".join(e["TextDelta"] for e in ev if isinstance(e, dict) and "TextDelta" in e) == \
         "echo: [image 20x12] hi"
+
+
+def test_browser_origin_policy_and_preflight():
+    """Reference: crates/server/src/lib.rs:12081-12240 (fail-closed origin guard aligned with CORS)."""
+    from bloom_b200.server.app import origin_permitted
+
+    app = create_app(EchoPipeline(), ServerSettings(model_id="echo", cors_origins=["https://ui.example"]))
+    with TestClient(app, base_url="http://127.0.0.1:3000") as c:
+        ok = c.get("/health", headers={"origin": "https://ui.example"})
+        assert ok.status_code == 200 and ok.headers["access-control-allow-origin"] == "https://ui.example"
+        assert "x-request-id" in ok.headers["access-control-expose-headers"]
+        same = c.get("/health", headers={"origin": "http://127.0.0.1:3000"})
+        assert same.status_code == 200 and same.headers["access-control-allow-origin"] == "https://ui.example"
+        assert c.get("/health").status_code == 200  # no Origin: not a browser
+        for path, family in (("/v1/models", "openai"), ("/api/version", "ollama")):
+            r = c.get(path, headers={"origin": "https://malicious.example"})
+            assert r.status_code == 403 and r.headers["cache-control"] == "no-store"
+            assert "x-request-id" in r.headers and "access-control-allow-origin" not in r.headers
+            body = r.json()
+            assert (body["error"]["type"] == "invalid_request_error") if family == "openai" else isinstance(
+                body["error"], str)
+        pre = c.options("/v1/models", headers={"origin": "https://malicious.example",
+                                               "access-control-request-method": "GET"})
+        assert pre.status_code == 403
+        pre = c.options("/v1/chat/completions", headers={"origin": "https://ui.example",
+                                                         "access-control-request-method": "POST",
+                                                         "access-control-request-headers": "content-type"})
+        assert pre.status_code == 204 and pre.headers["access-control-allow-origin"] == "https://ui.example"
+    # DNS rebinding: a loopback listener refuses non-loopback page origins even when Host matches
+    for origin in ("null", "http://attacker.example"):
+        assert not origin_permitted([], True, [origin], "attacker.example")
+    assert not origin_permitted(["https://ui.example"], True, ["https://ui.example", "https://x.example"], "h")
+    assert origin_permitted(["*"], True, ["https://anything.example"], "127.0.0.1:3000")
+    assert origin_permitted([], False, ["http://box.lan:8080"], "box.lan:8080")
+    assert not origin_permitted([], False, ["https://box.lan:8080"], "box.lan:8080")  # same-origin is http only
+
+
+def test_body_limit_and_concurrent_ndjson_streams(client):
+    big = b"{" + b" " * (17 * 1024 * 1024) + b"}"
+    r = client.post("/v1/chat/completions", content=big, headers={"content-type": "application/json"})
+    assert r.status_code == 413 and r.json()["error"]["message"] == "request body too large"
+    r = client.post("/api/chat", content=big, headers={"content-type": "application/json"})
+    assert r.status_code == 413 and isinstance(r.json()["error"], str)
+
+    import threading
+
+    results, errors = {}, []
+    app = create_app(EchoPipeline(), ServerSettings(model_id="echo", max_concurrent=8))
+    cc = TestClient(app)
+    cc.__enter__()
+
+    def stream(i):
+        try:
+            lines = []
+            with cc.stream("POST", "/api/generate", json={"model": "echo", "prompt": f"p{i} a b c"}) as s:
+                assert s.headers["content-type"].startswith("application/x-ndjson")
+                for line in s.iter_lines():
+                    if line:
+                        lines.append(json.loads(line))
+            results[i] = lines
+        except Exception as e:  # pragma: no cover - reported below
+            errors.append(repr(e))
+
+    ts = [threading.Thread(target=stream, args=(i,)) for i in range(6)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(timeout=60)
+    cc.__exit__(None, None, None)
+    assert not errors, errors
+    assert len(results) == 6
+    for i, lines in results.items():
+        assert lines[-1]["done"] is True and all(not l["done"] for l in lines[:-1])
+        text = "".join(l.get("response", "") for l in lines)
+        assert f"p{i}" in text  # each stream carries its own request's output, none interleaved
