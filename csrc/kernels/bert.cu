@@ -3,8 +3,10 @@
 //
 //   bert_embed_ln      x[t] = LayerNorm(word[id] + pos[p] + type[tt])
 //   varlen_attention   non-causal softmax(q k^T * scale) v per (sequence, head),
-//                      head_dim <= 64, sequences up to 512 tokens; K/V of one
-//                      head are staged in shared memory, one warp per query row
+//                      head_dim 32 / 64, sequences up to 512 tokens: tensor-core
+//                      (mma.sync) FlashAttention-2 tiles over the head's K / V
+//                      staged in shared memory; a scalar one-warp-per-query
+//                      kernel remains for unaligned inputs (BLOOM_BERT_ATTN_TC=0)
 //   mean_pool_l2       mean over each sequence's tokens, then L2-normalise
 //
 // Linear layers use the tcgen05 GEMM (bias and bias+GELU epilogues).  The
@@ -118,6 +120,165 @@ __global__ void varlen_attention_kernel(const __nv_bfloat16* __restrict__ qkv, c
   }
 }
 
+// Tensor-core variant (mma.sync m16n8k16, bf16 in, f32 accumulate) for
+// head_dim 32 / 64: grid (num_seqs, NH, query tiles of 64 rows), 4 warps of
+// 16 query rows.  The head's K and V rows (zero-padded to a multiple of 16
+// keys) are staged in shared memory as bf16; each warp runs FlashAttention-2
+// style over 16-key tiles: S = Q K^T into registers, online softmax in the
+// base-2 domain, P re-packed from the S accumulators straight into the A
+// operand of P V.  Keys past the sequence end are masked to -inf.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_raw(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  __nv_bfloat162 v;
+  v.x = lo;
+  v.y = hi;
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) varlen_attention_tc_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                  const int* __restrict__ cu,
+                                                                  __nv_bfloat16* __restrict__ out, int NH,
+                                                                  float scale_log2) {
+  constexpr int KC = D / 16;  // k-chunks of Q K^T
+  constexpr int NB = D / 8;   // n-blocks of the output
+  extern __shared__ __align__(16) uint8_t smraw[];
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int t0 = cu[s], L = cu[s + 1] - t0;
+  const int q0 = blockIdx.z * 64;
+  if (q0 >= L) return;
+  const int Lp = (L + 15) & ~15;
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smraw);  // [Lp][D]
+  __nv_bfloat16* Vs = Ks + (long)Lp * D;                        // [Lp][D]
+  const long ld = 3L * NH * D;
+  constexpr int VEC = D / 8;  // 16-byte vectors per row
+  for (int idx = threadIdx.x; idx < Lp * VEC; idx += blockDim.x) {
+    const int j = idx / VEC, c = idx - j * VEC;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (j < L) {
+      const __nv_bfloat16* row = qkv + (long)(t0 + j) * ld;
+      kv = *reinterpret_cast<const uint4*>(row + (long)NH * D + h * D + c * 8);
+      vv = *reinterpret_cast<const uint4*>(row + 2L * NH * D + h * D + c * 8);
+    }
+    reinterpret_cast<uint4*>(Ks)[idx] = kv;
+    reinterpret_cast<uint4*>(Vs)[idx] = vv;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;  // this thread's two query rows
+  if (q0 + warp * 16 >= L) return;
+  // Q fragments (A operand, row-major 16 x 16 per k-chunk)
+  uint32_t qf[KC][4];
+  const __nv_bfloat16* qb = qkv + (long)t0 * ld + h * D;
+  const __nv_bfloat16 zero = __float2bfloat16(0.f);
+#pragma unroll
+  for (int kc = 0; kc < KC; ++kc) {
+    const int c0 = kc * 16 + t4 * 2;
+    const __nv_bfloat16* p0 = qb + (long)r0 * ld;
+    const __nv_bfloat16* p1 = qb + (long)r1 * ld;
+    const bool v0 = r0 < L, v1 = r1 < L;
+    qf[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(p0 + c0) : pack_raw(zero, zero);
+    qf[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(p1 + c0) : pack_raw(zero, zero);
+    qf[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(p0 + c0 + 8) : pack_raw(zero, zero);
+    qf[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(p1 + c0 + 8) : pack_raw(zero, zero);
+  }
+  float o[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  for (int kt = 0; kt < Lp; kt += 16) {
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      const __nv_bfloat16* krow = Ks + (long)(kt + nt * 8 + g) * D;  // key n = g of this n-block
+#pragma unroll
+      for (int kc = 0; kc < KC; ++kc) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + kc * 16 + t4 * 2);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + kc * 16 + t4 * 2 + 8);
+        mma16816(sc[nt], qf[kc], b0, b1);
+      }
+    }
+    // scale, mask, online softmax (rows r0: elements 0,1; r1: elements 2,3)
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kt + nt * 8 + t4 * 2 + (e & 1);
+        sc[nt][e] = key < L ? sc[nt][e] * scale_log2 : -INFINITY;
+        if (e < 2) mx0 = fmaxf(mx0, sc[nt][e]);
+        else mx1 = fmaxf(mx1, sc[nt][e]);
+      }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float c0 = exp2f(m0 - mx0), c1 = exp2f(m1 - mx1);  // m = -inf at the start: exp2(-inf) = 0
+    m0 = mx0;
+    m1 = mx1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = exp2f(sc[nt][e] - (e < 2 ? mx0 : mx1));
+        sc[nt][e] = p;
+        if (e < 2) ps0 += p;
+        else ps1 += p;
+      }
+    l0 = l0 * c0 + ps0;  // per-thread partial row sums; combined over the quad at the end
+    l1 = l1 * c1 + ps1;
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      o[nb][0] *= c0;
+      o[nb][1] *= c0;
+      o[nb][2] *= c1;
+      o[nb][3] *= c1;
+    }
+    // P (16 q x 16 keys) as the A operand of P V
+    uint32_t pa[4];
+    pa[0] = pack_bf16(sc[0][0], sc[0][1]);
+    pa[1] = pack_bf16(sc[0][2], sc[0][3]);
+    pa[2] = pack_bf16(sc[1][0], sc[1][1]);
+    pa[3] = pack_bf16(sc[1][2], sc[1][3]);
+    const __nv_bfloat16* v0r = Vs + (long)(kt + t4 * 2) * D;  // keys t4*2, t4*2+1 (and +8, +9)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const int d = nb * 8 + g;
+      const uint32_t b0 = pack_raw(v0r[d], v0r[D + d]);
+      const uint32_t b1 = pack_raw(v0r[8 * D + d], v0r[9 * D + d]);
+      mma16816(o[nb], pa, b0, b1);
+    }
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float i0 = 1.f / l0, i1 = 1.f / l1;
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+    const int d = nb * 8 + t4 * 2;
+    if (r0 < L)
+      *reinterpret_cast<uint32_t*>(out + (long)(t0 + r0) * NH * D + h * D + d) = pack_bf16(o[nb][0] * i0, o[nb][1] * i0);
+    if (r1 < L)
+      *reinterpret_cast<uint32_t*>(out + (long)(t0 + r1) * NH * D + h * D + d) = pack_bf16(o[nb][2] * i1, o[nb][3] * i1);
+  }
+}
+
 // one CTA per sequence; out f32 [S, H]
 __global__ void mean_pool_l2_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ cu,
                                     float* __restrict__ out, int H, int normalize) {
@@ -160,8 +321,32 @@ void varlen_attention(const torch::Tensor& qkv, const torch::Tensor& cu_seqlens,
   TORCH_CHECK(head_dim == 32 || head_dim == 64, "varlen_attention: head_dim 32 or 64");
   TORCH_CHECK(max_len <= 512, "varlen_attention: sequences up to 512 tokens");
   const at::cuda::CUDAGuard guard(qkv.device());
-  const size_t smem = 2 * size_t(max_len) * head_dim * sizeof(float);
   auto s = at::cuda::getCurrentCUDAStream();
+  static const bool tc = [] {
+    const char* e = std::getenv("BLOOM_BERT_ATTN_TC");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  const bool aligned = reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0 && qkv.is_contiguous() &&
+                       out.is_contiguous() && reinterpret_cast<uintptr_t>(out.data_ptr()) % 4 == 0;
+  if (tc && aligned) {
+    const int Lp = int((max_len + 15) / 16 * 16);
+    const size_t smem_tc = 2 * size_t(Lp) * head_dim * sizeof(__nv_bfloat16);
+    dim3 g3(S, num_heads, int((max_len + 63) / 64));
+    if (head_dim == 32) {
+      cudaFuncSetAttribute(varlen_attention_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 32 * 2);
+      varlen_attention_tc_kernel<32><<<g3, 128, smem_tc, s>>>(
+          reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cu_seqlens.data_ptr<int>(),
+          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(num_heads), float(scale * 1.4426950408889634));
+    } else {
+      cudaFuncSetAttribute(varlen_attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 64 * 2);
+      varlen_attention_tc_kernel<64><<<g3, 128, smem_tc, s>>>(
+          reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cu_seqlens.data_ptr<int>(),
+          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(num_heads), float(scale * 1.4426950408889634));
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  const size_t smem = 2 * size_t(max_len) * head_dim * sizeof(float);
   dim3 grid(S, num_heads);
   if (head_dim == 32) {
     cudaFuncSetAttribute(varlen_attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 32 * 4);

@@ -36,3 +36,29 @@ def test_gemm_gelu_epilogue():
     y = ops.gemm(x, w, epi=ops.EPI_GELU, bias=b)
     ref = torch.nn.functional.gelu(x.float() @ w.float().t() + b.float())
     assert ((y.float() - ref).norm() / ref.norm()).item() < 1e-2
+
+
+@pytest.mark.parametrize("hd", [32, 64])
+def test_varlen_attention_tensor_core_matches_fp32(hd):
+    """Non-causal varlen attention (mma.sync tiles) against an fp32 softmax,
+    over odd lengths including 1, a partial 16-key tile and 512."""
+    import torch
+
+    from bloom_b200 import ops
+
+    torch.manual_seed(hd)
+    lens = [1, 17, 100, 64, 129, 512]
+    NH = 12 if hd == 32 else 6
+    cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), dtype=torch.int32, device="cuda")
+    T = int(cu[-1])
+    qkv = torch.randn(T, 3 * NH * hd, device="cuda").to(torch.bfloat16)
+    scale = hd ** -0.5
+    out = ops.varlen_attention(qkv, cu, NH, hd, max(lens), scale)
+    q, k, v = qkv.float().view(T, 3, NH, hd).unbind(1)
+    worst = 0.0
+    for i, L in enumerate(lens):
+        a, b = int(cu[i]), int(cu[i + 1])
+        s = torch.einsum("qhd,khd->hqk", q[a:b], k[a:b]) * scale
+        ref = torch.einsum("hqk,khd->qhd", s.softmax(-1), v[a:b]).reshape(L, NH * hd)
+        worst = max(worst, (out[a:b].float() - ref).abs().max().item())
+    assert worst < 2e-2, worst
