@@ -2,6 +2,7 @@
 
     python -m bloom_b200.cli.bench_embed [--steps K] [--warmup W]
     torchrun --nproc-per-node 8 -m bloom_b200.cli.bench_embed          (DP = 8)
+    ... --dtype fp32      full precision (fp32 weights, activations and arithmetic)
 
 Workload per step: 256 sequences per GPU with lengths uniform in [16, 128],
 uniform-random token ids, mean pooling and L2 normalisation (random N(0,0.02)
@@ -24,6 +25,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--dtype", choices=("bf16", "fp32"), default="bf16",
+                    help="fp32: full-precision weights and activations (the model config's stated precision)")
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -35,7 +38,7 @@ def main():
     rank, world, local = init_distributed("nccl")
     dev = torch.device("cuda", local)
     cfg = preset("minilm-l6")
-    e = BertEmbedder(cfg, dev)
+    e = BertEmbedder(cfg, dev, dtype=torch.float32 if args.dtype == "fp32" else torch.bfloat16)
     e.load_state_dict(BertEmbedder.random_state_dict(cfg, seed=0))
     rng = random.Random(1000 + rank)
 
@@ -79,7 +82,7 @@ def main():
         print(json.dumps({"metric": "embeddings/s (MiniLM-L6 shape, 256 seqs/GPU, len U[16,128])",
                           "value": round(value, 1), "unit": "embeddings/s (all GPUs)", "n_gpus": world,
                           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
-                          "parallelism": f"dp{world}", "dtype": "bf16", "data": "synthetic",
+                          "parallelism": f"dp{world}", "dtype": args.dtype, "data": "synthetic",
                           "includes": "H2D of ids from pinned memory, D2H of embeddings"}), flush=True)
     if world > 1:
         dist.barrier()

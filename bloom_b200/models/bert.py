@@ -31,8 +31,17 @@ def _strip(name: str) -> str:
 
 
 class BertEmbedder:
-    def __init__(self, cfg: ModelConfig, device="cuda"):
+    def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16):
+        """dtype bf16: tcgen05 GEMMs with fused bias / GELU and tensor-core
+        attention.  dtype fp32: full precision end to end -- fp32 weights and
+        activations, this repository's fp32 kernels for embeddings + LayerNorm,
+        attention, residual LayerNorm, GELU and pooling, and fp32 SGEMM from
+        cuBLAS (TF32 off) for the linear layers: tensor cores have no fp32
+        mode, so the library GEMM is the full-precision path."""
+        if dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("BertEmbedder dtype must be bf16 or fp32")
         self.cfg = cfg
+        self.dtype = dtype
         self.device = torch.device(device)
         self.w: Dict[str, torch.Tensor] = {}
         self.layers: List[Dict[str, torch.Tensor]] = []
@@ -40,7 +49,7 @@ class BertEmbedder:
 
     # ------------------------------------------------------------ weights
     def load_state_dict(self, sd: Dict[str, torch.Tensor]) -> None:
-        c, dev, bf = self.cfg, self.device, torch.bfloat16
+        c, dev, bf = self.cfg, self.device, self.dtype
         sd = {_strip(k): v for k, v in sd.items()}
 
         def g(k):
@@ -142,6 +151,8 @@ class BertEmbedder:
         scale = 1.0 / math.sqrt(hd)
         eps = c.layer_norm_eps
         x = ops.bert_embed_ln(ids, pos, None, w["word"], w["pos"], w["type"], w["ln_w"], w["ln_b"], eps)
+        if self.dtype == torch.float32:
+            return self._forward_f32(x, cu, max_len, nh, hd, scale, eps, normalize)
         for lay in self.layers:
             qkv = ops.gemm(x, lay["qkv"], bias=lay["qkv_b"])
             a = ops.varlen_attention(qkv, cu, nh, hd, max_len, scale)
@@ -150,6 +161,22 @@ class BertEmbedder:
             h = ops.gemm(x, lay["i"], epi=ops.EPI_GELU, bias=lay["i_b"])
             d = ops.gemm(h, lay["out"], bias=lay["out_b"])
             x = ops.layernorm(d, lay["ln2_w"], lay["ln2_b"], eps, resid=x)
+        return ops.mean_pool_l2(x, cu, normalize)
+
+    def _forward_f32(self, x, cu, max_len, nh, hd, scale, eps, normalize):
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            for lay in self.layers:
+                qkv = torch.addmm(lay["qkv_b"], x, lay["qkv"].t())
+                a = ops.varlen_attention(qkv, cu, nh, hd, max_len, scale)
+                o = torch.addmm(lay["o_b"], a, lay["o"].t())
+                x = ops.ln_residual_f32(o, x, lay["ln1_w"], lay["ln1_b"], eps)
+                h = ops.gelu_f32_(torch.addmm(lay["i_b"], x, lay["i"].t()))
+                d = torch.addmm(lay["out_b"], h, lay["out"].t())
+                x = ops.ln_residual_f32(d, x, lay["ln2_w"], lay["ln2_b"], eps)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
         return ops.mean_pool_l2(x, cu, normalize)
 
     def embed(self, texts: List[str], normalize: bool = True, dimensions: Optional[int] = None) -> List[List[float]]:

@@ -556,7 +556,7 @@ def sample(logits, temperature, top_p, top_k, seeds, offsets, draft=None, out: O
 # ---------------------------------------------------------------- encoder (BERT)
 def bert_embed_ln(ids, pos, types, word, pemb, temb, g, b, eps: float, out=None):
     if out is None:
-        out = torch.empty(ids.numel(), word.shape[1], dtype=torch.bfloat16, device=ids.device)
+        out = torch.empty(ids.numel(), word.shape[1], dtype=word.dtype, device=ids.device)
     _C().bert_embed_ln(ids, pos, types, word, pemb, temb, g, b, out, eps)
     _count()
     return out
@@ -564,10 +564,26 @@ def bert_embed_ln(ids, pos, types, word, pemb, temb, g, b, eps: float, out=None)
 
 def varlen_attention(qkv, cu_seqlens, num_heads: int, head_dim: int, max_len: int, scale: float, out=None):
     if out is None:
-        out = torch.empty(qkv.shape[0], num_heads * head_dim, dtype=torch.bfloat16, device=qkv.device)
+        out = torch.empty(qkv.shape[0], num_heads * head_dim, dtype=qkv.dtype, device=qkv.device)
     _C().varlen_attention(qkv, cu_seqlens, out, num_heads, head_dim, max_len, scale)
     _count()
     return out
+
+
+def ln_residual_f32(delta, resid, w, b, eps: float, out=None):
+    """fp32 LayerNorm(delta + resid) per row."""
+    if out is None:
+        out = torch.empty_like(resid)
+    _C().ln_residual_f32(delta, resid, w, b, out, eps)
+    _count()
+    return out
+
+
+def gelu_f32_(x):
+    """Exact (erf) GELU of an fp32 tensor, in place."""
+    _C().gelu_f32_(x)
+    _count()
+    return x
 
 
 def mean_pool_l2(x, cu_seqlens, normalize: bool = True, out=None):

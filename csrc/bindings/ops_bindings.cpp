@@ -63,6 +63,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_tensor", &bloom::status_tensor);
   m.def("bert_embed_ln", &bloom::bert_embed_ln);
   m.def("varlen_attention", &bloom::varlen_attention);
+  m.def("ln_residual_f32", &bloom::ln_residual_f32);
+  m.def("gelu_f32_", &bloom::gelu_f32_);
   m.def("mean_pool_l2", &bloom::mean_pool_l2);
   m.def("tp_flag_words", &bloom::tp_flag_words);
   m.def("tp_allreduce_rmsnorm", &bloom::tp_allreduce_rmsnorm, py::arg("partial_ptrs"), py::arg("x_ptrs"),

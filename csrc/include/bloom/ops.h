@@ -150,6 +150,9 @@ void bert_embed_ln(const torch::Tensor& ids, const torch::Tensor& pos, const c10
 void varlen_attention(const torch::Tensor& qkv, const torch::Tensor& cu_seqlens, torch::Tensor& out, int64_t num_heads,
                       int64_t head_dim, int64_t max_len, double scale);
 void mean_pool_l2(const torch::Tensor& x, const torch::Tensor& cu_seqlens, torch::Tensor& out, bool normalize);
+void ln_residual_f32(const torch::Tensor& delta, const torch::Tensor& resid, const torch::Tensor& g,
+                     const torch::Tensor& b, torch::Tensor& out, double eps);
+void gelu_f32_(torch::Tensor& x);
 
 // Status word.
 torch::Tensor status_tensor(int64_t device);

@@ -37,12 +37,24 @@ __device__ __forceinline__ float block_sum_b(float v, float* red) {
   return r;
 }
 
+// Kernels below are instantiated for bf16 (the tensor-core path) and fp32
+// (the full-precision path: fp32 weights and activations end to end).
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
+
 // one CTA per token; H <= 1024 (one element per thread)
+template <typename T>
 __global__ void bert_embed_ln_kernel(const int* __restrict__ ids, const int* __restrict__ pos,
-                                     const int* __restrict__ types, const __nv_bfloat16* __restrict__ word,
-                                     const __nv_bfloat16* __restrict__ pemb, const __nv_bfloat16* __restrict__ temb,
-                                     const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ b,
-                                     __nv_bfloat16* __restrict__ out, int H, int V, int P, float eps) {
+                                     const int* __restrict__ types, const T* __restrict__ word,
+                                     const T* __restrict__ pemb, const T* __restrict__ temb,
+                                     const T* __restrict__ g, const T* __restrict__ b,
+                                     T* __restrict__ out, int H, int V, int P, float eps) {
   __shared__ float red[33];
   const long t = blockIdx.x;
   const int i = threadIdx.x;
@@ -52,19 +64,39 @@ __global__ void bert_embed_ln_kernel(const int* __restrict__ ids, const int* __r
   p = p < 0 ? 0 : (p >= P ? P - 1 : p);
   const int tt = types != nullptr ? types[t] : 0;
   float v = 0.f;
-  if (i < H)
-    v = __bfloat162float(word[(long)id * H + i]) + __bfloat162float(pemb[(long)p * H + i]) +
-        __bfloat162float(temb[(long)tt * H + i]);
+  if (i < H) v = to_f(word[(long)id * H + i]) + to_f(pemb[(long)p * H + i]) + to_f(temb[(long)tt * H + i]);
   const float mean = block_sum_b(i < H ? v : 0.f, red) / H;
   const float d = i < H ? v - mean : 0.f;
   const float inv = rsqrtf(block_sum_b(d * d, red) / H + eps);
-  if (i < H) out[t * H + i] = __float2bfloat16(d * inv * __bfloat162float(g[i]) + __bfloat162float(b[i]));
+  if (i < H) out[t * H + i] = from_f<T>(d * inv * to_f(g[i]) + to_f(b[i]));
+}
+
+// fp32 path: out = LayerNorm(delta + resid) per row; one CTA per row, H <= 1024
+__global__ void ln_residual_f32_kernel(const float* __restrict__ delta, const float* __restrict__ resid,
+                                       const float* __restrict__ g, const float* __restrict__ b,
+                                       float* __restrict__ out, int H, float eps) {
+  __shared__ float red[33];
+  const long t = blockIdx.x;
+  const int i = threadIdx.x;
+  const float v = i < H ? delta[t * H + i] + resid[t * H + i] : 0.f;
+  const float mean = block_sum_b(v, red) / H;
+  const float d = i < H ? v - mean : 0.f;
+  const float inv = rsqrtf(block_sum_b(d * d, red) / H + eps);
+  if (i < H) out[t * H + i] = d * inv * g[i] + b[i];
+}
+
+// fp32 path: exact (erf) GELU in place
+__global__ void gelu_f32_kernel(float* __restrict__ x, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    x[i] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+  }
 }
 
 // qkv: [T, 3 * NH * D] (q | k | v); out: [T, NH * D].  grid (num_seqs, NH), block 256 threads.
-template <int D>
-__global__ void varlen_attention_kernel(const __nv_bfloat16* __restrict__ qkv, const int* __restrict__ cu,
-                                        __nv_bfloat16* __restrict__ out, int NH, float scale) {
+template <int D, typename T>
+__global__ void varlen_attention_kernel(const T* __restrict__ qkv, const int* __restrict__ cu,
+                                        T* __restrict__ out, int NH, float scale) {
   extern __shared__ float sm[];
   const int s = blockIdx.x, h = blockIdx.y;
   const int t0 = cu[s], L = cu[s + 1] - t0;
@@ -73,21 +105,21 @@ __global__ void varlen_attention_kernel(const __nv_bfloat16* __restrict__ qkv, c
   const long ld = 3L * NH * D;
   for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
     const int j = idx / D, d = idx - j * D;
-    const __nv_bfloat16* row = qkv + (long)(t0 + j) * ld;
-    Ks[idx] = __bfloat162float(row[(long)NH * D + h * D + d]);
-    Vs[idx] = __bfloat162float(row[2L * NH * D + h * D + d]);
+    const T* row = qkv + (long)(t0 + j) * ld;
+    Ks[idx] = to_f(row[(long)NH * D + h * D + d]);
+    Vs[idx] = to_f(row[2L * NH * D + h * D + d]);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
   constexpr int PER = (D + 31) / 32;  // dims per lane
   for (int qi = warp; qi < L; qi += nw) {
-    const __nv_bfloat16* qrow = qkv + (long)(t0 + qi) * ld + h * D;
+    const T* qrow = qkv + (long)(t0 + qi) * ld + h * D;
     float q[PER];
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int d = lane + 32 * k;
-      q[k] = d < D ? __bfloat162float(qrow[d]) * scale : 0.f;
+      q[k] = d < D ? to_f(qrow[d]) * scale : 0.f;
     }
     float m = -INFINITY, l = 0.f, o[PER];
 #pragma unroll
@@ -111,11 +143,11 @@ __global__ void varlen_attention_kernel(const __nv_bfloat16* __restrict__ qkv, c
       }
       m = mn;
     }
-    __nv_bfloat16* orow = out + (long)(t0 + qi) * NH * D + h * D;
+    T* orow = out + (long)(t0 + qi) * NH * D + h * D;
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int d = lane + 32 * k;
-      if (d < D) orow[d] = __float2bfloat16(o[k] / l);
+      if (d < D) orow[d] = from_f<T>(o[k] / l);
     }
   }
 }
@@ -280,7 +312,8 @@ __global__ void __launch_bounds__(128) varlen_attention_tc_kernel(const __nv_bfl
 }
 
 // one CTA per sequence; out f32 [S, H]
-__global__ void mean_pool_l2_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ cu,
+template <typename T>
+__global__ void mean_pool_l2_kernel(const T* __restrict__ x, const int* __restrict__ cu,
                                     float* __restrict__ out, int H, int normalize) {
   __shared__ float red[33];
   const int s = blockIdx.x;
@@ -288,7 +321,7 @@ __global__ void mean_pool_l2_kernel(const __nv_bfloat16* __restrict__ x, const i
   const int i = threadIdx.x;
   float acc = 0.f;
   if (i < H)
-    for (int j = 0; j < L; ++j) acc += __bfloat162float(x[(long)(t0 + j) * H + i]);
+    for (int j = 0; j < L; ++j) acc += to_f(x[(long)(t0 + j) * H + i]);
   acc = L > 0 ? acc / L : 0.f;
   float nrm = 1.f;
   if (normalize) nrm = rsqrtf(fmaxf(block_sum_b(i < H ? acc * acc : 0.f, red), 1e-24f));
@@ -302,15 +335,49 @@ void bert_embed_ln(const torch::Tensor& ids, const torch::Tensor& pos, const c10
                    const torch::Tensor& g, const torch::Tensor& b, torch::Tensor& out, double eps) {
   const int T = ids.numel(), H = word.size(1);
   TORCH_CHECK(H <= 1024, "bert_embed_ln: hidden size <= 1024");
+  TORCH_CHECK(out.scalar_type() == word.scalar_type(), "bert_embed_ln: out and tables share a dtype");
   if (T == 0) return;
   const at::cuda::CUDAGuard guard(ids.device());
   const int threads = ((H + 31) / 32) * 32;
-  bert_embed_ln_kernel<<<T, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int>(), pos.data_ptr<int>(), types.has_value() ? types->data_ptr<int>() : nullptr,
-      reinterpret_cast<const __nv_bfloat16*>(word.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(pemb.data_ptr()),
-      reinterpret_cast<const __nv_bfloat16*>(temb.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
-      reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H,
-      word.size(0), pemb.size(0), float(eps));
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int* tp = types.has_value() ? types->data_ptr<int>() : nullptr;
+  if (word.scalar_type() == at::kFloat) {
+    bert_embed_ln_kernel<float><<<T, threads, 0, st>>>(
+        ids.data_ptr<int>(), pos.data_ptr<int>(), tp, word.data_ptr<float>(), pemb.data_ptr<float>(),
+        temb.data_ptr<float>(), g.data_ptr<float>(), b.data_ptr<float>(), out.data_ptr<float>(), H, word.size(0),
+        pemb.size(0), float(eps));
+  } else {
+    TORCH_CHECK(word.scalar_type() == at::kBFloat16, "bert_embed_ln: bf16 or fp32 tables");
+    bert_embed_ln_kernel<__nv_bfloat16><<<T, threads, 0, st>>>(
+        ids.data_ptr<int>(), pos.data_ptr<int>(), tp, reinterpret_cast<const __nv_bfloat16*>(word.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(pemb.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(temb.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, word.size(0), pemb.size(0), float(eps));
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ln_residual_f32(const torch::Tensor& delta, const torch::Tensor& resid, const torch::Tensor& g,
+                     const torch::Tensor& b, torch::Tensor& out, double eps) {
+  TORCH_CHECK(delta.scalar_type() == at::kFloat && resid.scalar_type() == at::kFloat && delta.is_contiguous() &&
+                  resid.is_contiguous() && out.is_contiguous(), "ln_residual_f32: contiguous fp32 [T, H]");
+  const int T = delta.size(0), H = delta.size(1);
+  TORCH_CHECK(H <= 1024, "ln_residual_f32: hidden size <= 1024");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(delta.device());
+  ln_residual_f32_kernel<<<T, ((H + 31) / 32) * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      delta.data_ptr<float>(), resid.data_ptr<float>(), g.data_ptr<float>(), b.data_ptr<float>(),
+      out.data_ptr<float>(), H, float(eps));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gelu_f32_(torch::Tensor& x) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous(), "gelu_f32_: contiguous fp32");
+  const long n = x.numel();
+  if (n == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  const int blocks = static_cast<int>(std::min<long>((n + 255) / 256, 148L * 16));
+  gelu_f32_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(x.data_ptr<float>(), n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -328,7 +395,7 @@ void varlen_attention(const torch::Tensor& qkv, const torch::Tensor& cu_seqlens,
   }();
   const bool aligned = reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0 && qkv.is_contiguous() &&
                        out.is_contiguous() && reinterpret_cast<uintptr_t>(out.data_ptr()) % 4 == 0;
-  if (tc && aligned) {
+  if (tc && aligned && qkv.scalar_type() == at::kBFloat16) {
     const int Lp = int((max_len + 15) / 16 * 16);
     const size_t smem_tc = 2 * size_t(Lp) * head_dim * sizeof(__nv_bfloat16);
     dim3 g3(S, num_heads, int((max_len + 63) / 64));
@@ -348,18 +415,34 @@ void varlen_attention(const torch::Tensor& qkv, const torch::Tensor& cu_seqlens,
   }
   const size_t smem = 2 * size_t(max_len) * head_dim * sizeof(float);
   dim3 grid(S, num_heads);
+  if (qkv.scalar_type() == at::kFloat) {
+    TORCH_CHECK(out.scalar_type() == at::kFloat, "varlen_attention: fp32 qkv needs an fp32 output");
+    if (head_dim == 32) {
+      cudaFuncSetAttribute(varlen_attention_kernel<32, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           2 * 512 * 32 * 4);
+      varlen_attention_kernel<32, float><<<grid, 256, smem, s>>>(qkv.data_ptr<float>(), cu_seqlens.data_ptr<int>(),
+                                                                 out.data_ptr<float>(), int(num_heads), float(scale));
+    } else {
+      cudaFuncSetAttribute(varlen_attention_kernel<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           2 * 512 * 64 * 4);
+      varlen_attention_kernel<64, float><<<grid, 256, smem, s>>>(qkv.data_ptr<float>(), cu_seqlens.data_ptr<int>(),
+                                                                 out.data_ptr<float>(), int(num_heads), float(scale));
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   if (head_dim == 32) {
-    cudaFuncSetAttribute(varlen_attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 32 * 4);
-    varlen_attention_kernel<32><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
-                                                       cu_seqlens.data_ptr<int>(),
-                                                       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                       int(num_heads), float(scale));
+    cudaFuncSetAttribute(varlen_attention_kernel<32, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         2 * 512 * 32 * 4);
+    varlen_attention_kernel<32, __nv_bfloat16><<<grid, 256, smem, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cu_seqlens.data_ptr<int>(),
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(num_heads), float(scale));
   } else {
-    cudaFuncSetAttribute(varlen_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 64 * 4);
-    varlen_attention_kernel<64><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
-                                                       cu_seqlens.data_ptr<int>(),
-                                                       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                       int(num_heads), float(scale));
+    cudaFuncSetAttribute(varlen_attention_kernel<64, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         2 * 512 * 64 * 4);
+    varlen_attention_kernel<64, __nv_bfloat16><<<grid, 256, smem, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cu_seqlens.data_ptr<int>(),
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(num_heads), float(scale));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -369,9 +452,14 @@ void mean_pool_l2(const torch::Tensor& x, const torch::Tensor& cu_seqlens, torch
   TORCH_CHECK(H <= 1024, "mean_pool_l2: hidden size <= 1024");
   if (S <= 0) return;
   const at::cuda::CUDAGuard guard(x.device());
-  mean_pool_l2_kernel<<<S, ((H + 31) / 32) * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), cu_seqlens.data_ptr<int>(), out.data_ptr<float>(), H,
-      normalize ? 1 : 0);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (x.scalar_type() == at::kFloat)
+    mean_pool_l2_kernel<float><<<S, ((H + 31) / 32) * 32, 0, st>>>(x.data_ptr<float>(), cu_seqlens.data_ptr<int>(),
+                                                                  out.data_ptr<float>(), H, normalize ? 1 : 0);
+  else
+    mean_pool_l2_kernel<__nv_bfloat16><<<S, ((H + 31) / 32) * 32, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), cu_seqlens.data_ptr<int>(), out.data_ptr<float>(), H,
+        normalize ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
