@@ -123,6 +123,10 @@ class EngineConfig:
     # result to this JSON-lines file ("{rank}" expands to the TP rank; also
     # BLOOM_STEP_LOG); `python -m bloom_b200.engine.replay <file>` re-runs it
     step_log: str = ""
+    # KV cache element type: "bf16" or "int8" (per-token, per-head symmetric
+    # scale; halves the KV bytes decode attention reads).  BLOOM_KV_CACHE_DTYPE
+    # sets the default.
+    kv_cache_dtype: str = field(default_factory=lambda: os.environ.get("BLOOM_KV_CACHE_DTYPE", "bf16"))
 
 
 VICTIM_POLICIES = {"newest": 0, "priority": 1, "oldest": 2, "kv_cost": 3, "aegaeon": 4, "lru": 5, "largest_first": 6}
@@ -164,9 +168,9 @@ class LLMEngine:
             torch.cuda.synchronize(dev)
             free, total = torch.cuda.mem_get_info(dev)
             reserve = int(total * (1.0 - ec.gpu_memory_utilization)) + (4 << 30)  # activations, graphs
-            budget = max(free - reserve, 64 * kv_block_bytes(model))
+            budget = max(free - reserve, 64 * kv_block_bytes(model, 16, ec.kv_cache_dtype))
             need = ec.max_num_seqs * ((ec.max_model_len + 15) // 16) + 64
-            ec.num_blocks = int(min(budget // kv_block_bytes(model), max(need, 1024)))
+            ec.num_blocks = int(min(budget // kv_block_bytes(model, 16, ec.kv_cache_dtype), max(need, 1024)))
         sc = rt.SchedulerConfig()
         sc.max_num_seqs = ec.max_num_seqs
         sc.max_num_batched_tokens = ec.max_num_batched_tokens
@@ -183,7 +187,8 @@ class LLMEngine:
         sc.max_preemptions_per_request = int(ec.max_preemptions_per_request)
         sc.priority_preempt_ms = float(ec.priority_preemption_ms)
         sc.kv_admission_threshold = float(ec.kv_admission_threshold)
-        swap_slots = int(ec.swap_space_bytes) // kv_block_bytes(model) if ec.swap_space_bytes > 0 else 0
+        swap_slots = (int(ec.swap_space_bytes) // kv_block_bytes(model, 16, ec.kv_cache_dtype)
+                      if ec.swap_space_bytes > 0 else 0)
         sc.swap_slots = swap_slots
         self.scheduler = rt.Scheduler(sc, ec.num_blocks, 16, ec.enable_prefix_caching)
         log = ec.step_log or os.environ.get("BLOOM_STEP_LOG", "")
@@ -194,7 +199,8 @@ class LLMEngine:
             self.scheduler = SchedulerRecorder(self.scheduler, log.replace("{rank}", str(rank)), sc, ec.num_blocks,
                                                16, ec.enable_prefix_caching)
         self.runner = ModelRunner(model, ec.num_blocks, ec.max_num_seqs, ec.max_num_batched_tokens,
-                                  ec.max_model_len, ec.use_cuda_graphs, spec_len=int(ec.spec_len))
+                                  ec.max_model_len, ec.use_cuda_graphs, spec_len=int(ec.spec_len),
+                                  kv_dtype=ec.kv_cache_dtype)
         if ec.autotune and dev.type == "cuda":
             from .. import ops
 
@@ -417,9 +423,10 @@ class LLMEngine:
     def export_state(self, request_id: int) -> bytes:
         """Serialise a live request's KV cache and tokens (between steps) into
         a blob: magic, header length, JSON header (model fingerprint, layout,
-        tokens, sampling parameters), then the request's KV pages as bf16
-        [blocks, layers, 2, kv_heads, 16, head_dim] (this rank's heads under
-        tensor parallelism).  `import_state` on an engine with the same model
+        tokens, sampling parameters), then the request's KV pages in the cache's
+        own layout: bf16 [blocks, layers, 2, kv_heads, 16, head_dim], or for an
+        int8 cache the per-layer block bytes [blocks, layers, bytes] (this
+        rank's heads under tensor parallelism).  `import_state` on an engine with the same model
         and layout resumes it without recomputing the prefix.  Reference:
         Model::export_state / import_state and StateBlob
         (crates/engine/src/core/model.rs:11-21,215-238)."""
@@ -433,11 +440,12 @@ class LLMEngine:
             idx = torch.tensor(blocks, dtype=torch.long, device=self.model.device)
             pages = self.runner.kv_cache.index_select(1, idx).transpose(0, 1).contiguous().cpu()
         else:
-            pages = torch.empty(0, dtype=torch.bfloat16)
+            pages = torch.empty(0, dtype=self.runner.kv_cache.dtype)
         sp = st["params"]
         r = self.requests.get(int(request_id))
         hdr = {"kind": "kv_cache", "model": self._namespace(), "num_layers": self.cfg.num_layers,
-               "kv_heads": self.model.nkv, "head_dim": self.cfg.head_dim, "block_size": 16, "dtype": "bf16",
+               "kv_heads": self.model.nkv, "head_dim": self.cfg.head_dim, "block_size": 16,
+               "dtype": self.runner.kv_dtype,
                "tp": [self.model.tp.rank, self.model.tp.size], "tokens": list(st["tokens"]),
                "num_prompt": st["num_prompt"], "num_computed": st["num_computed"], "num_blocks": len(blocks),
                "priority": st["priority"],
@@ -459,19 +467,20 @@ class LLMEngine:
         n = struct.unpack("<I", blob[8:12])[0]
         hdr = _json.loads(blob[12:12 + n])
         want = {"model": self._namespace(), "num_layers": self.cfg.num_layers, "kv_heads": self.model.nkv,
-                "head_dim": self.cfg.head_dim, "block_size": 16, "dtype": "bf16",
+                "head_dim": self.cfg.head_dim, "block_size": 16, "dtype": self.runner.kv_dtype,
                 "tp": [self.model.tp.rank, self.model.tp.size]}
         for k, v in want.items():
             if hdr.get(k) != v:
                 raise ValueError(f"KV state blob does not match this engine: {k} {hdr.get(k)!r} != {v!r}")
         nb = int(hdr["num_blocks"])
         payload = memoryview(blob)[12 + n:]
-        shape = (nb, self.cfg.num_layers, 2, self.model.nkv, 16, self.cfg.head_dim)
+        kv = self.runner.kv_cache
+        shape = (nb, kv.shape[0], *kv.shape[2:])
         numel = 1
         for d in shape:
             numel *= d
-        if len(payload) != numel * 2:
-            raise ValueError(f"KV state blob payload has {len(payload)} bytes, expected {numel * 2}")
+        if len(payload) != numel * kv.element_size():
+            raise ValueError(f"KV state blob payload has {len(payload)} bytes, expected {numel * kv.element_size()}")
         if params is None:
             p = hdr["params"]
             params = SamplingParams(max_tokens=p["max_tokens"], temperature=p["temperature"], top_p=p["top_p"],
@@ -482,7 +491,7 @@ class LLMEngine:
         rid, table = self.scheduler.import_sequence(tokens, int(hdr["num_prompt"]), int(hdr["num_computed"]),
                                                     params.to_native(self._seed_counter), int(hdr["priority"]))
         if nb:
-            pages = torch.frombuffer(bytearray(payload), dtype=torch.bfloat16).view(shape)
+            pages = torch.frombuffer(bytearray(payload), dtype=kv.dtype).view(shape)
             dev_pages = pages.to(self.model.device, non_blocking=False)
             k = min(nb, len(table))
             idx = torch.tensor(list(table[:k]), dtype=torch.long, device=self.model.device)

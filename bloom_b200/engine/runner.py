@@ -28,8 +28,12 @@ from ..models.llama import DecoderLM, StepInputs
 DEFAULT_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512]
 
 
-def kv_block_bytes(model: DecoderLM, block_size: int = 16) -> int:
+def kv_block_bytes(model: DecoderLM, block_size: int = 16, kv_dtype: str = "bf16") -> int:
+    """Bytes of one KV block over all layers: bf16 pages, or int8 pages plus
+    one fp32 scale per token and head (ops.kv_q8_block_bytes)."""
     cfg = model.cfg
+    if kv_dtype == "int8":
+        return cfg.num_layers * ops.kv_q8_block_bytes(model.nkv, cfg.head_dim)
     return cfg.num_layers * 2 * model.nkv * block_size * cfg.head_dim * 2
 
 
@@ -44,6 +48,7 @@ class ModelRunner:
         use_cuda_graphs: bool = True,
         graph_buckets: Optional[List[int]] = None,
         spec_len: int = 0,
+        kv_dtype: str = "bf16",
     ):
         self.model = model
         self.cfg = model.cfg
@@ -57,8 +62,15 @@ class ModelRunner:
         self.num_blocks = num_blocks
         cfg = self.cfg
         # zero-filled: masked tail slots of a page are multiplied by p = 0, which must not meet NaN bit patterns
-        self.kv_cache = torch.zeros(cfg.num_layers, num_blocks, 2, model.nkv, self.block_size, cfg.head_dim,
-                                    dtype=torch.bfloat16, device=self.device)
+        if kv_dtype not in ("bf16", "int8"):
+            raise ValueError(f"kv cache dtype must be bf16 or int8, not {kv_dtype!r}")
+        self.kv_dtype = kv_dtype
+        if kv_dtype == "int8":
+            self.kv_cache = torch.zeros(cfg.num_layers, num_blocks, ops.kv_q8_block_bytes(model.nkv, cfg.head_dim),
+                                        dtype=torch.uint8, device=self.device)
+        else:
+            self.kv_cache = torch.zeros(cfg.num_layers, num_blocks, 2, model.nkv, self.block_size, cfg.head_dim,
+                                        dtype=torch.bfloat16, device=self.device)
         rt = _rt()
         worst = rt.arena_layout(self.max_tokens, max_num_seqs, max_num_seqs,
                                 self.max_tokens // 64 + max_num_seqs, self.max_tokens + max_num_seqs,
@@ -96,7 +108,12 @@ class ModelRunner:
 
     # ------------------------------------------------------------ CacheMesh tiers
     def kv_block_bytes(self) -> int:
-        return kv_block_bytes(self.model, self.block_size)
+        return kv_block_bytes(self.model, self.block_size, self.kv_dtype)
+
+    def _block_slots(self, buf: torch.Tensor, slots: int) -> torch.Tensor:
+        """A host byte buffer seen as `slots` KV blocks shaped like kv_cache[:, blk]."""
+        kv = self.kv_cache
+        return buf.view(kv.dtype).view(slots, kv.shape[0], *kv.shape[2:])
 
     def enable_cachemesh(self, scheduler, l2_bytes: int, l3_dir: str = "", l3_max_blocks: int = 0,
                          namespace: str = "default") -> None:
@@ -105,9 +122,7 @@ class ModelRunner:
         bb = self.kv_block_bytes()
         slots = max(1, int(l2_bytes) // bb)
         self.l2 = torch.empty(slots * bb, dtype=torch.uint8).pin_memory()
-        cfg = self.cfg
-        self.l2_view = self.l2.view(torch.bfloat16).view(slots, cfg.num_layers, 2, self.model.nkv, self.block_size,
-                                                         cfg.head_dim)
+        self.l2_view = self._block_slots(self.l2, slots)
         scheduler.enable_cachemesh(self.l2, bb, l3_dir, int(l3_max_blocks), namespace)
 
     def apply_kv_copies(self, restores, offloads) -> None:
@@ -126,9 +141,7 @@ class ModelRunner:
         """Pinned host slots (one KV block each, all layers) for swap preemption."""
         bb = self.kv_block_bytes()
         self.swap = torch.empty(max(1, slots) * bb, dtype=torch.uint8).pin_memory()
-        cfg = self.cfg
-        self.swap_view = self.swap.view(torch.bfloat16).view(max(1, slots), cfg.num_layers, 2, self.model.nkv,
-                                                             self.block_size, cfg.head_dim)
+        self.swap_view = self._block_slots(self.swap, max(1, slots))
 
     def apply_swaps(self, swap_ins, swap_outs) -> None:
         """Swap-ins (host slot -> block) before swap-outs (block -> slot): a

@@ -421,8 +421,58 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor
     return out
 
 
+# ---------------------------------------------------------------- int8 KV cache
+# An int8 cache is a uint8 tensor [L, NB, 2 x KVH x 16 x (128 + 4)]: per layer
+# and block the K pages [KVH][16][128], the dim-major V pages [KVH][128][16],
+# then one fp32 scale per (K or V, head, token).  head_dim 128 only.
+Q8_HEAD_DIM = 128
+
+
+def kv_q8_block_bytes(num_kv_heads: int, head_dim: int = Q8_HEAD_DIM) -> int:
+    if head_dim != Q8_HEAD_DIM:
+        raise ValueError(f"the int8 KV cache supports head_dim {Q8_HEAD_DIM} only (got {head_dim})")
+    return 2 * num_kv_heads * 16 * (head_dim + 4)
+
+
+def _q8_kv_heads(kv_cache: torch.Tensor) -> int:
+    return kv_cache.shape[2] // (2 * 16 * (Q8_HEAD_DIM + 4))
+
+
+def is_q8_cache(kv_cache: torch.Tensor) -> bool:
+    return kv_cache.dtype == torch.uint8
+
+
+_Q8_SCRATCH: dict = {}
+
+
+def _q8_prefill_view(kv_cache, layer, block_table, ctx_lens):
+    """Dequantise the pages the prefill rows read into a bf16 scratch cache;
+    returns (scratch as a one-layer bf16 cache, its block table)."""
+    S, W = int(ctx_lens.shape[0]), int(block_table.shape[1])
+    nkv = _q8_kv_heads(kv_cache)
+    dev = kv_cache.device
+    need = S * W * 2 * nkv * 16 * Q8_HEAD_DIM
+    buf = _Q8_SCRATCH.get(dev)
+    if buf is None or buf.numel() < need:
+        buf = torch.empty(need, dtype=torch.bfloat16, device=dev)
+        _Q8_SCRATCH[dev] = buf
+    key = (dev, "bt", S, W)
+    bt = _Q8_SCRATCH.get(key)
+    if bt is None:
+        bt = torch.arange(S * W, dtype=torch.int32, device=dev).view(S, W)
+        _Q8_SCRATCH[key] = bt
+    _C().kv_dequant_pages_q8(kv_cache, layer, nkv, block_table, ctx_lens, W, buf, status(dev.index))
+    _count()
+    return buf[:need].view(1, S * W, 2, nkv, 16, Q8_HEAD_DIM), bt
+
+
 def rope_kv_write(qkv, positions, slot_mapping, cos_sin, q_out, kv_cache, layer, num_q_heads, num_kv_heads,
                   q_norm=None, k_norm=None, eps: float = 1e-6):
+    if is_q8_cache(kv_cache):
+        _C().rope_kv_write_q8(qkv, positions, slot_mapping, cos_sin, q_out, kv_cache, layer, num_q_heads,
+                              num_kv_heads, q_norm, k_norm, eps)
+        _count()
+        return q_out
     _C().rope_kv_write(qkv, positions, slot_mapping, cos_sin, q_out, kv_cache, layer, num_q_heads, num_kv_heads,
                        q_norm, k_norm, eps)
     _count()
@@ -481,11 +531,17 @@ def decode_workspace_numel(batch: int, num_kv_heads: int, splits: int, head_chun
 
 def paged_decode_attention(q, kv_cache, layer, block_table, seq_lens, out, *, q_len: int = 1, splits: int = 1,
                            workspace: Optional[torch.Tensor] = None, scale: float):
+    nkv = _q8_kv_heads(kv_cache) if is_q8_cache(kv_cache) else kv_cache.shape[3]
     if workspace is None:
-        hc = decode_head_chunks(q.shape[-2], kv_cache.shape[3], q_len)
+        hc = decode_head_chunks(q.shape[-2], nkv, q_len)
         workspace = torch.empty(
-            decode_workspace_numel(seq_lens.shape[0], kv_cache.shape[3], splits, hc), dtype=torch.float32,
+            decode_workspace_numel(seq_lens.shape[0], nkv, splits, hc), dtype=torch.float32,
             device=q.device)
+    if is_q8_cache(kv_cache):
+        _C().paged_decode_attention_q8(q, kv_cache, layer, nkv, block_table, seq_lens, out, q_len, splits, workspace,
+                                       scale, status(q.device.index))
+        _count(2 if splits > 1 else 1)
+        return out
     _C().paged_decode_attention(q, kv_cache, layer, block_table, seq_lens, out, q_len, splits, workspace, scale,
                                 status(q.device.index))
     _count(2 if splits > 1 else 1)
@@ -500,6 +556,9 @@ def paged_prefill_attention(q, kv_cache, layer, block_table, ctx_lens, cu_seqlen
     """Causal (or full) attention of chunked-prefill query rows over the paged
     cache; tiles are 128 query rows (see `prefill_tiles`).  head_dim 128 runs
     on tcgen05 (S and O in TMEM), head_dim 64 on the mma.sync kernel."""
+    if is_q8_cache(kv_cache):  # int8 cache: the pages these rows read, dequantised
+        kv_cache, block_table = _q8_prefill_view(kv_cache, layer, block_table, ctx_lens)
+        layer = 0
     fn = _C().paged_prefill_attention_tc if (_PREFILL_TC and q.shape[-1] == 128) else _C().paged_prefill_attention
     fn(q, kv_cache, layer, block_table, ctx_lens, cu_seqlens_q, tile_seq, tile_start, out, scale, causal,
        status(q.device.index))

@@ -71,6 +71,27 @@ def gather_paged(kv_cache, layer, block_table_row, length):
     return k, v
 
 
+def dequant_q8_cache(kv_u8, num_kv_heads: int, head_dim: int = 128):
+    """fp32 [L, NB, 2, Hkv, 16, D] of an int8 cache [L, NB, block bytes]: K
+    pages [Hkv][16][D], dim-major V pages [Hkv][D][16], then fp32 scales
+    [2][Hkv][16] per block (the layout rope_kv_write writes for int8)."""
+    L, NB, BB = kv_u8.shape
+    P = num_kv_heads * 16 * head_dim
+    k = kv_u8[:, :, :P].contiguous().view(torch.int8).view(L, NB, num_kv_heads, 16, head_dim).float()
+    v = kv_u8[:, :, P:2 * P].contiguous().view(torch.int8).view(L, NB, num_kv_heads, head_dim, 16)
+    v = v.transpose(-1, -2).float()
+    sc = kv_u8[:, :, 2 * P:].contiguous().view(torch.float32).view(L, NB, 2, num_kv_heads, 16)
+    return torch.stack([k * sc[:, :, 0, :, :, None], v * sc[:, :, 1, :, :, None]], 2)
+
+
+def quantize_q8_rows(x):
+    """Symmetric int8 of the last dimension: (int8 values, fp32 scale = absmax / 127)."""
+    am = x.float().abs().amax(-1, keepdim=True)
+    inv = torch.where(am > 0, 127.0 / am, torch.zeros_like(am))
+    q = torch.round(x.float() * inv).clamp(-127, 127)
+    return q, (am / 127.0).squeeze(-1)
+
+
 # ---------------------------------------------------------------- quantised formats (fp32 restatements)
 
 NF4_CODEBOOK = (-1.0, -0.6961928009986877, -0.5250730514526367, -0.39491748809814453, -0.28444138169288635,

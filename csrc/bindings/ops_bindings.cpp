@@ -65,6 +65,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("varlen_attention", &bloom::varlen_attention);
   m.def("ln_residual_f32", &bloom::ln_residual_f32);
   m.def("gelu_f32_", &bloom::gelu_f32_);
+  m.def("paged_decode_attention_q8", &bloom::paged_decode_attention_q8);
+  m.def("kv_dequant_pages_q8", &bloom::kv_dequant_pages_q8);
+  m.def("rope_kv_write_q8", &bloom::rope_kv_write_q8);
   m.def("mean_pool_l2", &bloom::mean_pool_l2);
   m.def("tp_flag_words", &bloom::tp_flag_words);
   m.def("tp_allreduce_rmsnorm", &bloom::tp_allreduce_rmsnorm, py::arg("partial_ptrs"), py::arg("x_ptrs"),

@@ -69,6 +69,18 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
                             const torch::Tensor& block_table, const torch::Tensor& seq_lens, torch::Tensor& out,
                             int64_t q_len, int64_t splits, torch::Tensor& workspace, double scale,
                             const torch::Tensor& status);
+// int8 KV cache [L, NB, 2 x KVH x 16 x (128 + 4) bytes]: K pages, dim-major V pages, fp32 scales per block.
+void paged_decode_attention_q8(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                               int64_t num_kv_heads, const torch::Tensor& block_table, const torch::Tensor& seq_lens,
+                               torch::Tensor& out, int64_t q_len, int64_t splits, torch::Tensor& workspace,
+                               double scale, const torch::Tensor& status);
+void kv_dequant_pages_q8(const torch::Tensor& kv_cache, int64_t layer, int64_t num_kv_heads,
+                         const torch::Tensor& block_table, const torch::Tensor& ctx_lens, int64_t W,
+                         torch::Tensor& scratch, const torch::Tensor& status);
+void rope_kv_write_q8(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& slot_mapping,
+                      const torch::Tensor& cos_sin, torch::Tensor& q_out, torch::Tensor& kv_cache, int64_t layer,
+                      int64_t num_q_heads, int64_t num_kv_heads, const c10::optional<torch::Tensor>& q_norm,
+                      const c10::optional<torch::Tensor>& k_norm, double eps);
 void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
                              const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
                              const torch::Tensor& cu_seqlens_q, const torch::Tensor& tile_seq,

@@ -80,6 +80,10 @@ struct DecodeArgs {
   float scale_log2;
   int* status;
   int num_blocks;       // pages in the cache (index checks only)
+  // int8 cache (decode_q8_kernel): this layer's [NB][block bytes] region and
+  // the block size in bytes (K pages, dim-major V pages, then fp32 scales)
+  const uint8_t* q8_base;
+  long q8_block_bytes;
 };
 
 // Row r of the packed M dimension -> (q position qi, head-in-group hh).
@@ -561,6 +565,317 @@ __global__ void __launch_bounds__(kPfWarps * 32)
   }
 }
 
+// ---------------------------------------------------------------- int8 KV decode
+// Same work split, ring and merge as decode_kernel (head_dim 128), over an
+// int8 cache with one fp32 scale per (token, head).  Per page a warp's TMA
+// ring brings the K page [16 tokens][128] (128-byte swizzle), the V page
+// [128 dims][16 tokens] (dim-major) and the 2 x 16 scales (bulk copies):
+// 4.1 KB instead of 8 KB.  K and V bytes become bf16 MMA operands in
+// registers (int8 values are exact in bf16); the K scale multiplies each
+// score column and the V scale each column of P before P V, so no scaled
+// copy of a page is ever written.
+__device__ __forceinline__ uint32_t i8x2_bf16x2(uint32_t u16) {
+  const float lo = static_cast<float>(static_cast<int8_t>(u16 & 0xffu));
+  const float hi = static_cast<float>(static_cast<int8_t>((u16 >> 8) & 0xffu));
+  return pack_bf16(lo, hi);
+}
+
+template <int MT, int NWARPS, int NST>
+__global__ void __launch_bounds__(NWARPS * 32)
+    decode_q8_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                     const DecodeArgs a) {
+  constexpr int D = 128;
+  constexpr int kPageB = PAGE * D;      // one int8 page of one KV head: 2 KB
+  constexpr int kStageBytes = 2 * kPageB;
+  constexpr int kRing = NWARPS * NST * kStageBytes;
+  constexpr int kScl = NWARPS * NST * 128;  // 16 K + 16 V scales per stage
+  constexpr int kMerge = NWARPS * MT * 16 * (D + 2) * 4;
+  constexpr int kBarOff = (kRing + kScl > kMerge ? kRing + kScl : kMerge);
+  const int b = blockIdx.x, vkh = blockIdx.y, split = blockIdx.z;
+  const int kh = vkh / a.hc;
+  const int warp = warp_id(), lane = lane_id();
+  const int g = lane >> 2, t4 = lane & 3;
+  const int G = a.nq / (a.nkv * a.hc);
+  const int R = a.ql * G;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* wsm = smem + warp * NST * kStageBytes;
+  float* wscl = reinterpret_cast<float*>(smem + kRing) + warp * NST * 32;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff) + warp * NST;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
+
+  const int kv_len = a.seq_lens[b];
+  const int n_pages = (kv_len + PAGE - 1) / PAGE;
+  const int pps = (n_pages + a.splits - 1) / a.splits;
+  const int p0 = split * pps;
+  const int p1 = min(p0 + pps, n_pages);
+  const int first = p0 + warp;
+  const int my_n = (p1 > first) ? (p1 - first + NWARPS - 1) / NWARPS : 0;
+  const int* bt = a.block_table + (long)b * a.bt_stride;
+  const long rpbK = a.q8_block_bytes / D;   // K-map rows (128 B) per block
+  const long rpbV = a.q8_block_bytes / 16;  // V-map rows (16 B) per block
+
+  if (lane == 0) {
+    for (int s = 0; s < NST; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int i) {
+    const int s = i % NST;
+    const int page = first + i * NWARPS;
+    int blk = bt[page];
+    if (!kcheck(blk >= 0 && blk < a.num_blocks, a.status)) blk = 0;
+    uint8_t* st = wsm + s * kStageBytes;
+    mbar_arrive_expect_tx(&bars[s], kStageBytes + 128);
+    tma_load_2d(st, &tmK, &bars[s], 0, static_cast<int>(blk * rpbK + kh * PAGE));
+    tma_load_2d(st + kPageB, &tmV, &bars[s], 0, static_cast<int>(blk * rpbV + (long)(a.nkv + kh) * D));
+    const uint8_t* sc = a.q8_base + (long)blk * a.q8_block_bytes + 2L * a.nkv * PAGE * D;
+    bulk_load(wscl + s * 32, sc + kh * PAGE * 4, 64, &bars[s]);
+    bulk_load(wscl + s * 32 + 16, sc + (a.nkv + kh) * PAGE * 4, 64, &bars[s]);
+  };
+  if (lane == 0) {
+    for (int i = 0; i < NST && i < my_n; ++i) issue(i);
+  }
+
+  uint32_t qf[MT][D / 16][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = mt * 16 + g + 8 * hr;
+      const __nv_bfloat16* qrow = nullptr;
+      if (r < R) {
+        const int qi = r / G, hh = r - qi * G;
+        qrow = a.q + ((long)(b * a.ql + qi) * a.nq + vkh * G + hh) * D;
+      }
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const int d = ks * 16 + 2 * t4;
+        qf[mt][ks][hr] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
+        qf[mt][ks][hr + 2] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
+      }
+    }
+  }
+
+  float m_run[MT][2], l_run[MT][2];
+  float o[MT][D / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    m_run[mt][0] = m_run[mt][1] = kNegBig;
+    l_run[mt][0] = l_run[mt][1] = 0.f;
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) o[mt][n][0] = o[mt][n][1] = o[mt][n][2] = o[mt][n][3] = 0.f;
+  }
+  int limit[MT][2];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = mt * 16 + g + 8 * hr;
+      limit[mt][hr] = (r < R) ? kv_len - a.ql + r / G : -1;
+    }
+
+  int i = 0;
+  for (; i < my_n; ++i) {
+    const int s = i % NST;
+    if (!mbar_wait(&bars[s], (i / NST) & 1, &abort_flag, a.status, kStatusAttnTimeout)) break;
+    const uint8_t* kp = wsm + s * kStageBytes;
+    const uint8_t* vp = kp + kPageB;
+    const float* ksc = wscl + s * 32;
+    const float* vsc = ksc + 16;
+    const int tok_base = (first + i * NWARPS) * PAGE;
+    float skc[2][2], svc[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        skc[nt][e] = ksc[8 * nt + 2 * t4 + e];
+        svc[nt][e] = vsc[8 * nt + 2 * t4 + e];
+      }
+
+    float sc[MT][2][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int tok = 8 * nt + g;
+      const uint8_t* row = kp + tok * D;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint8_t* chunk = row + ((ks ^ (tok & 7)) << 4);  // 128-byte swizzle: 16-byte chunk ks of row tok
+        const uint32_t b0 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(chunk + 2 * t4));
+        const uint32_t b1 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(chunk + 8 + 2 * t4));
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) mma_bf16_16816(sc[mt][nt], qf[mt][ks], b0, b1);
+      }
+    }
+
+    uint32_t pa[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        float x[4];
+        float mx = kNegBig;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int idx = tok_base + 8 * nt + 2 * t4 + e;
+            float v = sc[mt][nt][2 * hr + e] * skc[nt][e] * a.scale_log2;
+            if (idx > limit[mt][hr]) v = -INFINITY;
+            x[nt * 2 + e] = v;
+            mx = fmaxf(mx, v);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run[mt][hr], mx);
+        const float alpha = exp2f(m_run[mt][hr] - m_new);
+        m_run[mt][hr] = m_new;
+        float ps = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          x[k] = exp2f(x[k] - m_new);
+          ps += x[k];
+        }
+        l_run[mt][hr] = l_run[mt][hr] * alpha + ps;
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) {
+          o[mt][n][2 * hr] *= alpha;
+          o[mt][n][2 * hr + 1] *= alpha;
+        }
+        pa[mt][hr] = pack_bf16(x[0] * svc[0][0], x[1] * svc[0][1]);
+        pa[mt][hr + 2] = pack_bf16(x[2] * svc[1][0], x[3] * svc[1][1]);
+      }
+    }
+
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      const uint8_t* vr = vp + (nb * 8 + g) * PAGE;  // dim nb*8+g, 16 tokens
+      const uint32_t b0 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(vr + 2 * t4));
+      const uint32_t b1 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(vr + 8 + 2 * t4));
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) mma_bf16_16816(o[mt][nb], pa[mt], b0, b1);
+    }
+    __syncwarp();
+    if (lane == 0 && i + NST < my_n) {
+      fence_proxy_async();
+      issue(i + NST);
+    }
+  }
+  if (i < my_n) {
+    if (lane == 0)
+      for (int k = i; k < my_n && k < i + NST; ++k) mbar_drain(&bars[k % NST], (k / NST) & 1);
+  }
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float l = l_run[mt][hr];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      l_run[mt][hr] = l;
+    }
+  __syncthreads();
+  constexpr int RS = D + 2;
+  float* cm = reinterpret_cast<float*>(smem);
+  float* wbuf = cm + warp * (MT * 16 * RS);
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = mt * 16 + g + 8 * hr;
+#pragma unroll
+      for (int n = 0; n < D / 8; ++n) {
+        wbuf[r * RS + 8 * n + 2 * t4] = o[mt][n][2 * hr];
+        wbuf[r * RS + 8 * n + 2 * t4 + 1] = o[mt][n][2 * hr + 1];
+      }
+      if (t4 == 0) {
+        wbuf[r * RS + D] = m_run[mt][hr];
+        wbuf[r * RS + D + 1] = l_run[mt][hr];
+      }
+    }
+  __syncthreads();
+  const int rows = min(R, MT * 16);
+  for (int idx = threadIdx.x; idx < rows * D; idx += NWARPS * 32) {
+    const int r = idx / D, d = idx - r * D;
+    float M = kNegBig;
+#pragma unroll
+    for (int w = 0; w < NWARPS; ++w) M = fmaxf(M, cm[w * MT * 16 * RS + r * RS + D]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARPS; ++w) {
+      const float* wb = cm + w * MT * 16 * RS + r * RS;
+      const float scl = exp2f(wb[D] - M);
+      L += wb[D + 1] * scl;
+      O += wb[d] * scl;
+    }
+    if (a.splits == 1) {
+      const int qi = r / G, hh = r - qi * G;
+      a.out[((long)(b * a.ql + qi) * a.nq + vkh * G + hh) * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+    } else {
+      float* pr = a.part + ((((long)b * a.nkv * a.hc + vkh) * a.splits + split) * 32 + r) * RS;
+      pr[d] = O;
+      if (d == 0) {
+        pr[D] = M;
+        pr[D + 1] = L;
+      }
+    }
+  }
+}
+
+template <int MT, int NWARPS, int NST>
+void launch_decode_q8(const CUtensorMap& tmK, const CUtensorMap& tmV, const DecodeArgs& a, int B, cudaStream_t stream) {
+  constexpr int D = 128;
+  constexpr int kRing = NWARPS * NST * 2 * PAGE * D;
+  constexpr int kScl = NWARPS * NST * 128;
+  constexpr int kMerge = NWARPS * MT * 16 * (D + 2) * 4;
+  constexpr int kBarOff = (kRing + kScl > kMerge ? kRing + kScl : kMerge);
+  constexpr int smem = kBarOff + NWARPS * NST * 8 + 1024;
+  auto kern = decode_q8_kernel<MT, NWARPS, NST>;
+  static uint64_t configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((configured >> dev) & 1u)) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured |= uint64_t(1) << dev;
+  }
+  dim3 grid(B, a.nkv * a.hc, a.splits);
+  kern<<<grid, NWARPS * 32, smem, stream>>>(tmK, tmV, a);
+}
+
+// Prefill over an int8 cache: the pages a step's prefill sequences read are
+// dequantised into a bf16 scratch cache laid out [S x W pages][2][KVH][16][128]
+// (sequence s, page p -> scratch block s * W + p), and the prefill kernels run
+// on it with the block table {s * W + p}.  grid (W, S), 256 threads.
+__global__ void kv_dequant_pages_q8_kernel(const uint8_t* __restrict__ layer_base, long block_bytes, int nkv,
+                                           const int* __restrict__ bt, int bt_stride, const int* __restrict__ ctx,
+                                           int W, __nv_bfloat16* __restrict__ scratch, int num_blocks,
+                                           int* status) {
+  constexpr int D = 128;
+  const int p = blockIdx.x, s = blockIdx.y;
+  if (p * PAGE >= ctx[s]) return;
+  int blk = bt[(long)s * bt_stride + p];
+  if (!kcheck(blk >= 0 && blk < num_blocks, status)) blk = 0;
+  const uint8_t* bp = layer_base + (long)blk * block_bytes;
+  const float* scl = reinterpret_cast<const float*>(bp + 2L * nkv * PAGE * D);
+  __nv_bfloat16* dst = scratch + ((long)s * W + p) * 2 * nkv * PAGE * D;
+  const int n = 2 * nkv * PAGE * D;
+  for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    // e = ((kv * nkv + kh) * 16 + tok) * D + d in the bf16 page layout
+    const int d = e % D, tok = (e / D) % PAGE, kvh = e / (D * PAGE);
+    const int kv = kvh / nkv;
+    const int8_t* page = reinterpret_cast<const int8_t*>(bp) + (long)kvh * PAGE * D;
+    const int8_t q = kv == 0 ? page[tok * D + d] : page[d * PAGE + tok];
+    dst[e] = __float2bfloat16(static_cast<float>(q) * scl[kvh * PAGE + tok]);
+  }
+}
+
 CUtensorMap kv_tmap(const torch::Tensor& kv_cache, int64_t layer) {
   TORCH_CHECK(kv_cache.dim() == 6 && kv_cache.size(2) == 2 && kv_cache.size(4) == PAGE &&
                   (kv_cache.size(5) == 128 || kv_cache.size(5) == 64),
@@ -675,6 +990,88 @@ void paged_decode_attention(const torch::Tensor& q, const torch::Tensor& kv_cach
                                                                             a.splits);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
+}
+
+void paged_decode_attention_q8(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,
+                               int64_t num_kv_heads, const torch::Tensor& block_table, const torch::Tensor& seq_lens,
+                               torch::Tensor& out, int64_t q_len, int64_t splits, torch::Tensor& workspace,
+                               double scale, const torch::Tensor& status) {
+  constexpr int hd = 128;
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.size(-1) == hd, "decode_q8: q [T, nq, 128] bf16");
+  TORCH_CHECK(kv_cache.scalar_type() == at::kByte && kv_cache.dim() == 3 && kv_cache.is_contiguous(),
+              "decode_q8: int8 kv cache [L, NB, block_bytes] uint8");
+  const int nkv = int(num_kv_heads);
+  const long bb = kv_cache.size(2);
+  TORCH_CHECK(bb == 2L * nkv * 16 * (hd + 4), "decode_q8: block bytes do not match 2 x KVH x 16 x (128 + 4)");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.stride(1) == 1, "decode_q8: block_table int32");
+  const int B = seq_lens.size(0);
+  if (B == 0) return;
+  const int nq = q.size(-2);
+  TORCH_CHECK(nq % nkv == 0, "decode_q8: nq must be a multiple of nkv");
+  const int hc = int(decode_head_chunks(nq, nkv, q_len));
+  TORCH_CHECK(hc > 0, "decode_q8: no split of the q heads per kv head fits 32 rows at q_len ", q_len);
+  TORCH_CHECK(q.numel() / (nq * hd) == B * q_len, "decode_q8: q rows must equal batch * q_len");
+  const at::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const uint8_t* base = kv_cache.data_ptr<uint8_t>() + layer * kv_cache.stride(0);
+  const uint64_t total = static_cast<uint64_t>(kv_cache.size(1)) * bb;
+  TORCH_CHECK(total / 16 < (1ull << 31), "decode_q8: cache layer too large for int32 TMA coordinates");
+  const CUtensorMap tmK = make_tmap_2d(base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, hd, total / hd, hd, hd, attn::PAGE,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tmV = make_tmap_2d(base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 16, total / 16, 16, 16, hd,
+                                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  attn::DecodeArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_stride = block_table.stride(0);
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.nq = nq;
+  a.nkv = nkv;
+  a.ql = int(q_len);
+  a.hc = hc;
+  a.splits = std::max<int>(1, int(splits));
+  a.scale_log2 = float(scale * 1.4426950408889634);
+  a.status = status.data_ptr<int>();
+  a.num_blocks = int(kv_cache.size(1));
+  a.q8_base = base;
+  a.q8_block_bytes = bb;
+  a.part = nullptr;
+  if (a.splits > 1) {
+    TORCH_CHECK(workspace.scalar_type() == at::kFloat &&
+                    workspace.numel() >= (int64_t)B * nkv * hc * a.splits * 32 * (hd + 2),
+                "decode_q8: workspace too small");
+    a.part = workspace.data_ptr<float>();
+  }
+  const bool mt1 = (nq / nkv / hc) * q_len <= 16;
+  if (mt1) attn::launch_decode_q8<1, 4, 3>(tmK, tmV, a, B, stream);
+  else attn::launch_decode_q8<2, 4, 3>(tmK, tmV, a, B, stream);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (a.splits > 1) {
+    attn::decode_combine_kernel<128><<<dim3(B, nkv * hc), 256, 0, stream>>>(a.part, a.out, nq, nkv * hc, a.ql,
+                                                                           a.splits);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+void kv_dequant_pages_q8(const torch::Tensor& kv_cache, int64_t layer, int64_t num_kv_heads,
+                         const torch::Tensor& block_table, const torch::Tensor& ctx_lens, int64_t W,
+                         torch::Tensor& scratch, const torch::Tensor& status) {
+  TORCH_CHECK(kv_cache.scalar_type() == at::kByte && kv_cache.dim() == 3 && kv_cache.is_contiguous(),
+              "kv_dequant_q8: int8 kv cache [L, NB, block_bytes] uint8");
+  const int S = ctx_lens.size(0);
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.stride(1) == 1 && block_table.size(1) <= W,
+              "kv_dequant_q8: block table int32 [S, <= W]");
+  TORCH_CHECK(scratch.scalar_type() == at::kBFloat16 && scratch.is_contiguous() &&
+                  scratch.numel() >= (int64_t)S * W * 2 * num_kv_heads * 16 * 128,
+              "kv_dequant_q8: scratch bf16 [S * W, 2, KVH, 16, 128]");
+  if (S == 0) return;
+  const at::cuda::CUDAGuard guard(kv_cache.device());
+  attn::kv_dequant_pages_q8_kernel<<<dim3(int(block_table.size(1)), S), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      kv_cache.data_ptr<uint8_t>() + layer * kv_cache.stride(0), kv_cache.size(2), int(num_kv_heads),
+      block_table.data_ptr<int>(), int(block_table.stride(0)), ctx_lens.data_ptr<int>(), int(W),
+      reinterpret_cast<__nv_bfloat16*>(scratch.data_ptr()), int(kv_cache.size(1)), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void paged_prefill_attention(const torch::Tensor& q, const torch::Tensor& kv_cache, int64_t layer,

@@ -203,13 +203,19 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
 // qkv row layout: [q heads | k heads | v heads] x 128.
 // cos_sin: [max_pos, 128] f32 = [cos(0..63) | sin(0..63)].
 // kv cache: [L, NB, 2, KVH, 16, 128].
-template <int D>
+// Q8: the cache is int8 with a per-(token, head) fp32 scale (symmetric,
+// absmax / 127).  Per layer and block: K pages [KVH][16 tokens][D], V pages
+// [KVH][D][16 tokens] (dim-major, so a V page is read as the k = token operand
+// of P V without a transpose), then the scales [2][KVH][16] fp32.
+// `layer_stride` is then in bytes and `block_bytes` the block's byte size.
+template <int D, bool Q8 = false>
 __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, long ldq, const int64_t* __restrict__ pos,
                                      const int* __restrict__ slots, const float* __restrict__ cos_sin,
-                                     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
+                                     __nv_bfloat16* __restrict__ q_out, void* __restrict__ cache_v,
                                      long layer_stride, int nq, int nkv, const __nv_bfloat16* __restrict__ qn,
                                      const __nv_bfloat16* __restrict__ kn, float eps, long max_pos,
-                                     long cache_slots, int* status) {
+                                     long cache_slots, int* status, long block_bytes = 0) {
+  __nv_bfloat16* cache = reinterpret_cast<__nv_bfloat16*>(cache_v);
   constexpr int NV = D / 32;  // values per lane: dims lane + 32 i
   const long t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -256,9 +262,29 @@ __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, long
       const int kvsel = is_k ? 0 : 1;
       const int kh = is_k ? h - nq : h - nq - nkv;
       const long blk = slot >> 4, off = slot & 15;
-      __nv_bfloat16* dst = cache + layer_stride + (((blk * 2 + kvsel) * nkv + kh) * 16 + off) * D;
+      if constexpr (Q8) {
+        float am = 0.f;
 #pragma unroll
-      for (int i = 0; i < NV; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
+        for (int i = 0; i < NV; ++i) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        const float inv = am > 0.f ? 127.f / am : 0.f;
+        uint8_t* bp = reinterpret_cast<uint8_t*>(cache_v) + layer_stride + blk * block_bytes;
+        int8_t* page = reinterpret_cast<int8_t*>(bp) + (long)((kvsel * nkv + kh) * 16) * D;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int q = max(-127, min(127, __float2int_rn(v[i] * inv)));
+          const int d = lane + 32 * i;
+          if (is_k) page[off * D + d] = static_cast<int8_t>(q);
+          else page[d * 16 + off] = static_cast<int8_t>(q);
+        }
+        if (lane == 0)
+          reinterpret_cast<float*>(bp + 2L * nkv * 16 * D)[(kvsel * nkv + kh) * 16 + off] = am / 127.f;
+      } else {
+        __nv_bfloat16* dst = cache + layer_stride + (((blk * 2 + kvsel) * nkv + kh) * 16 + off) * D;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) dst[lane + 32 * i] = __float2bfloat16(v[i]);
+      }
     }
   }
 }
@@ -384,12 +410,42 @@ void rope_kv_write(const torch::Tensor& qkv, const torch::Tensor& positions, con
   const __nv_bfloat16* kn = (k_norm.has_value() && k_norm->defined())
                                 ? reinterpret_cast<const __nv_bfloat16*>(k_norm->data_ptr())
                                 : nullptr;
-  auto kern = hd == 128 ? rope_kv_write_kernel<128> : rope_kv_write_kernel<64>;
+  auto kern = hd == 128 ? rope_kv_write_kernel<128, false> : rope_kv_write_kernel<64, false>;
   kern<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),
       slot_mapping.data_ptr<int>(), cos_sin.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(kv_cache.data_ptr()), layer_stride, int(num_q_heads), int(num_kv_heads), qn,
-      kn, float(eps), cos_sin.size(0), kv_cache.size(1) * 16, check_word(qkv.device().index()));
+      kn, float(eps), cos_sin.size(0), kv_cache.size(1) * 16, check_word(qkv.device().index()), 0L);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_kv_write_q8(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& slot_mapping,
+                      const torch::Tensor& cos_sin, torch::Tensor& q_out, torch::Tensor& kv_cache, int64_t layer,
+                      int64_t num_q_heads, int64_t num_kv_heads, const c10::optional<torch::Tensor>& q_norm,
+                      const c10::optional<torch::Tensor>& k_norm, double eps) {
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "rope_q8: qkv bf16 [T, *]");
+  constexpr int hd = 128;
+  TORCH_CHECK(kv_cache.scalar_type() == at::kByte && kv_cache.dim() == 3 && kv_cache.is_contiguous(),
+              "rope_q8: int8 kv cache [L, NB, block_bytes] uint8");
+  const long bb = kv_cache.size(2);
+  TORCH_CHECK(bb == 2L * num_kv_heads * 16 * (hd + 4), "rope_q8: block bytes do not match 2 x KVH x 16 x (128 + 4)");
+  TORCH_CHECK(qkv.size(1) >= (num_q_heads + 2 * num_kv_heads) * hd, "rope_q8: qkv narrower than the heads");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && slot_mapping.scalar_type() == at::kInt, "rope_q8: index dtypes");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == hd, "rope_q8: cos_sin f32 [P, 128]");
+  const int T = qkv.size(0);
+  if (T == 0) return;
+  const at::cuda::CUDAGuard g(qkv.device());
+  const __nv_bfloat16* qn = (q_norm.has_value() && q_norm->defined())
+                                ? reinterpret_cast<const __nv_bfloat16*>(q_norm->data_ptr())
+                                : nullptr;
+  const __nv_bfloat16* kn = (k_norm.has_value() && k_norm->defined())
+                                ? reinterpret_cast<const __nv_bfloat16*>(k_norm->data_ptr())
+                                : nullptr;
+  rope_kv_write_kernel<hd, true><<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),
+      slot_mapping.data_ptr<int>(), cos_sin.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
+      kv_cache.data_ptr(), layer * kv_cache.stride(0), int(num_q_heads), int(num_kv_heads), qn, kn, float(eps),
+      cos_sin.size(0), kv_cache.size(1) * 16, check_word(qkv.device().index()), bb);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
