@@ -216,6 +216,17 @@ def main():
         ms = timeit(lambda i=0: ops.paged_decode_attention(q, cache, i % L, bt, sl, o, splits=splits, workspace=ws,
                                                            scale=hd ** -0.5))
         report("paged_decode_attention", ms, None, kv_bytes, {"B": B, "avg_ctx": sum(lens) / B, "splits": splits})
+        if hd == 128:
+            # the same workload over an int8 cache (1 byte per element + 4 bytes of scale per token and head)
+            cache8 = torch.randint(0, 256, (L, NB, ops.kv_q8_block_bytes(nkv)), dtype=torch.uint8, device=dev)
+            sc_off = 2 * nkv * 16 * hd
+            cache8[:, :, sc_off:] = torch.full((L, NB, 2 * nkv * 16), 0.01, device=dev).view(torch.uint8).view(
+                L, NB, -1)
+            ms8 = timeit(lambda i=0: ops.paged_decode_attention(q, cache8, i % L, bt, sl, o, splits=splits,
+                                                                workspace=ws, scale=hd ** -0.5))
+            report("paged_decode_attention_int8", ms8, None, sum(lens) * nkv * (hd + 4) * 2,
+                   {"B": B, "avg_ctx": sum(lens) / B, "splits": splits, "speedup_vs_bf16": round(ms / ms8, 2)})
+            del cache8
         for Bs in (() if args.ncu else (1, 8, 32)):
             sl2 = sl[:Bs].contiguous()
             sp = ops.decode_attention_splits(Bs, nkv, MB, 0)
