@@ -97,6 +97,10 @@ class EngineConfig:
     # speculative decoding: proposals verified per sequence and step (0 = off);
     # attach a proposer with LLMEngine.attach_speculator / make_speculator
     spec_len: int = 0
+    # speculation pauses (plain one-row decode, no draft work) while the
+    # acceptance rate of its proposals stays below this; 0 = always speculate
+    spec_min_acceptance: float = field(
+        default_factory=lambda: float(os.environ.get("BLOOM_SPEC_MIN_ACCEPTANCE", "0.1")))
     # CacheMesh: pinned host bytes for evicted prefix blocks (0 = off) and an
     # optional directory of block files below it
     cachemesh_l2_bytes: int = 0
@@ -228,6 +232,10 @@ class LLMEngine:
     def attach_speculator(self, spec) -> None:
         if int(spec.k) != int(self.econf.spec_len):
             raise ValueError(f"speculator proposes {spec.k} tokens but the engine verifies {self.econf.spec_len}")
+        if getattr(spec, "gate", None) is None and self.econf.spec_min_acceptance > 0.0:
+            from .speculative import AdaptiveGate
+
+            spec.gate = AdaptiveGate(self.econf.spec_min_acceptance)
         self.speculator = spec
 
     # ------------------------------------------------------------ construction helpers
@@ -290,9 +298,11 @@ class LLMEngine:
     def _step(self) -> List[RequestOutput]:
         t0 = time.perf_counter()
         if self.speculator is not None:
-            self.speculator.propose(self)
-            for rid in self.constraints:
-                self.scheduler.set_draft(rid, [])
+            gate = getattr(self.speculator, "gate", None)
+            if gate is None or gate.allow(self.scheduler):
+                self.speculator.propose(self)
+                for rid in self.constraints:
+                    self.scheduler.set_draft(rid, [])
         meta = self.scheduler.schedule()
         if self.runner.l2 is not None:
             self.runner.apply_kv_copies(self.scheduler.take_restores(), self.scheduler.take_offloads())

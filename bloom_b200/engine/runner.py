@@ -97,7 +97,7 @@ class ModelRunner:
             self.decode_splits[b] = s
             ws = max(ws, ops.decode_workspace_numel(b, vkh, s))
         self.decode_ws = torch.empty(ws, dtype=torch.float32, device=self.device)
-        self.graphs: Dict[int, tuple] = {}
+        self.graphs: Dict[tuple, tuple] = {}  # (decode rows, q_len) -> captured step
         self.last_logits: Optional[torch.Tensor] = None
         import os as _os
 
@@ -190,7 +190,7 @@ class ModelRunner:
 
     def sampling_views(self, m):
         NL = m.num_logits
-        draft = self._v(m.off_draft_ids, NL) if self.q_len > 1 else None
+        draft = self._v(m.off_draft_ids, NL) if m.decode_q_len > 1 else None
         return (self._v(m.off_temperature, NL, torch.float32), self._v(m.off_top_p, NL, torch.float32),
                 self._v(m.off_top_k, NL), self._v(m.off_seeds, NL, torch.int64), self._v(m.off_offsets, NL, torch.int64),
                 draft)
@@ -221,9 +221,11 @@ class ModelRunner:
             return
         rt = _rt()
         buckets = sorted(buckets or self.buckets, reverse=True)
-        # a valid dummy step: every row reads one page of block 0, writes no KV
-        ql = self.q_len
-        for B in buckets:
+        # a valid dummy step: every row reads one page of block 0, writes no KV.
+        # With speculation both verify steps (q_len rows per sequence) and plain
+        # decode steps (one row: no proposal this step) get graphs.
+        shapes = [(B, self.q_len) for B in buckets] + ([(B, 1) for B in buckets] if self.q_len > 1 else [])
+        for B, ql in shapes:
             T = B * ql
             m = rt.arena_layout(T, B, 0, 0, T, self.max_blocks, ql)
             h = self.arena_host
@@ -250,7 +252,7 @@ class ModelRunner:
                 logits = self._forward_logits(s)
             if self.graph_pool is None:
                 self.graph_pool = g.pool()
-            self.graphs[B] = (g, logits, m, ops.LAUNCHES[0] - n0)
+            self.graphs[(B, ql)] = (g, logits, m, ops.LAUNCHES[0] - n0)
         torch.cuda.synchronize(self.device)
 
     def release_graphs(self) -> None:
@@ -267,7 +269,8 @@ class ModelRunner:
         logits tensor without waiting (the host may prepare token masks meanwhile)."""
         used = m.used_words
         self.arena_dev[:used].copy_(self.arena_host[:used], non_blocking=True)
-        graph = self.graphs.get(m.num_decode) if (m.num_prefill == 0 and m.num_decode > 0) else None
+        graph = (self.graphs.get((m.num_decode, m.decode_q_len)) if (m.num_prefill == 0 and m.num_decode > 0)
+                 else None)
         if graph is not None and graph[2].used_words == used:
             g, logits, _, nlaunch = graph
             g.replay()

@@ -41,11 +41,58 @@ from typing import Dict, List, Optional
 import torch
 
 
+class AdaptiveGate:
+    """Pauses speculation while it does not pay.  After every verify step the
+    gate reads the scheduler's cumulative (proposed, accepted) counters -- the
+    same on every tensor-parallel rank, so every rank decides alike -- and
+    keeps an exponential average of the acceptance rate.  Below
+    `min_acceptance` it pauses proposing for `backoff` steps (doubling up to
+    `max_backoff` while it stays low); a paused step schedules plain one-row
+    decode, so neither the draft nor the verify width costs anything.  After
+    a pause it proposes again to re-measure."""
+
+    def __init__(self, min_acceptance: float = 0.1, alpha: float = 0.25, backoff: int = 16, max_backoff: int = 512):
+        self.min_acceptance = float(min_acceptance)
+        self.alpha = float(alpha)
+        self.backoff0 = self.backoff = int(backoff)
+        self.max_backoff = int(max_backoff)
+        self.rate: Optional[float] = None
+        self.paused = 0
+        self.last = (0, 0)
+        self.pauses = 0
+        self.probing = False
+
+    def allow(self, scheduler) -> bool:
+        if self.min_acceptance <= 0.0:
+            return True
+        st = scheduler.spec_stats()
+        prop, acc = int(st["proposed"]), int(st["accepted"])
+        dp, da = prop - self.last[0], acc - self.last[1]
+        self.last = (prop, acc)
+        if dp > 0:
+            r = da / dp
+            self.rate = r if self.rate is None or self.probing else (1 - self.alpha) * self.rate + self.alpha * r
+            self.probing = False
+            if self.rate < self.min_acceptance:
+                self.paused = self.backoff
+                self.backoff = min(self.backoff * 2, self.max_backoff)
+                self.pauses += 1
+            else:
+                self.backoff = self.backoff0
+        if self.paused > 0:
+            self.paused -= 1
+            if self.paused == 0:
+                self.probing = True  # the next verify step re-measures from scratch
+            return False
+        return True
+
+
 class Speculator:
     """Engine hook: `propose(engine)` sets the next step's proposals on the
     engine's scheduler; `stats()` reports acceptance."""
 
     k: int = 0
+    gate: Optional[AdaptiveGate] = None
 
     def propose(self, engine) -> None:  # pragma: no cover - interface
         raise NotImplementedError
@@ -59,6 +106,9 @@ class Speculator:
         d["tokens_per_verify"] = ((d["accepted"] + d["verify_groups"]) / d["verify_groups"]
                                   if d["verify_groups"] else 0.0)
         d["num_speculative_tokens"] = self.k
+        if self.gate is not None:
+            d["gate_pauses"] = self.gate.pauses
+            d["gate_acceptance"] = self.gate.rate
         return d
 
 

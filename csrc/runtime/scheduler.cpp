@@ -191,7 +191,16 @@ StepMeta Scheduler::schedule() {
   maintain_long_context();
   StepMeta m;
   const int bs = bm_.block_size();
-  const int ql = cfg_.spec_len > 0 ? cfg_.spec_len + 1 : 1;
+  // verify width: spec_len + 1 rows per decode sequence when any running
+  // sequence carries a proposal this step, else plain one-row decode (the
+  // speculator may pause proposing when its drafts are not accepted)
+  int ql = 1;
+  if (cfg_.spec_len > 0)
+    for (const Sequence* s : running_)
+      if (!s->draft.empty()) {
+        ql = cfg_.spec_len + 1;
+        break;
+      }
   int budget = std::min(cfg_.max_num_batched_tokens, arena_.max_tokens);
   last_sampling_.clear();
   last_scheduled_.clear();

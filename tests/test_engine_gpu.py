@@ -201,6 +201,41 @@ def test_draft_model_speculation_same_weights():
     assert st["tokens_per_verify"] > 3.0, st
 
 
+def test_useless_draft_is_paused():
+    """A draft with unrelated weights proposes tokens the target rejects: the
+    adaptive gate pauses speculation (plain one-row decode steps, captured as
+    their own graphs), and the outputs still follow the oracle."""
+    from bloom_b200.engine.engine import EngineConfig, LLMEngine, SamplingParams
+    from bloom_b200.engine.speculative import DraftModelSpeculator
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.llama import DecoderLM
+    from bloom_b200.models.reference import random_weights
+
+    cfg = preset("tiny-llama")
+    w = random_weights(cfg, seed=3, std=0.08, device="cuda")
+    wd = random_weights(cfg, seed=99, std=0.08, device="cuda")
+
+    def engine(weights, spec_len, mlen, prefix):
+        m = DecoderLM(cfg, device="cuda")
+        m.shard_full(weights)
+        return LLMEngine(m, EngineConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=mlen,
+                                         num_blocks=256, use_cuda_graphs=True, spec_len=spec_len,
+                                         enable_prefix_caching=prefix, spec_min_acceptance=0.3))
+
+    eng = engine(w, 3, 512, True)
+    eng.attach_speculator(DraftModelSpeculator(engine(wd, 0, 520, False), 3))
+    torch.manual_seed(7)
+    prompts = [torch.randint(3, cfg.vocab_size, (n,)).tolist() for n in (4, 30, 77)]
+    outs = eng.generate(prompts, SamplingParams(max_tokens=48, temperature=0.0, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        assert len(o.token_ids) == 48
+        _check_greedy(cfg, w, p, o.token_ids)
+    st = eng.speculator.stats(eng)
+    assert st["gate_pauses"] >= 1, st
+    assert st["verify_groups"] < 20, st  # most of the ~48 decode steps ran without a verify width
+    assert eng.runner.stats["graph_steps"] > 0
+
+
 def test_speculation_sampled_runs():
     """Stochastic sampling with proposals: valid tokens, reproducible per seed."""
     from bloom_b200.engine.engine import SamplingParams

@@ -45,7 +45,11 @@ def test_rope_kv_write_int8_matches_quantised_bf16():
     deq = dequant_q8_cache(q8, nkv)
     ref = bf.float()
     am = ref.abs().amax(-1, keepdim=True)
-    assert ((deq - ref).abs() <= am / 254.0 + am * 2e-3 + 1e-6).all()
+    # int8 step (absmax / 254) plus the bf16 rounding of the reference (2^-8 relative)
+    excess = (deq - ref).abs() - (am / 254.0 + am * 4e-3 + 1e-6)
+    bad = (excess > 0).nonzero()
+    assert bad.shape[0] == 0, (bad[:8].tolist(), excess.max().item(), deq[tuple(bad[0].tolist())].item(),
+                               ref[tuple(bad[0].tolist())].item(), am[tuple(bad[0].tolist()[:-1] + [0])].item())
 
 
 @pytest.mark.parametrize("q_len,splits", [(1, 1), (1, 3), (3, 2)])

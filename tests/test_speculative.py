@@ -79,13 +79,20 @@ def test_verify_group_layout_and_acceptance(rt):
     assert s.sequence_tokens(rid)[20:] == [100, 101, 102, 55]
     st = s.spec_stats()
     assert st["verify_groups"] == 1 and st["proposed"] == 3 and st["accepted"] == 2
-    # next verify group starts right after the accepted prefix
+    # next step starts right after the accepted prefix; with no proposal set
+    # on any sequence it is a plain one-row decode (no verify width)
     m = s.schedule()
+    assert m.decode_q_len == 1 and m.num_tokens == 1 and m.num_logits == 1
     assert region(arena, m.off_positions, 1, torch.int64).tolist() == [23]
-    assert region(arena, m.off_input_ids, 4).tolist() == [55, 0, 0, 0]  # no proposals: padded
-    assert region(arena, m.off_draft_ids, 4).tolist() == [-1, -1, -1, -1]
-    ev = s.update(torch.tensor([60, 61, 62, 63], dtype=torch.int32), 4)
+    assert region(arena, m.off_input_ids, 1).tolist() == [55]
+    ev = s.update(torch.tensor([60], dtype=torch.int32), 1)
     assert [e[1] for e in ev] == [60]
+    # a proposal brings the verify width back
+    assert s.set_draft(rid, [61, 62])
+    m = s.schedule()
+    assert m.decode_q_len == 4 and m.num_tokens == 4
+    assert region(arena, m.off_input_ids, 4).tolist() == [60, 61, 62, 0]  # missing proposal: padded
+    assert region(arena, m.off_draft_ids, 4).tolist() == [61, 62, -1, -1]
 
 
 def test_all_accepted_gives_bonus_token(rt):
@@ -225,3 +232,29 @@ def test_greedy_speculation_equals_plain_greedy(rt):
     spec2, steps2, _ = drive(rt, 4, prompts, 40, oracle)
     assert spec2 == plain
     assert steps2 <= 1 + (40 + 4) // 5 + 1
+
+
+class _Sched:
+    def __init__(self):
+        self.proposed = self.accepted = 0
+
+    def spec_stats(self):
+        return {"proposed": self.proposed, "accepted": self.accepted}
+
+
+def test_adaptive_gate_pauses_and_probes():
+    from bloom_b200.engine.speculative import AdaptiveGate
+
+    s = _Sched()
+    g = AdaptiveGate(min_acceptance=0.2, alpha=0.5, backoff=4, max_backoff=8)
+    assert g.allow(s)  # nothing measured yet
+    s.proposed += 16  # a verify step that accepted nothing
+    assert not g.allow(s) and g.pauses == 1
+    assert [g.allow(s) for _ in range(4)] == [False, False, False, True]  # 4-step pause, then a probe
+    s.proposed += 16  # probe also rejected: the pause doubles
+    assert not g.allow(s) and g.pauses == 2
+    assert sum(1 for _ in range(9) if not g.allow(s)) == 7
+    s.proposed += 16
+    s.accepted += 12  # the draft became good: proposing continues, backoff resets
+    assert g.allow(s) and g.backoff == 4
+    assert AdaptiveGate(min_acceptance=0.0).allow(s)  # disabled gate always proposes
