@@ -259,9 +259,13 @@ class LLMEngine:
     def add_request(self, prompt_token_ids: List[int], params: Optional[SamplingParams] = None,
                     priority: int = 0) -> int:
         params = params or SamplingParams()
+        ids = [int(t) for t in prompt_token_ids]
+        V = self.cfg.vocab_size
+        bad = [t for t in ids if t < 0 or t >= V]
+        if bad:
+            raise ValueError(f"prompt token ids outside the vocabulary [0, {V}): {bad[:5]}")
         self._seed_counter += 1
-        rid = self.scheduler.add_request([int(t) for t in prompt_token_ids], params.to_native(self._seed_counter),
-                                         priority)
+        rid = self.scheduler.add_request(ids, params.to_native(self._seed_counter), priority)
         self.requests[rid] = RequestOutput(rid, list(prompt_token_ids), arrival_time=time.perf_counter())
         if (params.json_mode or params.json_schema is not None) and self.tokenizer is not None:
             from .structured import SchemaConstraint, TokenVocab

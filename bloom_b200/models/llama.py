@@ -551,16 +551,25 @@ class DecoderLM:
                 ops.paged_prefill_attention(q[Td:], kv_cache, li, s.prefill_block_table, s.prefill_ctx_lens,
                                             s.prefill_cu_q, s.tile_seq, s.tile_start, attn[Td:], scale=self.scale)
             a2 = attn.view(T, self.nq * cfg.head_dim)
+            moe_router = self.moe.layers[li].get("router") if self.moe is not None else None
             x, wait = self._row_parallel_norm(a2, lay["o"], residual, lay["ln2"], eps,
-                                              next_w=lay.get("gate_up") if self.moe is None else None)
+                                              next_w=lay.get("gate_up") if self.moe is None else moe_router)
             nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
             if self.moe is not None:
                 fused = self.tp.comm.fused if (self.tp.size > 1 and self.tp.comm is not None) else None
                 if fused is not None:
-                    self.moe.forward(li, x, out=fused.partial(T))
-                    x = fused.allreduce_rmsnorm(T, residual, nxt, eps)
+                    # the combine pushes each token's row to its owner (like the dense push
+                    # epilogue); the collective then reduces local slots only
+                    push = _TP_PUSH
+                    self.moe.forward(li, x, out=fused.partial(T), push=fused.push_args(T) if push else None,
+                                     wait=wait)
+                    nq_w = self.layers[li + 1].get("qkv") if (li + 1 < L and not self.offloaded) else None
+                    defer = _TP_DEFER and isinstance(nq_w, torch.Tensor)
+                    x = fused.allreduce_rmsnorm(T, residual, nxt, eps, pushed=push, defer=defer)
+                    wait = fused.wait_args() if defer else None
                 else:
-                    d = self._reduce(self.moe.forward(li, x))
+                    d = self._reduce(self.moe.forward(li, x, wait=wait))
+                    wait = None
                     x = ops.add_rmsnorm(d, residual, nxt, eps)
             else:
                 act = ops.gemm(x, lay["gate_up"], epi=ops.EPI_SWIGLU, wait=wait)

@@ -70,12 +70,18 @@ class MoEBlock:
                 return b
         return 256
 
-    def forward(self, li: int, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward(self, li: int, x: torch.Tensor, out: Optional[torch.Tensor] = None, push=None,
+                wait=None) -> torch.Tensor:
+        """Routed expert FFN of `x` for this rank's experts.  push=(peer
+        buffers, rank, rows) stores each token's combined row straight into
+        its owner rank's slot over NVLink (see parallel.fused.push_args);
+        wait=(flag block, timeout) makes the router GEMM wait for a deferred
+        all-gather of `x` first."""
         lay = self.layers[li]
         T = x.shape[0]
         C = _C()
         st = ops.status(self.dev.index)
-        logits = ops.gemm(x, lay["router"], epi=ops.EPI_F32)
+        logits = ops.gemm(x, lay["router"], epi=ops.EPI_F32, wait=wait)
         K = self.K
         topk_ids = torch.empty(T, K, dtype=torch.int32, device=self.dev)
         topk_w = torch.empty(T, K, dtype=torch.float32, device=self.dev)
@@ -98,6 +104,10 @@ class MoEBlock:
         C.gemm_grouped_out(act, lay["down"], ys, ops.EPI_BF16, tiles_d, self.n_d, self.H, bn, st)
         if out is None:
             out = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.dev)
-        C.moe_combine(ys, pos, topk_w, out)
+        if push is not None:
+            ptrs, rank, rows = push
+            C.moe_combine(ys, pos, topk_w, out, list(ptrs), int(rank), int(rows))
+        else:
+            C.moe_combine(ys, pos, topk_w, out)
         ops._count(6)
         return out

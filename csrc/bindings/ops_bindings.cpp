@@ -28,7 +28,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &bloom::moe_route);
   m.def("moe_plan", &bloom::moe_plan);
   m.def("moe_gather", &bloom::moe_gather);
-  m.def("moe_combine", &bloom::moe_combine);
+  m.def("moe_combine", &bloom::moe_combine, py::arg("ys"), py::arg("pos"), py::arg("topk_w"), py::arg("out"),
+        py::arg("push_ptrs") = std::vector<int64_t>{}, py::arg("push_rank") = 0, py::arg("push_rows") = 0);
   m.def("gemm_default_splits", &bloom::gemm_default_splits);
   m.def("gemm_max_active_clusters", &bloom::gemm_max_active_clusters, "resident clusters of the one-CTA GEMM");
   m.def("attn_tc_set_trace", &bloom::attn_tc_set_trace, "per-CTA phase profile of tcgen05 prefill launches (None = off)");

@@ -65,6 +65,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
 // sets kStatusCommTimeout; the caller goes on (the step is failed by the host).
 __device__ __forceinline__ bool wait_deferred_rows(uint32_t* flags, uint64_t timeout_ns, int* status);
 
+// Byte position of element i in an int8 KV page row stored in MMA fragment
+// order: within each group of 16 the elements (2t, 2t+1, 2t+8, 2t+9) of
+// thread-in-quad t are the four bytes at 4t (K rows: i = head dim; V rows,
+// which are dim-major: i = token).
+__host__ __device__ __forceinline__ int q8_perm16(int i) {
+  return (i & ~15) | (((i & 7) >> 1) << 2) | (((i >> 3) & 1) << 1) | (i & 1);
+}
+
 // Local (same-GPU) pipeline waits never legitimately take this long.
 constexpr uint64_t kLocalWaitTimeoutNs = 2000000000ull;  // 2 s
 

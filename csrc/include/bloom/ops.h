@@ -44,7 +44,8 @@ void moe_plan(torch::Tensor& counts, torch::Tensor& offsets, int64_t bn, int64_t
               torch::Tensor& tiles_gu, torch::Tensor& n_gu, torch::Tensor& tiles_d, torch::Tensor& n_d);
 void moe_gather(const torch::Tensor& x, int64_t e0, int64_t e_local, const torch::Tensor& topk_ids,
                 const torch::Tensor& slot, const torch::Tensor& offsets, torch::Tensor& pos, torch::Tensor& xs);
-void moe_combine(const torch::Tensor& ys, const torch::Tensor& pos, const torch::Tensor& topk_w, torch::Tensor& out);
+void moe_combine(const torch::Tensor& ys, const torch::Tensor& pos, const torch::Tensor& topk_w, torch::Tensor& out,
+                 const std::vector<int64_t>& push_ptrs = {}, int64_t push_rank = 0, int64_t push_rows = 0);
 
 // Normalisation.
 void rmsnorm(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, double eps);

@@ -570,14 +570,40 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 // int8 cache with one fp32 scale per (token, head).  Per page a warp's TMA
 // ring brings the K page [16 tokens][128] (128-byte swizzle), the V page
 // [128 dims][16 tokens] (dim-major) and the 2 x 16 scales (bulk copies):
-// 4.1 KB instead of 8 KB.  K and V bytes become bf16 MMA operands in
-// registers (int8 values are exact in bf16); the K scale multiplies each
-// score column and the V scale each column of P before P V, so no scaled
-// copy of a page is ever written.
-__device__ __forceinline__ uint32_t i8x2_bf16x2(uint32_t u16) {
-  const float lo = static_cast<float>(static_cast<int8_t>(u16 & 0xffu));
-  const float hi = static_cast<float>(static_cast<int8_t>((u16 >> 8) & 0xffu));
-  return pack_bf16(lo, hi);
+// 4.1 KB instead of 8 KB.  Pages are stored in MMA fragment order (see
+// q8_perm16), so each thread gets the four bytes of a B fragment with one
+// 32-bit shared load and turns them into fp16 with a byte permute and a
+// subtraction; the MMAs run in fp16 (q converted once per CTA, P in [0, 1]).
+// The K scale multiplies each score column after Q K^T; the V scale
+// multiplies the converted V values (x * scale <= absmax), so no scaled
+// copy of a page is ever stored.
+// Four int8 values (bytes of w) -> two f16x2 registers {b0, b1} and {b2, b3},
+// exactly: x + 128 is placed in the low mantissa byte of the fp16 1024.0
+// (0x64xx = 1024 + (x + 128)), then 1152.0 is subtracted.
+__device__ __forceinline__ void i8x4_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  lo = __byte_perm(u, 0x64646464u, 0x4140);
+  hi = __byte_perm(u, 0x64646464u, 0x4342);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  __half2 l = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);
+  __half2 h = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
+  lo = *reinterpret_cast<uint32_t*>(&l);
+  hi = *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t b) {
+  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b));
+  return pack_f16(f.x, f.y);
 }
 
 template <int MT, int NWARPS, int NST>
@@ -654,8 +680,8 @@ __global__ void __launch_bounds__(NWARPS * 32)
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
         const int d = ks * 16 + 2 * t4;
-        qf[mt][ks][hr] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
-        qf[mt][ks][hr + 2] = qrow ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
+        qf[mt][ks][hr] = qrow ? bf16x2_to_f16x2(*reinterpret_cast<const uint32_t*>(qrow + d)) : 0u;
+        qf[mt][ks][hr + 2] = qrow ? bf16x2_to_f16x2(*reinterpret_cast<const uint32_t*>(qrow + d + 8)) : 0u;
       }
     }
   }
@@ -707,11 +733,13 @@ __global__ void __launch_bounds__(NWARPS * 32)
       const uint8_t* row = kp + tok * D;
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
-        const uint8_t* chunk = row + ((ks ^ (tok & 7)) << 4);  // 128-byte swizzle: 16-byte chunk ks of row tok
-        const uint32_t b0 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(chunk + 2 * t4));
-        const uint32_t b1 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(chunk + 8 + 2 * t4));
+        // 128-byte swizzle: 16-byte chunk ks of row tok; bytes 4t4..4t4+3 are
+        // dims (2t4, 2t4+1, 2t4+8, 2t4+9) of the chunk (fragment order)
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(row + ((ks ^ (tok & 7)) << 4) + 4 * t4);
+        uint32_t b0, b1;
+        i8x4_f16x2(w, b0, b1);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma_bf16_16816(sc[mt][nt], qf[mt][ks], b0, b1);
+        for (int mt = 0; mt < MT; ++mt) mma_f16_16816(sc[mt][nt], qf[mt][ks], b0, b1);
       }
     }
 
@@ -749,18 +777,25 @@ __global__ void __launch_bounds__(NWARPS * 32)
           o[mt][n][2 * hr] *= alpha;
           o[mt][n][2 * hr + 1] *= alpha;
         }
-        pa[mt][hr] = pack_bf16(x[0] * svc[0][0], x[1] * svc[0][1]);
-        pa[mt][hr + 2] = pack_bf16(x[2] * svc[1][0], x[3] * svc[1][1]);
+        pa[mt][hr] = pack_f16(x[0], x[1]);
+        pa[mt][hr + 2] = pack_f16(x[2], x[3]);
       }
     }
 
+    // V scales of this thread's tokens (2t4, 2t4+1 | 2t4+8, 2t4+9) as f16 pairs
+    const __half2 vs0 = __floats2half2_rn(svc[0][0], svc[0][1]);
+    const __half2 vs1 = __floats2half2_rn(svc[1][0], svc[1][1]);
 #pragma unroll
     for (int nb = 0; nb < D / 8; ++nb) {
-      const uint8_t* vr = vp + (nb * 8 + g) * PAGE;  // dim nb*8+g, 16 tokens
-      const uint32_t b0 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(vr + 2 * t4));
-      const uint32_t b1 = i8x2_bf16x2(*reinterpret_cast<const uint16_t*>(vr + 8 + 2 * t4));
+      // dim nb*8+g: its 16 tokens in fragment order, this thread's four at 4t4
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(vp + (nb * 8 + g) * PAGE + 4 * t4);
+      uint32_t b0, b1;
+      i8x4_f16x2(w, b0, b1);
+      __half2 v0 = __hmul2(*reinterpret_cast<__half2*>(&b0), vs0);
+      __half2 v1 = __hmul2(*reinterpret_cast<__half2*>(&b1), vs1);
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) mma_bf16_16816(o[mt][nb], pa[mt], b0, b1);
+      for (int mt = 0; mt < MT; ++mt)
+        mma_f16_16816(o[mt][nb], pa[mt], *reinterpret_cast<uint32_t*>(&v0), *reinterpret_cast<uint32_t*>(&v1));
     }
     __syncwarp();
     if (lane == 0 && i + NST < my_n) {
@@ -871,7 +906,7 @@ __global__ void kv_dequant_pages_q8_kernel(const uint8_t* __restrict__ layer_bas
     const int d = e % D, tok = (e / D) % PAGE, kvh = e / (D * PAGE);
     const int kv = kvh / nkv;
     const int8_t* page = reinterpret_cast<const int8_t*>(bp) + (long)kvh * PAGE * D;
-    const int8_t q = kv == 0 ? page[tok * D + d] : page[d * PAGE + tok];
+    const int8_t q = kv == 0 ? page[tok * D + q8_perm16(d)] : page[d * PAGE + q8_perm16(tok)];
     dst[e] = __float2bfloat16(static_cast<float>(q) * scl[kvh * PAGE + tok]);
   }
 }

@@ -166,18 +166,57 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int H, in
   }
 }
 
+// out[t] = sum_j w[t, j] * ys[pos[t, j]].  With push pointers the row goes
+// straight to its owner rank's slot [rank][t % rows] over NVLink (16-byte
+// stores, then a system-scope fence), like the row-parallel GEMM's push
+// epilogue, so the collective that follows reduces local memory only.
+struct CombinePush {
+  unsigned long long p[8];
+  int world, rank, rows;
+};
+
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ ys, int H, int K, const int* __restrict__ pos,
                                    const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out, long ys_rows,
-                                   int* status) {
+                                   int* status, const CombinePush push) {
   const int t = blockIdx.x;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < K; ++j) {
-      const int r = pos[(long)t * K + j];
-      if (r >= 0 && kcheck(r < ys_rows, status)) acc += topk_w[(long)t * K + j] * __bfloat162float(ys[(long)r * H + i]);
-    }
-    out[(long)t * H + i] = __float2bfloat16(acc);
+  __nv_bfloat16* dst = out + (long)t * H;
+  if (push.world > 0) {
+    const int owner = t / push.rows, lr = t - owner * push.rows;
+    dst = reinterpret_cast<__nv_bfloat16*>(push.p[owner]) + ((long)push.rank * push.rows + lr) * H;
   }
+  if ((H & 7) == 0) {
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < K; ++j) {
+        const int r = pos[(long)t * K + j];
+        if (r < 0 || !kcheck(r < ys_rows, status)) continue;
+        const float w = topk_w[(long)t * K + j];
+        const uint4 u = *reinterpret_cast<const uint4*>(ys + (long)r * H + c * 8);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h2[k]);
+          acc[2 * k] += w * f.x;
+          acc[2 * k + 1] += w * f.y;
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+      *reinterpret_cast<uint4*>(dst + c * 8) = o;
+    }
+  } else {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      float acc = 0.f;
+      for (int j = 0; j < K; ++j) {
+        const int r = pos[(long)t * K + j];
+        if (r >= 0 && kcheck(r < ys_rows, status)) acc += topk_w[(long)t * K + j] * __bfloat162float(ys[(long)r * H + i]);
+      }
+      dst[i] = __float2bfloat16(acc);
+    }
+  }
+  if (push.world > 0) __threadfence_system();  // pushed rows performed before the collective's ready signal
 }
 
 }  // namespace
@@ -223,13 +262,28 @@ void moe_gather(const torch::Tensor& x, int64_t e0, int64_t e_local, const torch
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void moe_combine(const torch::Tensor& ys, const torch::Tensor& pos, const torch::Tensor& topk_w, torch::Tensor& out) {
+void moe_combine(const torch::Tensor& ys, const torch::Tensor& pos, const torch::Tensor& topk_w, torch::Tensor& out,
+                 const std::vector<int64_t>& push_ptrs, int64_t push_rank, int64_t push_rows) {
   const int T = out.size(0), H = out.size(1), K = pos.size(1);
   if (T == 0) return;
   const at::cuda::CUDAGuard g(out.device());
+  CombinePush push{};
+  if (!push_ptrs.empty()) {
+    TORCH_CHECK(push_ptrs.size() <= 8 && push_rank >= 0 && push_rank < (int64_t)push_ptrs.size(),
+                "moe_combine push: up to 8 ranks");
+    TORCH_CHECK(push_rows > 0 && push_rows * (int64_t)push_ptrs.size() >= T, "moe_combine push: rows cover T");
+    TORCH_CHECK(H % 8 == 0, "moe_combine push: H must be a multiple of 8");
+    for (size_t r = 0; r < push_ptrs.size(); ++r) {
+      TORCH_CHECK(push_ptrs[r] % 16 == 0, "moe_combine push: peer buffers must be 16-byte aligned");
+      push.p[r] = static_cast<unsigned long long>(push_ptrs[r]);
+    }
+    push.world = static_cast<int>(push_ptrs.size());
+    push.rank = static_cast<int>(push_rank);
+    push.rows = static_cast<int>(push_rows);
+  }
   moe_combine_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(ys.data_ptr()), H, K, pos.data_ptr<int>(), topk_w.data_ptr<float>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), long(ys.numel() / H), check_word(out.device().index()));
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), long(ys.numel() / H), check_word(out.device().index()), push);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -15,6 +15,13 @@ int64_t Scheduler::add_request(const std::vector<int32_t>& prompt, const Samplin
   if (prompt.empty()) throw std::invalid_argument("add_request: empty prompt");
   if (static_cast<int>(prompt.size()) >= cfg_.max_model_len)
     throw std::invalid_argument("add_request: prompt longer than max_model_len");
+  // a sequence alone must always fit the pool, or it could be preempted and
+  // re-admitted forever: prompts past the pool are refused, and generation
+  // stops at the pool's token capacity (length_limit)
+  if (static_cast<int>(prompt.size()) >= length_limit())
+    throw std::invalid_argument("add_request: prompt needs more KV blocks than the pool holds (" +
+                                std::to_string(bm_.num_blocks()) + " blocks of " +
+                                std::to_string(bm_.block_size()) + " tokens)");
   auto s = std::make_unique<Sequence>();
   s->id = next_id_++;
   s->tokens = prompt;
@@ -147,9 +154,13 @@ Sequence* Scheduler::pick_victim(const Sequence* requester, const std::vector<Se
   return best ? best : best_capped;
 }
 
+int Scheduler::length_limit() const {
+  return std::min(cfg_.max_model_len, bm_.num_blocks() * bm_.block_size() - cfg_.spec_len);
+}
+
 bool Scheduler::is_stop(const Sequence& s, int32_t tok) const {
   if (s.num_generated() >= s.sp.max_tokens) return true;
-  if (static_cast<int>(s.tokens.size()) >= cfg_.max_model_len) return true;
+  if (static_cast<int>(s.tokens.size()) >= length_limit()) return true;
   if (s.num_generated() < s.sp.min_tokens) return false;
   if (!s.sp.ignore_eos)
     for (int32_t e : cfg_.eos_token_ids)
@@ -519,7 +530,7 @@ StepMeta arena_layout(int T, int Bd, int Sp, int NT, int NL, int MB, int q_len) 
 
 FinishReason Scheduler::stop_reason(const Sequence& s, int32_t tok) const {
   const bool length =
-      s.num_generated() >= s.sp.max_tokens || static_cast<int>(s.tokens.size()) >= cfg_.max_model_len;
+      s.num_generated() >= s.sp.max_tokens || static_cast<int>(s.tokens.size()) >= length_limit();
   bool eos = false;
   if (!s.sp.ignore_eos)
     for (int32_t e : cfg_.eos_token_ids) eos |= (tok == e);
@@ -650,8 +661,8 @@ std::pair<int64_t, std::vector<int32_t>> Scheduler::import_sequence(const std::v
                                                                     const SamplingParams& sp, int priority) {
   if (tokens.empty() || num_prompt < 1 || num_prompt > static_cast<int>(tokens.size()))
     throw std::invalid_argument("import_sequence: bad token counts");
-  if (static_cast<int>(tokens.size()) >= cfg_.max_model_len)
-    throw std::invalid_argument("import_sequence: sequence longer than max_model_len");
+  if (static_cast<int>(tokens.size()) >= length_limit())
+    throw std::invalid_argument("import_sequence: sequence longer than max_model_len or the KV pool");
   // at least the last token is recomputed, so the first step samples from it
   num_computed = std::max(0, std::min(num_computed, static_cast<int>(tokens.size()) - 1));
   auto s = std::make_unique<Sequence>();
@@ -706,7 +717,7 @@ bool Scheduler::set_tail(int64_t id, int keep_len, const std::vector<int32_t>& t
   if (it == seqs_.end() || it->second->status == SeqStatus::Finished) return false;
   Sequence* s = it->second.get();
   if (keep_len < s->num_prompt || keep_len > static_cast<int>(s->tokens.size())) return false;
-  if (keep_len + static_cast<int>(tail.size()) >= cfg_.max_model_len) return false;
+  if (keep_len + static_cast<int>(tail.size()) >= length_limit()) return false;
   s->tokens.resize(keep_len);
   s->tokens.insert(s->tokens.end(), tail.begin(), tail.end());
   if (s->num_computed > keep_len) s->num_computed = keep_len;

@@ -271,6 +271,9 @@ class Scheduler {
   std::pair<int64_t, std::vector<int32_t>> import_sequence(const std::vector<int32_t>& tokens, int num_prompt,
                                                            int num_computed, const SamplingParams& sp, int priority);
 
+  // Longest sequence (prompt + generated tokens): max_model_len, or less when
+  // the KV pool cannot hold that many tokens of one sequence.
+  int length_limit() const;
   // Scheduler clock in milliseconds (steady clock; a test may pin it).
   double now_ms() const;
   void set_clock_ms(double ms) { clock_override_ms_ = ms; }

@@ -597,3 +597,55 @@ def test_export_import_sequence(rt):
         s.export_sequence(12345)
     with pytest.raises(Exception):
         s.import_sequence([1] * 600, 1, 10, st["params"], 0)
+
+
+# ---------------------------------------------------------------- malformed input and overflow safety
+# (reference: the scheduler's validation and executor-error tests,
+# crates/engine/src/scheduler/scheduler_test.rs:483-613)
+
+def test_invalid_requests_are_refused(rt):
+    s, arena, _ = make(rt, num_blocks=8, max_len=128)
+    with pytest.raises(ValueError, match="empty prompt"):
+        s.add_request([], params(rt))
+    with pytest.raises(ValueError, match="max_model_len"):
+        s.add_request(list(range(3, 200)), params(rt))
+    assert not s.abort(987654)  # unknown ids are not an error
+    m = s.schedule()
+    assert m.num_tokens == 0 and not s.has_unfinished()
+
+
+def test_prompt_larger_than_the_pool_is_refused_not_livelocked(rt):
+    s, arena, _ = make(rt, num_blocks=4, max_len=512)
+    with pytest.raises(ValueError, match="KV blocks"):
+        s.add_request(list(range(3, 100)), params(rt))  # 97 tokens > 4 blocks x 16
+    assert not s.has_unfinished()
+
+
+def test_generation_stops_at_pool_capacity(rt):
+    s, arena, _ = make(rt, num_blocks=4, max_len=512)
+    rid = s.add_request(list(range(3, 40)), params(rt, max_tokens=10_000, ignore_eos=True))
+    finished, generated = None, 0
+    for _ in range(200):
+        _, ev = run_step(s, arena, token=7)
+        for r, tok, fin, reason in ev:
+            generated += r == rid
+            if fin:
+                finished = reason
+        if not s.has_unfinished():
+            break
+    assert finished == 2  # length: the pool holds 4 x 16 tokens of one sequence
+    assert 37 + generated == 4 * 16
+    assert s.kv_metrics()["active_blocks"] == 0
+
+
+def test_update_rejects_malformed_results(rt):
+    s, arena, _ = make(rt)
+    s.add_request(list(range(3, 20)), params(rt))
+    m = s.schedule()
+    with pytest.raises(RuntimeError, match="smaller than n"):
+        s.update(torch.zeros(1, dtype=torch.int32), m.num_real_logits + 5)
+    with pytest.raises(ValueError, match="fewer sampled tokens"):
+        s.update(torch.zeros(4, dtype=torch.int32), 0)
+    # the step is still pending: a well-formed result completes it
+    ev = s.update(torch.full((max(m.num_logits, 1),), 9, dtype=torch.int32), m.num_real_logits)
+    assert len(ev) == 1 and ev[0][1] == 9
