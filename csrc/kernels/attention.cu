@@ -573,10 +573,10 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 // 4.1 KB instead of 8 KB.  Pages are stored in MMA fragment order (see
 // q8_perm16), so each thread gets the four bytes of a B fragment with one
 // 32-bit shared load and turns them into fp16 with a byte permute and a
-// subtraction; the MMAs run in fp16 (q converted once per CTA, P in [0, 1]).
-// The K scale multiplies each score column after Q K^T; the V scale
-// multiplies the converted V values (x * scale <= absmax), so no scaled
-// copy of a page is ever stored.
+// subtraction; the MMAs run in fp16 (q converted once per CTA).  The K scale
+// multiplies each score column after Q K^T; P carries the V scales (times
+// 2^8, divided out with the row sum), so V needs no per-element multiply.
+// The running max is rescaled lazily (only when it grows by more than 2^4).
 // Four int8 values (bytes of w) -> two f16x2 registers {b0, b1} and {b2, b3},
 // exactly: x + 128 is placed in the low mantissa byte of the fp16 1024.0
 // (0x64xx = 1024 + (x + 128)), then 1152.0 is subtracted.
@@ -719,7 +719,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         skc[nt][e] = ksc[8 * nt + 2 * t4 + e];
-        svc[nt][e] = vsc[8 * nt + 2 * t4 + e];
+        svc[nt][e] = vsc[8 * nt + 2 * t4 + e] * 256.f;
       }
 
     float sc[MT][2][4];
@@ -762,40 +762,42 @@ __global__ void __launch_bounds__(NWARPS * 32)
           }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run[mt][hr], mx);
-        const float alpha = exp2f(m_run[mt][hr] - m_new);
-        m_run[mt][hr] = m_new;
+        // lazy rescaling: the running max only moves (and O, l are rescaled)
+        // when a score exceeds it by more than 2^4; p <= 16 otherwise
+        if (mx > m_run[mt][hr] + 4.f) {
+          const float alpha = exp2f(m_run[mt][hr] - mx);
+          m_run[mt][hr] = mx;
+          l_run[mt][hr] *= alpha;
+#pragma unroll
+          for (int n = 0; n < D / 8; ++n) {
+            o[mt][n][2 * hr] *= alpha;
+            o[mt][n][2 * hr + 1] *= alpha;
+          }
+        }
+        const float m_use = m_run[mt][hr];
         float ps = 0.f;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          x[k] = exp2f(x[k] - m_new);
+          x[k] = exp2f(x[k] - m_use);
           ps += x[k];
         }
-        l_run[mt][hr] = l_run[mt][hr] * alpha + ps;
-#pragma unroll
-        for (int n = 0; n < D / 8; ++n) {
-          o[mt][n][2 * hr] *= alpha;
-          o[mt][n][2 * hr + 1] *= alpha;
-        }
-        pa[mt][hr] = pack_f16(x[0], x[1]);
-        pa[mt][hr + 2] = pack_f16(x[2], x[3]);
+        l_run[mt][hr] += ps;
+        // P carries the V scales times 2^8 (undone with 1 / l at the end):
+        // p * scale * 256 stays a normal fp16 number for V absmax from ~1e-2
+        // up to ~2000 (p <= 16)
+        pa[mt][hr] = pack_f16(x[0] * svc[0][0], x[1] * svc[0][1]);
+        pa[mt][hr + 2] = pack_f16(x[2] * svc[1][0], x[3] * svc[1][1]);
       }
     }
 
-    // V scales of this thread's tokens (2t4, 2t4+1 | 2t4+8, 2t4+9) as f16 pairs
-    const __half2 vs0 = __floats2half2_rn(svc[0][0], svc[0][1]);
-    const __half2 vs1 = __floats2half2_rn(svc[1][0], svc[1][1]);
 #pragma unroll
     for (int nb = 0; nb < D / 8; ++nb) {
       // dim nb*8+g: its 16 tokens in fragment order, this thread's four at 4t4
       const uint32_t w = *reinterpret_cast<const uint32_t*>(vp + (nb * 8 + g) * PAGE + 4 * t4);
       uint32_t b0, b1;
       i8x4_f16x2(w, b0, b1);
-      __half2 v0 = __hmul2(*reinterpret_cast<__half2*>(&b0), vs0);
-      __half2 v1 = __hmul2(*reinterpret_cast<__half2*>(&b1), vs1);
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-        mma_f16_16816(o[mt][nb], pa[mt], *reinterpret_cast<uint32_t*>(&v0), *reinterpret_cast<uint32_t*>(&v1));
+      for (int mt = 0; mt < MT; ++mt) mma_f16_16816(o[mt][nb], pa[mt], b0, b1);
     }
     __syncwarp();
     if (lane == 0 && i + NST < my_n) {
@@ -832,7 +834,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
       }
       if (t4 == 0) {
         wbuf[r * RS + D] = m_run[mt][hr];
-        wbuf[r * RS + D + 1] = l_run[mt][hr];
+        wbuf[r * RS + D + 1] = l_run[mt][hr] * 256.f;  // O holds sum p * (v scale * 2^8) * x
       }
     }
   __syncthreads();
