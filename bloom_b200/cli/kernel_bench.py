@@ -341,6 +341,23 @@ def main():
             flops = 2.0 * Tm * cfg.num_experts_per_tok / 8 * 3 * Im * Hm
             report("moe_layer_ep8", ms, flops, wbytes, {"tokens": Tm, "local_experts": El})
 
+    if not args.only or "quant" in args.only:
+        # GGUF decode GEMV straight from the block-quantised rows (Llama-3-8B gate_up / down
+        # rows at M = 1 and 8 tokens); bytes = the quantised weight planes
+        for kind in ("Q8_0", "Q4_0"):
+            for nm, N, K in (("gate_up", 2 * I // t, H), ("down", H, I // t)):
+                nrot = max(1, int(math.ceil(400e6 / (N * K))))
+                qw = [ops.QWeight(kind, (torch.randint(-127, 128, (N, K), device=dev, dtype=torch.int8) if kind == "Q8_0"
+                                         else torch.randint(0, 256, (N, K // 2), device=dev, dtype=torch.uint8)),
+                                  torch.full((N, K // 32), 0.01, device=dev, dtype=torch.float16), K)
+                      for _ in range(nrot)]
+                for M in (1, 8):
+                    x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+                    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                    ms = timeit(lambda i=0: ops.gemm(x, qw[i % nrot], out))
+                    report(f"qgemv_{kind}_{nm}", ms, 2.0 * M * N * K, qw[0].nbytes() + M * K * 2, {"M": M, "N": N, "K": K})
+                del qw
+
     if args.json:
         with open(args.json, "w") as f:
             json.dump({"peaks": {"hbm_gbs": hbm, "bf16_tflops": tfl, "source": src}, "rows": rows}, f, indent=1)

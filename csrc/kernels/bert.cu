@@ -192,8 +192,11 @@ __global__ void __launch_bounds__(128) varlen_attention_tc_kernel(const __nv_bfl
   const int q0 = blockIdx.z * 64;
   if (q0 >= L) return;
   const int Lp = (L + 15) & ~15;
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smraw);  // [Lp][D]
-  __nv_bfloat16* Vs = Ks + (long)Lp * D;                        // [Lp][D]
+  // rows padded by 8 elements (16 bytes): the 8 key rows one MMA fragment
+  // load touches then fall into distinct shared-memory banks
+  constexpr int RS = D + 8;
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smraw);  // [Lp][RS]
+  __nv_bfloat16* Vs = Ks + (long)Lp * RS;                       // [Lp][RS]
   const long ld = 3L * NH * D;
   constexpr int VEC = D / 8;  // 16-byte vectors per row
   for (int idx = threadIdx.x; idx < Lp * VEC; idx += blockDim.x) {
@@ -204,8 +207,8 @@ __global__ void __launch_bounds__(128) varlen_attention_tc_kernel(const __nv_bfl
       kv = *reinterpret_cast<const uint4*>(row + (long)NH * D + h * D + c * 8);
       vv = *reinterpret_cast<const uint4*>(row + 2L * NH * D + h * D + c * 8);
     }
-    reinterpret_cast<uint4*>(Ks)[idx] = kv;
-    reinterpret_cast<uint4*>(Vs)[idx] = vv;
+    *reinterpret_cast<uint4*>(Ks + (long)j * RS + c * 8) = kv;
+    *reinterpret_cast<uint4*>(Vs + (long)j * RS + c * 8) = vv;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -236,7 +239,7 @@ __global__ void __launch_bounds__(128) varlen_attention_tc_kernel(const __nv_bfl
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-      const __nv_bfloat16* krow = Ks + (long)(kt + nt * 8 + g) * D;  // key n = g of this n-block
+      const __nv_bfloat16* krow = Ks + (long)(kt + nt * 8 + g) * RS;  // key n = g of this n-block
 #pragma unroll
       for (int kc = 0; kc < KC; ++kc) {
         const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + kc * 16 + t4 * 2);
@@ -287,12 +290,12 @@ __global__ void __launch_bounds__(128) varlen_attention_tc_kernel(const __nv_bfl
     pa[1] = pack_bf16(sc[0][2], sc[0][3]);
     pa[2] = pack_bf16(sc[1][0], sc[1][1]);
     pa[3] = pack_bf16(sc[1][2], sc[1][3]);
-    const __nv_bfloat16* v0r = Vs + (long)(kt + t4 * 2) * D;  // keys t4*2, t4*2+1 (and +8, +9)
+    const __nv_bfloat16* v0r = Vs + (long)(kt + t4 * 2) * RS;  // keys t4*2, t4*2+1 (and +8, +9)
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
       const int d = nb * 8 + g;
-      const uint32_t b0 = pack_raw(v0r[d], v0r[D + d]);
-      const uint32_t b1 = pack_raw(v0r[8 * D + d], v0r[9 * D + d]);
+      const uint32_t b0 = pack_raw(v0r[d], v0r[RS + d]);
+      const uint32_t b1 = pack_raw(v0r[8 * RS + d], v0r[9 * RS + d]);
       mma16816(o[nb], pa, b0, b1);
     }
   }
@@ -397,15 +400,15 @@ void varlen_attention(const torch::Tensor& qkv, const torch::Tensor& cu_seqlens,
                        out.is_contiguous() && reinterpret_cast<uintptr_t>(out.data_ptr()) % 4 == 0;
   if (tc && aligned && qkv.scalar_type() == at::kBFloat16) {
     const int Lp = int((max_len + 15) / 16 * 16);
-    const size_t smem_tc = 2 * size_t(Lp) * head_dim * sizeof(__nv_bfloat16);
+    const size_t smem_tc = 2 * size_t(Lp) * (head_dim + 8) * sizeof(__nv_bfloat16);
     dim3 g3(S, num_heads, int((max_len + 63) / 64));
     if (head_dim == 32) {
-      cudaFuncSetAttribute(varlen_attention_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 32 * 2);
+      cudaFuncSetAttribute(varlen_attention_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 40 * 2);
       varlen_attention_tc_kernel<32><<<g3, 128, smem_tc, s>>>(
           reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cu_seqlens.data_ptr<int>(),
           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(num_heads), float(scale * 1.4426950408889634));
     } else {
-      cudaFuncSetAttribute(varlen_attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 64 * 2);
+      cudaFuncSetAttribute(varlen_attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 512 * 72 * 2);
       varlen_attention_tc_kernel<64><<<g3, 128, smem_tc, s>>>(
           reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cu_seqlens.data_ptr<int>(),
           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(num_heads), float(scale * 1.4426950408889634));
