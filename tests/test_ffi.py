@@ -44,10 +44,16 @@ def _load(L, engine=b"mock", ctx=2048):
     return p, err
 
 
-def test_header_smoke_compiles_as_c_and_cpp(tmp_path):
+def test_header_smoke_compiles_as_c_and_cpp(tmp_path, lib):
+    """Both smoke programs compile warning-free against the header and link
+    against the built library (the C one takes the address of every export
+    with its declared signature); running them checks statuses and layouts."""
+    _, path = lib
+    d = os.path.dirname(path)
     for src, cc, std in (("header_smoke.c", "gcc", "-std=c99"), ("header_smoke.cpp", "g++", "-std=c++17")):
         exe = str(tmp_path / src.replace(".", "_"))
-        subprocess.check_call([cc, std, "-Wall", "-Werror", os.path.join(FFI, "tests", src), "-o", exe])
+        subprocess.check_call([cc, std, "-Wall", "-Werror", os.path.join(FFI, "tests", src), "-o", exe, f"-L{d}",
+                               "-l:libbloom_ffi.so", f"-Wl,-rpath,{d}"])
         assert subprocess.call([exe]) == 0
 
 
