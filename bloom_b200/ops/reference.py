@@ -79,15 +79,14 @@ def q8_perm16(i: int) -> int:
 
 def dequant_q8_cache(kv_u8, num_kv_heads: int, head_dim: int = 128):
     """fp32 [L, NB, 2, Hkv, 16, D] of an int8 cache [L, NB, block bytes]: K
-    pages [Hkv][16][D], dim-major V pages [Hkv][D][16] (both rows in fragment
-    order, `q8_perm16`), then fp32 scales [2][Hkv][16] per block (the layout
-    rope_kv_write writes for int8)."""
+    pages [Hkv][16][D] in natural order, dim-major V pages [Hkv][D][16] with
+    each 16-token row in fragment order (`q8_perm16`), then fp32 scales
+    [2][Hkv][16] per block (the layout rope_kv_write writes for int8)."""
     L, NB, BB = kv_u8.shape
     P = num_kv_heads * 16 * head_dim
     dev = kv_u8.device
-    kp = torch.tensor([q8_perm16(d) for d in range(head_dim)], device=dev)
     tp = torch.tensor([q8_perm16(t) for t in range(16)], device=dev)
-    k = kv_u8[:, :, :P].contiguous().view(torch.int8).view(L, NB, num_kv_heads, 16, head_dim)[..., kp].float()
+    k = kv_u8[:, :, :P].contiguous().view(torch.int8).view(L, NB, num_kv_heads, 16, head_dim).float()
     v = kv_u8[:, :, P:2 * P].contiguous().view(torch.int8).view(L, NB, num_kv_heads, head_dim, 16)[..., tp]
     v = v.transpose(-1, -2).float()
     sc = kv_u8[:, :, 2 * P:].contiguous().view(torch.float32).view(L, NB, 2, num_kv_heads, 16)

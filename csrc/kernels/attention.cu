@@ -570,13 +570,14 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 // int8 cache with one fp32 scale per (token, head).  Per page a warp's TMA
 // ring brings the K page [16 tokens][128] (128-byte swizzle), the V page
 // [128 dims][16 tokens] (dim-major) and the 2 x 16 scales (bulk copies):
-// 4.1 KB instead of 8 KB.  Pages are stored in MMA fragment order (see
-// q8_perm16), so each thread gets the four bytes of a B fragment with one
-// 32-bit shared load and turns them into fp16 with a byte permute and a
-// subtraction; the MMAs run in fp16 (q converted once per CTA).  The K scale
-// multiplies each score column after Q K^T; P carries the V scales (times
-// 2^8, divided out with the row sum), so V needs no per-element multiply.
-// The running max is rescaled lazily (only when it grows by more than 2^4).
+// 4.1 KB instead of 8 KB.  Q K^T runs as int8 MMAs (m16n8k32, s32
+// accumulators): q is quantised per row once per CTA, K bytes are the B
+// operand as stored, and S = q scale x K scale x the integer dot product.
+// V pages are stored in fp16 fragment order (q8_perm16), so each thread gets
+// the four bytes of a B fragment with one 32-bit shared load and turns them
+// into fp16 with a byte permute and a subtraction; P V runs in fp16 with P
+// carrying the V scales (times 2^8, divided out with the row sum).  The
+// running max is rescaled lazily (only when it grows by more than 2^4).
 // Four int8 values (bytes of w) -> two f16x2 registers {b0, b1} and {b2, b3},
 // exactly: x + 128 is placed in the low mantissa byte of the fp16 1024.0
 // (0x64xx = 1024 + (x + 128)), then 1152.0 is subtracted.
@@ -595,6 +596,13 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
@@ -666,7 +674,11 @@ __global__ void __launch_bounds__(NWARPS * 32)
     for (int i = 0; i < NST && i < my_n; ++i) issue(i);
   }
 
-  uint32_t qf[MT][D / 16][4];
+  // q rows quantised to int8 per row (absmax / 127) for the int8 Q K^T MMAs:
+  // A fragment of m16n8k32, chunk kc of 32 dims: rows g / g+8, bytes 4t4..4t4+3
+  // and 16+4t4..16+4t4+3 of the chunk
+  uint32_t qf[MT][D / 32][4];
+  float qscale[MT][2];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -677,12 +689,39 @@ __global__ void __launch_bounds__(NWARPS * 32)
         const int qi = r / G, hh = r - qi * G;
         qrow = a.q + ((long)(b * a.ql + qi) * a.nq + vkh * G + hh) * D;
       }
+      float qv[D / 32][8];
+      float am = 0.f;
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        const int d = ks * 16 + 2 * t4;
-        qf[mt][ks][hr] = qrow ? bf16x2_to_f16x2(*reinterpret_cast<const uint32_t*>(qrow + d)) : 0u;
-        qf[mt][ks][hr + 2] = qrow ? bf16x2_to_f16x2(*reinterpret_cast<const uint32_t*>(qrow + d + 8)) : 0u;
-      }
+      for (int kc = 0; kc < D / 32; ++kc)
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int d = kc * 32 + h2 * 16 + 4 * t4;
+          uint2 u = qrow ? *reinterpret_cast<const uint2*>(qrow + d) : make_uint2(0u, 0u);
+          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+          qv[kc][4 * h2 + 0] = f0.x;
+          qv[kc][4 * h2 + 1] = f0.y;
+          qv[kc][4 * h2 + 2] = f1.x;
+          qv[kc][4 * h2 + 3] = f1.y;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(qv[kc][4 * h2 + e]));
+        }
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      const float inv = am > 0.f ? 127.f / am : 0.f;
+      qscale[mt][hr] = am / 127.f;
+#pragma unroll
+      for (int kc = 0; kc < D / 32; ++kc)
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t w = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int qi8 = max(-127, min(127, __float2int_rn(qv[kc][4 * h2 + e] * inv)));
+            w |= (static_cast<uint32_t>(qi8) & 0xffu) << (8 * e);
+          }
+          qf[mt][kc][hr + 2 * h2] = w;  // a0 / a1: bytes 4t4.. of rows g / g+8; a2 / a3: bytes 16+4t4..
+        }
     }
   }
 
@@ -722,26 +761,31 @@ __global__ void __launch_bounds__(NWARPS * 32)
         svc[nt][e] = vsc[8 * nt + 2 * t4 + e] * 256.f;
       }
 
-    float sc[MT][2][4];
+    int sci[MT][2][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.f;
+      for (int nt = 0; nt < 2; ++nt) sci[mt][nt][0] = sci[mt][nt][1] = sci[mt][nt][2] = sci[mt][nt][3] = 0;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       const int tok = 8 * nt + g;
       const uint8_t* row = kp + tok * D;
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        // 128-byte swizzle: 16-byte chunk ks of row tok; bytes 4t4..4t4+3 are
-        // dims (2t4, 2t4+1, 2t4+8, 2t4+9) of the chunk (fragment order)
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(row + ((ks ^ (tok & 7)) << 4) + 4 * t4);
-        uint32_t b0, b1;
-        i8x4_f16x2(w, b0, b1);
+      for (int kc = 0; kc < D / 32; ++kc) {
+        // 128-byte swizzle: 16-byte chunks 2kc and 2kc+1 of row tok, bytes 4t4..4t4+3 of each
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(row + (((2 * kc) ^ (tok & 7)) << 4) + 4 * t4);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(row + (((2 * kc + 1) ^ (tok & 7)) << 4) + 4 * t4);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma_f16_16816(sc[mt][nt], qf[mt][ks], b0, b1);
+        for (int mt = 0; mt < MT; ++mt) mma_s8_16832(sci[mt][nt], qf[mt][kc], b0, b1);
       }
     }
+    float sc[MT][2][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[mt][nt][e] = static_cast<float>(sci[mt][nt][e]) * qscale[mt][e >> 1];
 
     uint32_t pa[MT][4];
 #pragma unroll
@@ -908,7 +952,7 @@ __global__ void kv_dequant_pages_q8_kernel(const uint8_t* __restrict__ layer_bas
     const int d = e % D, tok = (e / D) % PAGE, kvh = e / (D * PAGE);
     const int kv = kvh / nkv;
     const int8_t* page = reinterpret_cast<const int8_t*>(bp) + (long)kvh * PAGE * D;
-    const int8_t q = kv == 0 ? page[tok * D + q8_perm16(d)] : page[d * PAGE + q8_perm16(tok)];
+    const int8_t q = kv == 0 ? page[tok * D + d] : page[d * PAGE + q8_perm16(tok)];
     dst[e] = __float2bfloat16(static_cast<float>(q) * scl[kvh * PAGE + tok]);
   }
 }

@@ -275,9 +275,9 @@ __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, long
         for (int i = 0; i < NV; ++i) {
           const int q = max(-127, min(127, __float2int_rn(v[i] * inv)));
           const int d = lane + 32 * i;
-          // fragment order: inside each 16-element group the four values one
-          // MMA thread needs (2t, 2t+1, 2t+8, 2t+9) are adjacent bytes
-          if (is_k) page[off * D + q8_perm16(d)] = static_cast<int8_t>(q);
+          // K rows in natural order (operands of int8 Q K^T MMAs); V rows (one
+          // per dimension, 16 tokens) in fp16 fragment order (q8_perm16)
+          if (is_k) page[off * D + d] = static_cast<int8_t>(q);
           else page[d * 16 + q8_perm16(static_cast<int>(off))] = static_cast<int8_t>(q);
         }
         if (lane == 0)

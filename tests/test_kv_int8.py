@@ -29,12 +29,10 @@ def test_reference_dequantiser_inverts_a_built_block():
     kq, ks = quantize_q8_rows(k)
     vq, vs = quantize_q8_rows(v)
     P = nkv * 16 * D
-    inv_d = torch.empty(D, dtype=torch.long)
-    inv_d[torch.tensor([q8_perm16(d) for d in range(D)])] = torch.arange(D)
     inv_t = torch.empty(16, dtype=torch.long)
     inv_t[torch.tensor([q8_perm16(t) for t in range(16)])] = torch.arange(16)
     buf = torch.zeros(L, NB, ops.kv_q8_block_bytes(nkv), dtype=torch.uint8)
-    buf[:, :, :P] = kq[..., inv_d].contiguous().to(torch.int8).view(L, NB, -1).view(torch.uint8)
+    buf[:, :, :P] = kq.contiguous().to(torch.int8).view(L, NB, -1).view(torch.uint8)
     vt = vq.transpose(-1, -2)[..., inv_t].contiguous()
     buf[:, :, P:2 * P] = vt.to(torch.int8).view(L, NB, -1).view(torch.uint8)
     buf[:, :, 2 * P:] = torch.stack([ks, vs], 2).contiguous().view(L, NB, -1).view(torch.uint8)

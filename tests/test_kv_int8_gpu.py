@@ -2,8 +2,9 @@
 
 * rope_kv_write into an int8 cache equals the bf16 write quantised per
   (token, head) (values within half a quantisation step);
-* decode attention over the int8 cache matches an fp32 softmax over the
-  dequantised pages, including split-K and a verify width of 3;
+* decode attention over the int8 cache (int8 Q K^T with per-row quantised
+  q, fp16 P V) matches an fp32 softmax over the dequantised pages, including
+  split-K and a verify width of 3;
 * prefill attention over the int8 cache (dequantised scratch pages) matches
   the fp32 oracle over the same dequantised pages;
 * an engine with kv_cache_dtype="int8" generates close to the fp32 oracle
@@ -81,7 +82,14 @@ def test_decode_attention_int8_matches_fp32(q_len, splits):
     torch.cuda.synchronize()
     assert int(ops.status(0)[0].item()) == 0
     G = nq // nkv
-    worst = 0.0
+    # the kernel quantises each q row to int8 (absmax / 127) for Q K^T: the
+    # same quantisation in the oracle isolates the kernel's arithmetic (tight),
+    # exact q bounds the end-to-end error of the int8 path (looser)
+    from bloom_b200.ops.reference import quantize_q8_rows
+
+    qi8, qs = quantize_q8_rows(q.float())
+    q_deq = qi8 * qs[..., None]
+    worst = {"quantised_q": 0.0, "exact_q": 0.0}
     for b, L in enumerate(lens):
         n = (L + 15) // 16
         pages = deq[bt[b, :n].long()]  # [n, 2, nkv, 16, 128]
@@ -89,11 +97,12 @@ def test_decode_attention_int8_matches_fp32(q_len, splits):
         v = pages[:, 1].permute(0, 2, 1, 3).reshape(n * 16, nkv, 128)[:L]
         for qi in range(q_len):
             lim = L - q_len + qi + 1
-            qq = q[b * q_len + qi].float().view(nkv, G, 128)
-            s = torch.einsum("hgd,khd->hgk", qq, k[:lim]) / math.sqrt(128)
-            o = torch.einsum("hgk,khd->hgd", s.softmax(-1), v[:lim]).reshape(nq, 128)
-            worst = max(worst, (out[b * q_len + qi].float() - o).abs().max().item())
-    assert worst < 2e-2, worst
+            for key, qsrc in (("quantised_q", q_deq), ("exact_q", q.float())):
+                qq = qsrc[b * q_len + qi].view(nkv, G, 128)
+                s = torch.einsum("hgd,khd->hgk", qq, k[:lim]) / math.sqrt(128)
+                o = torch.einsum("hgk,khd->hgd", s.softmax(-1), v[:lim]).reshape(nq, 128)
+                worst[key] = max(worst[key], (out[b * q_len + qi].float() - o).abs().max().item())
+    assert worst["quantised_q"] < 1e-2 and worst["exact_q"] < 4e-2, worst
 
 
 def test_prefill_attention_int8_matches_fp32():
