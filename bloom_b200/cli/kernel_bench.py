@@ -277,6 +277,41 @@ def main():
             extra["mma_warp_wait_Sfree_cycles_per_tile"] = round(t[:, 14].sum().item() / max(nkt, 1), 1)
             report("paged_prefill_attention_profile", float("nan"), None, None, extra)
 
+    if not args.only or "gemma" in args.only:
+        # Gemma4 wide-head attention, 64 sequences of 4,096 tokens: sliding layer (head_dim 256,
+        # 16 q / 8 KV heads, 1,024-key window, soft-cap 50) and global layer (head_dim 512, 16 q / 1
+        # KV head), decode and a 2 x 2,048-token prefill chunk; bytes = the KV pages a step must read
+        for D, gnq, gkv, win in ((256, 16, 8, 1024), (512, 16, 1, 0)):
+            B, ctx = 64, 4096
+            MB = ctx // 16
+            E = 2 * gkv * 16 * D
+            NB = B * MB
+            kvl = torch.randn(NB, E, device=dev, dtype=torch.bfloat16)
+            bt = torch.randperm(NB, device=dev).to(torch.int32).view(B, MB)
+            sl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+            q = torch.randn(B, gnq, D, device=dev, dtype=torch.bfloat16) * 0.1
+            o = torch.empty_like(q)
+            sp = ops.wide_decode_splits(B, gnq, gkv, D, 1, ctx, win, 0)
+            ws = torch.empty(ops.wide_decode_workspace_numel(B, gnq, gkv, D, 1, sp), device=dev)
+            keys = min(ctx, win) if win else ctx
+            ms = timeit(lambda i=0: ops.wide_decode_attention(q, kvl, gkv, bt, sl, o, window=win, softcap=50.0,
+                                                              splits=sp, workspace=ws))
+            report(f"wide_decode_attention_d{D}", ms, None, B * keys * gkv * D * 2 * 2,
+                   {"B": B, "ctx": ctx, "window": win, "splits": sp})
+            qp = torch.randn(2 * 2048, gnq, D, device=dev, dtype=torch.bfloat16) * 0.1
+            op = torch.empty_like(qp)
+            cu = [0, 2048, 4096]
+            ts, tst = [t.to(dev) for t in ops.prefill_tiles(cu, [2048, 2048])]
+            cuq = torch.tensor(cu, dtype=torch.int32, device=dev)
+            cl = torch.tensor([2048, 2048], dtype=torch.int32, device=dev)
+            ms = timeit(lambda i=0: ops.wide_prefill_attention(qp, kvl, gkv, bt[:2], cl, cuq, ts, tst, op,
+                                                               window=win, softcap=50.0))
+            # causal (or windowed) score + PV FLOPs of the two sequences
+            pairs = sum(min(t + 1, win) if win else t + 1 for t in range(2048)) * 2
+            report(f"wide_prefill_attention_d{D}", ms, 4.0 * pairs * gnq * D, None,
+                   {"tokens": 4096, "window": win})
+            del kvl
+
     if not args.only or "norm" in args.only:
         for M in (256, 8192):
             x = torch.randn(M, H, device=dev, dtype=torch.bfloat16)

@@ -242,8 +242,10 @@ class LLMEngine:
     @staticmethod
     def from_preset(name: str, tp: Optional[TPInfo] = None, config: Optional[EngineConfig] = None, seed: int = 0,
                     device=None) -> "LLMEngine":
+        from ..models import build_decoder
+
         cfg = preset(name)
-        model = DecoderLM(cfg, tp, device)
+        model = build_decoder(cfg, tp, device)
         model.random_init(seed)
         return LLMEngine(model, config)
 

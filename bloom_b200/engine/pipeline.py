@@ -187,7 +187,9 @@ class InferencePipeline:
         from ..models.llama import DecoderLM
 
         if man is None:
-            dm = DecoderLM(cfg, tp_info, None)
+            from ..models import build_decoder
+
+            dm = build_decoder(cfg, tp_info, None)
             dm.random_init(0)
         else:
             from ..formats.loader import load_decoder

@@ -85,7 +85,7 @@ class EngineRegistry:
 def default_registry() -> EngineRegistry:
     r = EngineRegistry()
     r.register(EngineCapability(
-        name="b200", maturity="Beta", devices=["gpu"], families=["Llama", "Qwen", "Bert"],
+        name="b200", maturity="Beta", devices=["gpu"], families=["Llama", "Qwen", "Bert", "Gemma"],
         formats=["Safetensors", "Gguf", "Preset"], native_dtypes=["BF16", "F16", "Q8", "Q4"], fallback_dtypes=["F32"],
         modalities=["Text", "Embedding"], parallel_strategies=["None", "TensorParallel", "ExpertParallel",
                                                                "DataParallel"], max_tp=8))

@@ -32,6 +32,8 @@ def kv_block_bytes(model: DecoderLM, block_size: int = 16, kv_dtype: str = "bf16
     """Bytes of one KV block over all layers: bf16 pages, or int8 pages plus
     one fp32 scale per token and head (ops.kv_q8_block_bytes)."""
     cfg = model.cfg
+    if hasattr(model, "kv_block_bytes"):  # models that lay out their own KV slots (wide heads)
+        return model.kv_block_bytes()
     if kv_dtype == "int8":
         return cfg.num_layers * ops.kv_q8_block_bytes(model.nkv, cfg.head_dim)
     return cfg.num_layers * 2 * model.nkv * block_size * cfg.head_dim * 2
@@ -65,7 +67,12 @@ class ModelRunner:
         if kv_dtype not in ("bf16", "int8"):
             raise ValueError(f"kv cache dtype must be bf16 or int8, not {kv_dtype!r}")
         self.kv_dtype = kv_dtype
-        if kv_dtype == "int8":
+        self.wide = bool(getattr(model, "wide_attention", False))
+        if self.wide:
+            if kv_dtype != "bf16":
+                raise ValueError(f"{cfg.arch} keeps a bf16 KV cache")
+            self.kv_cache = torch.zeros(model.kv_cache_shape(num_blocks), dtype=torch.bfloat16, device=self.device)
+        elif kv_dtype == "int8":
             self.kv_cache = torch.zeros(cfg.num_layers, num_blocks, ops.kv_q8_block_bytes(model.nkv, cfg.head_dim),
                                         dtype=torch.uint8, device=self.device)
         else:
@@ -88,14 +95,18 @@ class ModelRunner:
         # decode attention split-K workspace, sized for the largest need over buckets
         ws = 1
         self.decode_splits: Dict[int, int] = {}
-        self.head_chunks = ops.decode_head_chunks(model.nq, model.nkv, self.q_len)
-        if self.head_chunks == 0:
-            raise ValueError(f"speculation length {spec_len} does not fit the decode attention kernel")
-        vkh = model.nkv * self.head_chunks  # CTAs per sequence and split
-        for b in range(1, max_num_seqs + 1):  # eager steps may have any decode count
-            s = ops.decode_attention_splits(b, vkh, self.max_blocks, self.device.index)
-            self.decode_splits[b] = s
-            ws = max(ws, ops.decode_workspace_numel(b, vkh, s))
+        self.head_chunks = 1
+        if self.wide:  # the model sizes its own decode attention workspace
+            model.prepare_runner(max_num_seqs, self.q_len, self.max_blocks)
+        else:
+            self.head_chunks = ops.decode_head_chunks(model.nq, model.nkv, self.q_len)
+            if self.head_chunks == 0:
+                raise ValueError(f"speculation length {spec_len} does not fit the decode attention kernel")
+            vkh = model.nkv * self.head_chunks  # CTAs per sequence and split
+            for b in range(1, max_num_seqs + 1):  # eager steps may have any decode count
+                s = ops.decode_attention_splits(b, vkh, self.max_blocks, self.device.index)
+                self.decode_splits[b] = s
+                ws = max(ws, ops.decode_workspace_numel(b, vkh, s))
         self.decode_ws = torch.empty(ws, dtype=torch.float32, device=self.device)
         self.graphs: Dict[tuple, tuple] = {}  # (decode rows, q_len) -> captured step
         self.last_logits: Optional[torch.Tensor] = None
@@ -166,7 +177,7 @@ class ModelRunner:
         T, Bd, Sp, NT, NL = m.num_tokens, m.num_decode, m.num_prefill, m.num_tiles, m.num_logits
         MB = self.max_blocks
         splits = 1
-        if Bd:
+        if Bd and not self.wide:
             splits = self.decode_splits.get(Bd) or ops.decode_attention_splits(
                 Bd, self.model.nkv * self.head_chunks, MB, self.device.index)
         return StepInputs(

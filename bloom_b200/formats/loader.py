@@ -62,13 +62,13 @@ def load_decoder(path: str, tp=None, device=None):
 
 
 def _load_decoder(path: str, tp=None, device=None):
-    from ..models.llama import DecoderLM
+    from ..models import build_decoder
 
     man = load_manifest(path)
     cfg = model_config(man)
-    model = DecoderLM(cfg, tp, device)
+    model = build_decoder(cfg, tp, device)
     gg = [f for f in man.files if f.format == "Gguf"]
-    if gg and (tp is None or tp.size == 1) and man.primary_dtype in ("Q8", "Q4"):
+    if gg and (tp is None or tp.size == 1) and man.primary_dtype in ("Q8", "Q4") and hasattr(model, "load_gguf"):
         # Q8_0 / Q4_0 projections stay block-quantised on the GPU (qgemv / dequant + tcgen05)
         model.load_gguf(os.path.join(man.root, gg[0].name), quantized=True)
         return model

@@ -30,7 +30,7 @@ HBM_BYTES_PER_GPU = 183_359 * 1024 * 1024  # B200 (nvidia-smi 183,359 MiB)
 GIB = 1 << 30
 
 FAMILIES = {"llama": "Llama", "mistral": "Llama", "qwen2": "Qwen", "qwen3": "Qwen", "qwen3_moe": "Qwen",
-            "bert": "Bert", "gemma": "Gemma"}
+            "bert": "Bert", "gemma": "Gemma", "gemma4": "Gemma", "gemma4_text": "Gemma", "gemma4_unified": "Gemma"}
 DTYPE_BYTES = {"F32": 4.0, "F16": 2.0, "BF16": 2.0, "Q8": 34 / 32, "Q4": 18 / 32, "I8": 1.0, "U8": 1.0, "I4": 0.5,
                "NF4": 0.5}
 

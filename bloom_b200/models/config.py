@@ -16,7 +16,7 @@ from typing import List, Optional
 
 @dataclass
 class ModelConfig:
-    arch: str = "llama"  # llama | qwen2 | qwen3 | qwen3_moe | mistral | bert
+    arch: str = "llama"  # llama | qwen2 | qwen3 | qwen3_moe | mistral | bert | gemma4
     vocab_size: int = 32000
     hidden_size: int = 4096
     num_layers: int = 32
@@ -36,6 +36,20 @@ class ModelConfig:
     num_experts_per_tok: int = 0
     moe_intermediate_size: int = 0
     norm_topk_prob: bool = True
+    # Gemma4 (executor/gemma4.rs Config :175-336): every `sliding_window_pattern`-th
+    # layer is global (head_dim_global, num_kv_heads_global, rope_theta,
+    # partial rotary, optional k = v), the others slide over `sliding_window`
+    # keys with head_dim / num_kv_heads / rope_local_theta
+    head_dim_global: int = 0
+    num_kv_heads_global: int = 0
+    sliding_window: int = 0
+    sliding_window_pattern: int = 6
+    rope_local_theta: float = 10000.0
+    partial_rotary_factor: float = 1.0
+    attn_logit_softcapping: float = 0.0
+    final_logit_softcapping: float = 0.0
+    attention_k_eq_v: bool = False
+    hidden_activation: str = "silu"
     # BERT
     type_vocab_size: int = 2
     layer_norm_eps: float = 1e-12
@@ -55,8 +69,27 @@ class ModelConfig:
     def is_moe(self) -> bool:
         return self.num_experts > 0
 
+    def is_sliding(self, layer: int) -> bool:
+        """Gemma4: layer `layer` attends over a sliding window (the reference's
+        (i + 1) % pattern > 0 rule, executor/gemma4.rs:1000)."""
+        return self.arch == "gemma4" and (layer + 1) % self.sliding_window_pattern > 0
+
+    def layer_attn(self, layer: int):
+        """(head_dim, num_kv_heads) of one layer's attention."""
+        if self.arch == "gemma4" and not self.is_sliding(layer):
+            return self.head_dim_global, self.num_kv_heads_global
+        return self.head_dim, self.num_kv_heads
+
     def num_params(self) -> int:
         H, L, V = self.hidden_size, self.num_layers, self.vocab_size
+        if self.arch == "gemma4":
+            n = V * H + H
+            for i in range(L):
+                d, kvh = self.layer_attn(i)
+                nv = 0 if (self.attention_k_eq_v and not self.is_sliding(i)) else 1
+                n += H * self.num_heads * d * 2 + H * kvh * d * (1 + nv) + 2 * d + 3 * H * self.intermediate_size
+                n += 4 * H + 1
+            return n
         attn = H * (self.q_size + 2 * self.kv_size) + self.q_size * H
         if self.is_moe:
             mlp = self.num_experts * 3 * H * self.moe_intermediate_size + H * self.num_experts
@@ -67,6 +100,9 @@ class ModelConfig:
 
     def kv_bytes_per_token(self, dtype_bytes: int = 2) -> int:
         # KV/token = 2 * L * kv_heads * head_dim * bytes (reference core/manifest.rs:252)
+        if self.arch == "gemma4":  # every layer's slot is sized for the widest layer
+            return 2 * self.num_layers * max(d * k for d, k in map(self.layer_attn, range(self.num_layers))) \
+                * dtype_bytes
         return 2 * self.num_layers * self.num_kv_heads * self.head_dim * dtype_bytes
 
     def to_json(self) -> str:
@@ -78,9 +114,38 @@ class ModelConfig:
         return ModelConfig(**{k: v for k, v in d.items() if k in names})
 
 
+def _gemma4_from_hf(cfg: dict) -> ModelConfig:
+    """Gemma4 text config (top level or `text_config`), with the reference's
+    defaults (executor/gemma4.rs:201-336)."""
+    t = cfg.get("text_config") or cfg
+    rp = t.get("rope_parameters") or {}
+    full, slide = rp.get("full_attention") or {}, rp.get("sliding_attention") or {}
+    eos = cfg.get("eos_token_id", t.get("eos_token_id"))
+    eos_ids = eos if isinstance(eos, list) else ([eos] if eos is not None else [1, 106])
+    hd = t["head_dim"]
+    return ModelConfig(
+        arch="gemma4", vocab_size=t["vocab_size"], hidden_size=t["hidden_size"], num_layers=t["num_hidden_layers"],
+        num_heads=t["num_attention_heads"], num_kv_heads=t["num_key_value_heads"], head_dim=hd,
+        intermediate_size=t["intermediate_size"], rms_norm_eps=t.get("rms_norm_eps", 1e-6),
+        rope_theta=full.get("rope_theta", 1_000_000.0), max_position_embeddings=t.get("max_position_embeddings", 131072),
+        tie_word_embeddings=True, qkv_bias=bool(t.get("attention_bias", False)), qk_norm=True,
+        head_dim_global=t.get("global_head_dim") or 512, num_kv_heads_global=t.get("num_global_key_value_heads") or 1,
+        sliding_window=t.get("sliding_window") or 1024, sliding_window_pattern=6,
+        rope_local_theta=slide.get("rope_theta", 10000.0),
+        partial_rotary_factor=full.get("partial_rotary_factor", 1.0),
+        attn_logit_softcapping=t.get("attn_logit_softcapping") or 0.0,
+        final_logit_softcapping=t.get("final_logit_softcapping") or 0.0,
+        attention_k_eq_v=bool(t.get("attention_k_eq_v", False)),
+        hidden_activation=t.get("hidden_activation", "gelu_pytorch_tanh"),
+        bos_token_id=cfg.get("bos_token_id", t.get("bos_token_id")), eos_token_ids=eos_ids,
+        name=cfg.get("_name_or_path", ""))
+
+
 def from_hf_config(cfg: dict) -> ModelConfig:
     """Map a Hugging Face config.json onto ModelConfig."""
     mt = (cfg.get("model_type") or "llama").lower()
+    if mt in ("gemma4", "gemma4_text", "gemma4_unified"):
+        return _gemma4_from_hf(cfg)
     arch = {"llama": "llama", "mistral": "llama", "qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe",
             "bert": "bert"}.get(mt, "llama")
     H = cfg.get("hidden_size", 4096)
@@ -199,6 +264,15 @@ PRESETS = {
                              num_kv_heads=2, head_dim=64, intermediate_size=512, rms_norm_eps=1e-5,
                              rope_theta=10000.0, max_position_embeddings=1024, tie_word_embeddings=True,
                              eos_token_ids=[2], name="tiny-hd64"),
+    # Gemma4 layout at test size: 5 sliding layers (head_dim 256, window 24) + 1 global
+    # (head_dim 512, one KV head, k = v, quarter rotary), both soft-caps on
+    "tiny-gemma4": ModelConfig(arch="gemma4", vocab_size=512, hidden_size=256, num_layers=6, num_heads=4,
+                               num_kv_heads=2, head_dim=256, intermediate_size=512, rms_norm_eps=1e-6,
+                               rope_theta=1_000_000.0, max_position_embeddings=1024, tie_word_embeddings=True,
+                               qk_norm=True, head_dim_global=512, num_kv_heads_global=1, sliding_window=24,
+                               sliding_window_pattern=6, rope_local_theta=10000.0, partial_rotary_factor=0.25,
+                               attn_logit_softcapping=50.0, final_logit_softcapping=30.0, attention_k_eq_v=True,
+                               hidden_activation="gelu_pytorch_tanh", eos_token_ids=[1, 106], name="tiny-gemma4"),
     "tiny-moe": ModelConfig(arch="qwen3_moe", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
                             num_kv_heads=2, head_dim=128, intermediate_size=512, rms_norm_eps=1e-6,
                             rope_theta=1000000.0, max_position_embeddings=1024, qk_norm=True, num_experts=8,

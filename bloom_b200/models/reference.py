@@ -6,6 +6,7 @@ token sequence with no KV cache.  Semantics: HF Llama/Qwen2/Qwen3 modelling
 """
 from __future__ import annotations
 
+import math
 from typing import Dict
 
 import torch
@@ -114,3 +115,113 @@ def random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02, device="c
             w[p + "mlp.up_proj.weight"] = rn(cfg.intermediate_size, H)
             w[p + "mlp.down_proj.weight"] = rn(H, cfg.intermediate_size)
     return w
+
+
+# ---------------------------------------------------------------- Gemma4
+GEMMA4_PREFIX = "model.language_model."
+
+
+def gemma4_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
+                          device="cpu") -> Dict[str, torch.Tensor]:
+    """HF-named random Gemma4 text weights (bf16).  Norm weights and layer
+    scalars are drawn around 1 so the test exercises them."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    H, I, nh = cfg.hidden_size, cfg.intermediate_size, cfg.num_heads
+    P = GEMMA4_PREFIX
+
+    def rn(*s):
+        return (torch.randn(*s, generator=g) * std).to(torch.bfloat16).to(device)
+
+    def near1(*s):
+        return (1.0 + 0.2 * torch.randn(*s, generator=g)).to(torch.bfloat16).to(device)
+
+    w = {P + "embed_tokens.weight": rn(cfg.vocab_size, H), P + "norm.weight": near1(H)}
+    for i in range(cfg.num_layers):
+        p = f"{P}layers.{i}."
+        d, kvh = cfg.layer_attn(i)
+        w[p + "self_attn.q_proj.weight"] = rn(nh * d, H)
+        w[p + "self_attn.k_proj.weight"] = rn(kvh * d, H)
+        if not (cfg.attention_k_eq_v and not cfg.is_sliding(i)):
+            w[p + "self_attn.v_proj.weight"] = rn(kvh * d, H)
+        w[p + "self_attn.o_proj.weight"] = rn(H, nh * d)
+        w[p + "self_attn.q_norm.weight"] = near1(d)
+        w[p + "self_attn.k_norm.weight"] = near1(d)
+        for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                  "post_feedforward_layernorm"):
+            w[p + n + ".weight"] = near1(H)
+        w[p + "mlp.gate_proj.weight"] = rn(I, H)
+        w[p + "mlp.up_proj.weight"] = rn(I, H)
+        w[p + "mlp.down_proj.weight"] = rn(H, I)
+        w[p + "layer_scalar"] = (0.75 + 0.5 * torch.rand(1, generator=g)).to(torch.bfloat16).to(device)
+    return w
+
+
+def _gelu_tanh(x):
+    return 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
+
+
+def gemma4_forward_logits(cfg: ModelConfig, w: Dict[str, torch.Tensor], tokens) -> torch.Tensor:
+    """fp32 Gemma4 text forward over one sequence (executor/gemma4.rs semantics:
+    scaled embedding, q/k/v norms, partial RoPE on global layers, attention
+    scale 1, soft-capped scores, sliding-window masks of `sliding_window` keys,
+    sandwich norms, layer scalar, tied lm_head, soft-capped logits)."""
+    P = GEMMA4_PREFIX
+    emb = w[P + "embed_tokens.weight"]
+    dev = emb.device
+    ids = torch.as_tensor(tokens, device=dev).long()
+    T = ids.numel()
+    H, eps, nh = cfg.hidden_size, cfg.rms_norm_eps, cfg.num_heads
+    x = emb[ids].float() * math.sqrt(H)
+    x = x.to(torch.bfloat16).float()  # the embedding runs in bf16 in the model
+    pos = torch.arange(T, device=dev)
+    qi, kj = pos[:, None], pos[None, :]
+
+    def rms(t, wt=None):
+        y = t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps)
+        return y * wt.float() if wt is not None else y
+
+    def rope(t, rot, denom, theta):
+        half = rot // 2
+        inv = 1.0 / (theta ** (torch.arange(0, half, device=dev, dtype=torch.float64) * 2 / denom))
+        ang = (pos.double()[:, None] * inv[None, :]).float()
+        c, s = ang.cos()[:, None, :], ang.sin()[:, None, :]
+        x1, x2, rest = t[..., :half], t[..., half:rot], t[..., rot:]
+        return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s, rest], dim=-1)
+
+    for i in range(cfg.num_layers):
+        p = f"{P}layers.{i}."
+        sliding = cfg.is_sliding(i)
+        d, kvh = cfg.layer_attn(i)
+        rot = d if sliding else int(d * cfg.partial_rotary_factor)
+        theta = cfg.rope_local_theta if sliding else cfg.rope_theta
+        h = rms(x, w[p + "input_layernorm.weight"])
+        q = (h @ w[p + "self_attn.q_proj.weight"].float().t()).view(T, nh, d)
+        k = (h @ w[p + "self_attn.k_proj.weight"].float().t()).view(T, kvh, d)
+        vw = w.get(p + "self_attn.v_proj.weight")
+        v = (h @ vw.float().t()).view(T, kvh, d) if vw is not None else k
+        q = rope(rms(q, w[p + "self_attn.q_norm.weight"]), rot, d, theta)
+        k2 = rope(rms(k, w[p + "self_attn.k_norm.weight"]), rot, d, theta)
+        v = rms(v)
+        G = nh // kvh
+        kk = k2.repeat_interleave(G, dim=1)
+        vv = v.repeat_interleave(G, dim=1)
+        sc = torch.einsum("qhd,khd->hqk", q, kk)  # attention scale 1
+        if cfg.attn_logit_softcapping:
+            sc = cfg.attn_logit_softcapping * torch.tanh(sc / cfg.attn_logit_softcapping)
+        vis = kj <= qi
+        if sliding:
+            vis = vis & (kj > qi - cfg.sliding_window)
+        sc = sc.masked_fill(~vis[None], float("-inf"))
+        a = torch.einsum("hqk,khd->qhd", sc.softmax(-1), vv).reshape(T, nh * d)
+        a = a @ w[p + "self_attn.o_proj.weight"].float().t()
+        x = x + rms(a, w[p + "post_attention_layernorm.weight"])
+        h = rms(x, w[p + "pre_feedforward_layernorm.weight"])
+        gt = h @ w[p + "mlp.gate_proj.weight"].float().t()
+        up = h @ w[p + "mlp.up_proj.weight"].float().t()
+        m = (_gelu_tanh(gt) * up) @ w[p + "mlp.down_proj.weight"].float().t()
+        x = (x + rms(m, w[p + "post_feedforward_layernorm.weight"])) * w[p + "layer_scalar"].float()
+    logits = rms(x, w[P + "norm.weight"]) @ emb.float().t()
+    if cfg.final_logit_softcapping:
+        logits = cfg.final_logit_softcapping * torch.tanh(logits / cfg.final_logit_softcapping)
+    return logits

@@ -29,6 +29,7 @@ EPI_PARTIAL_F32 = 3
 EPI_RESIDUAL = 4
 EPI_GELU = 5  # erf form
 EPI_GELU_TANH = 6  # tanh approximation ("gelu_pytorch_tanh")
+EPI_GEGLU = 7  # gelu_tanh(gate) * up, weight rows interleaved like EPI_SWIGLU
 
 
 def status(device: Optional[int] = None) -> torch.Tensor:
@@ -170,7 +171,7 @@ def gemm(
     M, N = x.shape[0], w.shape[0]
     K = x.shape[1]
     if splits is None and bn is None:
-        tuned = GEMM_TUNED.get((_m_bucket(M), N, K, epi == EPI_SWIGLU)) if M <= 512 else None
+        tuned = GEMM_TUNED.get((_m_bucket(M), N, K, epi in (EPI_SWIGLU, EPI_GEGLU))) if M <= 512 else None
         if tuned is not None:
             bn, splits = tuned
     if bn is None:
@@ -183,7 +184,7 @@ def gemm(
     if splits > 1 and epi != EPI_PARTIAL_F32:
         fix_ws, fix_cnt = _fixup_buffers(x.device, _C().gemm_fixup_ws_floats(M, N, splits, bn))
     if out is None:
-        if epi == EPI_SWIGLU:
+        if epi in (EPI_SWIGLU, EPI_GEGLU):
             out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
         elif epi == EPI_F32:
             out = torch.empty(M, N, dtype=torch.float32, device=x.device)
@@ -564,6 +565,85 @@ def paged_prefill_attention(q, kv_cache, layer, block_table, ctx_lens, cu_seqlen
        status(q.device.index))
     _count()
     return out
+
+
+# ---------------------------------------------------------------- Gemma4 (wide heads)
+def _num_sms(device: int = 0) -> int:
+    if torch.cuda.is_available():
+        return torch.cuda.get_device_properties(device).multi_processor_count
+    return 148
+
+
+def wide_cos_sin(max_pos: int, rot: int, denom: int, theta: float, device=None) -> torch.Tensor:
+    """[max_pos, rot] f32 = [cos | sin] of the angles pos * theta^(-2i / denom),
+    i < rot / 2: RoPE on the first `rot` dims of a head of `denom` dims
+    (partial rotary keeps the full head's frequency spacing)."""
+    inv = 1.0 / (theta ** (torch.arange(0, rot // 2, dtype=torch.float64) * 2 / denom))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cat([ang.cos(), ang.sin()], dim=1).float().to(device).contiguous()
+
+
+def gemma_qkv_write(qkv, positions, slot_mapping, cos_sin, q_out, kv_layer, num_q_heads: int, num_kv_heads: int,
+                    rot: int, q_norm, k_norm, eps: float, k_eq_v: bool = False):
+    """q/k RMSNorm (scaled), v RMSNorm (unscaled; v = the raw k row when
+    k_eq_v), RoPE on the first `rot` dims of q and k, q -> q_out [T, nq, D],
+    k / v -> this layer's pages of the wide KV cache (kv_layer [NB, E])."""
+    _C().gemma_qkv_write(qkv, positions, slot_mapping, cos_sin, q_out, kv_layer, num_q_heads, num_kv_heads, rot,
+                         q_norm, k_norm, eps, k_eq_v, status(qkv.device.index))
+    _count()
+    return q_out
+
+
+def wide_decode_splits(batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int, q_len: int,
+                       max_kv_len: int, window: int = 0, device: int = 0) -> int:
+    return _C().wide_decode_splits(batch, num_q_heads, num_kv_heads, head_dim, q_len, max_kv_len, window,
+                                   _num_sms(device))
+
+
+def wide_decode_workspace_numel(batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int, q_len: int,
+                                splits: int) -> int:
+    return _C().wide_decode_workspace_numel(batch, num_q_heads, num_kv_heads, head_dim, q_len, splits)
+
+
+def wide_decode_attention(q, kv_layer, num_kv_heads: int, block_table, seq_lens, out, *, q_len: int = 1,
+                          window: int = 0, scale: float = 1.0, softcap: float = 0.0, splits: int = 1,
+                          workspace=None):
+    """Paged decode / verify attention for head_dim 256 / 512 (q [B*q_len, nq, D]).
+
+    window > 0: the query at position p sees keys p - window < j <= p.
+    softcap > 0: scores become softcap * tanh(scale * q.k / softcap)."""
+    _C().wide_decode_attention(q, out, kv_layer, num_kv_heads, block_table, seq_lens, q_len, window, scale, softcap,
+                               splits, workspace, status(q.device.index))
+    _count(2 if splits > 1 else 1)
+    return out
+
+
+def wide_prefill_attention(q, kv_layer, num_kv_heads: int, block_table, ctx_lens, cu_seqlens_q, tile_seq,
+                           tile_start, out, *, window: int = 0, scale: float = 1.0, softcap: float = 0.0):
+    """Chunked-prefill attention over the wide paged cache (tiles of `prefill_tiles`)."""
+    _C().wide_prefill_attention(q, out, kv_layer, num_kv_heads, block_table, ctx_lens, cu_seqlens_q, tile_seq,
+                                tile_start, window, scale, softcap, status(q.device.index))
+    _count()
+    return out
+
+
+def residual_norm(a, x, w_post=None, w_next=None, y=None, *, in_scale: float = 1.0, out_scale: float = 1.0,
+                  eps: float = 1e-6):
+    """Gemma residual stream step, in place on x (bf16 [T, H]):
+    w_post None: x = a * in_scale; else x = (x + rmsnorm(a) * w_post) * out_scale;
+    then y = rmsnorm(x) * w_next when w_next is given (y allocated if None)."""
+    if w_next is not None and y is None:
+        y = torch.empty_like(x)
+    _C().residual_norm(a, x, w_post, w_next, y if w_next is not None else None, in_scale, out_scale, eps)
+    _count()
+    return y
+
+
+def softcap_(v: torch.Tensor, cap: float) -> torch.Tensor:
+    """v = cap * tanh(v / cap) in place (bf16)."""
+    _C().softcap_(v, cap)
+    _count()
+    return v
 
 
 def prefill_tiles(cu_seqlens_q, ctx_lens, tile_rows: int = 128):

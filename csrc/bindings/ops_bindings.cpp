@@ -18,6 +18,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("EPI_PARTIAL_F32") = int(bloom::kEpiPartialF32);
   m.attr("EPI_RESIDUAL") = int(bloom::kEpiResidual);
   m.attr("EPI_GELU") = int(bloom::kEpiGelu);
+  m.attr("EPI_GEGLU") = int(bloom::kEpiGeGLU);
   m.def("gemm_out", &bloom::gemm_out, "y = x @ w^T on tcgen05 with fused epilogue", py::arg("x"), py::arg("w"),
         py::arg("out"), py::arg("epi"), py::arg("resid"), py::arg("bias"), py::arg("splits"), py::arg("status"),
         py::arg("fix_ws"), py::arg("fix_count"), py::arg("bn_override"),
@@ -27,6 +28,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped_out", &bloom::gemm_grouped_out);
   m.def("moe_route", &bloom::moe_route);
   m.def("moe_plan", &bloom::moe_plan);
+  m.def("wide_decode_splits", &bloom::wide_decode_splits);
+  m.def("wide_decode_workspace_numel", &bloom::wide_decode_workspace_numel);
+  m.def("wide_decode_attention", &bloom::wide_decode_attention);
+  m.def("wide_prefill_attention", &bloom::wide_prefill_attention);
+  m.def("gemma_qkv_write", &bloom::gemma_qkv_write);
+  m.def("residual_norm", &bloom::residual_norm);
+  m.def("softcap_", &bloom::softcap_);
+  m.def("moe_route_plan", &bloom::moe_route_plan, "routing + plan in one single-CTA launch (decode-sized batches)");
   m.def("moe_gather", &bloom::moe_gather);
   m.def("moe_combine", &bloom::moe_combine, py::arg("ys"), py::arg("pos"), py::arg("topk_w"), py::arg("out"),
         py::arg("push_ptrs") = std::vector<int64_t>{}, py::arg("push_rank") = 0, py::arg("push_rows") = 0);

@@ -14,6 +14,7 @@ enum GemmEpilogue : int {
   kEpiResidual = 4,    // out bf16 [M, N] = acc + resid
   kEpiGelu = 5,        // out bf16 [M, N] = gelu_erf(acc + bias)
   kEpiGeluTanh = 6,    // out bf16 [M, N] = gelu_tanh(acc + bias) (runs the kEpiGelu kernels with Args::gelu_tanh)
+  kEpiGeGLU = 7,       // as kEpiSwiGLU with gelu_tanh(g) * u (runs the kEpiSwiGLU kernels with Args::gelu_tanh)
 };
 
 // splits > 1 with a non-partial epilogue: split-K where the last-arriving CTA
@@ -40,6 +41,10 @@ void gemm_grouped_out(const torch::Tensor& x, const torch::Tensor& w, torch::Ten
 // Mixture of experts.
 void moe_route(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0, int64_t e_local,
                torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& counts);
+void moe_route_plan(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0, int64_t e_local,
+                    torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& offsets,
+                    int64_t bn, int64_t ft_gu, int64_t ft_d, torch::Tensor& tiles_gu, torch::Tensor& n_gu,
+                    torch::Tensor& tiles_d, torch::Tensor& n_d);
 void moe_plan(torch::Tensor& counts, torch::Tensor& offsets, int64_t bn, int64_t ft_gu, int64_t ft_d,
               torch::Tensor& tiles_gu, torch::Tensor& n_gu, torch::Tensor& tiles_d, torch::Tensor& n_d);
 void moe_gather(const torch::Tensor& x, int64_t e0, int64_t e_local, const torch::Tensor& topk_ids,
@@ -179,5 +184,29 @@ inline int* check_word(int64_t device) {
   return nullptr;
 #endif
 }
+
+// Gemma4 (csrc/kernels/gemma.cu): wide-head paged attention with sliding windows and
+// soft-capping, q/k/v norm + partial RoPE + KV write, sandwich residual norms, logit soft-cap
+int64_t wide_decode_splits(int64_t batch, int64_t nq, int64_t nkv, int64_t head_dim, int64_t q_len,
+                           int64_t max_kv_len, int64_t window, int64_t num_sms);
+int64_t wide_decode_workspace_numel(int64_t batch, int64_t nq, int64_t nkv, int64_t head_dim, int64_t q_len,
+                                    int64_t splits);
+void wide_decode_attention(const torch::Tensor& q, torch::Tensor& out, const torch::Tensor& kv_layer, int64_t nkv,
+                           const torch::Tensor& block_table, const torch::Tensor& seq_lens, int64_t q_len,
+                           int64_t window, double scale, double softcap, int64_t splits,
+                           const c10::optional<torch::Tensor>& workspace, const torch::Tensor& status);
+void wide_prefill_attention(const torch::Tensor& q, torch::Tensor& out, const torch::Tensor& kv_layer, int64_t nkv,
+                            const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
+                            const torch::Tensor& cu_q, const torch::Tensor& tile_seq,
+                            const torch::Tensor& tile_start, int64_t window, double scale, double softcap,
+                            const torch::Tensor& status);
+void gemma_qkv_write(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& slots,
+                     const torch::Tensor& cos_sin, torch::Tensor& q_out, torch::Tensor& kv_layer, int64_t nq,
+                     int64_t nkv, int64_t rot, const torch::Tensor& q_w, const torch::Tensor& k_w, double eps,
+                     bool k_eq_v, const torch::Tensor& status);
+void residual_norm(const torch::Tensor& a, torch::Tensor& x, const c10::optional<torch::Tensor>& w_post,
+                   const c10::optional<torch::Tensor>& w_next, const c10::optional<torch::Tensor>& y,
+                   double in_scale, double out_scale, double eps);
+void softcap_(torch::Tensor& v, double cap);
 
 }  // namespace bloom

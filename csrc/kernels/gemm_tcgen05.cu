@@ -73,7 +73,7 @@ struct Args {
   // [world][push_rows][ldo] layout, while the rest of the GEMM runs.
   unsigned long long push[8];
   int push_world, push_rank, push_rows;
-  int gelu_tanh;  // kEpiGelu: 1 = tanh approximation, 0 = erf
+  int gelu_tanh;  // kEpiGelu: 1 = tanh approximation, 0 = erf; kEpiSwiGLU: 1 = GeGLU gate
   // Activations written by a deferred tensor-parallel all-gather: before the
   // first activation tile, the producer waits (bounded) until every peer's
   // rows arrived (wait_deferred_rows on this rank's flag block); nullptr = none
@@ -201,7 +201,11 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const float up = __shfl_down_sync(0xffffffffu, v[j], 16);
-        scr[j * kScrStride + lane] = silu(v[j]) * up;  // lanes >= 16 write unused columns
+        // lanes >= 16 write unused columns; gelu_tanh: the GeGLU gate (kEpiGeGLU)
+        const float gate = a.gelu_tanh
+                               ? 0.5f * v[j] * (1.f + tanhf(0.7978845608028654f * (v[j] + 0.044715f * v[j] * v[j] * v[j])))
+                               : silu(v[j]);
+        scr[j * kScrStride + lane] = gate * up;
       }
       __syncwarp();
       const int tok = tok0 + c + r;
@@ -1137,8 +1141,9 @@ void gemm_out(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out
   TORCH_CHECK(w.size(1) == K, "gemm: K mismatch");
   TORCH_CHECK(K % 8 == 0, "gemm: K must be a multiple of 8");
   if (M == 0) return;
-  const bool gelu_tanh = epi == kEpiGeluTanh;
-  if (gelu_tanh) epi = kEpiGelu;
+  const bool gelu_tanh = epi == kEpiGeluTanh || epi == kEpiGeGLU;
+  if (epi == kEpiGeluTanh) epi = kEpiGelu;
+  if (epi == kEpiGeGLU) epi = kEpiSwiGLU;
   const at::cuda::CUDAGuard guard(x.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 

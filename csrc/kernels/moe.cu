@@ -4,6 +4,8 @@
 //   moe_route    per token: softmax over the router logits, top-k, optional
 //                renormalisation; tokens routed to this rank's experts
 //                [e0, e0 + E_local) take a slot in their expert (atomic count)
+//   moe_route_plan  decode-sized batches (T <= 512): both of the above in
+//                one single-CTA launch, expert counts in shared memory
 //   moe_plan     one CTA: exclusive scan of the expert counts into row
 //                offsets, then the tile lists of the two grouped GEMMs
 //                (gate_up with SwiGLU, down) -- built on the device, so the
@@ -32,33 +34,41 @@ namespace {
 
 constexpr int kMaxTopK = 16;
 
-// one warp per token
-__global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E, int K, int norm, int e0, int El,
-                                 int* __restrict__ topk_ids, float* __restrict__ topk_w, int* __restrict__ slot,
-                                 int* __restrict__ counts) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const float* row = logits + (long)warp * E;
+// Router softmax + top-k of one token by one warp, in registers: each lane
+// holds experts lane, lane + 32, ... (E <= 32 * NV); k rounds of a warp-wide
+// arg-max (lowest index wins ties), the owner lane marks its winner in a bit
+// mask.  Lane k returns the k-th choice and its (optionally renormalised)
+// probability.
+template <int NV>
+__device__ __forceinline__ void route_token_warp(const float* __restrict__ row, int E, int K, int norm, int lane,
+                                                 int& my_id, float& my_p) {
+  float v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int e = lane + 32 * i;
+    const float x = e < E ? row[e] : -INFINITY;
+    v[i] = x == x ? x : -INFINITY;  // a NaN logit ranks last
+  }
   float mx = -INFINITY;
-  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) mx = fmaxf(mx, v[i]);
   mx = warp_max(mx);
   float z = 0.f;
-  for (int e = lane; e < E; e += 32) z += __expf(row[e] - mx);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) z += (lane + 32 * i < E) ? __expf(v[i] - mx) : 0.f;
   z = warp_sum(z);
-  // iterative top-k (lowest index wins ties)
-  int chosen[kMaxTopK];
-  float prob[kMaxTopK];
+  uint32_t taken = 0u;
   float psum = 0.f;
+  my_id = 0;
+  my_p = 0.f;
   for (int k = 0; k < K; ++k) {
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int e = lane; e < E; e += 32) {
-      bool taken = false;
-      for (int j = 0; j < k; ++j) taken |= (chosen[j] == e);
-      const float v = taken ? -INFINITY : row[e];
-      if (v > best || (v == best && e < bi)) {
-        best = v;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((taken >> i) & 1u) && (v[i] > best || (v[i] == best && e < bi))) {
+        best = v[i];
         bi = e;
       }
     }
@@ -71,25 +81,93 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E,
         bi = i2;
       }
     }
-    chosen[k] = bi;
-    prob[k] = __expf(best - mx) / z;
-    psum += prob[k];
+    if (bi < E && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const float p = __expf(best - mx) / z;
+    psum += p;
+    if (lane == k) {
+      my_id = bi;
+      my_p = p;
+    }
   }
+  if (norm) my_p /= psum;
+}
+
+// one warp per token
+__global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E, int K, int norm, int e0, int El,
+                                 int* __restrict__ topk_ids, float* __restrict__ topk_w, int* __restrict__ slot,
+                                 int* __restrict__ counts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  int id;
+  float p;
+  route_token_warp<8>(logits + (long)warp * E, E, K, norm, lane, id, p);
   if (lane < K) {
-    float p = 0.f;
-    int id = 0;
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j)
-      if (j == lane) {
-        p = prob[j];
-        id = chosen[j];
-      }
-    if (norm) p /= psum;
     topk_ids[(long)warp * K + lane] = id;
     topk_w[(long)warp * K + lane] = p;
     int s = -1;
     if (id >= e0 && id < e0 + El) s = atomicAdd(counts + (id - e0), 1);
     slot[(long)warp * K + lane] = s;
+  }
+}
+
+// Decode-sized batches: routing and planning in one launch of one CTA (1,024
+// threads, 32 warps striding over the tokens, local expert counts in shared
+// memory), so the plan needs no second launch and no global counters.
+__global__ void __launch_bounds__(1024) moe_route_plan_kernel(
+    const float* __restrict__ logits, int T, int E, int K, int norm, int e0, int El, int* __restrict__ topk_ids,
+    float* __restrict__ topk_w, int* __restrict__ slot, int* __restrict__ offsets, int bn, int ft_gu, int ft_d,
+    int4* __restrict__ tiles_gu, int* __restrict__ n_gu, int4* __restrict__ tiles_d, int* __restrict__ n_d,
+    int max_tiles) {
+  __shared__ int cnt_s[1024];
+  __shared__ int off_s[1025];
+  __shared__ int cnt_gu, cnt_d;
+  for (int e = threadIdx.x; e < El; e += blockDim.x) cnt_s[e] = 0;
+  if (threadIdx.x == 0) {
+    cnt_gu = 0;
+    cnt_d = 0;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < T; t += 32) {
+    int id;
+    float p;
+    route_token_warp<8>(logits + (long)t * E, E, K, norm, lane, id, p);
+    if (lane < K) {
+      topk_ids[(long)t * K + lane] = id;
+      topk_w[(long)t * K + lane] = p;
+      slot[(long)t * K + lane] = (id >= e0 && id < e0 + El) ? atomicAdd(&cnt_s[id - e0], 1) : -1;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < El; ++e) {
+      off_s[e] = acc;
+      acc += cnt_s[e];
+    }
+    off_s[El] = acc;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e <= El; e += blockDim.x) offsets[e] = off_s[e];
+  for (int e = threadIdx.x; e < El; e += blockDim.x) {
+    const int c = off_s[e + 1] - off_s[e];
+    for (int tt = 0; tt < (c + bn - 1) / bn; ++tt) {
+      const int r0 = off_s[e] + tt * bn, r1 = off_s[e + 1];
+      for (int f = 0; f < ft_gu; ++f) {
+        const int i = atomicAdd(&cnt_gu, 1);
+        if (i < max_tiles) tiles_gu[i] = make_int4(e, f, r0, r1);
+      }
+      for (int f = 0; f < ft_d; ++f) {
+        const int i = atomicAdd(&cnt_d, 1);
+        if (i < max_tiles) tiles_d[i] = make_int4(e, f, r0, r1);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *n_gu = min(cnt_gu, max_tiles);
+    *n_d = min(cnt_d, max_tiles);
   }
 }
 
@@ -225,6 +303,7 @@ void moe_route(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0
                torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& counts) {
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "moe_route: f32 logits");
   TORCH_CHECK(top_k >= 1 && top_k <= kMaxTopK, "moe_route: top_k in [1, 16]");
+  TORCH_CHECK(logits.size(1) <= 256 && logits.size(1) >= top_k, "moe_route: top_k <= experts <= 256");
   const int T = logits.size(0), E = logits.size(1);
   if (T == 0) return;
   const at::cuda::CUDAGuard g(logits.device());
@@ -233,6 +312,25 @@ void moe_route(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0
   moe_route_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       logits.data_ptr<float>(), T, E, int(top_k), norm ? 1 : 0, int(e0), int(e_local), topk_ids.data_ptr<int>(),
       topk_w.data_ptr<float>(), slot.data_ptr<int>(), counts.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_route_plan(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0, int64_t e_local,
+                    torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& offsets,
+                    int64_t bn, int64_t ft_gu, int64_t ft_d, torch::Tensor& tiles_gu, torch::Tensor& n_gu,
+                    torch::Tensor& tiles_d, torch::Tensor& n_d) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "moe_route_plan: f32 logits");
+  TORCH_CHECK(top_k >= 1 && top_k <= kMaxTopK, "moe_route_plan: top_k in [1, 16]");
+  TORCH_CHECK(logits.size(1) <= 256 && logits.size(1) >= top_k, "moe_route_plan: top_k <= experts <= 256");
+  TORCH_CHECK(e_local <= 1024, "moe_route_plan: at most 1024 local experts");
+  TORCH_CHECK(tiles_gu.size(0) == tiles_d.size(0) && tiles_gu.size(1) == 4, "moe_route_plan: tiles [n, 4] int32");
+  const int T = logits.size(0), E = logits.size(1);
+  const at::cuda::CUDAGuard g(logits.device());
+  moe_route_plan_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      logits.data_ptr<float>(), T, E, int(top_k), norm ? 1 : 0, int(e0), int(e_local), topk_ids.data_ptr<int>(),
+      topk_w.data_ptr<float>(), slot.data_ptr<int>(), offsets.data_ptr<int>(), int(bn), int(ft_gu), int(ft_d),
+      reinterpret_cast<int4*>(tiles_gu.data_ptr<int>()), n_gu.data_ptr<int>(),
+      reinterpret_cast<int4*>(tiles_d.data_ptr<int>()), n_d.data_ptr<int>(), int(tiles_gu.size(0)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

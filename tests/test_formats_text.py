@@ -209,7 +209,53 @@ def test_registry_routing():
     assert r.route("Llama", "Safetensors", "F32", "gpu") == ("b200", FALLBACK)
     assert r.route("Llama", "Gguf", "Q8", "cpu") == ("cpu", NATIVE)
     assert r.route("Whisper", "Gguf", "Q8", "cpu")[1] == UNSUPPORTED
+    assert r.route("Gemma", "Safetensors", "BF16", "gpu") == ("b200", NATIVE)
     assert any(e["name"] == "b200" and e["max_tp"] == 8 for e in r.describe())
+
+
+def test_gemma4_config_from_hf_and_layer_geometry():
+    from bloom_b200.models import build_decoder
+    from bloom_b200.models.config import from_hf_config
+
+    hf = {"model_type": "gemma4", "eos_token_id": [1, 106],
+          "text_config": {"hidden_size": 2560, "num_hidden_layers": 12, "num_attention_heads": 8,
+                          "num_key_value_heads": 4, "head_dim": 256, "global_head_dim": 512,
+                          "num_global_key_value_heads": 1, "intermediate_size": 10240, "vocab_size": 262144,
+                          "sliding_window": 512, "attention_k_eq_v": True, "final_logit_softcapping": 30.0,
+                          "rope_parameters": {"full_attention": {"rope_theta": 1e6, "partial_rotary_factor": 0.25},
+                                              "sliding_attention": {"rope_theta": 1e4}}}}
+    c = from_hf_config(hf)
+    assert c.arch == "gemma4" and c.tie_word_embeddings and c.eos_token_ids == [1, 106]
+    assert [c.is_sliding(i) for i in range(12)] == [True] * 5 + [False] + [True] * 5 + [False]
+    assert c.layer_attn(0) == (256, 4) and c.layer_attn(5) == (512, 1)
+    assert c.partial_rotary_factor == 0.25 and c.rope_local_theta == 1e4 and c.sliding_window == 512
+    # every layer's KV slot is sized for the widest layer: max(2*4*256, 2*1*512) per token and layer
+    assert c.kv_bytes_per_token() == 2 * 12 * 1024 * 2
+    with pytest.raises(ValueError):
+        from bloom_b200.models.llama import TPInfo
+
+        build_decoder(c, TPInfo(rank=0, size=2), "cpu")
+
+
+def test_gemma4_oracle_window_and_softcap():
+    """The fp32 oracle: a window wider than the sequence is plain causal
+    attention, a narrower one changes late positions only; soft-capping
+    bounds the logits."""
+    import dataclasses
+
+    from bloom_b200.models.config import preset
+    from bloom_b200.models.reference import gemma4_forward_logits, gemma4_random_weights
+
+    cfg = preset("tiny-gemma4")
+    w = gemma4_random_weights(cfg, seed=1, std=0.08)
+    toks = list(range(3, 43))
+    wide = gemma4_forward_logits(dataclasses.replace(cfg, sliding_window=1000), w, toks)
+    full = gemma4_forward_logits(dataclasses.replace(cfg, sliding_window=len(toks)), w, toks)
+    assert torch.allclose(wide, full, atol=1e-4)
+    narrow = gemma4_forward_logits(cfg, w, toks)  # window 24
+    assert torch.allclose(narrow[:24], full[:24], atol=1e-4)
+    assert not torch.allclose(narrow[30:], full[30:], atol=1e-3)
+    assert narrow.abs().max().item() <= cfg.final_logit_softcapping + 1e-4
 
 
 # ---------------------------------------------------------------- CPU engine
