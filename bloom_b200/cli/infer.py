@@ -87,6 +87,15 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--no-cuda-graphs", action="store_true")
     ap.add_argument("--template", default=None, help="chat template override (chatml, llama3, llama2, gemma, ...)")
     ap.add_argument("--raw", action="store_true", help="do not apply a chat template")
+    # text-to-video (--backend wan; bloom_infer.rs VideoGeneration arguments)
+    ap.add_argument("--negative-prompt", default=None)
+    ap.add_argument("--width", type=int, default=832)
+    ap.add_argument("--height", type=int, default=480)
+    ap.add_argument("--num-frames", type=int, default=81)
+    ap.add_argument("--fps", type=float, default=16.0)
+    ap.add_argument("--guidance-scale", type=float, default=5.0)
+    ap.add_argument("--num-steps", type=int, default=50)
+    ap.add_argument("-o", "--output", default=None, help="video output: .gif, or a directory / .png for PNG frames")
     return ap
 
 
@@ -106,6 +115,33 @@ def read_prompt(args) -> Optional[str]:
     if args.prompt == "-":
         return sys.stdin.read()
     return args.prompt
+
+
+def run_video(args) -> int:
+    """Text-to-video with the Wan 2.1 pipeline.  --model names a preset pair
+    'dit[:vae[:t5]]' of random-weight shapes (no checkpoint download here)."""
+    from ..engine.video import WanVideoPipeline
+
+    parts = (args.model or "tiny-wan").split(":")
+    dit = parts[0]
+    vae = parts[1] if len(parts) > 1 else ("tiny" if dit.startswith("tiny") else "wan2.1")
+    t5 = parts[2] if len(parts) > 2 else ("tiny" if dit.startswith("tiny") else "umt5-xxl")
+    pipe = WanVideoPipeline.from_presets(dit, vae, t5, seed=0)
+    total = [0]
+
+    def progress(step, n):
+        total[0] = n
+        if not args.quiet:
+            print(f"diffusion step {step}/{n}", file=sys.stderr)
+
+    out = pipe.generate(args.prompt or "", negative_prompt=args.negative_prompt, width=args.width,
+                        height=args.height, num_frames=args.num_frames, fps=args.fps,
+                        guidance_scale=args.guidance_scale, num_steps=args.num_steps, seed=args.seed,
+                        progress=progress)
+    files = out.save(args.output) if args.output else []
+    print(json.dumps({"width": out.width, "height": out.height, "fps": out.fps, "frame_count": out.frame_count,
+                      "steps": total[0], "files": files, "timings": {k: round(v, 4) for k, v in out.timings.items()}}))
+    return 0
 
 
 def main(argv: Optional[List[str]] = None) -> int:
@@ -134,6 +170,8 @@ def main(argv: Optional[List[str]] = None) -> int:
         print(json.dumps(InferencePipeline.inspect(args.model, opts["context_size"], reg, tp=args.tp), indent=2))
         return 0
     t0 = time.perf_counter()
+    if args.backend == "wan":
+        return run_video(args)
     if args.image:
         return run_image(args, opts)
     if args.backend in ("llamacpp", "script"):

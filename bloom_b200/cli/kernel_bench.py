@@ -312,6 +312,46 @@ def main():
                    {"tokens": 4096, "window": win})
             del kvl
 
+    if args.only and "wan" in args.only:
+        # Wan2.1-T2V-1.3B: one guided DiT evaluation (batch 2) over a 17-frame 480 x 832 video latent
+        # (5 x 60 x 104 -> 7,800 tokens per sample) and the VAE decode of 2 latent frames to 480 x 832
+        from bloom_b200.models.wan import WanDiT, sampling_sigmas, wan_preset
+        from bloom_b200.models.wan_vae import WanVAE, vae_preset
+
+        wc = wan_preset("wan2.1-t2v-1.3b")
+        dit = WanDiT(wc, dev)
+        dit.random_init(0)
+        ctx = (torch.randn(2, wc.text_len, wc.text_dim, device=dev) * 0.3).to(torch.bfloat16)
+        text = dit.encode_text(ctx)
+        lat = torch.randn(wc.in_dim, 5, 60, 104, device=dev)
+        lb = lat.unsqueeze(0).expand(2, *lat.shape).contiguous()
+        def eager_ms(fn, iters, warmup):  # host-built timestep inputs: not graph-capturable, time eagerly
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / iters
+
+        ms = eager_ms(lambda: dit.velocity_tokens(lb, 500.0, text), 3, 2)
+        S = 5 * 30 * 52
+        T = 2 * S
+        D, Fd, L = wc.dim, wc.ffn_dim, wc.text_len
+        gemm_flops = 2.0 * T * wc.num_layers * (3 * D * D + D * D + D * D + D * D + 2 * D * Fd)
+        attn_flops = 4.0 * 2 * wc.num_layers * (S * S + S * L) * D
+        report("wan_dit_step_1.3b_cfg", ms, gemm_flops + attn_flops, None, {"tokens": T, "text_len": L})
+        del dit, text
+        vae = WanVAE(vae_preset("wan2.1"), dev)
+        vae.random_init(0)
+        z = torch.randn(16, 2, 60, 104, device=dev)
+        ms = eager_ms(lambda: vae.decode(z), 2, 1)
+        report("wan_vae_decode_2f_480x832", ms, None, None, {"frames": 2})
+        del vae
+
     if not args.only or "norm" in args.only:
         for M in (256, 8192):
             x = torch.randn(M, H, device=dev, dtype=torch.bfloat16)

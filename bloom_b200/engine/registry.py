@@ -98,6 +98,9 @@ def default_registry() -> EngineRegistry:
     r.register(EngineCapability(
         name="qwen3-vl", maturity="Experimental", devices=["gpu"], families=["QwenVL"], formats=["Preset", "Safetensors"],
         native_dtypes=["BF16"], modalities=["Text", "Vision"]))
+    r.register(EngineCapability(
+        name="wan", maturity="Experimental", devices=["gpu"], families=["Wan"], formats=["Preset", "Safetensors"],
+        native_dtypes=["BF16"], modalities=["Text", "Video"]))
     # external runtimes (explicit --backend only: their availability depends on binaries outside this build)
     r.register(EngineCapability(
         name="llamacpp", maturity="Beta", devices=["cpu", "gpu"], families=["*"], formats=["Gguf"],

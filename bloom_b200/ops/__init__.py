@@ -619,10 +619,13 @@ def wide_decode_attention(q, kv_layer, num_kv_heads: int, block_table, seq_lens,
 
 
 def wide_prefill_attention(q, kv_layer, num_kv_heads: int, block_table, ctx_lens, cu_seqlens_q, tile_seq,
-                           tile_start, out, *, window: int = 0, scale: float = 1.0, softcap: float = 0.0):
-    """Chunked-prefill attention over the wide paged cache (tiles of `prefill_tiles`)."""
+                           tile_start, out, *, window: int = 0, scale: float = 1.0, softcap: float = 0.0,
+                           causal: bool = True):
+    """Chunked-prefill attention over the wide paged cache (tiles of
+    `prefill_tiles`; head_dim 256 / 384 / 512).  causal=False: every query
+    sees all ctx_lens keys of its sequence."""
     _C().wide_prefill_attention(q, out, kv_layer, num_kv_heads, block_table, ctx_lens, cu_seqlens_q, tile_seq,
-                                tile_start, window, scale, softcap, status(q.device.index))
+                                tile_start, window, scale, softcap, status(q.device.index), causal)
     _count()
     return out
 

@@ -3,6 +3,7 @@
 #include <torch/extension.h>
 
 #include "bloom/ops.h"
+#include "bloom/ops_media.h"
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 sm_100a kernels";
@@ -31,10 +32,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wide_decode_splits", &bloom::wide_decode_splits);
   m.def("wide_decode_workspace_numel", &bloom::wide_decode_workspace_numel);
   m.def("wide_decode_attention", &bloom::wide_decode_attention);
-  m.def("wide_prefill_attention", &bloom::wide_prefill_attention);
+  m.def("wide_prefill_attention", &bloom::wide_prefill_attention, py::arg("q"), py::arg("out"), py::arg("kv_layer"),
+        py::arg("nkv"), py::arg("block_table"), py::arg("ctx_lens"), py::arg("cu_q"), py::arg("tile_seq"),
+        py::arg("tile_start"), py::arg("window"), py::arg("scale"), py::arg("softcap"), py::arg("status"),
+        py::arg("causal") = true);
   m.def("gemma_qkv_write", &bloom::gemma_qkv_write);
   m.def("residual_norm", &bloom::residual_norm);
   m.def("softcap_", &bloom::softcap_);
+  m.def("wan_residual_norm", &bloom::wan_residual_norm);
+  m.def("wan_qkv_norm_rope", &bloom::wan_qkv_norm_rope);
+  m.def("wan_patchify", &bloom::wan_patchify);
+  m.def("wan_unpatchify_step", &bloom::wan_unpatchify_step);
+  m.def("silu_bf16", &bloom::silu_bf16);
+  m.def("vae_gn_stats", &bloom::vae_gn_stats);
+  m.def("vae_im2col3x3", &bloom::vae_im2col3x3);
+  m.def("vae_gn_apply", &bloom::vae_gn_apply);
+  m.def("vae_pack_attn", &bloom::vae_pack_attn);
+  m.def("vae_rgb", &bloom::vae_rgb);
+  m.def("t5_rel_attention", &bloom::t5_rel_attention);
   m.def("moe_route_plan", &bloom::moe_route_plan, "routing + plan in one single-CTA launch (decode-sized batches)");
   m.def("moe_gather", &bloom::moe_gather);
   m.def("moe_combine", &bloom::moe_combine, py::arg("ys"), py::arg("pos"), py::arg("topk_w"), py::arg("out"),

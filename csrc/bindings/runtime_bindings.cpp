@@ -42,6 +42,7 @@ void register_admission(py::module_& m); // csrc/runtime/admission.cpp
 void register_schema(py::module_& m);    // csrc/runtime/schema_matcher.cpp
 void register_model_store(py::module_& m);  // csrc/runtime/model_store.cpp
 void register_image(py::module_& m);        // csrc/runtime/model_store.cpp (PNG scanlines)
+void register_media_encode(py::module_& m); // csrc/runtime/media_encode.cpp (GIF / PNG output)
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "bloom_b200 host runtime: KV block manager, in-flight batching scheduler, CPU kernels";
@@ -301,5 +302,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_admission(m);
   register_schema(m);
   register_model_store(m);
+  register_media_encode(m);
   register_image(m);
 }

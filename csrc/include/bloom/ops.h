@@ -11,7 +11,7 @@ enum GemmEpilogue : int {
   kEpiF32 = 1,         // out f32 [M, N] (+bias)
   kEpiSwiGLU = 2,      // w rows interleaved (16 gate | 16 up) per 32 rows; out bf16 [M, N/2] = silu(g) * u
   kEpiPartialF32 = 3,  // split-K: out f32 [splits, M, N] partial sums
-  kEpiResidual = 4,    // out bf16 [M, N] = acc + resid
+  kEpiResidual = 4,    // out bf16 [M, N] = acc (+bias) + resid
   kEpiGelu = 5,        // out bf16 [M, N] = gelu_erf(acc + bias)
   kEpiGeluTanh = 6,    // out bf16 [M, N] = gelu_tanh(acc + bias) (runs the kEpiGelu kernels with Args::gelu_tanh)
   kEpiGeGLU = 7,       // as kEpiSwiGLU with gelu_tanh(g) * u (runs the kEpiSwiGLU kernels with Args::gelu_tanh)
@@ -199,7 +199,7 @@ void wide_prefill_attention(const torch::Tensor& q, torch::Tensor& out, const to
                             const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
                             const torch::Tensor& cu_q, const torch::Tensor& tile_seq,
                             const torch::Tensor& tile_start, int64_t window, double scale, double softcap,
-                            const torch::Tensor& status);
+                            const torch::Tensor& status, bool causal = true);
 void gemma_qkv_write(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& slots,
                      const torch::Tensor& cos_sin, torch::Tensor& q_out, torch::Tensor& kv_layer, int64_t nq,
                      int64_t nkv, int64_t rot, const torch::Tensor& q_w, const torch::Tensor& k_w, double eps,

@@ -224,7 +224,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int
     float bias[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) bias[k] = 0.f;
-    if constexpr (EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiGelu) {
+    if constexpr (EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiGelu || EPI == kEpiResidual) {
       if (a.bias != nullptr) {
 #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -257,6 +257,8 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Tile& tl, int
         } else if constexpr (EPI == kEpiPartialF32) {
           store8_f32(reinterpret_cast<float*>(a.out) + ((long)tl.sp * a.M + tok) * a.N + f, x, nf, a.vec);
         } else if constexpr (EPI == kEpiResidual) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) x[k] += bias[k];
           const __nv_bfloat16* rp = a.resid + (long)tok * a.ldr + f;
           if (a.vec && nf >= 8) {
             const uint4 rv = *reinterpret_cast<const uint4*>(rp);

@@ -91,6 +91,7 @@ struct WideArgs {
   const int* tile_seq;
   const int* tile_start;
   int prefill;
+  int causal;       // 0: every row sees keys [0, kv_len) (window ignored)
   int window;       // > 0: key j is visible to the query at position p iff p - window < j <= p
   float scale;      // score scale before soft-capping
   float softcap;    // > 0: s = softcap * tanh(s / softcap)
@@ -172,8 +173,8 @@ __global__ void __launch_bounds__(kThreads) wide_attention_kernel(const WideArgs
   // key range of the tile's rows (rows are in increasing position order)
   const int p_first = nrows > 0 ? row_pos(0) : 0;
   const int p_last = nrows > 0 ? row_pos(nrows - 1) : -1;
-  const int lo = a.window > 0 ? max(0, p_first - a.window + 1) : 0;
-  const int hi = min(p_last + 1, kv_len);
+  const int lo = (a.causal && a.window > 0) ? max(0, p_first - a.window + 1) : 0;
+  const int hi = a.causal ? min(p_last + 1, kv_len) : (nrows > 0 ? kv_len : 0);
   const int kt0 = lo / kKeys;
   const int kt_all = hi > lo ? (hi + kKeys - 1) / kKeys - kt0 : 0;
   const int per_split = (kt_all + a.splits - 1) / a.splits;
@@ -289,7 +290,8 @@ __global__ void __launch_bounds__(kThreads) wide_attention_kernel(const WideArgs
             } else {
               v *= sl2;
             }
-            const bool vis = j <= pos[hr] && (a.window <= 0 || j > pos[hr] - a.window);
+            const bool vis = a.causal ? (j <= pos[hr] && (a.window <= 0 || j > pos[hr] - a.window))
+                                      : (rvalid[hr] && j < kv_len);
             v = vis ? v : -INFINITY;
             x[nt][e] = v;
             mx = fmaxf(mx, v);
@@ -645,7 +647,7 @@ static WideArgs wide_common(const torch::Tensor& q, torch::Tensor& out, const to
   TORCH_CHECK(kv_layer.scalar_type() == at::kBFloat16 && kv_layer.dim() == 2 && kv_layer.stride(1) == 1,
               "wide attention: kv layer [NB, E] bf16");
   const int D = q.size(2);
-  TORCH_CHECK(D == 256 || D == 512, "wide attention: head_dim 256 or 512");
+  TORCH_CHECK(D == 256 || D == 384 || D == 512, "wide attention: head_dim 256, 384 or 512");
   TORCH_CHECK(q.size(1) % nkv == 0, "wide attention: q heads must be a multiple of KV heads");
   TORCH_CHECK(kv_layer.stride(0) >= 2 * nkv * gemma::PAGE * D && kv_layer.stride(0) % 8 == 0,
               "wide attention: block stride too small or not 16-byte aligned");
@@ -660,6 +662,7 @@ static WideArgs wide_common(const torch::Tensor& q, torch::Tensor& out, const to
   a.num_blocks = kv_layer.size(0);
   a.block_table = block_table.data_ptr<int>();
   a.bt_stride = block_table.stride(0);
+  a.causal = 1;
   a.window = int(window);
   a.scale = float(scale);
   a.softcap = float(softcap);
@@ -673,6 +676,8 @@ static void launch_wide_any(const WideArgs& a, int D, dim3 grid, bool combine) {
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (D == 256)
     gemma::launch_wide<256>(a, grid, combine, stream);
+  else if (D == 384)
+    gemma::launch_wide<384>(a, grid, combine, stream);
   else
     gemma::launch_wide<512>(a, grid, combine, stream);
 }
@@ -727,8 +732,9 @@ void wide_prefill_attention(const torch::Tensor& q, torch::Tensor& out, const to
                             const torch::Tensor& block_table, const torch::Tensor& ctx_lens,
                             const torch::Tensor& cu_q, const torch::Tensor& tile_seq,
                             const torch::Tensor& tile_start, int64_t window, double scale, double softcap,
-                            const torch::Tensor& status) {
+                            const torch::Tensor& status, bool causal) {
   WideArgs a = wide_common(q, out, kv_layer, nkv, block_table, window, scale, softcap, status);
+  a.causal = causal ? 1 : 0;
   const int D = q.size(2);
   TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && cu_q.scalar_type() == at::kInt &&
                   tile_seq.scalar_type() == at::kInt && tile_start.scalar_type() == at::kInt,

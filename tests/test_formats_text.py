@@ -210,6 +210,7 @@ def test_registry_routing():
     assert r.route("Llama", "Gguf", "Q8", "cpu") == ("cpu", NATIVE)
     assert r.route("Whisper", "Gguf", "Q8", "cpu")[1] == UNSUPPORTED
     assert r.route("Gemma", "Safetensors", "BF16", "gpu") == ("b200", NATIVE)
+    assert r.route("Wan", "Preset", "BF16", "gpu") == ("wan", NATIVE)
     assert any(e["name"] == "b200" and e["max_tp"] == 8 for e in r.describe())
 
 
