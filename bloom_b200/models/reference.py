@@ -145,8 +145,11 @@ def gemma4_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
         if not (cfg.attention_k_eq_v and not cfg.is_sliding(i)):
             w[p + "self_attn.v_proj.weight"] = rn(kvh * d, H)
         w[p + "self_attn.o_proj.weight"] = rn(H, nh * d)
-        w[p + "self_attn.q_norm.weight"] = near1(d)
-        w[p + "self_attn.k_norm.weight"] = near1(d)
+        # q / k norm weights near 1/2 each: with attention scale 1, q.k of unit-RMS heads would have a
+        # standard deviation of sqrt(head_dim) (16 to 23 here) and an almost one-hot softmax whose
+        # near-ties flip under bf16 rounding; at 1/4 of that the oracle comparison stays well posed
+        w[p + "self_attn.q_norm.weight"] = (near1(d).float() * 0.5).to(torch.bfloat16)
+        w[p + "self_attn.k_norm.weight"] = (near1(d).float() * 0.5).to(torch.bfloat16)
         for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
                   "post_feedforward_layernorm"):
             w[p + n + ".weight"] = near1(H)

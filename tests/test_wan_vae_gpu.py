@@ -27,8 +27,10 @@ def test_vae_decode_matches_oracle():
     assert rgb.dtype == torch.uint8 and rgb.shape == (2, 32, 48, 3)
     diff = (rgb.int() - frames_to_rgb(ref).int()).abs().float()
     assert diff.mean().item() < 2.0, diff.mean().item()
-    # chunked decoding (one frame at a time) gives the same frames
+    # chunked decoding (one frame at a time) gives the same frames up to accumulation order
+    # (GEMM tiling and the GroupNorm partial sums depend on the chunk size)
     vae.max_im2col_bytes = 1
     rgb1 = vae.decode(lat)
     torch.cuda.synchronize()
-    assert torch.equal(rgb1, rgb)
+    d1 = (rgb1.int() - rgb.int()).abs()
+    assert d1.max().item() <= 3 and d1.float().mean().item() < 0.05, (d1.max().item(), d1.float().mean().item())
