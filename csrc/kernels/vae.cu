@@ -31,33 +31,57 @@ constexpr int kMaxGroups = 32;
 int grid_for(long n) { return int(std::min<long>((n + kThreads - 1) / kThreads, 148L * 32)); }
 
 // Partial sums of x and x^2 per (frame, group) over a slice of the frame's
-// pixels: grid (frames, slices); partial [frames][slices][G][2].
+// pixels: grid (frames, slices); partial [frames][slices][G][2].  Each
+// active thread keeps one 8-channel chunk for the whole slice (the thread
+// count is a multiple of C / 8), so the per-channel sums are private
+// registers, and the groups are then summed in a fixed order: the result
+// does not depend on scheduling (no floating-point atomics).
 __global__ void __launch_bounds__(kThreads) gn_partial_kernel(const __nv_bfloat16* __restrict__ x, long P, int C,
                                                                int G, int slices, float* __restrict__ partial) {
-  __shared__ float acc[kMaxGroups][2];
-  for (int i = threadIdx.x; i < G * 2; i += kThreads) acc[i / 2][i % 2] = 0.f;
-  __syncthreads();
+  __shared__ float red[kThreads][8][2];
   const int n = blockIdx.x, sl = blockIdx.y;
   const int cpg = C / G, c8 = C / 8;
-  const long items = P * c8;
-  const long per = (items + slices - 1) / slices;
-  const long i0 = sl * per, i1 = min(items, i0 + per);
+  const int active = (kThreads / c8) * c8;  // c8 <= kThreads (C <= 2048)
+  const long pix_per = (P + slices - 1) / slices;
+  const long p0 = sl * pix_per, p1 = min(P, p0 + pix_per);
   const __nv_bfloat16* xf = x + (long)n * P * C;
-  for (long i = i0 + threadIdx.x; i < i1; i += kThreads) {
-    const int cc = int(i % c8);
-    const uint4 u = *reinterpret_cast<const uint4*>(xf + i * 8);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+  float s[8], q[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float v = __bfloat162float(b[k]);
-      const int g = (cc * 8 + k) / cpg;
-      atomicAdd(&acc[g][0], v);
-      atomicAdd(&acc[g][1], v * v);
+  for (int k = 0; k < 8; ++k) s[k] = q[k] = 0.f;
+  const int cc = threadIdx.x % c8;
+  if (threadIdx.x < active) {
+    for (long p = p0 + threadIdx.x / c8; p < p1; p += active / c8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xf + p * C + cc * 8);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float v = __bfloat162float(b[k]);
+        s[k] += v;
+        q[k] += v * v;
+      }
     }
   }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    red[threadIdx.x][k][0] = threadIdx.x < active ? s[k] : 0.f;
+    red[threadIdx.x][k][1] = threadIdx.x < active ? q[k] : 0.f;
+  }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * 2; i += kThreads)
-    partial[(((long)n * slices + sl) * G + i / 2) * 2 + i % 2] = acc[i / 2][i % 2];
+  for (int g = threadIdx.x; g < G; g += kThreads) {
+    float gs = 0.f, gq = 0.f;
+    for (int t = 0; t < active; ++t) {
+      const int c0 = (t % c8) * 8;
+      if (c0 + 8 <= g * cpg || c0 >= (g + 1) * cpg) continue;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if ((c0 + k) / cpg == g) {
+          gs += red[t][k][0];
+          gq += red[t][k][1];
+        }
+    }
+    partial[(((long)n * slices + sl) * G + g) * 2] = gs;
+    partial[(((long)n * slices + sl) * G + g) * 2 + 1] = gq;
+  }
 }
 
 // stats [frames][G][2] = (mean, rstd) from the partial sums (double precision)
@@ -212,11 +236,12 @@ void vae_gn_stats(const torch::Tensor& x, int64_t groups, double eps, torch::Ten
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 4, "vae_gn_stats: x NHWC bf16");
   const int N = x.size(0), C = x.size(3);
   const long P = (long)x.size(1) * x.size(2);
-  TORCH_CHECK(C % 8 == 0 && groups > 0 && groups <= vae::kMaxGroups && C % groups == 0, "vae_gn_stats: C, groups");
+  TORCH_CHECK(C % 8 == 0 && C <= 8 * vae::kThreads && groups > 0 && groups <= vae::kMaxGroups && C % groups == 0,
+              "vae_gn_stats: C % 8 == 0, C <= 2048, groups");
   TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.is_contiguous() && stats.numel() == (int64_t)N * groups * 2,
               "vae_gn_stats: stats f32 [N, G, 2]");
   if (N == 0) return;
-  const int slices = int(std::max<long>(1, std::min<long>(256, P * (C / 8) / (vae::kThreads * 16))));
+  const int slices = int(std::max<long>(1, std::min<long>(256, P * (C / 8) / (vae::kThreads * 32))));
   auto partial = torch::empty({(int64_t)N * slices * groups * 2}, x.options().dtype(at::kFloat));
   const at::cuda::CUDAGuard g(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
