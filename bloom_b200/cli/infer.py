@@ -117,6 +117,41 @@ def read_prompt(args) -> Optional[str]:
     return args.prompt
 
 
+def run_image_edit(args) -> int:
+    """LongCat draft image edit: --image input (PNG / PPM), --output PNG.
+    --model names 'transformer[:vae]' presets (random weights: no checkpoint
+    download here); the prompt embeddings are a deterministic function of the
+    prompt bytes until a text encoder checkpoint is loaded."""
+    import torch
+
+    from ..engine.processor import decode_image
+    from ..models.longcat import LongCatEditPipeline
+
+    if not args.image:
+        print("error: --backend longcat needs --image", file=sys.stderr)
+        return 2
+    parts = (args.model or "tiny-longcat").split(":")
+    tr = parts[0]
+    vae = parts[1] if len(parts) > 1 else ("tiny" if tr.startswith("tiny") else "flux")
+    pipe = LongCatEditPipeline.from_presets(tr, vae, seed=0)
+    with open(args.image, "rb") as f:
+        img = decode_image(f.read())
+    h, w = (img.shape[0] // 16) * 16, (img.shape[1] // 16) * 16
+    img_t = torch.from_numpy(img[:h, :w, :3].copy())
+    g = torch.Generator().manual_seed(sum((args.prompt or "").encode()) + 1)
+    emb = torch.randn(max(1, len((args.prompt or "").encode())), pipe.tr.cfg.joint_attention_dim, generator=g)
+    out = pipe.edit(img_t, emb).cpu()
+    files = []
+    if args.output:
+        from .._ext import runtime
+
+        with open(args.output, "wb") as f:
+            f.write(runtime().encode_png(out.contiguous().numpy().tobytes(), out.shape[0], out.shape[1]))
+        files = [args.output]
+    print(json.dumps({"width": int(out.shape[1]), "height": int(out.shape[0]), "files": files}))
+    return 0
+
+
 def run_video(args) -> int:
     """Text-to-video with the Wan 2.1 pipeline.  --model names a preset pair
     'dit[:vae[:t5]]' of random-weight shapes (no checkpoint download here)."""
@@ -172,6 +207,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     t0 = time.perf_counter()
     if args.backend == "wan":
         return run_video(args)
+    if args.backend == "longcat":
+        return run_image_edit(args)
     if args.image:
         return run_image(args, opts)
     if args.backend in ("llamacpp", "script"):

@@ -101,6 +101,9 @@ def default_registry() -> EngineRegistry:
     r.register(EngineCapability(
         name="wan", maturity="Experimental", devices=["gpu"], families=["Wan"], formats=["Preset", "Safetensors"],
         native_dtypes=["BF16"], modalities=["Text", "Video"]))
+    r.register(EngineCapability(
+        name="longcat", maturity="Experimental", devices=["gpu"], families=["LongCat"],
+        formats=["Preset", "Safetensors"], native_dtypes=["BF16"], modalities=["Text", "Vision"]))
     # external runtimes (explicit --backend only: their availability depends on binaries outside this build)
     r.register(EngineCapability(
         name="llamacpp", maturity="Beta", devices=["cpu", "gpu"], families=["*"], formats=["Gguf"],

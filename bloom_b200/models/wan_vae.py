@@ -154,28 +154,37 @@ class WanVAE:
         self.max_im2col_bytes = max_im2col_bytes
         self.p: Dict[str, torch.Tensor] = {}
 
+    prefixes = ("decoder.",)
+    attn_prefixes = ("decoder.mid_block.attentions.0.",)
+
     def load(self, full: Dict[str, torch.Tensor]) -> None:
+        """Conv weights [Co, Ci, kh, kw] become GEMM rows [Co, kh * kw * Ci]
+        (tap-major, matching vae_im2col3x3); outputs narrower than 16
+        channels are zero-padded to 16 rows (sliced off after the GEMM)."""
         dev = self.device
         p = {}
+        self.out_ch: Dict[str, int] = {}
         for k, v in full.items():
-            if not k.startswith("decoder."):
+            if not k.startswith(self.prefixes):
                 continue
             v = v.to(dev)
-            if k.endswith(".weight") and v.dim() == 4:  # conv [Co, Ci, kh, kw] -> [Co, kh * kw * Ci] (tap-major)
+            if k.endswith(".weight") and v.dim() == 4:
                 co = v.shape[0]
                 v = v.permute(0, 2, 3, 1).reshape(co, -1)
-                if k == "decoder.conv_out.weight":  # pad the 3 output rows to one full GEMM tile
-                    v = torch.cat([v, torch.zeros(128 - co, v.shape[1], device=dev, dtype=v.dtype)], 0)
+                if co < 16:
+                    self.out_ch[k[:-len(".weight")]] = co
+                    v = torch.cat([v, torch.zeros(16 - co, v.shape[1], device=dev, dtype=v.dtype)], 0)
                 p[k] = v.to(torch.bfloat16).contiguous()
-            elif k == "decoder.conv_out.bias":
-                p[k] = torch.cat([v, torch.zeros(128 - v.numel(), device=dev, dtype=v.dtype)]).to(torch.bfloat16)
-            elif ".norm" in k or "group_norm" in k:
+            elif k.endswith(".bias") and k[:-len(".bias")] + ".weight" in full and full[k[:-len(".bias")] + ".weight"].dim() == 4 \
+                    and v.numel() < 16:
+                p[k] = torch.cat([v, torch.zeros(16 - v.numel(), device=dev, dtype=v.dtype)]).to(torch.bfloat16)
+            elif "norm" in k.rsplit(".", 2)[-2] or "group_norm" in k:
                 p[k] = v.float().contiguous()
             else:
                 p[k] = v.to(torch.bfloat16).contiguous()
-        a = "decoder.mid_block.attentions.0."
-        p[a + "qkv.weight"] = torch.cat([p[a + n + ".weight"] for n in ("to_q", "to_k", "to_v")], 0).contiguous()
-        p[a + "qkv.bias"] = torch.cat([p[a + n + ".bias"] for n in ("to_q", "to_k", "to_v")], 0).contiguous()
+        for a in self.attn_prefixes:
+            p[a + "qkv.weight"] = torch.cat([p[a + n + ".weight"] for n in ("to_q", "to_k", "to_v")], 0).contiguous()
+            p[a + "qkv.bias"] = torch.cat([p[a + n + ".bias"] for n in ("to_q", "to_k", "to_v")], 0).contiguous()
         self.p = p
 
     def random_init(self, seed: int = 0) -> None:
@@ -189,16 +198,19 @@ class WanVAE:
         ops._count(2)
         return st
 
-    def _conv3(self, x, name, up=1, norm=None, resid=None):
-        """3x3 conv of NHWC x (optionally GN+SiLU first, nearest x`up`) -> NHWC bf16."""
+    def _conv3(self, x, name, up=1, norm=None, resid=None, stride=1, pads=(1, 1, 1, 1)):
+        """3x3 conv of NHWC x (optionally GN+SiLU first, nearest x`up`,
+        stride 2 with pads (top, bottom, left, right)) -> NHWC bf16."""
         N, H, W, C = x.shape
-        Ho, Wo = H * up, W * up
+        pt, pb, pl, pr = pads
+        Ho, Wo = (H * up + pt + pb - 3) // stride + 1, (W * up + pl + pr - 3) // stride + 1
         cols = torch.empty(N * Ho * Wo, 9 * C, dtype=torch.bfloat16, device=self.device)
         if norm is not None:
             st, pn = norm
-            _C().vae_im2col3x3(x, up, st, self.p[pn + "weight"], self.p[pn + "bias"], st.shape[1], True, cols)
+            _C().vae_im2col3x3(x, up, st, self.p[pn + "weight"], self.p[pn + "bias"], st.shape[1], True, cols,
+                               stride, pt, pb, pl, pr)
         else:
-            _C().vae_im2col3x3(x, up, None, None, None, 0, False, cols)
+            _C().vae_im2col3x3(x, up, None, None, None, 0, False, cols, stride, pt, pb, pl, pr)
         ops._count()
         w, b = self.p[name + ".weight"], self.p[name + ".bias"]
         if resid is not None:
@@ -216,8 +228,7 @@ class WanVAE:
             sc = x
         return self._conv3(h, p + "conv2", norm=(self._stats(h), p + "norm2."), resid=sc)
 
-    def _attn(self, x):
-        a = "decoder.mid_block.attentions.0."
+    def _attn(self, x, a="decoder.mid_block.attentions.0."):
         N, H, W, C = x.shape
         P = H * W
         st = self._stats(x)
@@ -256,6 +267,9 @@ class WanVAE:
             if up:
                 x = self._conv3(x, f"decoder.up_blocks.{level}.upsamplers.0.conv", up=2)
         out = self._conv3(x, "decoder.conv_out", norm=(self._stats(x), "decoder.norm_out."))
+        return self._to_rgb(out, rgb)
+
+    def _to_rgb(self, out: torch.Tensor, rgb: bool) -> torch.Tensor:
         N, H, W, _ = out.shape
         if not rgb:
             return out[..., :3]

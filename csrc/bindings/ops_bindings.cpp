@@ -40,12 +40,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("residual_norm", &bloom::residual_norm);
   m.def("softcap_", &bloom::softcap_);
   m.def("wan_residual_norm", &bloom::wan_residual_norm);
-  m.def("wan_qkv_norm_rope", &bloom::wan_qkv_norm_rope);
+  m.def("wan_qkv_norm_rope", &bloom::wan_qkv_norm_rope, py::arg("src"), py::arg("q_col"), py::arg("k_col"),
+        py::arg("v_col"), py::arg("heads"), py::arg("head_dim"), py::arg("q_w"), py::arg("k_w"), py::arg("eps"),
+        py::arg("rope_tab"), py::arg("rope_pt"), py::arg("rope_ph"), py::arg("grid_f"), py::arg("grid_h"),
+        py::arg("grid_w"), py::arg("rows_per_batch"), py::arg("q_out"), py::arg("kv"), py::arg("blocks_per_batch"),
+        py::arg("head_norm") = false, py::arg("pos3") = py::none(), py::arg("out_rows_per_batch") = 0,
+        py::arg("out_offset") = 0);
   m.def("wan_patchify", &bloom::wan_patchify);
   m.def("wan_unpatchify_step", &bloom::wan_unpatchify_step);
   m.def("silu_bf16", &bloom::silu_bf16);
   m.def("vae_gn_stats", &bloom::vae_gn_stats);
-  m.def("vae_im2col3x3", &bloom::vae_im2col3x3);
+  m.def("vae_im2col3x3", &bloom::vae_im2col3x3, py::arg("src"), py::arg("up"), py::arg("stats"), py::arg("gamma"),
+        py::arg("beta"), py::arg("groups"), py::arg("silu"), py::arg("dst"), py::arg("stride") = 1,
+        py::arg("pad_t") = 1, py::arg("pad_b") = 1, py::arg("pad_l") = 1, py::arg("pad_r") = 1);
   m.def("vae_gn_apply", &bloom::vae_gn_apply);
   m.def("vae_pack_attn", &bloom::vae_pack_attn);
   m.def("vae_rgb", &bloom::vae_rgb);

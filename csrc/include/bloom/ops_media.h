@@ -20,7 +20,9 @@ void wan_qkv_norm_rope(const torch::Tensor& src, int64_t q_col, int64_t k_col, i
                        const c10::optional<torch::Tensor>& rope_tab, int64_t rope_pt, int64_t rope_ph,
                        int64_t grid_f, int64_t grid_h, int64_t grid_w, int64_t rows_per_batch,
                        const c10::optional<torch::Tensor>& q_out, const c10::optional<torch::Tensor>& kv,
-                       int64_t blocks_per_batch);
+                       int64_t blocks_per_batch, bool head_norm = false,
+                       const c10::optional<torch::Tensor>& pos3 = c10::nullopt, int64_t out_rows_per_batch = 0,
+                       int64_t out_offset = 0);
 void wan_patchify(const torch::Tensor& latent, torch::Tensor& tokens);
 void wan_unpatchify_step(const torch::Tensor& head_out, int64_t preds, double guidance, double dt,
                          torch::Tensor& latent);
@@ -30,7 +32,8 @@ void silu_bf16(const torch::Tensor& x, torch::Tensor& out);
 void vae_gn_stats(const torch::Tensor& x, int64_t groups, double eps, torch::Tensor& stats);
 void vae_im2col3x3(const torch::Tensor& src, int64_t up, const c10::optional<torch::Tensor>& stats,
                    const c10::optional<torch::Tensor>& gamma, const c10::optional<torch::Tensor>& beta,
-                   int64_t groups, bool silu, torch::Tensor& dst);
+                   int64_t groups, bool silu, torch::Tensor& dst, int64_t stride = 1, int64_t pad_t = 1,
+                   int64_t pad_b = 1, int64_t pad_l = 1, int64_t pad_r = 1);
 void vae_gn_apply(const torch::Tensor& src, const torch::Tensor& stats, const torch::Tensor& gamma,
                   const torch::Tensor& beta, int64_t groups, bool silu, torch::Tensor& dst);
 void vae_pack_attn(const torch::Tensor& qkv, int64_t frames, int64_t channels, torch::Tensor& q, torch::Tensor& kv);

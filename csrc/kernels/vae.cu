@@ -126,11 +126,13 @@ __device__ __forceinline__ void norm8(float (&v)[8], const NormArgs& nm, int n, 
 }
 
 // dst [frames * Ho * Wo, 9 * C]: row (n, y, x), column (ky * 3 + kx) * C + c =
-// act(src[n, (y + ky - 1) / up, (x + kx - 1) / up, c]) with zero padding.
+// act(src[n, yy / up, xx / up, c]) with yy = y * stride + ky - pad_t (and
+// likewise xx) in the x`up` nearest-upsampled source, zero outside it.
 __global__ void __launch_bounds__(kThreads) im2col3x3_kernel(const __nv_bfloat16* __restrict__ src, int frames,
-                                                              int Hs, int Ws, int C, int up, const NormArgs nm,
+                                                              int Hs, int Ws, int C, int up, int stride, int pad_t,
+                                                              int pad_l, int Ho, int Wo, const NormArgs nm,
                                                               __nv_bfloat16* __restrict__ dst) {
-  const int Ho = Hs * up, Wo = Ws * up, c8 = C / 8;
+  const int Hu = Hs * up, Wu = Ws * up, c8 = C / 8;
   const long total = (long)frames * Ho * Wo * 9 * c8;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int cc = int(i % c8);
@@ -138,9 +140,9 @@ __global__ void __launch_bounds__(kThreads) im2col3x3_kernel(const __nv_bfloat16
     const int tap = int(r % 9);
     const long pix = r / 9;
     const int x = int(pix % Wo), y = int((pix / Wo) % Ho), n = int(pix / ((long)Wo * Ho));
-    const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
+    const int yy = y * stride + tap / 3 - pad_t, xx = x * stride + tap % 3 - pad_l;
     uint4 out = make_uint4(0, 0, 0, 0);
-    if (yy >= 0 && yy < Ho && xx >= 0 && xx < Wo) {
+    if (yy >= 0 && yy < Hu && xx >= 0 && xx < Wu) {
       const int sy = yy / up, sx = xx / up;
       const uint4 u = *reinterpret_cast<const uint4*>(src + (((long)n * Hs + sy) * Ws + sx) * C + cc * 8);
       if (nm.stats != nullptr || nm.silu) {
@@ -255,13 +257,16 @@ void vae_gn_stats(const torch::Tensor& x, int64_t groups, double eps, torch::Ten
 
 void vae_im2col3x3(const torch::Tensor& src, int64_t up, const c10::optional<torch::Tensor>& stats,
                    const c10::optional<torch::Tensor>& gamma, const c10::optional<torch::Tensor>& beta,
-                   int64_t groups, bool silu, torch::Tensor& dst) {
+                   int64_t groups, bool silu, torch::Tensor& dst, int64_t stride, int64_t pad_t, int64_t pad_b,
+                   int64_t pad_l, int64_t pad_r) {
   TORCH_CHECK(src.scalar_type() == at::kBFloat16 && src.is_contiguous() && src.dim() == 4,
               "vae_im2col3x3: src NHWC bf16");
   const int N = src.size(0), Hs = src.size(1), Ws = src.size(2), C = src.size(3);
-  TORCH_CHECK(C % 8 == 0 && (up == 1 || up == 2), "vae_im2col3x3: C % 8 == 0, up 1 or 2");
-  TORCH_CHECK(dst.scalar_type() == at::kBFloat16 && dst.is_contiguous() &&
-                  dst.numel() == (int64_t)N * Hs * up * Ws * up * 9 * C,
+  TORCH_CHECK(C % 8 == 0 && (up == 1 || up == 2) && (stride == 1 || stride == 2), "vae_im2col3x3: C % 8, up, stride");
+  TORCH_CHECK(pad_t >= 0 && pad_b >= 0 && pad_l >= 0 && pad_r >= 0 && pad_t <= 2 && pad_l <= 2, "vae_im2col3x3: pads");
+  const int Ho = int((Hs * up + pad_t + pad_b - 3) / stride + 1), Wo = int((Ws * up + pad_l + pad_r - 3) / stride + 1);
+  TORCH_CHECK(Ho > 0 && Wo > 0, "vae_im2col3x3: empty output");
+  TORCH_CHECK(dst.scalar_type() == at::kBFloat16 && dst.is_contiguous() && dst.numel() == (int64_t)N * Ho * Wo * 9 * C,
               "vae_im2col3x3: dst bf16 [N * Ho * Wo, 9 * C]");
   const vae::NormArgs nm = vae::norm_args(stats, gamma, beta, groups, silu, C);
   if (stats.has_value()) TORCH_CHECK(stats->numel() == (int64_t)N * groups * 2, "vae_im2col3x3: stats [N, G, 2]");
@@ -269,8 +274,8 @@ void vae_im2col3x3(const torch::Tensor& src, int64_t up, const c10::optional<tor
   if (total == 0) return;
   const at::cuda::CUDAGuard g(src.device());
   vae::im2col3x3_kernel<<<vae::grid_for(total), vae::kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), N, Hs, Ws, C, int(up), nm,
-      reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()));
+      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), N, Hs, Ws, C, int(up), int(stride), int(pad_t),
+      int(pad_l), Ho, Wo, nm, reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -139,59 +139,96 @@ struct QkvArgs {
   const float* qw;
   const float* kw;
   float eps;
-  const float2* rope;  // [1024][hd / 2] (cos, sin) of each pair's own axis frequency, or null
+  int head_norm;       // 1: RMSNorm over each head (weights [hd]); 0: over the whole model dim (weights [D])
+  const float2* rope;  // [positions][hd / 2] (cos, sin) of each pair's own axis frequency, or null
+  int rope_rows;       // positions in the table (larger positions are clamped)
   int pt, ph;          // pairs [0, pt) rotate with the frame index, [pt, pt + ph) the row, the rest the column
-  int gf, gh, gw;
-  int S;               // tokens per sample
-  __nv_bfloat16* q_out;  // [T, nh, hd]
+  int gf, gh, gw;      // token grid (positions from the token index) when pos3 is null
+  const int* pos3;     // [S_out][3] (frame, row, column) of each output token, or null
+  int S;               // src rows per sample
+  int S_out, off;      // output tokens per sample; these rows land at [off, off + S)
+  __nv_bfloat16* q_out;  // [B * S_out, nh, hd]
   __nv_bfloat16* kv;     // pages [NB][2][nh][16][hd]
   int bpb;               // pages per sample
 };
 
-// One CTA per token: RMSNorm of q and k over the whole model dim (weights
-// [D]), 3-D RoPE on (even, odd) pairs, q -> q_out, k / v -> pages.
+// One CTA per src row: RMSNorm of q and k (over the model dim or per head),
+// RoPE on (even, odd) pairs, q -> q_out, k / v -> pages.  Sums are formed
+// in a fixed order (no atomics), so results do not depend on scheduling.
 __global__ void __launch_bounds__(kThreads) qkv_norm_rope_kernel(const QkvArgs a) {
   __shared__ float red[kThreads / 32];
+  extern __shared__ float sq[];  // head_norm: [D / 2] pair squares, then [nh] head sums
   const long row = blockIdx.x;
   const int b = int(row / a.S), n = int(row - (long)b * a.S);
-  const int hw = a.gh * a.gw;
-  const int pf = n / hw, ph_ = (n / a.gw) % a.gh, pw = n % a.gw;
+  const int no = a.off + n;
+  const long orow = (long)b * a.S_out + no;
+  int pf, ph_, pw;
+  if (a.pos3 != nullptr) {
+    pf = a.pos3[no * 3];
+    ph_ = a.pos3[no * 3 + 1];
+    pw = a.pos3[no * 3 + 2];
+  } else {
+    const int hw = a.gh * a.gw;
+    pf = n / hw;
+    ph_ = (n / a.gw) % a.gh;
+    pw = n % a.gw;
+  }
   const int half = a.hd / 2;
   const int np = a.D / 2;
   const __nv_bfloat16* s = a.src + row * a.ld;
-  const int blk = b * a.bpb + n / 16, slot = n % 16;
+  const int blk = b * a.bpb + no / 16, slot = no % 16;
 
   auto rot = [&](int P, float& x0, float& x1) {
     if (a.rope == nullptr) return;
     const int p = P % half;
-    const int pos = p < a.pt ? pf : (p < a.pt + a.ph ? ph_ : pw);
+    const int pos = min(max(p < a.pt ? pf : (p < a.pt + a.ph ? ph_ : pw), 0), a.rope_rows - 1);
     const float2 cs = a.rope[(long)pos * half + p];
     const float r0 = x0 * cs.x - x1 * cs.y;
     const float r1 = x0 * cs.y + x1 * cs.x;
     x0 = r0;
     x1 = r1;
   };
+  float* hsum = sq + np;
   for (int part = 0; part < 2; ++part) {  // 0: q, 1: k
     const int col = part == 0 ? a.q_col : a.k_col;
     if (col < 0) continue;
     const float* w = part == 0 ? a.qw : a.kw;
-    float ss = 0.f;
-    for (int P = threadIdx.x; P < np; P += kThreads) {
-      const __nv_bfloat162 t = *reinterpret_cast<const __nv_bfloat162*>(s + col + 2 * P);
-      const float x0 = __bfloat162float(t.x), x1 = __bfloat162float(t.y);
-      ss += x0 * x0 + x1 * x1;
+    float inv_all = 1.f;
+    if (w != nullptr && !a.head_norm) {
+      float ss = 0.f;
+      for (int P = threadIdx.x; P < np; P += kThreads) {
+        const __nv_bfloat162 t = *reinterpret_cast<const __nv_bfloat162*>(s + col + 2 * P);
+        const float x0 = __bfloat162float(t.x), x1 = __bfloat162float(t.y);
+        ss += x0 * x0 + x1 * x1;
+      }
+      inv_all = rsqrtf(block_sum(ss, red) / a.D + a.eps);
+    } else if (w != nullptr) {
+      __syncthreads();  // sq / hsum reuse across parts
+      for (int P = threadIdx.x; P < np; P += kThreads) {
+        const __nv_bfloat162 t = *reinterpret_cast<const __nv_bfloat162*>(s + col + 2 * P);
+        const float x0 = __bfloat162float(t.x), x1 = __bfloat162float(t.y);
+        sq[P] = x0 * x0 + x1 * x1;
+      }
+      __syncthreads();
+      for (int h = threadIdx.x; h < a.nh; h += kThreads) {
+        float acc = 0.f;
+        for (int i = 0; i < half; ++i) acc += sq[h * half + i];
+        hsum[h] = rsqrtf(acc / a.hd + a.eps);
+      }
+      __syncthreads();
     }
-    const float inv = w != nullptr ? rsqrtf(block_sum(ss, red) / a.D + a.eps) : 1.f;
     for (int P = threadIdx.x; P < np; P += kThreads) {
       const __nv_bfloat162 t = *reinterpret_cast<const __nv_bfloat162*>(s + col + 2 * P);
-      float x0 = __bfloat162float(t.x) * inv, x1 = __bfloat162float(t.y) * inv;
+      const int h = (2 * P) / a.hd, d = 2 * P - h * a.hd;
+      float x0 = __bfloat162float(t.x), x1 = __bfloat162float(t.y);
       if (w != nullptr) {
-        x0 *= w[2 * P];
-        x1 *= w[2 * P + 1];
+        const float inv = a.head_norm ? hsum[h] : inv_all;
+        const int wi = a.head_norm ? d : 2 * P;
+        x0 *= inv * w[wi];
+        x1 *= inv * w[wi + 1];
       }
       rot(P, x0, x1);
-      const int h = (2 * P) / a.hd, d = 2 * P - h * a.hd;
-      __nv_bfloat16* dst = part == 0 ? a.q_out + (row * a.nh + h) * a.hd + d
+      __nv_bfloat16* dst = part == 0 ? a.q_out + (orow * a.nh + h) * a.hd + d
                                      : a.kv + (((long)blk * 2 + 0) * a.nh + h) * 16 * a.hd + slot * a.hd + d;
       *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(x0, x1);
     }
@@ -311,26 +348,44 @@ void wan_qkv_norm_rope(const torch::Tensor& src, int64_t q_col, int64_t k_col, i
                        const c10::optional<torch::Tensor>& rope_tab, int64_t rope_pt, int64_t rope_ph,
                        int64_t grid_f, int64_t grid_h, int64_t grid_w, int64_t rows_per_batch,
                        const c10::optional<torch::Tensor>& q_out, const c10::optional<torch::Tensor>& kv,
-                       int64_t blocks_per_batch) {
+                       int64_t blocks_per_batch, bool head_norm, const c10::optional<torch::Tensor>& pos3,
+                       int64_t out_rows_per_batch, int64_t out_offset) {
   TORCH_CHECK(src.scalar_type() == at::kBFloat16 && src.dim() == 2 && src.stride(1) == 1 && src.stride(0) % 2 == 0,
               "wan_qkv_norm_rope: src bf16 [T, cols]");
   const int T = src.size(0);
   const int D = int(heads * head_dim);
   TORCH_CHECK(head_dim % 2 == 0 && D % 2 == 0, "wan_qkv_norm_rope: even head dim");
+  const int64_t S_out = out_rows_per_batch > 0 ? out_rows_per_batch : rows_per_batch;
+  TORCH_CHECK(out_offset >= 0 && out_offset + rows_per_batch <= S_out, "wan_qkv_norm_rope: output placement");
+  TORCH_CHECK(rows_per_batch > 0 && T % rows_per_batch == 0, "wan_qkv_norm_rope: rows per batch");
+  const int64_t B = T / rows_per_batch;
   for (int64_t c : {q_col, k_col, v_col})
     TORCH_CHECK(c < 0 || (c % 2 == 0 && c + D <= src.size(1)), "wan_qkv_norm_rope: column range");
-  TORCH_CHECK(q_col < 0 || (q_out.has_value() && q_out->is_contiguous() && q_out->numel() == (int64_t)T * D),
-              "wan_qkv_norm_rope: q_out [T, heads, head_dim]");
+  TORCH_CHECK(q_col < 0 || (q_out.has_value() && q_out->is_contiguous() && q_out->numel() >= B * S_out * D),
+              "wan_qkv_norm_rope: q_out [B * S_out, heads, head_dim]");
   TORCH_CHECK((k_col < 0 && v_col < 0) || (kv.has_value() && kv->is_contiguous()), "wan_qkv_norm_rope: kv pages");
   if (kv.has_value()) {
-    const int64_t nblk = (int64_t)((T / rows_per_batch) - 1) * blocks_per_batch + (rows_per_batch + 15) / 16;
+    const int64_t nblk = (B - 1) * blocks_per_batch + (S_out + 15) / 16;
     TORCH_CHECK(kv->numel() >= nblk * 2 * D * 16, "wan_qkv_norm_rope: kv pages too small");
   }
+  if (head_norm) {
+    if (q_w.has_value()) TORCH_CHECK(q_w->numel() == head_dim, "wan_qkv_norm_rope: per-head q weights [head_dim]");
+    if (k_w.has_value()) TORCH_CHECK(k_w->numel() == head_dim, "wan_qkv_norm_rope: per-head k weights [head_dim]");
+  } else {
+    if (q_w.has_value()) TORCH_CHECK(q_w->numel() == D, "wan_qkv_norm_rope: q weights [D]");
+    if (k_w.has_value()) TORCH_CHECK(k_w->numel() == D, "wan_qkv_norm_rope: k weights [D]");
+  }
+  if (pos3.has_value()) {
+    TORCH_CHECK(pos3->scalar_type() == at::kInt && pos3->is_contiguous() && pos3->numel() == S_out * 3,
+                "wan_qkv_norm_rope: pos3 int32 [S_out, 3]");
+  } else {
+    TORCH_CHECK(grid_f * grid_h * grid_w == rows_per_batch, "wan_qkv_norm_rope: grid");
+  }
+  const int64_t maxpos = pos3.has_value() ? 1 : std::max({grid_f, grid_h, grid_w});
   if (rope_tab.has_value())
     TORCH_CHECK(rope_tab->scalar_type() == at::kFloat && rope_tab->is_contiguous() &&
-                    rope_tab->numel() >= std::max({grid_f, grid_h, grid_w}) * head_dim,
+                    rope_tab->numel() >= maxpos * head_dim && rope_tab->numel() % head_dim == 0,
                 "wan_qkv_norm_rope: rope table [positions, head_dim / 2, 2] f32");
-  TORCH_CHECK(grid_f * grid_h * grid_w == rows_per_batch && T % rows_per_batch == 0, "wan_qkv_norm_rope: grid");
   if (T == 0) return;
   wan::QkvArgs a{};
   a.src = reinterpret_cast<const __nv_bfloat16*>(src.data_ptr());
@@ -344,18 +399,25 @@ void wan_qkv_norm_rope(const torch::Tensor& src, int64_t q_col, int64_t k_col, i
   a.qw = fptr(q_w, "q norm");
   a.kw = fptr(k_w, "k norm");
   a.eps = float(eps);
+  a.head_norm = head_norm ? 1 : 0;
   a.rope = rope_tab.has_value() ? reinterpret_cast<const float2*>(rope_tab->data_ptr<float>()) : nullptr;
+  a.rope_rows = rope_tab.has_value() ? int(rope_tab->numel() / head_dim) : 0;
   a.pt = int(rope_pt);
   a.ph = int(rope_ph);
   a.gf = int(grid_f);
   a.gh = int(grid_h);
   a.gw = int(grid_w);
+  a.pos3 = pos3.has_value() ? pos3->data_ptr<int>() : nullptr;
   a.S = int(rows_per_batch);
+  a.S_out = int(S_out);
+  a.off = int(out_offset);
   a.q_out = q_out.has_value() ? reinterpret_cast<__nv_bfloat16*>(q_out->data_ptr()) : nullptr;
   a.kv = kv.has_value() ? reinterpret_cast<__nv_bfloat16*>(kv->data_ptr()) : nullptr;
   a.bpb = int(blocks_per_batch);
+  const size_t smem = head_norm ? (size_t(D / 2) + size_t(heads)) * sizeof(float) : 0;
+  TORCH_CHECK(smem <= 48 * 1024, "wan_qkv_norm_rope: model dim too large for per-head norms");
   const at::cuda::CUDAGuard g(src.device());
-  wan::qkv_norm_rope_kernel<<<T, wan::kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  wan::qkv_norm_rope_kernel<<<T, wan::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
