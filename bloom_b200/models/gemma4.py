@@ -165,8 +165,10 @@ class Gemma4LM:
             self._ws = torch.empty(need, dtype=torch.float32, device=self.device)
         return self._ws
 
-    def forward(self, s: StepInputs, kv_cache: torch.Tensor) -> torch.Tensor:
-        """Final-normed hidden states of the logits rows [NL, H] (bf16)."""
+    def forward(self, s: StepInputs, kv_cache: torch.Tensor, trace=None) -> torch.Tensor:
+        """Final-normed hidden states of the logits rows [NL, H] (bf16).
+        trace: an optional list that receives the residual stream after every
+        sub-layer (debugging against the oracle)."""
         cfg = self.cfg
         T = s.input_ids.shape[0]
         Bd, ql = s.num_decode, s.decode_q_len
@@ -199,10 +201,14 @@ class Gemma4LM:
                                            scale=1.0, softcap=cap)
             o = ops.gemm(attn.view(T, self.nq * d), lay["o"])
             y = ops.residual_norm(o, x, lay["ln_post_attn"], lay["ln_pre_ff"], eps=eps)
+            if trace is not None:
+                trace.append(x.float().clone())
             act = ops.gemm(y, lay["gate_up"], epi=ops.EPI_GEGLU)
             m = ops.gemm(act, lay["down"])
             nxt = self.layers[li + 1]["ln_in"] if li + 1 < len(self.layers) else self.final_norm
             y = ops.residual_norm(m, x, lay["ln_post_ff"], nxt, out_scale=lay["scalar"], eps=eps)
+            if trace is not None:
+                trace.append(x.float().clone())
         return y.index_select(0, s.logits_rows)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:

@@ -164,7 +164,7 @@ def _gelu_tanh(x):
     return 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
 
 
-def gemma4_forward_logits(cfg: ModelConfig, w: Dict[str, torch.Tensor], tokens) -> torch.Tensor:
+def gemma4_forward_logits(cfg: ModelConfig, w: Dict[str, torch.Tensor], tokens, trace=None) -> torch.Tensor:
     """fp32 Gemma4 text forward over one sequence (executor/gemma4.rs semantics:
     scaled embedding, q/k/v norms, partial RoPE on global layers, attention
     scale 1, soft-capped scores, sliding-window masks of `sliding_window` keys,
@@ -219,11 +219,15 @@ def gemma4_forward_logits(cfg: ModelConfig, w: Dict[str, torch.Tensor], tokens) 
         a = torch.einsum("hqk,khd->qhd", sc.softmax(-1), vv).reshape(T, nh * d)
         a = a @ w[p + "self_attn.o_proj.weight"].float().t()
         x = x + rms(a, w[p + "post_attention_layernorm.weight"])
+        if trace is not None:
+            trace.append(x.clone())
         h = rms(x, w[p + "pre_feedforward_layernorm.weight"])
         gt = h @ w[p + "mlp.gate_proj.weight"].float().t()
         up = h @ w[p + "mlp.up_proj.weight"].float().t()
         m = (_gelu_tanh(gt) * up) @ w[p + "mlp.down_proj.weight"].float().t()
         x = (x + rms(m, w[p + "post_feedforward_layernorm.weight"])) * w[p + "layer_scalar"].float()
+        if trace is not None:
+            trace.append(x.clone())
     logits = rms(x, w[P + "norm.weight"]) @ emb.float().t()
     if cfg.final_logit_softcapping:
         logits = cfg.final_logit_softcapping * torch.tanh(logits / cfg.final_logit_softcapping)

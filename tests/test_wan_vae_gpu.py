@@ -33,4 +33,5 @@ def test_vae_decode_matches_oracle():
     rgb1 = vae.decode(lat)
     torch.cuda.synchronize()
     d1 = (rgb1.int() - rgb.int()).abs()
-    assert d1.max().item() <= 3 and d1.float().mean().item() < 0.05, (d1.max().item(), d1.float().mean().item())
+    # (one level of rounding at most; the GEMMs pick split-K by the chunk's row count)
+    assert d1.max().item() <= 2 and d1.float().mean().item() < 0.25, (d1.max().item(), d1.float().mean().item())
