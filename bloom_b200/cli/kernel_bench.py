@@ -407,6 +407,32 @@ def main():
                 "model.layers.0.mlp.experts.down_proj": torch.randn(E, Hm, Im, device=dev, dtype=torch.bfloat16) * 0.02}
         blk = MoEBlock(sh, full)
         del full
+        # routing alone: one single-CTA route+plan launch against route (warp per token) + plan
+        from bloom_b200._ext import cuda as _cuda
+
+        Cx = _cuda()
+        K8, El8 = cfg.num_experts_per_tok, E // 8
+        for Tm in (128, 512):
+            lg = torch.randn(Tm, E, device=dev)
+            ids = torch.empty(Tm, K8, dtype=torch.int32, device=dev)
+            wts = torch.empty(Tm, K8, device=dev)
+            slot = torch.empty(Tm, K8, dtype=torch.int32, device=dev)
+            offs = torch.empty(El8 + 1, dtype=torch.int32, device=dev)
+            mt = ((Tm * K8 + 15) // 16 + El8) * 12
+            tg = torch.empty(mt, 4, dtype=torch.int32, device=dev)
+            td = torch.empty_like(tg)
+            ng = torch.zeros(1, dtype=torch.int32, device=dev)
+            nd = torch.zeros_like(ng)
+            cnt = torch.zeros(El8, dtype=torch.int32, device=dev)
+            ms1 = timeit(lambda i=0: Cx.moe_route_plan(lg, K8, True, 0, El8, ids, wts, slot, offs, 16, 12, 16, tg, ng, td,
+                                                        nd))
+
+            def two(i=0):
+                Cx.moe_route(lg, K8, True, 0, El8, ids, wts, slot, cnt)
+                Cx.moe_plan(cnt, offs, 16, 12, 16, tg, ng, td, nd)
+
+            ms2 = timeit(two)
+            report("moe_route_plan", ms1, None, None, {"tokens": Tm, "two_kernel_ms": round(ms2, 4)})
         for Tm in (128, 4096):
             x = torch.randn(Tm, Hm, device=dev, dtype=torch.bfloat16)
             out = torch.empty_like(x)

@@ -100,20 +100,25 @@ struct WideArgs {
   int* status;
 };
 
-template <int D>
+template <int D, int ROWS, int STAGES>
 struct Smem {
   static constexpr int kQS = D + 8;    // padded row stride (elements): ldmatrix rows hit distinct banks
   static constexpr int kVS = kDC + 8;
-  static constexpr int kQBytes = kRows * kQS * 2;
+  static constexpr int kQBytes = ROWS * kQS * 2;
   static constexpr int kKBytes = kKeys * kQS * 2;
   static constexpr int kVBytes = kKeys * kVS * 2;
   static constexpr int kStage = kKBytes + kVBytes;
-  static constexpr int kTotal = kQBytes + 2 * kStage;
+  static constexpr int kTotal = kQBytes + STAGES * kStage;
 };
 
-template <int D>
+// ROWS query rows per CTA (64 = 4 computing warps; 16 = decode rows of one
+// KV head, one computing warp while all four load), STAGES-deep cp.async
+// ring of K / V tiles (one barrier per tile: a stage is refilled right after
+// the barrier that follows its last use).
+template <int D, int ROWS, int STAGES>
 __global__ void __launch_bounds__(kThreads) wide_attention_kernel(const WideArgs a) {
-  using S = Smem<D>;
+  using S = Smem<D, ROWS, STAGES>;
+  constexpr int kRows = ROWS;
   constexpr int NDC = D / kDC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
@@ -228,8 +233,11 @@ __global__ void __launch_bounds__(kThreads) wide_attention_kernel(const WideArgs
       }
     }
   };
-  if (n_kt > 0) load_tile(ka, 0);
-  cp_async_commit();
+#pragma unroll
+  for (int st = 0; st < STAGES - 1; ++st) {
+    if (st < n_kt) load_tile(ka + st, st);
+    cp_async_commit();  // the Q tile rides in the first group
+  }
 
   // per-thread rows g and g + 8 of this warp's 16
   int pos[2];
@@ -248,11 +256,11 @@ __global__ void __launch_bounds__(kThreads) wide_attention_kernel(const WideArgs
   const bool warp_live = warp * 16 < nrows;
 
   for (int i = 0; i < n_kt; ++i) {
-    const int stage = i & 1;
-    if (i + 1 < n_kt) load_tile(ka + i + 1, stage ^ 1);
+    const int stage = i % STAGES;
+    cp_async_wait<STAGES - 2>();  // tile i (and Q) landed
+    __syncthreads();              // ... for every thread; stage (i - 1) % STAGES is free again
+    if (i + STAGES - 1 < n_kt) load_tile(ka + i + STAGES - 1, (i + STAGES - 1) % STAGES);
     cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
     if (warp_live) {
       const uint32_t sK = sStage + stage * S::kStage;
       const uint32_t sV = sK + S::kKBytes;
@@ -332,7 +340,6 @@ __global__ void __launch_bounds__(kThreads) wide_attention_kernel(const WideArgs
           mma16816(o[2 * j + 1], pa[kk], b2, b3);
         }
     }
-    __syncthreads();  // the next iteration's load overwrites this stage
   }
   cp_async_wait<0>();
 
@@ -370,8 +377,9 @@ __global__ void __launch_bounds__(kThreads) wide_attention_kernel(const WideArgs
 }
 
 // Merge the decode key-range splits: one CTA per (sequence, row tile / slice).
-template <int D>
+template <int D, int ROWS>
 __global__ void wide_combine_kernel(const WideArgs a) {
+  constexpr int kRows = ROWS;
   constexpr int NDC = D / kDC;
   constexpr int RS = kDC + 2;
   const int G = a.nq / a.nkv;
@@ -617,21 +625,25 @@ __global__ void softcap_kernel(__nv_bfloat16* __restrict__ v, long n8, float cap
   }
 }
 
-template <int D>
+template <int D, int ROWS, int STAGES>
 void launch_wide(const WideArgs& a, dim3 grid, bool combine, cudaStream_t stream) {
-  const int smem = Smem<D>::kTotal;
+  const int smem = Smem<D, ROWS, STAGES>::kTotal;
   static bool attr = false;  // first call per instantiation (host-serial launch path)
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(wide_attention_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(wide_attention_kernel<D, ROWS, STAGES>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  wide_attention_kernel<D><<<grid, kThreads, smem, stream>>>(a);
+  wide_attention_kernel<D, ROWS, STAGES><<<grid, kThreads, smem, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (combine) {
-    wide_combine_kernel<D><<<dim3(grid.x, grid.y), 256, 0, stream>>>(a);
+    wide_combine_kernel<D, ROWS><<<dim3(grid.x, grid.y), 256, 0, stream>>>(a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
+
+// query rows per CTA: decode rows of one KV head that fit 16 rows take the one-warp tile
+inline int decode_rows(int64_t q_len, int64_t G) { return q_len * G <= 16 ? 16 : kRows; }
 
 }  // namespace gemma
 
@@ -672,20 +684,30 @@ static WideArgs wide_common(const torch::Tensor& q, torch::Tensor& out, const to
   return a;
 }
 
-static void launch_wide_any(const WideArgs& a, int D, dim3 grid, bool combine) {
+static void launch_wide_any(const WideArgs& a, int D, int rows, dim3 grid, bool combine) {
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (D == 256)
-    gemma::launch_wide<256>(a, grid, combine, stream);
-  else if (D == 384)
-    gemma::launch_wide<384>(a, grid, combine, stream);
-  else
-    gemma::launch_wide<512>(a, grid, combine, stream);
+  if (rows == 16) {
+    if (D == 256)
+      gemma::launch_wide<256, 16, 4>(a, grid, combine, stream);
+    else if (D == 384)
+      gemma::launch_wide<384, 16, 4>(a, grid, combine, stream);
+    else
+      gemma::launch_wide<512, 16, 4>(a, grid, combine, stream);
+  } else {
+    if (D == 256)
+      gemma::launch_wide<256, 64, 3>(a, grid, combine, stream);
+    else if (D == 384)
+      gemma::launch_wide<384, 64, 2>(a, grid, combine, stream);
+    else
+      gemma::launch_wide<512, 64, 2>(a, grid, combine, stream);
+  }
 }
 
 int64_t wide_decode_splits(int64_t batch, int64_t nq, int64_t nkv, int64_t head_dim, int64_t q_len,
                            int64_t max_kv_len, int64_t window, int64_t num_sms) {
   const int64_t G = nq / nkv;
-  const int64_t ctas = batch * nkv * ((q_len * G + gemma::kRows - 1) / gemma::kRows) * (head_dim / gemma::kDC);
+  const int rows = gemma::decode_rows(q_len, G);
+  const int64_t ctas = batch * nkv * ((q_len * G + rows - 1) / rows) * (head_dim / gemma::kDC);
   int64_t keys = window > 0 ? std::min<int64_t>(window + q_len, max_kv_len) : max_kv_len;
   const int64_t tiles = std::max<int64_t>(1, (keys + gemma::kKeys - 1) / gemma::kKeys + 1);
   int64_t s = (2 * num_sms + ctas - 1) / std::max<int64_t>(ctas, 1);
@@ -696,8 +718,9 @@ int64_t wide_decode_splits(int64_t batch, int64_t nq, int64_t nkv, int64_t head_
 int64_t wide_decode_workspace_numel(int64_t batch, int64_t nq, int64_t nkv, int64_t head_dim, int64_t q_len,
                                     int64_t splits) {
   const int64_t G = nq / nkv;
-  const int64_t gy = nkv * ((q_len * G + gemma::kRows - 1) / gemma::kRows) * (head_dim / gemma::kDC);
-  return splits > 1 ? batch * gy * splits * gemma::kRows * (gemma::kDC + 2) : 1;
+  const int rows = gemma::decode_rows(q_len, G);
+  const int64_t gy = nkv * ((q_len * G + rows - 1) / rows) * (head_dim / gemma::kDC);
+  return splits > 1 ? batch * gy * splits * rows * (gemma::kDC + 2) : 1;
 }
 
 void wide_decode_attention(const torch::Tensor& q, torch::Tensor& out, const torch::Tensor& kv_layer, int64_t nkv,
@@ -717,7 +740,8 @@ void wide_decode_attention(const torch::Tensor& q, torch::Tensor& out, const tor
   a.prefill = 0;
   a.splits = int(splits);
   const int G = a.nq / a.nkv;
-  const int gy = a.nkv * ((a.ql * G + gemma::kRows - 1) / gemma::kRows) * (D / gemma::kDC);
+  const int rows = gemma::decode_rows(a.ql, G);
+  const int gy = a.nkv * ((a.ql * G + rows - 1) / rows) * (D / gemma::kDC);
   if (splits > 1) {
     TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
                     workspace->numel() >= wide_decode_workspace_numel(B, a.nq, a.nkv, D, q_len, splits),
@@ -725,7 +749,7 @@ void wide_decode_attention(const torch::Tensor& q, torch::Tensor& out, const tor
     a.part = workspace->data_ptr<float>();
   }
   const at::cuda::CUDAGuard g(q.device());
-  launch_wide_any(a, D, dim3(B, gy, int(splits)), splits > 1);
+  launch_wide_any(a, D, rows, dim3(B, gy, int(splits)), splits > 1);
 }
 
 void wide_prefill_attention(const torch::Tensor& q, torch::Tensor& out, const torch::Tensor& kv_layer, int64_t nkv,
@@ -748,7 +772,7 @@ void wide_prefill_attention(const torch::Tensor& q, torch::Tensor& out, const to
   a.prefill = 1;
   const at::cuda::CUDAGuard g(q.device());
   // 128-row scheduler tiles run as two 64-row halves (an empty half exits at once)
-  launch_wide_any(a, D, dim3(NT, a.nq * (D / gemma::kDC), 2), false);
+  launch_wide_any(a, D, gemma::kRows, dim3(NT, a.nq * (D / gemma::kDC), 2), false);
 }
 
 void gemma_qkv_write(const torch::Tensor& qkv, const torch::Tensor& positions, const torch::Tensor& slots,
