@@ -407,7 +407,7 @@ def main():
                 "model.layers.0.mlp.experts.down_proj": torch.randn(E, Hm, Im, device=dev, dtype=torch.bfloat16) * 0.02}
         blk = MoEBlock(sh, full)
         del full
-        # routing alone: one single-CTA route+plan launch against route (warp per token) + plan
+        # routing alone: route (warp per token, register top-k) + plan
         from bloom_b200._ext import cuda as _cuda
 
         Cx = _cuda()
@@ -424,15 +424,12 @@ def main():
             ng = torch.zeros(1, dtype=torch.int32, device=dev)
             nd = torch.zeros_like(ng)
             cnt = torch.zeros(El8, dtype=torch.int32, device=dev)
-            ms1 = timeit(lambda i=0: Cx.moe_route_plan(lg, K8, True, 0, El8, ids, wts, slot, offs, 16, 12, 16, tg, ng, td,
-                                                        nd))
 
-            def two(i=0):
+            def route_plan(i=0):
                 Cx.moe_route(lg, K8, True, 0, El8, ids, wts, slot, cnt)
                 Cx.moe_plan(cnt, offs, 16, 12, 16, tg, ng, td, nd)
 
-            ms2 = timeit(two)
-            report("moe_route_plan", ms1, None, None, {"tokens": Tm, "two_kernel_ms": round(ms2, 4)})
+            report("moe_route_plan", timeit(route_plan), None, None, {"tokens": Tm})
         for Tm in (128, 4096):
             x = torch.randn(Tm, Hm, device=dev, dtype=torch.bfloat16)
             out = torch.empty_like(x)

@@ -34,9 +34,10 @@ def kv_block_bytes(model: DecoderLM, block_size: int = 16, kv_dtype: str = "bf16
     cfg = model.cfg
     if hasattr(model, "kv_block_bytes"):  # models that lay out their own KV slots (wide heads)
         return model.kv_block_bytes()
+    L = getattr(model, "num_kv_layers", cfg.num_layers)  # a pipeline stage holds its own layers
     if kv_dtype == "int8":
-        return cfg.num_layers * ops.kv_q8_block_bytes(model.nkv, cfg.head_dim)
-    return cfg.num_layers * 2 * model.nkv * block_size * cfg.head_dim * 2
+        return L * ops.kv_q8_block_bytes(model.nkv, cfg.head_dim)
+    return L * 2 * model.nkv * block_size * cfg.head_dim * 2
 
 
 class ModelRunner:
@@ -73,11 +74,12 @@ class ModelRunner:
                 raise ValueError(f"{cfg.arch} keeps a bf16 KV cache")
             self.kv_cache = torch.zeros(model.kv_cache_shape(num_blocks), dtype=torch.bfloat16, device=self.device)
         elif kv_dtype == "int8":
-            self.kv_cache = torch.zeros(cfg.num_layers, num_blocks, ops.kv_q8_block_bytes(model.nkv, cfg.head_dim),
-                                        dtype=torch.uint8, device=self.device)
+            self.kv_cache = torch.zeros(getattr(model, "num_kv_layers", cfg.num_layers), num_blocks,
+                                        ops.kv_q8_block_bytes(model.nkv, cfg.head_dim), dtype=torch.uint8,
+                                        device=self.device)
         else:
-            self.kv_cache = torch.zeros(cfg.num_layers, num_blocks, 2, model.nkv, self.block_size, cfg.head_dim,
-                                        dtype=torch.bfloat16, device=self.device)
+            self.kv_cache = torch.zeros(getattr(model, "num_kv_layers", cfg.num_layers), num_blocks, 2, model.nkv,
+                                        self.block_size, cfg.head_dim, dtype=torch.bfloat16, device=self.device)
         rt = _rt()
         worst = rt.arena_layout(self.max_tokens, max_num_seqs, max_num_seqs,
                                 self.max_tokens // 64 + max_num_seqs, self.max_tokens + max_num_seqs,
@@ -91,7 +93,9 @@ class ModelRunner:
         if max_num_seqs not in self.buckets:
             self.buckets.append(max_num_seqs)
         # streamed (host-placed) layers order copies across two streams: eager steps only
-        self.use_cuda_graphs = use_cuda_graphs and not getattr(model, "offloaded", False)
+        # (pipeline stages exchange activations with NCCL point-to-point calls: eager steps)
+        self.pp = getattr(model, "pp", None)
+        self.use_cuda_graphs = use_cuda_graphs and not getattr(model, "offloaded", False) and self.pp is None
         # decode attention split-K workspace, sized for the largest need over buckets
         ws = 1
         self.decode_splits: Dict[int, int] = {}
@@ -207,8 +211,21 @@ class ModelRunner:
                 draft)
 
     # ------------------------------------------------------------ sampling
-    def _sample(self, logits: torch.Tensor, m, greedy: bool) -> torch.Tensor:
+    def _sample(self, logits: Optional[torch.Tensor], m, greedy: bool) -> torch.Tensor:
         """int32 [NL + 1]: sampled tokens, then the (rank-combined) status word."""
+        if self.pp is not None:
+            # the last stage samples; every stage gets its tokens and the worst status of all stages
+            NL = m.num_logits
+            out = torch.empty(NL + 1, dtype=torch.int32, device=self.device)
+            st = ops.status(self.device.index)[:1].clone()
+            self.pp.max_status(st)
+            if self.pp.last:
+                if greedy:
+                    ops.argmax(logits, out=out[:NL])
+                else:
+                    ops.sample(logits, *self.sampling_views(m), out=out[:NL])
+                out[NL:].copy_(st)
+            return self.pp.broadcast_from_last(out)
         tp = self.model.tp
         if tp.size == 1:
             NL = logits.shape[0]
@@ -222,9 +239,9 @@ class ModelRunner:
         return tp.comm.sample_vocab_parallel(logits, greedy, self.sampling_views(m) if not greedy else None,
                                              self.model.vocab_local)
 
-    def _forward_logits(self, s: StepInputs) -> torch.Tensor:
+    def _forward_logits(self, s: StepInputs) -> Optional[torch.Tensor]:
         h = self.model.forward(s, self.kv_cache)
-        return self.model.logits(h)
+        return None if h is None else self.model.logits(h)  # None: a pipeline stage before the last
 
     # ------------------------------------------------------------ graphs
     def capture_graphs(self, buckets: Optional[List[int]] = None) -> None:
@@ -290,7 +307,7 @@ class ModelRunner:
         else:
             logits = self._forward_logits(self.views(m))
             self.stats["eager_steps"] += 1
-        if self.check_finite and m.num_logits:
+        if self.check_finite and m.num_logits and logits is not None:
             bad = (~torch.isfinite(logits[:m.num_real_logits].float())).any(dim=1)
             if bool(bad.any()):
                 rows = bad.nonzero().flatten().tolist()
@@ -303,7 +320,7 @@ class ModelRunner:
         """Optional constrained-decoding masks (rows int32 [R], mask int32
         [R, words] on the device), sampling, and the one device-to-host read
         of the tokens and the status word."""
-        if token_mask is not None:
+        if token_mask is not None and logits is not None:
             rows, mask = token_mask
             ops.apply_token_mask(logits, rows, mask, self.model.tp.rank * self.model.vocab_local)
         toks = self._sample(logits, m, m.all_greedy)

@@ -89,9 +89,18 @@ def _local_heads(cfg: ModelConfig, tp: int, rank: int):
 class DecoderLM:
     """Weights + forward of a decoder LM shard on one GPU."""
 
-    def __init__(self, cfg: ModelConfig, tp: Optional[TPInfo] = None, device=None):
+    def __init__(self, cfg: ModelConfig, tp: Optional[TPInfo] = None, device=None, pp=None):
         self.cfg = cfg
         self.tp = tp or TPInfo()
+        # pipeline stage (parallel.pipeline.PPInfo): this process holds layers [l0, l1)
+        self.pp = pp if (pp is not None and pp.stages > 1) else None
+        self.l0, self.l1 = 0, cfg.num_layers
+        if self.pp is not None:
+            from ..parallel.pipeline import layer_range
+
+            if self.tp.size != 1 or cfg.is_moe:
+                raise ValueError("pipeline stages run dense models at TP=1")
+            self.l0, self.l1 = layer_range(cfg.num_layers, self.pp.stage, self.pp.stages)
         dev = torch.device(device) if device is not None else torch.device("cuda")
         if dev.type == "cuda" and dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
@@ -132,7 +141,7 @@ class DecoderLM:
         V = cfg.vocab_size
         self.lm_head = lm[r * V // t:(r + 1) * V // t].to(dev, bf).contiguous()
         self.layers = []
-        for i in range(cfg.num_layers):
+        for i in range(self.l0, self.l1):
             p = f"model.layers.{i}."
             q = get(p + "self_attn.q_proj.weight")[self.q0 * hd:(self.q0 + self.nq) * hd]
             k = get(p + "self_attn.k_proj.weight")[self.kv0 * hd:(self.kv0 + self.nkv) * hd]
@@ -305,7 +314,8 @@ class DecoderLM:
                 lay[p + "mlp.gate_proj.weight"] = randn(cfg.intermediate_size, H)
                 lay[p + "mlp.up_proj.weight"] = randn(cfg.intermediate_size, H)
                 lay[p + "mlp.down_proj.weight"] = randn(H, cfg.intermediate_size)
-            self._install_layer(i, lay)
+            if self.l0 <= i < self.l1:  # every stage draws all layers: the same model at any stage count
+                self._install_layer(i, lay, slot=i - self.l0)
             if cfg.is_moe:
                 self.moe.add_layer(i, lay)
             del lay
@@ -320,6 +330,8 @@ class DecoderLM:
         Dense decoders only."""
         if self.cfg.is_moe:
             raise NotImplementedError("random_init_flat covers dense decoders; use random_init for MoE")
+        if self.pp is not None:
+            raise NotImplementedError("pipeline stages load with random_init or shard_full")
         cfg, dev, bf = self.cfg, self.device, torch.bfloat16
         H, hd = cfg.hidden_size, cfg.head_dim
         qkv_rows = (self.nq + 2 * self.nkv) * hd
@@ -377,7 +389,8 @@ class DecoderLM:
             self.layers.append(lay)
         self._finish()
 
-    def _install_layer(self, i: int, lay: Dict[str, torch.Tensor]) -> None:
+    def _install_layer(self, i: int, lay: Dict[str, torch.Tensor], slot: Optional[int] = None) -> None:
+        """Install global layer i (weight names) at position `slot` (default i) of self.layers."""
         cfg, hd, bf = self.cfg, self.cfg.head_dim, torch.bfloat16
         r = self.tp.rank
         p = f"model.layers.{i}."
@@ -405,10 +418,11 @@ class DecoderLM:
             u = lay[p + "mlp.up_proj.weight"][r * I:(r + 1) * I].to(self.device, bf)
             layer["gate_up"] = ops.interleave_gate_up(g, u)
             layer["down"] = lay[p + "mlp.down_proj.weight"][:, r * I:(r + 1) * I].to(self.device, bf).contiguous()
-        if len(self.layers) <= i:
+        slot = i if slot is None else slot
+        if len(self.layers) <= slot:
             self.layers.append(layer)
         else:
-            self.layers[i] = layer
+            self.layers[slot] = layer
 
     # ------------------------------------------------------------ layer placement
     def place_layers(self, gpu_layers: int) -> None:
@@ -475,6 +489,11 @@ class DecoderLM:
         self.cos_sin = ops.rope_cos_sin(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, self.device,
                                         cfg.rope_scaling)
 
+    @property
+    def num_kv_layers(self) -> int:
+        """Layers whose KV pages this process holds (a pipeline stage holds its own)."""
+        return self.l1 - self.l0
+
     def gemm_shapes(self):
         """(N, K, swiglu) of every distinct projection, for the GEMM autotuner."""
         cfg = self.cfg
@@ -530,7 +549,10 @@ class DecoderLM:
         H = cfg.hidden_size
         eps = cfg.rms_norm_eps
         dev = self.device
-        residual = ops.embedding(s.input_ids, self.embed)
+        if self.pp is not None and not self.pp.first:  # the previous stage's residual stream
+            residual = self.pp.recv_prev(torch.empty(T, H, dtype=torch.bfloat16, device=dev))
+        else:
+            residual = ops.embedding(s.input_ids, self.embed)
         x = ops.rmsnorm(residual, self.layers[0]["ln1"], eps)
         qkv_dim = (self.nq + 2 * self.nkv) * cfg.head_dim
         wait = None  # a deferred all-gather the next GEMM must wait for
@@ -554,7 +576,8 @@ class DecoderLM:
             moe_router = self.moe.layers[li].get("router") if self.moe is not None else None
             x, wait = self._row_parallel_norm(a2, lay["o"], residual, lay["ln2"], eps,
                                               next_w=lay.get("gate_up") if self.moe is None else moe_router)
-            nxt = self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else self.final_norm
+            nxt = (self.layers[li + 1]["ln1"] if li + 1 < len(self.layers) else
+                   self.final_norm if self.pp is None or self.pp.last else lay["ln1"])  # the next stage renormalises
             if self.moe is not None:
                 fused = self.tp.comm.fused if (self.tp.size > 1 and self.tp.comm is not None) else None
                 if fused is not None:
@@ -578,6 +601,9 @@ class DecoderLM:
                 nq_w = self.layers[li + 1].get("qkv") if (li + 1 < L and not self.offloaded) else None
                 x, wait = self._row_parallel_norm(act, lay["down"], residual, nxt, eps, next_w=nq_w)
             self._release(li)
+        if self.pp is not None and not self.pp.last:
+            self.pp.send_next(residual)
+            return None
         return x.index_select(0, s.logits_rows)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:

@@ -21,10 +21,6 @@ import torch
 from .. import ops
 from .._ext import cuda as _C
 
-# token counts up to which routing and the tile plan run as one single-CTA
-# launch (32 warps x 16 tokens); larger batches use one warp per token
-_ROUTE_PLAN_MAX_T = 512
-
 
 class MoEBlock:
     def __init__(self, model, full: Optional[Dict[str, torch.Tensor]] = None):
@@ -96,12 +92,8 @@ class MoEBlock:
         max_tiles = ((T * K + bn - 1) // bn + self.El) * max(ft_gu, ft_d)
         tiles_gu = torch.empty(max_tiles, 4, dtype=torch.int32, device=self.dev)
         tiles_d = torch.empty(max_tiles, 4, dtype=torch.int32, device=self.dev)
-        if T <= _ROUTE_PLAN_MAX_T:  # decode-sized: routing and planning in one launch
-            C.moe_route_plan(logits, K, self.cfg.norm_topk_prob, self.e0, self.El, topk_ids, topk_w, slot,
-                             self.offsets, bn, ft_gu, ft_d, tiles_gu, self.n_gu, tiles_d, self.n_d)
-        else:
-            C.moe_route(logits, K, self.cfg.norm_topk_prob, self.e0, self.El, topk_ids, topk_w, slot, self.counts)
-            C.moe_plan(self.counts, self.offsets, bn, ft_gu, ft_d, tiles_gu, self.n_gu, tiles_d, self.n_d)
+        C.moe_route(logits, K, self.cfg.norm_topk_prob, self.e0, self.El, topk_ids, topk_w, slot, self.counts)
+        C.moe_plan(self.counts, self.offsets, bn, ft_gu, ft_d, tiles_gu, self.n_gu, tiles_d, self.n_d)
         R = T * K
         xs = torch.empty(R, self.H, dtype=torch.bfloat16, device=self.dev)
         pos = torch.empty(T, K, dtype=torch.int32, device=self.dev)

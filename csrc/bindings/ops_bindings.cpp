@@ -57,7 +57,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("vae_pack_attn", &bloom::vae_pack_attn);
   m.def("vae_rgb", &bloom::vae_rgb);
   m.def("t5_rel_attention", &bloom::t5_rel_attention);
-  m.def("moe_route_plan", &bloom::moe_route_plan, "routing + plan in one single-CTA launch (decode-sized batches)");
   m.def("moe_gather", &bloom::moe_gather);
   m.def("moe_combine", &bloom::moe_combine, py::arg("ys"), py::arg("pos"), py::arg("topk_w"), py::arg("out"),
         py::arg("push_ptrs") = std::vector<int64_t>{}, py::arg("push_rank") = 0, py::arg("push_rows") = 0);

@@ -41,10 +41,6 @@ void gemm_grouped_out(const torch::Tensor& x, const torch::Tensor& w, torch::Ten
 // Mixture of experts.
 void moe_route(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0, int64_t e_local,
                torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& counts);
-void moe_route_plan(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0, int64_t e_local,
-                    torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& offsets,
-                    int64_t bn, int64_t ft_gu, int64_t ft_d, torch::Tensor& tiles_gu, torch::Tensor& n_gu,
-                    torch::Tensor& tiles_d, torch::Tensor& n_d);
 void moe_plan(torch::Tensor& counts, torch::Tensor& offsets, int64_t bn, int64_t ft_gu, int64_t ft_d,
               torch::Tensor& tiles_gu, torch::Tensor& n_gu, torch::Tensor& tiles_d, torch::Tensor& n_d);
 void moe_gather(const torch::Tensor& x, int64_t e0, int64_t e_local, const torch::Tensor& topk_ids,

@@ -4,8 +4,6 @@
 //   moe_route    per token: softmax over the router logits, top-k, optional
 //                renormalisation; tokens routed to this rank's experts
 //                [e0, e0 + E_local) take a slot in their expert (atomic count)
-//   moe_route_plan  decode-sized batches (T <= 512): both of the above in
-//                one single-CTA launch, expert counts in shared memory
 //   moe_plan     one CTA: exclusive scan of the expert counts into row
 //                offsets, then the tile lists of the two grouped GEMMs
 //                (gate_up with SwiGLU, down) -- built on the device, so the
@@ -108,66 +106,6 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E,
     int s = -1;
     if (id >= e0 && id < e0 + El) s = atomicAdd(counts + (id - e0), 1);
     slot[(long)warp * K + lane] = s;
-  }
-}
-
-// Decode-sized batches: routing and planning in one launch of one CTA (1,024
-// threads, 32 warps striding over the tokens, local expert counts in shared
-// memory), so the plan needs no second launch and no global counters.
-__global__ void __launch_bounds__(1024) moe_route_plan_kernel(
-    const float* __restrict__ logits, int T, int E, int K, int norm, int e0, int El, int* __restrict__ topk_ids,
-    float* __restrict__ topk_w, int* __restrict__ slot, int* __restrict__ offsets, int bn, int ft_gu, int ft_d,
-    int4* __restrict__ tiles_gu, int* __restrict__ n_gu, int4* __restrict__ tiles_d, int* __restrict__ n_d,
-    int max_tiles) {
-  __shared__ int cnt_s[1024];
-  __shared__ int off_s[1025];
-  __shared__ int cnt_gu, cnt_d;
-  for (int e = threadIdx.x; e < El; e += blockDim.x) cnt_s[e] = 0;
-  if (threadIdx.x == 0) {
-    cnt_gu = 0;
-    cnt_d = 0;
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < T; t += 32) {
-    int id;
-    float p;
-    route_token_warp<8>(logits + (long)t * E, E, K, norm, lane, id, p);
-    if (lane < K) {
-      topk_ids[(long)t * K + lane] = id;
-      topk_w[(long)t * K + lane] = p;
-      slot[(long)t * K + lane] = (id >= e0 && id < e0 + El) ? atomicAdd(&cnt_s[id - e0], 1) : -1;
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int e = 0; e < El; ++e) {
-      off_s[e] = acc;
-      acc += cnt_s[e];
-    }
-    off_s[El] = acc;
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e <= El; e += blockDim.x) offsets[e] = off_s[e];
-  for (int e = threadIdx.x; e < El; e += blockDim.x) {
-    const int c = off_s[e + 1] - off_s[e];
-    for (int tt = 0; tt < (c + bn - 1) / bn; ++tt) {
-      const int r0 = off_s[e] + tt * bn, r1 = off_s[e + 1];
-      for (int f = 0; f < ft_gu; ++f) {
-        const int i = atomicAdd(&cnt_gu, 1);
-        if (i < max_tiles) tiles_gu[i] = make_int4(e, f, r0, r1);
-      }
-      for (int f = 0; f < ft_d; ++f) {
-        const int i = atomicAdd(&cnt_d, 1);
-        if (i < max_tiles) tiles_d[i] = make_int4(e, f, r0, r1);
-      }
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    *n_gu = min(cnt_gu, max_tiles);
-    *n_d = min(cnt_d, max_tiles);
   }
 }
 
@@ -312,25 +250,6 @@ void moe_route(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0
   moe_route_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       logits.data_ptr<float>(), T, E, int(top_k), norm ? 1 : 0, int(e0), int(e_local), topk_ids.data_ptr<int>(),
       topk_w.data_ptr<float>(), slot.data_ptr<int>(), counts.data_ptr<int>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-void moe_route_plan(const torch::Tensor& logits, int64_t top_k, bool norm, int64_t e0, int64_t e_local,
-                    torch::Tensor& topk_ids, torch::Tensor& topk_w, torch::Tensor& slot, torch::Tensor& offsets,
-                    int64_t bn, int64_t ft_gu, int64_t ft_d, torch::Tensor& tiles_gu, torch::Tensor& n_gu,
-                    torch::Tensor& tiles_d, torch::Tensor& n_d) {
-  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "moe_route_plan: f32 logits");
-  TORCH_CHECK(top_k >= 1 && top_k <= kMaxTopK, "moe_route_plan: top_k in [1, 16]");
-  TORCH_CHECK(logits.size(1) <= 256 && logits.size(1) >= top_k, "moe_route_plan: top_k <= experts <= 256");
-  TORCH_CHECK(e_local <= 1024, "moe_route_plan: at most 1024 local experts");
-  TORCH_CHECK(tiles_gu.size(0) == tiles_d.size(0) && tiles_gu.size(1) == 4, "moe_route_plan: tiles [n, 4] int32");
-  const int T = logits.size(0), E = logits.size(1);
-  const at::cuda::CUDAGuard g(logits.device());
-  moe_route_plan_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
-      logits.data_ptr<float>(), T, E, int(top_k), norm ? 1 : 0, int(e0), int(e_local), topk_ids.data_ptr<int>(),
-      topk_w.data_ptr<float>(), slot.data_ptr<int>(), offsets.data_ptr<int>(), int(bn), int(ft_gu), int(ft_d),
-      reinterpret_cast<int4*>(tiles_gu.data_ptr<int>()), n_gu.data_ptr<int>(),
-      reinterpret_cast<int4*>(tiles_d.data_ptr<int>()), n_d.data_ptr<int>(), int(tiles_gu.size(0)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

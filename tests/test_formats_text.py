@@ -311,3 +311,13 @@ def test_inspect_gguf_cli(tiny_gguf, capsys):
     assert d["tensor_count"] > 3 and d["primary_dtype"] == "Q8_0"
     assert main([p]) == 0 and "GGUF v3" in capsys.readouterr().out
     assert main([p + ".missing"]) == 1
+
+
+def test_pipeline_layer_ranges():
+    from bloom_b200.parallel.pipeline import layer_range
+
+    assert [layer_range(32, s, 2) for s in range(2)] == [(0, 16), (16, 32)]
+    assert [layer_range(10, s, 4) for s in range(4)] == [(0, 3), (3, 6), (6, 8), (8, 10)]
+    assert layer_range(80, 7, 8) == (70, 80)
+    with pytest.raises(ValueError):
+        layer_range(2, 0, 3)
