@@ -90,6 +90,7 @@ class InferencePipeline:
              use_cuda_graphs: bool = True, template: Optional[str] = None, strict: Optional[bool] = None,
              speculative: str = "none", draft_model: Optional[str] = None, num_speculative_tokens: int = 5,
              ngram_order: int = 4, max_num_seqs: int = 64, tp_info=None, gpu_layers: Optional[int] = None,
+             pp_info=None,
              max_num_batched_tokens: Optional[int] = None, threads: Optional[int] = None) -> "InferencePipeline":
         """`gpu_layers`: layers kept in HBM (the rest stream from pinned host
         memory; default all, or BLOOM_GPU_LAYERS); `max_num_batched_tokens`:
@@ -112,7 +113,7 @@ class InferencePipeline:
             try:
                 return InferencePipeline._load_once(model, dev, ctx, tp, use_cuda_graphs, template, speculative,
                                                     draft_model, num_speculative_tokens, ngram_order, max_num_seqs,
-                                                    tp_info, gpu_layers, max_num_batched_tokens)
+                                                    tp_info, gpu_layers, max_num_batched_tokens, pp_info)
             except Exception as e:  # degradation ladder on OOM only
                 if not _is_oom(e) or strict:
                     raise
@@ -130,7 +131,7 @@ class InferencePipeline:
 
     @staticmethod
     def _load_once(model, device, ctx, tp, use_cuda_graphs, template, speculative, draft_model, nspec, ngram_order,
-                   max_num_seqs, tp_info, gpu_layers=None, max_num_batched_tokens=None):
+                   max_num_seqs, tp_info, gpu_layers=None, max_num_batched_tokens=None, pp_info=None):
         from ..formats.loader import load_tokenizer, load_weights, model_config
         from ..formats.manifest import load_manifest, verify_hashes
 
@@ -189,12 +190,12 @@ class InferencePipeline:
         if man is None:
             from ..models import build_decoder
 
-            dm = build_decoder(cfg, tp_info, None)
+            dm = build_decoder(cfg, tp_info, None, pp=pp_info)
             dm.random_init(0)
         else:
             from ..formats.loader import load_decoder
 
-            dm = load_decoder(model, tp_info, None)
+            dm = load_decoder(model, tp_info, None, pp=pp_info)
         if gpu_layers is not None and gpu_layers < cfg.num_layers:
             dm.place_layers(gpu_layers)
         spec_len = nspec if speculative in ("ngram", "draft") else 0

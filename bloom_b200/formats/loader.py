@@ -54,19 +54,19 @@ def load_weights(man: ModelManifest, device=None) -> dict:
     return out
 
 
-def load_decoder(path: str, tp=None, device=None):
+def load_decoder(path: str, tp=None, device=None, pp=None):
     from ..utils.tracing import span
 
     with span("model.load", path=str(path)):
-        return _load_decoder(path, tp, device)
+        return _load_decoder(path, tp, device, pp)
 
 
-def _load_decoder(path: str, tp=None, device=None):
+def _load_decoder(path: str, tp=None, device=None, pp=None):
     from ..models import build_decoder
 
     man = load_manifest(path)
     cfg = model_config(man)
-    model = build_decoder(cfg, tp, device)
+    model = build_decoder(cfg, tp, device, pp=pp)
     gg = [f for f in man.files if f.format == "Gguf"]
     if gg and (tp is None or tp.size == 1) and man.primary_dtype in ("Q8", "Q4") and hasattr(model, "load_gguf"):
         # Q8_0 / Q4_0 projections stay block-quantised on the GPU (qgemv / dequant + tcgen05)

@@ -39,6 +39,8 @@ def build_parser():
     ap.add_argument("--doctor-format", choices=["text", "json"], default="text")
     ap.add_argument("--models-dir", default=os.environ.get("BLOOM_MODELS_DIR"),
                     help="catalog for /v1/model-management (list, preflight, switch, unload, remove)")
+    ap.add_argument("--pipeline", action="store_true",
+                    help="under torchrun: the ranks are pipeline stages (layer ranges) instead of tensor-parallel shards")
     ap.add_argument("--comm", choices=["fused", "nccl"], default="fused",
                     help="tensor-parallel collectives (torchrun launches): fused NVLink kernels or NCCL")
     ap.add_argument("--enable-ifb", action="store_true", default=True,
@@ -73,7 +75,7 @@ def main(argv=None) -> int:
     from .app import ServerSettings, create_app
     from .runtime import ServingRuntime, TPControl, follower_loop
 
-    tp_info, ctrl = None, None
+    tp_info, pp_info, ctrl = None, None, None
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:  # launched by torchrun: tensor parallel over the ranks
         from ..models.llama import TPInfo
         from ..models.config import PRESETS, preset
@@ -83,15 +85,20 @@ def main(argv=None) -> int:
 
         rank, world, local = init_distributed("nccl")
         dev = torch.device("cuda", local)
-        hidden = preset(args.model).hidden_size if args.model in PRESETS else 8192
-        comm = Communicator(rank, world, dev, dist.group.WORLD, mode=args.comm,
-                            max_tokens=max(args.context_size, 8192), hidden=hidden)
-        tp_info = TPInfo(rank=rank, size=world, group=dist.group.WORLD, comm=comm)
+        if args.pipeline:
+            from ..parallel.pipeline import pipeline_from_world
+
+            pp_info = pipeline_from_world()
+        else:
+            hidden = preset(args.model).hidden_size if args.model in PRESETS else 8192
+            comm = Communicator(rank, world, dev, dist.group.WORLD, mode=args.comm,
+                                max_tokens=max(args.context_size, 8192), hidden=hidden)
+            tp_info = TPInfo(rank=rank, size=world, group=dist.group.WORLD, comm=comm)
         ctrl = TPControl()
     pipe = InferencePipeline.load(args.model, device=args.device, context_size=args.context_size,
                                   speculative=args.speculative, draft_model=args.draft_model,
                                   num_speculative_tokens=args.num_speculative_tokens,
-                                  max_num_seqs=max(4, args.max_concurrent), tp_info=tp_info)
+                                  max_num_seqs=max(4, args.max_concurrent), tp_info=tp_info, pp_info=pp_info)
     if ctrl is not None and ctrl.rank != 0:
         follower_loop(pipe.llm, ctrl)  # returns when rank 0 shuts down
         return 0
