@@ -352,6 +352,34 @@ def main():
         report("wan_vae_decode_2f_480x832", ms, None, None, {"frames": 2})
         del vae
 
+    if args.only and "longcat" in args.only:
+        # LongCat image-edit transformer, full width (3072, 24 heads): 2 joint + 4 single blocks
+        # timed together and per block, 1,024 image tokens (512 x 512 image) + 512 text tokens
+        import dataclasses as _dc
+
+        from bloom_b200.models.longcat import LongCatTransformer, longcat_preset
+
+        lc = _dc.replace(longcat_preset("longcat-image-edit"), num_layers=2, num_single_layers=4)
+        tr = LongCatTransformer(lc, dev)
+        tr.random_init(0)
+        packed = torch.randn(1024, lc.in_channels, device=dev).to(torch.bfloat16)
+        ctx = torch.randn(512, lc.joint_attention_dim, device=dev).to(torch.bfloat16)
+        for _ in range(2):
+            tr.forward(packed, ctx, 0.5, (32, 32))
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            tr.forward(packed, ctx, 0.5, (32, 32))
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 3
+        T, D = 1536, lc.dim
+        blk = 2 * T * (3 * D * D + D * D + 2 * 4 * D * D) + 4 * T * T * D  # per block, both streams
+        flops = 2 * blk + 4 * (2 * T * (3 * D * D + 4 * D * D + 5 * D * D) + 4 * T * T * D)
+        report("longcat_transformer_2j4s_1536tok", ms, flops, None, {"tokens": T})
+        del tr
+
     if not args.only or "norm" in args.only:
         for M in (256, 8192):
             x = torch.randn(M, H, device=dev, dtype=torch.bfloat16)

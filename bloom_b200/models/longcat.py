@@ -112,16 +112,19 @@ def unpack_latents(p: torch.Tensor, C: int, H: int, W: int) -> torch.Tensor:
 
 
 def longcat_random_weights(cfg: LongCatConfig, seed: int = 0, device="cpu") -> Dict[str, torch.Tensor]:
-    g = torch.Generator(device="cpu").manual_seed(seed)
+    """Random weights drawn on `device` (a CUDA device draws them there: the full-size model
+    has ~12 B parameters)."""
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(seed)
     D, hd, Fd = cfg.dim, cfg.head_dim, cfg.ff_mult * cfg.dim
 
     def lin(name, o, i, scale=None):
         s = scale if scale is not None else i ** -0.5
-        w[name + ".weight"] = (torch.randn(o, i, generator=g) * s).to(torch.bfloat16).to(device)
-        w[name + ".bias"] = (torch.randn(o, generator=g) * 0.02).to(torch.bfloat16).to(device)
+        w[name + ".weight"] = (torch.randn(o, i, generator=g, device=dev) * s).to(torch.bfloat16)
+        w[name + ".bias"] = (torch.randn(o, generator=g, device=dev) * 0.02).to(torch.bfloat16)
 
     def nrm(name, n):
-        w[name + ".weight"] = (1.0 + 0.1 * torch.randn(n, generator=g)).float().to(device)
+        w[name + ".weight"] = (1.0 + 0.1 * torch.randn(n, generator=g, device=dev)).float()
 
     w: Dict[str, torch.Tensor] = {}
     lin("x_embedder", D, cfg.in_channels)
