@@ -321,3 +321,43 @@ def test_pipeline_layer_ranges():
     assert layer_range(80, 7, 8) == (70, 80)
     with pytest.raises(ValueError):
         layer_range(2, 0, 3)
+
+
+def test_gemma4_checkpoint_loads_through_the_manifest(tmp_path):
+    """A Gemma4 safetensors package (HF config with text_config, weights under
+    model.language_model.*) routes to the Gemma family and loads into
+    Gemma4LM with per-layer geometry (host memory only, no forward)."""
+    from bloom_b200.formats.loader import load_manifest, load_weights, model_config
+    from bloom_b200.formats.safetensors_io import save_file
+    from bloom_b200.models import build_decoder
+    from bloom_b200.models.config import preset, to_hf_config
+    from bloom_b200.models.reference import gemma4_random_weights
+
+    cfg = preset("tiny-gemma4")
+    hf = {"model_type": "gemma4", "eos_token_id": [1, 106], "text_config": {
+        "hidden_size": cfg.hidden_size, "num_hidden_layers": cfg.num_layers, "num_attention_heads": cfg.num_heads,
+        "num_key_value_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim, "global_head_dim": cfg.head_dim_global,
+        "num_global_key_value_heads": cfg.num_kv_heads_global, "intermediate_size": cfg.intermediate_size,
+        "vocab_size": cfg.vocab_size, "sliding_window": cfg.sliding_window, "attention_k_eq_v": True,
+        "final_logit_softcapping": 30.0, "attn_logit_softcapping": 50.0, "max_position_embeddings": 1024,
+        "rope_parameters": {"full_attention": {"rope_theta": 1e6, "partial_rotary_factor": 0.25},
+                            "sliding_attention": {"rope_theta": 1e4}}}}
+    d = tmp_path / "gemma4"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(hf))
+    from tokenizers import Tokenizer
+    from tokenizers.models import WordLevel
+
+    Tokenizer(WordLevel({"<unk>": 0, "<eos>": 1, "a": 2}, unk_token="<unk>")).save(str(d / "tokenizer.json"))
+    w = gemma4_random_weights(cfg, seed=0)
+    save_file({k: v.contiguous() for k, v in w.items()}, str(d / "model.safetensors"))
+    man = load_manifest(str(d))
+    assert man.family == "Gemma"
+    c2 = model_config(man)
+    assert c2.arch == "gemma4" and c2.layer_attn(5) == (512, 1) and c2.attention_k_eq_v
+    m = build_decoder(c2, None, "cpu")
+    m.shard_full(load_weights(man))
+    assert len(m.layers) == cfg.num_layers
+    assert m.layers[0]["qkv"].shape == ((4 + 2 * 2) * 256, 256)      # sliding: q + k + v
+    assert m.layers[5]["qkv"].shape == ((4 + 1) * 512, 256)          # global, k = v: q + k only
+    assert m.kv_elems == 2 * 2 * 16 * 256 and m.cos_sin[(128, 512, False)].shape == (1024, 128)
