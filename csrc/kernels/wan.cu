@@ -131,6 +131,83 @@ __global__ void __launch_bounds__(kThreads) residual_norm_kernel(const ResArgs a
   }
 }
 
+// The same step with one warp per row (8 rows per 256-thread CTA): warp
+// shuffles instead of block barriers, and no idle threads for D = 1536 /
+// 3072 (the CTA-per-row kernel leaves 64 of 256 threads idle at D = 1536).
+// CPL = 8-element chunks per lane (D <= 256 * CPL).
+template <int CPL>
+__global__ void __launch_bounds__(kThreads) residual_norm_warp_kernel(const ResArgs a, long T) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * (kThreads / 32) + warp;
+  if (row >= T) return;
+  const int b = int(row / a.S);
+  const int nch = a.D / 8;
+  float v[CPL][8];
+  float s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[i][k] = 0.f;
+    if (c >= nch) continue;
+    float* xp = a.x + row * a.D + c * 8;
+    const float4 x0 = *reinterpret_cast<const float4*>(xp);
+    const float4 x1 = *reinterpret_cast<const float4*>(xp + 4);
+    v[i][0] = x0.x, v[i][1] = x0.y, v[i][2] = x0.z, v[i][3] = x0.w;
+    v[i][4] = x1.x, v[i][5] = x1.y, v[i][6] = x1.z, v[i][7] = x1.w;
+    if (a.delta != nullptr) {
+      const uint4 u = *reinterpret_cast<const uint4*>(a.delta + row * a.D + c * 8);
+      const __nv_bfloat16* db = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float g = 1.f;
+        if (a.gi >= 0) {
+          const int d = c * 8 + k;
+          g = a.gmod[a.gi * a.D + d] + a.ge[b * a.gbs + a.gi * a.gis + d];
+        }
+        v[i][k] += __bfloat162float(db[k]) * g;
+      }
+      *reinterpret_cast<float4*>(xp) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+      *reinterpret_cast<float4*>(xp + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s1 += v[i][k];
+  }
+  float mean = 0.f, inv = 1.f;
+  if (a.mode != 0) {
+    mean = warp_sum(s1) / a.D;
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      if (lane + 32 * i >= nch) continue;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s2 += (v[i][k] - mean) * (v[i][k] - mean);
+    }
+    inv = rsqrtf(warp_sum(s2) / a.D + a.eps);
+  }
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= nch) continue;
+    float o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = c * 8 + k;
+      float t = v[i][k];
+      if (a.mode == 1) {
+        t = (t - mean) * inv * (a.lw ? a.lw[d] : 1.f) + (a.lb ? a.lb[d] : 0.f);
+      } else if (a.mode == 2) {
+        const float sc = a.nmod[a.isc * a.D + d] + a.ne[b * a.ebs + a.isc * a.eis + d];
+        const float sh = a.nmod[a.ish * a.D + d] + a.ne[b * a.ebs + a.ish * a.eis + d];
+        t = (t - mean) * inv * (1.f + sc) + sh;
+      }
+      o[k] = t;
+    }
+    *reinterpret_cast<uint4*>(a.y + row * a.D + c * 8) = make_uint4(
+        pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  }
+}
+
 struct QkvArgs {
   const __nv_bfloat16* src;
   long ld;
@@ -242,6 +319,73 @@ __global__ void __launch_bounds__(kThreads) qkv_norm_rope_kernel(const QkvArgs a
   }
 }
 
+// Full-model-dim norms (head_norm == 0) with one warp per src row: the
+// squares are summed with shuffles, the pairs re-read from L1 for the write.
+__global__ void __launch_bounds__(kThreads) qkv_norm_rope_warp_kernel(const QkvArgs a, long T) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * (kThreads / 32) + warp;
+  if (row >= T) return;
+  const int b = int(row / a.S), n = int(row - (long)b * a.S);
+  const int no = a.off + n;
+  const long orow = (long)b * a.S_out + no;
+  int pf, ph_, pw;
+  if (a.pos3 != nullptr) {
+    pf = a.pos3[no * 3];
+    ph_ = a.pos3[no * 3 + 1];
+    pw = a.pos3[no * 3 + 2];
+  } else {
+    const int hw = a.gh * a.gw;
+    pf = n / hw;
+    ph_ = (n / a.gw) % a.gh;
+    pw = n % a.gw;
+  }
+  const int half = a.hd / 2, np = a.D / 2;
+  const __nv_bfloat16* s = a.src + row * a.ld;
+  const int blk = b * a.bpb + no / 16, slot = no % 16;
+  for (int part = 0; part < 2; ++part) {
+    const int col = part == 0 ? a.q_col : a.k_col;
+    if (col < 0) continue;
+    const float* w = part == 0 ? a.qw : a.kw;
+    float inv = 1.f;
+    if (w != nullptr) {
+      float ss = 0.f;
+      for (int P = lane; P < np; P += 32) {
+        const __nv_bfloat162 t = *reinterpret_cast<const __nv_bfloat162*>(s + col + 2 * P);
+        const float x0 = __bfloat162float(t.x), x1 = __bfloat162float(t.y);
+        ss += x0 * x0 + x1 * x1;
+      }
+      inv = rsqrtf(warp_sum(ss) / a.D + a.eps);
+    }
+    for (int P = lane; P < np; P += 32) {
+      const __nv_bfloat162 t = *reinterpret_cast<const __nv_bfloat162*>(s + col + 2 * P);
+      float x0 = __bfloat162float(t.x) * inv, x1 = __bfloat162float(t.y) * inv;
+      if (w != nullptr) {
+        x0 *= w[2 * P];
+        x1 *= w[2 * P + 1];
+      }
+      if (a.rope != nullptr) {
+        const int p = P % half;
+        const int pos = min(max(p < a.pt ? pf : (p < a.pt + a.ph ? ph_ : pw), 0), a.rope_rows - 1);
+        const float2 cs = a.rope[(long)pos * half + p];
+        const float r0 = x0 * cs.x - x1 * cs.y, r1 = x0 * cs.y + x1 * cs.x;
+        x0 = r0;
+        x1 = r1;
+      }
+      const int h = (2 * P) / a.hd, d = 2 * P - h * a.hd;
+      __nv_bfloat16* dst = part == 0 ? a.q_out + (orow * a.nh + h) * a.hd + d
+                                     : a.kv + (((long)blk * 2 + 0) * a.nh + h) * 16 * a.hd + slot * a.hd + d;
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(x0, x1);
+    }
+  }
+  if (a.v_col >= 0) {
+    for (int P = lane; P < np; P += 32) {
+      const int h = (2 * P) / a.hd, d = 2 * P - h * a.hd;
+      *reinterpret_cast<uint32_t*>(a.kv + (((long)blk * 2 + 1) * a.nh + h) * 16 * a.hd + slot * a.hd + d) =
+          *reinterpret_cast<const uint32_t*>(s + a.v_col + 2 * P);
+    }
+  }
+}
+
 // latent f32 [B, C, F, H, W] -> tokens bf16 [B * F * (H/2) * (W/2), C * 4],
 // column c * 4 + i * 2 + j = latent[b, c, f, 2h + i, 2w + j] (the 1x2x2 patch
 // conv's weight layout [dim, C, 1, 2, 2] flattened)
@@ -338,7 +482,17 @@ void wan_residual_norm(torch::Tensor& x, const c10::optional<torch::Tensor>& del
   a.eps = float(eps);
   a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
   const at::cuda::CUDAGuard g(x.device());
-  wan::residual_norm_kernel<<<T, wan::kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int nch = D / 8;
+  const int blocks = (T + wan::kThreads / 32 - 1) / (wan::kThreads / 32);
+  if (nch <= 64)
+    wan::residual_norm_warp_kernel<2><<<blocks, wan::kThreads, 0, st>>>(a, T);
+  else if (nch <= 192)
+    wan::residual_norm_warp_kernel<6><<<blocks, wan::kThreads, 0, st>>>(a, T);
+  else if (nch <= 384)
+    wan::residual_norm_warp_kernel<12><<<blocks, wan::kThreads, 0, st>>>(a, T);
+  else
+    wan::residual_norm_kernel<<<T, wan::kThreads, 0, st>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -417,7 +571,12 @@ void wan_qkv_norm_rope(const torch::Tensor& src, int64_t q_col, int64_t k_col, i
   const size_t smem = head_norm ? (size_t(D / 2) + size_t(heads)) * sizeof(float) : 0;
   TORCH_CHECK(smem <= 48 * 1024, "wan_qkv_norm_rope: model dim too large for per-head norms");
   const at::cuda::CUDAGuard g(src.device());
-  wan::qkv_norm_rope_kernel<<<T, wan::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(a);
+  if (head_norm) {
+    wan::qkv_norm_rope_kernel<<<T, wan::kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(a);
+  } else {
+    const int blocks = (T + wan::kThreads / 32 - 1) / (wan::kThreads / 32);
+    wan::qkv_norm_rope_warp_kernel<<<blocks, wan::kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a, T);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
